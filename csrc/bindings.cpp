@@ -1,0 +1,213 @@
+// Python bindings of the sm_100a kernels (module lunaflux_b200._C).
+//
+// Every entry launches on the current torch CUDA stream and allocates nothing,
+// so all of them can be captured inside a CUDA graph.  Shapes, dtypes and
+// strides are checked here; kernels never see an operand they cannot handle.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "kernels/attention.h"
+#include "kernels/elementwise.h"
+#include "kernels/gemm_bf16.h"
+#include "kernels/runtime.h"
+
+namespace {
+
+#define LF_CHECK(cond, msg) TORCH_CHECK(cond, "lunaflux: ", msg)
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  LF_CHECK(t.is_cuda(), std::string(name) + " must be a CUDA tensor");
+}
+void check_rowmajor(const at::Tensor& t, const char* name) {
+  LF_CHECK(t.dim() == 2 && t.stride(1) == 1, std::string(name) + " must be 2-D with unit inner stride");
+}
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, int64_t epi, int64_t bn) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(D, "D");
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  check_rowmajor(D, "D");
+  LF_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
+  LF_CHECK(A.size(1) == B.size(1), "gemm K mismatch");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  if (epi == 2) {
+    LF_CHECK(D.size(0) == M && D.size(1) == N / 2, "SwiGLU output must be [M, N/2]");
+    LF_CHECK(D.scalar_type() == at::kBFloat16, "SwiGLU output must be bf16");
+  } else {
+    LF_CHECK(D.size(0) == M && D.size(1) == N, "gemm output must be [M, N]");
+    LF_CHECK(D.scalar_type() == (epi == 1 ? at::kFloat : at::kBFloat16), "gemm output dtype mismatch");
+  }
+  c10::cuda::CUDAGuard g(A.device());
+  lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), B.stride(0), D.stride(0)};
+  lf::gemm::run(a, (int)epi, (int)bn, stream());
+}
+
+int64_t gemm_choose_bn(int64_t M, int64_t N, int64_t epi) { return lf::gemm::choose_bn(M, N, epi); }
+
+void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) {
+  LF_CHECK(ids.scalar_type() == at::kInt && table.scalar_type() == at::kBFloat16, "embed dtypes");
+  LF_CHECK(table.is_contiguous() && out.is_contiguous() && ids.is_contiguous(), "embed needs contiguous tensors");
+  LF_CHECK(table.size(1) % 8 == 0, "hidden must be a multiple of 8");
+  LF_CHECK(out.size(0) >= ids.size(0), "embed output too small");
+  c10::cuda::CUDAGuard g(table.device());
+  lf::ew::embed(ids.data_ptr<int32_t>(), table.data_ptr(), out.data_ptr(), ids.size(0), table.size(1), table.size(0),
+                stream());
+}
+
+void rmsnorm(const at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w, at::Tensor& out,
+             double eps) {
+  LF_CHECK(x.is_contiguous() && out.is_contiguous() && w.is_contiguous(), "rmsnorm needs contiguous tensors");
+  LF_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "rmsnorm is bf16");
+  const int H = x.size(-1);
+  LF_CHECK(H % 8 == 0 && w.numel() == H, "rmsnorm hidden size");
+  void* r = nullptr;
+  if (residual.has_value()) {
+    LF_CHECK(residual->is_contiguous() && residual->numel() == x.numel(), "residual shape");
+    r = residual->data_ptr();
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  lf::ew::rmsnorm(x.data_ptr(), r, w.data_ptr(), out.data_ptr(), x.numel() / H, H, (float)eps, stream());
+}
+
+void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slots, const at::Tensor& cos_sin,
+                   at::Tensor& kcache, at::Tensor& vcache, int64_t Hq, int64_t Hkv, int64_t page) {
+  check_rowmajor(qkv, "qkv");
+  LF_CHECK(qkv.scalar_type() == at::kBFloat16, "qkv must be bf16");
+  LF_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin must be contiguous fp32");
+  LF_CHECK(kcache.is_contiguous() && vcache.is_contiguous(), "kv cache must be contiguous");
+  const int D = kcache.size(-1);
+  LF_CHECK(qkv.size(1) >= (Hq + 2 * Hkv) * D, "qkv width");
+  LF_CHECK(positions.size(0) >= qkv.size(0) && slots.size(0) >= qkv.size(0), "positions/slots length");
+  const int64_t num_slots = kcache.numel() / (Hkv * D);
+  c10::cuda::CUDAGuard g(qkv.device());
+  lf::ew::rope_kv_write(qkv.data_ptr(), qkv.stride(0), positions.data_ptr<int32_t>(), slots.data_ptr<int32_t>(),
+                        cos_sin.data_ptr(), kcache.data_ptr(), vcache.data_ptr(), qkv.size(0), Hq, Hkv, D, page,
+                        cos_sin.size(0), num_slots, stream());
+}
+
+void swiglu(const at::Tensor& gu, at::Tensor& out) {
+  LF_CHECK(gu.is_contiguous() && out.is_contiguous(), "swiglu needs contiguous tensors");
+  c10::cuda::CUDAGuard g(gu.device());
+  lf::ew::swiglu(gu.data_ptr(), out.data_ptr(), gu.size(0), gu.size(1) / 2, stream());
+}
+
+void argmax(const at::Tensor& logits, at::Tensor& out, c10::optional<at::Tensor> status) {
+  check_rowmajor(logits, "logits");
+  LF_CHECK(logits.scalar_type() == at::kFloat, "logits must be fp32");
+  c10::cuda::CUDAGuard g(logits.device());
+  lf::ew::argmax(logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1), out.data_ptr<int32_t>(),
+                 status.has_value() ? status->data_ptr<int32_t>() : nullptr, stream());
+}
+
+void sample(const at::Tensor& logits, const at::Tensor& params, at::Tensor& out, c10::optional<at::Tensor> status) {
+  check_rowmajor(logits, "logits");
+  LF_CHECK(logits.scalar_type() == at::kFloat, "logits must be fp32");
+  LF_CHECK(params.is_contiguous() && params.nbytes() >= (size_t)logits.size(0) * sizeof(lf::ew::SampleParams),
+           "sample params: one 32-byte record per row");
+  c10::cuda::CUDAGuard g(logits.device());
+  lf::ew::sample(logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1),
+                 reinterpret_cast<const lf::ew::SampleParams*>(params.data_ptr()), out.data_ptr<int32_t>(),
+                 status.has_value() ? status->data_ptr<int32_t>() : nullptr, stream());
+}
+
+void attn_decode(const at::Tensor& q, at::Tensor& out, const at::Tensor& tok_index, const at::Tensor& seq_lens,
+                 const at::Tensor& block_table, const at::Tensor& kcache, const at::Tensor& vcache, int64_t Hq,
+                 int64_t Hkv, int64_t splits, c10::optional<at::Tensor> part_o, c10::optional<at::Tensor> part_lse) {
+  check_rowmajor(q, "q");
+  check_rowmajor(out, "out");
+  check_rowmajor(block_table, "block_table");
+  LF_CHECK(kcache.is_contiguous() && vcache.is_contiguous() && kcache.dim() == 4, "kv cache must be [pages, Hkv, 16, D]");
+  lf::attn::DecodeArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.q_ld = q.stride(0);
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.out_ld = out.stride(0);
+  a.tok_index = tok_index.data_ptr<int32_t>();
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.block_table = block_table.data_ptr<int32_t>();
+  a.bt_stride = block_table.stride(0);
+  a.rows = seq_lens.size(0);
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.D = kcache.size(3);
+  a.page = kcache.size(2);
+  a.num_pages = kcache.size(0);
+  LF_CHECK(kcache.size(1) == Hkv, "kv cache head count");
+  a.splits = splits;
+  a.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)a.D));
+  if (splits > 1) {
+    LF_CHECK(part_o.has_value() && part_lse.has_value(), "split-KV needs part_o / part_lse");
+    LF_CHECK(part_o->numel() >= (int64_t)a.rows * Hq * splits * a.D && part_lse->numel() >= (int64_t)a.rows * Hq * splits,
+             "split-KV workspace too small");
+    a.part_o = part_o->data_ptr<float>();
+    a.part_lse = part_lse->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  lf::attn::decode(a, kcache.data_ptr(), vcache.data_ptr(), stream());
+}
+
+int64_t attn_decode_splits(int64_t rows, int64_t Hkv, int64_t max_seq, int64_t num_sms) {
+  return lf::attn::decode_splits(rows, Hkv, max_seq, num_sms);
+}
+
+void attn_prefill(const at::Tensor& q, at::Tensor& out, const at::Tensor& q_start, const at::Tensor& seq_lens,
+                  const at::Tensor& block_table, const at::Tensor& kcache, const at::Tensor& vcache, int64_t Hq,
+                  int64_t Hkv, int64_t max_q_len) {
+  check_rowmajor(q, "q");
+  check_rowmajor(out, "out");
+  check_rowmajor(block_table, "block_table");
+  LF_CHECK(kcache.is_contiguous() && vcache.is_contiguous() && kcache.dim() == 4, "kv cache must be [pages, Hkv, 16, D]");
+  lf::attn::PrefillArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.q_ld = q.stride(0);
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.out_ld = out.stride(0);
+  a.q_start = q_start.data_ptr<int32_t>();
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.block_table = block_table.data_ptr<int32_t>();
+  a.bt_stride = block_table.stride(0);
+  a.rows = seq_lens.size(0);
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.D = kcache.size(3);
+  a.page = kcache.size(2);
+  a.num_pages = kcache.size(0);
+  a.max_q_len = max_q_len;
+  a.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)a.D));
+  c10::cuda::CUDAGuard g(q.device());
+  lf::attn::prefill(a, kcache.data_ptr(), vcache.data_ptr(), stream());
+}
+
+std::pair<int64_t, int64_t> read_error(bool clear) {
+  auto st = lf::rt::read_error(stream(), clear);
+  return {st.code, (int64_t)st.info};
+}
+
+void inject_error(int64_t code) { lf::rt::inject_error((int)code); }
+
+double counter_unit(uint64_t seed, int64_t idx) { return lf::ew::host_counter_unit(seed, idx); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "LunaFlux sm_100a kernels";
+  m.def("gemm", &gemm, "D = A @ B^T on tcgen05 (epi 0 bf16, 1 fp32, 2 SwiGLU)");
+  m.def("gemm_choose_bn", &gemm_choose_bn);
+  m.def("embed", &embed);
+  m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"));
+  m.def("rope_kv_write", &rope_kv_write);
+  m.def("swiglu", &swiglu);
+  m.def("argmax", &argmax, py::arg("logits"), py::arg("out"), py::arg("status") = py::none());
+  m.def("sample", &sample, py::arg("logits"), py::arg("params"), py::arg("out"), py::arg("status") = py::none());
+  m.def("attn_decode", &attn_decode);
+  m.def("attn_decode_splits", &attn_decode_splits);
+  m.def("attn_prefill", &attn_prefill);
+  m.def("read_error", &read_error, py::arg("clear") = true);
+  m.def("inject_error", &inject_error);
+  m.def("counter_unit", &counter_unit);
+}

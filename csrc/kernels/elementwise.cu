@@ -1,0 +1,422 @@
+// Memory-bound sm_100a kernels of the decoder step: embedding gather,
+// RMSNorm with fused residual add, RoPE fused with the paged-KV write, SwiGLU,
+// and the on-device samplers (greedy argmax and top-k / top-p / temperature).
+//
+// Oracle semantics (reference file:line):
+//   embedding         kernels/reference/basic.mbt:3-28
+//   RMSNorm           kernels/reference/basic.mbt:31-68   x * rsqrt(mean(x^2) + eps) * w
+//   residual add      kernels/reference/basic.mbt:156-171
+//   split-half RoPE   kernels/reference/rotary.mbt:187-243
+//   SiLU-gated MLP    kernels/reference/mlp.mbt:335-369
+//   greedy            sampling/greedy.mbt (max finite logit, lowest id on ties)
+//   stochastic        sampling/stochastic.mbt (sort desc / lowest id, top-k,
+//                     max-shifted temperature softmax, smallest nucleus with
+//                     mass >= top_p * total, draw where cumulative > u * mass)
+//   counter RNG       sampling/rng.mbt (splitmix-style counter_state/counter_unit)
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "elementwise.h"
+
+namespace lf {
+namespace ew {
+
+// ---------------------------------------------------------------------------
+// Embedding gather: out[t, :] = E[ids[t], :]   (bf16, 16-byte vectors)
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const uint4* __restrict__ table,
+                             uint4* __restrict__ out, int T, int vec_per_row, int vocab) {
+  const int t = blockIdx.x;
+  int id = ids[t];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) set_error(kErrBadIndex, (unsigned long long)t);
+    for (int i = threadIdx.x; i < vec_per_row; i += blockDim.x) out[(size_t)t * vec_per_row + i] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  for (int i = threadIdx.x; i < vec_per_row; i += blockDim.x)
+    out[(size_t)t * vec_per_row + i] = table[(size_t)id * vec_per_row + i];
+}
+
+void embed(const int32_t* ids, const void* table, void* out, int T, int H, int vocab, cudaStream_t s) {
+  if (T <= 0) return;
+  const int vpr = H / 8;
+  embed_kernel<<<T, 128, 0, s>>>(ids, reinterpret_cast<const uint4*>(table), reinterpret_cast<uint4*>(out), T, vpr, vocab);
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm (+ residual).  If `residual` is non-null:
+//   r = x + residual;  residual = r;  out = r * rsqrt(mean(r^2) + eps) * w
+// else out = x * rsqrt(mean(x^2) + eps) * w.   fp32 math, bf16 storage.
+// One CTA per row, each thread owns VPT 16-byte vectors held in registers.
+// ---------------------------------------------------------------------------
+template <int VPT>
+__global__ void __launch_bounds__(128) rmsnorm_kernel(const uint4* __restrict__ x, uint4* __restrict__ residual,
+                                                      const uint4* __restrict__ w, uint4* __restrict__ out,
+                                                      int vec_per_row, float eps, int H) {
+  const size_t row = blockIdx.x;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * 128;
+    if (i < vec_per_row) {
+      uint4 a = x[row * vec_per_row + i];
+      const __nv_bfloat16* ab = reinterpret_cast<const __nv_bfloat16*>(&a);
+      if (residual != nullptr) {
+        uint4 r = residual[row * vec_per_row + i];
+        const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&r);
+        uint4 sum;
+        __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(&sum);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          // The residual stream is kept in bf16, as the model's activations are.
+          sb[e] = __float2bfloat16(__bfloat162float(ab[e]) + __bfloat162float(rb[e]));
+          v[j][e] = __bfloat162float(sb[e]);
+        }
+        residual[row * vec_per_row + i] = sum;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[j][e] = __bfloat162float(ab[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[j][e] * v[j][e];
+    }
+  }
+  __shared__ float red[4];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  const float total = red[0] + red[1] + red[2] + red[3];
+  const float inv = rsqrtf(total / (float)H + eps);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * 128;
+    if (i < vec_per_row) {
+      uint4 wv = w[i];
+      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv);
+      uint4 o;
+      __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16(v[j][e] * inv * __bfloat162float(wb[e]));
+      out[row * vec_per_row + i] = o;
+    }
+  }
+}
+
+void rmsnorm(const void* x, void* residual, const void* w, void* out, int T, int H, float eps, cudaStream_t s) {
+  if (T <= 0) return;
+  const int vpr = H / 8;
+  const int vpt = (vpr + 127) / 128;
+  auto X = reinterpret_cast<const uint4*>(x);
+  auto R = reinterpret_cast<uint4*>(residual);
+  auto W = reinterpret_cast<const uint4*>(w);
+  auto O = reinterpret_cast<uint4*>(out);
+  if (vpt <= 1) rmsnorm_kernel<1><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
+  else if (vpt <= 2) rmsnorm_kernel<2><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
+  else if (vpt <= 4) rmsnorm_kernel<4><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
+  else if (vpt <= 8) rmsnorm_kernel<8><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
+  else rmsnorm_kernel<16><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
+}
+
+// ---------------------------------------------------------------------------
+// RoPE + paged KV write.
+// qkv: [T, (Hq + 2*Hkv) * D] bf16, rows of stride ld; Q heads, then K, then V.
+// Q is rotated in place.  K is rotated and, with V, written to the paged cache
+// at slot_mapping[t] (= page * PAGE + offset).  Cache layout per layer and per
+// K/V: [page][kv_head][PAGE][D] (one (page, head) block is contiguous).
+// cos_sin: [max_pos, D/2] float2 (cos, sin) for angle = pos / theta^(2i/D).
+// A negative slot skips the write (padding rows of a captured batch).
+// ---------------------------------------------------------------------------
+__global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const int32_t* __restrict__ positions,
+                               const int32_t* __restrict__ slots, const float2* __restrict__ cos_sin,
+                               __nv_bfloat16* __restrict__ kcache, __nv_bfloat16* __restrict__ vcache, int Hq,
+                               int Hkv, int D, int page, int max_pos, int64_t num_slots) {
+  const int t = blockIdx.x;
+  const int half = D / 2;
+  const int pos = positions[t];
+  const int slot = slots[t];
+  __nv_bfloat16* row = qkv + (size_t)t * ld;
+  const bool pos_ok = pos >= 0 && pos < max_pos;
+  if (!pos_ok && threadIdx.x == 0) set_error(kErrBadIndex, (unsigned long long)t);
+  const bool slot_ok = slot >= 0 && (int64_t)slot < num_slots;
+  const int pg = slot / page, off = slot % page;
+  // Rotate Q and K heads: work item = (head, i) with i < D/2.
+  const int n_rot = (Hq + Hkv) * half;
+  for (int w = threadIdx.x; w < n_rot; w += blockDim.x) {
+    const int h = w / half, i = w % half;
+    __nv_bfloat16* hp = row + h * D;
+    const float x1 = __bfloat162float(hp[i]);
+    const float x2 = __bfloat162float(hp[i + half]);
+    float2 cs = pos_ok ? cos_sin[(size_t)pos * half + i] : make_float2(1.f, 0.f);
+    const __nv_bfloat16 o1 = __float2bfloat16(x1 * cs.x - x2 * cs.y);
+    const __nv_bfloat16 o2 = __float2bfloat16(x2 * cs.x + x1 * cs.y);
+    if (h < Hq) {
+      hp[i] = o1;
+      hp[i + half] = o2;
+    } else if (slot_ok) {
+      const int kh = h - Hq;
+      __nv_bfloat16* dst = kcache + (((size_t)pg * Hkv + kh) * page + off) * D;
+      dst[i] = o1;
+      dst[i + half] = o2;
+    }
+  }
+  if (slot_ok) {
+    // V heads: plain copy, 8 bf16 per thread-iteration.
+    const int n_v = Hkv * D / 8;
+    const uint4* vsrc = reinterpret_cast<const uint4*>(row + (Hq + Hkv) * D);
+    for (int w = threadIdx.x; w < n_v; w += blockDim.x) {
+      const int kh = (w * 8) / D, d = (w * 8) % D;
+      uint4* dst = reinterpret_cast<uint4*>(vcache + (((size_t)pg * Hkv + kh) * page + off) * D + d);
+      *dst = vsrc[w];
+    }
+  }
+}
+
+void rope_kv_write(void* qkv, int64_t ld, const int32_t* positions, const int32_t* slots, const void* cos_sin,
+                   void* kcache, void* vcache, int T, int Hq, int Hkv, int D, int page, int max_pos,
+                   int64_t num_slots, cudaStream_t s) {
+  if (T <= 0) return;
+  rope_kv_kernel<<<T, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(qkv), ld, positions, slots,
+                                    reinterpret_cast<const float2*>(cos_sin), reinterpret_cast<__nv_bfloat16*>(kcache),
+                                    reinterpret_cast<__nv_bfloat16*>(vcache), Hq, Hkv, D, page, max_pos, num_slots);
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU over a [T, 2F] gate|up buffer (gate = first F columns): out = silu(g)*u.
+// Used where the gate/up projection is not the fused tcgen05 epilogue.
+// ---------------------------------------------------------------------------
+__global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int F) {
+  const size_t t = blockIdx.x;
+  for (int i = threadIdx.x; i < F; i += blockDim.x) {
+    const float g = __bfloat162float(gu[t * 2 * F + i]);
+    const float u = __bfloat162float(gu[t * 2 * F + F + i]);
+    const float gs = __bfloat162float(__float2bfloat16(g / (1.f + __expf(-g))));
+    out[t * F + i] = __float2bfloat16(gs * u);
+  }
+}
+
+void swiglu(const void* gu, void* out, int T, int F, cudaStream_t s) {
+  if (T <= 0) return;
+  swiglu_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), F);
+}
+
+// ---------------------------------------------------------------------------
+// Samplers.
+// ---------------------------------------------------------------------------
+// Monotone map float -> uint32 (larger float => larger key).
+__device__ __forceinline__ uint32_t fkey(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Composite total order used by the reference sort: larger logit first, then
+// lower token id first.  Larger composite key == earlier in sorted order.
+__device__ __forceinline__ uint64_t ckey(float f, int id) {
+  return ((uint64_t)fkey(f) << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)id);
+}
+
+template <int NT>
+__device__ __forceinline__ uint64_t block_max_u64(uint64_t v, uint64_t* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  uint64_t r = sh[0];
+#pragma unroll
+  for (int i = 1; i < NT / 32; ++i) r = sh[i] > r ? sh[i] : r;
+  return r;
+}
+
+template <int NT>
+__device__ __forceinline__ double block_sum_f64(double v, double* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double r = 0.0;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) r += sh[i];
+  return r;
+}
+
+template <int NT>
+__device__ __forceinline__ int block_sum_i(int v, int* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  int r = 0;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) r += sh[i];
+  return r;
+}
+
+// Greedy: per row, the max finite logit, lowest id on ties.  Non-finite logits
+// record kErrBadIndex-free status -1 in out_status[row].
+template <int NT>
+__global__ void __launch_bounds__(NT) argmax_kernel(const float* __restrict__ logits, int64_t ld, int V,
+                                                    int32_t* __restrict__ out_tok, int32_t* __restrict__ status) {
+  __shared__ uint64_t sh[NT / 32];
+  __shared__ int shi[NT / 32];
+  const float* row = logits + (size_t)blockIdx.x * ld;
+  uint64_t best = 0;
+  int bad = 0;
+  for (int i = threadIdx.x; i < V; i += NT) {
+    const float v = row[i];
+    if (!isfinite(v)) { bad = 1; continue; }
+    const uint64_t k = ckey(v, i);
+    best = k > best ? k : best;
+  }
+  best = block_max_u64<NT>(best, sh);
+  bad = block_sum_i<NT>(bad, shi);
+  if (threadIdx.x == 0) {
+    out_tok[blockIdx.x] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+    if (status) status[blockIdx.x] = bad ? -1 : 0;
+  }
+}
+
+void argmax(const float* logits, int64_t ld, int R, int V, int32_t* out, int32_t* status, cudaStream_t s) {
+  if (R <= 0) return;
+  argmax_kernel<1024><<<R, 1024, 0, s>>>(logits, ld, V, out, status);
+}
+
+// Counter-addressed uniform draw in [0, 1) with 53 random bits
+// (sampling/rng.mbt counter_state / counter_unit).
+__host__ __device__ inline double counter_unit(uint64_t seed, int64_t sample_index) {
+  uint64_t v = seed + (uint64_t)(sample_index + 1) * 0x9e3779b97f4a7c15ull;
+  v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+  v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+  v = v ^ (v >> 31);
+  if (v == 0) v = 0x9e3779b97f4a7c15ull;
+  return (double)(v >> 11) * 1.1102230246251565e-16;
+}
+
+// Per-row sampling parameters (SampleParams in elementwise.h).
+// For each row: mode 0 = greedy, 1 = sample.
+//
+// Stochastic rows: every quantity over the sorted order is computed as a
+// function of a composite-key threshold K ("all tokens whose key >= K" is a
+// prefix of the reference's sorted order), and the thresholds are found by
+// bisection on the 64-bit key space (64 passes).  No sort and no scratch.
+template <int NT>
+__global__ void __launch_bounds__(NT) sample_kernel(const float* __restrict__ logits, int64_t ld, int V,
+                                                    const SampleParams* __restrict__ params,
+                                                    int32_t* __restrict__ out_tok, int32_t* __restrict__ status) {
+  __shared__ uint64_t shk[NT / 32];
+  __shared__ double shd[NT / 32];
+  __shared__ int shi[NT / 32];
+  const int r = blockIdx.x;
+  const float* row = logits + (size_t)r * ld;
+  const SampleParams p = params[r];
+
+  // Pass 1: validation and the top key (max logit, lowest id).
+  uint64_t best = 0;
+  int bad = 0;
+  for (int i = threadIdx.x; i < V; i += NT) {
+    const float v = row[i];
+    if (!isfinite(v)) { bad = 1; continue; }
+    const uint64_t k = ckey(v, i);
+    best = k > best ? k : best;
+  }
+  best = block_max_u64<NT>(best, shk);
+  bad = block_sum_i<NT>(bad, shi);
+  const int top_id = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+  if (bad) {
+    if (threadIdx.x == 0) { out_tok[r] = top_id; if (status) status[r] = -1; }
+    return;
+  }
+  if (p.mode == 0 || !(p.temperature > 0.f)) {
+    if (threadIdx.x == 0) { out_tok[r] = top_id; if (status) status[r] = 0; }
+    return;
+  }
+  const float mx = row[top_id];
+  const float inv_t = 1.0f / p.temperature;
+
+  // Key-space bisection helpers.
+  auto count_ge = [&](uint64_t K) -> int {
+    int c = 0;
+    for (int i = threadIdx.x; i < V; i += NT) c += ckey(row[i], i) >= K;
+    return block_sum_i<NT>(c, shi);
+  };
+  auto mass_ge = [&](uint64_t K, uint64_t floor_key) -> double {
+    double m = 0.0;
+    for (int i = threadIdx.x; i < V; i += NT) {
+      const float v = row[i];
+      const uint64_t k = ckey(v, i);
+      if (k >= K && k >= floor_key) m += (double)__expf((v - mx) * inv_t);
+    }
+    return block_sum_f64<NT>(m, shd);
+  };
+
+  // Top-k: the k-th largest key (largest K with count_ge(K) >= k).
+  uint64_t kfloor = 0;
+  if (p.top_k > 0 && p.top_k < V) {
+    uint64_t lo = 0, hi = best;  // invariant: count_ge(lo) >= k, answer in [lo, hi]
+    while (lo < hi) {
+      const uint64_t mid = lo + (hi - lo + 1) / 2;
+      if (count_ge(mid) >= p.top_k) lo = mid; else hi = mid - 1;
+    }
+    kfloor = lo;
+  }
+  const double total = mass_ge(0, kfloor);
+
+  // Top-p: smallest prefix with cumulative >= top_p * total
+  //   == the largest K with mass_ge(K) >= threshold.
+  uint64_t pfloor = kfloor;
+  if (p.top_p > 0.f && p.top_p < 1.f) {
+    const double thr = (double)p.top_p * total;
+    uint64_t lo = kfloor, hi = best;
+    while (lo < hi) {
+      const uint64_t mid = lo + (hi - lo + 1) / 2;
+      if (mass_ge(mid, kfloor) >= thr) lo = mid; else hi = mid - 1;
+    }
+    pfloor = lo;
+  }
+  const double retained = mass_ge(pfloor, pfloor);
+
+  // Draw: the first sorted token whose inclusive cumulative mass exceeds
+  // u * retained  == the largest K with mass_ge(K) > target; if rounding leaves
+  // none, the final nucleus member closes the gap.
+  const double u = counter_unit(p.seed, p.sample_index);
+  const double target = u * retained;
+  uint64_t lo = pfloor, hi = best;
+  if (!(mass_ge(lo, pfloor) > target)) {
+    hi = lo;
+  } else {
+    while (lo < hi) {
+      const uint64_t mid = lo + (hi - lo + 1) / 2;
+      if (mass_ge(mid, pfloor) > target) lo = mid; else hi = mid - 1;
+    }
+  }
+  // `lo` is a key threshold; the selected token is the smallest existing key >= lo.
+  uint64_t sel = ~0ull;
+  for (int i = threadIdx.x; i < V; i += NT) {
+    const uint64_t k = ckey(row[i], i);
+    if (k >= lo && k < sel) sel = k;
+  }
+  // block min via max of complements
+  sel = ~block_max_u64<NT>(~sel, shk);
+  if (threadIdx.x == 0) {
+    out_tok[r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(sel & 0xFFFFFFFFull));
+    if (status) status[r] = 0;
+  }
+}
+
+void sample(const float* logits, int64_t ld, int R, int V, const SampleParams* params, int32_t* out, int32_t* status,
+            cudaStream_t s) {
+  if (R <= 0) return;
+  sample_kernel<512><<<R, 512, 0, s>>>(logits, ld, V, params, out, status);
+}
+
+double host_counter_unit(uint64_t seed, int64_t idx) { return counter_unit(seed, idx); }
+
+}  // namespace ew
+}  // namespace lf

@@ -1,0 +1,31 @@
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lf {
+namespace ew {
+
+// Per-row sampling parameters, laid out for a single H2D copy per step.
+struct SampleParams {
+  int32_t mode;          // 0 greedy, 1 stochastic
+  int32_t top_k;         // <= 0: disabled
+  float temperature;     // > 0 for stochastic rows
+  float top_p;           // (0, 1]; >= 1 disables
+  uint64_t seed;         // non-zero request seed
+  int64_t sample_index;  // index of the token being drawn (output position)
+};
+static_assert(sizeof(SampleParams) == 32, "SampleParams is a 32-byte wire record");
+
+void embed(const int32_t* ids, const void* table, void* out, int T, int H, int vocab, cudaStream_t s);
+void rmsnorm(const void* x, void* residual, const void* w, void* out, int T, int H, float eps, cudaStream_t s);
+void rope_kv_write(void* qkv, int64_t ld, const int32_t* positions, const int32_t* slots, const void* cos_sin,
+                   void* kcache, void* vcache, int T, int Hq, int Hkv, int D, int page, int max_pos,
+                   int64_t num_slots, cudaStream_t s);
+void swiglu(const void* gu, void* out, int T, int F, cudaStream_t s);
+void argmax(const float* logits, int64_t ld, int R, int V, int32_t* out, int32_t* status, cudaStream_t s);
+void sample(const float* logits, int64_t ld, int R, int V, const SampleParams* params, int32_t* out, int32_t* status,
+            cudaStream_t s);
+double host_counter_unit(uint64_t seed, int64_t idx);
+
+}  // namespace ew
+}  // namespace lf

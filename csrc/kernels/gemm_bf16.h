@@ -1,0 +1,27 @@
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lf {
+namespace gemm {
+
+struct GemmArgs {
+  const void* A;   // [M, K] bf16, row stride lda (elements)
+  const void* B;   // [N, K] bf16, row stride ldb (elements)
+  void* D;         // [M, N] (bf16 or fp32), row stride ldd; [M, N/2] for SwiGLU
+  int M, N, K;
+  int64_t lda, ldb, ldd;
+};
+
+// epi: 0 = bf16 store, 1 = fp32 store, 2 = SwiGLU (gate/up rows interleaved in
+// groups of 64: 32 gate rows then the matching 32 up rows).  bn = 0 picks a tile width from the shape.
+void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream);
+int choose_bn(int M, int N, int epi);
+
+CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
+                         uint64_t cols, uint64_t ld_elems, uint32_t box_rows, uint32_t box_cols,
+                         CUtensorMapSwizzle swizzle);
+
+}  // namespace gemm
+}  // namespace lf

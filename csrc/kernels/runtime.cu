@@ -1,0 +1,60 @@
+// Host side of the device error word.  Kernels never trap: they record a code
+// in their translation unit's error word and return, so a failed wait or a
+// bad index leaves the CUDA context usable and the host decides what to do
+// with the step.  This file folds the per-translation-unit words together.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace lf {
+namespace rt {
+
+namespace {
+struct Hooks {
+  ErrReadFn read;
+  ErrInjectFn inject;
+};
+std::vector<Hooks>& hooks() {
+  static std::vector<Hooks> h;
+  return h;
+}
+std::mutex& hooks_mu() {
+  static std::mutex m;
+  return m;
+}
+}  // namespace
+
+void register_error_word(ErrReadFn read, ErrInjectFn inject) {
+  std::lock_guard<std::mutex> g(hooks_mu());
+  hooks().push_back({read, inject});
+}
+
+ErrorState read_error(cudaStream_t s, bool clear) {
+  ErrorState st{0, 0};
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("lunaflux: stream sync: ") + cudaGetErrorString(e));
+  std::lock_guard<std::mutex> g(hooks_mu());
+  for (auto& h : hooks()) {
+    unsigned long long info = 0;
+    int code = h.read(clear, &info);
+    if (code != 0 && st.code == 0) {
+      st.code = code;
+      st.info = info;
+    }
+  }
+  return st;
+}
+
+void inject_error(int code) {
+  std::lock_guard<std::mutex> g(hooks_mu());
+  if (!hooks().empty()) hooks().front().inject(code);
+}
+
+}  // namespace rt
+}  // namespace lf

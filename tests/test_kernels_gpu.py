@@ -1,0 +1,280 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def C():
+    from lunaflux_b200.ops import _ext
+    return _ext.load()
+
+
+def _close(a, b, atol, rtol, what):
+    err = (a.float() - b.float()).abs()
+    tol = atol + rtol * b.float().abs()
+    bad = (err > tol).sum().item()
+    assert bad == 0, f"{what}: {bad} / {err.numel()} elements off, max err {err.max().item():.4g}"
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (7, 512, 128), (128, 1024, 4096), (300, 6144, 4096),
+                                   (1024, 4096, 1024), (129, 32, 8), (256, 14336 * 2 // 8, 4096)])
+@pytest.mark.parametrize("bn", [0, 32, 64, 128, 256])
+def test_gemm_bf16(C, M, N, K, bn):
+    if bn and N % bn:
+        pytest.skip("N not a multiple of BN")
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    D = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, D, 0, bn)
+    ref = A.float() @ B.float().t()
+    _close(D, ref, 2e-2, 2e-2, f"gemm {M}x{N}x{K} bn={bn}")
+    D32 = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    C.gemm(A, B, D32, 1, bn)
+    _close(D32, ref, 1e-3, 1e-3, f"gemm fp32 {M}x{N}x{K} bn={bn}")
+
+
+def test_gemm_strided_a(C):
+    A_full = torch.randn(64, 3 * 256, device="cuda").bfloat16()
+    A = A_full[:, 256:512]
+    B = torch.randn(128, 256, device="cuda").bfloat16() * 0.1
+    D = torch.empty(64, 128, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, D, 0, 0)
+    _close(D, A.float() @ B.float().t(), 2e-2, 2e-2, "strided gemm")
+
+
+@pytest.mark.parametrize("M,F,K", [(5, 256, 128), (200, 1792, 4096), (1024, 512, 512)])
+@pytest.mark.parametrize("bn", [0, 64, 128, 256])
+def test_gemm_swiglu(C, M, F, K, bn):
+    if bn and (2 * F) % bn:
+        pytest.skip("shape")
+    Wg = torch.randn(F, K, device="cuda") * 0.05
+    Wu = torch.randn(F, K, device="cuda") * 0.05
+    # interleave in groups of 32 rows: [g0..g31, u0..u31, g32..]
+    W = torch.stack([Wg.view(F // 32, 32, K), Wu.view(F // 32, 32, K)], 1).reshape(2 * F, K).bfloat16()
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    out = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+    C.gemm(x, W, out, 2, bn)
+    g = x.float() @ Wg.bfloat16().float().t()
+    u = x.float() @ Wu.bfloat16().float().t()
+    ref = torch.nn.functional.silu(g) * u
+    _close(out, ref, 3e-2, 3e-2, "swiglu gemm")
+
+
+@pytest.mark.parametrize("H", [64, 4096, 8192])
+def test_rmsnorm(C, H):
+    T = 37
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    r = torch.randn(T, H, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16()
+    out = torch.empty_like(x)
+    C.rmsnorm(x, None, w, out, 1e-5)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+    _close(out, ref, 2e-2, 2e-2, "rmsnorm")
+    r2 = r.clone()
+    C.rmsnorm(x, r2, w, out, 1e-5)
+    s = (x.float() + r.float()).bfloat16().float()
+    _close(r2, s, 1e-6, 0, "residual")
+    ref = s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+    _close(out, ref, 2e-2, 2e-2, "rmsnorm+residual")
+
+
+def test_embed(C):
+    E = torch.randn(1000, 256, device="cuda").bfloat16()
+    ids = torch.randint(0, 1000, (33,), device="cuda", dtype=torch.int32)
+    out = torch.empty(33, 256, device="cuda", dtype=torch.bfloat16)
+    C.embed(ids, E, out)
+    assert torch.equal(out, E[ids.long()])
+
+
+def rope_table(max_pos, D, theta):
+    inv = 1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.float64) / D))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None]
+    return torch.stack([ang.cos(), ang.sin()], -1).float()
+
+
+def ref_rope(x, pos, table):
+    D = x.shape[-1]
+    cs = table[pos.long()]
+    c, s = cs[..., 0][:, None, :], cs[..., 1][:, None, :]
+    x1, x2 = x[..., : D // 2], x[..., D // 2:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], -1)
+
+
+def test_rope_kv_write(C):
+    T, Hq, Hkv, D, P = 20, 8, 2, 128, 16
+    pages = 10
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+    pos = torch.randint(0, 500, (T,), device="cuda", dtype=torch.int32)
+    slots = torch.randperm(pages * P, device="cuda")[:T].int()
+    table = rope_table(1024, D, 500000.0).cuda()
+    kc = torch.zeros(pages, Hkv, P, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q0 = qkv.clone()
+    C.rope_kv_write(qkv, pos, slots, table, kc, vc, Hq, Hkv, P)
+    q = q0[:, : Hq * D].float().view(T, Hq, D)
+    k = q0[:, Hq * D:(Hq + Hkv) * D].float().view(T, Hkv, D)
+    v = q0[:, (Hq + Hkv) * D:].view(T, Hkv, D)
+    _close(qkv[:, : Hq * D].view(T, Hq, D), ref_rope(q, pos, table.cuda()), 2e-2, 2e-2, "rope q")
+    kr = ref_rope(k, pos, table.cuda())
+    pg, off = (slots // P).long(), (slots % P).long()
+    _close(kc[pg, :, off], kr, 2e-2, 2e-2, "k cache")
+    assert torch.equal(vc[pg, :, off], v)
+
+
+def make_paged(rows_lens, Hkv, D, P, extra_pages=7, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    n_pages = [math.ceil(L / P) for L in rows_lens]
+    total = sum(n_pages) + extra_pages + 1
+    perm = torch.randperm(total - 1, generator=g) + 1  # page 0 is the reserved zero page
+    kc = torch.randn(total, Hkv, P, D, generator=g).bfloat16()
+    vc = torch.randn(total, Hkv, P, D, generator=g).bfloat16()
+    kc[0] = 0
+    vc[0] = 0
+    maxp = max(n_pages)
+    bt = torch.zeros(len(rows_lens), maxp + 3, dtype=torch.int32)
+    i = 0
+    for r, n in enumerate(n_pages):
+        bt[r, :n] = perm[i:i + n].int()
+        i += n
+    return kc.cuda(), vc.cuda(), bt.cuda()
+
+
+def ref_attention(q, kc, vc, bt, L, qpos, Hq, Hkv):
+    """q [nq, Hq, D] for one row at absolute positions qpos; full causal softmax in fp32."""
+    D, P = kc.shape[-1], kc.shape[2]
+    n = math.ceil(L / P)
+    pages = bt[:n].long()
+    K = kc[pages].float().permute(1, 0, 2, 3).reshape(Hkv, n * P, D)[:, :L]
+    V = vc[pages].float().permute(1, 0, 2, 3).reshape(Hkv, n * P, D)[:, :L]
+    G = Hq // Hkv
+    K = K.repeat_interleave(G, 0)
+    V = V.repeat_interleave(G, 0)
+    s = torch.einsum("qhd,hkd->hqk", q.float(), K) / math.sqrt(D)
+    mask = torch.arange(L, device=q.device)[None, :] > qpos[:, None]
+    s = s.masked_fill(mask[None], float("-inf"))
+    p = s.softmax(-1)
+    return torch.einsum("hqk,hkd->qhd", p, V)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (8, 8), (64, 8), (4, 1)])
+@pytest.mark.parametrize("splits", [1, 2, 5])
+def test_attn_decode(C, Hq, Hkv, splits):
+    D, P = 128, 16
+    lens = [1, 15, 16, 17, 100, 1025, 333]
+    kc, vc, bt = make_paged(lens, Hkv, D, P)
+    R = len(lens)
+    T = R + 3
+    q = torch.randn(T, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+    tok = torch.tensor([3, 0, 1, 2, 4, 5, 6], device="cuda", dtype=torch.int32)[:R]
+    out = torch.zeros(T, Hq * D, device="cuda", dtype=torch.bfloat16)
+    sl = torch.tensor(lens, device="cuda", dtype=torch.int32)
+    po = torch.empty(R * Hq * splits * D, device="cuda")
+    pl = torch.empty(R * Hq * splits, device="cuda")
+    C.attn_decode(q, out, tok, sl, bt, kc, vc, Hq, Hkv, splits, po, pl)
+    assert C.read_error(True)[0] == 0
+    for r, L in enumerate(lens):
+        t = tok[r].item()
+        qq = q[t, : Hq * D].view(1, Hq, D)
+        ref = ref_attention(qq, kc, vc, bt[r], L, torch.tensor([L - 1], device="cuda"), Hq, Hkv)
+        _close(out[t].view(Hq, D), ref[0], 2e-2, 2e-2, f"decode row {r} L={L}")
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (16, 16), (8, 1)])
+def test_attn_prefill(C, Hq, Hkv):
+    D, P = 128, 16
+    # (query chunk length, total kv length) per row: fresh prompts and later chunks
+    rows = [(5, 5), (64, 64), (65, 200), (130, 130), (1, 17), (200, 1000)]
+    lens = [L for _, L in rows]
+    kc, vc, bt = make_paged(lens, Hkv, D, P, seed=1)
+    qls = [ql for ql, _ in rows]
+    qs = torch.tensor([0] + list(torch.tensor(qls).cumsum(0)), dtype=torch.int32, device="cuda")
+    T = sum(qls)
+    q = torch.randn(T, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+    out = torch.zeros(T, Hq * D, device="cuda", dtype=torch.bfloat16)
+    sl = torch.tensor(lens, device="cuda", dtype=torch.int32)
+    C.attn_prefill(q, out, qs, sl, bt, kc, vc, Hq, Hkv, max(qls))
+    assert C.read_error(True)[0] == 0
+    for r, (ql, L) in enumerate(rows):
+        s0 = qs[r].item()
+        qq = q[s0:s0 + ql, : Hq * D].view(ql, Hq, D)
+        qpos = torch.arange(L - ql, L, device="cuda")
+        ref = ref_attention(qq, kc, vc, bt[r], L, qpos, Hq, Hkv)
+        _close(out[s0:s0 + ql].view(ql, Hq, D), ref, 2e-2, 2e-2, f"prefill row {r}")
+
+
+def test_argmax(C):
+    R, V = 9, 128256
+    logits = torch.randn(R, V, device="cuda")
+    logits[3, 77] = 50.0
+    logits[3, 99] = 50.0  # tie: lowest id wins
+    out = torch.empty(R, device="cuda", dtype=torch.int32)
+    st = torch.empty(R, device="cuda", dtype=torch.int32)
+    C.argmax(logits, out, st)
+    exp = logits.argmax(-1)
+    exp[3] = 77
+    assert torch.equal(out.long(), exp)
+    assert int(st.abs().sum()) == 0
+
+
+def _params(rows):
+    import numpy as np
+    dt = np.dtype([("mode", "<i4"), ("top_k", "<i4"), ("temperature", "<f4"), ("top_p", "<f4"),
+                   ("seed", "<u8"), ("sample_index", "<i8")])
+    a = np.zeros(len(rows), dtype=dt)
+    for i, r in enumerate(rows):
+        a[i] = r
+    return torch.from_numpy(a.view(np.uint8).copy()).cuda()
+
+
+def _host_sample(logits, temperature, top_k, top_p, u):
+    """fp64 restatement of the reference sampler (sampling/stochastic.mbt)."""
+    l = logits.double().cpu()
+    order = sorted(range(l.numel()), key=lambda i: (-l[i].item(), i))
+    if top_k > 0:
+        order = order[:top_k]
+    mx = l[order[0]].item()
+    w = [math.exp((l[i].item() - mx) / temperature) for i in order]
+    total = sum(w)
+    cnt = len(order)
+    if 0 < top_p < 1:
+        thr, cum, cnt = top_p * total, 0.0, 0
+        while cnt < len(order) and cum < thr:
+            cum += w[cnt]
+            cnt += 1
+        cnt = max(cnt, 1)
+    ret = sum(w[:cnt])
+    target, cum = u * ret, 0.0
+    for j in range(cnt):
+        cum += w[j]
+        if cum > target:
+            return order[j]
+    return order[cnt - 1]
+
+
+def test_sample_matches_host_replay(C):
+    V = 3000
+    g = torch.Generator(device="cpu").manual_seed(3)
+    logits = (torch.randn(6, V, generator=g) * 3).cuda()
+    rows = [(1, 0, 0.7, 0.9, 11, 0), (1, 50, 1.0, 1.0, 12, 5), (1, 0, 1.3, 0.5, 13, 9),
+            (0, 0, 1.0, 1.0, 14, 0), (1, 1, 0.5, 1.0, 15, 2), (1, 200, 0.8, 0.95, 16, 100)]
+    out = torch.empty(6, device="cuda", dtype=torch.int32)
+    C.sample(logits, _params(rows), out, None)
+    for i, (mode, k, t, p, seed, idx) in enumerate(rows):
+        if mode == 0:
+            assert out[i].item() == logits[i].argmax().item()
+            continue
+        u = C.counter_unit(seed, idx)
+        assert out[i].item() == _host_sample(logits[i], t, k, p, u), f"row {i}"
+
+
+def test_error_word_roundtrip(C):
+    assert C.read_error(True)[0] == 0
+    C.inject_error(5)
+    assert C.read_error(True)[0] == 5
+    assert C.read_error(True)[0] == 0
