@@ -25,7 +25,8 @@ void check_rowmajor(const at::Tensor& t, const char* name) {
 
 cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
-void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, int64_t epi, int64_t bn) {
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, int64_t epi, int64_t bn,
+          c10::optional<at::Tensor> ws) {
   check_cuda(A, "A");
   check_cuda(B, "B");
   check_cuda(D, "D");
@@ -44,7 +45,19 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, int64_t epi, 
   }
   c10::cuda::CUDAGuard g(A.device());
   lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), B.stride(0), D.stride(0)};
-  lf::gemm::run(a, (int)epi, (int)bn, stream());
+  float* wsp = nullptr;
+  int64_t ws_elems = 0;
+  if (ws.has_value()) {
+    LF_CHECK(ws->is_cuda() && ws->scalar_type() == at::kFloat && ws->is_contiguous(), "gemm workspace must be fp32");
+    wsp = ws->data_ptr<float>();
+    ws_elems = ws->numel();
+  }
+  lf::gemm::run(a, (int)epi, (int)bn, stream(), wsp, ws_elems);
+}
+
+int64_t gemm_plan_splitk(int64_t M, int64_t N, int64_t K) {
+  int kb = 0;
+  return lf::gemm::plan_splitk(M, N, K, &kb);
 }
 
 int64_t gemm_choose_bn(int64_t M, int64_t N, int64_t epi) { return lf::gemm::choose_bn(M, N, epi); }
@@ -196,7 +209,9 @@ double counter_unit(uint64_t seed, int64_t idx) { return lf::ew::host_counter_un
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "LunaFlux sm_100a kernels";
-  m.def("gemm", &gemm, "D = A @ B^T on tcgen05 (epi 0 bf16, 1 fp32, 2 SwiGLU)");
+  m.def("gemm", &gemm, "D = A @ B^T on tcgen05 (epi 0 bf16, 1 fp32, 2 SwiGLU)", py::arg("A"), py::arg("B"),
+        py::arg("D"), py::arg("epi") = 0, py::arg("bn") = 0, py::arg("ws") = py::none());
+  m.def("gemm_plan_splitk", &gemm_plan_splitk);
   m.def("gemm_choose_bn", &gemm_choose_bn);
   m.def("embed", &embed);
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"));

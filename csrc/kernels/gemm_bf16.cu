@@ -41,7 +41,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;                 // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;
 
-enum Epi : int { kStoreBf16 = 0, kStoreF32 = 1, kSwiGLU = 2 };
+enum Epi : int { kStoreBf16 = 0, kStoreF32 = 1, kSwiGLU = 2, kSplitF32 = 3 };
 
 template <int BN, int STAGES>
 struct Smem {
@@ -62,7 +62,7 @@ template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M,
-                     int N, int K, int ldd) {
+                     int N, int K, int ldd, int splits, int kb_per_split) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -77,6 +77,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_m = (M + BM - 1) / BM;
   const int num_n = N / BN;
   const int num_tiles = num_m * num_n;
+  const int num_units = num_tiles * splits;
   const int num_kb = (K + BK - 1) / BK;
   constexpr uint32_t kCols = tmem_cols<BN>();
 
@@ -108,10 +109,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+        const int tile = unit % num_tiles;
+        const int kb0 = (unit / num_tiles) * kb_per_split;
+        const int kb1 = min(num_kb, kb0 + kb_per_split);
         const int m0 = (tile % num_m) * BM;
         const int n0 = (tile / num_m) * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, 1)) { ok = false; break; }
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
@@ -129,13 +133,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x, ++local) {
+        const int kb0 = (unit / num_tiles) * kb_per_split;
+        const int kb1 = min(num_kb, kb0 + kb_per_split);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, 3)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
@@ -143,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             umma_f16_ss(d_tmem, sw128_kmajor_desc(sa + kk * 32), sw128_kmajor_desc(sb + kk * 32),
-                        idesc, (kb | kk) != 0);
+                        idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -155,7 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Epilogue warps 2..5 -> TMEM lane quadrant (warp % 4).
     const int quad = warp & 3;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++local) {
+      const int tile = unit % num_tiles;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, 4)) break;
@@ -201,6 +208,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
               for (int j = 0; j < 8; ++j) d4[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            } else if constexpr (EPI == kSplitF32) {
+              // Split-K partial: vector fp32 reduction into the (L2-resident) workspace.
+              float* dst = reinterpret_cast<float*>(out) + (size_t)row * ldd + n0 + c;
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * j),
+                             "f"(__uint_as_float(r[4 * j])), "f"(__uint_as_float(r[4 * j + 1])),
+                             "f"(__uint_as_float(r[4 * j + 2])), "f"(__uint_as_float(r[4 * j + 3]))
+                             : "memory");
             } else {
               uint32_t packed[16];
 #pragma unroll
@@ -225,6 +241,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kCols);
+  }
+}
+
+// Split-K finalisation: read the fp32 sums, write the real output (bf16,
+// fp32 or SwiGLU of the interleaved gate/up columns) and zero the workspace
+// so the next split-K GEMM can accumulate into it again.
+template <int EPI>
+__global__ void splitk_finalize_kernel(float* __restrict__ ws, void* __restrict__ out, int M, int N, int64_t ldd) {
+  const int row = blockIdx.y;
+  if (EPI == kSwiGLU) {
+    const int half = N / 2;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < half; j += gridDim.x * blockDim.x) {
+      const int grp = j >> 5, off = j & 31;
+      float* pg = ws + (size_t)row * N + grp * 64 + off;
+      const float g = pg[0], u = pg[32];
+      pg[0] = 0.f;
+      pg[32] = 0.f;
+      reinterpret_cast<__nv_bfloat16*>(out)[(size_t)row * ldd + j] = __float2bfloat16(silu(g) * u);
+    }
+  } else {
+    for (int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4; j < N; j += gridDim.x * blockDim.x * 4) {
+      float4* p = reinterpret_cast<float4*>(ws + (size_t)row * N + j);
+      const float4 v = *p;
+      *p = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (EPI == kStoreF32) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)row * ldd + j) = v;
+      } else {
+        uint2 pk = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + j) = pk;
+      }
+    }
   }
 }
 
@@ -310,7 +357,7 @@ static int num_sms() {
 }
 
 template <int BN, int STAGES, int EPI>
-static void launch(const GemmArgs& a, cudaStream_t stream) {
+static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int kb_per = 0, float* ws = nullptr) {
   using S = Smem<BN, STAGES>;
   auto kfn = gemm_bf16_kernel<BN, STAGES, EPI>;
   static bool attr_set = false;
@@ -320,9 +367,32 @@ static void launch(const GemmArgs& a, cudaStream_t stream) {
   }
   CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
   CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, BN);
-  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
+  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN) * splits;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd);
+  if (kb_per <= 0) kb_per = (a.K + BK - 1) / BK;
+  if (EPI == kSplitF32) {
+    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, ws, a.M, a.N, a.K, a.N, splits, kb_per);
+  } else {
+    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, splits, kb_per);
+  }
+}
+
+// Split-K plan for skinny GEMMs: 256-wide tiles (so the activations are
+// re-read from L2 as few times as possible) and enough K-splits to cover the
+// SMs, each split at least 4 k-blocks.  Returns splits (1 = no split).
+int plan_splitk(int M, int N, int K, int* kb_per_out) {
+  const int sms = num_sms();
+  const int num_m = (M + BM - 1) / BM;
+  const int num_kb = (K + BK - 1) / BK;
+  if (N % 256 != 0) return 1;
+  const int tiles = num_m * (N / 256);
+  if (tiles >= sms / 2) return 1;
+  int splits = (sms + tiles - 1) / tiles;
+  if (splits > num_kb / 4) splits = num_kb / 4;
+  if (splits < 2) return 1;
+  const int kb_per = (num_kb + splits - 1) / splits;
+  *kb_per_out = kb_per;
+  return (num_kb + kb_per - 1) / kb_per;
 }
 
 // Tile-width choice: the widest BN that still yields enough tiles to cover
@@ -344,8 +414,21 @@ int choose_bn(int M, int N, int epi) {
   return 0;
 }
 
-void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream) {
+void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws, int64_t ws_elems) {
   if (a.M <= 0) return;
+  if (ws != nullptr && bn == 0 && (int64_t)a.M * a.N <= ws_elems && (a.N % 256) == 0) {
+    int kb_per = 0;
+    const int splits = plan_splitk(a.M, a.N, a.K, &kb_per);
+    if (splits > 1) {
+      if (a.K % 8 != 0) throw std::runtime_error("lunaflux gemm: K must be a multiple of 8");
+      launch<256, 4, kSplitF32>(a, stream, splits, kb_per, ws);
+      dim3 grid((a.N + 1023) / 1024, a.M);
+      if (epi == kSwiGLU) splitk_finalize_kernel<kSwiGLU><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd);
+      else if (epi == kStoreF32) splitk_finalize_kernel<kStoreF32><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd);
+      else splitk_finalize_kernel<kStoreBf16><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd);
+      return;
+    }
+  }
   if (bn == 0) bn = choose_bn(a.M, a.N, epi);
   if (bn == 0 || a.N % bn != 0) throw std::runtime_error("lunaflux gemm: N must be a multiple of 32");
   if (a.K % 8 != 0) throw std::runtime_error("lunaflux gemm: K must be a multiple of 8");

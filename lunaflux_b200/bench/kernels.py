@@ -1,0 +1,185 @@
+"""Kernel micro-benchmarks: each hot sm_100a kernel against its library baseline.
+
+    python -m lunaflux_b200.bench.kernels [--only gemm|attn|norm] [--json out.json]
+
+Timing: CUDA events on the launching stream, warm-up first, an L2 flush (a
+256 MB write) before every timed launch, median of the timed launches.  The
+roofline denominators come from MEASURED_PEAKS.json when present.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+
+import torch
+
+from lunaflux_b200.ops import _ext
+
+_FLUSH = None
+
+
+def _flush():
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 * 1024 * 1024 // 4, device="cuda", dtype=torch.float32)
+    _FLUSH.fill_(1.0)
+
+
+def time_fn(fn, iters=10, warmup=3, flush=True):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        if flush:
+            _flush()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
+def peaks():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def bench_gemm(C, results):
+    hbm, tflops_peak, src = peaks()
+    shapes = [
+        ("prefill qkv", 8192, 6144, 4096, 0), ("prefill o", 8192, 4096, 4096, 0),
+        ("prefill gate_up+swiglu", 8192, 28672, 4096, 2), ("prefill down", 8192, 4096, 14336, 0),
+        ("decode256 qkv", 256, 6144, 4096, 0), ("decode256 o", 256, 4096, 4096, 0),
+        ("decode256 gate_up+swiglu", 256, 28672, 4096, 2), ("decode256 down", 256, 4096, 14336, 0),
+        ("decode256 lm_head", 256, 128256, 4096, 1), ("decode64 qkv", 64, 6144, 4096, 0),
+        ("decode1 down", 1, 4096, 14336, 0), ("tp8 decode256 gate_up", 256, 3584, 4096, 2),
+        ("square 8192", 8192, 8192, 8192, 0),
+    ]
+    for name, M, N, K, epi in shapes:
+        A = torch.randn(M, K, device="cuda").bfloat16()
+        B = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+        if epi == 2:
+            D = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
+        elif epi == 1:
+            D = torch.empty(M, N, device="cuda", dtype=torch.float32)
+        else:
+            D = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        ws = torch.zeros(512 * 32768, device="cuda")
+        ours = time_fn(lambda: C.gemm(A, B, D, epi, 0, ws))
+        if epi == 2:
+            def base():
+                gu = A @ B.t()
+                torch.nn.functional.silu(gu[:, : N // 2]) * gu[:, N // 2:]
+        elif epi == 1:
+            def base():
+                torch.matmul(A, B.t(), out=None).float()
+        else:
+            def base():
+                A @ B.t()
+        ref = time_fn(base)
+        flops = 2.0 * M * N * K
+        bytes_ = 2.0 * (M * K + N * K) + D.numel() * D.element_size()
+        t_roof = max(flops / (tflops_peak * 1e12), bytes_ / (hbm * 1e9)) * 1e3
+        r = dict(kernel="gemm_bf16", case=name, M=M, N=N, K=K, bn=C.gemm_choose_bn(M, N, epi),
+                 splitk=C.gemm_plan_splitk(M, N, K), ours_ms=ours,
+                 torch_ms=ref, speedup=ref / ours, tflops=flops / ours / 1e9, roofline_ms=t_roof,
+                 frac_of_roofline=t_roof / ours, peaks=src)
+        results.append(r)
+        print(json.dumps(r))
+        del A, B, D
+
+
+def bench_attn(C, results):
+    hbm, _, src = peaks()
+    D, P = 128, 16
+    for rows, L, Hq, Hkv in [(256, 1152, 32, 8), (64, 2048, 32, 8), (1, 4096, 32, 8), (128, 2304, 8, 1)]:
+        pages_per = math.ceil(L / P)
+        n_pages = rows * pages_per + 1
+        kc = torch.randn(n_pages, Hkv, P, D, device="cuda").bfloat16()
+        vc = torch.randn_like(kc)
+        bt = (torch.randperm(n_pages - 1, device="cuda")[: rows * pages_per] + 1).int().view(rows, pages_per)
+        q = torch.randn(rows, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+        out = torch.empty(rows, Hq * D, device="cuda", dtype=torch.bfloat16)
+        tok = torch.arange(rows, device="cuda", dtype=torch.int32)
+        sl = torch.full((rows,), L, device="cuda", dtype=torch.int32)
+        splits = C.attn_decode_splits(rows, Hkv, L, torch.cuda.get_device_properties(0).multi_processor_count)
+        po = torch.empty(rows * Hq * splits * D, device="cuda")
+        pl = torch.empty(rows * Hq * splits, device="cuda")
+        ms = time_fn(lambda: C.attn_decode(q, out, tok, sl, bt, kc, vc, Hq, Hkv, splits, po, pl))
+        kv_bytes = rows * L * Hkv * D * 2 * 2
+        r = dict(kernel="attn_decode", rows=rows, seq=L, Hq=Hq, Hkv=Hkv, splits=splits, ours_ms=ms,
+                 gbs=kv_bytes / ms / 1e6, frac_of_hbm=kv_bytes / ms / 1e6 / hbm, peaks=src)
+        results.append(r)
+        print(json.dumps(r))
+    # prefill: 8 prompts x 1024 tokens, causal
+    for nreq, L, Hq, Hkv in [(8, 1024, 32, 8), (2, 4096, 32, 8)]:
+        pages_per = math.ceil(L / P)
+        n_pages = nreq * pages_per + 1
+        kc = torch.randn(n_pages, Hkv, P, D, device="cuda").bfloat16()
+        vc = torch.randn_like(kc)
+        bt = (torch.randperm(n_pages - 1, device="cuda")[: nreq * pages_per] + 1).int().view(nreq, pages_per)
+        T = nreq * L
+        q = torch.randn(T, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+        out = torch.empty(T, Hq * D, device="cuda", dtype=torch.bfloat16)
+        qs = torch.arange(0, T + 1, L, device="cuda", dtype=torch.int32)
+        sl = torch.full((nreq,), L, device="cuda", dtype=torch.int32)
+        ms = time_fn(lambda: C.attn_prefill(q, out, qs, sl, bt, kc, vc, Hq, Hkv, L))
+        flops = nreq * Hq * 4.0 * D * L * L / 2
+        qf = q[:, : Hq * D].view(nreq, L, Hq, D).transpose(1, 2)
+        kf = torch.randn(nreq, Hkv, L, D, device="cuda").bfloat16().repeat_interleave(Hq // Hkv, 1)
+        vf = torch.randn_like(kf)
+        base = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(qf, kf, vf, is_causal=True))
+        r = dict(kernel="attn_prefill", nreq=nreq, seq=L, ours_ms=ms, sdpa_dense_ms=base, tflops=flops / ms / 1e9,
+                 peaks=src)
+        results.append(r)
+        print(json.dumps(r))
+
+
+def bench_norm(C, results):
+    hbm, _, src = peaks()
+    for T, H in [(8192, 4096), (256, 4096), (8192, 8192)]:
+        x = torch.randn(T, H, device="cuda").bfloat16()
+        res = torch.randn_like(x)
+        w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+        out = torch.empty_like(x)
+        ms = time_fn(lambda: C.rmsnorm(x, res, w, out, 1e-5))
+        byts = 4 * T * H * 2
+        r = dict(kernel="rmsnorm_residual", T=T, H=H, ours_ms=ms, gbs=byts / ms / 1e6, frac_of_hbm=byts / ms / 1e6 / hbm,
+                 peaks=src)
+        results.append(r)
+        print(json.dumps(r))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="")
+    ap.add_argument("--json", default="")
+    args = ap.parse_args()
+    C = _ext.load()
+    results = []
+    if args.only in ("", "gemm"):
+        bench_gemm(C, results)
+    if args.only in ("", "attn"):
+        bench_attn(C, results)
+    if args.only in ("", "norm"):
+        bench_norm(C, results)
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(results, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

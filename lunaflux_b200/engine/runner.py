@@ -1,0 +1,279 @@
+"""Per-rank model runner: weights, paged KV arena, static workspace, the
+decoder forward over an operator set, and CUDA-graph capture of decode steps.
+
+Reference counterparts: engine/device_step (PagedGraphExecutor: stage ->
+execute -> sample_completion -> finish; paged_executor_prepare.mbt:292),
+engine/device_memory (one activation arena reused by every step),
+kv/device_arena (one allocation for the whole KV arena, prepare.mbt:66).
+Differences by design: no per-launch synchronisation (the reference calls
+cuStreamSynchronize after every launch, internal/cuda/launch.c:146-161); the
+whole decode step is one CUDA-graph replay per batch bucket; sampling runs on
+the device and only the sampled int32 ids come back to the host.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from ..models.spec import LlamaSpec
+from ..models.weights import ModelWeights
+from ..scheduler.scheduler import StepPlan
+from .step_inputs import HostStep, build_host_step, device_views, make_layout
+
+
+class StepFailed(RuntimeError):
+    def __init__(self, code: int, info: int):
+        super().__init__(f"device error {code} (info {info})")
+        self.code = code
+        self.info = info
+
+
+def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None]
+    return torch.stack([ang.cos(), ang.sin()], -1).float().contiguous().to(device)
+
+
+class ModelRunner:
+    def __init__(self, weights: ModelWeights, ops, device, num_pages: int, max_tokens: int, max_rows: int,
+                 max_context: int, page: int = 16, graph_sizes: Sequence[int] = (), comm=None,
+                 check_errors_every: int = 16):
+        self.w = weights
+        self.spec: LlamaSpec = weights.spec
+        self.shard = weights.shard
+        self.ops = ops
+        self.device = torch.device(device)
+        self.comm = comm
+        self.P = page
+        self.max_tokens = max_tokens
+        self.max_rows = max_rows
+        self.max_context = max_context
+        self.W = -(-max_context // page)
+        self.num_pages = num_pages + 1          # physical page 0 is the reserved zero page
+        self.check_every = check_errors_every
+        s, sh = self.spec, self.shard
+        dt = weights.embed.dtype
+        self.dtype = dt
+        self.Hq, self.Hkv, self.D = sh.heads, sh.kv_heads, s.head_dim
+        H = s.hidden
+        dev = self.device
+        # KV arena: [layer][K/V][page][kv_head][16][D]
+        self.kv = torch.zeros(s.layers, 2, self.num_pages, self.Hkv, page, self.D, dtype=dt, device=dev)
+        self.cos_sin = rope_table(s.max_position, s.head_dim, s.rope_theta, dev)
+        T, R = max_tokens, max_rows
+        self.resid = torch.empty(T, H, dtype=dt, device=dev)
+        self.h = torch.empty(T, H, dtype=dt, device=dev)
+        self.delta = torch.empty(T, H, dtype=dt, device=dev)
+        self.qkv = torch.empty(T, sh.qkv_size, dtype=dt, device=dev)
+        self.attn = torch.empty(T, self.Hq * self.D, dtype=dt, device=dev)
+        self.act = torch.empty(T, sh.ffn_padded, dtype=dt, device=dev)
+        self.hs = torch.empty(R, H, dtype=dt, device=dev)
+        self.logits = torch.empty(R, sh.vocab, dtype=torch.float32, device=dev)
+        self.full_logits = (torch.empty(R, s.vocab, dtype=torch.float32, device=dev)
+                            if sh.size > 1 else self.logits)
+        self.out_tok = torch.zeros(R, dtype=torch.int32, device=dev)
+        # split-K GEMM workspace (kept all-zero between GEMMs) and split-KV decode partials
+        self.gemm_ws = torch.zeros(512 * max(32768, sh.qkv_size, 2 * sh.ffn_padded), dtype=torch.float32, device=dev) \
+            if dev.type == "cuda" else None
+        self.max_splits = 32
+        self.part_o = torch.empty(R * self.Hq * self.max_splits * self.D, dtype=torch.float32, device=dev)
+        self.part_lse = torch.empty(R * self.Hq * self.max_splits, dtype=torch.float32, device=dev)
+        # packed step inputs: one device block + two pinned host blocks (double buffer)
+        cap = make_layout(T, R, R, R, self.W).total + 64
+        self.in_dev = torch.zeros(cap, dtype=torch.int32, device=dev)
+        pin = dev.type == "cuda"
+        self.in_host = [torch.zeros(cap, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self.in_evt = [None, None]
+        self.out_host = torch.zeros(R, dtype=torch.int32, pin_memory=pin)
+        self._flip = 0
+        self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: Dict[tuple, int] = {}
+        self.graph_sizes = sorted(b for b in graph_sizes if b <= R)
+        self.stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
+        self.steps = 0
+        # accounting for the bench
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.device_ms = 0.0          # sum over steps of device time from first kernel to sampled ids
+        if dev.type == "cuda":
+            self._ev_begin = torch.cuda.Event(enable_timing=True)
+            self._ev_end = torch.cuda.Event(enable_timing=True)
+
+    # ------------------------------------------------------------------ forward
+    def _layer_kv(self, l):
+        return self.kv[l, 0], self.kv[l, 1]
+
+    def forward(self, v: Dict[str, torch.Tensor], T: int, Tp: int, Rp: int, Rd: int, Rs: int, max_q_len: int,
+                splits: int, stochastic: bool, host_meta=None, gather: bool = True):
+        ops, s, w = self.ops, self.spec, self.w
+        Hq, Hkv = self.Hq, self.Hkv
+        eps = s.rms_eps
+        resid, h, delta = self.resid[:T], self.h[:T], self.delta[:T]
+        qkv, attn, act = self.qkv[:T], self.attn[:T], self.act[:T]
+        ws = self.gemm_ws
+        hm = host_meta or {}
+        ops.embed(v["tokens"], w.embed, resid)
+        for l, lw in enumerate(w.layers):
+            kc, vc = self._layer_kv(l)
+            if l == 0:
+                ops.rmsnorm(resid, None, lw.ln1, h, eps)
+            else:
+                ops.rmsnorm(delta, resid, lw.ln1, h, eps)
+            ops.gemm(h, lw.wqkv, qkv, 0, ws)
+            ops.rope_kv_write(qkv, v["positions"], v["slots"], self.cos_sin, kc, vc, Hq, Hkv, self.P)
+            if Rp:
+                ops.attn_prefill(qkv[:Tp], attn[:Tp], v["p_qstart"], v["p_seqlen"], v["p_bt"], kc, vc, Hq, Hkv,
+                                 max_q_len, host={"q_start": hm.get("q_start"), "seq_lens": hm.get("seq_lens")})
+            if Rd:
+                ops.attn_decode(qkv, attn, v["d_tok"], v["d_seqlen"], v["d_bt"], kc, vc, Hq, Hkv, splits,
+                                self.part_o, self.part_lse,
+                                host={"seq_lens": hm.get("d_seq_lens"), "tok": hm.get("d_tok")})
+            ops.gemm(attn, lw.wo, delta, 0, ws)
+            if self.comm is not None:
+                self.comm.all_reduce(delta)
+            ops.rmsnorm(delta, resid, lw.ln2, h, eps)
+            if s.is_moe:
+                self.moe(h, delta, lw)
+            else:
+                ops.gemm(h, lw.wgu, act, 2, ws)
+                ops.gemm(act, lw.wd, delta, 0, ws)
+                if self.comm is not None:
+                    self.comm.all_reduce(delta)
+        ops.rmsnorm(delta, resid, w.norm, h, eps)
+        if gather:
+            hs = self.hs[:Rs]
+            torch.index_select(h, 0, v["s_idx"].long(), out=hs)
+        else:
+            hs = h[:Rs]
+        logits = self.logits[:Rs]
+        ops.gemm(hs, w.lm_head, logits, 1, ws)
+        if self.comm is not None and self.shard.size > 1:
+            full = self.full_logits[:Rs]
+            self.comm.all_gather_cols(logits, full)
+            logits = full
+        out = self.out_tok[:Rs]
+        if stochastic:
+            ops.sample(logits, v["s_params"], out)
+        else:
+            ops.argmax(logits, out)
+        return out
+
+    def moe(self, h, delta, lw):
+        raise NotImplementedError("MoE layers are served by MoERunner")
+
+    # ------------------------------------------------------------------ one step
+    def _upload(self, hs: HostStep, host_buf: torch.Tensor):
+        n = hs.layout.total
+        if self.device.type == "cuda":
+            self.in_dev[:n].copy_(host_buf[:n], non_blocking=True)
+        else:
+            self.in_dev[:n].copy_(host_buf[:n])
+        self.h2d_bytes += n * 4
+
+    def execute(self, plan: StepPlan, table_matrix: np.ndarray) -> np.ndarray:
+        """Runs one step and returns the sampled token ids (sampling rows, plan order)."""
+        rows = plan.rows
+        decode_only = all(r.decode for r in rows)
+        stoch = any(r.sample and r.req.sampling.mode.value == 1 for r in rows)
+        bucket = None
+        if decode_only and self.graph_sizes and self.device.type == "cuda":
+            nd = len(rows)
+            bucket = next((b for b in self.graph_sizes if b >= nd), None)
+        slot = self._flip
+        self._flip ^= 1
+        if self.in_evt[slot] is not None:
+            self.in_evt[slot].synchronize()  # the previous upload from this pinned block has finished
+        host_buf = self.in_host[slot]
+        hs = build_host_step(plan, table_matrix, self.P, self.W, host_buf.numpy(), bucket=bucket)
+        L = hs.layout
+        Rs_real = sum(1 for r in rows if r.sample)
+        if bucket is not None:
+            key = (bucket, stoch)
+            g = self.graphs.get(key)
+            if g is None:
+                g = self.capture(bucket, stoch)
+            self._upload(hs, host_buf)
+            self._record_upload(slot)
+            self._begin_step()
+            g.replay()
+            self.ops.launches += self.graph_launches[key]
+        else:
+            self._upload(hs, host_buf)
+            self._record_upload(slot)
+            self._begin_step()
+            v = device_views(self.in_dev, L)
+            Tp = L.T - L.Rd
+            splits = self.ops.decode_splits(L.Rd, self.Hkv, max(hs.max_seq, 1)) if L.Rd else 1
+            self.forward(v, L.T, Tp, L.Rp, L.Rd, L.Rs, hs.max_q_len, splits, stoch, hs.host_meta)
+        out = self.out_tok[:Rs_real]
+        if self.device.type == "cuda":
+            self._ev_end.record()
+            self.out_host[:Rs_real].copy_(out, non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            self.device_ms += self._ev_begin.elapsed_time(self._ev_end)
+            res = self.out_host[:Rs_real].numpy().copy()
+        else:
+            res = out.numpy().copy()
+        self.d2h_bytes += Rs_real * 4
+        self.steps += 1
+        if self.check_every and self.steps % self.check_every == 0:
+            self.check_device_errors()
+        return res
+
+    def _begin_step(self):
+        if self.device.type == "cuda":
+            self._ev_begin.record()
+
+    def _record_upload(self, slot):
+        if self.device.type == "cuda":
+            e = torch.cuda.Event()
+            e.record()
+            self.in_evt[slot] = e
+
+    def check_device_errors(self):
+        code, info = self.ops.read_error(True)
+        if code:
+            raise StepFailed(code, info)
+
+    # ------------------------------------------------------------------ graphs
+    def capture(self, bucket: int, stochastic: bool) -> "torch.cuda.CUDAGraph":
+        """Captures the decode step for ``bucket`` rows reading its inputs at
+        the fixed offsets of ``make_layout(bucket, 0, bucket, bucket, W)``."""
+        L = make_layout(bucket, 0, bucket, bucket, self.W)
+        v = device_views(self.in_dev, L)
+        splits = self.ops.decode_splits(bucket, self.Hkv, self.max_context)
+        splits = min(splits, self.max_splits)
+        # inputs for warm-up: every row a padded row (zero page, no KV write)
+        self.in_dev[: L.total].zero_()
+        o, n = L.field("slots")
+        self.in_dev[o:o + n].fill_(-1)
+        o, n = L.field("d_seqlen")
+        self.in_dev[o:o + n].fill_(1)
+        o, n = L.field("d_tok")
+        self.in_dev[o:o + n].copy_(torch.arange(n, dtype=torch.int32, device=self.device))
+        o, n = L.field("s_idx")
+        self.in_dev[o:o + n].copy_(torch.arange(n, dtype=torch.int32, device=self.device))
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.forward(v, bucket, 0, 0, bucket, bucket, 0, splits, stochastic, gather=False)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        before = getattr(self.ops, "launches", 0)
+        with torch.cuda.graph(g, stream=s):
+            self.forward(v, bucket, 0, 0, bucket, bucket, 0, splits, stochastic, gather=False)
+        torch.cuda.synchronize(self.device)
+        self.graph_launches[(bucket, stochastic)] = getattr(self.ops, "launches", 0) - before
+        self.ops.launches = before
+        self.graphs[(bucket, stochastic)] = g
+        return g
+
+    def capture_all(self, stochastic: bool = False):
+        for b in self.graph_sizes:
+            if (b, stochastic) not in self.graphs:
+                self.capture(b, stochastic)

@@ -1,0 +1,130 @@
+"""Fixed-capacity per-request block tables (logical page -> physical PageId).
+
+Reference: kv/block_table/arena.mbt:12-369 and allocation_checkpoint.mbt:17-166.
+Tables live in an arena of generational slots; each table holds at most
+``max_pages`` page ids.  Besides the PageIds, the arena keeps a dense
+``int32 [capacity, max_pages]`` matrix of physical page indices (generations
+stripped, as the reference does before upload:
+engine/device_step/README.mbt.md:23-29) that the engine slices directly into
+the per-step descriptor without per-row Python loops.
+"""
+from __future__ import annotations
+
+from typing import List, NamedTuple, Optional
+
+import numpy as np
+
+from .page_allocator import PageAllocator, PageId
+
+
+class BlockTableError(RuntimeError):
+    pass
+
+
+class TableId(NamedTuple):
+    index: int
+    generation: int
+
+
+class BlockTableArena:
+    def __init__(self, capacity: int, max_pages: int, tokens_per_page: int = 16):
+        self.capacity = capacity
+        self.max_pages = max_pages
+        self.tokens_per_page = tokens_per_page
+        self._gen = [0] * capacity
+        self._live = [False] * capacity
+        self._pages: List[List[PageId]] = [[] for _ in range(capacity)]
+        self._free = list(range(capacity - 1, -1, -1))
+        self.matrix = np.zeros((capacity, max_pages), dtype=np.int32)
+        self._ckpt = None
+
+    def _slot(self, tid: TableId) -> int:
+        if not (0 <= tid.index < self.capacity) or not self._live[tid.index] or self._gen[tid.index] != tid.generation:
+            raise BlockTableError("stale or unknown table id")
+        return tid.index
+
+    def free_table_count(self) -> int:
+        return len(self._free)
+
+    def allocated_table_count(self) -> int:
+        return self.capacity - len(self._free)
+
+    def allocate(self) -> TableId:
+        if not self._free:
+            raise BlockTableError("no free block table")
+        s = self._free.pop()
+        self._live[s] = True
+        self._pages[s] = []
+        return TableId(s, self._gen[s])
+
+    def release(self, tid: TableId):
+        s = self._slot(tid)
+        if self._pages[s]:
+            raise BlockTableError("table still owns pages; use reset_and_release")
+        self._live[s] = False
+        self._gen[s] += 1
+        self._free.append(s)
+
+    def page_count(self, tid: TableId) -> int:
+        return len(self._pages[self._slot(tid)])
+
+    def pages(self, tid: TableId) -> List[PageId]:
+        return list(self._pages[self._slot(tid)])
+
+    def append_pages(self, tid: TableId, pids: List[PageId]):
+        s = self._slot(tid)
+        n = len(self._pages[s])
+        if n + len(pids) > self.max_pages:
+            raise BlockTableError("block table full")
+        self._pages[s].extend(pids)
+        self.matrix[s, n:n + len(pids)] = [p.index for p in pids]
+
+    def page_at(self, tid: TableId, logical: int) -> PageId:
+        return self._pages[self._slot(tid)][logical]
+
+    def resolve_token_position(self, tid: TableId, position: int):
+        """(physical page index, offset in page) of a token position."""
+        s = self._slot(tid)
+        lp, off = divmod(position, self.tokens_per_page)
+        if lp >= len(self._pages[s]):
+            raise BlockTableError("position beyond the table")
+        return self._pages[s][lp].index, off
+
+    def truncate(self, tid: TableId, keep: int, allocator: Optional[PageAllocator] = None) -> List[PageId]:
+        s = self._slot(tid)
+        dropped = self._pages[s][keep:]
+        del self._pages[s][keep:]
+        self.matrix[s, keep:keep + len(dropped)] = 0
+        if allocator is not None:
+            for p in dropped:
+                allocator.release_active(p)
+        return dropped
+
+    def reset_and_release(self, tid: TableId, allocator: PageAllocator):
+        self.truncate(tid, 0, allocator)
+        self.release(tid)
+
+    # -- transactions: remember lengths, roll back appended suffixes ---------------
+    def checkpoint(self):
+        if self._ckpt is not None:
+            raise BlockTableError("checkpoint already open")
+        self._ckpt = {}
+        return True
+
+    def note(self, tid: TableId):
+        """Record a table's length before a provisional append."""
+        if self._ckpt is not None and tid.index not in self._ckpt:
+            self._ckpt[tid.index] = len(self._pages[tid.index])
+
+    def commit_checkpoint(self):
+        self._ckpt = None
+
+    def rollback(self):
+        """Detach every suffix appended since the checkpoint (pages are not released:
+        the page allocator's own rollback reclaims them)."""
+        for s, n in (self._ckpt or {}).items():
+            extra = len(self._pages[s]) - n
+            if extra > 0:
+                del self._pages[s][n:]
+                self.matrix[s, n:n + extra] = 0
+        self._ckpt = None

@@ -1,0 +1,74 @@
+"""The sm_100a operator set: thin wrappers over the ``_C`` extension.
+
+Every call launches on the current CUDA stream and allocates nothing, so the
+decode step can be captured into a CUDA graph.  ``launches`` counts the
+kernels this process launched through the extension (a graph replay adds the
+count recorded while it was captured).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _ext
+
+EPI_BF16, EPI_F32, EPI_SWIGLU = 0, 1, 2
+
+
+class KernelOps:
+    name = "kernels"
+
+    def __init__(self):
+        self.C = _ext.load()
+        self.launches = 0
+        self.num_sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        self._splitk = {}
+
+    def embed(self, ids, table, out):
+        self.launches += 1
+        self.C.embed(ids, table, out)
+
+    def rmsnorm(self, x, residual, w, out, eps):
+        self.launches += 1
+        self.C.rmsnorm(x, residual, w, out, eps)
+
+    def gemm(self, A, B, out, epi: int = EPI_BF16, ws: Optional[torch.Tensor] = None):
+        M, N, K = A.shape[0], B.shape[0], A.shape[1]
+        if M == 0:
+            return
+        if ws is not None:
+            key = (M, N, K)
+            s = self._splitk.get(key)
+            if s is None:
+                s = self._splitk[key] = self.C.gemm_plan_splitk(M, N, K)
+            self.launches += 2 if (s > 1 and M * N <= ws.numel() and N % 256 == 0) else 1
+        else:
+            self.launches += 1
+        self.C.gemm(A, B, out, epi, 0, ws)
+
+    def rope_kv_write(self, qkv, positions, slots, cos_sin, kc, vc, Hq, Hkv, page):
+        self.launches += 1
+        self.C.rope_kv_write(qkv, positions, slots, cos_sin, kc, vc, Hq, Hkv, page)
+
+    def attn_prefill(self, q, out, q_start, seq_lens, bt, kc, vc, Hq, Hkv, max_q_len, host=None):
+        self.launches += 1
+        self.C.attn_prefill(q, out, q_start, seq_lens, bt, kc, vc, Hq, Hkv, max_q_len)
+
+    def decode_splits(self, rows, Hkv, max_seq):
+        return self.C.attn_decode_splits(rows, Hkv, max_seq, self.num_sms)
+
+    def attn_decode(self, q, out, tok, seq_lens, bt, kc, vc, Hq, Hkv, splits, part_o, part_lse, host=None):
+        self.launches += 2 if splits > 1 else 1
+        self.C.attn_decode(q, out, tok, seq_lens, bt, kc, vc, Hq, Hkv, splits, part_o, part_lse)
+
+    def argmax(self, logits, out):
+        self.launches += 1
+        self.C.argmax(logits, out, None)
+
+    def sample(self, logits, params, out):
+        self.launches += 1
+        self.C.sample(logits, params, out, None)
+
+    def read_error(self, clear=True):
+        return self.C.read_error(clear)

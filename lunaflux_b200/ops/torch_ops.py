@@ -1,0 +1,150 @@
+"""PyTorch restatement of the operator contracts (CPU path and baseline).
+
+Same signatures and in-place semantics as ``KernelOps``; attention reads the
+same paged KV layout ([page][kv_head][token][dim]) through the block table.
+Host-side copies of the row metadata (``host=`` dicts of numpy arrays) are
+used so no device->host synchronisation happens inside a step.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from ..sampling.host import PARAM_DTYPE, counter_unit, stochastic_sample
+
+
+class TorchOps:
+    name = "torch"
+
+    def __init__(self, device="cpu"):
+        self.device = torch.device(device)
+        self.launches = 0
+
+    def embed(self, ids, table, out):
+        out[: ids.shape[0]] = table[ids.long()]
+
+    def rmsnorm(self, x, residual, w, out, eps):
+        if residual is not None:
+            residual.copy_(x + residual)
+            src = residual
+        else:
+            src = x
+        xf = src.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+        out.copy_(y.to(out.dtype))
+
+    def gemm(self, A, B, out, epi: int = 0, ws=None):
+        if epi == 2:
+            gu = (A @ B.t()).float()
+            M, N = gu.shape
+            v = gu.view(M, N // 64, 2, 32)
+            out.copy_((F.silu(v[:, :, 0]) * v[:, :, 1]).reshape(M, N // 2).to(out.dtype))
+        elif epi == 1:
+            out.copy_((A @ B.t()).float())
+        else:
+            torch.matmul(A, B.t(), out=out) if A.dtype == out.dtype else out.copy_(A @ B.t())
+
+    def rope_kv_write(self, qkv, positions, slots, cos_sin, kc, vc, Hq, Hkv, page):
+        T = qkv.shape[0]
+        D = kc.shape[-1]
+        h = D // 2
+        cs = cos_sin[positions[:T].long()]  # [T, D/2, 2]
+        c, s = cs[..., 0][:, None, :], cs[..., 1][:, None, :]
+        q = qkv[:, : Hq * D].view(T, Hq, D)
+        k = qkv[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
+        v = qkv[:, (Hq + Hkv) * D:(Hq + 2 * Hkv) * D].view(T, Hkv, D)
+
+        def rot(x):
+            xf = x.float()
+            x1, x2 = xf[..., :h], xf[..., h:]
+            return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], -1).to(x.dtype)
+
+        q.copy_(rot(q))
+        kr = rot(k)
+        sl = slots[:T].long()
+        ok = sl >= 0
+        pg, off = (sl // page)[ok], (sl % page)[ok]
+        kc[pg, :, off] = kr[ok]
+        vc[pg, :, off] = v[ok]
+
+    def _row_kv(self, kc, vc, bt_row, L):
+        P = kc.shape[2]
+        n = -(-L // P)
+        pages = bt_row[:n].long()
+        Hkv, D = kc.shape[1], kc.shape[3]
+        K = kc[pages].permute(1, 0, 2, 3).reshape(Hkv, n * P, D)[:, :L]
+        V = vc[pages].permute(1, 0, 2, 3).reshape(Hkv, n * P, D)[:, :L]
+        return K, V
+
+    def attn_prefill(self, q, out, q_start, seq_lens, bt, kc, vc, Hq, Hkv, max_q_len, host=None):
+        qs = host["q_start"]
+        sl = host["seq_lens"]
+        D = kc.shape[-1]
+        G = Hq // Hkv
+        scale = 1.0 / math.sqrt(D)
+        for r in range(len(sl)):
+            s0, s1 = int(qs[r]), int(qs[r + 1])
+            ql, L = s1 - s0, int(sl[r])
+            K, V = self._row_kv(kc, vc, bt[r], L)
+            qq = q[s0:s1, : Hq * D].view(ql, Hq, D).float().transpose(0, 1)
+            Kf = K.float().repeat_interleave(G, 0)
+            Vf = V.float().repeat_interleave(G, 0)
+            sc = torch.matmul(qq, Kf.transpose(1, 2)) * scale
+            qpos = torch.arange(L - ql, L, device=q.device)
+            mask = torch.arange(L, device=q.device)[None, :] > qpos[:, None]
+            sc = sc.masked_fill(mask[None], float("-inf"))
+            p = sc.softmax(-1)
+            o = torch.matmul(p, Vf).transpose(0, 1).reshape(ql, Hq * D)
+            out[s0:s1, : Hq * D] = o.to(out.dtype)
+
+    def decode_splits(self, rows, Hkv, max_seq):
+        return 1
+
+    def attn_decode(self, q, out, tok, seq_lens, bt, kc, vc, Hq, Hkv, splits, part_o, part_lse, host=None):
+        sl = host["seq_lens"]
+        tk = host["tok"]
+        R = len(sl)
+        if R == 0:
+            return
+        D, P = kc.shape[-1], kc.shape[2]
+        G = Hq // Hkv
+        Lmax = int(sl.max())
+        n = -(-Lmax // P)
+        pages = bt[:R, :n].long()                                   # [R, n]
+        K = kc[pages].permute(0, 2, 1, 3, 4).reshape(R, Hkv, n * P, D)
+        V = vc[pages].permute(0, 2, 1, 3, 4).reshape(R, Hkv, n * P, D)
+        tok_t = torch.as_tensor(tk, device=q.device, dtype=torch.long)
+        qq = q[tok_t, : Hq * D].view(R, Hkv, G, D).float()
+        sc = torch.matmul(qq, K.float().transpose(-1, -2)) / math.sqrt(D)  # [R, Hkv, G, n*P]
+        lens = torch.as_tensor(sl, device=q.device, dtype=torch.long)
+        mask = torch.arange(n * P, device=q.device)[None, :] >= lens[:, None]
+        sc = sc.masked_fill(mask[:, None, None, :], float("-inf"))
+        p = sc.softmax(-1)
+        o = torch.matmul(p, V.float()).reshape(R, Hq * D)
+        out[tok_t, : Hq * D] = o.to(out.dtype)
+
+    def argmax(self, logits, out):
+        out[: logits.shape[0]] = torch.argmax(logits, -1).to(torch.int32)
+
+    def sample(self, logits, params, out):
+        R = logits.shape[0]
+        p = params.detach().cpu().numpy().view(PARAM_DTYPE)[:R]
+        lg = logits.detach().double().cpu().numpy()
+        res = np.zeros(R, dtype=np.int32)
+        for i in range(R):
+            if p["mode"][i] == 0:
+                res[i] = int(np.argmax(lg[i]))
+            else:
+                tk = int(p["top_k"][i])
+                tp = float(p["top_p"][i])
+                u = counter_unit(int(p["seed"][i]), int(p["sample_index"][i]))
+                res[i] = stochastic_sample(lg[i], float(p["temperature"][i]), tk if tk > 0 else None,
+                                           tp if 0 < tp < 1 else None, u)
+        out[:R] = torch.from_numpy(res).to(out.device)
+
+    def read_error(self, clear=True):
+        return (0, 0)

@@ -38,6 +38,26 @@ def test_gemm_bf16(C, M, N, K, bn):
     _close(D32, ref, 1e-3, 1e-3, f"gemm fp32 {M}x{N}x{K} bn={bn}")
 
 
+@pytest.mark.parametrize("M,N,K,epi", [(1, 4096, 14336, 0), (256, 4096, 4096, 0), (100, 6144, 4096, 0),
+                                       (256, 3584, 4096, 2), (3, 512, 4096, 1), (256, 4096, 14336, 2)])
+def test_gemm_splitk(C, M, N, K, epi):
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    ws = torch.zeros(512 * 32768, device="cuda")
+    out_cols = N // 2 if epi == 2 else N
+    D = torch.empty(M, out_cols, device="cuda", dtype=torch.float32 if epi == 1 else torch.bfloat16)
+    for _ in range(2):  # the second call checks the workspace was left zero
+        C.gemm(A, B, D, epi, 0, ws)
+        ref = A.float() @ B.float().t()
+        if epi == 2:
+            Fh = N // 2
+            v = ref.view(M, Fh // 32, 2, 32)
+            ref = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(M, Fh)
+        _close(D, ref, 3e-2, 3e-2, f"split-K gemm {M}x{N}x{K} epi={epi}")
+    assert C.gemm_plan_splitk(M, N, K) >= 1
+    assert ws.abs().max().item() == 0.0
+
+
 def test_gemm_strided_a(C):
     A_full = torch.randn(64, 3 * 256, device="cuda").bfloat16()
     A = A_full[:, 256:512]
