@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--json-out", default="")
+    ap.add_argument("--profile", default="", help="write a per-kernel time table of one extra pass here")
     return ap.parse_args()
 
 
@@ -253,6 +254,17 @@ def main():
         if args.json_out:
             with open(args.json_out, "w") as f:
                 json.dump(line, f, indent=1)
+    if args.profile:
+        # One extra, untimed pass under the CUDA activity profiler: kernel time shares only.
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            one_pass()
+            torch.cuda.synchronize()
+        if rank == 0:
+            table = prof.key_averages().table(sort_by="cuda_time_total", row_limit=25, max_name_column_width=90)
+            with open(args.profile, "w") as f:
+                f.write(table)
+            print(table)
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -209,14 +209,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 8; ++j) d4[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
             } else if constexpr (EPI == kSplitF32) {
-              // Split-K partial: vector fp32 reduction into the (L2-resident) workspace.
-              float* dst = reinterpret_cast<float*>(out) + (size_t)row * ldd + n0 + c;
+              // Split-K partial: plain fp32 stores into this split's slab of
+              // the workspace; the finalize kernel sums the slabs in a fixed
+              // order, so results are bitwise reproducible.
+              float* dst = reinterpret_cast<float*>(out) + (size_t)(unit / num_tiles) * M * N +
+                           (size_t)row * ldd + n0 + c;
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-              for (int j = 0; j < 8; ++j)
-                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * j),
-                             "f"(__uint_as_float(r[4 * j])), "f"(__uint_as_float(r[4 * j + 1])),
-                             "f"(__uint_as_float(r[4 * j + 2])), "f"(__uint_as_float(r[4 * j + 3]))
-                             : "memory");
+              for (int j = 0; j < 8; ++j) d4[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
             } else {
               uint32_t packed[16];
 #pragma unroll
@@ -244,27 +244,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Split-K finalisation: read the fp32 sums, write the real output (bf16,
-// fp32 or SwiGLU of the interleaved gate/up columns) and zero the workspace
-// so the next split-K GEMM can accumulate into it again.
+// Split-K finalisation: sum the per-split fp32 slabs in split order and write
+// the real output (bf16, fp32, or SwiGLU of the interleaved gate/up columns).
 template <int EPI>
-__global__ void splitk_finalize_kernel(float* __restrict__ ws, void* __restrict__ out, int M, int N, int64_t ldd) {
+__global__ void splitk_finalize_kernel(const float* __restrict__ ws, void* __restrict__ out, int M, int N,
+                                       int64_t ldd, int splits) {
   const int row = blockIdx.y;
+  const size_t slab = (size_t)M * N;
   if (EPI == kSwiGLU) {
     const int half = N / 2;
     for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < half; j += gridDim.x * blockDim.x) {
       const int grp = j >> 5, off = j & 31;
-      float* pg = ws + (size_t)row * N + grp * 64 + off;
-      const float g = pg[0], u = pg[32];
-      pg[0] = 0.f;
-      pg[32] = 0.f;
+      const float* pg = ws + (size_t)row * N + grp * 64 + off;
+      float g = 0.f, u = 0.f;
+      for (int s = 0; s < splits; ++s) {
+        g += pg[s * slab];
+        u += pg[s * slab + 32];
+      }
       reinterpret_cast<__nv_bfloat16*>(out)[(size_t)row * ldd + j] = __float2bfloat16(silu(g) * u);
     }
   } else {
     for (int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4; j < N; j += gridDim.x * blockDim.x * 4) {
-      float4* p = reinterpret_cast<float4*>(ws + (size_t)row * N + j);
-      const float4 v = *p;
-      *p = make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s = 0; s < splits; ++s) {
+        const float4 p = *reinterpret_cast<const float4*>(ws + s * slab + (size_t)row * N + j);
+        v.x += p.x;
+        v.y += p.y;
+        v.z += p.z;
+        v.w += p.w;
+      }
       if (EPI == kStoreF32) {
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)row * ldd + j) = v;
       } else {
@@ -416,16 +424,16 @@ int choose_bn(int M, int N, int epi) {
 
 void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws, int64_t ws_elems) {
   if (a.M <= 0) return;
-  if (ws != nullptr && bn == 0 && (int64_t)a.M * a.N <= ws_elems && (a.N % 256) == 0) {
+  if (ws != nullptr && bn == 0 && (a.N % 256) == 0) {
     int kb_per = 0;
     const int splits = plan_splitk(a.M, a.N, a.K, &kb_per);
-    if (splits > 1) {
+    if (splits > 1 && (int64_t)splits * a.M * a.N <= ws_elems) {
       if (a.K % 8 != 0) throw std::runtime_error("lunaflux gemm: K must be a multiple of 8");
       launch<256, 4, kSplitF32>(a, stream, splits, kb_per, ws);
       dim3 grid((a.N + 1023) / 1024, a.M);
-      if (epi == kSwiGLU) splitk_finalize_kernel<kSwiGLU><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd);
-      else if (epi == kStoreF32) splitk_finalize_kernel<kStoreF32><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd);
-      else splitk_finalize_kernel<kStoreBf16><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd);
+      if (epi == kSwiGLU) splitk_finalize_kernel<kSwiGLU><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd, splits);
+      else if (epi == kStoreF32) splitk_finalize_kernel<kStoreF32><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd, splits);
+      else splitk_finalize_kernel<kStoreBf16><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd, splits);
       return;
     }
   }

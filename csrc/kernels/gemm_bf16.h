@@ -16,9 +16,10 @@ struct GemmArgs {
 
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = SwiGLU (gate/up rows interleaved in
 // groups of 64: 32 gate rows then the matching 32 up rows).  bn = 0 picks a tile width from the shape.
-// ws: optional fp32 workspace of ws_elems floats, all zero on entry (and left
-// zero on exit); when given and the GEMM is too skinny to fill the SMs, the
-// K dimension is split and reduced into it.
+// ws: optional fp32 scratch of ws_elems floats; when given and the GEMM is
+// too skinny to fill the SMs, the K dimension is split, each split writes its
+// own [M, N] slab of ws and a finalize kernel sums the slabs in split order
+// (deterministic; needs splits * M * N <= ws_elems, else no split).
 void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws = nullptr, int64_t ws_elems = 0);
 int plan_splitk(int M, int N, int K, int* kb_per_out);
 int choose_bn(int M, int N, int epi);

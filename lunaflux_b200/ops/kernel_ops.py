@@ -42,7 +42,7 @@ class KernelOps:
             s = self._splitk.get(key)
             if s is None:
                 s = self._splitk[key] = self.C.gemm_plan_splitk(M, N, K)
-            self.launches += 2 if (s > 1 and M * N <= ws.numel() and N % 256 == 0) else 1
+            self.launches += 2 if (s > 1 and s * M * N <= ws.numel() and N % 256 == 0) else 1
         else:
             self.launches += 1
         self.C.gemm(A, B, out, epi, 0, ws)
