@@ -117,6 +117,22 @@ void argmax(const at::Tensor& logits, at::Tensor& out, c10::optional<at::Tensor>
                  status.has_value() ? status->data_ptr<int32_t>() : nullptr, stream());
 }
 
+void argmax_keys(const at::Tensor& logits, int64_t id_offset, at::Tensor& keys) {
+  check_rowmajor(logits, "logits");
+  LF_CHECK(logits.scalar_type() == at::kFloat, "logits must be fp32");
+  LF_CHECK(keys.scalar_type() == at::kLong && keys.numel() >= logits.size(0), "keys must be int64 [rows]");
+  c10::cuda::CUDAGuard g(logits.device());
+  lf::ew::argmax_keys(logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1), (int)id_offset,
+                      reinterpret_cast<unsigned long long*>(keys.data_ptr<int64_t>()), stream());
+}
+
+void keys_to_tokens(const at::Tensor& keys, int64_t rows, int64_t ranks, at::Tensor& out) {
+  LF_CHECK(keys.scalar_type() == at::kLong && keys.is_contiguous() && keys.numel() >= rows * ranks, "keys shape");
+  c10::cuda::CUDAGuard g(keys.device());
+  lf::ew::keys_to_tokens(reinterpret_cast<const unsigned long long*>(keys.data_ptr<int64_t>()), rows, ranks,
+                         out.data_ptr<int32_t>(), stream());
+}
+
 void sample(const at::Tensor& logits, const at::Tensor& params, at::Tensor& out, c10::optional<at::Tensor> status) {
   check_rowmajor(logits, "logits");
   LF_CHECK(logits.scalar_type() == at::kFloat, "logits must be fp32");
@@ -218,6 +234,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_kv_write", &rope_kv_write);
   m.def("swiglu", &swiglu);
   m.def("argmax", &argmax, py::arg("logits"), py::arg("out"), py::arg("status") = py::none());
+  m.def("argmax_keys", &argmax_keys);
+  m.def("keys_to_tokens", &keys_to_tokens);
   m.def("sample", &sample, py::arg("logits"), py::arg("params"), py::arg("out"), py::arg("status") = py::none());
   m.def("attn_decode", &attn_decode);
   m.def("attn_decode_splits", &attn_decode_splits);

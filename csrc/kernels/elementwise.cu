@@ -288,6 +288,46 @@ void argmax(const float* logits, int64_t ld, int R, int V, int32_t* out, int32_t
   argmax_kernel<1024><<<R, 1024, 0, s>>>(logits, ld, V, out, status);
 }
 
+// Vocab-parallel greedy, step 1: per row, the composite key (logit, lowest id)
+// of this rank's vocab shard, with ids offset to global vocabulary ids.
+// Non-finite logits are skipped (a row with none finite yields key 0).
+template <int NT>
+__global__ void __launch_bounds__(NT) argmax_key_kernel(const float* __restrict__ logits, int64_t ld, int V,
+                                                        int id_offset, unsigned long long* __restrict__ keys) {
+  __shared__ uint64_t sh[NT / 32];
+  const float* row = logits + (size_t)blockIdx.x * ld;
+  uint64_t best = 0;
+  for (int i = threadIdx.x; i < V; i += NT) {
+    const float v = row[i];
+    if (!isfinite(v)) continue;
+    const uint64_t k = ckey(v, i + id_offset);
+    best = k > best ? k : best;
+  }
+  best = block_max_u64<NT>(best, sh);
+  if (threadIdx.x == 0) keys[blockIdx.x] = best;
+}
+
+// Step 2 (after an all-gather of keys [ranks, R]): the winning token per row.
+__global__ void keys_to_tokens_kernel(const unsigned long long* __restrict__ keys, int R, int ranks,
+                                      int32_t* __restrict__ out) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= R) return;
+  uint64_t best = 0;
+  for (int k = 0; k < ranks; ++k) best = keys[(size_t)k * R + r] > best ? keys[(size_t)k * R + r] : best;
+  out[r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+}
+
+void argmax_keys(const float* logits, int64_t ld, int R, int V, int id_offset, unsigned long long* keys,
+                 cudaStream_t s) {
+  if (R <= 0) return;
+  argmax_key_kernel<1024><<<R, 1024, 0, s>>>(logits, ld, V, id_offset, keys);
+}
+
+void keys_to_tokens(const unsigned long long* keys, int R, int ranks, int32_t* out, cudaStream_t s) {
+  if (R <= 0) return;
+  keys_to_tokens_kernel<<<(R + 127) / 128, 128, 0, s>>>(keys, R, ranks, out);
+}
+
 // Counter-addressed uniform draw in [0, 1) with 53 random bits
 // (sampling/rng.mbt counter_state / counter_unit).
 __host__ __device__ inline double counter_unit(uint64_t seed, int64_t sample_index) {

@@ -23,6 +23,9 @@ void rope_kv_write(void* qkv, int64_t ld, const int32_t* positions, const int32_
                    int64_t num_slots, cudaStream_t s);
 void swiglu(const void* gu, void* out, int T, int F, cudaStream_t s);
 void argmax(const float* logits, int64_t ld, int R, int V, int32_t* out, int32_t* status, cudaStream_t s);
+void argmax_keys(const float* logits, int64_t ld, int R, int V, int id_offset, unsigned long long* keys,
+                 cudaStream_t s);
+void keys_to_tokens(const unsigned long long* keys, int R, int ranks, int32_t* out, cudaStream_t s);
 void sample(const float* logits, int64_t ld, int R, int V, const SampleParams* params, int32_t* out, int32_t* status,
             cudaStream_t s);
 double host_counter_unit(uint64_t seed, int64_t idx);

@@ -75,6 +75,8 @@ class ModelRunner:
         self.full_logits = (torch.empty(R, s.vocab, dtype=torch.float32, device=dev)
                             if sh.size > 1 else self.logits)
         self.out_tok = torch.zeros(R, dtype=torch.int32, device=dev)
+        self.keys_local = torch.zeros(R, dtype=torch.int64, device=dev)
+        self.keys_all = torch.zeros(R * sh.size, dtype=torch.int64, device=dev)
         # split-K GEMM workspace (kept all-zero between GEMMs) and split-KV decode partials
         self.gemm_ws = torch.zeros(512 * max(32768, sh.qkv_size, 2 * sh.ffn_padded), dtype=torch.float32, device=dev) \
             if dev.type == "cuda" else None
@@ -150,11 +152,22 @@ class ModelRunner:
             hs = h[:Rs]
         logits = self.logits[:Rs]
         ops.gemm(hs, w.lm_head, logits, 1, ws)
-        if self.comm is not None and self.shard.size > 1:
-            full = self.full_logits[:Rs]
-            self.comm.all_gather_cols(logits, full)
-            logits = full
         out = self.out_tok[:Rs]
+        tp = self.shard.size
+        if self.comm is not None and tp > 1:
+            if stochastic:
+                # top-k / top-p need the whole distribution: gather the vocab shards
+                full = self.full_logits[:Rs]
+                self.comm.all_gather_cols(logits, full)
+                ops.sample(full, v["s_params"], out)
+            else:
+                # greedy: exchange one (logit, lowest id) key per row and shard
+                keys = self.keys_local[:Rs]
+                ops.argmax_keys(logits, self.shard.rank * self.shard.vocab, keys)
+                allk = self.keys_all[: tp * Rs]
+                self.comm.all_gather_flat(keys, allk)
+                ops.keys_to_tokens(allk, Rs, tp, out)
+            return out
         if stochastic:
             ops.sample(logits, v["s_params"], out)
         else:

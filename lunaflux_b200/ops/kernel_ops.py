@@ -72,3 +72,11 @@ class KernelOps:
 
     def read_error(self, clear=True):
         return self.C.read_error(clear)
+
+    def argmax_keys(self, logits, id_offset, keys):
+        self.launches += 1
+        self.C.argmax_keys(logits, id_offset, keys)
+
+    def keys_to_tokens(self, keys, rows, ranks, out):
+        self.launches += 1
+        self.C.keys_to_tokens(keys, rows, ranks, out)

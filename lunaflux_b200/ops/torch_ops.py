@@ -148,3 +148,19 @@ class TorchOps:
 
     def read_error(self, clear=True):
         return (0, 0)
+
+    # vocab-parallel greedy: composite key (logit, lowest global id) per row
+    def argmax_keys(self, logits, id_offset, keys):
+        R = logits.shape[0]
+        idx = torch.argmax(logits, -1)
+        val = logits.gather(1, idx[:, None])[:, 0]
+        u = val.float().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+        fk = torch.where(u >= 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
+        keys[:R] = (fk << 32) | (0xFFFFFFFF - (idx + id_offset))
+
+    def keys_to_tokens(self, keys, rows, ranks, out):
+        k = keys[: rows * ranks].view(ranks, rows)
+        # int64 compare is signed; flip the top bit so unsigned order is kept
+        kk = k ^ torch.iinfo(torch.int64).min
+        best = k.gather(0, kk.argmax(0)[None])[0]
+        out[:rows] = (0xFFFFFFFF - (best & 0xFFFFFFFF)).to(torch.int32)

@@ -64,6 +64,11 @@ class TPComm:
         dist.all_gather_into_tensor(buf, local.contiguous(), group=self.group)
         full.view(R, self.world, Vl).copy_(buf.view(self.world, R, Vl).transpose(0, 1))
 
+    def all_gather_flat(self, local: torch.Tensor, out: torch.Tensor):
+        """out[k * n:(k + 1) * n] = local of rank k."""
+        self.calls += 1
+        dist.all_gather_into_tensor(out, local, group=self.group)
+
     def barrier(self):
         dist.barrier(group=self.group)
 
