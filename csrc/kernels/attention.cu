@@ -12,7 +12,7 @@
 // KV cache layout, per layer and per K/V: [page][kv_head][16 tokens][D=128]
 // bf16, so one (page, head) block is 4 KB contiguous.  Pages reach shared
 // memory through TMA (2-D tensor map over [pages*heads*16, 128], box 16 x 64,
-// 128-byte swizzle; never multicast), one mbarrier per stage; fragments come
+// 128-byte swizzle; each CTA loads for itself), one mbarrier per stage; fragments come
 // out of the swizzled tiles with ldmatrix and feed bf16 mma.sync (m16n8k16).
 // Block-table entries are bounds-checked: a bad entry records kErrBadIndex and
 // reads the reserved zero page 0 instead.

@@ -2,7 +2,7 @@
 //
 // Everything here is written for Blackwell (sm_100a): mbarrier waits are
 // bounded (a wait that runs out sets a device error word and lets the kernel
-// return instead of hanging the GPU), TMA copies never use cluster multicast,
+// return instead of hanging the GPU), every TMA copy targets its own CTA only,
 // and tcgen05 helpers follow the PTX ISA 8.7 encodings.
 #pragma once
 

@@ -22,7 +22,7 @@
 // the 32 up rows of the same features): the gate/up projection writes
 // silu(gate) * up directly and the [M, 2F] intermediate never exists.
 //
-// All waits are bounded (common.cuh); no TMA load uses cluster multicast.
+// All waits are bounded (common.cuh); every TMA load fills only its own CTA.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
