@@ -220,8 +220,10 @@ class StopConditions:
 
 
 class CachePermission(enum.Enum):
+    """Prefix-cache permission; the values are the framed-wire codes."""
     DISABLED = 0
-    READ_WRITE = 1
+    READ_ONLY = 1
+    READ_WRITE = 2
 
 
 @dataclasses.dataclass(frozen=True)
@@ -253,6 +255,9 @@ class GenerateRequest:
     deadline_millis: Optional[int] = None
     cache: CacheScope = CacheScope()
     trace: Optional[bytes] = None
+    # loaded-model identity the client targets (lowercase SHA-256 hex, "" = any)
+    model_content_digest: str = ""
+    model_plan_digest: str = ""
 
     def validate(self, limits: InferenceLimits) -> "GenerateRequest":
         if not (0 <= self.request_id < (1 << 64)):
@@ -300,12 +305,14 @@ class FinishReason(enum.Enum):
 
 
 class PublicErrorCode(enum.Enum):
-    INVALID_REQUEST = 1
-    OVERLOADED = 2
-    DEADLINE_EXCEEDED = 3
-    WORKER_UNAVAILABLE = 4
-    INTERNAL = 5
-    CONTEXT_OVERFLOW = 6
+    """Bounded machine-readable failure codes; the value is the wire string."""
+    INVALID_REQUEST = "invalid_request"
+    OVERLOADED = "overloaded"
+    DEADLINE_EXCEEDED = "deadline_exceeded"
+    WORKER_UNAVAILABLE = "worker_unavailable"
+    INTERNAL = "internal"
+    CONTEXT_OVERFLOW = "context_overflow"
+    CANCELLED = "cancelled"
 
 
 @dataclasses.dataclass(frozen=True)

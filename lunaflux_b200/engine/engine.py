@@ -116,7 +116,7 @@ class LLMEngine:
             raise ValueError("text requests must be tokenized by the service layer first")
         return self.add_request(g.input_tokens, g.max_new_tokens, g.sampling, g.stop.token_ids, rid=g.request_id,
                                 deadline_s=None if g.deadline_millis is None else g.deadline_millis / 1000.0,
-                                cache_scope=g.cache.scope, use_prefix_cache=g.cache.permission.value == 1)
+                                cache_scope=g.cache.scope, use_prefix_cache=g.cache.permission.value != 0)
 
     def cancel(self, rid: int) -> bool:
         ok = self.scheduler.cancel(rid)

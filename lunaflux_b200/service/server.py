@@ -1,0 +1,259 @@
+"""The serving loop and the framed TCP endpoint.
+
+Reference: service/online_session (LunaOnlineInstance begin / progress /
+take_event, admission.mbt:90, progression.mbt:225), service/online_tcp
+(endpoint_prepare.mbt:53, endpoint_reactor.mbt:203), service/request_admission
+(prepare_luna_request, admit.mbt:329).  Kept: request receipt time is taken
+before the first byte is parsed and the deadline is derived from it once;
+the event order Accepted -> Token* -> Usage -> Completed | Failed; a worker
+failure fails active requests with ``worker_unavailable`` (retryable);
+draining rejects new admissions.  Changed: many concurrent connections and
+requests (the reference serves one request on one connection), continuous
+batching underneath, and client disconnect cancels the request.
+
+Threads: the engine runs in one dedicated thread (it owns the GPU stream and
+the scheduler); asyncio handles sockets; the two meet through a locked inbox
+and ``call_soon_threadsafe``.
+"""
+from __future__ import annotations
+
+import asyncio
+import collections
+import threading
+import time
+from dataclasses import dataclass
+from typing import Callable, Deque, Dict, Optional
+
+from ..contracts.inference import (CompletedEvent, FailedEvent, FinishReason, GenerateRequest, InferenceLimits,
+                                   PublicErrorCode, TokenEvent, Usage)
+from ..engine.engine import LLMEngine
+from ..scheduler.scheduler import AdmissionRejected
+from ..tokenizer.bpe import Tokenizer
+from .detokenize import IncrementalOutput
+from .framed_wire import (REQUEST_MAGIC, AcceptedWire, FrameReader, FramedWireError, decode_request, encode_event)
+
+
+@dataclass
+class _Live:
+    req: GenerateRequest
+    sink: Callable[[object], None]
+    out: IncrementalOutput
+    prompt_len: int
+    n_out: int = 0
+
+
+class EngineService:
+    """Owns the engine thread; thread-safe submit / cancel; events via sinks."""
+
+    def __init__(self, engine: LLMEngine, tokenizer: Optional[Tokenizer], limits: InferenceLimits,
+                 content_digest: str = "", plan_digest: str = ""):
+        self.engine = engine
+        self.tokenizer = tokenizer
+        self.limits = limits
+        self.content_digest = content_digest
+        self.plan_digest = plan_digest or engine.spec.plan_digest()
+        self._inbox: Deque = collections.deque()
+        self._cv = threading.Condition()
+        self._live: Dict[int, _Live] = {}
+        self._stop = False
+        self.draining = False
+        self.failed = False
+        self._thread = threading.Thread(target=self._run, name="lunaflux-engine", daemon=True)
+        self.engine.listeners.append(self._on_outputs)
+
+    def start(self):
+        self._thread.start()
+
+    def stop(self):
+        with self._cv:
+            self._stop = True
+            self._cv.notify()
+        self._thread.join(timeout=30)
+
+    # -------------------------------------------------------------- producer side
+    def submit(self, req: GenerateRequest, sink: Callable[[object], None]):
+        with self._cv:
+            self._inbox.append(("add", req, sink))
+            self._cv.notify()
+
+    def cancel(self, rid: int):
+        with self._cv:
+            self._inbox.append(("cancel", rid, None))
+            self._cv.notify()
+
+    # -------------------------------------------------------------- engine thread
+    def _admit(self, req: GenerateRequest, sink):
+        if self.draining or self.failed:
+            sink(FailedEvent(req.request_id, PublicErrorCode.WORKER_UNAVAILABLE if self.failed
+                             else PublicErrorCode.OVERLOADED, True))
+            return
+        if (req.model_content_digest and self.content_digest and req.model_content_digest != self.content_digest) or \
+                (req.model_plan_digest and req.model_plan_digest != self.plan_digest):
+            sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
+            return
+        if req.input_tokens is not None:
+            prompt = list(req.input_tokens)
+        else:
+            if self.tokenizer is None:
+                sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
+                return
+            try:
+                prompt = self.tokenizer.encode_bytes(req.input_text, allow_special=False)
+            except ValueError:
+                sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
+                return
+        if not prompt or max(prompt) > self.limits.max_token_id:
+            sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
+            return
+        try:
+            self.engine.submit(GenerateRequest(**{**req.__dict__, "input_tokens": tuple(prompt), "input_text": None}))
+        except AdmissionRejected as e:
+            sink(FailedEvent(req.request_id, e.code, e.code is PublicErrorCode.OVERLOADED))
+            return
+        ctx = req.context_ceiling or self.engine.opts.max_context
+        sink(AcceptedWire(req.request_id, req.max_new_tokens, ctx, self.content_digest, self.plan_digest))
+        self._live[req.request_id] = _Live(req, sink, IncrementalOutput(req.stop.strings), len(prompt))
+
+    def _on_outputs(self, outs):
+        for o in outs:
+            lv = self._live.get(o.rid)
+            if lv is None:
+                continue
+            lv.n_out += 1
+            delta = b""
+            stop_hit = False
+            if self.tokenizer is not None and o.token in self.tokenizer.id_to_token:
+                delta, stop_hit = lv.out.push(self.tokenizer.token_bytes(o.token))
+            lv.sink(TokenEvent(o.rid, o.position, o.token, delta))
+            if stop_hit and not o.finished:
+                self.engine.scheduler.cancel(o.rid)
+                self._finish(o.rid, FinishReason.STOP_SEQUENCE)
+            elif o.finished:
+                self._finish(o.rid, o.reason)
+
+    def _finish(self, rid: int, reason: Optional[FinishReason], error: Optional[PublicErrorCode] = None):
+        lv = self._live.pop(rid, None)
+        if lv is None:
+            return
+        res = self.engine.results.get(rid)
+        cached = res.cached_tokens if res is not None else 0
+        usage = Usage(lv.prompt_len, min(cached, lv.prompt_len), lv.n_out)
+        lv.sink(usage)
+        if error is not None:
+            lv.sink(FailedEvent(rid, error, error in (PublicErrorCode.WORKER_UNAVAILABLE, PublicErrorCode.OVERLOADED)))
+        else:
+            lv.sink(CompletedEvent(rid, reason or FinishReason.TOKEN_LIMIT, usage, lv.out.finish()))
+
+    def _drain_terminals(self):
+        for rid, res in list(self.engine.results.items()):
+            if rid in self._live:
+                if res.error is not None:
+                    self._finish(rid, None, res.error)
+                else:
+                    self._finish(rid, res.reason)
+            self.engine.results.pop(rid, None)
+
+    def _run(self):
+        while True:
+            with self._cv:
+                while not self._inbox and not self.engine.has_work() and not self._stop:
+                    self._cv.wait(timeout=0.5)
+                if self._stop:
+                    break
+                items = list(self._inbox)
+                self._inbox.clear()
+            for kind, a, b in items:
+                if kind == "add":
+                    self._admit(a, b)
+                elif kind == "cancel":
+                    self.engine.cancel(a)
+            if self.engine.has_work():
+                try:
+                    self.engine.step()
+                except Exception:
+                    self.failed = True
+                    self.engine.scheduler.fail_active(PublicErrorCode.WORKER_UNAVAILABLE)
+                    self.engine._drain_terminals()
+            self._drain_terminals()
+
+
+class TCPServer:
+    """Framed request-v1 / event-v2 endpoint on asyncio; many concurrent clients."""
+
+    def __init__(self, service: EngineService, host: str = "127.0.0.1", port: int = 0, max_frame: int = 16 << 20):
+        self.service = service
+        self.host = host
+        self.port = port
+        self.max_frame = max_frame
+        self.server: Optional[asyncio.AbstractServer] = None
+
+    async def start(self):
+        self.server = await asyncio.start_server(self._client, self.host, self.port)
+        self.port = self.server.sockets[0].getsockname()[1]
+        return self.port
+
+    async def _client(self, reader: asyncio.StreamReader, writer: asyncio.StreamWriter):
+        loop = asyncio.get_running_loop()
+        frames = FrameReader(REQUEST_MAGIC, self.max_frame)
+        open_rids = set()
+        q: asyncio.Queue = asyncio.Queue()
+
+        def sink_for(rid):
+            def sink(ev):
+                loop.call_soon_threadsafe(q.put_nowait, (rid, ev))
+            return sink
+
+        state = {"eof": False}
+        done = asyncio.Event()
+
+        async def pump():
+            # Writes events in order; a broken transport cancels the client's requests.
+            try:
+                while True:
+                    rid, ev = await q.get()
+                    if ev is not None:
+                        writer.write(encode_event(ev))
+                        await writer.drain()
+                        if isinstance(ev, (CompletedEvent, FailedEvent)):
+                            open_rids.discard(rid)
+                    if state["eof"] and not open_rids:
+                        return
+            except (ConnectionError, OSError):
+                for rid in list(open_rids):
+                    self.service.cancel(rid)
+            finally:
+                done.set()
+
+        pump_task = asyncio.create_task(pump())
+        try:
+            while True:
+                data = await reader.read(65536)
+                if not data:
+                    break
+                try:
+                    for fr in frames.feed(data):
+                        req = decode_request(fr, self.service.limits)
+                        if req.request_id in open_rids:
+                            raise FramedWireError("request", "duplicate_id")
+                        open_rids.add(req.request_id)
+                        self.service.submit(req, sink_for(req.request_id))
+                except FramedWireError:
+                    # malformed input: drop the connection and its requests
+                    for rid in list(open_rids):
+                        self.service.cancel(rid)
+                    open_rids.clear()
+                    break
+        finally:
+            # A half-closed client still receives the events of its requests.
+            state["eof"] = True
+            await q.put((0, None))
+            await done.wait()
+            writer.close()
+
+    async def serve_forever(self):
+        async with self.server:
+            await self.server.serve_forever()
+
+    def close(self):
+        if self.server is not None:
+            self.server.close()

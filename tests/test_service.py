@@ -1,0 +1,181 @@
+"""Framed wire codecs, incremental output and the TCP serving path (CPU)."""
+import asyncio
+import struct
+
+import pytest
+import torch
+
+from lunaflux_b200.contracts.inference import (CachePermission, CacheScope, CompletedEvent, FailedEvent,
+                                               FinishReason, GenerateRequest, PublicErrorCode, SamplingParameters,
+                                               StopConditions, TokenEvent, Usage, default_limits)
+from lunaflux_b200.service.detokenize import IncrementalOutput
+from lunaflux_b200.service.framed_wire import (EVENT_MAGIC, AcceptedWire, FrameReader, FramedWireError, decode_event,
+                                               decode_request, encode_event, encode_request, fnv1a)
+
+LIM = default_limits(256, 512)
+
+
+def full_request():
+    return GenerateRequest(request_id=77, input_tokens=(1, 2, 3, 250), max_new_tokens=9, context_ceiling=300,
+                           sampling=SamplingParameters.sample(0.7, top_k=40, top_p=0.9, seed=5),
+                           stop=StopConditions((7, 9), (b"ab", b"\xc3\xa9")), streaming=True, deadline_millis=1500,
+                           cache=CacheScope(b"tenant-1", CachePermission.READ_ONLY), trace=b"trace:1",
+                           model_plan_digest="a" * 64)
+
+
+def test_request_layout_offsets():
+    fr = encode_request(full_request())
+    magic, ver, kind, total = struct.unpack_from("<IIII", fr, 0)
+    assert (magic, ver, kind, total) == (0x5152464C, 1, 1, len(fr))
+    assert struct.unpack_from("<I", fr, 20)[0] == 2 | 4 | 8 | 16 | 32
+    assert struct.unpack_from("<i", fr, 28)[0] == 4 and struct.unpack_from("<i", fr, 52)[0] == 9
+    assert struct.unpack_from("<d", fr, 72)[0] == 0.7 and struct.unpack_from("<Q", fr, 104)[0] == 77
+    assert fr[176:240] == b"a" * 64 and struct.unpack_from("<i", fr, 240)[0] == 1
+    assert struct.unpack_from("<i", fr, 248)[0] == 256
+    assert struct.unpack_from("<I", fr, 16)[0] == fnv1a(fr)
+
+
+def test_request_roundtrip():
+    req = full_request()
+    assert decode_request(encode_request(req), LIM) == req.validate(LIM)
+    t = GenerateRequest(request_id=1, input_text="héllo".encode(), max_new_tokens=2)
+    assert decode_request(encode_request(t), LIM) == t
+
+
+@pytest.mark.parametrize("mutate,rule", [
+    (lambda b: b.__setitem__(slice(0, 4), b"XXXX"), "magic"),
+    (lambda b: b.__setitem__(300, b[300] ^ 1), "checksum"),
+    (lambda b: b.__setitem__(slice(4, 8), struct.pack("<I", 2)), "version"),
+])
+def test_request_hostile(mutate, rule):
+    b = bytearray(encode_request(full_request()))
+    mutate(b)
+    with pytest.raises(FramedWireError) as e:
+        decode_request(bytes(b), LIM)
+    assert e.value.rule == rule
+
+
+def _fix_checksum(b):
+    struct.pack_into("<I", b, 16, fnv1a(b))
+    return bytes(b)
+
+
+def test_request_nonzero_reserved_and_unused_rejected():
+    b = bytearray(encode_request(GenerateRequest(1, input_tokens=(1,), max_new_tokens=1)))
+    b[253] = 1
+    with pytest.raises(FramedWireError):
+        decode_request(_fix_checksum(b), LIM)
+    b = bytearray(encode_request(GenerateRequest(1, input_tokens=(1,), max_new_tokens=1)))
+    struct.pack_into("<i", b, 64, 5)  # top_k without its flag
+    with pytest.raises(FramedWireError):
+        decode_request(_fix_checksum(b), LIM)
+    with pytest.raises(FramedWireError):
+        decode_request(encode_request(GenerateRequest(1, input_tokens=(999,), max_new_tokens=1)), LIM)
+
+
+def test_event_roundtrip_and_layout():
+    evs = [AcceptedWire(3, 9, 300, "", "b" * 64), TokenEvent(3, 12, 99, "é".encode()), TokenEvent(3, 13, 5, b""),
+           Usage(4, 0, 2), CompletedEvent(3, FinishReason.STOP_SEQUENCE, Usage(4, 2, 2), b"tail"),
+           FailedEvent(3, PublicErrorCode.WORKER_UNAVAILABLE, True)]
+    for ev in evs:
+        fr = encode_event(ev)
+        assert struct.unpack_from("<II", fr, 0) == (EVENT_MAGIC, 2)
+        assert struct.unpack_from("<i", fr, 196)[0] == 208
+        back = decode_event(fr, 3)
+        assert back == ev
+    fr = encode_event(TokenEvent(3, 12, 99, b"x"))
+    assert struct.unpack_from("<ii", fr, 24) == (99, 12) and struct.unpack_from("<I", fr, 20)[0] == 1
+    fr = encode_event(CompletedEvent(3, FinishReason.CANCELLED, Usage(4, 0, 1)))
+    assert struct.unpack_from("<i", fr, 24)[0] == 2 and struct.unpack_from("<iiii", fr, 32) == (4, 0, 1, 5)
+    assert decode_event(encode_event(FailedEvent(1, PublicErrorCode.DEADLINE_EXCEEDED, False)), 1).code \
+        is PublicErrorCode.DEADLINE_EXCEEDED
+
+
+def test_frame_reader_splits_and_poisons():
+    a = encode_event(Usage(1, 0, 1))
+    b = encode_event(Usage(2, 0, 3))
+    r = FrameReader(EVENT_MAGIC, header=208)
+    assert r.feed(a[:10]) == []
+    assert r.feed(a[10:] + b[:100]) == [a]
+    assert r.feed(b[100:]) == [b]
+    with pytest.raises(FramedWireError):
+        r.feed(b"\x00" * 16)
+
+
+def test_incremental_output_stop_across_tokens_and_utf8():
+    o = IncrementalOutput([b"STOP"])
+    assert o.push(b"hello S") == (b"hello ", False)  # "S" withheld: may start STOP
+    assert o.push(b"T") == (b"", False)
+    assert o.push(b"Xy") == (b"STXy", False)
+    assert o.push(b"zzST") == (b"zz", False)
+    assert o.push(b"OPmore") == (b"", True)
+    o = IncrementalOutput()
+    e = "é".encode()
+    assert o.push(e[:1]) == (b"", False)  # incomplete code point withheld
+    assert o.push(e[1:] + b"!") == (e + b"!", False)
+    assert o.push(b"\xf0\x9f") == (b"", False)
+    assert o.finish() == "�".encode()
+
+
+def test_tcp_end_to_end():
+    from lunaflux_b200.config import CacheConfig, SchedulerConfig
+    from lunaflux_b200.engine.engine import EngineOptions, LLMEngine
+    from lunaflux_b200.models.spec import tiny_llama
+    from lunaflux_b200.models.weights import build_runtime, random_checkpoint
+    from lunaflux_b200.ops.torch_ops import TorchOps
+    from lunaflux_b200.oracle.reference import ReferenceModel
+    from lunaflux_b200.service.framed_wire import EVENT_HEADER
+    from lunaflux_b200.service.server import EngineService, TCPServer
+    from lunaflux_b200.tokenizer.bpe import synthetic_byte_tokenizer
+
+    spec = tiny_llama()
+    ck = random_checkpoint(spec, 0)
+    eng = LLMEngine(build_runtime(spec, lambda n: ck[n]), TorchOps(), "cpu",
+                    SchedulerConfig(step_token_budget=64, max_active_requests=4, prefill_chunk_tokens=64,
+                                    emergency_decode_page_reserve=1),
+                    CacheConfig(), EngineOptions(max_context=256, num_pages=64, graph_sizes=()))
+    svc = EngineService(eng, synthetic_byte_tokenizer(), LIM)
+    svc.start()
+    prompt = [5, 17, 99, 3, 200]
+    expect = ReferenceModel(spec, ck).generate_greedy(prompt, 6)
+
+    async def client(req):
+        r, w = await asyncio.open_connection("127.0.0.1", port)
+        w.write(encode_request(req))
+        await w.drain()
+        fr = FrameReader(EVENT_MAGIC, header=EVENT_HEADER)
+        events = []
+        while True:
+            data = await r.read(65536)
+            if not data:
+                break
+            for f in fr.feed(data):
+                events.append(decode_event(f, req.request_id))
+            if events and isinstance(events[-1], (CompletedEvent, FailedEvent)):
+                break
+        w.close()
+        return events
+
+    async def main():
+        global port
+        server = TCPServer(svc)
+        p = await server.start()
+        globals()["port"] = p
+        a, b, c = await asyncio.gather(
+            client(GenerateRequest(1, input_tokens=tuple(prompt), max_new_tokens=6)),
+            client(GenerateRequest(2, input_text=b"hi there", max_new_tokens=4)),
+            client(GenerateRequest(3, input_tokens=(1,), max_new_tokens=4, model_plan_digest="f" * 64)))
+        server.close()
+        return a, b, c
+
+    try:
+        a, b, c = asyncio.run(main())
+    finally:
+        svc.stop()
+    assert isinstance(a[0], AcceptedWire)
+    toks = [e.token_id for e in a if isinstance(e, TokenEvent)]
+    assert toks == expect
+    assert isinstance(a[-2], Usage) and a[-2].output_tokens == 6
+    assert isinstance(a[-1], CompletedEvent) and a[-1].reason is FinishReason.TOKEN_LIMIT
+    assert isinstance(b[-1], CompletedEvent) and sum(isinstance(e, TokenEvent) for e in b) == 4
+    assert isinstance(c[-1], FailedEvent) and c[-1].code is PublicErrorCode.INVALID_REQUEST
