@@ -1,0 +1,135 @@
+"""Hugging Face ``config.json`` reader for Llama and Mixtral.
+
+Reference: model/config_reader/schema.mbt:4-181 and reader.mbt:70.  Same
+admission rules: strict JSON (duplicate keys rejected); executable metadata
+(``auto_map``, ``trust_remote_code``, ``custom_pipelines``) rejected; unknown
+fields rejected; untied embeddings; ``rope_scaling`` and ``sliding_window``
+null; ``hidden_act`` silu; no attention / MLP bias; ``pretraining_tp`` 1.
+Added: ``model_type == "mixtral"`` with ``num_local_experts`` and
+``num_experts_per_tok``, and a ``quantization_config`` for block-scaled fp8
+(``quant_method == "fp8"``, ``weight_block_size == [128, 128]``).
+"""
+from __future__ import annotations
+
+import hashlib
+from typing import Any, Dict
+
+from ..utils.json_strict import loads_strict
+from .spec import LlamaSpec, SpecError
+
+
+class ConfigReaderError(ValueError):
+    pass
+
+
+_EXECUTABLE = {"auto_map", "trust_remote_code", "custom_pipelines"}
+_SEMANTIC = {"architectures", "model_type", "vocab_size", "hidden_size", "intermediate_size", "num_hidden_layers",
+             "num_attention_heads", "num_key_value_heads", "max_position_embeddings", "rope_theta", "torch_dtype",
+             "tie_word_embeddings", "rope_scaling", "sliding_window", "hidden_act", "rms_norm_eps", "attention_bias",
+             "attention_dropout", "mlp_bias", "head_dim", "pretraining_tp",
+             # Mixtral
+             "num_local_experts", "num_experts_per_tok", "router_aux_loss_coef", "output_router_logits",
+             "router_jitter_noise",
+             # fp8
+             "quantization_config"}
+_INERT = {"_name_or_path", "transformers_version", "bos_token_id", "eos_token_id", "pad_token_id",
+          "initializer_range", "use_cache"}
+
+
+def _int(d, k, required=True, default=None):
+    v = d.get(k, default)
+    if v is None and not required:
+        return None
+    if type(v) is not int or v <= 0:
+        raise ConfigReaderError(f"{k} must be a positive integer")
+    return v
+
+
+def _num(d, k, default=None):
+    v = d.get(k, default)
+    if isinstance(v, bool) or not isinstance(v, (int, float)):
+        raise ConfigReaderError(f"{k} must be a number")
+    return float(v)
+
+
+def parse_config(text: str | bytes, dtype: str = "bf16") -> LlamaSpec:
+    try:
+        d: Dict[str, Any] = loads_strict(text)
+    except ValueError as e:
+        raise ConfigReaderError(f"config is not strict JSON: {e}") from None
+    if not isinstance(d, dict):
+        raise ConfigReaderError("config must be an object")
+    for k in d:
+        if k in _EXECUTABLE:
+            raise ConfigReaderError(f"executable metadata {k!r} is rejected")
+        if k not in _SEMANTIC and k not in _INERT:
+            raise ConfigReaderError("unknown config field")
+    mt = d.get("model_type")
+    if mt not in ("llama", "mixtral"):
+        raise ConfigReaderError("model_type must be llama or mixtral")
+    arch = d.get("architectures")
+    if arch is not None and (not isinstance(arch, list) or len(arch) != 1):
+        raise ConfigReaderError("exactly one architecture is required")
+    if d.get("tie_word_embeddings", False) is not False:
+        raise ConfigReaderError("tied embeddings are not supported")
+    for k in ("rope_scaling", "sliding_window"):
+        if d.get(k) is not None:
+            raise ConfigReaderError(f"{k} must be null")
+    if d.get("hidden_act", "silu") != "silu":
+        raise ConfigReaderError("hidden_act must be silu")
+    for k in ("attention_bias", "mlp_bias"):
+        if d.get(k, False) is not False:
+            raise ConfigReaderError(f"{k} must be false")
+    if _num(d, "attention_dropout", 0.0) != 0.0:
+        raise ConfigReaderError("attention_dropout must be 0")
+    if d.get("pretraining_tp", 1) != 1:
+        raise ConfigReaderError("pretraining_tp must be 1")
+    hidden = _int(d, "hidden_size")
+    heads = _int(d, "num_attention_heads")
+    kv = _int(d, "num_key_value_heads", default=heads)
+    head_dim = d.get("head_dim") or hidden // heads
+    if hidden != heads * head_dim:
+        raise ConfigReaderError("hidden_size must equal heads * head_dim")
+    experts = topk = 0
+    if mt == "mixtral":
+        experts = _int(d, "num_local_experts")
+        topk = _int(d, "num_experts_per_tok")
+    fp8 = 0
+    q = d.get("quantization_config")
+    if q is not None:
+        if not isinstance(q, dict) or q.get("quant_method") != "fp8" or q.get("weight_block_size") != [128, 128]:
+            raise ConfigReaderError("only block-scaled fp8 (128 x 128) quantisation is supported")
+        fp8 = 128
+    try:
+        return LlamaSpec(hidden=hidden, layers=_int(d, "num_hidden_layers"), heads=heads, kv_heads=kv,
+                         head_dim=head_dim, ffn=_int(d, "intermediate_size"), vocab=_int(d, "vocab_size"),
+                         rope_theta=_num(d, "rope_theta", 10000.0), rms_eps=_num(d, "rms_norm_eps", 1e-5),
+                         max_position=_int(d, "max_position_embeddings", default=4096), dtype=dtype,
+                         experts=experts, experts_per_token=topk, fp8_block=fp8)
+    except SpecError as e:
+        raise ConfigReaderError(str(e)) from None
+
+
+def to_config(spec: LlamaSpec) -> Dict[str, Any]:
+    """The config.json of a spec (used to write synthetic checkpoints)."""
+    d = {"architectures": ["MixtralForCausalLM" if spec.is_moe else "LlamaForCausalLM"],
+         "model_type": "mixtral" if spec.is_moe else "llama", "vocab_size": spec.vocab, "hidden_size": spec.hidden,
+         "intermediate_size": spec.ffn, "num_hidden_layers": spec.layers, "num_attention_heads": spec.heads,
+         "num_key_value_heads": spec.kv_heads, "head_dim": spec.head_dim,
+         "max_position_embeddings": spec.max_position, "rope_theta": spec.rope_theta, "rms_norm_eps": spec.rms_eps,
+         "tie_word_embeddings": False, "hidden_act": "silu", "rope_scaling": None,
+         "torch_dtype": "bfloat16" if spec.dtype == "bf16" else "float32"}
+    if spec.is_moe:
+        d["num_local_experts"] = spec.experts
+        d["num_experts_per_tok"] = spec.experts_per_token
+    if spec.fp8_block:
+        d["quantization_config"] = {"quant_method": "fp8", "weight_block_size": [128, 128]}
+    return d
+
+
+def sha256_file(path: str) -> str:
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 20), b""):
+            h.update(chunk)
+    return h.hexdigest()

@@ -12,6 +12,7 @@ import json
 import mmap
 import os
 import struct
+import warnings
 from dataclasses import dataclass
 from typing import Dict, Iterable, List, Mapping, Optional, Tuple
 
@@ -121,7 +122,10 @@ class SafetensorsFile:
         dt, _ = _DTYPES[m.dtype]
         start = self.data_start + m.begin
         arr = np.frombuffer(self._mm, dtype=np.uint8, count=m.nbytes, offset=start)
-        t = torch.frombuffer(arr, dtype=torch.uint8) if m.nbytes else torch.empty(0, dtype=torch.uint8)
+        with warnings.catch_warnings():
+            # the view is read-only by construction (the mmap is opened read-only)
+            warnings.simplefilter("ignore", UserWarning)
+            t = torch.frombuffer(arr, dtype=torch.uint8) if m.nbytes else torch.empty(0, dtype=torch.uint8)
         return t.view(dt).reshape(m.shape)
 
     def unchanged(self) -> bool:

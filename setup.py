@@ -29,8 +29,9 @@ cuda_sources = [
 cuda_sources += [os.path.join("csrc/kernels", f) for f in sorted(os.listdir(os.path.join(CSRC, "kernels")))
                  if f.endswith(".cu") and os.path.join("csrc/kernels", f) not in cuda_sources]
 
-host_sources = sorted(os.path.join("csrc/host", f) for f in os.listdir(os.path.join(CSRC, "host"))
-                      if f.endswith(".cpp"))
+_host_dir = os.path.join(CSRC, "host")
+host_sources = sorted(os.path.join("csrc/host", f) for f in os.listdir(_host_dir)
+                      if f.endswith(".cpp")) if os.path.isdir(_host_dir) else []
 
 NVCC_FLAGS = [
     "-O3",
