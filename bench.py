@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--step-token-budget", type=int, default=8192)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                    help="row-parallel all-reduce: fused into the GEMM kernel, or NCCL after it")
     ap.add_argument("--json-out", default="")
     ap.add_argument("--profile", default="", help="write a per-kernel time table of one extra pass here")
     return ap.parse_args()
@@ -145,8 +147,13 @@ def main():
     comm = None
     if world > 1:
         init_distributed("nccl", device_id=local)
-        comm = TPComm()
     spec = specs.PRESETS[args.model]()
+    if world > 1:
+        if args.impl == "ours" and args.comm == "fused":
+            from lunaflux_b200.parallel.fused import FusedTPComm
+            comm = FusedTPComm(args.step_token_budget + args.requests, spec.hidden, dev)
+        else:
+            comm = TPComm()
     if args.layers:
         spec = spec.with_layers(args.layers)
     shard = TPShard(rank, world, spec)
@@ -237,7 +244,7 @@ def main():
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded uniform prompts, random-init N(0,0.02) weights)",
         "impl": args.impl,
         "config": {"model": f"{args.model} ({spec.layers} layers)", "global_batch": args.requests,
-                   "seq_len": args.prompt_len, "output_len": args.output_len, "parallelism": f"tp{world}",
+                   "seq_len": args.prompt_len, "output_len": args.output_len, "parallelism": f"tp{world}", "comm": (args.comm if world > 1 else "none"),
                    "l2": "weights (16 GB) and KV (>10 GB) exceed L2 every step; no flush needed",
                    "engine_iterations_per_step": steps_run / args.steps},
         "ttft_p50_ms": round(statistics.median(ttfts), 2) if ttfts else None,
@@ -266,7 +273,14 @@ def main():
                 f.write(table)
             print(table)
     if world > 1:
-        dist.destroy_process_group()
+        # Captured CUDA graphs still reference the NCCL communicator, and tearing
+        # it down under them can block; every rank is past its last collective
+        # here, so synchronise once more and leave the process directly.
+        torch.cuda.synchronize()
+        dist.barrier()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
     return 0
 
 

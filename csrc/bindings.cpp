@@ -55,6 +55,43 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, int64_t epi, 
   lf::gemm::run(a, (int)epi, (int)bn, stream(), wsp, ws_elems);
 }
 
+// GEMM + all-reduce over the tensor-parallel group.  Pointers are raw device
+// addresses of this rank's symmetric slot, its multicast address (0 if none)
+// and every rank's slot; the same for the int32 arrival counters.
+void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, c10::optional<at::Tensor> ws,
+                    int64_t local, int64_t mc, std::vector<int64_t> peers, int64_t cnt_local, int64_t cnt_mc,
+                    std::vector<int64_t> cnt_peers, int64_t cnt_capacity) {
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  check_rowmajor(D, "D");
+  LF_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && D.scalar_type() == at::kBFloat16,
+           "gemm_allreduce is bf16");
+  LF_CHECK(peers.size() == cnt_peers.size() && !peers.empty() && peers.size() <= (size_t)lf::gemm::kMaxRanks,
+           "gemm_allreduce: peer lists");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  LF_CHECK(D.size(0) == M && D.size(1) == N, "gemm_allreduce output must be [M, N]");
+  lf::gemm::ArArgs ar{};
+  ar.local = reinterpret_cast<__nv_bfloat16*>(local);
+  ar.mc = reinterpret_cast<__nv_bfloat16*>(mc);
+  for (size_t i = 0; i < peers.size(); ++i) {
+    ar.peer[i] = reinterpret_cast<const __nv_bfloat16*>(peers[i]);
+    ar.cnt_peer[i] = reinterpret_cast<int*>(cnt_peers[i]);
+  }
+  ar.cnt_local = reinterpret_cast<int*>(cnt_local);
+  ar.cnt_mc = reinterpret_cast<int*>(cnt_mc);
+  ar.world = (int)peers.size();
+  ar.cnt_capacity = (int)cnt_capacity;
+  float* wsp = nullptr;
+  int64_t ws_elems = 0;
+  if (ws.has_value()) {
+    wsp = ws->data_ptr<float>();
+    ws_elems = ws->numel();
+  }
+  c10::cuda::CUDAGuard g(A.device());
+  lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), B.stride(0), D.stride(0)};
+  lf::gemm::run_allreduce(a, ar, stream(), wsp, ws_elems);
+}
+
 int64_t gemm_plan_splitk(int64_t M, int64_t N, int64_t K) {
   int kb = 0;
   return lf::gemm::plan_splitk(M, N, K, &kb);
@@ -228,6 +265,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "D = A @ B^T on tcgen05 (epi 0 bf16, 1 fp32, 2 SwiGLU)", py::arg("A"), py::arg("B"),
         py::arg("D"), py::arg("epi") = 0, py::arg("bn") = 0, py::arg("ws") = py::none());
   m.def("gemm_plan_splitk", &gemm_plan_splitk);
+  m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_choose_bn", &gemm_choose_bn);
   m.def("embed", &embed);
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"));

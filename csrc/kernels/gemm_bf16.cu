@@ -121,7 +121,8 @@ static int num_sms() {
 }
 
 template <int BN, int STAGES, int EPI>
-static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int kb_per = 0, float* ws = nullptr) {
+static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int kb_per = 0, float* ws = nullptr,
+                   const ArArgs& ar = ArArgs{}) {
   using S = Smem<BN, STAGES>;
   auto kfn = gemm_bf16_kernel<BN, STAGES, EPI>;
   static bool attr_set = false;
@@ -135,9 +136,9 @@ static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int k
   const int grid = tiles < num_sms() ? tiles : num_sms();
   if (kb_per <= 0) kb_per = (a.K + BK - 1) / BK;
   if (EPI == kSplitF32) {
-    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, ws, a.M, a.N, a.K, a.N, splits, kb_per);
+    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, ws, a.M, a.N, a.K, a.N, splits, kb_per, ArArgs{});
   } else {
-    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, splits, kb_per);
+    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, splits, kb_per, ar);
   }
 }
 
@@ -215,6 +216,35 @@ void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws, int
       throw std::runtime_error("lunaflux gemm: unsupported BN");
   }
 #undef LF_GEMM_CASE
+}
+
+// GEMM + tensor-parallel all-reduce in one kernel: D = sum over ranks of
+// A_r . B_r^T (row-parallel projections).  Skinny shapes use split-K with the
+// all-reduce fused into the persistent finalize kernel instead.
+void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, float* ws, int64_t ws_elems) {
+  if (a.M <= 0) return;
+  if (ar.world < 1 || ar.world > kMaxRanks) throw std::runtime_error("lunaflux gemm_allreduce: bad world size");
+  if (a.N % 32 != 0 || a.K % 8 != 0) throw std::runtime_error("lunaflux gemm_allreduce: N % 32 and K % 8 required");
+  int kb_per = 0;
+  const int splits = (ws != nullptr && a.N % 256 == 0) ? plan_splitk(a.M, a.N, a.K, &kb_per) : 1;
+  if (splits > 1 && (int64_t)splits * a.M * a.N <= ws_elems) {
+    const int items = a.M * ((a.N + 1023) / 1024);
+    if (items > ar.cnt_capacity) throw std::runtime_error("lunaflux gemm_allreduce: too many rows for the counters");
+    launch<256, 4, kSplitF32>(a, stream, splits, kb_per, ws);
+    const int grid = items < 4 * num_sms() ? items : 4 * num_sms();
+    splitk_finalize_ar_kernel<<<grid, 256, 0, stream>>>(ws, reinterpret_cast<__nv_bfloat16*>(a.D), a.M, a.N, a.ldd,
+                                                        splits, ar);
+    return;
+  }
+  const int bn = choose_bn(a.M, a.N, kStoreBf16);
+  const int tiles = ((a.M + BM - 1) / BM) * (a.N / bn);
+  if (tiles > ar.cnt_capacity) throw std::runtime_error("lunaflux gemm_allreduce: too many tiles for the counters");
+  switch (bn) {
+    case 256: launch<256, 4, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
+    case 128: launch<128, 6, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
+    case 64: launch<64, 8, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
+    default: launch<32, 8, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
+  }
 }
 
 }  // namespace gemm

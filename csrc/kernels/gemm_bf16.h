@@ -1,5 +1,6 @@
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -22,6 +23,28 @@ struct GemmArgs {
 // (deterministic; needs splits * M * N <= ws_elems, else no split).
 void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws = nullptr, int64_t ws_elems = 0);
 int plan_splitk(int M, int N, int K, int* kb_per_out);
+
+// Peer view of one tensor-parallel group for the fused GEMM + all-reduce
+// epilogue.  `local` is this rank's slot of a symmetric (every rank holds one,
+// same size) bf16 buffer [rows, N]; `mc` is the NVLink-multicast address of
+// the same slot (null when the fabric has no multicast); `peer[r]` are the
+// slot's addresses on every rank.  `cnt_*` are per-tile int32 arrival counters
+// laid out the same way.
+constexpr int kMaxRanks = 8;
+struct ArArgs {
+  __nv_bfloat16* local;
+  __nv_bfloat16* mc;
+  const __nv_bfloat16* peer[kMaxRanks];
+  int* cnt_local;
+  int* cnt_mc;
+  int* cnt_peer[kMaxRanks];
+  int world;
+  int cnt_capacity;
+};
+
+// D = sum over the tensor-parallel group of this rank's A . B^T, computed and
+// all-reduced by one kernel over NVLink (see ArArgs).
+void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, float* ws, int64_t ws_elems);
 int choose_bn(int M, int N, int epi);
 
 CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,

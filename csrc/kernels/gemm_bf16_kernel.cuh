@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "gemm_bf16.h"
 
 namespace lf {
 namespace gemm {
@@ -15,7 +16,77 @@ constexpr int BM = 128;
 constexpr int BK = 64;                 // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;
 
-enum Epi : int { kStoreBf16 = 0, kStoreF32 = 1, kSwiGLU = 2, kSplitF32 = 3 };
+enum Epi : int { kStoreBf16 = 0, kStoreF32 = 1, kSwiGLU = 2, kSplitF32 = 3, kAllReduceBf16 = 4 };
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Publishes "this rank's piece with index `idx` is in its buffer" to every
+// rank: one multicast reduction (NVSwitch fans it out) or one remote atomic
+// per rank.  Caller has ordered its data stores before this (bar + fence).
+__device__ __forceinline__ void ar_signal(const ArArgs& ar, int idx) {
+  if (ar.cnt_mc != nullptr) {
+    asm volatile("multimem.red.release.sys.global.add.s32 [%0], 1;" ::"l"(ar.cnt_mc + idx) : "memory");
+  } else {
+    for (int r = 0; r < ar.world; ++r)
+      asm volatile("red.release.sys.global.add.s32 [%0], 1;" ::"l"(ar.cnt_peer[r] + idx) : "memory");
+  }
+}
+
+// Waits (bounded) until every rank published piece `idx`, then re-arms the
+// counter.  Returns false after recording kErrPeerTimeout.
+__device__ __forceinline__ bool ar_wait(const ArArgs& ar, int idx) {
+  int* c = ar.cnt_local + idx;
+  if (ld_acquire_sys(c) < ar.world) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (ld_acquire_sys(c) < ar.world) {
+      if ((++spins & 63u) == 0) {
+        if (error_pending()) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_error(kErrPeerTimeout, (unsigned long long)idx);
+          return false;
+        }
+      }
+    }
+  }
+  // Every rank has arrived; nobody signals this slot again until this rank's
+  // next operation on the other slot has completed, so a plain reset is safe.
+  atomicSub(c, ar.world);
+  return true;
+}
+
+// Sum over ranks of 8 bf16 at element offset `off` of the slot (fp32 accumulation).
+__device__ __forceinline__ uint4 ar_load_sum8(const ArArgs& ar, size_t off) {
+  uint4 r;
+  if (ar.mc != nullptr) {
+    asm volatile("multimem.ld_reduce.weak.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(ar.mc + off)
+                 : "memory");
+    return r;
+  }
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int k = 0; k < ar.world; ++k) {
+    uint4 v;
+    asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(ar.peer[k] + off)
+                 : "memory");
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += __bfloat162float(b[e]);
+  }
+  return make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                    pack_bf16x2(acc[6], acc[7]));
+}
 
 template <int BN, int STAGES>
 struct Smem {
@@ -36,7 +107,7 @@ template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M,
-                     int N, int K, int ldd, int splits, int kb_per_split) {
+                     int N, int K, int ldd, int splits, int kb_per_split, ArArgs ar) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -76,6 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  __shared__ volatile int s_ar_ok;  // fused all-reduce: did the wait succeed
 
   if (warp == 0) {
     if (lane == 0) {
@@ -196,7 +268,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j)
                 packed[j] = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + n0 + c;
+              // kAllReduceBf16 first publishes the partial tile in this rank's
+              // symmetric slot (row stride N); the reduced tile goes to `out` below.
+              __nv_bfloat16* dst = EPI == kAllReduceBf16
+                                       ? ar.local + (size_t)row * N + n0 + c
+                                       : reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + n0 + c;
               uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
               for (int j = 0; j < 4; ++j)
@@ -206,7 +282,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
+      mbar_arrive(&tempty_bar[acc]);  // the MMA warp may start the next tile now
+      if constexpr (EPI == kAllReduceBf16) {
+        // Tile-level all-reduce: publish, wait for the same tile of every
+        // rank, then read the sum through the NVLink fabric while the MMA warp
+        // already computes this CTA's next tile.
+        named_bar_sync(1, 128);
+        if (threadIdx.x == 64) {
+          fence_acq_rel_sys();
+          ar_signal(ar, tile);
+          s_ar_ok = ar_wait(ar, tile) ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        if (s_ar_ok && row < M) {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + n0;
+#pragma unroll 4
+          for (int c = 0; c < BN; c += 8)
+            *reinterpret_cast<uint4*>(dst + c) = ar_load_sum8(ar, (size_t)row * N + n0 + c);
+        }
+      }
     }
   }
 
@@ -215,6 +309,67 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kCols);
+  }
+}
+
+// Sum over ranks of 4 bf16 at element offset `off` of the slot (fp32 accumulation).
+__device__ __forceinline__ uint2 ar_load_sum4(const ArArgs& ar, size_t off) {
+  uint2 r;
+  if (ar.mc != nullptr) {
+    asm volatile("multimem.ld_reduce.weak.global.add.acc::f32.v2.bf16x2 {%0, %1}, [%2];"
+                 : "=r"(r.x), "=r"(r.y)
+                 : "l"(ar.mc + off)
+                 : "memory");
+    return r;
+  }
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k = 0; k < ar.world; ++k) {
+    uint2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(ar.peer[k] + off)
+                 : "memory");
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[e] += __bfloat162float(b[e]);
+  }
+  return make_uint2(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]));
+}
+
+// Split-K finalisation fused with the tensor-parallel all-reduce (persistent:
+// the grid never exceeds what is resident, and every rank walks the items in
+// the same order, so the cross-rank waits cannot deadlock).  Item = one row x
+// 1024 columns: sum the split slabs, publish the bf16 partial in this rank's
+// symmetric slot, signal, wait for every rank's same item, read the sum.
+static __global__ void __launch_bounds__(256) splitk_finalize_ar_kernel(const float* __restrict__ ws,
+                                                                 __nv_bfloat16* __restrict__ out, int M, int N,
+                                                                 int64_t ldd, int splits, ArArgs ar) {
+  __shared__ volatile int ok;
+  const size_t slab = (size_t)M * N;
+  const int chunks = (N + 1023) / 1024;
+  const int items = M * chunks;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int row = item / chunks;
+    const int col = (item % chunks) * 1024 + threadIdx.x * 4;
+    if (col < N) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < splits; ++sp) {
+        const float4 p = *reinterpret_cast<const float4*>(ws + sp * slab + (size_t)row * N + col);
+        v.x += p.x;
+        v.y += p.y;
+        v.z += p.z;
+        v.w += p.w;
+      }
+      *reinterpret_cast<uint2*>(ar.local + (size_t)row * N + col) =
+          make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      fence_acq_rel_sys();
+      ar_signal(ar, item);
+      ok = ar_wait(ar, item) ? 1 : 0;
+    }
+    __syncthreads();
+    if (ok && col < N) *reinterpret_cast<uint2*>(out + (size_t)row * ldd + col) = ar_load_sum4(ar, (size_t)row * N + col);
+    __syncthreads();
   }
 }
 

@@ -1,0 +1,83 @@
+"""Fused GEMM + all-reduce on 2+ GPUs (one process per GPU, NCCL bootstrap).
+
+Every rank multiplies its own A_r by its own B_r; the fused kernel must return
+sum_r A_r . B_r^T on every rank, for the tile path and the split-K path, over
+many calls in a row (exercising both ping-pong slots and counter re-arming).
+Reference: the fp32 products all-reduced with NCCL.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+SHAPES = [(256, 4096, 512), (1, 4096, 1792), (8192, 4096, 512), (300, 2048, 1024), (37, 4096, 14336 // 8)]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    try:
+        from lunaflux_b200.parallel.comm import init_distributed
+        from lunaflux_b200.parallel.fused import FusedTPComm
+        init_distributed("nccl", timeout_s=120, device_id=rank)
+        comm = FusedTPComm(8192, 4096, dev)
+        C = comm.C
+        ws = torch.zeros(512 * 32768, device=dev)
+        errs = []
+        for it in range(3):
+            for (M, N, K) in SHAPES:
+                g = torch.Generator(device=dev).manual_seed(1000 * rank + 7 * it + M)
+                A = torch.randn(M, K, device=dev, generator=g).bfloat16()
+                B = (torch.randn(N, K, device=dev, generator=g) * 0.05).bfloat16()
+                ref = A.float() @ B.float().t()
+                dist.all_reduce(ref)
+                out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                comm.gemm_allreduce(A, B, out, ws)
+                torch.cuda.synchronize(dev)
+                code = C.read_error(True)[0]
+                err = (out.float() - ref).abs()
+                tol = 3e-2 + 3e-2 * ref.abs()
+                errs.append((M, N, K, code, int((err > tol).sum().item()), float(err.max().item())))
+        q.put((rank, errs, comm.multicast))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e), None))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_gemm_allreduce_matches_nccl():
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, errs, mc = q.get(timeout=300)
+        res[r] = (errs, mc)
+    for p in procs:
+        p.join(timeout=60)
+    for r, (errs, mc) in res.items():
+        assert not isinstance(errs, str), errs
+        for (M, N, K, code, bad, mx) in errs:
+            assert code == 0, f"rank {r} {M}x{N}x{K}: device error {code}"
+            assert bad == 0, f"rank {r} {M}x{N}x{K}: {bad} elements off (max {mx}); multicast={mc}"
