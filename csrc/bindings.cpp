@@ -10,6 +10,7 @@
 #include "kernels/attention.h"
 #include "kernels/elementwise.h"
 #include "kernels/gemm_bf16.h"
+#include "kernels/moe.h"
 #include "kernels/runtime.h"
 
 namespace {
@@ -90,6 +91,53 @@ void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, c10
   c10::cuda::CUDAGuard g(A.device());
   lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), B.stride(0), D.stride(0)};
   lf::gemm::run_allreduce(a, ar, stream(), wsp, ws_elems);
+}
+
+void gemm_grouped(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const at::Tensor& groups,
+                  int64_t num_groups, int64_t epi) {
+  check_rowmajor(A, "A");
+  check_rowmajor(D, "D");
+  LF_CHECK(B.is_contiguous() && B.dim() == 3 && B.size(0) >= num_groups, "grouped B must be [groups, N, K]");
+  LF_CHECK(groups.scalar_type() == at::kInt && groups.numel() >= num_groups + 1, "groups must be int32 [groups+1]");
+  const int M = A.size(0), N = B.size(1), K = A.size(1);
+  LF_CHECK(B.size(2) == K, "grouped K mismatch");
+  LF_CHECK(D.size(0) == M && D.size(1) == (epi == 2 ? N / 2 : N), "grouped output shape");
+  c10::cuda::CUDAGuard g(A.device());
+  lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), K, D.stride(0)};
+  lf::gemm::run_grouped(a, groups.data_ptr<int32_t>(), (int)num_groups, (int)epi, stream());
+}
+
+void moe_route(const at::Tensor& h, const at::Tensor& wr, c10::optional<at::Tensor> bias, int64_t topk,
+               at::Tensor& ids, at::Tensor& weights) {
+  LF_CHECK(h.is_contiguous() && wr.is_contiguous() && wr.scalar_type() == at::kFloat, "route operands");
+  const int E = wr.size(0);
+  LF_CHECK(E == 2 || E == 4 || E == 8 || E == 16, "router supports 2/4/8/16 experts");
+  LF_CHECK(topk >= 1 && topk <= 8 && topk <= E && h.size(1) % 256 == 0, "route shape");
+  c10::cuda::CUDAGuard g(h.device());
+  lf::moe::route(h.data_ptr(), wr.data_ptr<float>(), bias.has_value() ? bias->data_ptr<float>() : nullptr,
+                 h.size(0), h.size(1), E, topk, ids.data_ptr<int32_t>(), weights.data_ptr<float>(), stream());
+}
+
+void moe_align(const at::Tensor& ids, int64_t T, int64_t topk, int64_t e0, int64_t El, at::Tensor& groups,
+               at::Tensor& perm, at::Tensor& slot) {
+  LF_CHECK(El >= 1 && El <= 64, "1..64 local experts");
+  c10::cuda::CUDAGuard g(ids.device());
+  lf::moe::align(ids.data_ptr<int32_t>(), T, topk, e0, El, perm.numel(), groups.data_ptr<int32_t>(),
+                 perm.data_ptr<int32_t>(), slot.data_ptr<int32_t>(), stream());
+}
+
+void moe_gather(const at::Tensor& h, const at::Tensor& perm, const at::Tensor& groups, int64_t El, int64_t topk,
+                at::Tensor& out) {
+  c10::cuda::CUDAGuard g(h.device());
+  lf::moe::gather(h.data_ptr(), perm.data_ptr<int32_t>(), groups.data_ptr<int32_t>(), El, topk, h.size(1),
+                  out.size(0), out.data_ptr(), stream());
+}
+
+void moe_combine(const at::Tensor& y, const at::Tensor& slot, const at::Tensor& w, int64_t T, int64_t topk,
+                 at::Tensor& out) {
+  c10::cuda::CUDAGuard g(y.device());
+  lf::moe::combine(y.data_ptr(), slot.data_ptr<int32_t>(), w.data_ptr<float>(), T, topk, y.size(1), out.data_ptr(),
+                   stream());
 }
 
 int64_t gemm_plan_splitk(int64_t M, int64_t N, int64_t K) {
@@ -266,6 +314,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("D"), py::arg("epi") = 0, py::arg("bn") = 0, py::arg("ws") = py::none());
   m.def("gemm_plan_splitk", &gemm_plan_splitk);
   m.def("gemm_allreduce", &gemm_allreduce);
+  m.def("gemm_grouped", &gemm_grouped);
+  m.def("moe_route", &moe_route);
+  m.def("moe_align", &moe_align);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_combine", &moe_combine);
   m.def("gemm_choose_bn", &gemm_choose_bn);
   m.def("embed", &embed);
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"));

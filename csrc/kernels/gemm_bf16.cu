@@ -136,9 +136,9 @@ static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int k
   const int grid = tiles < num_sms() ? tiles : num_sms();
   if (kb_per <= 0) kb_per = (a.K + BK - 1) / BK;
   if (EPI == kSplitF32) {
-    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, ws, a.M, a.N, a.K, a.N, splits, kb_per, ArArgs{});
+    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, ws, a.M, a.N, a.K, a.N, splits, kb_per, ArArgs{}, nullptr, 0);
   } else {
-    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, splits, kb_per, ar);
+    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, splits, kb_per, ar, nullptr, 0);
   }
 }
 
@@ -244,6 +244,42 @@ void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, flo
     case 128: launch<128, 6, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
     case 64: launch<64, 8, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
     default: launch<32, 8, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
+  }
+}
+
+// Grouped GEMM (mixture-of-experts): A [M_max, K] rows in expert segments
+// groups[0..num_groups] (device memory, multiples of BM), B [num_groups * N, K]
+// the experts' stacked weights, D [M_max, N] (or [M_max, N / 2] for SwiGLU).
+template <int BN, int STAGES, int EPI>
+static void launch_grouped(const GemmArgs& a, const int* groups, int num_groups, cudaStream_t stream) {
+  using S = Smem<BN, STAGES>;
+  auto kfn = gemm_bf16_kernel<BN, STAGES, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    attr_set = true;
+  }
+  CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
+  CUtensorMap tb = cached_tmap_bf16(a.B, (uint64_t)a.N * num_groups, a.K, a.ldb, BN);
+  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, 1, (a.K + BK - 1) / BK, ArArgs{},
+                                             groups, num_groups);
+}
+
+void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, cudaStream_t stream) {
+  if (a.M <= 0) return;
+  if (a.M % BM != 0) throw std::runtime_error("lunaflux grouped gemm: M_max must be a multiple of 128");
+  if (a.K % 8 != 0 || a.N % 64 != 0) throw std::runtime_error("lunaflux grouped gemm: K % 8 and N % 64 required");
+  const int bn = a.N % 256 == 0 && ((a.M / BM) * (a.N / 256) >= num_sms()) ? 256 : (a.N % 128 == 0 ? 128 : 64);
+  if (epi == kSwiGLU) {
+    if (bn == 256) launch_grouped<256, 4, kSwiGLU>(a, groups, num_groups, stream);
+    else if (bn == 128) launch_grouped<128, 6, kSwiGLU>(a, groups, num_groups, stream);
+    else launch_grouped<64, 8, kSwiGLU>(a, groups, num_groups, stream);
+  } else {
+    if (bn == 256) launch_grouped<256, 4, kStoreBf16>(a, groups, num_groups, stream);
+    else if (bn == 128) launch_grouped<128, 6, kStoreBf16>(a, groups, num_groups, stream);
+    else launch_grouped<64, 8, kStoreBf16>(a, groups, num_groups, stream);
   }
 }
 

@@ -103,11 +103,24 @@ constexpr uint32_t tmem_cols() {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+// Grouped GEMM: row block m0 -> its segment (-1 when past the used rows).
+__device__ __forceinline__ int group_of(const int* groups, int num_groups, int m0) {
+  if (m0 >= groups[num_groups]) return -1;
+  int g = 0;
+  while (g + 1 < num_groups && groups[g + 1] <= m0) ++g;
+  return g;
+}
+
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M,
-                     int N, int K, int ldd, int splits, int kb_per_split, ArArgs ar) {
+                     int N, int K, int ldd, int splits, int kb_per_split, ArArgs ar,
+                     const int* __restrict__ groups, int num_groups) {
+  // Grouped mode (groups != nullptr, mixture-of-experts): A's rows are split
+  // into num_groups segments, groups[g]..groups[g+1] (each a multiple of BM,
+  // read from device memory), and segment g multiplies B rows [g*N, (g+1)*N).
+  // M is then an upper bound on groups[num_groups]; blocks past it are skipped.
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -161,13 +174,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb1 = min(num_kb, kb0 + kb_per_split);
         const int m0 = (tile % num_m) * BM;
         const int n0 = (tile / num_m) * BN;
+        int brow = n0;
+        if (groups != nullptr) {
+          const int g = group_of(groups, num_groups, m0);
+          if (g < 0) continue;
+          brow = g * N + n0;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, 1)) { ok = false; break; }
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
           tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, m0);
-          tma_load_2d_hint(sb, &tmap_b, &full_bar[stage], kb * BK, n0, pol_b);
+          tma_load_2d_hint(sb, &tmap_b, &full_bar[stage], kb * BK, brow, pol_b);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -182,6 +201,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x, ++local) {
         const int kb0 = (unit / num_tiles) * kb_per_split;
         const int kb1 = min(num_kb, kb0 + kb_per_split);
+        if (groups != nullptr && group_of(groups, num_groups, ((unit % num_tiles) % num_m) * BM) < 0) {
+          --local;  // skipped units use no accumulator
+          continue;
+        }
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, 2)) break;
@@ -209,6 +232,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++local) {
       const int tile = unit % num_tiles;
+      if (groups != nullptr && group_of(groups, num_groups, (tile % num_m) * BM) < 0) {
+        --local;
+        continue;
+      }
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, 4)) break;

@@ -75,6 +75,8 @@ class ModelRunner:
         self.full_logits = (torch.empty(R, s.vocab, dtype=torch.float32, device=dev)
                             if sh.size > 1 else self.logits)
         self.out_tok = torch.zeros(R, dtype=torch.int32, device=dev)
+        if s.is_moe:
+            self._init_moe(T, dev)
         self.keys_local = torch.zeros(R, dtype=torch.int64, device=dev)
         self.keys_all = torch.zeros(R * sh.size, dtype=torch.int64, device=dev)
         # split-K GEMM workspace (kept all-zero between GEMMs) and split-KV decode partials
@@ -185,8 +187,44 @@ class ModelRunner:
             self.ops.gemm(A, W, out, 0, ws)
             self.comm.all_reduce(out)
 
+    def _moe_rows(self, T: int) -> int:
+        """Rows of the expert-ordered activations for T tokens: every
+        assignment plus up to 127 padding rows per local expert."""
+        return -(-(T * self.spec.experts_per_token + self.moe_El * 127) // 128) * 128
+
+    def _init_moe(self, T: int, dev):
+        s = self.spec
+        k = s.experts_per_token
+        self.moe_El = s.experts // self.w.ep_size
+        self.moe_e0 = self.w.ep_rank * self.moe_El
+        rows = self._moe_rows(T)
+        Fp = self.w.layers[0].experts_d.shape[-1]
+        self.moe_ids = torch.zeros(T, k, dtype=torch.int32, device=dev)
+        self.moe_w = torch.zeros(T, k, dtype=torch.float32, device=dev)
+        self.moe_groups = torch.zeros(self.moe_El + 1, dtype=torch.int32, device=dev)
+        self.moe_perm = torch.zeros(rows, dtype=torch.int32, device=dev)
+        self.moe_slot = torch.zeros(T * k, dtype=torch.int32, device=dev)
+        self.moe_x = torch.zeros(rows, s.hidden, dtype=self.dtype, device=dev)
+        self.moe_act = torch.zeros(rows, Fp, dtype=self.dtype, device=dev)
+        self.moe_y = torch.zeros(rows, s.hidden, dtype=self.dtype, device=dev)
+        self.router_bias: Optional[torch.Tensor] = None  # fp32 [E] logit bias (load-skew experiments)
+
     def moe(self, h, delta, lw):
-        raise NotImplementedError("MoE layers are served by MoERunner")
+        """Routed SwiGLU experts: route -> align -> gather -> grouped gate/up
+        GEMM (SwiGLU epilogue) -> grouped down GEMM -> weighted combine, then
+        the sum over ranks (experts or expert shards live on different ranks)."""
+        ops, k, El = self.ops, self.spec.experts_per_token, self.moe_El
+        T = h.shape[0]
+        rows = self._moe_rows(T)
+        ids, w = self.moe_ids[:T], self.moe_w[:T]
+        ops.moe_route(h, lw.router, self.router_bias, k, ids, w)
+        ops.moe_align(ids, T, k, self.moe_e0, El, self.moe_groups, self.moe_perm[:rows], self.moe_slot[:T * k])
+        ops.moe_gather(h, self.moe_perm[:rows], self.moe_groups, El, k, self.moe_x[:rows])
+        ops.gemm_grouped(self.moe_x[:rows], lw.experts_gu, self.moe_act[:rows], self.moe_groups, El, 2)
+        ops.gemm_grouped(self.moe_act[:rows], lw.experts_d, self.moe_y[:rows], self.moe_groups, El, 0)
+        ops.moe_combine(self.moe_y[:rows], self.moe_slot[:T * k], w, T, k, delta)
+        if self.comm is not None:
+            self.comm.all_reduce(delta)
 
     # ------------------------------------------------------------------ one step
     def _upload(self, hs: HostStep, host_buf: torch.Tensor):

@@ -120,6 +120,8 @@ class ModelWeights:
     layers: List[LayerWeights]
     norm: torch.Tensor
     lm_head: torch.Tensor                      # [V / tp, H]
+    ep_rank: int = 0                           # expert-parallel position (MoE)
+    ep_size: int = 1
 
     def nbytes(self) -> int:
         n = self.embed.nbytes + self.norm.nbytes + self.lm_head.nbytes
@@ -215,4 +217,5 @@ def build_runtime(spec: LlamaSpec, source: Source, shard: Optional[TPShard] = No
     vr = shard.vocab_range
     lm_head = get(head_name)[vr.start:vr.stop].to(dtype).contiguous()
     return ModelWeights(spec=spec, shard=shard, embed=embed, layers=layers,
-                        norm=get("model.norm.weight").to(dtype).contiguous(), lm_head=lm_head)
+                        norm=get("model.norm.weight").to(dtype).contiguous(), lm_head=lm_head,
+                        ep_rank=ep_rank, ep_size=ep_size)

@@ -80,3 +80,24 @@ class KernelOps:
     def keys_to_tokens(self, keys, rows, ranks, out):
         self.launches += 1
         self.C.keys_to_tokens(keys, rows, ranks, out)
+
+    # ---------------------------------------------------------------- MoE
+    def moe_route(self, h, router, bias, topk, ids, weights):
+        self.launches += 1
+        self.C.moe_route(h, router, bias, topk, ids, weights)
+
+    def moe_align(self, ids, T, topk, e0, El, groups, perm, slot):
+        self.launches += 1
+        self.C.moe_align(ids, T, topk, e0, El, groups, perm, slot)
+
+    def moe_gather(self, h, perm, groups, El, topk, out):
+        self.launches += 1
+        self.C.moe_gather(h, perm, groups, El, topk, out)
+
+    def gemm_grouped(self, A, B, out, groups, num_groups, epi):
+        self.launches += 1
+        self.C.gemm_grouped(A, B, out, groups, num_groups, epi)
+
+    def moe_combine(self, y, slot, w, T, topk, out):
+        self.launches += 1
+        self.C.moe_combine(y, slot, w, T, topk, out)

@@ -164,3 +164,52 @@ class TorchOps:
         kk = k ^ torch.iinfo(torch.int64).min
         best = k.gather(0, kk.argmax(0)[None])[0]
         out[:rows] = (0xFFFFFFFF - (best & 0xFFFFFFFF)).to(torch.int32)
+
+    # ---------------------------------------------------------------- MoE
+    def moe_route(self, h, router, bias, topk, ids, weights):
+        logits = h.float() @ router.float().t()
+        if bias is not None:
+            logits = logits + bias
+        p = logits.softmax(-1)
+        w, i = p.topk(topk, -1)
+        T = h.shape[0]
+        ids[:T] = i.to(torch.int32)
+        weights[:T] = w / w.sum(-1, keepdim=True)
+
+    def moe_align(self, ids, T, topk, e0, El, groups, perm, slot):
+        flat = ids[:T].reshape(-1).long().cpu()
+        perm.fill_(-1)
+        slot_h = torch.full((T * topk,), -1, dtype=torch.int32)
+        off = 0
+        offs = []
+        for e in range(El):
+            offs.append(off)
+            sel = (flat == e0 + e).nonzero().flatten()
+            for j, a in enumerate(sel.tolist()):
+                perm[off + j] = a
+                slot_h[a] = off + j
+            off += -(-len(sel) // 128) * 128
+        offs.append(off)
+        groups[:El + 1] = torch.tensor(offs, dtype=torch.int32)
+        slot.view(-1)[:T * topk] = slot_h.to(slot.device)
+
+    def moe_gather(self, h, perm, groups, El, topk, out):
+        used = int(groups[El])
+        p = perm[:used].long()
+        ok = p >= 0
+        out[:used] = 0
+        out[:used][ok] = h[(p[ok] // topk)]
+
+    def gemm_grouped(self, A, B, out, groups, num_groups, epi):
+        g = groups[:num_groups + 1].tolist()
+        for e in range(num_groups):
+            if g[e + 1] > g[e]:
+                self.gemm(A[g[e]:g[e + 1]], B[e], out[g[e]:g[e + 1]], epi)
+
+    def moe_combine(self, y, slot, w, T, topk, out):
+        s = slot.view(-1)[:T * topk].long().view(T, topk)
+        acc = torch.zeros(T, y.shape[1], dtype=torch.float32, device=y.device)
+        for k in range(topk):
+            ok = s[:, k] >= 0
+            acc[ok] += w[:T, k][ok, None].float() * y[s[ok, k]].float()
+        out[:T] = acc.to(out.dtype)

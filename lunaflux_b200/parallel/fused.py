@@ -40,10 +40,6 @@ class FusedTPComm(TPComm):
         self.hidden = hidden
         g = group or dist.group.WORLD
         name = g.group_name
-        try:
-            symm.enable_symm_mem_for_group(name)
-        except Exception:
-            pass
         slot_elems = max_rows * hidden
         self.data = symm.empty(2 * slot_elems, dtype=torch.bfloat16, device=device)
         self.cnt = symm.empty(2 * COUNTER_CAPACITY, dtype=torch.int32, device=device)

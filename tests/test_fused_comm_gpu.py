@@ -22,7 +22,7 @@ def _port():
     return p
 
 
-SHAPES = [(256, 4096, 512), (1, 4096, 1792), (8192, 4096, 512), (300, 2048, 1024), (37, 4096, 14336 // 8)]
+SHAPES = [(256, 4096, 512), (1, 4096, 1792), (8192, 4096, 512), (300, 4096, 1024), (37, 4096, 14336 // 8)]
 
 
 def _worker(rank, world, port, q):
