@@ -10,6 +10,7 @@
 #include "kernels/attention.h"
 #include "kernels/elementwise.h"
 #include "kernels/gemm_bf16.h"
+#include "kernels/gemm_fp8.h"
 #include "kernels/moe.h"
 #include "kernels/runtime.h"
 
@@ -138,6 +139,33 @@ void moe_combine(const at::Tensor& y, const at::Tensor& slot, const at::Tensor& 
   c10::cuda::CUDAGuard g(y.device());
   lf::moe::combine(y.data_ptr(), slot.data_ptr<int32_t>(), w.data_ptr<float>(), T, topk, y.size(1), out.data_ptr(),
                    stream());
+}
+
+void gemm_fp8(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, const at::Tensor& sb, at::Tensor& D,
+              int64_t epi) {
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  check_rowmajor(D, "D");
+  check_rowmajor(sa, "sa");
+  LF_CHECK(A.element_size() == 1 && B.element_size() == 1, "fp8 operands must be 1-byte e4m3");
+  LF_CHECK(sa.scalar_type() == at::kFloat && sb.scalar_type() == at::kFloat && sb.is_contiguous(), "fp8 scales fp32");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  LF_CHECK(B.size(1) == K && K % 128 == 0 && N % 128 == 0, "fp8 gemm: K and N multiples of 128");
+  LF_CHECK(sa.size(0) >= M && sa.size(1) >= K / 128 && sb.numel() >= (int64_t)(N / 128) * (K / 128), "fp8 scales");
+  LF_CHECK(D.size(0) == M && D.size(1) == (epi == 2 ? N / 2 : N), "fp8 gemm output shape");
+  c10::cuda::CUDAGuard g(A.device());
+  lf::fp8::Fp8Args a{A.data_ptr(), B.data_ptr(), sa.data_ptr<float>(), sa.stride(0), sb.data_ptr<float>(), D.data_ptr(),
+                     M, N, K, A.stride(0), B.stride(0), D.stride(0)};
+  lf::fp8::run(a, (int)epi, stream());
+}
+
+void act_quant(const at::Tensor& x, at::Tensor& q, at::Tensor& s) {
+  check_rowmajor(x, "x");
+  LF_CHECK(x.scalar_type() == at::kBFloat16 && q.element_size() == 1 && s.scalar_type() == at::kFloat, "act_quant dtypes");
+  LF_CHECK(q.is_contiguous() && q.size(0) >= x.size(0) && q.size(1) == x.size(1), "act_quant output shape");
+  c10::cuda::CUDAGuard g(x.device());
+  lf::fp8::act_quant(x.data_ptr(), x.stride(0), x.size(0), x.size(1), q.data_ptr(), s.data_ptr<float>(), s.stride(0),
+                     stream());
 }
 
 int64_t gemm_plan_splitk(int64_t M, int64_t N, int64_t K) {
@@ -315,6 +343,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan_splitk", &gemm_plan_splitk);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_grouped", &gemm_grouped);
+  m.def("gemm_fp8", &gemm_fp8);
+  m.def("act_quant", &act_quant);
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);

@@ -1,0 +1,280 @@
+// Block-scaled fp8 GEMM for sm_100a (tcgen05 kind::f8f6f4, e4m3 x e4m3 -> fp32).
+//
+//   D[M, N] = sum_kb  sa[m, kb] * sb[n / 128, kb] * (A8[m, kb] . B8[n, kb]^T)
+//
+// A8: activations, e4m3 [M, K], one fp32 scale per (row, 128-wide K block).
+// B8: weights, e4m3 [N, K], one fp32 scale per 128 x 128 block.
+// This is the DeepSeek-style block scaling of the 70B fp8 configuration; the
+// scales are not MX (ue8m0, 32-wide), so the tensor core cannot apply them.
+// Instead every 128-wide K block is accumulated into its own TMEM buffer
+// (4 MMAs of K = 32), and the epilogue warps read it back with tcgen05.ld,
+// scale it and add it to fp32 register accumulators, while the MMA warp
+// already fills the other TMEM buffer with the next K block.
+//
+// Roles (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer (A: 128 x 128 B box, B: 128 x 128 B box, 128-byte swizzle)
+//   warp 1      TMEM allocation; lane 0 issues the MMAs
+//   warps 2..5  scale-and-accumulate, then the epilogue (bf16 store, fp32
+//               store, or SwiGLU over 32-row interleaved gate/up weights)
+// All waits are bounded (common.cuh); every TMA load fills only its own CTA.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "gemm_bf16.h"
+#include "gemm_fp8.h"
+
+namespace lf {
+namespace fp8 {
+
+constexpr int BM = 128;
+constexpr int BN = 128;      // one weight scale block per tile
+constexpr int BK = 128;      // 128 e4m3 = 128 bytes = one swizzle row = one scale block
+constexpr int STAGES = 6;
+constexpr int kThreads = 192;
+constexpr int kStageBytes = (BM + BN) * BK;
+constexpr int kSmem = STAGES * kStageBytes + 1024 + 256;
+
+enum Epi : int { kBf16 = 0, kF32 = 1, kSwiGLU = 2 };
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    const float* __restrict__ sa, int64_t lds_a, const float* __restrict__ sb, void* __restrict__ out,
+                    int M, int N, int K, int64_t ldd) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull = empty_bar + STAGES;  // [2] per-K-block TMEM buffers
+  uint64_t* tempty = tfull + 2;          // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM, num_n = N / BN, tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+  constexpr uint32_t kCols = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, 31)) { ok = false; break; }
+          uint8_t* sa_s = smem + stage * kStageBytes;
+          mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+          tma_load_2d(sa_s, &tmap_a, &full_bar[stage], kb * BK, m0);
+          tma_load_2d_hint(sa_s + BM * BK, &tmap_b, &full_bar[stage], kb * BK, n0, pol);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0, tb = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        for (int kb = 0; kb < num_kb; ++kb, ++tb) {
+          const int b = tb & 1;
+          if (!mbar_wait(&tempty[b], ((tb >> 1) & 1) ^ 1, 32)) { ok = false; break; }
+          if (!mbar_wait(&full_bar[stage], phase, 33)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * kStageBytes);
+          const uint32_t b_addr = a_addr + BM * BK;
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk)
+            umma_f8_ss(tmem_base + b * BN, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32),
+                       idesc, kk > 0 ? 1u : 0u);
+          umma_commit(&empty_bar[stage]);
+          umma_commit(&tfull[b]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    const int ksb = (K + BK - 1) / BK;  // scale blocks per row
+    uint32_t tb = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
+      const int row = m0 + quad * 32 + lane;
+      const int rr = row < M ? row : M - 1;
+      float acc[BN];
+#pragma unroll
+      for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+      for (int kb = 0; kb < num_kb; ++kb, ++tb) {
+        const int b = tb & 1;
+        if (!mbar_wait(&tfull[b], (tb >> 1) & 1, 34)) { ok = false; break; }
+        tc_fence_after();
+        const float scale = sa[(size_t)rr * lds_a + kb] * sb[(size_t)(n0 / 128) * ksb + kb];
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + b * BN;
+#pragma unroll
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(taddr + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[c + j] = fmaf(__uint_as_float(r[j]), scale, acc[c + j]);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[b]);
+      }
+      if (!ok || row >= M) continue;
+      if constexpr (EPI == kSwiGLU) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + n0 / 2;
+#pragma unroll
+        for (int g = 0; g < BN / 64; ++g) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 v;
+            uint32_t* p = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = g * 64 + j + 2 * e;
+              p[e] = pack_bf16x2(silu(acc[c]) * acc[c + 32], silu(acc[c + 1]) * acc[c + 33]);
+            }
+            *reinterpret_cast<uint4*>(dst + g * 32 + j) = v;
+          }
+        }
+      } else if constexpr (EPI == kF32) {
+        float* dst = reinterpret_cast<float*>(out) + (size_t)row * ldd + n0;
+#pragma unroll
+        for (int j = 0; j < BN; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      } else {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + n0;
+#pragma unroll
+        for (int j = 0; j < BN; j += 8)
+          *reinterpret_cast<uint4*>(dst + j) =
+              make_uint4(pack_bf16x2(acc[j], acc[j + 1]), pack_bf16x2(acc[j + 2], acc[j + 3]),
+                         pack_bf16x2(acc[j + 4], acc[j + 5]), pack_bf16x2(acc[j + 6], acc[j + 7]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kCols);
+  }
+}
+
+// Per (row, 128-column block) quantisation: scale = amax / 448, q = x / scale.
+// One warp per block, 4 elements per lane.
+__global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int M, int K,
+                                 __nv_fp8_e4m3* __restrict__ q, float* __restrict__ s, int64_t lds) {
+  const int nb = K / 128;
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= M * nb) return;
+  const int row = w / nb, blk = w % nb;
+  const __nv_bfloat16* src = x + (size_t)row * ldx + blk * 128 + lane * 4;
+  const uint2 raw = *reinterpret_cast<const uint2*>(src);
+  const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+  float v[4];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = __bfloat162float(b[i]);
+    amax = fmaxf(amax, fabsf(v[i]));
+  }
+  amax = warp_max(amax);
+  const float scale = fmaxf(amax, 1e-12f) / 448.f;
+  const float inv = 1.f / scale;
+  __nv_fp8x4_e4m3 packed(make_float4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv));
+  *reinterpret_cast<__nv_fp8x4_e4m3*>(q + (size_t)row * K + blk * 128 + lane * 4) = packed;
+  if (lane == 0) s[(size_t)row * lds + blk] = scale;
+}
+
+// ---------------------------------------------------------------------------
+namespace {
+std::mutex g_mu;
+std::unordered_map<uint64_t, CUtensorMap> g_maps;
+int sms() {
+  static int n = 0;
+  if (!n) {
+    int d = 0;
+    cudaGetDevice(&d);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+  }
+  return n;
+}
+CUtensorMap map_u8(const void* p, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+  const uint64_t key = reinterpret_cast<uint64_t>(p) ^ (rows * 0x9E3779B97F4A7C15ull) ^ (cols << 40) ^ (ld << 20) ^
+                       box_rows;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) return it->second;
+  if (g_maps.size() > 65536) g_maps.clear();
+  CUtensorMap m = gemm::make_tmap_2d(p, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols, ld, box_rows, BK,
+                                     CU_TENSOR_MAP_SWIZZLE_128B);
+  g_maps.emplace(key, m);
+  return m;
+}
+template <int EPI>
+void launch(const Fp8Args& a, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemm_fp8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    attr = true;
+  }
+  const CUtensorMap ta = map_u8(a.A, a.M, a.K, a.lda, BM);
+  const CUtensorMap tb = map_u8(a.B, a.N, a.K, a.ldb, BN);
+  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
+  const int grid = tiles < sms() ? tiles : sms();
+  gemm_fp8_kernel<EPI><<<grid, kThreads, kSmem, s>>>(ta, tb, a.sa, a.lds_a, a.sb, a.D, a.M, a.N, a.K, a.ldd);
+}
+}  // namespace
+
+void run(const Fp8Args& a, int epi, cudaStream_t s) {
+  if (a.M <= 0) return;
+  if (a.N % BN != 0 || a.K % BK != 0) throw std::runtime_error("lunaflux fp8 gemm: N and K must be multiples of 128");
+  if (epi == kSwiGLU) launch<kSwiGLU>(a, s);
+  else if (epi == kF32) launch<kF32>(a, s);
+  else launch<kBf16>(a, s);
+}
+
+void act_quant(const void* x, int64_t ldx, int M, int K, void* q, float* s, int64_t lds, cudaStream_t st) {
+  if (M <= 0) return;
+  if (K % 128 != 0) throw std::runtime_error("lunaflux act_quant: K must be a multiple of 128");
+  const int warps = M * (K / 128);
+  act_quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, K,
+                                                              reinterpret_cast<__nv_fp8_e4m3*>(q), s, lds);
+}
+
+}  // namespace fp8
+}  // namespace lf

@@ -93,3 +93,19 @@ def test_prefix_cache_reuse_gives_same_tokens():
     again = eng.generate([p1], 6)[0]
     assert eng.scheduler.prefix_hit_tokens >= 64
     assert first == again
+
+
+def test_moe_engine_matches_oracle():
+    from lunaflux_b200.models.spec import LlamaSpec
+    from lunaflux_b200.oracle.reference import ReferenceModel
+    spec = LlamaSpec(hidden=1024, layers=2, heads=8, kv_heads=2, head_dim=128, ffn=1024, vocab=4096,
+                     rope_theta=1e6, max_position=2048, dtype="bf16", experts=8, experts_per_token=2)
+    ck = bf16_checkpoint(spec, seed=9)
+    ref = ReferenceModel(spec, ck)
+    eng = make_engine(spec, ck)
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, spec.vocab, (n,), generator=g).tolist() for n in (7, 64, 200)]
+    outs = eng.generate(prompts, 8)
+    assert eng.runner.ops.read_error(True)[0] == 0
+    for p, o in zip(prompts, outs):
+        check_near_argmax(ref, p, o, slack=0.1)

@@ -301,3 +301,53 @@ def test_error_word_roundtrip(C):
     C.inject_error(5)
     assert C.read_error(True)[0] == 5
     assert C.read_error(True)[0] == 0
+
+
+def test_moe_kernels_match_torch(C):
+    T, H, E, k, F = 300, 1024, 8, 2, 512
+    torch.manual_seed(0)
+    h = torch.randn(T, H, device="cuda").bfloat16()
+    wr = torch.randn(E, H, device="cuda") * 0.05
+    ids = torch.empty(T, k, device="cuda", dtype=torch.int32)
+    w = torch.empty(T, k, device="cuda")
+    C.moe_route(h, wr, None, k, ids, w)
+    p = (h.float() @ wr.t()).softmax(-1)
+    pv, pi = p.topk(k, -1)
+    assert (ids.long() == pi).float().mean().item() > 0.99
+    _close(w, pv / pv.sum(-1, keepdim=True), 1e-4, 1e-4, "route weights")
+    rows = -(-(T * k + E * 127) // 128) * 128
+    groups = torch.empty(E + 1, device="cuda", dtype=torch.int32)
+    perm = torch.empty(rows, device="cuda", dtype=torch.int32)
+    slot = torch.empty(T * k, device="cuda", dtype=torch.int32)
+    C.moe_align(ids, T, k, 0, E, groups, perm, slot)
+    g = groups.tolist()
+    assert all(x % 128 == 0 for x in g) and g[0] == 0
+    flat = ids.view(-1).long()
+    for e in range(E):
+        seg = perm[g[e]:g[e + 1]]
+        real = seg[seg >= 0].long()
+        assert torch.equal(torch.sort(real).values, (flat == e).nonzero().flatten())
+    x = torch.empty(rows, H, device="cuda", dtype=torch.bfloat16)
+    C.moe_gather(h, perm, groups, E, k, x)
+    Wg = torch.randn(E, F, H, device="cuda") * 0.03
+    Wu = torch.randn(E, F, H, device="cuda") * 0.03
+    Wd = (torch.randn(E, H, F, device="cuda") * 0.03).bfloat16()
+    Wgu = torch.stack([Wg.view(E, F // 32, 32, H), Wu.view(E, F // 32, 32, H)], 2).reshape(E, 2 * F, H).bfloat16()
+    act = torch.empty(rows, F, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty(rows, H, device="cuda", dtype=torch.bfloat16)
+    C.gemm_grouped(x, Wgu, act, groups, E, 2)
+    C.gemm_grouped(act, Wd, y, groups, E, 0)
+    out = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+    C.moe_combine(y, slot, w, T, k, out)
+    ref = torch.zeros(T, H, device="cuda")
+    hf = h.float()
+    for e in range(E):
+        sel = (ids.long() == e)
+        rows_e = sel.any(-1).nonzero().flatten()
+        if rows_e.numel() == 0:
+            continue
+        a = torch.nn.functional.silu(hf[rows_e] @ Wg[e].bfloat16().float().t()) * (hf[rows_e] @ Wu[e].bfloat16().float().t())
+        ye = a.bfloat16().float() @ Wd[e].float().t()
+        ref[rows_e] += (w * sel).sum(-1)[rows_e, None] * ye
+    _close(out, ref, 3e-2, 5e-2, "moe forward")
+    assert C.read_error(True)[0] == 0
