@@ -141,6 +141,30 @@ void moe_combine(const at::Tensor& y, const at::Tensor& slot, const at::Tensor& 
                    stream());
 }
 
+// All-reduce of fp32 partial slabs (sum of `splits` slabs, then the sum over
+// ranks) into bf16 D, through the symmetric slot given by raw addresses.
+void partials_allreduce(const at::Tensor& ws, at::Tensor& D, int64_t splits, int64_t local, int64_t mc,
+                        std::vector<int64_t> peers, int64_t cnt_local, int64_t cnt_mc, std::vector<int64_t> cnt_peers,
+                        int64_t cnt_capacity) {
+  check_rowmajor(D, "D");
+  LF_CHECK(ws.scalar_type() == at::kFloat && D.scalar_type() == at::kBFloat16, "partials_allreduce dtypes");
+  const int M = D.size(0), N = D.size(1);
+  LF_CHECK(ws.numel() >= (int64_t)splits * M * N && N % 4 == 0, "partials_allreduce workspace");
+  lf::gemm::ArArgs ar{};
+  ar.local = reinterpret_cast<__nv_bfloat16*>(local);
+  ar.mc = reinterpret_cast<__nv_bfloat16*>(mc);
+  for (size_t i = 0; i < peers.size() && i < (size_t)lf::gemm::kMaxRanks; ++i) {
+    ar.peer[i] = reinterpret_cast<const __nv_bfloat16*>(peers[i]);
+    ar.cnt_peer[i] = reinterpret_cast<int*>(cnt_peers[i]);
+  }
+  ar.cnt_local = reinterpret_cast<int*>(cnt_local);
+  ar.cnt_mc = reinterpret_cast<int*>(cnt_mc);
+  ar.world = (int)peers.size();
+  ar.cnt_capacity = (int)cnt_capacity;
+  c10::cuda::CUDAGuard g(D.device());
+  lf::gemm::partials_allreduce(ws.data_ptr<float>(), D.data_ptr(), M, N, D.stride(0), (int)splits, ar, stream());
+}
+
 void gemm_fp8(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, const at::Tensor& sb, at::Tensor& D,
               int64_t epi) {
   check_rowmajor(A, "A");
@@ -344,6 +368,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_fp8", &gemm_fp8);
+  m.def("partials_allreduce", &partials_allreduce);
   m.def("act_quant", &act_quant);
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);

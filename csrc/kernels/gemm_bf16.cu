@@ -267,6 +267,15 @@ static void launch_grouped(const GemmArgs& a, const int* groups, int num_groups,
                                              groups, num_groups);
 }
 
+void partials_allreduce(const float* ws, void* D, int M, int N, int64_t ldd, int splits, const ArArgs& ar,
+                        cudaStream_t stream) {
+  if (M <= 0) return;
+  const int items = M * ((N + 1023) / 1024);
+  if (items > ar.cnt_capacity) throw std::runtime_error("lunaflux partials_allreduce: too many rows for the counters");
+  const int grid = items < 4 * num_sms() ? items : 4 * num_sms();
+  splitk_finalize_ar_kernel<<<grid, 256, 0, stream>>>(ws, reinterpret_cast<__nv_bfloat16*>(D), M, N, ldd, splits, ar);
+}
+
 void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, cudaStream_t stream) {
   if (a.M <= 0) return;
   if (a.M % BM != 0) throw std::runtime_error("lunaflux grouped gemm: M_max must be a multiple of 128");

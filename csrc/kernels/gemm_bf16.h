@@ -44,6 +44,10 @@ struct ArArgs {
 
 // D = sum over the tensor-parallel group of this rank's A . B^T, computed and
 // all-reduced by one kernel over NVLink (see ArArgs).
+// Sum of `splits` fp32 [M, N] slabs in ws, then the sum over the group, into
+// bf16 D (the split-K finalize kernel with its fused all-reduce).
+void partials_allreduce(const float* ws, void* D, int M, int N, int64_t ldd, int splits, const ArArgs& ar,
+                        cudaStream_t stream);
 void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, cudaStream_t stream);
 void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, float* ws, int64_t ws_elems);
 int choose_bn(int M, int N, int epi);

@@ -77,11 +77,17 @@ class ModelRunner:
         self.out_tok = torch.zeros(R, dtype=torch.int32, device=dev)
         if s.is_moe:
             self._init_moe(T, dev)
+        if s.fp8_block:
+            kmax = max(H, self.Hq * self.D, sh.ffn_padded)
+            self.q8 = torch.zeros(T * kmax, dtype=torch.float8_e4m3fn, device=dev)
+            self.q8s = torch.zeros(T * (kmax // 128), dtype=torch.float32, device=dev)
         self.keys_local = torch.zeros(R, dtype=torch.int64, device=dev)
         self.keys_all = torch.zeros(R * sh.size, dtype=torch.int64, device=dev)
         # split-K GEMM workspace (kept all-zero between GEMMs) and split-KV decode partials
-        self.gemm_ws = torch.zeros(512 * max(32768, sh.qkv_size, 2 * sh.ffn_padded), dtype=torch.float32, device=dev) \
-            if dev.type == "cuda" else None
+        ws_elems = 512 * max(32768, sh.qkv_size, 2 * sh.ffn_padded)
+        if s.fp8_block and comm is not None and getattr(comm, "fused", False):
+            ws_elems = max(ws_elems, T * H)  # fp32 partials of the fp8 row-parallel projections
+        self.gemm_ws = torch.zeros(ws_elems, dtype=torch.float32, device=dev) if dev.type == "cuda" else None
         self.max_splits = 32
         self.part_o = torch.empty(R * self.Hq * self.max_splits * self.D, dtype=torch.float32, device=dev)
         self.part_lse = torch.empty(R * self.Hq * self.max_splits, dtype=torch.float32, device=dev)
@@ -128,7 +134,7 @@ class ModelRunner:
                 ops.rmsnorm(resid, None, lw.ln1, h, eps)
             else:
                 ops.rmsnorm(delta, resid, lw.ln1, h, eps)
-            ops.gemm(h, lw.wqkv, qkv, 0, ws)
+            self._proj(h, lw, "wqkv", qkv, 0)
             ops.rope_kv_write(qkv, v["positions"], v["slots"], self.cos_sin, kc, vc, Hq, Hkv, self.P)
             if Rp:
                 ops.attn_prefill(qkv[:Tp], attn[:Tp], v["p_qstart"], v["p_seqlen"], v["p_bt"], kc, vc, Hq, Hkv,
@@ -137,13 +143,13 @@ class ModelRunner:
                 ops.attn_decode(qkv, attn, v["d_tok"], v["d_seqlen"], v["d_bt"], kc, vc, Hq, Hkv, splits,
                                 self.part_o, self.part_lse,
                                 host={"seq_lens": hm.get("d_seq_lens"), "tok": hm.get("d_tok")})
-            self._row_parallel(attn, lw.wo, delta, ws)
+            self._row_parallel(attn, lw, "wo", delta, ws)
             ops.rmsnorm(delta, resid, lw.ln2, h, eps)
             if s.is_moe:
                 self.moe(h, delta, lw)
             else:
-                ops.gemm(h, lw.wgu, act, 2, ws)
-                self._row_parallel(act, lw.wd, delta, ws)
+                self._proj(h, lw, "wgu", act, 2)
+                self._row_parallel(act, lw, "wd", delta, ws)
         ops.rmsnorm(delta, resid, w.norm, h, eps)
         if gather:
             hs = self.hs[:Rs]
@@ -174,13 +180,49 @@ class ModelRunner:
             ops.argmax(logits, out)
         return out
 
-    def _row_parallel(self, A, W, out, ws):
+    def _fp8(self, lw, name):
+        return lw.fp8.get(name) if lw.fp8 is not None else None
+
+    def _quant(self, x):
+        """Per-token, per-128-channel e4m3 copy of x (static buffers)."""
+        T, K = x.shape
+        q = self.q8[: T * K].view(T, K)
+        s = self.q8s[: T * (K // 128)].view(T, K // 128)
+        self.ops.act_quant(x, q, s)
+        return q, s
+
+    def _proj(self, x, lw, name, out, epi):
+        """Column-parallel projection: block-scaled fp8 when the layer has fp8
+        weights, bf16 tcgen05 GEMM otherwise."""
+        f = self._fp8(lw, name)
+        if f is not None:
+            q, s = self._quant(x)
+            self.ops.gemm_fp8(q, s, f[0], f[1], out, epi)
+        else:
+            self.ops.gemm(x, getattr(lw, name), out, epi, self.gemm_ws)
+
+    def _row_parallel(self, A, lw, name, out, ws):
         """Row-parallel projection: partial GEMM then the sum over ranks, either
         as one fused GEMM + all-reduce kernel or as GEMM followed by the
         library all-reduce (the measured baseline)."""
+        f = self._fp8(lw, name)
+        fused = self.comm is not None and getattr(self.comm, "fused", False)
+        if f is not None:
+            q, s = self._quant(A)
+            if fused:
+                part = ws[: out.numel()].view(out.shape)
+                self.ops.gemm_fp8(q, s, f[0], f[1], part, 1)
+                self.comm.reduce_partials(part, out)
+                self.ops.launches += 1
+                return
+            self.ops.gemm_fp8(q, s, f[0], f[1], out, 0)
+            if self.comm is not None:
+                self.comm.all_reduce(out)
+            return
+        W = getattr(lw, name)
         if self.comm is None:
             self.ops.gemm(A, W, out, 0, ws)
-        elif getattr(self.comm, "fused", False):
+        elif fused:
             self.comm.gemm_allreduce(A, W, out, ws)
             self.ops.launches += 2
         else:

@@ -211,6 +211,14 @@ def build_runtime(spec: LlamaSpec, source: Source, shard: Optional[TPShard] = No
             u = rows(get(p + "mlp.up_proj.weight"), fr)
             lw.wgu = interleave_gate_up(g, u).to(dtype).contiguous()
             lw.wd = pad_cols(get(p + "mlp.down_proj.weight")[:, fr.start:fr.stop], shard.ffn_padded).to(dtype).contiguous()
+        if spec.fp8_block and not spec.is_moe:
+            # Block-scaled fp8 projections: quantise in the runtime layout (after
+            # sharding and the gate/up interleave) and drop the bf16 copies.
+            from .fp8 import quantize_weight
+            lw.fp8 = {}
+            for name in ("wqkv", "wo", "wgu", "wd"):
+                lw.fp8[name] = quantize_weight(getattr(lw, name))
+                setattr(lw, name, None)
         layers.append(lw)
     embed = get("model.embed_tokens.weight").to(dtype).contiguous()
     head_name = "model.embed_tokens.weight" if spec.tie_embeddings else "lm_head.weight"

@@ -101,3 +101,12 @@ class KernelOps:
     def moe_combine(self, y, slot, w, T, topk, out):
         self.launches += 1
         self.C.moe_combine(y, slot, w, T, topk, out)
+
+    # ---------------------------------------------------------------- fp8
+    def act_quant(self, x, q, s):
+        self.launches += 1
+        self.C.act_quant(x, q, s)
+
+    def gemm_fp8(self, q, s, w8, sw, out, epi):
+        self.launches += 1
+        self.C.gemm_fp8(q, s, w8, sw, out, epi)

@@ -213,3 +213,16 @@ class TorchOps:
             ok = s[:, k] >= 0
             acc[ok] += w[:T, k][ok, None].float() * y[s[ok, k]].float()
         out[:T] = acc.to(out.dtype)
+
+    # ---------------------------------------------------------------- fp8
+    def act_quant(self, x, q, s):
+        from ..models.fp8 import quantize_act
+        rq, rs = quantize_act(x)
+        q.copy_(rq)
+        s.copy_(rs)
+
+    def gemm_fp8(self, q, s, w8, sw, out, epi):
+        from ..models.fp8 import dequantize_weight
+        a = (q.float() * s.repeat_interleave(128, 1)).to(torch.bfloat16)
+        w = dequantize_weight(w8, sw).to(torch.bfloat16)
+        self.gemm(a, w, out, epi)

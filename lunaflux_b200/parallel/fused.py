@@ -78,3 +78,13 @@ class FusedTPComm(TPComm):
         self.calls += 1
         self.C.gemm_allreduce(A, B, out, ws, s["local"], s["mc"], s["peers"], s["cnt_local"], s["cnt_mc"],
                               s["cnt_peers"], COUNTER_CAPACITY)
+
+    def reduce_partials(self, part: torch.Tensor, out: torch.Tensor):
+        """out (bf16) = sum over ranks of this rank's fp32 partial ``part``."""
+        if part.shape[0] > self.max_rows or part.shape[1] != self.hidden:
+            raise ValueError("reduce_partials: shape exceeds the symmetric buffer")
+        s = self.slots[self.op_index & 1]
+        self.op_index += 1
+        self.calls += 1
+        self.C.partials_allreduce(part, out, 1, s["local"], s["mc"], s["peers"], s["cnt_local"], s["cnt_mc"],
+                                  s["cnt_peers"], COUNTER_CAPACITY)
