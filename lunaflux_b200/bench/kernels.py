@@ -57,7 +57,7 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def bench_gemm(C, results):
+def bench_gemm(C, results, only_case=""):
     hbm, tflops_peak, src = peaks()
     shapes = [
         ("prefill qkv", 8192, 6144, 4096, 0), ("prefill o", 8192, 4096, 4096, 0),
@@ -69,6 +69,8 @@ def bench_gemm(C, results):
         ("square 8192", 8192, 8192, 8192, 0),
     ]
     for name, M, N, K, epi in shapes:
+        if only_case and name != only_case:
+            continue
         A = torch.randn(M, K, device="cuda").bfloat16()
         B = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
         if epi == 2:
@@ -167,11 +169,12 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="")
     ap.add_argument("--json", default="")
+    ap.add_argument("--case", default="", help="run only this GEMM case (for profiler captures)")
     args = ap.parse_args()
     C = _ext.load()
     results = []
     if args.only in ("", "gemm"):
-        bench_gemm(C, results)
+        bench_gemm(C, results, args.case)
     if args.only in ("", "attn"):
         bench_attn(C, results)
     if args.only in ("", "norm"):

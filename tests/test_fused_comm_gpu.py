@@ -44,15 +44,26 @@ def _worker(rank, world, port, q):
                 g = torch.Generator(device=dev).manual_seed(1000 * rank + 7 * it + M)
                 A = torch.randn(M, K, device=dev, generator=g).bfloat16()
                 B = (torch.randn(N, K, device=dev, generator=g) * 0.05).bfloat16()
-                ref = A.float() @ B.float().t()
+                part = A.float() @ B.float().t()
+                ref = part.clone()
                 dist.all_reduce(ref)
+                # The library baseline on the same data: bf16 partials, bf16 all-reduce.
+                lib = part.bfloat16()
+                dist.all_reduce(lib)
+                lib_err = float((lib.float() - ref).abs().max().item())
                 out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
                 comm.gemm_allreduce(A, B, out, ws)
                 torch.cuda.synchronize(dev)
                 code = C.read_error(True)[0]
                 err = (out.float() - ref).abs()
-                tol = 3e-2 + 3e-2 * ref.abs()
-                errs.append((M, N, K, code, int((err > tol).sum().item()), float(err.max().item())))
+                # bf16 partials are summed over `world` ranks: allow the rounding of
+                # every partial, and never more than twice the library's own error.
+                tol = (3e-2 + 3e-2 * ref.abs()) * max(1.0, world / 2)
+                bad = int((err > tol).sum().item())
+                mx = float(err.max().item())
+                if mx > max(2 * lib_err, 0.05):
+                    bad = max(bad, 1)
+                errs.append((M, N, K, code, bad, mx))
         q.put((rank, errs, comm.multicast))
         dist.barrier()
         dist.destroy_process_group()
