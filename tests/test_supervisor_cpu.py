@@ -1,0 +1,100 @@
+"""Supervised rank processes on CPU (gloo): lock-step serving, and recovery
+from a rank that dies or stops answering.  Failures are made on the host: a
+rank process exits, or stops itself (SIGSTOP) so its heartbeats cease."""
+import os
+import signal
+
+import pytest
+import torch
+
+from lunaflux_b200.contracts import PublicErrorCode
+from lunaflux_b200.engine.supervisor import Supervisor
+
+
+def _spec():
+    from lunaflux_b200.models.spec import LlamaSpec
+    return LlamaSpec(hidden=64, layers=2, heads=4, kv_heads=2, head_dim=16, ffn=172, vocab=256, max_position=512,
+                     dtype="fp32")
+
+
+class _FaultyEngine:
+    """Wraps an engine; on the configured rank / generation / step it fails."""
+
+    def __init__(self, eng, rank):
+        self.eng = eng
+        self.rank = rank
+        self.steps = 0
+        self.mode = os.environ.get("LF_TEST_FAULT", "")
+        self.gen = int(os.environ.get("LUNAFLUX_GENERATION", "1"))
+
+    def __getattr__(self, k):
+        return getattr(self.eng, k)
+
+    def step(self):
+        self.steps += 1
+        if self.rank == 1 and self.gen == 1 and self.steps == 3:
+            if self.mode == "exit":
+                os._exit(3)
+            if self.mode == "stop":
+                os.kill(os.getpid(), signal.SIGSTOP)
+        return self.eng.step()
+
+
+def tiny_factory(rank, world):
+    import torch.distributed as dist
+
+    from lunaflux_b200.config import CacheConfig, SchedulerConfig
+    from lunaflux_b200.engine.engine import EngineOptions, LLMEngine
+    from lunaflux_b200.models.weights import build_runtime, random_checkpoint
+    from lunaflux_b200.ops.torch_ops import TorchOps
+    from lunaflux_b200.parallel.comm import TPComm
+    from lunaflux_b200.parallel.tp import TPShard
+    import datetime
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=30))
+    spec = _spec()
+    ck = random_checkpoint(spec, 0)
+    w = build_runtime(spec, lambda n: ck[n], TPShard(rank, world, spec))
+    eng = LLMEngine(w, TorchOps(), "cpu", SchedulerConfig(step_token_budget=64, max_active_requests=4,
+                                                          prefill_chunk_tokens=64, emergency_decode_page_reserve=1),
+                    CacheConfig(), EngineOptions(max_context=256, num_pages=64, graph_sizes=()), comm=TPComm())
+    return _FaultyEngine(eng, rank)
+
+
+def _expect(prompts, n):
+    from lunaflux_b200.models.weights import random_checkpoint
+    from lunaflux_b200.oracle.reference import ReferenceModel
+    ref = ReferenceModel(_spec(), random_checkpoint(_spec(), 0))
+    return [ref.generate_greedy(p, n) for p in prompts]
+
+
+PROMPTS = [[5, 6, 7], [9, 10, 11, 12, 13], [1, 2, 3, 4], [200, 100]]
+
+
+@pytest.mark.parametrize("fault", ["", "exit", "stop"])
+def test_supervised_tp_ranks(fault, monkeypatch):
+    monkeypatch.setenv("LF_TEST_FAULT", fault)
+    sup = Supervisor(2, tiny_factory, heartbeat_s=0.1, dead_after_s=2.0, step_timeout_s=60.0)
+    sup.start()
+    try:
+        sup.submit(1, PROMPTS[0], 6)
+        sup.submit(2, PROMPTS[1], 6)
+        sup.step()
+        sup.step()
+        sup.submit(3, PROMPTS[2], 6)
+        sup.submit(4, PROMPTS[3], 6)
+        sup.run_until_done()
+    finally:
+        sup.close()
+    expect = _expect(PROMPTS, 6)
+    if not fault:
+        assert sup.failures == 0
+        for i in range(4):
+            assert sup.reqs[i + 1].tokens == expect[i]
+        return
+    assert sup.failures == 1 and sup.generation == 2
+    # requests that were producing tokens fail retryably; the ones still
+    # waiting survive and complete correctly in the new generation
+    for rid in (1, 2):
+        assert sup.reqs[rid].error is PublicErrorCode.WORKER_UNAVAILABLE
+    for rid in (3, 4):
+        assert sup.reqs[rid].error is None and sup.reqs[rid].tokens == expect[rid - 1]
