@@ -152,7 +152,8 @@ int plan_splitk(int M, int N, int K, int* kb_per_out) {
   if (N % 256 != 0) return 1;
   const int tiles = num_m * (N / 256);
   if (tiles >= sms / 2) return 1;
-  int splits = (sms + tiles - 1) / tiles;
+  // one wave: tiles * splits <= SMs (a partial second wave doubles the time)
+  int splits = sms / tiles;
   if (splits > num_kb / 4) splits = num_kb / 4;
   if (splits < 2) return 1;
   const int kb_per = (num_kb + splits - 1) / splits;

@@ -46,7 +46,94 @@ class _Checkpoint:
     prev_gen: List[int]
 
 
-class PageAllocator:
+class NativePageAllocator:
+    """The same allocator backed by the C++ core (``lunaflux_b200._host``)."""
+
+    def __init__(self, capacity: int, first_index: int = 1, max_generation: int = (1 << 31) - 1,
+                 max_active_refs: int = 1 << 20, max_cached_refs: int = 1 << 20):
+        from .. import _host
+        self._h = _host
+        self._c = _host.PageAllocator(capacity, first_index, max_generation, max_active_refs, max_cached_refs)
+        self.capacity = capacity
+        self.first_index = first_index
+
+    def _call(self, fn, *a):
+        try:
+            return fn(*a)
+        except self._h.OutOfPages as e:
+            raise OutOfPages(str(e)) from None
+        except self._h.PageError as e:
+            raise PageAllocatorError(str(e)) from None
+
+    def free_page_count(self) -> int:
+        return self._c.free_page_count()
+
+    def allocated_page_count(self) -> int:
+        return self._c.allocated_page_count()
+
+    def retired_page_count(self) -> int:
+        return self._c.retired_page_count()
+
+    def allocate_one(self) -> PageId:
+        return self.allocate_run(1)[0]
+
+    def allocate_run(self, n: int) -> List[PageId]:
+        return [PageId(i, g) for i, g in self._call(self._c.allocate_run, n)]
+
+    def retain_active(self, pid: PageId):
+        self._call(self._c.retain_active, pid.index, pid.generation)
+
+    def release_active(self, pid: PageId):
+        self._call(self._c.release_active, pid.index, pid.generation)
+
+    def release_active_many(self, pids: Iterable[PageId]):
+        for p in pids:
+            self.release_active(p)
+
+    def retain_cached(self, pid: PageId):
+        self._call(self._c.retain_cached, pid.index, pid.generation)
+
+    def release_cached(self, pid: PageId):
+        self._call(self._c.release_cached, pid.index, pid.generation)
+
+    def active_reference_count(self, pid: PageId) -> int:
+        return self._call(self._c.active_reference_count, pid.index, pid.generation)
+
+    def cached_reference_count(self, pid: PageId) -> int:
+        return self._call(self._c.cached_reference_count, pid.index, pid.generation)
+
+    def validate_active(self, pid: PageId) -> bool:
+        return self._c.validate_active(pid.index, pid.generation)
+
+    def checkpoint(self) -> int:
+        return self._call(self._c.checkpoint)
+
+    def commit_checkpoint(self, token: int):
+        self._call(self._c.commit_checkpoint, token)
+
+    def rollback_to(self, token: int):
+        self._call(self._c.rollback_to, token)
+
+    @property
+    def _free(self):
+        return self._c.free_queue()
+
+    def debug_check_invariants(self):
+        self._call(self._c.debug_check_invariants)
+
+
+def native_available() -> bool:
+    try:
+        from .. import _host  # noqa: F401
+        return True
+    except ImportError:
+        return False
+
+
+class PyPageAllocator:
+    """Reference implementation of the allocator (the spec the C++ core is
+    differentially tested against)."""
+
     def __init__(self, capacity: int, first_index: int = 1, max_generation: int = (1 << 31) - 1,
                  max_active_refs: int = 1 << 20, max_cached_refs: int = 1 << 20):
         if capacity <= 0:
@@ -207,3 +294,14 @@ class PageAllocator:
                 n_ret += 1
         assert n_alloc == self._allocated and n_ret == self._retired
         assert len(free) + n_alloc + n_ret == self.capacity
+
+
+def _select():
+    import os
+    if os.environ.get("LUNAFLUX_HOST_CORE", "native") == "native" and native_available():
+        return NativePageAllocator
+    return PyPageAllocator
+
+
+# The serving path uses the C++ core whenever the host extension is built.
+PageAllocator = _select()

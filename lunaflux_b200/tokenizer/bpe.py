@@ -67,6 +67,16 @@ class Tokenizer:
         for s, i in added:
             self.id_to_token.setdefault(i, s)
         self.digest = digest
+        # The merge loop runs in the C++ host core when it is built (same
+        # semantics, on ids); the Python loop below is its reference.
+        self._byte_ids = [self.vocab[_B2U[b]] for b in range(256)]
+        self._native = None
+        try:
+            from .. import _host
+            self._native = _host.BpeEncoder([(self.vocab[a], self.vocab[b], self.vocab[a + b])
+                                             for (a, b) in sorted(self.ranks, key=self.ranks.get)])
+        except ImportError:
+            pass
         self.vocab_size = max(self.id_to_token) + 1 if self.id_to_token else 0
 
     # ------------------------------------------------------------------ loading
@@ -115,6 +125,11 @@ class Tokenizer:
 
     # ------------------------------------------------------------------ encode
     def _bpe(self, data: bytes) -> List[int]:
+        if self._native is not None:
+            return self._native.encode([self._byte_ids[b] for b in data])
+        return self._bpe_reference(data)
+
+    def _bpe_reference(self, data: bytes) -> List[int]:
         syms = [_B2U[b] for b in data]
         if len(syms) > 1:
             ranks = self.ranks

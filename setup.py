@@ -51,12 +51,16 @@ ext_modules = [
     ),
 ]
 if host_sources:
+    import pybind11
+    from setuptools import Extension
+    # plain pybind11 module: no torch linkage, importable on any host
     ext_modules.append(
-        CppExtension(
+        Extension(
             name="lunaflux_b200._host",
             sources=host_sources,
-            include_dirs=[CSRC],
-            extra_compile_args={"cxx": ["-O3", "-std=c++20"]},
+            include_dirs=[CSRC, pybind11.get_include()],
+            extra_compile_args=["-O3", "-std=c++20", "-fvisibility=hidden"],
+            language="c++",
         ))
 
 setup(

@@ -67,8 +67,8 @@ def test_noalloc_matches_allocating_entry_point(lib, M, N, K, epi):
 
 def test_noalloc_rejects_oversized_plans_and_bad_arguments(lib):
     C, fn = lib
-    # 256 x 8192 needs splits x 2M floats of scratch, more than the 4M-float array.
-    M, N, K = 256, 8192, 16384
+    # 256 x 2560 splits K 7 ways: 7 x 655360 floats of scratch, more than the 4M-float array.
+    M, N, K = 256, 2560, 16384
     splits = C.gemm_plan_splitk(M, N, K)
     assert splits * M * N > SCRATCH_FLOATS
     A = torch.zeros(M, K, device="cuda", dtype=torch.bfloat16)
