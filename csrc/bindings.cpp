@@ -60,29 +60,43 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, int64_t epi, 
 // GEMM + all-reduce over the tensor-parallel group.  Pointers are raw device
 // addresses of this rank's symmetric slot, its multicast address (0 if none)
 // and every rank's slot; the same for the int32 arrival counters.
-void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, c10::optional<at::Tensor> ws,
-                    int64_t local, int64_t mc, std::vector<int64_t> peers, int64_t cnt_local, int64_t cnt_mc,
-                    std::vector<int64_t> cnt_peers, int64_t cnt_capacity) {
-  check_rowmajor(A, "A");
-  check_rowmajor(B, "B");
-  check_rowmajor(D, "D");
-  LF_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && D.scalar_type() == at::kBFloat16,
-           "gemm_allreduce is bf16");
-  LF_CHECK(peers.size() == cnt_peers.size() && !peers.empty() && peers.size() <= (size_t)lf::gemm::kMaxRanks,
-           "gemm_allreduce: peer lists");
-  const int M = A.size(0), N = B.size(0), K = A.size(1);
-  LF_CHECK(D.size(0) == M && D.size(1) == N, "gemm_allreduce output must be [M, N]");
+static lf::gemm::ArArgs make_ar(int64_t local, int64_t mc, const std::vector<int64_t>& peers, int64_t out_mc,
+                                const std::vector<int64_t>& out_peers, int64_t cnt_local, int64_t cnt_mc,
+                                const std::vector<int64_t>& cnt_peers, int64_t rank, int64_t cnt_capacity,
+                                int64_t trace) {
+  LF_CHECK(!peers.empty() && peers.size() <= (size_t)lf::gemm::kMaxRanks && out_peers.size() == peers.size() &&
+               cnt_peers.size() == peers.size(),
+           "fused all-reduce: peer lists");
+  LF_CHECK(rank >= 0 && rank < (int64_t)peers.size(), "fused all-reduce: rank");
   lf::gemm::ArArgs ar{};
   ar.local = reinterpret_cast<__nv_bfloat16*>(local);
   ar.mc = reinterpret_cast<__nv_bfloat16*>(mc);
+  ar.out_mc = reinterpret_cast<__nv_bfloat16*>(out_mc);
   for (size_t i = 0; i < peers.size(); ++i) {
     ar.peer[i] = reinterpret_cast<const __nv_bfloat16*>(peers[i]);
+    ar.out_peer[i] = reinterpret_cast<__nv_bfloat16*>(out_peers[i]);
     ar.cnt_peer[i] = reinterpret_cast<int*>(cnt_peers[i]);
   }
   ar.cnt_local = reinterpret_cast<int*>(cnt_local);
   ar.cnt_mc = reinterpret_cast<int*>(cnt_mc);
+  ar.rank = (int)rank;
   ar.world = (int)peers.size();
   ar.cnt_capacity = (int)cnt_capacity;
+  ar.trace = reinterpret_cast<unsigned long long*>(trace);
+  return ar;
+}
+
+// Result region (out_peers[rank], [M, N] row-major) = sum over ranks of A . B^T.
+void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, c10::optional<at::Tensor> ws, int64_t local, int64_t mc,
+                    std::vector<int64_t> peers, int64_t out_mc, std::vector<int64_t> out_peers, int64_t cnt_local,
+                    int64_t cnt_mc, std::vector<int64_t> cnt_peers, int64_t rank, int64_t cnt_capacity,
+                    int64_t trace) {
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  LF_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm_allreduce is bf16");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  lf::gemm::ArArgs ar =
+      make_ar(local, mc, peers, out_mc, out_peers, cnt_local, cnt_mc, cnt_peers, rank, cnt_capacity, trace);
   float* wsp = nullptr;
   int64_t ws_elems = 0;
   if (ws.has_value()) {
@@ -90,8 +104,56 @@ void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, c10
     ws_elems = ws->numel();
   }
   c10::cuda::CUDAGuard g(A.device());
-  lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), B.stride(0), D.stride(0)};
+  lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), ar.out_peer[rank], M, N, K, A.stride(0), B.stride(0), N};
   lf::gemm::run_allreduce(a, ar, stream(), wsp, ws_elems);
+}
+
+static lf::ar::LLArgs make_ll(const std::vector<int64_t>& rs, const std::vector<int64_t>& ag, const at::Tensor& state,
+                              int64_t rank, int64_t max_pairs) {
+  LF_CHECK(!rs.empty() && rs.size() <= (size_t)lf::ar::kMaxRanks && ag.size() == rs.size(), "low-latency all-reduce: peers");
+  LF_CHECK(rank >= 0 && rank < (int64_t)rs.size(), "low-latency all-reduce: rank");
+  LF_CHECK(state.is_cuda() && state.scalar_type() == at::kInt && state.numel() >= 2, "low-latency all-reduce: state");
+  lf::ar::LLArgs a{};
+  for (size_t i = 0; i < rs.size(); ++i) {
+    a.rs[i] = reinterpret_cast<uint2*>(rs[i]);
+    a.ag[i] = reinterpret_cast<uint2*>(ag[i]);
+  }
+  a.state = state.data_ptr<int>();
+  a.rank = (int)rank;
+  a.world = (int)rs.size();
+  a.max_pairs = max_pairs;
+  return a;
+}
+
+// D (bf16 [M, N]) = sum over ranks of A . B^T, low-latency protocol (decode shapes).
+void gemm_allreduce_ll(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, at::Tensor& ws, std::vector<int64_t> rs,
+                       std::vector<int64_t> ag, const at::Tensor& state, int64_t rank, int64_t max_pairs) {
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  check_rowmajor(D, "D");
+  LF_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && D.scalar_type() == at::kBFloat16,
+           "gemm_allreduce_ll is bf16");
+  LF_CHECK(ws.scalar_type() == at::kFloat && ws.is_cuda(), "gemm_allreduce_ll: fp32 workspace");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  LF_CHECK(D.size(0) == M && D.size(1) == N, "gemm_allreduce_ll output must be [M, N]");
+  lf::ar::LLArgs ll = make_ll(rs, ag, state, rank, max_pairs);
+  c10::cuda::CUDAGuard g(A.device());
+  lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), B.stride(0), D.stride(0)};
+  lf::gemm::run_allreduce_ll(a, ll, stream(), ws.data_ptr<float>(), ws.numel());
+}
+
+// D = sum over ranks of the sum of `splits` fp32 [M, N] slabs of ws (low-latency protocol).
+void partials_allreduce_ll(const at::Tensor& ws, int64_t splits, at::Tensor& D, std::vector<int64_t> rs,
+                           std::vector<int64_t> ag, const at::Tensor& state, int64_t rank, int64_t max_pairs) {
+  check_rowmajor(D, "D");
+  LF_CHECK(ws.scalar_type() == at::kFloat && ws.is_cuda() && D.scalar_type() == at::kBFloat16,
+           "partials_allreduce_ll dtypes");
+  const int M = D.size(0), N = D.size(1);
+  LF_CHECK(ws.numel() >= splits * M * N, "partials_allreduce_ll workspace");
+  lf::ar::LLArgs ll = make_ll(rs, ag, state, rank, max_pairs);
+  c10::cuda::CUDAGuard g(D.device());
+  lf::ar::finalize_ll(ws.data_ptr<float>(), (int)splits, M, N, reinterpret_cast<__nv_bfloat16*>(D.data_ptr()),
+                      D.stride(0), ll, stream());
 }
 
 void gemm_grouped(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const at::Tensor& groups,
@@ -143,26 +205,17 @@ void moe_combine(const at::Tensor& y, const at::Tensor& slot, const at::Tensor& 
 
 // All-reduce of fp32 partial slabs (sum of `splits` slabs, then the sum over
 // ranks) into bf16 D, through the symmetric slot given by raw addresses.
-void partials_allreduce(const at::Tensor& ws, at::Tensor& D, int64_t splits, int64_t local, int64_t mc,
-                        std::vector<int64_t> peers, int64_t cnt_local, int64_t cnt_mc, std::vector<int64_t> cnt_peers,
-                        int64_t cnt_capacity) {
-  check_rowmajor(D, "D");
-  LF_CHECK(ws.scalar_type() == at::kFloat && D.scalar_type() == at::kBFloat16, "partials_allreduce dtypes");
-  const int M = D.size(0), N = D.size(1);
-  LF_CHECK(ws.numel() >= (int64_t)splits * M * N && N % 4 == 0, "partials_allreduce workspace");
-  lf::gemm::ArArgs ar{};
-  ar.local = reinterpret_cast<__nv_bfloat16*>(local);
-  ar.mc = reinterpret_cast<__nv_bfloat16*>(mc);
-  for (size_t i = 0; i < peers.size() && i < (size_t)lf::gemm::kMaxRanks; ++i) {
-    ar.peer[i] = reinterpret_cast<const __nv_bfloat16*>(peers[i]);
-    ar.cnt_peer[i] = reinterpret_cast<int*>(cnt_peers[i]);
-  }
-  ar.cnt_local = reinterpret_cast<int*>(cnt_local);
-  ar.cnt_mc = reinterpret_cast<int*>(cnt_mc);
-  ar.world = (int)peers.size();
-  ar.cnt_capacity = (int)cnt_capacity;
-  c10::cuda::CUDAGuard g(D.device());
-  lf::gemm::partials_allreduce(ws.data_ptr<float>(), D.data_ptr(), M, N, D.stride(0), (int)splits, ar, stream());
+// Result region ([M, N]) = sum over ranks of the sum of `splits` fp32 slabs of ws.
+void partials_allreduce(const at::Tensor& ws, int64_t M, int64_t N, int64_t splits, int64_t local, int64_t mc,
+                        std::vector<int64_t> peers, int64_t out_mc, std::vector<int64_t> out_peers, int64_t cnt_local,
+                        int64_t cnt_mc, std::vector<int64_t> cnt_peers, int64_t rank, int64_t cnt_capacity,
+                        int64_t trace) {
+  LF_CHECK(ws.scalar_type() == at::kFloat && ws.is_cuda(), "partials_allreduce: fp32 CUDA workspace");
+  LF_CHECK(ws.numel() >= splits * M * N && N % 8 == 0, "partials_allreduce workspace");
+  lf::gemm::ArArgs ar =
+      make_ar(local, mc, peers, out_mc, out_peers, cnt_local, cnt_mc, cnt_peers, rank, cnt_capacity, trace);
+  c10::cuda::CUDAGuard g(ws.device());
+  lf::gemm::partials_allreduce(ws.data_ptr<float>(), (int)M, (int)N, (int)splits, ar, stream());
 }
 
 void gemm_fp8(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, const at::Tensor& sb, at::Tensor& D,
@@ -369,6 +422,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_fp8", &gemm_fp8);
   m.def("partials_allreduce", &partials_allreduce);
+  m.def("gemm_allreduce_ll", &gemm_allreduce_ll);
+  m.def("partials_allreduce_ll", &partials_allreduce_ll);
   m.def("act_quant", &act_quant);
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);

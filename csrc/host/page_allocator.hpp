@@ -1,30 +1,18 @@
-// Native host cores of the serving loop (module lunaflux_b200._host).
-//
-// * PageAllocator: the generational KV page allocator (reference semantics of
-//   kv/page_allocator/allocator.mbt:13-302 and allocation_checkpoint.mbt:7-107:
-//   (index, generation) ids, separate active and cached reference counts, an
-//   intrusive FIFO free queue, retirement at the terminal generation, one
-//   exclusive checkpoint with exact rollback).  O(1) per page.
-// * BpeEncoder: the byte-level BPE merge loop of tokenizer/encode.mbt
-//   (best-ranked adjacent pair over the whole sequence, then every
-//   non-overlapping occurrence merged left to right, repeat), on token ids.
-//
-// Both are exact restatements of the Python reference implementations in
-// lunaflux_b200/kv/page_allocator.py and lunaflux_b200/tokenizer/bpe.py, which
-// the tests run side by side.
-#include <pybind11/pybind11.h>
-#include <pybind11/stl.h>
-
+// Generational KV page allocator (reference semantics of
+// kv/page_allocator/allocator.mbt:13-302 and allocation_checkpoint.mbt:7-107):
+// (index, generation) ids, separate active and cached reference counts, an
+// FIFO free queue, retirement at the terminal generation, one exclusive
+// checkpoint with exact rollback.  O(1) per page.  Exact restatement of the
+// Python reference class PyPageAllocator (lunaflux_b200/kv/page_allocator.py).
+#pragma once
 #include <cstdint>
 #include <deque>
 #include <stdexcept>
-#include <unordered_map>
 #include <utility>
 #include <vector>
 
-namespace py = pybind11;
-
 namespace lf_host {
+
 
 class PageError : public std::runtime_error {
  public:
@@ -192,77 +180,4 @@ class PageAllocator {
   std::vector<int64_t> prev_gen_;
 };
 
-class BpeEncoder {
- public:
-  // merges: (left id, right id, merged id) in rank order
-  explicit BpeEncoder(const std::vector<std::tuple<int, int, int>>& merges) {
-    for (size_t r = 0; r < merges.size(); ++r) {
-      const auto& m = merges[r];
-      table_.emplace(key(std::get<0>(m), std::get<1>(m)), std::make_pair((int)r, std::get<2>(m)));
-    }
-  }
-
-  std::vector<int> encode(std::vector<int> syms) const {
-    while (syms.size() > 1) {
-      int best_rank = -1, best_id = -1, a = -1, b = -1;
-      for (size_t i = 0; i + 1 < syms.size(); ++i) {
-        auto it = table_.find(key(syms[i], syms[i + 1]));
-        if (it != table_.end() && (best_rank < 0 || it->second.first < best_rank)) {
-          best_rank = it->second.first;
-          best_id = it->second.second;
-          a = syms[i];
-          b = syms[i + 1];
-        }
-      }
-      if (best_rank < 0) break;
-      std::vector<int> out;
-      out.reserve(syms.size());
-      for (size_t i = 0; i < syms.size();) {
-        if (i + 1 < syms.size() && syms[i] == a && syms[i + 1] == b) {
-          out.push_back(best_id);
-          i += 2;
-        } else {
-          out.push_back(syms[i]);
-          i += 1;
-        }
-      }
-      syms.swap(out);
-    }
-    return syms;
-  }
-
- private:
-  static uint64_t key(int a, int b) { return ((uint64_t)(uint32_t)a << 32) | (uint32_t)b; }
-  std::unordered_map<uint64_t, std::pair<int, int>> table_;
-};
-
 }  // namespace lf_host
-
-PYBIND11_MODULE(_host, m) {
-  using namespace lf_host;
-  m.doc() = "LunaFlux native host cores";
-  auto page_err = py::register_exception<PageError>(m, "PageError", PyExc_RuntimeError);
-  py::register_exception<OutOfPages>(m, "OutOfPages", page_err.ptr());
-  py::class_<PageAllocator>(m, "PageAllocator")
-      .def(py::init<int, int, int64_t, int, int>())
-      .def("free_page_count", &PageAllocator::free_page_count)
-      .def("allocated_page_count", &PageAllocator::allocated_page_count)
-      .def("retired_page_count", &PageAllocator::retired_page_count)
-      .def("capacity", &PageAllocator::capacity)
-      .def("allocate_run", &PageAllocator::allocate_run)
-      .def("retain_active", &PageAllocator::retain_active)
-      .def("release_active", &PageAllocator::release_active)
-      .def("retain_cached", &PageAllocator::retain_cached)
-      .def("release_cached", &PageAllocator::release_cached)
-      .def("active_reference_count", &PageAllocator::active_reference_count)
-      .def("cached_reference_count", &PageAllocator::cached_reference_count)
-      .def("validate_active", &PageAllocator::validate_active)
-      .def("checkpoint", &PageAllocator::checkpoint)
-      .def("commit_checkpoint", &PageAllocator::commit_checkpoint)
-      .def("rollback_to", &PageAllocator::rollback_to)
-      .def("free_queue", &PageAllocator::free_queue)
-      .def("debug_check_invariants", &PageAllocator::debug_check_invariants);
-  py::class_<BpeEncoder>(m, "BpeEncoder")
-      .def(py::init<const std::vector<std::tuple<int, int, int>>&>())
-      .def("encode", &BpeEncoder::encode);
-}

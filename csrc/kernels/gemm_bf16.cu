@@ -138,7 +138,8 @@ static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int k
   if (EPI == kSplitF32) {
     kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, ws, a.M, a.N, a.K, a.N, splits, kb_per, ArArgs{}, nullptr, 0);
   } else {
-    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, splits, kb_per, ar, nullptr, 0);
+    kfn<<<grid, threads_for(EPI), S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, splits, kb_per, ar, nullptr,
+                                                       0);
   }
 }
 
@@ -222,30 +223,56 @@ void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws, int
 // GEMM + tensor-parallel all-reduce in one kernel: D = sum over ranks of
 // A_r . B_r^T (row-parallel projections).  Skinny shapes use split-K with the
 // all-reduce fused into the persistent finalize kernel instead.
+static int finalize_ar_grid(int64_t vecs) {
+  // Every CTA must be resident (the kernel has a grid-wide barrier), and the
+  // grid must be the same on every rank (a function of the shape, the kernel
+  // and the device only).
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, splitk_finalize_ar_kernel, 256, 0);
+    if (per_sm < 1) throw std::runtime_error("lunaflux partials_allreduce: kernel cannot be resident");
+    if (per_sm > 2) per_sm = 2;
+  }
+  const int64_t cap = (int64_t)per_sm * num_sms();
+  const int64_t want = (vecs + 255) / 256;
+  return (int)(want < cap ? (want < 1 ? 1 : want) : cap);
+}
+
 void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, float* ws, int64_t ws_elems) {
   if (a.M <= 0) return;
-  if (ar.world < 1 || ar.world > kMaxRanks) throw std::runtime_error("lunaflux gemm_allreduce: bad world size");
+  if (ar.world < 1 || ar.world > kMaxRanks || ar.rank < 0 || ar.rank >= ar.world)
+    throw std::runtime_error("lunaflux gemm_allreduce: bad rank or world size");
   if (a.N % 32 != 0 || a.K % 8 != 0) throw std::runtime_error("lunaflux gemm_allreduce: N % 32 and K % 8 required");
   int kb_per = 0;
   const int splits = (ws != nullptr && a.N % 256 == 0) ? plan_splitk(a.M, a.N, a.K, &kb_per) : 1;
   if (splits > 1 && (int64_t)splits * a.M * a.N <= ws_elems) {
-    const int items = a.M * ((a.N + 1023) / 1024);
-    if (items > ar.cnt_capacity) throw std::runtime_error("lunaflux gemm_allreduce: too many rows for the counters");
     launch<256, 4, kSplitF32>(a, stream, splits, kb_per, ws);
-    const int grid = items < 4 * num_sms() ? items : 4 * num_sms();
-    splitk_finalize_ar_kernel<<<grid, 256, 0, stream>>>(ws, reinterpret_cast<__nv_bfloat16*>(a.D), a.M, a.N, a.ldd,
-                                                        splits, ar);
+    partials_allreduce(ws, a.M, a.N, splits, ar, stream);
     return;
   }
   const int bn = choose_bn(a.M, a.N, kStoreBf16);
   const int tiles = ((a.M + BM - 1) / BM) * (a.N / bn);
-  if (tiles > ar.cnt_capacity) throw std::runtime_error("lunaflux gemm_allreduce: too many tiles for the counters");
+  if (tiles > ar.cnt_capacity - kFinReserved) throw std::runtime_error("lunaflux gemm_allreduce: too many tiles for the counters");
   switch (bn) {
     case 256: launch<256, 4, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
     case 128: launch<128, 6, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
     case 64: launch<64, 8, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
     default: launch<32, 8, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
   }
+}
+
+void run_allreduce_ll(const GemmArgs& a, const ar::LLArgs& ll, cudaStream_t stream, float* ws, int64_t ws_elems) {
+  if (a.M <= 0) return;
+  if (a.N % 256 != 0 || a.K % 8 != 0) throw std::runtime_error("lunaflux gemm_allreduce_ll: N % 256 and K % 8 required");
+  int kb_per = 0;
+  int splits = plan_splitk(a.M, a.N, a.K, &kb_per);
+  if (splits < 1 || (int64_t)splits * a.M * a.N > ws_elems) {
+    splits = 1;
+    kb_per = 0;
+  }
+  if ((int64_t)a.M * a.N > ws_elems) throw std::runtime_error("lunaflux gemm_allreduce_ll: workspace too small");
+  launch<256, 4, kSplitF32>(a, stream, splits, kb_per, ws);
+  ar::finalize_ll(ws, splits, a.M, a.N, reinterpret_cast<__nv_bfloat16*>(a.D), a.ldd, ll, stream);
 }
 
 // Grouped GEMM (mixture-of-experts): A [M_max, K] rows in expert segments
@@ -268,13 +295,12 @@ static void launch_grouped(const GemmArgs& a, const int* groups, int num_groups,
                                              groups, num_groups);
 }
 
-void partials_allreduce(const float* ws, void* D, int M, int N, int64_t ldd, int splits, const ArArgs& ar,
-                        cudaStream_t stream) {
+void partials_allreduce(const float* ws, int M, int N, int splits, const ArArgs& ar, cudaStream_t stream) {
   if (M <= 0) return;
-  const int items = M * ((N + 1023) / 1024);
-  if (items > ar.cnt_capacity) throw std::runtime_error("lunaflux partials_allreduce: too many rows for the counters");
-  const int grid = items < 4 * num_sms() ? items : 4 * num_sms();
-  splitk_finalize_ar_kernel<<<grid, 256, 0, stream>>>(ws, reinterpret_cast<__nv_bfloat16*>(D), M, N, ldd, splits, ar);
+  if (N % 8 != 0) throw std::runtime_error("lunaflux partials_allreduce: N % 8 required");
+  if (ar.cnt_capacity < 64) throw std::runtime_error("lunaflux partials_allreduce: counter capacity");
+  const int grid = finalize_ar_grid((int64_t)M * N / 8);
+  splitk_finalize_ar_kernel<<<grid, 256, 0, stream>>>(ws, M, N, splits, ar);
 }
 
 void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, cudaStream_t stream) {

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "allreduce_ll.h"
+
 namespace lf {
 namespace gemm {
 
@@ -24,33 +26,50 @@ struct GemmArgs {
 void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws = nullptr, int64_t ws_elems = 0);
 int plan_splitk(int M, int N, int K, int* kb_per_out);
 
-// Peer view of one tensor-parallel group for the fused GEMM + all-reduce
-// epilogue.  `local` is this rank's slot of a symmetric (every rank holds one,
-// same size) bf16 buffer [rows, N]; `mc` is the NVLink-multicast address of
-// the same slot (null when the fabric has no multicast); `peer[r]` are the
-// slot's addresses on every rank.  `cnt_*` are per-tile int32 arrival counters
-// laid out the same way.
+// Peer view of one tensor-parallel group for the fused GEMM + all-reduce.
+// Two symmetric bf16 regions of [rows, N] (every rank holds both, same size):
+// `local`/`mc`/`peer[r]` address this rank's partial-sum region (own address,
+// NVLink multicast address or null, address on rank r); `out_mc`/`out_peer[r]`
+// address the result region, which is the operation's output on every rank.
+// A piece (an output tile, or a group of rows) has one owner rank: every rank
+// publishes its partial of the piece and signals the owner; the owner reads
+// the sum of all partials through the switch (multimem.ld_reduce) and writes
+// it into every rank's result region (multimem.st), then signals "done" to
+// every rank.  Each rank's NVLink traffic is then about twice the output size,
+// independent of the group size (a bandwidth-optimal all-reduce).
+// `cnt_*` address int32 counters: [0, cnt_capacity) arrivals, then
+// [cnt_capacity, 2 cnt_capacity) completions; every wait re-arms its counter.
 constexpr int kMaxRanks = 8;
 struct ArArgs {
   __nv_bfloat16* local;
   __nv_bfloat16* mc;
   const __nv_bfloat16* peer[kMaxRanks];
+  __nv_bfloat16* out_mc;
+  __nv_bfloat16* out_peer[kMaxRanks];
   int* cnt_local;
   int* cnt_mc;
   int* cnt_peer[kMaxRanks];
+  int rank;
   int world;
   int cnt_capacity;
+  // Optional timeline (null in production): per tile, %globaltimer at
+  // [4 t] partial published, [4 t + 1] owner saw every partial, [4 t + 2]
+  // owner's sum written everywhere; [4 t + 3] = 1 + the owner CTA's index.
+  unsigned long long* trace;
 };
 
-// D = sum over the tensor-parallel group of this rank's A . B^T, computed and
-// all-reduced by one kernel over NVLink (see ArArgs).
 // Sum of `splits` fp32 [M, N] slabs in ws, then the sum over the group, into
-// bf16 D (the split-K finalize kernel with its fused all-reduce).
-void partials_allreduce(const float* ws, void* D, int M, int N, int64_t ldd, int splits, const ArArgs& ar,
-                        cudaStream_t stream);
+// the result region (the split-K finalize kernel with its fused all-reduce).
+void partials_allreduce(const float* ws, int M, int N, int splits, const ArArgs& ar, cudaStream_t stream);
 void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, cudaStream_t stream);
+// Result region = sum over the tensor-parallel group of this rank's A . B^T,
+// computed and all-reduced over NVLink by one kernel (split-K shapes: the GEMM
+// and the finalize kernel that carries the all-reduce).  a.D is unused.
 void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, float* ws, int64_t ws_elems);
 int choose_bn(int M, int N, int epi);
+// Decode shapes: GEMM into fp32 slabs of ws (split-K when it fills the SMs),
+// then the low-latency all-reduce (allreduce_ll.h) into a.D.
+void run_allreduce_ll(const GemmArgs& a, const ar::LLArgs& ll, cudaStream_t stream, float* ws, int64_t ws_elems);
 
 CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
                          uint64_t cols, uint64_t ld_elems, uint32_t box_rows, uint32_t box_cols,

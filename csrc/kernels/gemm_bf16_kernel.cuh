@@ -14,9 +14,12 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;                 // 64 bf16 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;                 // TMA warp, MMA warp, 4 epilogue warps
 
 enum Epi : int { kStoreBf16 = 0, kStoreF32 = 1, kSwiGLU = 2, kSplitF32 = 3, kAllReduceBf16 = 4 };
+
+// The fused all-reduce adds 4 communication warps (6..9).
+constexpr int threads_for(int epi) { return epi == kAllReduceBf16 ? kThreads + 128 : kThreads; }
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -28,26 +31,27 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   return v;
 }
 
-// Publishes "this rank's piece with index `idx` is in its buffer" to every
-// rank: one multicast reduction (NVSwitch fans it out) or one remote atomic
-// per rank.  Caller has ordered its data stores before this (bar + fence).
-__device__ __forceinline__ void ar_signal(const ArArgs& ar, int idx) {
+// Arrival / completion signals of the fused all-reduce (see ArArgs).  The
+// caller has ordered its data stores before the signal (barrier + fence).
+__device__ __forceinline__ void ar_signal_one(const ArArgs& ar, int r, int idx) {
+  asm volatile("red.release.sys.global.add.s32 [%0], 1;" ::"l"(ar.cnt_peer[r] + idx) : "memory");
+}
+__device__ __forceinline__ void ar_signal_all(const ArArgs& ar, int idx) {
   if (ar.cnt_mc != nullptr) {
     asm volatile("multimem.red.release.sys.global.add.s32 [%0], 1;" ::"l"(ar.cnt_mc + idx) : "memory");
   } else {
-    for (int r = 0; r < ar.world; ++r)
-      asm volatile("red.release.sys.global.add.s32 [%0], 1;" ::"l"(ar.cnt_peer[r] + idx) : "memory");
+    for (int r = 0; r < ar.world; ++r) ar_signal_one(ar, r, idx);
   }
 }
 
-// Waits (bounded) until every rank published piece `idx`, then re-arms the
-// counter.  Returns false after recording kErrPeerTimeout.
-__device__ __forceinline__ bool ar_wait(const ArArgs& ar, int idx) {
+// Waits (bounded) until counter `idx` reaches `target`, then re-arms it.
+// Returns false after recording kErrPeerTimeout.
+__device__ __forceinline__ bool ar_wait(const ArArgs& ar, int idx, int target) {
   int* c = ar.cnt_local + idx;
-  if (ld_acquire_sys(c) < ar.world) {
+  if (ld_acquire_sys(c) < target) {
     const uint64_t t0 = globaltimer_ns();
     uint32_t spins = 0;
-    while (ld_acquire_sys(c) < ar.world) {
+    while (ld_acquire_sys(c) < target) {
       if ((++spins & 63u) == 0) {
         if (error_pending()) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -57,14 +61,14 @@ __device__ __forceinline__ bool ar_wait(const ArArgs& ar, int idx) {
       }
     }
   }
-  // Every rank has arrived; nobody signals this slot again until this rank's
-  // next operation on the other slot has completed, so a plain reset is safe.
-  atomicSub(c, ar.world);
+  // Every signal of this use has arrived, and none of the next use of the
+  // counter can come before this rank starts that use: a plain re-arm is safe.
+  atomicSub(c, target);
   return true;
 }
 
-// Sum over ranks of 8 bf16 at element offset `off` of the slot (fp32 accumulation).
-__device__ __forceinline__ uint4 ar_load_sum8(const ArArgs& ar, size_t off) {
+// Sum over ranks of the 8 bf16 partials at element offset `off` (fp32 accumulation).
+__device__ __forceinline__ uint4 ar_reduce8(const ArArgs& ar, size_t off) {
   uint4 r;
   if (ar.mc != nullptr) {
     asm volatile("multimem.ld_reduce.weak.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
@@ -86,6 +90,17 @@ __device__ __forceinline__ uint4 ar_load_sum8(const ArArgs& ar, size_t off) {
   }
   return make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
                     pack_bf16x2(acc[6], acc[7]));
+}
+
+// Writes 8 reduced bf16 into every rank's result region at offset `off`.
+__device__ __forceinline__ void ar_store8(const ArArgs& ar, size_t off, uint4 v) {
+  if (ar.out_mc != nullptr) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(ar.out_mc + off),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+    return;
+  }
+  for (int k = 0; k < ar.world; ++k) *reinterpret_cast<uint4*>(ar.out_peer[k] + off) = v;
 }
 
 template <int BN, int STAGES>
@@ -112,7 +127,7 @@ __device__ __forceinline__ int group_of(const int* groups, int num_groups, int m
 }
 
 template <int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for(EPI), 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M,
                      int N, int K, int ldd, int splits, int kb_per_split, ArArgs ar,
@@ -226,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) umma_commit(&tfull_bar[acc]);
       }
     }
-  } else {
+  } else if (warp < 6) {
     // Epilogue warps 2..5 -> TMEM lane quadrant (warp % 4).
     const int quad = warp & 3;
     int local = 0;
@@ -295,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j)
                 packed[j] = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-              // kAllReduceBf16 first publishes the partial tile in this rank's
-              // symmetric slot (row stride N); the reduced tile goes to `out` below.
+              // kAllReduceBf16 publishes the partial tile in this rank's
+              // symmetric partial region (row stride N).
               __nv_bfloat16* dst = EPI == kAllReduceBf16
                                        ? ar.local + (size_t)row * N + n0 + c
                                        : reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + n0 + c;
@@ -311,23 +326,70 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);  // the MMA warp may start the next tile now
       if constexpr (EPI == kAllReduceBf16) {
-        // Tile-level all-reduce: publish, wait for the same tile of every
-        // rank, then read the sum through the NVLink fabric while the MMA warp
-        // already computes this CTA's next tile.
+        // The partial tile is published: signal the tile's owner rank (tiles
+        // are dealt round-robin over the ranks) and go on with the next tile.
         named_bar_sync(1, 128);
         if (threadIdx.x == 64) {
           fence_acq_rel_sys();
-          ar_signal(ar, tile);
-          s_ar_ok = ar_wait(ar, tile) ? 1 : 0;
-        }
-        named_bar_sync(1, 128);
-        if (s_ar_ok && row < M) {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + n0;
-#pragma unroll 4
-          for (int c = 0; c < BN; c += 8)
-            *reinterpret_cast<uint4*>(dst + c) = ar_load_sum8(ar, (size_t)row * N + n0 + c);
+          ar_signal_one(ar, tile % ar.world, tile);
+          if (ar.trace != nullptr) ar.trace[4 * tile] = globaltimer_ns();
         }
       }
+    }
+  } else if constexpr (EPI == kAllReduceBf16) {
+    // Communication warps 6..9: for every tile this rank owns, wait for all
+    // ranks' partials, read their sum through the switch and write it into
+    // every rank's result region, then signal completion to every rank.  They
+    // trail the epilogue without ever blocking it or the MMA warp.
+    const int t = threadIdx.x - 192;
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+      const int tile = unit % num_tiles;
+      if (tile % ar.world != ar.rank) continue;
+      if (t == 0) {
+        s_ar_ok = ar_wait(ar, tile, ar.world) ? 1 : 0;
+        if (ar.trace != nullptr) ar.trace[4 * tile + 1] = globaltimer_ns();
+      }
+      named_bar_sync(2, 128);
+      if (s_ar_ok) {
+        // Coalesced over the tile (consecutive threads, consecutive 16-byte
+        // vectors of a row); up to 16 switch reductions in flight per
+        // thread before their results are stored.
+        const int m0 = (tile % num_m) * BM;
+        const int n0 = (tile / num_m) * BN;
+        constexpr int kVecs = BN / 8;
+        constexpr int kIters = BM * kVecs / 128;
+        constexpr int kBatch = kIters < 16 ? kIters : 16;
+#pragma unroll 1
+        for (int it = 0; it < kIters; it += kBatch) {
+          uint4 v[kBatch];
+          size_t off[kBatch];
+#pragma unroll
+          for (int j = 0; j < kBatch; ++j) {
+            const int i = (it + j) * 128 + t;
+            const int r = m0 + i / kVecs;
+            off[j] = r < M ? (size_t)r * N + n0 + (i % kVecs) * 8 : ~size_t(0);
+            if (r < M) v[j] = ar_reduce8(ar, off[j]);
+          }
+#pragma unroll
+          for (int j = 0; j < kBatch; ++j)
+            if (off[j] != ~size_t(0)) ar_store8(ar, off[j], v[j]);
+        }
+      }
+      named_bar_sync(2, 128);
+      if (t == 0) {
+        fence_acq_rel_sys();
+        ar_signal_all(ar, ar.cnt_capacity + tile);
+        if (ar.trace != nullptr) {
+          ar.trace[4 * tile + 2] = globaltimer_ns();
+          ar.trace[4 * tile + 3] = blockIdx.x + 1;
+        }
+      }
+    }
+    // The kernel ends only when the owners of this CTA's tiles have written
+    // their sums everywhere, so the next kernel on this stream sees them.
+    if (t == 0) {
+      for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x)
+        if (!ar_wait(ar, ar.cnt_capacity + unit % num_tiles, 1)) break;
     }
   }
 
@@ -339,65 +401,99 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Sum over ranks of 4 bf16 at element offset `off` of the slot (fp32 accumulation).
-__device__ __forceinline__ uint2 ar_load_sum4(const ArArgs& ar, size_t off) {
-  uint2 r;
-  if (ar.mc != nullptr) {
-    asm volatile("multimem.ld_reduce.weak.global.add.acc::f32.v2.bf16x2 {%0, %1}, [%2];"
-                 : "=r"(r.x), "=r"(r.y)
-                 : "l"(ar.mc + off)
-                 : "memory");
-    return r;
-  }
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int k = 0; k < ar.world; ++k) {
-    uint2 v;
-    asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(ar.peer[k] + off)
-                 : "memory");
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[e] += __bfloat162float(b[e]);
-  }
-  return make_uint2(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]));
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Split-K finalisation fused with the tensor-parallel all-reduce (persistent:
-// the grid never exceeds what is resident, and every rank walks the items in
-// the same order, so the cross-rank waits cannot deadlock).  Item = one row x
-// 1024 columns: sum the split slabs, publish the bf16 partial in this rank's
-// symmetric slot, signal, wait for every rank's same item, read the sum.
-static __global__ void __launch_bounds__(256) splitk_finalize_ar_kernel(const float* __restrict__ ws,
-                                                                 __nv_bfloat16* __restrict__ out, int M, int N,
-                                                                 int64_t ldd, int splits, ArArgs ar) {
-  __shared__ volatile int ok;
-  const size_t slab = (size_t)M * N;
-  const int chunks = (N + 1023) / 1024;
-  const int items = M * chunks;
-  for (int item = blockIdx.x; item < items; item += gridDim.x) {
-    const int row = item / chunks;
-    const int col = (item % chunks) * 1024 + threadIdx.x * 4;
-    if (col < N) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int sp = 0; sp < splits; ++sp) {
-        const float4 p = *reinterpret_cast<const float4*>(ws + sp * slab + (size_t)row * N + col);
-        v.x += p.x;
-        v.y += p.y;
-        v.z += p.z;
-        v.w += p.w;
+// Counters of the finalize kernel, at the top of the arrival half (the tile
+// path keeps below them): two cross-rank barriers, and the arrival count and
+// generation of this rank's grid barrier.
+constexpr int kFinReserved = 4;
+
+// Barrier over every CTA of this grid and every rank: each CTA makes its
+// stores visible system-wide and arrives on a local counter; the last CTA to
+// arrive signals every rank on counter `xidx`, waits for all of them, and
+// releases this rank's CTAs by bumping the generation.  One cross-rank round
+// trip per rank, whatever the grid size.  Needs every CTA resident.
+__device__ __forceinline__ bool grid_rank_barrier(const ArArgs& ar, int xidx) {
+  __shared__ volatile int s_ok;
+  int* arrive = ar.cnt_local + ar.cnt_capacity - 2;
+  int* gen = ar.cnt_local + ar.cnt_capacity - 1;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    fence_acq_rel_sys();
+    const int g = ld_acquire_gpu(gen);
+    if (atom_add_acq_rel_gpu(arrive, 1) == (int)gridDim.x - 1) {
+      atomicExch(arrive, 0);
+      ar_signal_all(ar, xidx);
+      ok = ar_wait(ar, xidx, ar.world);
+      st_release_gpu(gen, g + 1);
+    } else if (ld_acquire_gpu(gen) == g) {
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ld_acquire_gpu(gen) == g) {
+        if ((++spins & 63u) == 0 && (error_pending() || globaltimer_ns() - t0 > kWaitLimitNs)) {
+          if (!error_pending()) set_error(kErrPeerTimeout, (unsigned long long)xidx);
+          ok = false;
+          break;
+        }
       }
-      *reinterpret_cast<uint2*>(ar.local + (size_t)row * N + col) =
-          make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      fence_acq_rel_sys();
-      ar_signal(ar, item);
-      ok = ar_wait(ar, item) ? 1 : 0;
-    }
-    __syncthreads();
-    if (ok && col < N) *reinterpret_cast<uint2*>(out + (size_t)row * ldd + col) = ar_load_sum4(ar, (size_t)row * N + col);
-    __syncthreads();
+    s_ok = ok ? 1 : 0;
   }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// Split-K finalisation fused with the tensor-parallel all-reduce, over the
+// flattened [M, N] output in 8-element vectors (persistent grid, every CTA
+// resident, same grid on every rank):
+//   1. sum the split slabs, publish the bf16 partials;   barrier
+//   2. reduce this rank's 1/world of the output through the switch and write
+//      it into every rank's result region (8 reductions in flight a thread);
+//                                                         barrier
+// Two cross-rank round trips per operation.
+static __global__ void __launch_bounds__(256, 2) splitk_finalize_ar_kernel(const float* __restrict__ ws, int M, int N,
+                                                                 int splits, ArArgs ar) {
+  const size_t slab = (size_t)M * N;
+  const int64_t nvec = (int64_t)slab / 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int64_t v = first; v < nvec; v += stride) {
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4* p = reinterpret_cast<const float4*>(ws + sp * slab + v * 8);
+      const float4 x = p[0], y = p[1];
+      a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
+      a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
+    }
+    *reinterpret_cast<uint4*>(ar.local + v * 8) =
+        make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+  }
+  if (!grid_rank_barrier(ar, ar.cnt_capacity - kFinReserved)) return;
+  const int64_t v0 = nvec * ar.rank / ar.world, v1 = nvec * (ar.rank + 1) / ar.world;
+  constexpr int kBatch = 8;
+  for (int64_t base = v0 + first; base < v1; base += kBatch * stride) {
+    uint4 r[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (base + j * stride < v1) r[j] = ar_reduce8(ar, (size_t)(base + j * stride) * 8);
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (base + j * stride < v1) ar_store8(ar, (size_t)(base + j * stride) * 8, r[j]);
+  }
+  grid_rank_barrier(ar, ar.cnt_capacity - kFinReserved + 1);
 }
 
 // Split-K finalisation: sum the per-split fp32 slabs in split order and write

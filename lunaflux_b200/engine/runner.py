@@ -143,13 +143,14 @@ class ModelRunner:
                 ops.attn_decode(qkv, attn, v["d_tok"], v["d_seqlen"], v["d_bt"], kc, vc, Hq, Hkv, splits,
                                 self.part_o, self.part_lse,
                                 host={"seq_lens": hm.get("d_seq_lens"), "tok": hm.get("d_tok")})
-            self._row_parallel(attn, lw, "wo", delta, ws)
+            delta = self._row_parallel(attn, lw, "wo", self.delta[:T], ws)
             ops.rmsnorm(delta, resid, lw.ln2, h, eps)
             if s.is_moe:
+                delta = self.delta[:T]
                 self.moe(h, delta, lw)
             else:
                 self._proj(h, lw, "wgu", act, 2)
-                self._row_parallel(act, lw, "wd", delta, ws)
+                delta = self._row_parallel(act, lw, "wd", self.delta[:T], ws)
         ops.rmsnorm(delta, resid, w.norm, h, eps)
         if gather:
             hs = self.hs[:Rs]
@@ -204,7 +205,9 @@ class ModelRunner:
     def _row_parallel(self, A, lw, name, out, ws):
         """Row-parallel projection: partial GEMM then the sum over ranks, either
         as one fused GEMM + all-reduce kernel or as GEMM followed by the
-        library all-reduce (the measured baseline)."""
+        library all-reduce (the measured baseline).  Returns the tensor holding
+        the result: ``out``, or with the fused path a view of the symmetric
+        result region."""
         f = self._fp8(lw, name)
         fused = self.comm is not None and getattr(self.comm, "fused", False)
         if f is not None:
@@ -212,22 +215,22 @@ class ModelRunner:
             if fused:
                 part = ws[: out.numel()].view(out.shape)
                 self.ops.gemm_fp8(q, s, f[0], f[1], part, 1)
-                self.comm.reduce_partials(part, out)
                 self.ops.launches += 1
-                return
+                return self.comm.reduce_partials(part)
             self.ops.gemm_fp8(q, s, f[0], f[1], out, 0)
             if self.comm is not None:
                 self.comm.all_reduce(out)
-            return
+            return out
         W = getattr(lw, name)
         if self.comm is None:
             self.ops.gemm(A, W, out, 0, ws)
         elif fused:
-            self.comm.gemm_allreduce(A, W, out, ws)
             self.ops.launches += 2
+            return self.comm.gemm_allreduce(A, W, ws)
         else:
             self.ops.gemm(A, W, out, 0, ws)
             self.comm.all_reduce(out)
+        return out
 
     def _moe_rows(self, T: int) -> int:
         """Rows of the expert-ordered activations for T tokens: every

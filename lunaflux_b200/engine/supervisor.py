@@ -16,14 +16,16 @@ fails the generation: every rank is terminated and reaped, requests that had
 produced tokens fail with ``worker_unavailable`` (retryable), requests that had
 not are re-submitted to the next generation, which is started fresh.
 
-The control channel is a multiprocessing pipe (length-prefixed pickled
-frames of plain tuples); the GPU data path never crosses it.
+The control channel is a socketpair carrying framed, checksummed messages
+(``engine/channel.py``: the C++ channel core with exact I/O and deadlines);
+the GPU data path never crosses it.
 """
 from __future__ import annotations
 
 import dataclasses
 import multiprocessing as mp
 import os
+import select
 import socket
 import threading
 import time
@@ -31,6 +33,7 @@ import traceback
 from typing import Callable, Dict, List, Optional, Tuple
 
 from ..contracts import PublicErrorCode
+from .channel import MessageChannel
 
 
 def _free_port() -> int:
@@ -41,16 +44,15 @@ def _free_port() -> int:
     return p
 
 
-def _rank_main(rank: int, world: int, port: int, factory: Callable, conn, heartbeat_s: float, generation: int):
+def _rank_main(rank: int, world: int, port: int, factory: Callable, sock, heartbeat_s: float, generation: int):
     """Worker process body: build the engine, then serve the command stream."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), LUNAFLUX_GENERATION=str(generation))
-    lock = threading.Lock()
+    conn = MessageChannel(sock)
     stop = threading.Event()
 
     def send(msg):
-        with lock:
-            conn.send(msg)
+        conn.send(msg)  # the channel serialises concurrent senders
 
     def beat():
         while not stop.is_set():
@@ -65,7 +67,9 @@ def _rank_main(rank: int, world: int, port: int, factory: Callable, conn, heartb
         engine = factory(rank, world)
         send(("ready", rank))
         while True:
-            msg = conn.recv()
+            msg = conn.recv(1.0)
+            if msg is None:
+                continue
             kind = msg[0]
             if kind == "add":
                 _, rid, prompt, max_new, sampling, stop_ids = msg
@@ -131,13 +135,13 @@ class Supervisor:
         port = _free_port()
         self.procs, self.conns = [], []
         for r in range(self.world):
-            parent, child = self.ctx.Pipe()
+            parent, child = socket.socketpair()
             p = self.ctx.Process(target=_rank_main, args=(r, self.world, port, self.factory, child, self.heartbeat_s,
                                                           self.generation), daemon=True)
             p.start()
             child.close()
             self.procs.append(p)
-            self.conns.append(parent)
+            self.conns.append(MessageChannel(parent))
         now = time.monotonic()
         self.last_beat = {r: now for r in range(self.world)}
         self.ready = set()  # heartbeats are checked once a rank has finished starting
@@ -196,13 +200,15 @@ class Supervisor:
                     raise WorkerLost(f"rank {r} missed heartbeats")
             if now > deadline:
                 raise WorkerLost("step timed out")
-            ready = mp.connection.wait(self.conns, timeout=min(0.05, self.heartbeat_s))
+            ready = select.select(self.conns, [], [], min(0.05, self.heartbeat_s))[0]
             for c in ready:
                 r = self.conns.index(c)
                 try:
-                    msg = c.recv()
+                    msg = c.recv(0.0)
                 except (EOFError, OSError):
                     raise WorkerLost(f"rank {r} channel closed")
+                if msg is None:
+                    continue
                 if msg[0] == "hb":
                     self.last_beat[r] = time.monotonic()
                 elif msg[0] == "error":

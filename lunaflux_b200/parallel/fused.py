@@ -3,20 +3,37 @@
 The o_proj and down projections of a tensor-parallel layer produce partial
 sums on every rank.  Instead of a GEMM followed by a library all-reduce,
 ``gemm_allreduce`` runs ONE tcgen05 kernel per rank whose epilogue publishes
-each finished output tile in a symmetric buffer, signals the tile to every
-rank, waits (bounded) for the same tile of all ranks and reads the sum back
-through the NVSwitch fabric with ``multimem.ld_reduce`` (or peer loads when
-the fabric offers no multicast), while the MMA warp of the same CTA already
-computes its next tile.  Skinny decode shapes use split-K; there the
-all-reduce is fused into the persistent split-K finalize kernel.
+each finished output tile in a symmetric buffer and signals the tile's owner
+rank (tiles are dealt round-robin over the ranks).  The owner reads the sum of
+all ranks' partials through the NVSwitch (``multimem.ld_reduce``) and writes
+it into every rank's result region (``multimem.st``); the other ranks' CTAs
+go straight on to their next tile, and the MMA warp of every CTA keeps
+computing while its epilogue communicates.  Each rank moves about twice the
+output size over NVLink whatever the group size: a bandwidth-optimal
+all-reduce with no extra launch.  Without multicast support the same steps
+use peer loads and stores.
 
-Buffers: two slots (ping-pong) of [max_rows, hidden] bf16 plus per-piece
-int32 arrival counters, allocated with ``torch.distributed._symmetric_memory``
-so that every rank has the peer and multicast addresses.  Two slots suffice:
-a rank can only re-use a slot after passing the next operation's wait, which
-needs every peer to have finished reading the previous contents.
+Decode row counts (at most ``ll_rows``) are latency-bound instead: the GEMM
+writes fp32 split-K slabs and the finalize kernel runs a low-latency
+reduce-scatter + all-gather whose 8-byte words carry the data and the
+operation's epoch together (no fences, no flags, no barriers; see
+csrc/kernels/allreduce_ll.cu).  Its result lands in a local buffer.
+
+Buffers: two slots (ping-pong), each a partial region and a result region of
+[max_rows, hidden] bf16 plus int32 arrival / completion counters, allocated
+with ``torch.distributed._symmetric_memory`` so that every rank has the peer
+and multicast addresses.  The result of an operation is a view of the result
+region, consumed before the operation after next re-uses the slot.  Two slots
+suffice: an owner writes a rank's result region of slot s only after that
+rank has published a tile of the new operation, so it has finished every
+kernel before it, including the consumer of the previous result in slot s;
+and an operation ends on every rank only after every owner has read its
+partials.
 """
 from __future__ import annotations
+
+import os
+from typing import Optional
 
 import torch
 import torch.distributed as dist
@@ -32,7 +49,7 @@ class FusedTPComm(TPComm):
 
     fused = True
 
-    def __init__(self, max_rows: int, hidden: int, device, group=None):
+    def __init__(self, max_rows: int, hidden: int, device, group=None, ll_rows: Optional[int] = None):
         super().__init__(group)
         import torch.distributed._symmetric_memory as symm
         self.C = _ext.load()
@@ -41,8 +58,9 @@ class FusedTPComm(TPComm):
         g = group or dist.group.WORLD
         name = g.group_name
         slot_elems = max_rows * hidden
-        self.data = symm.empty(2 * slot_elems, dtype=torch.bfloat16, device=device)
-        self.cnt = symm.empty(2 * COUNTER_CAPACITY, dtype=torch.int32, device=device)
+        # [slot][partial | result][max_rows * hidden]
+        self.data = symm.empty(4 * slot_elems, dtype=torch.bfloat16, device=device)
+        self.cnt = symm.empty(2 * 2 * COUNTER_CAPACITY, dtype=torch.int32, device=device)
         self.data.zero_()
         self.cnt.zero_()
         hd = symm.rendezvous(self.data, name)
@@ -50,41 +68,85 @@ class FusedTPComm(TPComm):
         torch.cuda.synchronize(device)
         dist.barrier(group=g)
         self.multicast = bool(getattr(hd, "multicast_ptr", 0)) and bool(getattr(hc, "multicast_ptr", 0))
+        if os.environ.get("LUNAFLUX_FUSED_MULTICAST", "1") == "0":
+            self.multicast = False   # peer loads and stores only
         dbytes = slot_elems * 2
-        cbytes = COUNTER_CAPACITY * 4
+        cbytes = 2 * COUNTER_CAPACITY * 4
         self.slots = []
         for s in range(2):
+            part, res = 2 * s * dbytes, (2 * s + 1) * dbytes
             self.slots.append(dict(
-                local=self.data.data_ptr() + s * dbytes,
-                mc=(hd.multicast_ptr + s * dbytes) if self.multicast else 0,
-                peers=[p + s * dbytes for p in hd.buffer_ptrs],
+                local=self.data.data_ptr() + part,
+                mc=(hd.multicast_ptr + part) if self.multicast else 0,
+                peers=[p + part for p in hd.buffer_ptrs],
+                out_mc=(hd.multicast_ptr + res) if self.multicast else 0,
+                out_peers=[p + res for p in hd.buffer_ptrs],
                 cnt_local=self.cnt.data_ptr() + s * cbytes,
                 cnt_mc=(hc.multicast_ptr + s * cbytes) if self.multicast else 0,
                 cnt_peers=[p + s * cbytes for p in hc.buffer_ptrs],
+                result=self.data[(2 * s + 1) * slot_elems:(2 * s + 2) * slot_elems],
             ))
-        self._handles = (hd, hc)
+        # Low-latency protocol for decode row counts (rows <= ll_rows): inboxes
+        # of 8-byte words (bf16 pair + epoch), see csrc/kernels/allreduce_ll.cu.
+        if ll_rows is None:
+            ll_rows = int(os.environ.get("LUNAFLUX_FUSED_LL_ROWS", str(min(max_rows, 1024))))
+        self.ll_rows = ll_rows
+        self.ll_pairs = max(self.ll_rows, 1) * hidden // 2
+        rs_words = self.ll_pairs + self.world
+        self.ll = symm.empty(rs_words + self.ll_pairs, dtype=torch.int64, device=device)
+        self.ll.zero_()
+        hl = symm.rendezvous(self.ll, name)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=g)
+        self.ll_rs = list(hl.buffer_ptrs)
+        self.ll_ag = [p + rs_words * 8 for p in hl.buffer_ptrs]
+        self.ll_state = torch.zeros(2, dtype=torch.int32, device=device)
+        self.ll_out = torch.empty(max(self.ll_rows, 1), hidden, dtype=torch.bfloat16, device=device)
+        self._handles = (hd, hc, hl)
         self.op_index = 0
+        self.trace = None   # optional int64 tensor [4 * tiles]: per-tile timeline of the next calls
 
     def begin_forward(self):
         """Every forward has an even number of fused operations, so starting
         each forward on slot 0 keeps the strict slot alternation."""
         self.op_index = 0
 
-    def gemm_allreduce(self, A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, ws=None):
-        if A.shape[0] > self.max_rows or B.shape[0] != self.hidden:
-            raise ValueError("gemm_allreduce: shape exceeds the symmetric buffer")
+    def _slot(self):
         s = self.slots[self.op_index & 1]
         self.op_index += 1
         self.calls += 1
-        self.C.gemm_allreduce(A, B, out, ws, s["local"], s["mc"], s["peers"], s["cnt_local"], s["cnt_mc"],
-                              s["cnt_peers"], COUNTER_CAPACITY)
+        return s
 
-    def reduce_partials(self, part: torch.Tensor, out: torch.Tensor):
-        """out (bf16) = sum over ranks of this rank's fp32 partial ``part``."""
-        if part.shape[0] > self.max_rows or part.shape[1] != self.hidden:
+    def _args(self, s):
+        return (s["local"], s["mc"], s["peers"], s["out_mc"], s["out_peers"], s["cnt_local"], s["cnt_mc"],
+                s["cnt_peers"], self.rank, COUNTER_CAPACITY,
+                self.trace.data_ptr() if self.trace is not None else 0)
+
+    def gemm_allreduce(self, A: torch.Tensor, B: torch.Tensor, ws=None) -> torch.Tensor:
+        """Returns the [M, hidden] bf16 sum over ranks of A . B^T (a view of the
+        slot's result region, valid until the operation after next)."""
+        M = A.shape[0]
+        if M > self.max_rows or B.shape[0] != self.hidden:
+            raise ValueError("gemm_allreduce: shape exceeds the symmetric buffer")
+        if M <= self.ll_rows and ws is not None:
+            out = self.ll_out[:M]
+            self.calls += 1
+            self.C.gemm_allreduce_ll(A, B, out, ws, self.ll_rs, self.ll_ag, self.ll_state, self.rank, self.ll_pairs)
+            return out
+        s = self._slot()
+        self.C.gemm_allreduce(A, B, ws, *self._args(s))
+        return s["result"][: M * self.hidden].view(M, self.hidden)
+
+    def reduce_partials(self, part: torch.Tensor) -> torch.Tensor:
+        """Returns the bf16 sum over ranks of this rank's fp32 partial ``part``."""
+        M, N = part.shape
+        if M > self.max_rows or N != self.hidden:
             raise ValueError("reduce_partials: shape exceeds the symmetric buffer")
-        s = self.slots[self.op_index & 1]
-        self.op_index += 1
-        self.calls += 1
-        self.C.partials_allreduce(part, out, 1, s["local"], s["mc"], s["peers"], s["cnt_local"], s["cnt_mc"],
-                                  s["cnt_peers"], COUNTER_CAPACITY)
+        if M <= self.ll_rows:
+            out = self.ll_out[:M]
+            self.calls += 1
+            self.C.partials_allreduce_ll(part, 1, out, self.ll_rs, self.ll_ag, self.ll_state, self.rank, self.ll_pairs)
+            return out
+        s = self._slot()
+        self.C.partials_allreduce(part, M, N, 1, *self._args(s))
+        return s["result"][: M * N].view(M, N)

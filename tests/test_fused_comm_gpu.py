@@ -1,8 +1,10 @@
 """Fused GEMM + all-reduce on 2+ GPUs (one process per GPU, NCCL bootstrap).
 
-Every rank multiplies its own A_r by its own B_r; the fused kernel must return
-sum_r A_r . B_r^T on every rank, for the tile path and the split-K path, over
-many calls in a row (exercising both ping-pong slots and counter re-arming).
+Every rank multiplies its own A_r by its own B_r; the fused kernels must return
+sum_r A_r . B_r^T on every rank: the low-latency protocol (decode rows), the
+flag protocol's tile path and split-K finalize path, and the partial-sum
+reduction of each, over many calls in a row (exercising the epochs, both
+ping-pong slots and the counter re-arming).
 Reference: the fp32 products all-reduced with NCCL.
 """
 import os
@@ -35,35 +37,42 @@ def _worker(rank, world, port, q):
         from lunaflux_b200.parallel.comm import init_distributed
         from lunaflux_b200.parallel.fused import FusedTPComm
         init_distributed("nccl", timeout_s=120, device_id=rank)
-        comm = FusedTPComm(8192, 4096, dev)
-        C = comm.C
+        # default routing (low-latency protocol up to 1024 rows, tile path above)
+        # and the flag protocol everywhere (split-K finalize kernel, tile path)
+        comms = [FusedTPComm(8192, 4096, dev), FusedTPComm(8192, 4096, dev, ll_rows=0)]
+        C = comms[0].C
         ws = torch.zeros(512 * 32768, device=dev)
         errs = []
         for it in range(3):
-            for (M, N, K) in SHAPES:
-                g = torch.Generator(device=dev).manual_seed(1000 * rank + 7 * it + M)
-                A = torch.randn(M, K, device=dev, generator=g).bfloat16()
-                B = (torch.randn(N, K, device=dev, generator=g) * 0.05).bfloat16()
-                part = A.float() @ B.float().t()
-                ref = part.clone()
-                dist.all_reduce(ref)
-                # The library baseline on the same data: bf16 partials, bf16 all-reduce.
-                lib = part.bfloat16()
-                dist.all_reduce(lib)
-                lib_err = float((lib.float() - ref).abs().max().item())
-                out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-                comm.gemm_allreduce(A, B, out, ws)
-                torch.cuda.synchronize(dev)
-                code = C.read_error(True)[0]
-                err = (out.float() - ref).abs()
-                # bf16 partials are summed over `world` ranks: allow the rounding of
-                # every partial, and never more than twice the library's own error.
-                tol = (3e-2 + 3e-2 * ref.abs()) * max(1.0, world / 2)
-                bad = int((err > tol).sum().item())
-                mx = float(err.max().item())
-                if mx > max(2 * lib_err, 0.05):
-                    bad = max(bad, 1)
-                errs.append((M, N, K, code, bad, mx))
+            for ci, comm in enumerate(comms):
+                for (M, N, K) in SHAPES:
+                    g = torch.Generator(device=dev).manual_seed(1000 * rank + 7 * it + M)
+                    A = torch.randn(M, K, device=dev, generator=g).bfloat16()
+                    B = (torch.randn(N, K, device=dev, generator=g) * 0.05).bfloat16()
+                    part = A.float() @ B.float().t()
+                    ref = part.clone()
+                    dist.all_reduce(ref)
+                    # The library baseline on the same data: bf16 partials, bf16 all-reduce.
+                    lib = part.bfloat16()
+                    dist.all_reduce(lib)
+                    lib_err = float((lib.float() - ref).abs().max().item())
+                    outs = [comm.gemm_allreduce(A, B, ws).clone()]
+                    if M <= 1024:
+                        ws[: M * N].copy_(part.flatten())
+                        outs.append(comm.reduce_partials(ws[: M * N].view(M, N)).clone())
+                    torch.cuda.synchronize(dev)
+                    code = C.read_error(True)[0]
+                    for out in outs:
+                        err = (out.float() - ref).abs()
+                        # bf16 partials are summed over `world` ranks: allow the rounding of
+                        # every partial, and never more than twice the library's own error.
+                        tol = (3e-2 + 3e-2 * ref.abs()) * max(1.0, world / 2)
+                        bad = int((err > tol).sum().item())
+                        mx = float(err.max().item())
+                        if mx > max(2 * lib_err, 0.05):
+                            bad = max(bad, 1)
+                        errs.append((ci, M, N, K, code, bad, mx))
+        comm = comms[0]
         q.put((rank, errs, comm.multicast))
         dist.barrier()
         dist.destroy_process_group()
@@ -89,6 +98,6 @@ def test_fused_gemm_allreduce_matches_nccl():
         p.join(timeout=60)
     for r, (errs, mc) in res.items():
         assert not isinstance(errs, str), errs
-        for (M, N, K, code, bad, mx) in errs:
-            assert code == 0, f"rank {r} {M}x{N}x{K}: device error {code}"
-            assert bad == 0, f"rank {r} {M}x{N}x{K}: {bad} elements off (max {mx}); multicast={mc}"
+        for (ci, M, N, K, code, bad, mx) in errs:
+            assert code == 0, f"rank {r} comm {ci} {M}x{N}x{K}: device error {code}"
+            assert bad == 0, f"rank {r} comm {ci} {M}x{N}x{K}: {bad} elements off (max {mx}); multicast={mc}"
