@@ -8,6 +8,11 @@ relative locator is resolved one component at a time with
 component can leave the root.  ``read_snapshot`` returns the bytes together
 with a (device, inode, size, mtime, ctime) stamp and fails if the file changed
 while it was read.
+
+``ApprovedRoot`` uses the C++ core (``lunaflux_b200._host.ApprovedRoot``:
+the same traversal, reads with the GIL released, ``read_into`` straight into a
+caller's buffer such as pinned host memory) when it is built; ``PyApprovedRoot``
+is the reference implementation it is tested against.
 """
 from __future__ import annotations
 
@@ -34,7 +39,9 @@ def _stamp(st) -> Stamp:
     return Stamp(st.st_dev, st.st_ino, st.st_size, st.st_mtime_ns, st.st_ctime_ns)
 
 
-class ApprovedRoot:
+class PyApprovedRoot:
+    """Reference implementation (pure Python, os.open with dir_fd)."""
+
     def __init__(self, path: str):
         if not os.path.isabs(path):
             raise ApprovedFsError("approved root must be an absolute path")
@@ -99,3 +106,57 @@ class ApprovedRoot:
             return data, before
         finally:
             os.close(fd)
+
+
+class NativeApprovedRoot:
+    """The same interface backed by the C++ core."""
+
+    def __init__(self, path: str):
+        from .. import _host
+        self._h = _host
+        try:
+            self._r = _host.ApprovedRoot(path)
+        except _host.ApprovedFsError as e:
+            raise ApprovedFsError(str(e)) from None
+        self.identity = Stamp(*self._r.identity())
+
+    def close(self):
+        self._r.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def read_snapshot(self, locator: str, max_bytes: int = 1 << 34) -> Tuple[bytes, Stamp]:
+        try:
+            data, st = self._r.read_snapshot(locator, max_bytes)
+        except self._h.ApprovedFsError as e:
+            raise ApprovedFsError(str(e)) from None
+        return data, Stamp(*st)
+
+    def stat(self, locator: str) -> Stamp:
+        try:
+            return Stamp(*self._r.stat(locator))
+        except self._h.ApprovedFsError as e:
+            raise ApprovedFsError(str(e)) from None
+
+    def read_into(self, locator: str, buf) -> Stamp:
+        """Reads the whole file into the start of a writable buffer (e.g. a
+        pinned uint8 tensor's numpy view); fails if it does not fit."""
+        try:
+            return Stamp(*self._r.read_into(locator, buf))
+        except self._h.ApprovedFsError as e:
+            raise ApprovedFsError(str(e)) from None
+
+
+def _select():
+    try:
+        from .. import _host  # noqa: F401
+        return NativeApprovedRoot
+    except ImportError:
+        return PyApprovedRoot
+
+
+ApprovedRoot = _select()

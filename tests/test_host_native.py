@@ -88,3 +88,102 @@ def test_bpe_native_equals_reference():
     for _ in range(300):
         data = bytes(rng.choice(alphabet) for _ in range(rng.randint(0, 60)))
         assert tok._bpe(data) == tok._bpe_reference(data)
+
+
+# ---------------------------------------------------------------- framed channel
+import socket
+import struct
+
+from lunaflux_b200.engine import channel as chan
+
+
+def _pair(native_a: bool, native_b: bool, frame_timeout_s: float = 0.3):
+    a, b = socket.socketpair()
+    ca = chan.open_channel(a.fileno(), 1 << 20, frame_timeout_s, native=native_a)
+    cb = chan.open_channel(b.fileno(), 1 << 20, frame_timeout_s, native=native_b)
+    return a, b, ca, cb
+
+
+@pytest.mark.parametrize("na,nb", [(True, True), (True, False), (False, True), (False, False)])
+def test_channel_roundtrip_across_implementations(na, nb):
+    a, b, ca, cb = _pair(na, nb)
+    msgs = [b"", b"x", bytes(range(256)) * 300]
+    for m in msgs:
+        ca.send(m, 1.0)
+    for m in msgs:
+        assert cb.recv(1.0) == m
+    assert cb.recv(0.05) is None          # nothing pending: a timeout, not an error
+    cb.send(b"back", 1.0)
+    assert ca.recv(1.0) == b"back"
+
+
+@pytest.mark.parametrize("native", [True, False])
+def test_channel_rejects_corrupt_frames(native):
+    closed = chan.CLOSED_ERRORS
+    for bad in (struct.pack("<IIQ", 0xDEADBEEF, 1, chan.fnv1a64(b"a")) + b"a",       # magic
+                struct.pack("<IIQ", chan.MAGIC, 1, chan.fnv1a64(b"a") ^ 1) + b"a",   # checksum
+                struct.pack("<IIQ", chan.MAGIC, (1 << 20) + 1, 0)):                  # length
+        a, b = socket.socketpair()
+        c = chan.open_channel(b.fileno(), 1 << 20, 0.3, native=native)
+        a.sendall(bad)
+        with pytest.raises(closed):
+            c.recv(1.0)
+        with pytest.raises(closed):       # poisoned from now on
+            c.recv(0.01)
+
+
+@pytest.mark.parametrize("native", [True, False])
+def test_channel_partial_frame_times_out_and_eof_is_closed(native):
+    a, b = socket.socketpair()
+    c = chan.open_channel(b.fileno(), 1 << 20, 0.2, native=native)
+    a.sendall(struct.pack("<IIQ", chan.MAGIC, 10, 0) + b"abc")   # frame never completes
+    with pytest.raises(chan.TIMEOUT_ERRORS):
+        c.recv(1.0)
+    a2, b2 = socket.socketpair()
+    c2 = chan.open_channel(b2.fileno(), 1 << 20, 0.2, native=native)
+    a2.close()
+    with pytest.raises(chan.CLOSED_ERRORS):
+        c2.recv(1.0)
+
+
+def test_message_channel_pickles_tuples():
+    a, b = socket.socketpair()
+    ma, mb = chan.MessageChannel(a), chan.MessageChannel(b)
+    ma.send(("outs", 1, [(3, 7, False)], [], True))
+    assert mb.recv(1.0) == ("outs", 1, [(3, 7, False)], [], True)
+    ma.close()
+    with pytest.raises(EOFError):
+        mb.recv(1.0)
+
+
+# ---------------------------------------------------------------- approved root
+def test_approved_root_native_matches_reference(tmp_path):
+    import os
+
+    import numpy as np
+
+    from lunaflux_b200.utils.approved_fs import ApprovedFsError, NativeApprovedRoot, PyApprovedRoot
+    (tmp_path / "d").mkdir()
+    (tmp_path / "d" / "w.bin").write_bytes(bytes(range(200)) * 50)
+    (tmp_path / "outside.txt").write_text("secret")
+    os.symlink(str(tmp_path / "outside.txt"), str(tmp_path / "d" / "link"))
+    os.symlink(str(tmp_path / "d"), str(tmp_path / "dlink"))
+    with PyApprovedRoot(str(tmp_path)) as p, NativeApprovedRoot(str(tmp_path)) as n:
+        assert p.identity == n.identity
+        dp, sp = p.read_snapshot("d/w.bin")
+        dn, sn = n.read_snapshot("d/w.bin")
+        assert dp == dn and sp == sn
+        buf = np.zeros(20000, dtype=np.uint8)
+        assert n.read_into("d/w.bin", buf) == sp
+        assert bytes(buf[:10000]) == dp
+        for loc in ("d/link", "dlink/w.bin", "../x", "/etc/passwd", "d/./w.bin", "d//w.bin", "", "d", "nope"):
+            with pytest.raises(ApprovedFsError):
+                p.read_snapshot(loc)
+            with pytest.raises(ApprovedFsError):
+                n.read_snapshot(loc)
+        with pytest.raises(ApprovedFsError):
+            n.read_snapshot("d/w.bin", 100)          # size limit
+        with pytest.raises(ApprovedFsError):
+            n.read_into("d/w.bin", np.zeros(10, dtype=np.uint8))
+    with pytest.raises(ApprovedFsError):
+        NativeApprovedRoot("relative/path")
