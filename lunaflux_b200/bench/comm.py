@@ -85,7 +85,7 @@ def main(argv=None):
         for name, K in (("o", 4096), ("down", 14336)):
             shapes.append((f"M{M} {name}", M, K // world))
     max_rows = max(M for _, M, _ in shapes)
-    comm = FusedTPComm(max_rows, hidden, torch.device("cuda", local))
+    comm = FusedTPComm(max_rows, hidden, torch.device("cuda", local), tile_min_k=0)  # the fused kernels themselves
     ws = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
     _, tflops, src = peaks()
     rows = []

@@ -49,7 +49,8 @@ class FusedTPComm(TPComm):
 
     fused = True
 
-    def __init__(self, max_rows: int, hidden: int, device, group=None, ll_rows: Optional[int] = None):
+    def __init__(self, max_rows: int, hidden: int, device, group=None, ll_rows: Optional[int] = None,
+                 tile_min_k: Optional[int] = None):
         super().__init__(group)
         import torch.distributed._symmetric_memory as symm
         self.C = _ext.load()
@@ -102,6 +103,15 @@ class FusedTPComm(TPComm):
         self.ll_ag = [p + rs_words * 8 for p in hl.buffer_ptrs]
         self.ll_state = torch.zeros(2, dtype=torch.int32, device=device)
         self.ll_out = torch.empty(max(self.ll_rows, 1), hidden, dtype=torch.bfloat16, device=device)
+        # Prefill rows: the tile path overlaps each tile's reduction with the
+        # next tiles' math, which pays off when a rank's K share is large
+        # (Llama-3-8B down at TP=2, K=7168: 1.17x over GEMM -> NCCL) and not
+        # when it is small (o_proj at TP=2, K=2048: 0.83x); below tile_min_k
+        # the GEMM is followed by the library all-reduce.
+        if tile_min_k is None:
+            tile_min_k = int(os.environ.get("LUNAFLUX_FUSED_TILE_MIN_K", "4096"))
+        self.tile_min_k = tile_min_k
+        self.lib_out = torch.empty(max_rows, hidden, dtype=torch.bfloat16, device=device)
         self._handles = (hd, hc, hl)
         self.op_index = 0
         self.trace = None   # optional int64 tensor [4 * tiles]: per-tile timeline of the next calls
@@ -132,6 +142,13 @@ class FusedTPComm(TPComm):
             out = self.ll_out[:M]
             self.calls += 1
             self.C.gemm_allreduce_ll(A, B, out, ws, self.ll_rs, self.ll_ag, self.ll_state, self.rank, self.ll_pairs)
+            return out
+        if A.shape[1] < self.tile_min_k:
+            # too little math per tile to hide the tile's reduction behind:
+            # the GEMM, then the library all-reduce (measured faster here)
+            out = self.lib_out[:M]
+            self.C.gemm(A, B, out, 0, 0, ws)
+            self.all_reduce(out)
             return out
         s = self._slot()
         self.C.gemm_allreduce(A, B, ws, *self._args(s))

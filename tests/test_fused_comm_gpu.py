@@ -39,7 +39,7 @@ def _worker(rank, world, port, q):
         init_distributed("nccl", timeout_s=120, device_id=rank)
         # default routing (low-latency protocol up to 1024 rows, tile path above)
         # and the flag protocol everywhere (split-K finalize kernel, tile path)
-        comms = [FusedTPComm(8192, 4096, dev), FusedTPComm(8192, 4096, dev, ll_rows=0)]
+        comms = [FusedTPComm(8192, 4096, dev), FusedTPComm(8192, 4096, dev, ll_rows=0, tile_min_k=0)]
         C = comms[0].C
         ws = torch.zeros(512 * 32768, device=dev)
         errs = []
