@@ -108,8 +108,8 @@ void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, c10::optional<at::
   lf::gemm::run_allreduce(a, ar, stream(), wsp, ws_elems);
 }
 
-static lf::ar::LLArgs make_ll(const std::vector<int64_t>& rs, const std::vector<int64_t>& ag, const at::Tensor& state,
-                              int64_t rank, int64_t max_pairs) {
+static lf::ar::LLArgs make_ll(const std::vector<int64_t>& rs, const std::vector<int64_t>& ag, int64_t ag_mc,
+                              const at::Tensor& state, int64_t rank, int64_t max_pairs) {
   LF_CHECK(!rs.empty() && rs.size() <= (size_t)lf::ar::kMaxRanks && ag.size() == rs.size(), "low-latency all-reduce: peers");
   LF_CHECK(rank >= 0 && rank < (int64_t)rs.size(), "low-latency all-reduce: rank");
   LF_CHECK(state.is_cuda() && state.scalar_type() == at::kInt && state.numel() >= 2, "low-latency all-reduce: state");
@@ -118,6 +118,7 @@ static lf::ar::LLArgs make_ll(const std::vector<int64_t>& rs, const std::vector<
     a.rs[i] = reinterpret_cast<uint2*>(rs[i]);
     a.ag[i] = reinterpret_cast<uint2*>(ag[i]);
   }
+  a.ag_mc = reinterpret_cast<uint2*>(ag_mc);
   a.state = state.data_ptr<int>();
   a.rank = (int)rank;
   a.world = (int)rs.size();
@@ -127,7 +128,8 @@ static lf::ar::LLArgs make_ll(const std::vector<int64_t>& rs, const std::vector<
 
 // D (bf16 [M, N]) = sum over ranks of A . B^T, low-latency protocol (decode shapes).
 void gemm_allreduce_ll(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, at::Tensor& ws, std::vector<int64_t> rs,
-                       std::vector<int64_t> ag, const at::Tensor& state, int64_t rank, int64_t max_pairs) {
+                       std::vector<int64_t> ag, int64_t ag_mc, const at::Tensor& state, int64_t rank,
+                       int64_t max_pairs) {
   check_rowmajor(A, "A");
   check_rowmajor(B, "B");
   check_rowmajor(D, "D");
@@ -136,7 +138,7 @@ void gemm_allreduce_ll(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, 
   LF_CHECK(ws.scalar_type() == at::kFloat && ws.is_cuda(), "gemm_allreduce_ll: fp32 workspace");
   const int M = A.size(0), N = B.size(0), K = A.size(1);
   LF_CHECK(D.size(0) == M && D.size(1) == N, "gemm_allreduce_ll output must be [M, N]");
-  lf::ar::LLArgs ll = make_ll(rs, ag, state, rank, max_pairs);
+  lf::ar::LLArgs ll = make_ll(rs, ag, ag_mc, state, rank, max_pairs);
   c10::cuda::CUDAGuard g(A.device());
   lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), B.stride(0), D.stride(0)};
   lf::gemm::run_allreduce_ll(a, ll, stream(), ws.data_ptr<float>(), ws.numel());
@@ -144,13 +146,14 @@ void gemm_allreduce_ll(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, 
 
 // D = sum over ranks of the sum of `splits` fp32 [M, N] slabs of ws (low-latency protocol).
 void partials_allreduce_ll(const at::Tensor& ws, int64_t splits, at::Tensor& D, std::vector<int64_t> rs,
-                           std::vector<int64_t> ag, const at::Tensor& state, int64_t rank, int64_t max_pairs) {
+                           std::vector<int64_t> ag, int64_t ag_mc, const at::Tensor& state, int64_t rank,
+                       int64_t max_pairs) {
   check_rowmajor(D, "D");
   LF_CHECK(ws.scalar_type() == at::kFloat && ws.is_cuda() && D.scalar_type() == at::kBFloat16,
            "partials_allreduce_ll dtypes");
   const int M = D.size(0), N = D.size(1);
   LF_CHECK(ws.numel() >= splits * M * N, "partials_allreduce_ll workspace");
-  lf::ar::LLArgs ll = make_ll(rs, ag, state, rank, max_pairs);
+  lf::ar::LLArgs ll = make_ll(rs, ag, ag_mc, state, rank, max_pairs);
   c10::cuda::CUDAGuard g(D.device());
   lf::ar::finalize_ll(ws.data_ptr<float>(), (int)splits, M, N, reinterpret_cast<__nv_bfloat16*>(D.data_ptr()),
                       D.stride(0), ll, stream());
@@ -251,6 +254,13 @@ int64_t gemm_plan_splitk(int64_t M, int64_t N, int64_t K) {
 }
 
 int64_t gemm_choose_bn(int64_t M, int64_t N, int64_t epi) { return lf::gemm::choose_bn(M, N, epi); }
+
+// (cluster size, BN, k-blocks per CTA) of the cluster split-K plan; cluster size 0 = plain tiles.
+std::vector<int64_t> gemm_plan_cluster(int64_t M, int64_t N, int64_t K, int64_t epi) {
+  int bn = 0, kb = 0;
+  const int c = lf::gemm::plan_cluster(M, N, K, epi, &bn, &kb);
+  return {c, bn, kb};
+}
 
 void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) {
   LF_CHECK(ids.scalar_type() == at::kInt && table.scalar_type() == at::kBFloat16, "embed dtypes");
@@ -418,6 +428,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "D = A @ B^T on tcgen05 (epi 0 bf16, 1 fp32, 2 SwiGLU)", py::arg("A"), py::arg("B"),
         py::arg("D"), py::arg("epi") = 0, py::arg("bn") = 0, py::arg("ws") = py::none());
   m.def("gemm_plan_splitk", &gemm_plan_splitk);
+  m.def("gemm_plan_cluster", &gemm_plan_cluster);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_fp8", &gemm_fp8);

@@ -14,8 +14,9 @@
 //      and stores the partial into the inbox of the pair's owner rank (pairs
 //      are dealt to the ranks in contiguous chunks);
 //   2. the owner polls its inbox for the other ranks' partials, adds its own,
-//      writes the result and stores it (with the epoch) into every other
-//      rank's all-gather inbox;
+//      writes the result and stores it (with the epoch) into every rank's
+//      all-gather inbox (one multicast store through the NVSwitch, or one
+//      store per peer);
 //   3. every rank polls its all-gather inbox for the pairs it does not own.
 //
 // Inboxes are reused by consecutive operations without a barrier: a rank
@@ -39,6 +40,10 @@ namespace ar {
 
 __device__ __forceinline__ void st_word(uint2* p, uint32_t data, uint32_t ep) {
   asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(ep) : "memory");
+}
+
+__device__ __forceinline__ void st_word_mc(uint2* p, uint32_t data, uint32_t ep) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(ep) : "memory");
 }
 
 __device__ __forceinline__ uint2 ld_word(const uint2* p) {
@@ -130,8 +135,12 @@ __global__ void __launch_bounds__(256, 2) finalize_ll_kernel(const float* __rest
     }
     const uint32_t r = pack2(acc.x, acc.y);
     *out_word(p) = r;
-    for (int k = 0; k < a.world; ++k)
-      if (k != a.rank) st_word(a.ag[k] + p, r, ep);
+    if (a.ag_mc != nullptr) {
+      st_word_mc(a.ag_mc + p, r, ep);   // every rank's inbox, this one included
+    } else {
+      for (int k = 0; k < a.world; ++k)
+        if (k != a.rank) st_word(a.ag[k] + p, r, ep);
+    }
   }
   // 3. the pairs other ranks own
   for (int64_t p = first; p < P && ok; p += stride) {

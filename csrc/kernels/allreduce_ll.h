@@ -15,10 +15,13 @@ constexpr int kMaxRanks = 8;
 // no fence, no separate flag, no round trip.
 //   rs[r]  inbox of rank r for the reduce-scatter step: [world][chunk] words
 //   ag[r]  inbox of rank r for the all-gather step: [pairs] words
+//   ag_mc  NVLink multicast address of the all-gather inboxes (null when the
+//          fabric has none): one store reaches every rank
 //   state  this rank's (epoch, finished CTAs), in local memory
 struct LLArgs {
   uint2* rs[kMaxRanks];
   uint2* ag[kMaxRanks];
+  uint2* ag_mc;
   int* state;
   int rank;
   int world;

@@ -162,6 +162,121 @@ int plan_splitk(int M, int N, int K, int* kb_per_out) {
   return (num_kb + kb_per - 1) / kb_per;
 }
 
+// Cluster split-K (skinny decode GEMMs): one cluster of c CTAs per output
+// tile, the partial tiles summed through distributed shared memory.
+template <int BN, int STAGES, int OUT>
+static bool cluster_fits(int c, int clusters) {
+  using S = Smem<BN, STAGES>;
+  static int cached[9] = {0};
+  if (cached[c] == 0) {
+    auto kfn = gemm_cluster_splitk_kernel<BN, STAGES, OUT>;
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c * clusters, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = S::kTotal;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = c;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = -1;
+    }
+    cached[c] = n;
+  }
+  return cached[c] >= clusters;
+}
+
+template <int BN, int STAGES, int OUT>
+static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int64_t ldd, cudaStream_t stream) {
+  using S = Smem<BN, STAGES>;
+  auto kfn = gemm_cluster_splitk_kernel<BN, STAGES, OUT>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    attr_set = true;
+  }
+  CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
+  CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, BN);
+  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles * c, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = S::kTotal;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = c;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, out, a.M, a.N, a.K, (int)ldd, kb_per);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("lunaflux cluster gemm launch: ") + cudaGetErrorString(e));
+}
+
+// Plan: BN 256 when the 256-wide tiles times up to 8 splits reach half of
+// the SMs, else BN 128; as many splits (cluster size, <= 8) as one wave allows, with
+// at least two k-blocks per split; only when the plain tiles would leave more
+// than half of the SMs idle.  Returns the cluster size (0: no split).
+int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out) {
+  const int sms = num_sms();
+  const int num_m = (M + BM - 1) / BM;
+  const int num_kb = (K + BK - 1) / BK;
+  if (N % 128 != 0 || K % 8 != 0) return 0;
+  const int t256 = N % 256 == 0 ? num_m * (N / 256) : 0;
+  const int t128 = num_m * (N / 128);
+  if ((t256 ? t256 : t128) >= sms / 2) return 0;
+  // 256-wide tiles halve the activation bytes staged per weight byte; narrower
+  // tiles only when the 256-wide ones cannot reach half of the SMs
+  const int bn = (t256 && t256 * 8 >= sms / 2) ? 256 : 128;
+  const int tiles = bn == 256 ? t256 : t128;
+  int c = sms / tiles;
+  if (c > 8) c = 8;
+  if (c > num_kb / 2) c = num_kb / 2;
+  for (; c >= 2; --c) {
+    bool fits;
+    if (bn == 256) {
+      fits = epi == kSwiGLU ? cluster_fits<256, 4, kSwiGLU>(c, tiles)
+             : epi == kStoreF32 ? cluster_fits<256, 4, kStoreF32>(c, tiles)
+                                : cluster_fits<256, 4, kStoreBf16>(c, tiles);
+    } else {
+      fits = epi == kSwiGLU ? cluster_fits<128, 6, kSwiGLU>(c, tiles)
+             : epi == kStoreF32 ? cluster_fits<128, 6, kStoreF32>(c, tiles)
+                                : cluster_fits<128, 6, kStoreBf16>(c, tiles);
+    }
+    if (fits) break;
+  }
+  if (c < 2) return 0;
+  const int kb_per = (num_kb + c - 1) / c;
+  c = (num_kb + kb_per - 1) / kb_per;  // no empty slice
+  if (c < 2) return 0;
+  *bn_out = bn;
+  *kb_per_out = kb_per;
+  return c;
+}
+
+static bool run_cluster(const GemmArgs& a, int epi, void* out, int64_t ldd, cudaStream_t stream) {
+  int bn = 0, kb_per = 0;
+  const int c = plan_cluster(a.M, a.N, a.K, epi, &bn, &kb_per);
+  if (c < 2) return false;
+  if (bn == 256) {
+    if (epi == kSwiGLU) launch_cluster<256, 4, kSwiGLU>(a, c, kb_per, out, ldd, stream);
+    else if (epi == kStoreF32) launch_cluster<256, 4, kStoreF32>(a, c, kb_per, out, ldd, stream);
+    else launch_cluster<256, 4, kStoreBf16>(a, c, kb_per, out, ldd, stream);
+  } else {
+    if (epi == kSwiGLU) launch_cluster<128, 6, kSwiGLU>(a, c, kb_per, out, ldd, stream);
+    else if (epi == kStoreF32) launch_cluster<128, 6, kStoreF32>(a, c, kb_per, out, ldd, stream);
+    else launch_cluster<128, 6, kStoreBf16>(a, c, kb_per, out, ldd, stream);
+  }
+  return true;
+}
+
 // Tile-width choice: the widest BN that still yields enough tiles to cover
 // the SMs (wide tiles reuse A best; narrow tiles spread a skinny decode GEMM
 // over more SMs so the weight stream uses all of HBM).
@@ -183,19 +298,9 @@ int choose_bn(int M, int N, int epi) {
 
 void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws, int64_t ws_elems) {
   if (a.M <= 0) return;
-  if (ws != nullptr && bn == 0 && (a.N % 256) == 0) {
-    int kb_per = 0;
-    const int splits = plan_splitk(a.M, a.N, a.K, &kb_per);
-    if (splits > 1 && (int64_t)splits * a.M * a.N <= ws_elems) {
-      if (a.K % 8 != 0) throw std::runtime_error("lunaflux gemm: K must be a multiple of 8");
-      launch<256, 4, kSplitF32>(a, stream, splits, kb_per, ws);
-      dim3 grid((a.N + 1023) / 1024, a.M);
-      if (epi == kSwiGLU) splitk_finalize_kernel<kSwiGLU><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd, splits);
-      else if (epi == kStoreF32) splitk_finalize_kernel<kStoreF32><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd, splits);
-      else splitk_finalize_kernel<kStoreBf16><<<grid, 256, 0, stream>>>(ws, a.D, a.M, a.N, a.ldd, splits);
-      return;
-    }
-  }
+  (void)ws;
+  (void)ws_elems;
+  if (bn == 0 && run_cluster(a, epi, a.D, a.ldd, stream)) return;
   if (bn == 0) bn = choose_bn(a.M, a.N, epi);
   if (bn == 0 || a.N % bn != 0) throw std::runtime_error("lunaflux gemm: N must be a multiple of 32");
   if (a.K % 8 != 0) throw std::runtime_error("lunaflux gemm: K must be a multiple of 8");
@@ -264,15 +369,10 @@ void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, flo
 void run_allreduce_ll(const GemmArgs& a, const ar::LLArgs& ll, cudaStream_t stream, float* ws, int64_t ws_elems) {
   if (a.M <= 0) return;
   if (a.N % 256 != 0 || a.K % 8 != 0) throw std::runtime_error("lunaflux gemm_allreduce_ll: N % 256 and K % 8 required");
-  int kb_per = 0;
-  int splits = plan_splitk(a.M, a.N, a.K, &kb_per);
-  if (splits < 1 || (int64_t)splits * a.M * a.N > ws_elems) {
-    splits = 1;
-    kb_per = 0;
-  }
   if ((int64_t)a.M * a.N > ws_elems) throw std::runtime_error("lunaflux gemm_allreduce_ll: workspace too small");
-  launch<256, 4, kSplitF32>(a, stream, splits, kb_per, ws);
-  ar::finalize_ll(ws, splits, a.M, a.N, reinterpret_cast<__nv_bfloat16*>(a.D), a.ldd, ll, stream);
+  // this rank's fp32 partial [M, N] in ws (cluster split-K when it pays), then the all-reduce
+  run(GemmArgs{a.A, a.B, ws, a.M, a.N, a.K, a.lda, a.ldb, a.N}, kStoreF32, 0, stream);
+  ar::finalize_ll(ws, 1, a.M, a.N, reinterpret_cast<__nv_bfloat16*>(a.D), a.ldd, ll, stream);
 }
 
 // Grouped GEMM (mixture-of-experts): A [M_max, K] rows in expert segments

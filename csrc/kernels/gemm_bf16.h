@@ -19,12 +19,14 @@ struct GemmArgs {
 
 // epi: 0 = bf16 store, 1 = fp32 store, 2 = SwiGLU (gate/up rows interleaved in
 // groups of 64: 32 gate rows then the matching 32 up rows).  bn = 0 picks a tile width from the shape.
-// ws: optional fp32 scratch of ws_elems floats; when given and the GEMM is
-// too skinny to fill the SMs, the K dimension is split, each split writes its
-// own [M, N] slab of ws and a finalize kernel sums the slabs in split order
-// (deterministic; needs splits * M * N <= ws_elems, else no split).
+// Skinny shapes (the plain tiles would leave more than half of the SMs idle)
+// run as cluster split-K: one thread-block cluster per output tile, partial
+// tiles summed through distributed shared memory, deterministic.  ws is
+// accepted for interface stability and unused.
 void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws = nullptr, int64_t ws_elems = 0);
 int plan_splitk(int M, int N, int K, int* kb_per_out);
+// Cluster split-K plan: returns the cluster size (0 = plain tiles) and its BN / k-blocks per CTA.
+int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out);
 
 // Peer view of one tensor-parallel group for the fused GEMM + all-reduce.
 // Two symmetric bf16 regions of [rows, N] (every rank holds both, same size):

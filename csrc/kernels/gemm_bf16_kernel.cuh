@@ -401,6 +401,221 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Cluster split-K for skinny (decode) GEMMs.  One thread-block cluster of c
+// CTAs per output tile, CTA r of the cluster computes K slice r into its own
+// TMEM accumulator; the partial tiles are then summed through distributed
+// shared memory (each CTA owns 1/c of the tile's rows and reads that band of
+// every peer's partial, in cluster-rank order, so the result is
+// deterministic) and written once, in the final format.  No fp32 workspace
+// round trip through HBM and no second kernel.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+template <int BN>
+struct ClusterRed {
+  static constexpr int kStride = BN + 4;  // fp32 row stride of the partial tile (bank spread)
+  static constexpr int kBytes = BM * kStride * 4;
+};
+
+// OUT: kStoreBf16, kStoreF32 or kSwiGLU (interleaved gate/up groups of 32).
+template <int BN, int STAGES, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_cluster_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                               const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M, int N,
+                               int K, int ldd, int kb_per_split) {
+  using S = Smem<BN, STAGES>;
+  static_assert(ClusterRed<BN>::kBytes <= STAGES * S::kStageBytes, "partial tile must fit the pipeline buffers");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull_bar + 1);
+  float* red = reinterpret_cast<float*>(smem);  // the partial tile, once the pipeline has drained
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int c = (int)cluster_nctarank();
+  const int r = (int)cluster_ctarank();
+  const int num_m = (M + BM - 1) / BM;
+  const int tile = blockIdx.x / c;
+  const int m0 = (tile % num_m) * BM;
+  const int n0 = (tile / num_m) * BN;
+  const int num_kb = (K + BK - 1) / BK;
+  const int kb0 = r * kb_per_split;
+  const int kb1 = min(num_kb, kb0 + kb_per_split);
+  constexpr uint32_t kCols = BN < 32 ? 32 : BN;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&full_bar[st], 1);
+      mbar_init(&empty_bar[st], 1);
+    }
+    mbar_init(tfull_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_b = l2_policy_evict_first();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1, 11)) break;
+        uint8_t* sa = smem + stage * S::kStageBytes;
+        uint8_t* sb = sa + S::kABytes;
+        mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
+        tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, m0);
+        tma_load_2d_hint(sb, &tmap_b, &full_bar[stage], kb * BK, n0, pol_b);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, 12)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
+        const uint32_t sb = sa + S::kABytes;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          umma_f16_ss(tmem_base, sw128_kmajor_desc(sa + kk * 32), sw128_kmajor_desc(sb + kk * 32), idesc,
+                      (kb > kb0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty_bar[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      // commit also when the slice was empty or a wait failed, so the
+      // epilogue never waits for nothing (it then writes zeros)
+      if (ok) umma_commit(tfull_bar);
+      else mbar_arrive(tfull_bar);
+    }
+  } else {
+    // TMEM -> this CTA's fp32 partial tile in shared memory (row = TMEM lane)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const bool have = kb1 > kb0;
+    if (mbar_wait(tfull_bar, 0, 13)) {
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16);
+      float* dst = red + row * ClusterRed<BN>::kStride;
+#pragma unroll 1
+      for (int col = 0; col < BN; col += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + col, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float4 f = have ? make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                        __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(dst + col + 4 * j) = f;
+        }
+      }
+    }
+  }
+  // every CTA's partial tile is in its shared memory
+  cluster_sync_all();
+  if (warp >= 2) {
+    const int t = threadIdx.x - 64;
+    const int rows_per = (BM + c - 1) / c;
+    const int r0 = r * rows_per;
+    const int r1 = min(BM, r0 + rows_per);
+    const uint32_t red_base = smem_u32(red);
+    if constexpr (OUT == kSwiGLU) {
+      // thread -> (row, 4 consecutive output features): gate cols g*64 + j,
+      // up cols g*64 + 32 + j of the tile
+      constexpr int kQuads = BN / 2 / 4;
+      for (int i = t; i < (r1 - r0) * kQuads; i += 128) {
+        const int rl = r0 + i / kQuads;
+        const int j = (i % kQuads) * 4;            // output feature within the tile
+        const int gcol = (j / 32) * 64 + (j % 32);
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+        const uint32_t off_g = red_base + (uint32_t)(rl * ClusterRed<BN>::kStride + gcol) * 4;
+        for (int q = 0; q < c; ++q) {
+          const float4 a = ld_shared_cluster_f4(mapa_shared(off_g, q));
+          const float4 b = ld_shared_cluster_f4(mapa_shared(off_g + 32 * 4, q));
+          g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
+          u.x += b.x; u.y += b.y; u.z += b.z; u.w += b.w;
+        }
+        const int grow = m0 + rl;
+        if (grow < M) {
+          __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)grow * ldd + n0 / 2 + j;
+          *reinterpret_cast<uint2*>(d) =
+              make_uint2(pack_bf16x2(silu(g.x) * u.x, silu(g.y) * u.y), pack_bf16x2(silu(g.z) * u.z, silu(g.w) * u.w));
+        }
+      }
+    } else {
+      constexpr int kQuads = BN / 4;
+      for (int i = t; i < (r1 - r0) * kQuads; i += 128) {
+        const int rl = r0 + i / kQuads;
+        const int col = (i % kQuads) * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        const uint32_t off = red_base + (uint32_t)(rl * ClusterRed<BN>::kStride + col) * 4;
+        for (int q = 0; q < c; ++q) {
+          const float4 a = ld_shared_cluster_f4(mapa_shared(off, q));
+          acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+        }
+        const int grow = m0 + rl;
+        if (grow < M) {
+          if constexpr (OUT == kStoreF32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)grow * ldd + n0 + col) = acc;
+          } else {
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)grow * ldd + n0 + col) =
+                make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+          }
+        }
+      }
+    }
+  }
+  // no CTA leaves (and releases its shared memory) while a peer still reads it
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kCols);
+  }
+}
+
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -37,14 +37,7 @@ class KernelOps:
         M, N, K = A.shape[0], B.shape[0], A.shape[1]
         if M == 0:
             return
-        if ws is not None:
-            key = (M, N, K)
-            s = self._splitk.get(key)
-            if s is None:
-                s = self._splitk[key] = self.C.gemm_plan_splitk(M, N, K)
-            self.launches += 2 if (s > 1 and s * M * N <= ws.numel() and N % 256 == 0) else 1
-        else:
-            self.launches += 1
+        self.launches += 1   # plain tiles or cluster split-K: one kernel either way
         self.C.gemm(A, B, out, epi, 0, ws)
 
     def rope_kv_write(self, qkv, positions, slots, cos_sin, kc, vc, Hq, Hkv, page):

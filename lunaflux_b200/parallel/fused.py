@@ -101,13 +101,16 @@ class FusedTPComm(TPComm):
         dist.barrier(group=g)
         self.ll_rs = list(hl.buffer_ptrs)
         self.ll_ag = [p + rs_words * 8 for p in hl.buffer_ptrs]
+        self.ll_ag_mc = (hl.multicast_ptr + rs_words * 8) if (self.multicast and getattr(hl, "multicast_ptr", 0)) else 0
         self.ll_state = torch.zeros(2, dtype=torch.int32, device=device)
         self.ll_out = torch.empty(max(self.ll_rows, 1), hidden, dtype=torch.bfloat16, device=device)
         # Prefill rows: the tile path overlaps each tile's reduction with the
-        # next tiles' math, which pays off when a rank's K share is large
-        # (Llama-3-8B down at TP=2, K=7168: 1.17x over GEMM -> NCCL) and not
-        # when it is small (o_proj at TP=2, K=2048: 0.83x); below tile_min_k
-        # the GEMM is followed by the library all-reduce.
+        # next tiles' math.  At TP=2 that pays off when a rank's K share is
+        # large (Llama-3-8B down, K=7168: 1.17x over GEMM -> NCCL) and not when
+        # it is small (o_proj, K=2048: 0.83x), so below tile_min_k the GEMM is
+        # followed by the library all-reduce; at TP=8 the library all-reduce
+        # is slower and the tile path wins at every K (o_proj K=512: 1.39x,
+        # down K=1792: 1.54x).
         if tile_min_k is None:
             tile_min_k = int(os.environ.get("LUNAFLUX_FUSED_TILE_MIN_K", "4096"))
         self.tile_min_k = tile_min_k
@@ -141,9 +144,9 @@ class FusedTPComm(TPComm):
         if M <= self.ll_rows and ws is not None:
             out = self.ll_out[:M]
             self.calls += 1
-            self.C.gemm_allreduce_ll(A, B, out, ws, self.ll_rs, self.ll_ag, self.ll_state, self.rank, self.ll_pairs)
+            self.C.gemm_allreduce_ll(A, B, out, ws, self.ll_rs, self.ll_ag, self.ll_ag_mc, self.ll_state, self.rank, self.ll_pairs)
             return out
-        if A.shape[1] < self.tile_min_k:
+        if self.world <= 2 and A.shape[1] < self.tile_min_k:
             # too little math per tile to hide the tile's reduction behind:
             # the GEMM, then the library all-reduce (measured faster here)
             out = self.lib_out[:M]
@@ -162,7 +165,7 @@ class FusedTPComm(TPComm):
         if M <= self.ll_rows:
             out = self.ll_out[:M]
             self.calls += 1
-            self.C.partials_allreduce_ll(part, 1, out, self.ll_rs, self.ll_ag, self.ll_state, self.rank, self.ll_pairs)
+            self.C.partials_allreduce_ll(part, 1, out, self.ll_rs, self.ll_ag, self.ll_ag_mc, self.ll_state, self.rank, self.ll_pairs)
             return out
         s = self._slot()
         self.C.partials_allreduce(part, M, N, 1, *self._args(s))

@@ -61,6 +61,31 @@ def test_gemm_splitk(C, M, N, K, epi):
     assert C.gemm_plan_splitk(M, N, K) >= 1
 
 
+@pytest.mark.parametrize("M,N,K,epi", [(256, 6144, 4096, 0), (256, 4096, 14336, 0), (256, 768, 4096, 0),
+                                       (256, 4096, 512, 1), (64, 3584, 4096, 2), (1, 4096, 1792, 1),
+                                       (129, 1024, 4096, 2)])
+def test_gemm_cluster_splitk(C, M, N, K, epi):
+    """Decode shapes that take the cluster split-K path: values against the fp32
+    reference, bitwise reproducibility, and the plan itself."""
+    c, bn, kb = C.gemm_plan_cluster(M, N, K, epi)
+    assert c >= 2, (c, bn, kb)
+    assert (c - 1) * kb < (K + 63) // 64 <= c * kb
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    out_cols = N // 2 if epi == 2 else N
+    D = torch.empty(M, out_cols, device="cuda", dtype=torch.float32 if epi == 1 else torch.bfloat16)
+    ref = A.float() @ B.float().t()
+    if epi == 2:
+        v = ref.view(M, N // 64, 2, 32)
+        ref = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(M, N // 2)
+    C.gemm(A, B, D, epi, 0, None)
+    first = D.clone()
+    C.gemm(A, B, D, epi, 0, None)
+    assert torch.equal(first, D)
+    _close(D, ref, 3e-2, 3e-2, f"cluster split-K {M}x{N}x{K} epi={epi}")
+    assert C.read_error(True)[0] == 0
+
+
 def test_gemm_strided_a(C):
     A_full = torch.randn(64, 3 * 256, device="cuda").bfloat16()
     A = A_full[:, 256:512]
