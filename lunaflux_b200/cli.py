@@ -209,7 +209,7 @@ def serve(args: List[str]):
     from .models import spec as specs
     from .models.weights import build_runtime, random_source
     from .ops import KernelOps, TorchOps
-    from .service.server import EngineService, TCPServer
+    from .service.server import EngineService, MetricsServer, TCPServer
     from .tokenizer.bpe import Tokenizer, synthetic_byte_tokenizer
     ap = argparse.ArgumentParser(prog="lunaflux serve")
     ap.add_argument("--config", default="")
@@ -219,6 +219,7 @@ def serve(args: List[str]):
     ap.add_argument("--port", type=int, default=7841)
     ap.add_argument("--tokenizer", default="")
     ap.add_argument("--max-context", type=int, default=4096)
+    ap.add_argument("--metrics-port", type=int, default=-1, help="HTTP /metrics and /health (-1: off, 0: any)")
     a = ap.parse_args(args)
     sched, cache = SchedulerConfig(), CacheConfig()
     preset = a.preset
@@ -246,6 +247,9 @@ def serve(args: List[str]):
         srv = TCPServer(svc, a.host, a.port)
         port = await srv.start()
         print(f"lunaflux serving {preset} on {a.host}:{port}", flush=True)
+        if a.metrics_port >= 0:
+            ms = MetricsServer(svc, a.host, a.metrics_port)
+            print(f"lunaflux metrics on http://{a.host}:{await ms.start()}/metrics", flush=True)
         await srv.serve_forever()
 
     try:

@@ -22,6 +22,7 @@ from ..config import CacheConfig, SchedulerConfig
 from ..contracts import (CompletedEvent, FailedEvent, FinishReason, GenerateRequest, PublicErrorCode,
                          SamplingParameters, TokenEvent, Usage)
 from ..kv.layout import kv_bytes_per_page
+from ..metrics import EngineMetrics
 from ..models.spec import LlamaSpec
 from ..models.weights import ModelWeights
 from ..prefix.radix import PrefixIdentity
@@ -82,6 +83,7 @@ class LLMEngine:
         self.live: Dict[int, Request] = {}
         self._next_rid = 1
         self.listeners: List[Callable] = []
+        self.metrics = EngineMetrics()
 
     def _pages_from_memory(self, weights, cache, sched, opts) -> int:
         per_page = kv_bytes_per_page(self.spec, weights.shard.kv_heads, cache.tokens_per_page,
@@ -109,6 +111,7 @@ class LLMEngine:
                       cache_enabled=use_prefix_cache, arrival=arrival if arrival is not None else now)
         self.scheduler.add_request(req)
         self.live[rid] = req
+        self.metrics.requests.inc()
         return rid
 
     def submit(self, g: GenerateRequest) -> int:
@@ -128,10 +131,16 @@ class LLMEngine:
 
     # ------------------------------------------------------------------ loop
     def step(self) -> List[TokenOutput]:
+        t0 = self.clock()
         plan = self.scheduler.schedule()
         if plan is None:
             self._drain_terminals()
             return []
+        m = self.metrics
+        for r in plan.rows:
+            if not r.decode and r.start == r.req.cached_tokens:
+                m.queue.observe(t0 - r.req.arrival)        # first step of this request
+        graphs_before = len(self.runner.graphs)
         try:
             sampled = self.runner.execute(plan, self.scheduler.tables.matrix)
         except StepFailed:
@@ -143,6 +152,22 @@ class LLMEngine:
         for cb in self.listeners:
             cb(outs)
         self._drain_terminals()
+        t1 = self.clock()
+        kind = "prefill" if plan.prefill_rows else "decode"
+        m.step_time.observe(t1 - t0, kind=kind)
+        m.step_tokens.observe(plan.num_tokens)
+        m.step_rows.observe(len(plan.rows))
+        m.graph.inc(mode="captured" if self.runner.last_bucket is not None else "eager")
+        if len(self.runner.graphs) > graphs_before:
+            m.graph_capture.observe(self.runner.last_capture_s)
+        if outs:
+            m.output_tokens.inc(len(outs))
+            if m._last_emit is not None:
+                m.itl.observe(t1 - m._last_emit)
+            m._last_emit = t1
+        a = self.scheduler.allocator
+        m.kv_pages.set(a.free_page_count(), state="free")
+        m.kv_pages.set(a.allocated_page_count(), state="allocated")
         return outs
 
     def _drain_terminals(self):
@@ -150,9 +175,20 @@ class LLMEngine:
             req = self.live.pop(t.rid, None)
             if req is None:
                 continue
-            self.results[t.rid] = RequestResult(req.rid, len(req.prompt), list(req.output), t.reason, t.error,
-                                                req.arrival, req.first_token_time, req.finish_time,
-                                                req.cached_tokens)
+            res = self.results[t.rid] = RequestResult(req.rid, len(req.prompt), list(req.output), t.reason, t.error,
+                                                      req.arrival, req.first_token_time, req.finish_time,
+                                                      req.cached_tokens)
+            m = self.metrics
+            if t.error is not None:
+                m.failed.inc(code=t.error.name.lower())
+            else:
+                m.finished.inc(reason=t.reason.name.lower() if t.reason is not None else "none")
+            m.prompt_tokens.inc(res.prompt_len)
+            m.cached_tokens.inc(res.cached_tokens)
+            if res.ttft is not None:
+                m.ttft.observe(res.ttft)
+            if res.tpot is not None:
+                m.tpot.observe(res.tpot)
 
     def run_until_done(self, max_steps: int = 1 << 30):
         n = 0

@@ -13,6 +13,7 @@ the device and only the sampled int32 ids come back to the host.
 from __future__ import annotations
 
 import math
+import time
 from typing import Dict, List, Optional, Sequence
 
 import numpy as np
@@ -104,6 +105,8 @@ class ModelRunner:
         self.graph_sizes = sorted(b for b in graph_sizes if b <= R)
         self.stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
         self.steps = 0
+        self.last_bucket: Optional[int] = None      # graph bucket of the last step (None: eager)
+        self.last_capture_s = 0.0
         # accounting for the bench
         self.h2d_bytes = 0
         self.d2h_bytes = 0
@@ -281,7 +284,19 @@ class ModelRunner:
         self.h2d_bytes += n * 4
 
     def execute(self, plan: StepPlan, table_matrix: np.ndarray) -> np.ndarray:
-        """Runs one step and returns the sampled token ids (sampling rows, plan order)."""
+        """Runs one step and returns the sampled token ids (sampling rows, plan
+        order).  On CUDA the step is one NVTX range (visible to Nsight tools),
+        named by its kind and size."""
+        if self.device.type != "cuda":
+            return self._execute(plan, table_matrix)
+        kind = "decode" if all(r.decode for r in plan.rows) else "mixed"
+        torch.cuda.nvtx.range_push(f"lunaflux.step.{kind} rows={len(plan.rows)} tokens={plan.num_tokens}")
+        try:
+            return self._execute(plan, table_matrix)
+        finally:
+            torch.cuda.nvtx.range_pop()
+
+    def _execute(self, plan: StepPlan, table_matrix: np.ndarray) -> np.ndarray:
         rows = plan.rows
         decode_only = all(r.decode for r in rows)
         stoch = any(r.sample and r.req.sampling.mode.value == 1 for r in rows)
@@ -289,6 +304,7 @@ class ModelRunner:
         if decode_only and self.graph_sizes and self.device.type == "cuda":
             nd = len(rows)
             bucket = next((b for b in self.graph_sizes if b >= nd), None)
+        self.last_bucket = bucket
         slot = self._flip
         self._flip ^= 1
         if self.in_evt[slot] is not None:
@@ -301,7 +317,9 @@ class ModelRunner:
             key = (bucket, stoch)
             g = self.graphs.get(key)
             if g is None:
+                t0 = time.perf_counter()
                 g = self.capture(bucket, stoch)
+                self.last_capture_s = time.perf_counter() - t0
             self._upload(hs, host_buf)
             self._record_upload(slot)
             self._begin_step()

@@ -64,6 +64,10 @@ class EngineService:
     def start(self):
         self._thread.start()
 
+    def alive(self) -> bool:
+        """The engine loop runs and has not failed."""
+        return self._thread.is_alive() and not self.failed and not self._stop
+
     def stop(self):
         with self._cv:
             self._stop = True
@@ -257,3 +261,48 @@ class TCPServer:
     def close(self):
         if self.server is not None:
             self.server.close()
+
+
+class MetricsServer:
+    """Minimal HTTP endpoint for the engine's metrics: ``GET /metrics``
+    (Prometheus text) and ``GET /health`` (200 while the engine loop runs,
+    503 otherwise).  Read-only, no request payloads, one response per
+    connection."""
+
+    def __init__(self, service: EngineService, host: str = "127.0.0.1", port: int = 0):
+        self.service = service
+        self.host = host
+        self.port = port
+        self.server: Optional[asyncio.AbstractServer] = None
+
+    async def start(self):
+        self.server = await asyncio.start_server(self._client, self.host, self.port)
+        self.port = self.server.sockets[0].getsockname()[1]
+        return self.port
+
+    async def _client(self, reader: asyncio.StreamReader, writer: asyncio.StreamWriter):
+        try:
+            line = await asyncio.wait_for(reader.readline(), 5.0)
+            parts = line.decode("latin-1").split()
+            path = parts[1] if len(parts) >= 2 and parts[0] == "GET" else ""
+            if path == "/metrics":
+                body = self.service.engine.metrics.registry.render_prometheus().encode()
+                status = "200 OK"
+            elif path == "/health":
+                alive = self.service.alive()
+                body = b"ok\n" if alive else b"unavailable\n"
+                status = "200 OK" if alive else "503 Service Unavailable"
+            else:
+                body, status = b"not found\n", "404 Not Found"
+            writer.write(f"HTTP/1.1 {status}\r\nContent-Type: text/plain; version=0.0.4\r\n"
+                         f"Content-Length: {len(body)}\r\nConnection: close\r\n\r\n".encode() + body)
+            await writer.drain()
+        except (asyncio.TimeoutError, ConnectionError, OSError):
+            pass
+        finally:
+            writer.close()
+
+    async def stop(self):
+        if self.server is not None:
+            self.server.close()
+            await self.server.wait_closed()

@@ -125,7 +125,7 @@ def test_tcp_end_to_end():
     from lunaflux_b200.ops.torch_ops import TorchOps
     from lunaflux_b200.oracle.reference import ReferenceModel
     from lunaflux_b200.service.framed_wire import EVENT_HEADER
-    from lunaflux_b200.service.server import EngineService, TCPServer
+    from lunaflux_b200.service.server import EngineService, MetricsServer, TCPServer
     from lunaflux_b200.tokenizer.bpe import synthetic_byte_tokenizer
 
     spec = tiny_llama()
@@ -166,12 +166,26 @@ def test_tcp_end_to_end():
             client(GenerateRequest(2, input_text=b"hi there", max_new_tokens=4)),
             client(GenerateRequest(3, input_tokens=(1,), max_new_tokens=4, model_plan_digest="f" * 64)))
         server.close()
-        return a, b, c
+        # the metrics endpoint: Prometheus text and the health probe
+        ms = MetricsServer(svc)
+        mp = await ms.start()
+        texts = []
+        for path in ("/metrics", "/health", "/nope"):
+            r, w = await asyncio.open_connection("127.0.0.1", mp)
+            w.write(f"GET {path} HTTP/1.1\r\nHost: x\r\n\r\n".encode())
+            await w.drain()
+            texts.append((await r.read()).decode())
+            w.close()
+        await ms.stop()
+        return a, b, c, texts
 
     try:
-        a, b, c = asyncio.run(main())
+        a, b, c, texts = asyncio.run(main())
     finally:
         svc.stop()
+    assert texts[0].startswith("HTTP/1.1 200") and "lunaflux_output_tokens_total" in texts[0]
+    assert "lunaflux_ttft_seconds_count 2" in texts[0]
+    assert texts[1].startswith("HTTP/1.1 200") and texts[2].startswith("HTTP/1.1 404")
     assert isinstance(a[0], AcceptedWire)
     toks = [e.token_id for e in a if isinstance(e, TokenEvent)]
     assert toks == expect
