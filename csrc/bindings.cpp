@@ -14,6 +14,12 @@
 #include "kernels/moe.h"
 #include "kernels/runtime.h"
 
+namespace lf {
+namespace rt {
+pybind11::dict device_report();
+}
+}  // namespace lf
+
 namespace {
 
 #define LF_CHECK(cond, msg) TORCH_CHECK(cond, "lunaflux: ", msg)
@@ -428,6 +434,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "D = A @ B^T on tcgen05 (epi 0 bf16, 1 fp32, 2 SwiGLU)", py::arg("A"), py::arg("B"),
         py::arg("D"), py::arg("epi") = 0, py::arg("bn") = 0, py::arg("ws") = py::none());
   m.def("gemm_plan_splitk", &gemm_plan_splitk);
+  m.def("device_report", &lf::rt::device_report, "devices, compute capability, peer access, NVLink multicast, typed status");
   m.def("gemm_plan_cluster", &gemm_plan_cluster);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_grouped", &gemm_grouped);

@@ -90,6 +90,15 @@ def doctor(out=print) -> bool:
     except RuntimeError as e:
         out(f"native kernels: unavailable; {e}")
         ready = False
+    try:
+        from .runtime.device import probe
+        rep = probe()
+        out(f"device runtime: {rep.status.value} (driver {rep.driver_version}, runtime {rep.runtime_version})")
+        for d in rep.devices:
+            out(f"  device {d.index}: {d.status.value}, NVLink multicast "
+                f"{'yes' if d.multicast else 'no' if d.multicast is not None else 'unknown'}")
+    except Exception as e:  # the probe itself must never stop the report
+        out(f"device runtime: probe failed ({e})")
     if not torch.cuda.is_available():
         out("CUDA device probe: unavailable; no devices")
         ready = False
@@ -190,7 +199,12 @@ def inspect_kernels(out=print):
     out("LunaFlux kernels")
     out("arch: sm_100a (B200)")
     out(f"module: {os.path.basename(C.__file__)} sha256 {h}")
+    from .ops.registry import manifest
+    out("ops:")
+    for line in manifest(C):
+        out(f"  {line}")
     names = sorted(n for n in dir(C) if not n.startswith("_"))
+    out("entry points:")
     for n in names:
         out(f"  {n}")
     out('  lf_gemm_bf16_noalloc (extern "C")')

@@ -27,7 +27,7 @@ from ..models.spec import LlamaSpec
 from ..models.weights import ModelWeights
 from ..prefix.radix import PrefixIdentity
 from ..scheduler.scheduler import Request, Scheduler, StepPlan, TokenOutput
-from .runner import ModelRunner, StepFailed
+from .runner import ModelRunner, StepFailed  # noqa: F401  (re-exported)
 
 
 @dataclasses.dataclass
@@ -143,7 +143,9 @@ class LLMEngine:
         graphs_before = len(self.runner.graphs)
         try:
             sampled = self.runner.execute(plan, self.scheduler.tables.matrix)
-        except StepFailed:
+        except Exception:
+            # a device error word, or a launch that raised: the step's work is
+            # void; active requests fail (retryably), waiting ones stay queued
             self.scheduler.abort_plan(plan)
             self.scheduler.fail_active(PublicErrorCode.INTERNAL)
             self._drain_terminals()

@@ -21,6 +21,8 @@ class KernelOps:
 
     def __init__(self):
         self.C = _ext.load()
+        from .registry import validate
+        validate(self.C)   # every op has its compiled entry point, or startup fails
         self.launches = 0
         self.num_sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
         self._splitk = {}

@@ -28,6 +28,8 @@ cuda_sources = [
 ]
 cuda_sources += [os.path.join("csrc/kernels", f) for f in sorted(os.listdir(os.path.join(CSRC, "kernels")))
                  if f.endswith(".cu") and os.path.join("csrc/kernels", f) not in cuda_sources]
+cuda_sources += [os.path.join("csrc/runtime", f) for f in sorted(os.listdir(os.path.join(CSRC, "runtime")))
+                 if f.endswith(".cpp")] if os.path.isdir(os.path.join(CSRC, "runtime")) else []
 
 _host_dir = os.path.join(CSRC, "host")
 host_sources = sorted(os.path.join("csrc/host", f) for f in os.listdir(_host_dir)

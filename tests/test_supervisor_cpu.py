@@ -1,6 +1,7 @@
 """Supervised rank processes on CPU (gloo): lock-step serving, and recovery
-from a rank that dies or stops answering.  Failures are made on the host: a
-rank process exits, or stops itself (SIGSTOP) so its heartbeats cease."""
+from a rank that dies, stops answering, or whose device fails.  Failures are
+made on the host: a rank process exits, stops itself (SIGSTOP) so its
+heartbeats cease, or runs on the fake device whose kernel launch raises."""
 import os
 import signal
 
@@ -54,7 +55,12 @@ def tiny_factory(rank, world):
     spec = _spec()
     ck = random_checkpoint(spec, 0)
     w = build_runtime(spec, lambda n: ck[n], TPShard(rank, world, spec))
-    eng = LLMEngine(w, TorchOps(), "cpu", SchedulerConfig(step_token_budget=64, max_active_requests=4,
+    ops = TorchOps()
+    if os.environ.get("LF_TEST_FAULT") == "device" and rank == 1 and os.environ.get("LUNAFLUX_GENERATION") == "1":
+        # a kernel launch that fails on the fake device in the third forward
+        from lunaflux_b200.testing import FakeDeviceOps, FaultPlan
+        ops = FakeDeviceOps(FaultPlan(at_forward=3, kind="launch_error"))
+    eng = LLMEngine(w, ops, "cpu", SchedulerConfig(step_token_budget=64, max_active_requests=4,
                                                           prefill_chunk_tokens=64, emergency_decode_page_reserve=1),
                     CacheConfig(), EngineOptions(max_context=256, num_pages=64, graph_sizes=()), comm=TPComm())
     return _FaultyEngine(eng, rank)
@@ -70,7 +76,7 @@ def _expect(prompts, n):
 PROMPTS = [[5, 6, 7], [9, 10, 11, 12, 13], [1, 2, 3, 4], [200, 100]]
 
 
-@pytest.mark.parametrize("fault", ["", "exit", "stop"])
+@pytest.mark.parametrize("fault", ["", "exit", "stop", "device"])
 def test_supervised_tp_ranks(fault, monkeypatch):
     monkeypatch.setenv("LF_TEST_FAULT", fault)
     sup = Supervisor(2, tiny_factory, heartbeat_s=0.1, dead_after_s=2.0, step_timeout_s=60.0)
