@@ -121,9 +121,9 @@ class RunStats:
                 "iterations": self.iterations}
 
 
-def run(engine, wl: Workload, comm=None, realtime: bool = True) -> RunStats:
+def run(engine, wl: Workload, comm=None, realtime: bool = True, clock=time.perf_counter) -> RunStats:
     """Feeds a workload through ``engine`` and returns per-request statistics.
-    Requests with arrival > 0 are admitted when wall time reaches them
+    Requests with arrival > 0 are admitted when ``clock`` reaches them
     (rank 0's clock, broadcast); cancellations happen after the given number
     of produced tokens."""
     import torch.distributed as dist
@@ -134,7 +134,7 @@ def run(engine, wl: Workload, comm=None, realtime: bool = True) -> RunStats:
     rid_of = {}
     produced: Dict[int, int] = {}
     cancel_at: Dict[int, int] = {}
-    t0 = time.perf_counter()
+    t0 = clock()
     nxt = 0
     iters = 0
     prompt_tokens = 0
@@ -154,7 +154,7 @@ def run(engine, wl: Workload, comm=None, realtime: bool = True) -> RunStats:
             nxt += 1
 
     while nxt < len(pending) or engine.has_work():
-        now = time.perf_counter() - t0
+        now = clock() - t0
         n = nxt
         while n < len(pending) and (not realtime or wl.items[pending[n]].arrival <= now):
             n += 1
@@ -175,7 +175,7 @@ def run(engine, wl: Workload, comm=None, realtime: bool = True) -> RunStats:
             if c is not None and produced[o.rid] >= c and not o.finished:
                 engine.cancel(o.rid)
                 cancel_at.pop(o.rid)
-    wall = time.perf_counter() - t0
+    wall = clock() - t0
     ttft, tpot = [], []
     toks = good = fin = canc = 0
     for rid, res in engine.results.items():

@@ -39,7 +39,10 @@ def test_driver_with_arrivals_cancels_and_prefix_hits():
     shared = rng.integers(0, 256, 48, dtype=np.int32)
     items = [W.WorkItem(np.concatenate([shared, rng.integers(0, 256, 5, dtype=np.int32)]), 6, SamplingParameters(),
                         arrival=0.01 * i, cancel_after=3 if i == 2 else None) for i in range(6)]
-    st = W.run(eng, W.Workload("t", "tiny", items, prefix_cache=True))
+    ticks = iter(range(1 << 30))
+    # a clock that advances 5 ms per reading: arrivals interleave with steps
+    # the same way on a loaded machine as on an idle one
+    st = W.run(eng, W.Workload("t", "tiny", items, prefix_cache=True), clock=lambda: 0.005 * next(ticks))
     s = st.summary()
     assert s["cancelled"] == 1 and s["finished"] == 5
     assert st.tokens == 5 * 6 + 3
