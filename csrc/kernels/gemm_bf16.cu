@@ -120,11 +120,11 @@ static int num_sms() {
   return n;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, int MB = 1>
 static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int kb_per = 0, float* ws = nullptr,
                    const ArArgs& ar = ArArgs{}) {
-  using S = Smem<BN, STAGES>;
-  auto kfn = gemm_bf16_kernel<BN, STAGES, EPI>;
+  using S = Smem<BN, STAGES, MB>;
+  auto kfn = gemm_bf16_kernel<BN, STAGES, EPI, MB>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
@@ -132,7 +132,7 @@ static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int k
   }
   CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
   CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, BN);
-  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN) * splits;
+  const int tiles = ((a.M + MB * BM - 1) / (MB * BM)) * (a.N / BN) * splits;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   if (kb_per <= 0) kb_per = (a.K + BK - 1) / BK;
   if (EPI == kSplitF32) {
@@ -301,6 +301,14 @@ void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws, int
   (void)ws;
   (void)ws_elems;
   if (bn == 0 && run_cluster(a, epi, a.D, a.ldd, stream)) return;
+  if (bn == 0 && a.M > BM && a.M <= 2 * BM && a.N % 256 == 0 && a.K % 8 == 0) {
+    // 129..256 rows (decode batches): 256-row tiles, each weight slab staged
+    // once for both M-blocks
+    if (epi == kStoreBf16) launch<256, 3, kStoreBf16, 2>(a, stream);
+    else if (epi == kStoreF32) launch<256, 3, kStoreF32, 2>(a, stream);
+    else launch<256, 3, kSwiGLU, 2>(a, stream);
+    return;
+  }
   if (bn == 0) bn = choose_bn(a.M, a.N, epi);
   if (bn == 0 || a.N % bn != 0) throw std::runtime_error("lunaflux gemm: N must be a multiple of 32");
   if (a.K % 8 != 0) throw std::runtime_error("lunaflux gemm: K must be a multiple of 8");

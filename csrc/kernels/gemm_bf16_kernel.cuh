@@ -103,13 +103,23 @@ __device__ __forceinline__ void ar_store8(const ArArgs& ar, size_t off, uint4 v)
   for (int k = 0; k < ar.world; ++k) *reinterpret_cast<uint4*>(ar.out_peer[k] + off) = v;
 }
 
-template <int BN, int STAGES>
+// MB: 128-row M-blocks per tile (2: a 256-row tile whose two MMAs share each
+// staged B slab, so a skinny GEMM streams its weights once instead of once
+// per M-block).
+template <int BN, int STAGES, int MB = 1>
 struct Smem {
-  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kABytes = MB * BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTotal = STAGES * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
 };
+
+// Accumulators in flight per CTA: two (epilogue of one tile overlaps the
+// MMAs of the next) when they fit the 512 TMEM columns, else one.
+template <int BN, int MB>
+constexpr int tmem_accs() {
+  return 2 * MB * BN <= 512 ? 2 : 1;
+}
 
 template <int BN>
 constexpr uint32_t tmem_cols() {
@@ -126,7 +136,7 @@ __device__ __forceinline__ int group_of(const int* groups, int num_groups, int m
   return g;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, int MB = 1>
 __global__ void __launch_bounds__(threads_for(EPI), 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M,
@@ -136,7 +146,10 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
   // into num_groups segments, groups[g]..groups[g+1] (each a multiple of BM,
   // read from device memory), and segment g multiplies B rows [g*N, (g+1)*N).
   // M is then an upper bound on groups[num_groups]; blocks past it are skipped.
-  using S = Smem<BN, STAGES>;
+  static_assert(MB == 1 || (EPI != kSplitF32 && EPI != kAllReduceBf16), "256-row tiles: plain epilogues only");
+  using S = Smem<BN, STAGES, MB>;
+  constexpr int kAccs = tmem_accs<BN, MB>();
+  constexpr int TM = MB * BM;                 // rows per tile
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
@@ -147,12 +160,12 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (M + BM - 1) / BM;
+  const int num_m = (M + TM - 1) / TM;
   const int num_n = N / BN;
   const int num_tiles = num_m * num_n;
   const int num_units = num_tiles * splits;
   const int num_kb = (K + BK - 1) / BK;
-  constexpr uint32_t kCols = tmem_cols<BN>();
+  constexpr uint32_t kCols = MB == 1 ? tmem_cols<BN>() : 512;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmap_a);
@@ -187,7 +200,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
         const int tile = unit % num_tiles;
         const int kb0 = (unit / num_tiles) * kb_per_split;
         const int kb1 = min(num_kb, kb0 + kb_per_split);
-        const int m0 = (tile % num_m) * BM;
+        const int m0 = (tile % num_m) * TM;
         const int n0 = (tile / num_m) * BN;
         int brow = n0;
         if (groups != nullptr) {
@@ -200,7 +213,8 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
-          tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, m0);
+#pragma unroll
+          for (int j = 0; j < MB; ++j) tma_load_2d(sa + j * BM * BK * 2, &tmap_a, &full_bar[stage], kb * BK, m0 + j * BM);
           tma_load_2d_hint(sb, &tmap_b, &full_bar[stage], kb * BK, brow, pol_b);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -220,11 +234,11 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
           --local;  // skipped units use no accumulator
           continue;
         }
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
+        const int acc = kAccs == 2 ? (local & 1) : 0;
+        const uint32_t acc_phase = kAccs == 2 ? ((local >> 1) & 1) : (local & 1);
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, 2)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * MB * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, 3)) { ok = false; break; }
           tc_fence_after();
@@ -232,8 +246,10 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
           const uint32_t sb = sa + S::kABytes;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            umma_f16_ss(d_tmem, sw128_kmajor_desc(sa + kk * 32), sw128_kmajor_desc(sb + kk * 32),
-                        idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+            for (int j = 0; j < MB; ++j)
+              umma_f16_ss(d_tmem + j * BN, sw128_kmajor_desc(sa + j * BM * BK * 2 + kk * 32),
+                          sw128_kmajor_desc(sb + kk * 32), idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -251,14 +267,16 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
         --local;
         continue;
       }
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      const int acc = kAccs == 2 ? (local & 1) : 0;
+      const uint32_t acc_phase = kAccs == 2 ? ((local >> 1) & 1) : (local & 1);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, 4)) break;
       tc_fence_after();
-      const int m0 = (tile % num_m) * BM;
       const int n0 = (tile / num_m) * BN;
+#pragma unroll 1
+      for (int mb = 0; mb < MB; ++mb) {
+      const int m0 = (tile % num_m) * TM + mb * BM;
       const int row = m0 + quad * 32 + lane;
-      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * MB * BN + mb * BN;
       if constexpr (EPI == kSwiGLU) {
         // Weight rows are interleaved in groups of 64: 32 gate rows then the
         // 32 up rows of the same output features.
@@ -323,6 +341,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
           }
         }
       }
+      }  // M-blocks of the tile
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);  // the MMA warp may start the next tile now
       if constexpr (EPI == kAllReduceBf16) {

@@ -95,6 +95,25 @@ def test_prefix_cache_reuse_gives_same_tokens():
     assert first == again
 
 
+def min_router_margin(ref, prompt):
+    """Smallest gap between the k-th and (k+1)-th router score over the
+    prompt's tokens and the model's layers (fp32 oracle)."""
+    import lunaflux_b200.oracle.reference as R
+    margins = []
+    orig = R.moe_mlp
+
+    def spy(x, router, experts, top_k):
+        s = (x @ router.t()).sort(-1, descending=True).values
+        margins.append(float((s[:, top_k - 1] - s[:, top_k]).min()))
+        return orig(x, router, experts, top_k)
+    R.moe_mlp = spy
+    try:
+        ref.forward(prompt)
+    finally:
+        R.moe_mlp = orig
+    return min(margins)
+
+
 def test_moe_engine_matches_oracle():
     from lunaflux_b200.models.spec import LlamaSpec
     from lunaflux_b200.oracle.reference import ReferenceModel
@@ -103,8 +122,18 @@ def test_moe_engine_matches_oracle():
     ck = bf16_checkpoint(spec, seed=9)
     ref = ReferenceModel(spec, ck)
     eng = make_engine(spec, ck)
+    # Top-k routing is discontinuous: a prompt whose router scores for the
+    # k-th and (k+1)-th expert nearly tie in fp32 can route differently under
+    # bf16 activations, which no kernel tolerance covers.  Use prompts whose
+    # routing margins are clear of bf16 rounding.
     g = torch.Generator().manual_seed(3)
-    prompts = [torch.randint(0, spec.vocab, (n,), generator=g).tolist() for n in (7, 64, 200)]
+    prompts = []
+    for n in (7, 64, 200):
+        while True:
+            p = torch.randint(0, spec.vocab, (n,), generator=g).tolist()
+            if min_router_margin(ref, p) > 5e-3:
+                prompts.append(p)
+                break
     outs = eng.generate(prompts, 8)
     assert eng.runner.ops.read_error(True)[0] == 0
     for p, o in zip(prompts, outs):

@@ -63,7 +63,7 @@ def test_gemm_splitk(C, M, N, K, epi):
 
 @pytest.mark.parametrize("M,N,K,epi", [(256, 6144, 4096, 0), (256, 4096, 14336, 0), (256, 768, 4096, 0),
                                        (256, 4096, 512, 1), (64, 3584, 4096, 2), (1, 4096, 1792, 1),
-                                       (129, 1024, 4096, 2)])
+                                       (129, 1024, 4096, 2), (256, 1536, 1024, 0), (250, 1536, 1024, 2)])
 def test_gemm_cluster_splitk(C, M, N, K, epi):
     """Decode shapes that take the cluster split-K path: values against the fp32
     reference, bitwise reproducibility, and the plan itself."""
@@ -83,6 +83,25 @@ def test_gemm_cluster_splitk(C, M, N, K, epi):
     C.gemm(A, B, D, epi, 0, None)
     assert torch.equal(first, D)
     _close(D, ref, 3e-2, 3e-2, f"cluster split-K {M}x{N}x{K} epi={epi}")
+    assert C.read_error(True)[0] == 0
+
+
+@pytest.mark.parametrize("M,N,K,epi", [(200, 10240, 512, 0), (256, 28672, 4096, 2), (129, 32768, 256, 1),
+                                       (256, 9728, 1024, 0)])
+def test_gemm_256_row_tiles(C, M, N, K, epi):
+    """129..256 rows with enough 256-wide tiles: one 256-row tile per CTA (two
+    M=128 MMAs sharing each staged weight slab, a single TMEM accumulator)."""
+    assert C.gemm_plan_cluster(M, N, K, epi)[0] == 0
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    out_cols = N // 2 if epi == 2 else N
+    D = torch.empty(M, out_cols, device="cuda", dtype=torch.float32 if epi == 1 else torch.bfloat16)
+    C.gemm(A, B, D, epi, 0, None)
+    ref = A.float() @ B.float().t()
+    if epi == 2:
+        v = ref.view(M, N // 64, 2, 32)
+        ref = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(M, N // 2)
+    _close(D, ref, 3e-2, 3e-2, f"256-row tiles {M}x{N}x{K} epi={epi}")
     assert C.read_error(True)[0] == 0
 
 
