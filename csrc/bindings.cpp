@@ -414,6 +414,7 @@ void attn_prefill(const at::Tensor& q, at::Tensor& out, const at::Tensor& q_star
   a.num_pages = kcache.size(0);
   a.max_q_len = max_q_len;
   a.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)a.D));
+  a.q_rows = q.size(0);
   c10::cuda::CUDAGuard g(q.device());
   lf::attn::prefill(a, kcache.data_ptr(), vcache.data_ptr(), stream());
 }

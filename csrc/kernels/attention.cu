@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <unordered_map>
@@ -520,6 +521,10 @@ void prefill(const PrefillArgs& a, const void* kcache, const void* vcache, cudaS
   if (a.D != D || a.page != PAGE) throw std::runtime_error("lunaflux attention: head_dim 128 and page 16 only");
   const int64_t rows = (int64_t)a.num_pages * a.Hkv * PAGE;
   CUtensorMap tk = cache_map(kcache, rows), tv = cache_map(vcache, rows);
+  if (prefill_tc_supported(a) && !std::getenv("LUNAFLUX_PREFILL_MMA_SYNC")) {
+    prefill_tc(a, tk, tv, stream);
+    return;
+  }
   const int smem = kPreStages * 2 * kTileBytes + 1024 + 64;
   static bool attr = false;
   if (!attr) {

@@ -1,4 +1,5 @@
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -32,11 +33,16 @@ struct PrefillArgs {
   int64_t bt_stride;
   int rows, Hq, Hkv, D, page, num_pages, max_q_len;
   float scale_log2;
+  int q_rows;                  // rows of q (token rows of this step's prefill part)
 };
 
 int decode_splits(int rows, int Hkv, int max_seq, int num_sms);
 void decode(const DecodeArgs& a, const void* kcache, const void* vcache, cudaStream_t stream);
+// Prefill attention: the tcgen05 kernel (attention_tc.cu) for GQA groups of
+// 1, 2, 4, 8 or 16 heads, else the mma.sync kernel.
 void prefill(const PrefillArgs& a, const void* kcache, const void* vcache, cudaStream_t stream);
+bool prefill_tc_supported(const PrefillArgs& a);
+void prefill_tc(const PrefillArgs& a, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream);
 
 }  // namespace attn
 }  // namespace lf

@@ -140,13 +140,18 @@ def bench_attn(C, results):
         qs = torch.arange(0, T + 1, L, device="cuda", dtype=torch.int32)
         sl = torch.full((nreq,), L, device="cuda", dtype=torch.int32)
         ms = time_fn(lambda: C.attn_prefill(q, out, qs, sl, bt, kc, vc, Hq, Hkv, L))
+        os.environ["LUNAFLUX_PREFILL_MMA_SYNC"] = "1"     # the earlier mma.sync kernel, for comparison
+        try:
+            ms_sync = time_fn(lambda: C.attn_prefill(q, out, qs, sl, bt, kc, vc, Hq, Hkv, L))
+        finally:
+            del os.environ["LUNAFLUX_PREFILL_MMA_SYNC"]
         flops = nreq * Hq * 4.0 * D * L * L / 2
         qf = q[:, : Hq * D].view(nreq, L, Hq, D).transpose(1, 2)
         kf = torch.randn(nreq, Hkv, L, D, device="cuda").bfloat16().repeat_interleave(Hq // Hkv, 1)
         vf = torch.randn_like(kf)
         base = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(qf, kf, vf, is_causal=True))
-        r = dict(kernel="attn_prefill", nreq=nreq, seq=L, ours_ms=ms, sdpa_dense_ms=base, tflops=flops / ms / 1e9,
-                 peaks=src)
+        r = dict(kernel="attn_prefill", nreq=nreq, seq=L, ours_ms=ms, mma_sync_ms=ms_sync, sdpa_dense_ms=base,
+                 tflops=flops / ms / 1e9, peaks=src)
         results.append(r)
         print(json.dumps(r))
 
