@@ -16,7 +16,8 @@
 //                             computed while the softmax works on S_j)
 //   P_j  = exp2(S_j - m)      4 softmax warps, one TMEM lane (row) per thread;
 //                             P written to shared memory (bf16, 128-byte
-//                             swizzle) for the next MMA
+//                             swizzle, double-buffered, so the softmax of
+//                             block j+1 overlaps the P.V MMA of block j)
 //   O   += P_j . V_j          tcgen05.mma, V_j MN-major (the page layout
 //                             itself), O in TMEM
 //
@@ -53,13 +54,13 @@ constexpr int PAGE = 16;
 constexpr int KB = 128;                    // keys per block
 constexpr int kTile = 128 * 128 * 2;       // one 128 x 128 bf16 operand tile, 32 KB
 constexpr int kHalf = kTile / 2;           // its 64-column half (16 KB)
-// shared memory: Q | K[2] | V[2] | P | barriers
+// shared memory: Q | K[2] | V[2] | P[2] | barriers  (224 KB + barriers)
 constexpr int kOffQ = 0;
 constexpr int kOffK = kTile;
 constexpr int kOffV = 3 * kTile;
 constexpr int kOffP = 5 * kTile;
-constexpr int kOffBar = 6 * kTile;
-constexpr int kSmem = 6 * kTile + 256 + 1024;
+constexpr int kOffBar = 7 * kTile;
+constexpr int kSmem = 7 * kTile + 256 + 1024;
 constexpr uint32_t kColsS0 = 0, kColsS1 = 128, kColsO = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -128,9 +129,9 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
   uint64_t* v_empty = bars + 7;    // [2]
   uint64_t* s_full = bars + 9;     // [2]
   uint64_t* s_empty = bars + 11;   // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* pv_done = bars + 14;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* p_full = bars + 13;    // [2] per P buffer
+  uint64_t* pv_done = bars + 15;   // [2] per P buffer: P . V of that buffer's block done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int QT = 128 / G;                         // query tokens per tile
@@ -158,8 +159,10 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&p_full[b], 128);
+      mbar_init(&pv_done[b], 1);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -222,22 +225,26 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
         const uint32_t qa = sbase + kOffQ, kb = sbase + kOffK + s * kTile;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) umma_f16_ss(dS, kmajor_desc(qa, kk), kmajor_desc(kb, kk), idesc_s, kk > 0);
-        umma_commit(&s_full[s]);
+        // the stage release first, the barrier someone waits on last: commits
+        // land in issue order, so no arrive is still in flight once the
+        // waiter has seen the last one (a CTA must not exit under a pending
+        // arrive on its shared memory)
         umma_commit(&k_empty[s]);
+        umma_commit(&s_full[s]);
         return true;
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; j < nkb && ok; ++j) {
         if (j + 1 < nkb && !issue_s(j + 1)) break;
         const int s = j & 1;
-        if (!mbar_wait(p_full, j & 1, 26) || !mbar_wait(&v_full[s], (j >> 1) & 1, 27)) break;
+        if (!mbar_wait(&p_full[s], (j >> 1) & 1, 26) || !mbar_wait(&v_full[s], (j >> 1) & 1, 27)) break;
         tc_fence_after();
-        const uint32_t pa = sbase + kOffP, vb = sbase + kOffV + s * kTile;
+        const uint32_t pa = sbase + kOffP + s * kTile, vb = sbase + kOffV + s * kTile;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_f16_ss(tmem + kColsO, kmajor_desc(pa, kk), mnmajor_desc(vb, kk), idesc_o, (j > 0 || kk > 0));
-        umma_commit(pv_done);
         umma_commit(&v_empty[s]);
+        umma_commit(&pv_done[s]);
       }
     }
   } else {
@@ -252,19 +259,26 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
     const float sl2 = a.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    uint8_t* prow = smem + kOffP + row * 128;
+    uint8_t* prow0 = smem + kOffP + row * 128;
     for (int j = 0; j < nkb && ok; ++j) {
       const int s = j & 1;
       if (!mbar_wait(&s_full[s], (j >> 1) & 1, 28)) { ok = false; break; }
       tc_fence_after();
+      // the whole S row: four TMEM loads in flight, one wait
+      uint32_t v0[32], v1[32], v2[32], v3[32];
+      const uint32_t srow = tmem + lane_off + (s ? kColsS1 : kColsS0);
+      tmem_ld_32x32b_x32(srow, v0);
+      tmem_ld_32x32b_x32(srow + 32, v1);
+      tmem_ld_32x32b_x32(srow + 64, v2);
+      tmem_ld_32x32b_x32(srow + 96, v3);
+      tmem_wait_ld();
       float x[128];
 #pragma unroll
-      for (int c = 0; c < 128; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + (s ? kColsS1 : kColsS0) + c, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) x[c + e] = __uint_as_float(v[e]);
+      for (int e = 0; e < 32; ++e) {
+        x[e] = __uint_as_float(v0[e]);
+        x[32 + e] = __uint_as_float(v1[e]);
+        x[64 + e] = __uint_as_float(v2[e]);
+        x[96 + e] = __uint_as_float(v3[e]);
       }
       tc_fence_before();
       mbar_arrive(&s_empty[s]);     // the MMA warp may compute S_{j+2} into this buffer
@@ -283,9 +297,12 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
         }
       }
       const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;   // log2 units
-      // P_{j-1} has been consumed and O_{j-1} is complete before P_j or O change
-      if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, 29)) { ok = false; break; }
+      // P buffer j % 2 is free once P . V of block j - 2 is done; a rescale of O
+      // also needs P . V of block j - 1 done
+      if (j > 1 && !mbar_wait(&pv_done[s], ((j >> 1) & 1) ^ 1, 29)) { ok = false; break; }
+      uint8_t* prow = prow0 + s * kTile;
       if (mx > m_used + kRescaleThreshold) {
+        if (j > 0 && !mbar_wait(&pv_done[s ^ 1], ((j - 1) >> 1) & 1, 31)) { ok = false; break; }
         const float alpha = m_used == -INFINITY ? 0.f : ex2_approx(m_used - mx);
         if (j > 0) {
           tc_fence_after();
@@ -323,9 +340,9 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
       l += l2[0] + l2[1];
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[s]);
     }
-    if (ok && mbar_wait(pv_done, (nkb - 1) & 1, 30)) {
+    if (ok && mbar_wait(&pv_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, 30)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* dst = a.out + (int64_t)(qs + tok) * a.out_ld + (h * G + g) * D;
