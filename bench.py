@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="row-parallel all-reduce: fused into the GEMM kernel, or NCCL after it")
+    ap.add_argument("--sp", action="store_true",
+                    help="sequence parallelism (residual stream sharded by tokens; library reduce-scatter / all-gather)")
     ap.add_argument("--json-out", default="")
     ap.add_argument("--profile", default="", help="write a per-kernel time table of one extra pass here")
     return ap.parse_args()
@@ -149,7 +151,7 @@ def main():
         init_distributed("nccl", device_id=local)
     spec = specs.PRESETS[args.model]()
     if world > 1:
-        if args.impl == "ours" and args.comm == "fused":
+        if args.impl == "ours" and args.comm == "fused" and not args.sp:
             from lunaflux_b200.parallel.fused import FusedTPComm
             comm = FusedTPComm(args.step_token_budget + args.requests, spec.hidden, dev)
         else:
@@ -173,7 +175,8 @@ def main():
                             max_waiting_requests=max(4096, args.requests))
     pages = args.requests * (-(-max_ctx // 16)) + 2 * args.requests + 64
     opts = EngineOptions(max_context=max_ctx, num_pages=pages,
-                         graph_sizes=() if (args.no_graphs or args.impl != "ours") else EngineOptions().graph_sizes)
+                         graph_sizes=() if (args.no_graphs or args.impl != "ours") else EngineOptions().graph_sizes,
+                         sequence_parallel=args.sp)
     engine = LLMEngine(weights, ops, dev, sched, CacheConfig(prefix_enabled=False), opts, comm=comm)
     if args.impl == "ours":
         engine.runner.capture_all(False)

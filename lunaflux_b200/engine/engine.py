@@ -38,6 +38,7 @@ class EngineOptions:
     graph_sizes: Sequence[int] = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256)
     check_errors_every: int = 16
     tokenizer_digest: str = ""
+    sequence_parallel: bool = False        # TP only: residual stream sharded by tokens (reduce-scatter / all-gather)
 
 
 @dataclasses.dataclass
@@ -78,7 +79,8 @@ class LLMEngine:
         self.scheduler = Scheduler(sched, cache, num_pages, ident, clock=clock, max_context=opts.max_context)
         self.runner = ModelRunner(weights, ops, device, num_pages, sched.step_token_budget + sched.max_rows_per_step,
                                   sched.max_rows_per_step, opts.max_context, P, opts.graph_sizes, comm=comm,
-                                  check_errors_every=opts.check_errors_every)
+                                  check_errors_every=opts.check_errors_every,
+                                  sequence_parallel=opts.sequence_parallel)
         self.results: Dict[int, RequestResult] = {}
         self.live: Dict[int, Request] = {}
         self._next_rid = 1

@@ -41,7 +41,7 @@ def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tenso
 class ModelRunner:
     def __init__(self, weights: ModelWeights, ops, device, num_pages: int, max_tokens: int, max_rows: int,
                  max_context: int, page: int = 16, graph_sizes: Sequence[int] = (), comm=None,
-                 check_errors_every: int = 16):
+                 check_errors_every: int = 16, sequence_parallel: bool = False):
         self.w = weights
         self.spec: LlamaSpec = weights.spec
         self.shard = weights.shard
@@ -68,6 +68,21 @@ class ModelRunner:
         self.resid = torch.empty(T, H, dtype=dt, device=dev)
         self.h = torch.empty(T, H, dtype=dt, device=dev)
         self.delta = torch.empty(T, H, dtype=dt, device=dev)
+        # Sequence parallelism (Megatron): between the row-parallel projections
+        # and the next column-parallel one the residual stream lives sharded by
+        # tokens, so the norms and residual adds run on T / tp rows; the
+        # row-parallel partial sums are reduce-scattered instead of all-reduced
+        # and the normed rows all-gathered before the next projection.
+        self.sp = bool(sequence_parallel) and comm is not None and sh.size > 1
+        if self.sp:
+            if getattr(comm, "fused", False):
+                raise ValueError("sequence parallelism uses the library reduce-scatter / all-gather")
+            tp = sh.size
+            Tl = -(-T // tp)
+            self.sp_full = torch.zeros(Tl * tp, H, dtype=dt, device=dev)    # gathered rows / partial sums
+            self.sp_resid = torch.zeros(Tl, H, dtype=dt, device=dev)
+            self.sp_h = torch.zeros(Tl, H, dtype=dt, device=dev)
+            self.sp_delta = torch.zeros(Tl, H, dtype=dt, device=dev)
         self.qkv = torch.empty(T, sh.qkv_size, dtype=dt, device=dev)
         self.attn = torch.empty(T, self.Hq * self.D, dtype=dt, device=dev)
         self.act = torch.empty(T, sh.ffn_padded, dtype=dt, device=dev)
@@ -121,31 +136,23 @@ class ModelRunner:
 
     def forward(self, v: Dict[str, torch.Tensor], T: int, Tp: int, Rp: int, Rd: int, Rs: int, max_q_len: int,
                 splits: int, stochastic: bool, host_meta=None, gather: bool = True):
+        if self.sp:
+            return self.forward_sp(v, T, Tp, Rp, Rd, Rs, max_q_len, splits, stochastic, host_meta, gather)
         ops, s, w = self.ops, self.spec, self.w
-        Hq, Hkv = self.Hq, self.Hkv
         eps = s.rms_eps
         resid, h, delta = self.resid[:T], self.h[:T], self.delta[:T]
-        qkv, attn, act = self.qkv[:T], self.attn[:T], self.act[:T]
+        act = self.act[:T]
         ws = self.gemm_ws
         hm = host_meta or {}
         if self.comm is not None and getattr(self.comm, "fused", False):
             self.comm.begin_forward()
         ops.embed(v["tokens"], w.embed, resid)
         for l, lw in enumerate(w.layers):
-            kc, vc = self._layer_kv(l)
             if l == 0:
                 ops.rmsnorm(resid, None, lw.ln1, h, eps)
             else:
                 ops.rmsnorm(delta, resid, lw.ln1, h, eps)
-            self._proj(h, lw, "wqkv", qkv, 0)
-            ops.rope_kv_write(qkv, v["positions"], v["slots"], self.cos_sin, kc, vc, Hq, Hkv, self.P)
-            if Rp:
-                ops.attn_prefill(qkv[:Tp], attn[:Tp], v["p_qstart"], v["p_seqlen"], v["p_bt"], kc, vc, Hq, Hkv,
-                                 max_q_len, host={"q_start": hm.get("q_start"), "seq_lens": hm.get("seq_lens")})
-            if Rd:
-                ops.attn_decode(qkv, attn, v["d_tok"], v["d_seqlen"], v["d_bt"], kc, vc, Hq, Hkv, splits,
-                                self.part_o, self.part_lse,
-                                host={"seq_lens": hm.get("d_seq_lens"), "tok": hm.get("d_tok")})
+            attn = self._attention(l, lw, v, h, T, Tp, Rp, Rd, max_q_len, splits, hm)
             delta = self._row_parallel(attn, lw, "wo", self.delta[:T], ws)
             ops.rmsnorm(delta, resid, lw.ln2, h, eps)
             if s.is_moe:
@@ -155,13 +162,19 @@ class ModelRunner:
                 self._proj(h, lw, "wgu", act, 2)
                 delta = self._row_parallel(act, lw, "wd", self.delta[:T], ws)
         ops.rmsnorm(delta, resid, w.norm, h, eps)
+        return self._sample(h, v, Rs, stochastic, gather)
+
+    def _sample(self, h, v, Rs, stochastic, gather):
+        """LM head on the sampled rows of h and the on-device sampler (vocab
+        shards exchange candidates or logits under tensor parallelism)."""
+        ops, w = self.ops, self.w
         if gather:
             hs = self.hs[:Rs]
             torch.index_select(h, 0, v["s_idx"].long(), out=hs)
         else:
             hs = h[:Rs]
         logits = self.logits[:Rs]
-        ops.gemm(hs, w.lm_head, logits, 1, ws)
+        ops.gemm(hs, w.lm_head, logits, 1, self.gemm_ws)
         out = self.out_tok[:Rs]
         tp = self.shard.size
         if self.comm is not None and tp > 1:
@@ -183,6 +196,85 @@ class ModelRunner:
         else:
             ops.argmax(logits, out)
         return out
+
+    def _attention(self, l, lw, v, h, T, Tp, Rp, Rd, max_q_len, splits, hm):
+        """QKV projection, RoPE + paged KV write, prefill and decode attention
+        for the T token rows of h; returns the attention output rows."""
+        ops, Hq, Hkv = self.ops, self.Hq, self.Hkv
+        kc, vc = self._layer_kv(l)
+        qkv, attn = self.qkv[:T], self.attn[:T]
+        self._proj(h, lw, "wqkv", qkv, 0)
+        ops.rope_kv_write(qkv, v["positions"], v["slots"], self.cos_sin, kc, vc, Hq, Hkv, self.P)
+        if Rp:
+            ops.attn_prefill(qkv[:Tp], attn[:Tp], v["p_qstart"], v["p_seqlen"], v["p_bt"], kc, vc, Hq, Hkv,
+                             max_q_len, host={"q_start": hm.get("q_start"), "seq_lens": hm.get("seq_lens")})
+        if Rd:
+            ops.attn_decode(qkv, attn, v["d_tok"], v["d_seqlen"], v["d_bt"], kc, vc, Hq, Hkv, splits,
+                            self.part_o, self.part_lse,
+                            host={"seq_lens": hm.get("d_seq_lens"), "tok": hm.get("d_tok")})
+        return attn
+
+    def forward_sp(self, v, T, Tp, Rp, Rd, Rs, max_q_len, splits, stochastic, host_meta=None, gather=True):
+        """The forward with the residual stream sharded by tokens: this rank
+        owns rows [rank * Tl, (rank + 1) * Tl) of the (padded) step."""
+        ops, s, w, comm = self.ops, self.spec, self.w, self.comm
+        tp, rank = self.shard.size, self.shard.rank
+        eps = s.rms_eps
+        hm = host_meta or {}
+        Tl = -(-T // tp)
+        full = self.sp_full[: Tl * tp]
+        resid, h, delta = self.sp_resid[:Tl], self.sp_h[:Tl], self.sp_delta[:Tl]
+        act = self.act[:T]
+        ws = self.gemm_ws
+        # embeddings of every token, then this rank's rows (padding rows are zero)
+        emb = self.h[:T]
+        ops.embed(v["tokens"], w.embed, emb)
+        full[T:].zero_()
+        full[:T].copy_(emb)
+        resid.copy_(full[rank * Tl:(rank + 1) * Tl])
+
+        def gather_rows(local):
+            comm.all_gather_rows(local, full)
+            return full[:T]
+
+        def scatter_partial(partial_rows):
+            # partial_rows: [T, H] this rank's partial sums; padding rows add zero
+            if partial_rows.data_ptr() != full.data_ptr():
+                full[:T].copy_(partial_rows)
+            full[T:].zero_()
+            comm.reduce_scatter_rows(full, delta)
+
+        for l, lw in enumerate(w.layers):
+            if l == 0:
+                ops.rmsnorm(resid, None, lw.ln1, h, eps)
+            else:
+                ops.rmsnorm(delta, resid, lw.ln1, h, eps)
+            hf = gather_rows(h)
+            attn = self._attention(l, lw, v, hf, T, Tp, Rp, Rd, max_q_len, splits, hm)
+            o_part = self.delta[:T]
+            self._row_parallel_partial(attn, lw, "wo", o_part, ws)
+            scatter_partial(o_part)
+            ops.rmsnorm(delta, resid, lw.ln2, h, eps)
+            hf = gather_rows(h)
+            d_part = self.delta[:T]
+            if s.is_moe:
+                self.moe(hf, d_part, lw, reduce=False)
+            else:
+                self._proj(hf, lw, "wgu", act, 2)
+                self._row_parallel_partial(act, lw, "wd", d_part, ws)
+            scatter_partial(d_part)
+        ops.rmsnorm(delta, resid, w.norm, h, eps)
+        hf = gather_rows(h)
+        return self._sample(hf, v, Rs, stochastic, gather)
+
+    def _row_parallel_partial(self, A, lw, name, out, ws):
+        """This rank's partial sum of a row-parallel projection (no reduction)."""
+        f = self._fp8(lw, name)
+        if f is not None:
+            q, s = self._quant(A)
+            self.ops.gemm_fp8(q, s, f[0], f[1], out, 0)
+        else:
+            self.ops.gemm(A, getattr(lw, name), out, 0, ws)
 
     def _fp8(self, lw, name):
         return lw.fp8.get(name) if lw.fp8 is not None else None
@@ -257,7 +349,7 @@ class ModelRunner:
         self.moe_y = torch.zeros(rows, s.hidden, dtype=self.dtype, device=dev)
         self.router_bias: Optional[torch.Tensor] = None  # fp32 [E] logit bias (load-skew experiments)
 
-    def moe(self, h, delta, lw):
+    def moe(self, h, delta, lw, reduce: bool = True):
         """Routed SwiGLU experts: route -> align -> gather -> grouped gate/up
         GEMM (SwiGLU epilogue) -> grouped down GEMM -> weighted combine, then
         the sum over ranks (experts or expert shards live on different ranks)."""
@@ -271,7 +363,7 @@ class ModelRunner:
         ops.gemm_grouped(self.moe_x[:rows], lw.experts_gu, self.moe_act[:rows], self.moe_groups, El, 2)
         ops.gemm_grouped(self.moe_act[:rows], lw.experts_d, self.moe_y[:rows], self.moe_groups, El, 0)
         ops.moe_combine(self.moe_y[:rows], self.moe_slot[:T * k], w, T, k, delta)
-        if self.comm is not None:
+        if self.comm is not None and reduce:
             self.comm.all_reduce(delta)
 
     # ------------------------------------------------------------------ one step

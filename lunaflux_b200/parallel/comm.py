@@ -69,6 +69,18 @@ class TPComm:
         self.calls += 1
         dist.all_gather_into_tensor(out, local, group=self.group)
 
+    def reduce_scatter_rows(self, full: torch.Tensor, local: torch.Tensor):
+        """local = rows [rank * n, (rank + 1) * n) of the sum over ranks of
+        full [world * n, H] (sequence parallelism: the residual stream is
+        sharded by tokens)."""
+        self.calls += 1
+        dist.reduce_scatter_tensor(local, full, group=self.group)
+
+    def all_gather_rows(self, local: torch.Tensor, full: torch.Tensor):
+        """full [world * n, H] = the ranks' local [n, H] blocks in rank order."""
+        self.calls += 1
+        dist.all_gather_into_tensor(full, local, group=self.group)
+
     def barrier(self):
         dist.barrier(group=self.group)
 
