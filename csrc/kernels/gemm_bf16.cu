@@ -22,6 +22,15 @@
 // the 32 up rows of the same features): the gate/up projection writes
 // silu(gate) * up directly and the [M, 2F] intermediate never exists.
 //
+// Shape variants chosen by run():
+//   * skinny GEMMs (the tiles would leave more than half of the SMs idle):
+//     cluster split-K, gemm_cluster_splitk_kernel (one cluster of up to 8
+//     CTAs per tile, partials summed through distributed shared memory);
+//   * 129..256 rows: 256-row tiles (two M=128 MMAs per weight slab);
+//   * otherwise the widest BN that still covers the SMs.
+// The fused all-reduce epilogue (kAllReduceBf16), the fp32 split slabs
+// (kSplitF32) and the grouped mixture-of-experts mode share the kernel.
+//
 // All waits are bounded (common.cuh); every TMA load fills only its own CTA.
 #include <cuda.h>
 #include <cudaTypedefs.h>
