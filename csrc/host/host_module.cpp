@@ -59,7 +59,7 @@ PYBIND11_MODULE(_host, m) {
 
   py::class_<BpeEncoder>(m, "BpeEncoder")
       .def(py::init<const std::vector<std::tuple<int, int, int>>&>())
-      .def("encode", &BpeEncoder::encode);
+      .def("encode", &BpeEncoder::encode, py::call_guard<py::gil_scoped_release>());
 
   py::class_<Channel>(m, "Channel")
       .def(py::init<int, uint32_t, double>(), py::arg("fd"), py::arg("max_frame") = 64u << 20,

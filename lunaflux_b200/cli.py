@@ -149,6 +149,9 @@ def plan(root, config_rel, config_sha, model_sha, kv_budget, tokens_per_page, ou
     out(f"kv bytes per page: {lay.bytes_per_page}")
     out(f"kv pages: {pages}")
     out(f"kv token capacity: {pages * P}")
+    from .models.admission import admit
+    adm = admit(spec, max_context=min(spec.max_position, 4096), max_batch=1)
+    out(f"kernel admission: {'ok' if adm.ok else 'rejected: ' + '; '.join(adm.details)}")
     out(f"readiness: {'true' if pages > 0 else 'false'}")
     return pages
 

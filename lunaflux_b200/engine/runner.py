@@ -170,7 +170,7 @@ class ModelRunner:
         ops, w = self.ops, self.w
         if gather:
             hs = self.hs[:Rs]
-            torch.index_select(h, 0, v["s_idx"].long(), out=hs)
+            torch.index_select(h, 0, v["s_idx"], out=hs)   # int32 ids: no index copy
         else:
             hs = h[:Rs]
         logits = self.logits[:Rs]

@@ -1,0 +1,131 @@
+"""Model admission: can this model run on this deployment, and if not, why.
+
+Reference: model/llama_admission (a model spec is admitted against the
+device and kernel capabilities before any weight is loaded, with typed
+rejection reasons).  Here the checks are those of the sm_100a kernels and
+the tensor / expert-parallel plan, plus a memory plan per rank: weights,
+the KV arena for the requested context and batch, and the activation
+workspace, against the device's memory.
+"""
+from __future__ import annotations
+
+import dataclasses
+import enum
+from typing import List, Optional
+
+from .spec import LlamaSpec
+
+
+class Rejection(enum.Enum):
+    HEAD_DIM = "head_dim"                  # attention kernels are built for head_dim 128
+    GQA_GROUP = "gqa_group"                # decode attention packs at most 16 query heads per KV head
+    TP_HEADS = "tp_heads"                  # query heads not divisible by the TP degree
+    TP_KV_HEADS = "tp_kv_heads"            # KV heads neither divisible by TP nor dividing it
+    TP_FFN = "tp_ffn"                      # FFN width not divisible by TP
+    TP_VOCAB = "tp_vocab"                  # vocabulary not divisible by TP (vocab-parallel LM head)
+    TP_WORLD = "tp_world"                  # more than 8 ranks (one NVSwitch domain)
+    EP_EXPERTS = "ep_experts"              # experts not divisible by the EP degree
+    FP8_BLOCK = "fp8_block"                # block-scaled fp8 needs 128-aligned projection dims
+    GEMM_ALIGN = "gemm_align"              # hidden size not a multiple of 256 (GEMM tiles)
+    CONTEXT = "context"                    # requested context beyond max_position
+    MEMORY = "memory"                      # weights + KV + workspace exceed the device memory
+
+
+@dataclasses.dataclass(frozen=True)
+class MemoryPlan:
+    weight_bytes: int          # per rank
+    kv_bytes: int              # per rank, for max_batch sequences of max_context tokens
+    workspace_bytes: int       # activations, logits, GEMM workspace (per rank)
+    device_bytes: int          # 0: unknown
+
+    @property
+    def total(self) -> int:
+        return self.weight_bytes + self.kv_bytes + self.workspace_bytes
+
+
+@dataclasses.dataclass(frozen=True)
+class Admission:
+    ok: bool
+    reasons: List[Rejection]
+    details: List[str]
+    memory: MemoryPlan
+
+
+def _elem(spec: LlamaSpec) -> int:
+    return 2 if spec.dtype == "bf16" else 4
+
+
+def memory_plan(spec: LlamaSpec, tp: int, ep: int, max_context: int, max_batch: int, step_tokens: int,
+                page: int = 16, device_bytes: int = 0) -> MemoryPlan:
+    e = _elem(spec)
+    H, D = spec.hidden, spec.head_dim
+    q = spec.heads * D
+    kv = spec.kv_heads * D
+    per_layer_attn = H * (q + 2 * kv) + q * H
+    if spec.is_moe:
+        per_layer_mlp = (spec.experts // max(ep, 1)) * 3 * H * spec.ffn + H * spec.experts
+        attn_share = per_layer_attn // tp
+        mlp_share = per_layer_mlp if ep > 1 else per_layer_mlp // tp
+    else:
+        attn_share = per_layer_attn // tp
+        mlp_share = 3 * H * spec.ffn // tp
+    wbytes_per = 1 if spec.fp8_block else e
+    weights = spec.layers * (attn_share + mlp_share) * wbytes_per
+    weights += 2 * spec.vocab * H * e // tp + (2 * spec.layers + 1) * H * e
+    kv_heads_local = max(1, spec.kv_heads // tp)
+    pages = max_batch * -(-max_context // page)
+    kv_bytes = spec.layers * 2 * pages * kv_heads_local * page * D * e
+    T = step_tokens + max_batch
+    ws = T * (4 * H + (q + 2 * kv) // tp + 2 * spec.ffn // tp) * e + max_batch * spec.vocab * 4 // tp
+    ws += 512 * 32768 * 4                  # split / all-reduce workspace
+    return MemoryPlan(int(weights), int(kv_bytes), int(ws), int(device_bytes))
+
+
+def admit(spec: LlamaSpec, tp: int = 1, ep: int = 1, max_context: int = 4096, max_batch: int = 256,
+          step_tokens: int = 8192, device_bytes: int = 0, reserve_fraction: float = 0.05) -> Admission:
+    """Checks the model against the kernels, the parallel plan and (when
+    device_bytes > 0) the memory of one device; every failed check is listed."""
+    reasons: List[Rejection] = []
+    details: List[str] = []
+
+    def no(r: Rejection, msg: str):
+        reasons.append(r)
+        details.append(msg)
+
+    if spec.head_dim != 128:
+        no(Rejection.HEAD_DIM, f"head_dim {spec.head_dim} (kernels support 128)")
+    if spec.heads // spec.kv_heads > 16:
+        no(Rejection.GQA_GROUP, f"{spec.heads // spec.kv_heads} query heads per KV head (at most 16)")
+    if not 1 <= tp <= 8:
+        no(Rejection.TP_WORLD, f"tensor-parallel degree {tp} (1..8 in one NVSwitch domain)")
+    else:
+        if spec.heads % tp:
+            no(Rejection.TP_HEADS, f"{spec.heads} heads over {tp} ranks")
+        if not ((spec.kv_heads >= tp and spec.kv_heads % tp == 0) or (spec.kv_heads < tp and tp % spec.kv_heads == 0)):
+            no(Rejection.TP_KV_HEADS, f"{spec.kv_heads} KV heads over {tp} ranks")
+        if spec.ffn % tp:
+            no(Rejection.TP_FFN, f"ffn {spec.ffn} over {tp} ranks")
+        if spec.vocab % tp:
+            no(Rejection.TP_VOCAB, f"vocab {spec.vocab} over {tp} ranks")
+    if ep > 1 and (not spec.is_moe or spec.experts % ep):
+        no(Rejection.EP_EXPERTS, f"{spec.experts} experts over {ep} expert-parallel ranks")
+    if spec.fp8_block and (spec.hidden % 128 or (spec.ffn // max(tp, 1)) % 128 or (spec.heads * spec.head_dim) % 128):
+        no(Rejection.FP8_BLOCK, "fp8 projections need hidden, per-rank ffn and heads*head_dim multiples of 128")
+    if spec.hidden % 256:
+        no(Rejection.GEMM_ALIGN, f"hidden {spec.hidden} is not a multiple of 256")
+    if max_context > spec.max_position:
+        no(Rejection.CONTEXT, f"context {max_context} beyond max_position {spec.max_position}")
+    mem = memory_plan(spec, max(tp, 1), ep, max_context, max_batch, step_tokens, device_bytes=device_bytes)
+    if device_bytes > 0 and mem.total > device_bytes * (1.0 - reserve_fraction):
+        no(Rejection.MEMORY, f"needs {mem.total / 2**30:.1f} GiB per rank, device has {device_bytes / 2**30:.1f} GiB")
+    return Admission(not reasons, reasons, details, mem)
+
+
+def admit_on_device(spec: LlamaSpec, tp: int = 1, ep: int = 1, device_index: Optional[int] = 0, **kw) -> Admission:
+    """admit() with the memory of a probed device (no memory check when none)."""
+    from ..runtime.device import DeviceStatus, probe
+    r = probe()
+    dev_bytes = 0
+    if r.status is DeviceStatus.OK and device_index is not None and device_index < len(r.devices):
+        dev_bytes = r.devices[device_index].total_bytes
+    return admit(spec, tp, ep, device_bytes=dev_bytes, **kw)

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import asyncio
 import collections
+import concurrent.futures
 import threading
 import time
 from dataclasses import dataclass
@@ -46,7 +47,7 @@ class EngineService:
     """Owns the engine thread; thread-safe submit / cancel; events via sinks."""
 
     def __init__(self, engine: LLMEngine, tokenizer: Optional[Tokenizer], limits: InferenceLimits,
-                 content_digest: str = "", plan_digest: str = ""):
+                 content_digest: str = "", plan_digest: str = "", tokenizer_threads: int = 2):
         self.engine = engine
         self.tokenizer = tokenizer
         self.limits = limits
@@ -59,6 +60,8 @@ class EngineService:
         self.draining = False
         self.failed = False
         self._thread = threading.Thread(target=self._run, name="lunaflux-engine", daemon=True)
+        self._tok_pool = concurrent.futures.ThreadPoolExecutor(max_workers=tokenizer_threads,
+                                                               thread_name_prefix="lunaflux-tokenizer")
         self.engine.listeners.append(self._on_outputs)
 
     def start(self):
@@ -73,12 +76,32 @@ class EngineService:
             self._stop = True
             self._cv.notify()
         self._thread.join(timeout=30)
+        self._tok_pool.shutdown(wait=False, cancel_futures=True)
 
     # -------------------------------------------------------------- producer side
     def submit(self, req: GenerateRequest, sink: Callable[[object], None]):
+        """Queues a request for the engine thread.  Text prompts are tokenized
+        first on the tokenizer pool, so a long prompt never stalls a step."""
+        if req.input_text is not None and self.tokenizer is not None:
+            self._tok_pool.submit(self._tokenize_then_queue, req, sink)
+            return
+        self._queue(req, sink)
+
+    def _queue(self, req, sink):
         with self._cv:
             self._inbox.append(("add", req, sink))
             self._cv.notify()
+
+    def _tokenize_then_queue(self, req: GenerateRequest, sink):
+        try:
+            ids = tuple(self.tokenizer.encode_bytes(req.input_text, allow_special=False))
+        except ValueError:
+            sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
+            return
+        if not ids:
+            sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
+            return
+        self._queue(GenerateRequest(**{**req.__dict__, "input_tokens": ids, "input_text": None}), sink)
 
     def cancel(self, rid: int):
         with self._cv:
@@ -184,11 +207,17 @@ class EngineService:
 class TCPServer:
     """Framed request-v1 / event-v2 endpoint on asyncio; many concurrent clients."""
 
-    def __init__(self, service: EngineService, host: str = "127.0.0.1", port: int = 0, max_frame: int = 16 << 20):
+    def __init__(self, service: EngineService, host: str = "127.0.0.1", port: int = 0, max_frame: int = 16 << 20,
+                 max_pending_events: int = 1 << 16):
         self.service = service
         self.host = host
         self.port = port
         self.max_frame = max_frame
+        # A client that stops reading cannot grow the server's memory: past
+        # this many undelivered events its requests are cancelled and the
+        # connection is closed.
+        self.max_pending_events = max_pending_events
+        self.overflows = 0
         self.server: Optional[asyncio.AbstractServer] = None
 
     async def start(self):
@@ -200,11 +229,24 @@ class TCPServer:
         loop = asyncio.get_running_loop()
         frames = FrameReader(REQUEST_MAGIC, self.max_frame)
         open_rids = set()
-        q: asyncio.Queue = asyncio.Queue()
+        q: asyncio.Queue = asyncio.Queue(maxsize=self.max_pending_events)
+        overflow = {"hit": False}
+
+        def put(item):
+            if overflow["hit"]:
+                return
+            try:
+                q.put_nowait(item)
+            except asyncio.QueueFull:
+                overflow["hit"] = True
+                self.overflows += 1
+                for rid in list(open_rids):
+                    self.service.cancel(rid)
+                writer.close()
 
         def sink_for(rid):
             def sink(ev):
-                loop.call_soon_threadsafe(q.put_nowait, (rid, ev))
+                loop.call_soon_threadsafe(put, (rid, ev))
             return sink
 
         state = {"eof": False}

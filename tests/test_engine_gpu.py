@@ -70,6 +70,29 @@ def test_engine_eager_and_graph_agree_mostly():
     assert same >= 2, (a, b)
 
 
+def test_decode_steps_allocate_nothing():
+    """Steady state: once every request decodes, a step (packed upload, graph
+    replay, on-device sampling, token readback) makes no device allocation.
+    Reference behaviour: tests/hot_path_alloc (zero allocations after warm-up)."""
+    spec = small_spec()
+    ck = bf16_checkpoint(spec, seed=4)
+    eng = make_engine(spec, ck, graphs=True)
+    g = torch.Generator().manual_seed(5)
+    for n in (20, 31, 45, 60):
+        eng.add_request(torch.randint(0, spec.vocab, (n,), generator=g).tolist(), 48)
+    for _ in range(8):                      # prefill, then warm-up decode steps (graph capture)
+        eng.step()
+    assert all(r.num_computed >= len(r.prompt) for r in eng.live.values())
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_stats()["allocation.all.allocated"]
+    for _ in range(16):
+        assert eng.step()
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_stats()["allocation.all.allocated"] == before
+    assert eng.runner.last_bucket is not None      # the steps replayed a captured graph
+    assert eng.runner.ops.read_error(True)[0] == 0
+
+
 def test_stochastic_is_reproducible():
     from lunaflux_b200.contracts import SamplingParameters
     spec = small_spec(1)
