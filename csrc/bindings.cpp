@@ -392,7 +392,7 @@ int64_t attn_decode_splits(int64_t rows, int64_t Hkv, int64_t max_seq, int64_t n
 
 void attn_prefill(const at::Tensor& q, at::Tensor& out, const at::Tensor& q_start, const at::Tensor& seq_lens,
                   const at::Tensor& block_table, const at::Tensor& kcache, const at::Tensor& vcache, int64_t Hq,
-                  int64_t Hkv, int64_t max_q_len) {
+                  int64_t Hkv, int64_t max_q_len, int64_t progress) {
   check_rowmajor(q, "q");
   check_rowmajor(out, "out");
   check_rowmajor(block_table, "block_table");
@@ -415,6 +415,7 @@ void attn_prefill(const at::Tensor& q, at::Tensor& out, const at::Tensor& q_star
   a.max_q_len = max_q_len;
   a.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)a.D));
   a.q_rows = q.size(0);
+  a.progress = reinterpret_cast<int*>(progress);
   c10::cuda::CUDAGuard g(q.device());
   lf::attn::prefill(a, kcache.data_ptr(), vcache.data_ptr(), stream());
 }
@@ -459,7 +460,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample, py::arg("logits"), py::arg("params"), py::arg("out"), py::arg("status") = py::none());
   m.def("attn_decode", &attn_decode);
   m.def("attn_decode_splits", &attn_decode_splits);
-  m.def("attn_prefill", &attn_prefill);
+  m.def("attn_prefill", &attn_prefill, py::arg("q"), py::arg("out"), py::arg("q_start"), py::arg("seq_lens"),
+        py::arg("block_table"), py::arg("kcache"), py::arg("vcache"), py::arg("Hq"), py::arg("Hkv"),
+        py::arg("max_q_len"), py::arg("progress") = 0);
   m.def("read_error", &read_error, py::arg("clear") = true);
   m.def("inject_error", &inject_error);
   m.def("counter_unit", &counter_unit);

@@ -34,6 +34,7 @@ struct PrefillArgs {
   int rows, Hq, Hkv, D, page, num_pages, max_q_len;
   float scale_log2;
   int q_rows;                  // rows of q (token rows of this step's prefill part)
+  int* progress;               // optional (null in production): per-CTA progress codes, host-visible memory
 };
 
 int decode_splits(int rows, int Hkv, int max_seq, int num_sms);

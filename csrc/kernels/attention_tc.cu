@@ -21,10 +21,11 @@
 //   O   += P_j . V_j          tcgen05.mma, V_j MN-major (the page layout
 //                             itself), O in TMEM
 //
-// The running maximum used for P only moves when the row maximum grows by
-// more than 8 (in log2 units): then O and the row sum are rescaled through
-// TMEM.  Between such events P may exceed 1 by at most 2^8, well inside fp32
-// and bf16 range; the final O / l is unchanged.
+// The running maximum used for P only moves when a row maximum grows by more
+// than 8 (in log2 units): then O and the row sums of the warp are rescaled
+// through TMEM (warp-uniformly: tcgen05.ld / st are warp-collective).
+// Between such events P may exceed 1 by at most 2^8, well inside fp32 and
+// bf16 range; the final O / l is unchanged.
 //
 // Warp roles (192 threads): warp 0 lane 0 issues the TMA loads (Q once, then
 // K and V pages of each block into a 2-stage ring), warp 1 owns TMEM and its
@@ -106,6 +107,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Diagnostics: the CTA's progress code, written through to host-visible memory.
+__device__ __forceinline__ void mark(const PrefillArgs& a, int code) {
+  if (a.progress != nullptr) {
+    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(a.progress + cta), "r"(code) : "memory");
+  }
+}
+
 __device__ __forceinline__ int bt_page(const PrefillArgs& a, int r, int idx) {
   int p = a.block_table[(int64_t)r * a.bt_stride + idx];
   if (p < 0 || p >= a.num_pages) {
@@ -140,12 +149,16 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
   const int qs = a.q_start[r];
   const int n = a.q_start[r + 1] - qs;
   const int t0 = qb * QT;
-  if (t0 >= n) return;                            // uniform for the CTA: before any barrier
+  if (t0 >= n) {                                  // uniform for the CTA: before any barrier
+    if (threadIdx.x == 0) mark(a, 1001);
+    return;
+  }
   const int L = a.seq_lens[r];
   const int pos0 = L - n;                         // position of the row's first query
   const int kmax = pos0 + min(n, t0 + QT) - 1;    // last key any query of the tile sees
   const int nkb = kmax / KB + 1;
 
+  if (threadIdx.x == 0) mark(a, 1);
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
@@ -174,6 +187,7 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
+  if (threadIdx.x == 0) mark(a, 2);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -262,7 +276,9 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
     uint8_t* prow0 = smem + kOffP + row * 128;
     for (int j = 0; j < nkb && ok; ++j) {
       const int s = j & 1;
-      if (!mbar_wait(&s_full[s], (j >> 1) & 1, 28)) { ok = false; break; }
+      // every wait before a warp-collective TMEM access is made warp-uniform:
+      // tcgen05.ld / st are .sync.aligned and must not run in a diverged warp
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[s], (j >> 1) & 1, 28))) { ok = false; break; }
       tc_fence_after();
       // the whole S row: four TMEM loads in flight, one wait
       uint32_t v0[32], v1[32], v2[32], v3[32];
@@ -299,11 +315,18 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
       const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;   // log2 units
       // P buffer j % 2 is free once P . V of block j - 2 is done; a rescale of O
       // also needs P . V of block j - 1 done
-      if (j > 1 && !mbar_wait(&pv_done[s], ((j >> 1) & 1) ^ 1, 29)) { ok = false; break; }
+      if (j > 1 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[s], ((j >> 1) & 1) ^ 1, 29))) { ok = false; break; }
       uint8_t* prow = prow0 + s * kTile;
-      if (mx > m_used + kRescaleThreshold) {
-        if (j > 0 && !mbar_wait(&pv_done[s ^ 1], ((j - 1) >> 1) & 1, 31)) { ok = false; break; }
-        const float alpha = m_used == -INFINITY ? 0.f : ex2_approx(m_used - mx);
+      // The rescale touches O through TMEM with warp-collective instructions,
+      // so the whole warp rescales when any of its rows needs to; rows whose
+      // maximum moved less rescale by their own (exact) factor.
+      if (__any_sync(0xffffffffu, mx > m_used + kRescaleThreshold)) {
+        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[s ^ 1], ((j - 1) >> 1) & 1, 31))) {
+          ok = false;
+          break;
+        }
+        const float m_new = fmaxf(m_used, mx);
+        const float alpha = m_used == -INFINITY ? (m_new == -INFINITY ? 1.f : 0.f) : ex2_approx(m_used - m_new);
         if (j > 0) {
           tc_fence_after();
 #pragma unroll 1
@@ -318,7 +341,7 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
           tmem_wait_st();
         }
         l *= alpha;
-        m_used = mx;
+        m_used = m_new;
       }
       // P = exp2(s * scale_log2 - m) as bf16 into the swizzled [key-half][row][128 B] tile
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;   // all-masked row: every p is 0
@@ -341,8 +364,9 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[s]);
+      if (threadIdx.x == 64) mark(a, 10 + j);
     }
-    if (ok && mbar_wait(&pv_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, 30)) {
+    if (__all_sync(0xffffffffu, ok && mbar_wait(&pv_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, 30))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* dst = a.out + (int64_t)(qs + tok) * a.out_ld + (h * G + g) * D;
@@ -364,11 +388,13 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
     }
   }
   tc_fence_before();
+  if (threadIdx.x == 64) mark(a, 1000);
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (threadIdx.x == 32) mark(a, 1001);
 }
 
 static std::mutex g_mu;
