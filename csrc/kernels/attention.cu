@@ -521,9 +521,9 @@ void prefill(const PrefillArgs& a, const void* kcache, const void* vcache, cudaS
   if (a.D != D || a.page != PAGE) throw std::runtime_error("lunaflux attention: head_dim 128 and page 16 only");
   const int64_t rows = (int64_t)a.num_pages * a.Hkv * PAGE;
   CUtensorMap tk = cache_map(kcache, rows), tv = cache_map(vcache, rows);
-  // The tcgen05 kernel is opt-in until its hang in the engine's layer
-  // sequence is explained (it runs correctly in isolation).
-  if (prefill_tc_supported(a) && std::getenv("LUNAFLUX_PREFILL_TC") != nullptr) {
+  // The tcgen05 kernel for supported GQA groups; LUNAFLUX_PREFILL_MMA_SYNC
+  // selects the mma.sync kernel instead (for comparison).
+  if (prefill_tc_supported(a) && std::getenv("LUNAFLUX_PREFILL_MMA_SYNC") == nullptr) {
     prefill_tc(a, tk, tv, stream);
     return;
   }

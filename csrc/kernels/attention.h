@@ -39,8 +39,9 @@ struct PrefillArgs {
 
 int decode_splits(int rows, int Hkv, int max_seq, int num_sms);
 void decode(const DecodeArgs& a, const void* kcache, const void* vcache, cudaStream_t stream);
-// Prefill attention: the mma.sync kernel, or with LUNAFLUX_PREFILL_TC set the
-// tcgen05 kernel (attention_tc.cu) for GQA groups of 1, 2, 4, 8 or 16 heads.
+// Prefill attention: the tcgen05 kernel (attention_tc.cu) for GQA groups of
+// 1, 2, 4, 8 or 16 heads, else (or with LUNAFLUX_PREFILL_MMA_SYNC set) the
+// mma.sync kernel.
 void prefill(const PrefillArgs& a, const void* kcache, const void* vcache, cudaStream_t stream);
 bool prefill_tc_supported(const PrefillArgs& a);
 void prefill_tc(const PrefillArgs& a, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream);

@@ -140,14 +140,11 @@ def bench_attn(C, results):
         qs = torch.arange(0, T + 1, L, device="cuda", dtype=torch.int32)
         sl = torch.full((nreq,), L, device="cuda", dtype=torch.int32)
         ms = time_fn(lambda: C.attn_prefill(q, out, qs, sl, bt, kc, vc, Hq, Hkv, L))
-        ms_sync = ms
-        if os.environ.get("LUNAFLUX_PREFILL_TC"):
-            # the tcgen05 kernel is selected: time the mma.sync kernel beside it
-            del os.environ["LUNAFLUX_PREFILL_TC"]
-            try:
-                ms_sync = time_fn(lambda: C.attn_prefill(q, out, qs, sl, bt, kc, vc, Hq, Hkv, L))
-            finally:
-                os.environ["LUNAFLUX_PREFILL_TC"] = "1"
+        os.environ["LUNAFLUX_PREFILL_MMA_SYNC"] = "1"     # the mma.sync kernel, for comparison
+        try:
+            ms_sync = time_fn(lambda: C.attn_prefill(q, out, qs, sl, bt, kc, vc, Hq, Hkv, L))
+        finally:
+            del os.environ["LUNAFLUX_PREFILL_MMA_SYNC"]
         flops = nreq * Hq * 4.0 * D * L * L / 2
         qf = q[:, : Hq * D].view(nreq, L, Hq, D).transpose(1, 2)
         kf = torch.randn(nreq, Hkv, L, D, device="cuda").bfloat16().repeat_interleave(Hq // Hkv, 1)
