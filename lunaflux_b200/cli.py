@@ -151,7 +151,7 @@ def plan(root, config_rel, config_sha, model_sha, kv_budget, tokens_per_page, ou
     out(f"kv token capacity: {pages * P}")
     from .models.admission import admit
     adm = admit(spec, max_context=min(spec.max_position, 4096), max_batch=1)
-    out(f"kernel admission: {'ok' if adm.ok else 'rejected: ' + '; '.join(adm.details)}")
+    out(f"sm_100a kernel admission: {'ok' if adm.ok else 'rejected: ' + '; '.join(adm.details)}")
     out(f"readiness: {'true' if pages > 0 else 'false'}")
     return pages
 
@@ -237,6 +237,8 @@ def serve(args: List[str]):
     ap.add_argument("--tokenizer", default="")
     ap.add_argument("--max-context", type=int, default=4096)
     ap.add_argument("--metrics-port", type=int, default=-1, help="HTTP /metrics and /health (-1: off, 0: any)")
+    ap.add_argument("--model-dir", default="",
+                    help="Hugging Face style directory: config.json, safetensors weights (index or single), tokenizer.json")
     a = ap.parse_args(args)
     sched, cache = SchedulerConfig(), CacheConfig()
     preset = a.preset
@@ -246,17 +248,36 @@ def serve(args: List[str]):
         sched, cache = cfg.scheduler, cfg.cache
         preset = cfg.model.preset or preset
         a.host, a.port = cfg.service.listen_host, cfg.service.listen_port
-    spec = specs.PRESETS[preset]()
-    if a.layers:
-        spec = spec.with_layers(a.layers)
     cuda = torch.cuda.is_available()
     dev = torch.device("cuda", 0) if cuda else torch.device("cpu")
-    if not cuda:
-        spec = specs.LlamaSpec(**{**spec.__dict__, "dtype": "fp32"})
-    w = build_runtime(spec, random_source(spec, 0, dev, torch.bfloat16 if cuda else torch.float32), device=dev)
+    ckpt = None
+    if a.model_dir:
+        from .models.checkpoint import CheckpointDir
+        ckpt = CheckpointDir(a.model_dir)
+        spec = ckpt.spec(dtype="bf16" if cuda else "fp32")
+        preset = os.path.basename(os.path.abspath(a.model_dir))
+    else:
+        spec = specs.PRESETS[preset]()
+        if a.layers:
+            spec = spec.with_layers(a.layers)
+        if not cuda:
+            spec = specs.LlamaSpec(**{**spec.__dict__, "dtype": "fp32"})
+    from .models.admission import admit
+    adm = admit(spec, max_context=a.max_context, max_batch=sched.max_active_requests,
+                step_tokens=sched.step_token_budget,
+                device_bytes=torch.cuda.get_device_properties(0).total_memory if cuda else 0, kernels=cuda)
+    if not adm.ok:
+        raise CliError("model not admitted: " + "; ".join(adm.details))
+    source = ckpt.source() if ckpt is not None else random_source(spec, 0, dev, torch.bfloat16 if cuda else torch.float32)
+    w = build_runtime(spec, source, device=dev)
+    tok_from_dir = None
+    if ckpt is not None:
+        if not a.tokenizer:
+            tok_from_dir = ckpt.tokenizer()
+        ckpt.close()
     eng = LLMEngine(w, KernelOps() if cuda else TorchOps(), dev, sched, cache,
                     EngineOptions(max_context=a.max_context, graph_sizes=EngineOptions().graph_sizes if cuda else ()))
-    tok = Tokenizer.from_file(a.tokenizer) if a.tokenizer else synthetic_byte_tokenizer()
+    tok = Tokenizer.from_file(a.tokenizer) if a.tokenizer else (tok_from_dir or synthetic_byte_tokenizer())
     svc = EngineService(eng, tok, default_limits(spec.vocab, a.max_context))
     svc.start()
 

@@ -82,9 +82,12 @@ def memory_plan(spec: LlamaSpec, tp: int, ep: int, max_context: int, max_batch: 
 
 
 def admit(spec: LlamaSpec, tp: int = 1, ep: int = 1, max_context: int = 4096, max_batch: int = 256,
-          step_tokens: int = 8192, device_bytes: int = 0, reserve_fraction: float = 0.05) -> Admission:
-    """Checks the model against the kernels, the parallel plan and (when
-    device_bytes > 0) the memory of one device; every failed check is listed."""
+          step_tokens: int = 8192, device_bytes: int = 0, reserve_fraction: float = 0.05,
+          kernels: bool = True) -> Admission:
+    """Checks the model against the kernels (``kernels``: the sm_100a operator
+    set; the CPU reference operators take any shape), the parallel plan and
+    (when device_bytes > 0) the memory of one device; every failed check is
+    listed."""
     reasons: List[Rejection] = []
     details: List[str] = []
 
@@ -92,9 +95,9 @@ def admit(spec: LlamaSpec, tp: int = 1, ep: int = 1, max_context: int = 4096, ma
         reasons.append(r)
         details.append(msg)
 
-    if spec.head_dim != 128:
+    if kernels and spec.head_dim != 128:
         no(Rejection.HEAD_DIM, f"head_dim {spec.head_dim} (kernels support 128)")
-    if spec.heads // spec.kv_heads > 16:
+    if kernels and spec.heads // spec.kv_heads > 16:
         no(Rejection.GQA_GROUP, f"{spec.heads // spec.kv_heads} query heads per KV head (at most 16)")
     if not 1 <= tp <= 8:
         no(Rejection.TP_WORLD, f"tensor-parallel degree {tp} (1..8 in one NVSwitch domain)")
@@ -109,9 +112,9 @@ def admit(spec: LlamaSpec, tp: int = 1, ep: int = 1, max_context: int = 4096, ma
             no(Rejection.TP_VOCAB, f"vocab {spec.vocab} over {tp} ranks")
     if ep > 1 and (not spec.is_moe or spec.experts % ep):
         no(Rejection.EP_EXPERTS, f"{spec.experts} experts over {ep} expert-parallel ranks")
-    if spec.fp8_block and (spec.hidden % 128 or (spec.ffn // max(tp, 1)) % 128 or (spec.heads * spec.head_dim) % 128):
+    if kernels and spec.fp8_block and (spec.hidden % 128 or (spec.ffn // max(tp, 1)) % 128 or (spec.heads * spec.head_dim) % 128):
         no(Rejection.FP8_BLOCK, "fp8 projections need hidden, per-rank ffn and heads*head_dim multiples of 128")
-    if spec.hidden % 256:
+    if kernels and spec.hidden % 256:
         no(Rejection.GEMM_ALIGN, f"hidden {spec.hidden} is not a multiple of 256")
     if max_context > spec.max_position:
         no(Rejection.CONTEXT, f"context {max_context} beyond max_position {spec.max_position}")

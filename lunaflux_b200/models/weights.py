@@ -173,7 +173,13 @@ def build_runtime(spec: LlamaSpec, source: Source, shard: Optional[TPShard] = No
     D = spec.head_dim
 
     def get(name):
-        return source(name).to(device=device)
+        # the source's own tensor (a zero-copy view of a memory-mapped file for
+        # checkpoints): slicing it first means only this rank's bytes are read
+        return source(name)
+
+    def dev(t, dt=None):
+        # always a copy: the runtime weights never alias the source (a mapped file)
+        return t.to(device=device, dtype=dt or dtype, copy=True).contiguous()
 
     def rows(t, r):
         return t[r.start:r.stop]
@@ -184,15 +190,15 @@ def build_runtime(spec: LlamaSpec, source: Source, shard: Optional[TPShard] = No
     layers = []
     for i in range(spec.layers):
         p = layer_prefix(i)
-        q = get(p + "self_attn.q_proj.weight")[hr.start * D:hr.stop * D]
-        k = get(p + "self_attn.k_proj.weight")[kr.start * D:kr.stop * D]
-        v = get(p + "self_attn.v_proj.weight")[kr.start * D:kr.stop * D]
-        wqkv = torch.cat([q, k, v], 0).to(dtype).contiguous()
-        wo = get(p + "self_attn.o_proj.weight")[:, hr.start * D:hr.stop * D].to(dtype).contiguous()
-        lw = LayerWeights(ln1=get(p + "input_layernorm.weight").to(dtype).contiguous(), wqkv=wqkv, wo=wo,
-                          ln2=get(p + "post_attention_layernorm.weight").to(dtype).contiguous())
+        q = dev(get(p + "self_attn.q_proj.weight")[hr.start * D:hr.stop * D])
+        k = dev(get(p + "self_attn.k_proj.weight")[kr.start * D:kr.stop * D])
+        v = dev(get(p + "self_attn.v_proj.weight")[kr.start * D:kr.stop * D])
+        wqkv = torch.cat([q, k, v], 0).contiguous()
+        wo = dev(get(p + "self_attn.o_proj.weight")[:, hr.start * D:hr.stop * D])
+        lw = LayerWeights(ln1=dev(get(p + "input_layernorm.weight")), wqkv=wqkv, wo=wo,
+                          ln2=dev(get(p + "post_attention_layernorm.weight")))
         if spec.is_moe:
-            lw.router = get(p + "block_sparse_moe.gate.weight").to(torch.float32).contiguous()
+            lw.router = dev(get(p + "block_sparse_moe.gate.weight"), torch.float32)
             e_per = spec.experts // ep_size
             gus, ds = [], []
             for e in range(ep_rank * e_per, (ep_rank + 1) * e_per):
@@ -202,15 +208,15 @@ def build_runtime(spec: LlamaSpec, source: Source, shard: Optional[TPShard] = No
                 d = get(qq + "w2.weight")
                 if ep_size == 1:
                     g, u, d = rows(g, fr), rows(u, fr), d[:, fr.start:fr.stop]
-                gus.append(interleave_gate_up(g, u).to(dtype))
-                ds.append(pad_cols(d, -(-d.shape[1] // SWIGLU_GROUP) * SWIGLU_GROUP).to(dtype))
+                gus.append(interleave_gate_up(dev(g), dev(u)))
+                ds.append(pad_cols(dev(d), -(-d.shape[1] // SWIGLU_GROUP) * SWIGLU_GROUP))
             lw.experts_gu = torch.stack(gus).contiguous()
             lw.experts_d = torch.stack(ds).contiguous()
         else:
-            g = rows(get(p + "mlp.gate_proj.weight"), fr)
-            u = rows(get(p + "mlp.up_proj.weight"), fr)
-            lw.wgu = interleave_gate_up(g, u).to(dtype).contiguous()
-            lw.wd = pad_cols(get(p + "mlp.down_proj.weight")[:, fr.start:fr.stop], shard.ffn_padded).to(dtype).contiguous()
+            g = dev(rows(get(p + "mlp.gate_proj.weight"), fr))
+            u = dev(rows(get(p + "mlp.up_proj.weight"), fr))
+            lw.wgu = interleave_gate_up(g, u).contiguous()
+            lw.wd = pad_cols(dev(get(p + "mlp.down_proj.weight")[:, fr.start:fr.stop]), shard.ffn_padded).contiguous()
         if spec.fp8_block and not spec.is_moe:
             # Block-scaled fp8 projections: quantise in the runtime layout (after
             # sharding and the gate/up interleave) and drop the bf16 copies.
@@ -220,10 +226,10 @@ def build_runtime(spec: LlamaSpec, source: Source, shard: Optional[TPShard] = No
                 lw.fp8[name] = quantize_weight(getattr(lw, name))
                 setattr(lw, name, None)
         layers.append(lw)
-    embed = get("model.embed_tokens.weight").to(dtype).contiguous()
+    embed = dev(get("model.embed_tokens.weight"))
     head_name = "model.embed_tokens.weight" if spec.tie_embeddings else "lm_head.weight"
     vr = shard.vocab_range
-    lm_head = get(head_name)[vr.start:vr.stop].to(dtype).contiguous()
+    lm_head = dev(get(head_name)[vr.start:vr.stop])
     return ModelWeights(spec=spec, shard=shard, embed=embed, layers=layers,
-                        norm=get("model.norm.weight").to(dtype).contiguous(), lm_head=lm_head,
+                        norm=dev(get("model.norm.weight")), lm_head=lm_head,
                         ep_rank=ep_rank, ep_size=ep_size)

@@ -1,0 +1,63 @@
+"""Model directories: sharded safetensors + index + config.json, loaded per
+tensor-parallel rank from memory-mapped shards; the engine on the loaded
+weights equals the oracle on the original tensors."""
+import json
+import os
+
+import pytest
+import torch
+
+from lunaflux_b200.models.checkpoint import CheckpointDir, CheckpointError, save_sharded
+from lunaflux_b200.models.config_reader import to_config
+from lunaflux_b200.models.spec import tiny_llama
+from lunaflux_b200.models.weights import build_runtime, random_checkpoint
+
+
+@pytest.mark.parametrize("shard_bytes", [1 << 30, 40000])
+def test_sharded_dir_roundtrip_and_engine(tmp_path, shard_bytes):
+    from lunaflux_b200.config import CacheConfig, SchedulerConfig
+    from lunaflux_b200.engine.engine import EngineOptions, LLMEngine
+    from lunaflux_b200.oracle.reference import ReferenceModel
+    from lunaflux_b200.ops.torch_ops import TorchOps
+    spec = tiny_llama()
+    ck = random_checkpoint(spec, 3)
+    files = save_sharded(ck, str(tmp_path), max_shard_bytes=shard_bytes, config=to_config(spec))
+    assert (len(files) == 1) == (shard_bytes == 1 << 30)
+    with CheckpointDir(str(tmp_path)) as d:
+        assert d.names() == sorted(ck)
+        loaded_spec = d.spec(dtype="fp32")
+        assert loaded_spec.hidden == spec.hidden and loaded_spec.layers == spec.layers
+        for n in ck:
+            assert torch.equal(d.tensor(n), ck[n])
+        w = build_runtime(loaded_spec, d.source(), device="cpu", dtype=torch.float32)
+        eng = LLMEngine(w, TorchOps(), "cpu", SchedulerConfig(), CacheConfig(),
+                        EngineOptions(max_context=256, num_pages=64, graph_sizes=()))
+        prompt = [7, 19, 3, 200, 41]
+        assert eng.generate([prompt], 8)[0] == ReferenceModel(spec, ck).generate_greedy(prompt, 8)
+        assert len(d.content_digest()) == 64
+        with pytest.raises(CheckpointError):
+            d.tensor("model.nope.weight")
+
+
+def test_rejects_inconsistent_directories(tmp_path):
+    spec = tiny_llama()
+    ck = random_checkpoint(spec, 0)
+    save_sharded(ck, str(tmp_path / "a"), max_shard_bytes=40000)
+    idx_path = tmp_path / "a" / "model.safetensors.index.json"
+    idx = json.loads(idx_path.read_text())
+    first = next(iter(idx["weight_map"]))
+    other = [f for f in set(idx["weight_map"].values()) if f != idx["weight_map"][first]][0]
+    idx["weight_map"][first] = other           # points at a shard that does not hold it
+    idx_path.write_text(json.dumps(idx))
+    with pytest.raises(CheckpointError):
+        CheckpointDir(str(tmp_path / "a"))
+    # the same tensor in two files without an index
+    from lunaflux_b200.models.safetensors import save_file
+    os.makedirs(tmp_path / "b")
+    save_file({"x": torch.ones(2)}, str(tmp_path / "b" / "one.safetensors"))
+    save_file({"x": torch.ones(2)}, str(tmp_path / "b" / "two.safetensors"))
+    with pytest.raises(CheckpointError):
+        CheckpointDir(str(tmp_path / "b"))
+    os.makedirs(tmp_path / "c")
+    with pytest.raises(CheckpointError):
+        CheckpointDir(str(tmp_path / "c"))

@@ -94,3 +94,57 @@ def test_config_reader_rejections():
 def test_doctor_runs(capsys):
     cli.doctor()
     assert "readiness:" in capsys.readouterr().out
+
+
+def test_serve_model_dir_end_to_end(tmp_path):
+    """`lunaflux serve --model-dir` on a Hugging Face style directory (sharded
+    safetensors + index + config.json), driven over the framed TCP protocol;
+    the served tokens equal the oracle's."""
+    import asyncio
+    import subprocess
+    import sys
+
+    from lunaflux_b200.contracts.inference import CompletedEvent, FailedEvent, GenerateRequest
+    from lunaflux_b200.models.checkpoint import save_sharded
+    from lunaflux_b200.models.config_reader import to_config
+    from lunaflux_b200.models.spec import tiny_llama
+    from lunaflux_b200.models.weights import random_checkpoint
+    from lunaflux_b200.oracle.reference import ReferenceModel
+    from lunaflux_b200.service.framed_wire import EVENT_HEADER, EVENT_MAGIC, FrameReader, decode_event, encode_request
+    spec = tiny_llama()
+    ck = random_checkpoint(spec, 5)
+    save_sharded(ck, str(tmp_path / "m"), max_shard_bytes=50000, config=to_config(spec))
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    p = subprocess.Popen([sys.executable, "-m", "lunaflux_b200", "serve", "--model-dir", str(tmp_path / "m"),
+                          "--port", "0", "--max-context", "256"], stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                         text=True, env=env)
+    try:
+        port = None
+        for _ in range(200):
+            line = p.stdout.readline()
+            if "serving" in line:
+                port = int(line.strip().rsplit(":", 1)[1])
+                break
+        assert port, "server did not start"
+        prompt = (3, 9, 27, 81, 243 % 256)
+
+        async def client():
+            r, w = await asyncio.open_connection("127.0.0.1", port)
+            w.write(encode_request(GenerateRequest(1, input_tokens=prompt, max_new_tokens=6)))
+            await w.drain()
+            fr = FrameReader(EVENT_MAGIC, header=EVENT_HEADER)
+            evs = []
+            while not evs or not isinstance(evs[-1], (CompletedEvent, FailedEvent)):
+                data = await asyncio.wait_for(r.read(65536), 60)
+                assert data
+                evs.extend(decode_event(f, 1) for f in fr.feed(data))
+            w.close()
+            return evs
+
+        evs = asyncio.run(client())
+        toks = [e.token_id for e in evs if hasattr(e, "token_id")]
+        assert isinstance(evs[-1], CompletedEvent)
+        assert toks == ReferenceModel(spec, ck).generate_greedy(list(prompt), 6)
+    finally:
+        p.kill()
+        p.wait(timeout=30)
