@@ -155,26 +155,51 @@ def build_host_step(plan: StepPlan, table_matrix: np.ndarray, P: int, W: int, ou
             slots[nd:] = -1
             bt[nd:] = 0
         put("d_seqlen", seql)
-    # --- sampling rows
+    # --- sampling rows (columns gathered in one pass, written field by field)
     sidx = view("s_idx")
     params = view("s_params").view(PARAM_DTYPE) if Rs else np.zeros(0, dtype=PARAM_DTYPE)
     any_stoch = False
     if Rs:
-        params[:] = np.zeros(Rs, dtype=PARAM_DTYPE)
+        params[:] = 0
         qs_arr = view("p_qstart") if Rp else None
-        pi = {id(r): i for i, r in enumerate(pr)}
-        di = {id(r): i for i, r in enumerate(dr)}
-        for j, r in enumerate(srows):
-            sidx[j] = (qs_arr[pi[id(r)] + 1] - 1) if not r.decode else Tp + di[id(r)]
+        idx, mode, topk, temp, topp, seed, count = [], [], [], [], [], [], []
+        p_i = d_i = 0
+        for r in plan.rows:
+            if r.decode:
+                row_last = Tp + d_i
+                d_i += 1
+            else:
+                row_last = int(qs_arr[p_i + 1]) - 1
+                p_i += 1
+            if not r.sample:
+                continue
             sp = r.req.sampling
+            idx.append(row_last)
+            seed.append(sp.seed)
+            count.append(len(r.req.output))
             if sp.mode.value == 1:
                 any_stoch = True
-                params[j] = (1, sp.top_k or 0, sp.temperature, sp.top_p if sp.top_p is not None else 1.0,
-                             sp.seed, len(r.req.output))
+                mode.append(1)
+                topk.append(sp.top_k or 0)
+                temp.append(sp.temperature)
+                topp.append(sp.top_p if sp.top_p is not None else 1.0)
             else:
-                params[j] = (0, 0, 1.0, 1.0, sp.seed, len(r.req.output))
-        if Rs > len(srows):
-            sidx[len(srows):] = np.arange(Tp + len(srows), Tp + Rs, dtype=np.int32)
+                mode.append(0)
+                topk.append(0)
+                temp.append(1.0)
+                topp.append(1.0)
+        n = len(idx)
+        sidx[:n] = idx
+        params["mode"][:n] = mode
+        params["top_k"][:n] = topk
+        params["temperature"][:n] = temp
+        params["top_p"][:n] = topp
+        params["seed"][:n] = seed
+        params["sample_index"][:n] = count
+        if Rs > n:
+            sidx[n:] = np.arange(Tp + n, Tp + Rs, dtype=np.int32)
+            params["temperature"][n:] = 1.0
+            params["top_p"][n:] = 1.0
     host_meta = {}
     if Rp:
         host_meta["q_start"] = view("p_qstart").copy()

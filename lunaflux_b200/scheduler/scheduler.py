@@ -41,6 +41,9 @@ from ..kv.page_allocator import OutOfPages, PageAllocator, PageId
 from ..prefix.radix import PrefixIdentity, PrefixIndex
 
 
+_TERMINAL_STATES = frozenset(st for st in RequestState if st.terminal)
+
+
 class SchedulerError(RuntimeError):
     pass
 
@@ -409,32 +412,38 @@ class Scheduler:
         self.in_flight = None
         now = self.clock()
         outs: List[TokenOutput] = []
+        append = outs.append
+        toks = [int(t) for t in sampled]
+        terminal = _TERMINAL_STATES
+        DECODE = RequestState.DECODE
         si = 0
         for row in plan.rows:
             tok = None
             if row.sample:
-                tok = int(sampled[si])
+                tok = toks[si]
                 si += 1
             req = row.req
-            if req.generation != row.generation or req.state.terminal:
+            if req.generation != row.generation or req.state in terminal:
                 continue  # stale: cancelled / expired while in flight
             req.num_computed = row.start + row.n
             if not row.decode:
                 self.prompt_tokens_computed += row.n
                 if req.num_computed == req.prefill_target:
-                    req.state = RequestState.DECODE
+                    req.state = DECODE
             if tok is None:
                 continue
-            req.output.append(tok)
+            out = req.output
+            out.append(tok)
             if req.first_token_time is None:
                 req.first_token_time = now
             req.last_token_time = now
+            total = len(req.prompt) + len(out)
             reason = None
             if tok in req.stop_ids:
                 reason = FinishReason.STOP_SEQUENCE
-            elif len(req.output) >= req.max_new or req.total_len >= req.context_ceiling:
+            elif len(out) >= req.max_new or total >= req.context_ceiling:
                 reason = FinishReason.TOKEN_LIMIT
-            outs.append(TokenOutput(req.rid, tok, req.total_len - 1, reason is not None, reason))
+            append(TokenOutput(req.rid, tok, total - 1, reason is not None, reason))
             if reason is not None:
                 self._finish(req, RequestState.FINISHED, reason, None)
         return outs
