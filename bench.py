@@ -35,7 +35,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_VALUE = None  # the reference publishes no number
+BASELINE_VALUE = None  # the reference publishes no throughput number
 METRIC = "output tok/s/box at 1/2/4/8 B200 (max over ranks); p50 TTFT; p50 TPOT"
 
 
