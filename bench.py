@@ -57,6 +57,8 @@ def parse():
                     help="row-parallel all-reduce: fused into the GEMM kernel, or NCCL after it")
     ap.add_argument("--sp", action="store_true",
                     help="sequence parallelism (residual stream sharded by tokens; library reduce-scatter / all-gather)")
+    ap.add_argument("--overlap", action="store_true",
+                    help="overlapped steps: plan and launch step n+1 before step n's tokens reach the host")
     ap.add_argument("--json-out", default="")
     ap.add_argument("--profile", default="", help="write a per-kernel time table of one extra pass here")
     return ap.parse_args()
@@ -176,7 +178,7 @@ def main():
     pages = args.requests * (-(-max_ctx // 16)) + 2 * args.requests + 64
     opts = EngineOptions(max_context=max_ctx, num_pages=pages,
                          graph_sizes=() if (args.no_graphs or args.impl != "ours") else EngineOptions().graph_sizes,
-                         sequence_parallel=args.sp)
+                         sequence_parallel=args.sp, overlap_steps=args.overlap and args.impl == "ours")
     engine = LLMEngine(weights, ops, dev, sched, CacheConfig(prefix_enabled=False), opts, comm=comm)
     if args.impl == "ours":
         engine.runner.capture_all(False)
@@ -248,6 +250,7 @@ def main():
         "impl": args.impl,
         "config": {"model": f"{args.model} ({spec.layers} layers)", "global_batch": args.requests,
                    "seq_len": args.prompt_len, "output_len": args.output_len, "parallelism": f"tp{world}", "comm": (args.comm if world > 1 else "none"),
+                   "overlap_steps": bool(args.overlap),
                    "l2": "weights (16 GB) and KV (>10 GB) exceed L2 every step; no flush needed",
                    "engine_iterations_per_step": steps_run / args.steps},
         "ttft_p50_ms": round(statistics.median(ttfts), 2) if ttfts else None,

@@ -39,6 +39,7 @@ class EngineOptions:
     check_errors_every: int = 16
     tokenizer_digest: str = ""
     sequence_parallel: bool = False        # TP only: residual stream sharded by tokens (reduce-scatter / all-gather)
+    overlap_steps: bool = False            # plan and launch step n+1 before step n's tokens reach the host
 
 
 @dataclasses.dataclass
@@ -80,7 +81,10 @@ class LLMEngine:
         self.runner = ModelRunner(weights, ops, device, num_pages, sched.step_token_budget + sched.max_rows_per_step,
                                   sched.max_rows_per_step, opts.max_context, P, opts.graph_sizes, comm=comm,
                                   check_errors_every=opts.check_errors_every,
-                                  sequence_parallel=opts.sequence_parallel)
+                                  sequence_parallel=opts.sequence_parallel, overlap=opts.overlap_steps)
+        if opts.overlap_steps:
+            self.scheduler.max_inflight = 2
+        self._launched: List[tuple] = []       # (plan, runner handle, t0), oldest first
         self.results: Dict[int, RequestResult] = {}
         self.live: Dict[int, Request] = {}
         self._next_rid = 1
@@ -133,25 +137,67 @@ class LLMEngine:
 
     # ------------------------------------------------------------------ loop
     def step(self) -> List[TokenOutput]:
+        """One engine step.  Synchronous by default: plan, run, commit.  With
+        ``overlap_steps`` the next plan is built and launched while the
+        previous step still runs (its decode rows take the pending tokens on
+        the device), and then the previous step is committed, so host work
+        of step n+1 hides behind the device time of step n."""
+        if self.opts.overlap_steps:
+            return self._step_overlap()
         t0 = self.clock()
         plan = self.scheduler.schedule()
         if plan is None:
             self._drain_terminals()
             return []
-        m = self.metrics
-        for r in plan.rows:
-            if not r.decode and r.start == r.req.cached_tokens:
-                m.queue.observe(t0 - r.req.arrival)        # first step of this request
+        self._observe_queue(plan, t0)
         graphs_before = len(self.runner.graphs)
         try:
             sampled = self.runner.execute(plan, self.scheduler.tables.matrix)
         except Exception:
             # a device error word, or a launch that raised: the step's work is
             # void; active requests fail (retryably), waiting ones stay queued
-            self.scheduler.abort_plan(plan)
-            self.scheduler.fail_active(PublicErrorCode.INTERNAL)
-            self._drain_terminals()
+            self._fail(plan)
             raise
+        return self._commit(plan, sampled, t0, graphs_before)
+
+    def _step_overlap(self) -> List[TokenOutput]:
+        t0 = self.clock()
+        graphs_before = len(self.runner.graphs)
+        plan = self.scheduler.schedule()
+        if plan is not None:
+            self._observe_queue(plan, t0)
+            try:
+                handle = self.runner.launch(plan, self.scheduler.tables.matrix)
+            except Exception:
+                self._fail(self._launched[0][0] if self._launched else plan)
+                raise
+            self._launched.append((plan, handle, t0))
+        if not self._launched:
+            self._drain_terminals()
+            return []
+        if plan is not None and len(self._launched) < 2:
+            return []          # the first step of a burst: nothing to commit yet
+        old, handle, ts = self._launched.pop(0)
+        try:
+            sampled = self.runner.wait(handle)
+        except Exception:
+            self._fail(old)
+            raise
+        return self._commit(old, sampled, ts, graphs_before)
+
+    def _fail(self, plan):
+        self._launched = []
+        self.scheduler.abort_plan(plan)
+        self.scheduler.fail_active(PublicErrorCode.INTERNAL)
+        self._drain_terminals()
+
+    def _observe_queue(self, plan, t0):
+        for r in plan.rows:
+            if not r.decode and r.start == r.req.cached_tokens:
+                self.metrics.queue.observe(t0 - r.req.arrival)        # first step of this request
+
+    def _commit(self, plan, sampled, t0, graphs_before) -> List[TokenOutput]:
+        m = self.metrics
         outs = self.scheduler.complete(plan, sampled)
         for cb in self.listeners:
             cb(outs)

@@ -41,7 +41,7 @@ def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tenso
 class ModelRunner:
     def __init__(self, weights: ModelWeights, ops, device, num_pages: int, max_tokens: int, max_rows: int,
                  max_context: int, page: int = 16, graph_sizes: Sequence[int] = (), comm=None,
-                 check_errors_every: int = 16, sequence_parallel: bool = False):
+                 check_errors_every: int = 16, sequence_parallel: bool = False, overlap: bool = False):
         self.w = weights
         self.spec: LlamaSpec = weights.spec
         self.shard = weights.shard
@@ -91,6 +91,10 @@ class ModelRunner:
         self.full_logits = (torch.empty(R, s.vocab, dtype=torch.float32, device=dev)
                             if sh.size > 1 else self.logits)
         self.out_tok = torch.zeros(R, dtype=torch.int32, device=dev)
+        # Overlapped steps: the next step is launched before this one's tokens
+        # reach the host; its decode rows read them here, on the device.
+        self.overlap = bool(overlap)
+        self.prev_tok = torch.zeros(R, dtype=torch.int32, device=dev)
         if s.is_moe:
             self._init_moe(T, dev)
         if s.fp8_block:
@@ -113,7 +117,8 @@ class ModelRunner:
         pin = dev.type == "cuda"
         self.in_host = [torch.zeros(cap, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         self.in_evt = [None, None]
-        self.out_host = torch.zeros(R, dtype=torch.int32, pin_memory=pin)
+        self.out_host = [torch.zeros(R, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self._oflip = 0
         self._flip = 0
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         self.graph_launches: Dict[tuple, int] = {}
@@ -127,8 +132,8 @@ class ModelRunner:
         self.d2h_bytes = 0
         self.device_ms = 0.0          # sum over steps of device time from first kernel to sampled ids
         if dev.type == "cuda":
-            self._ev_begin = torch.cuda.Event(enable_timing=True)
-            self._ev_end = torch.cuda.Event(enable_timing=True)
+            self._ev_begin = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            self._ev_end = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
 
     # ------------------------------------------------------------------ forward
     def _layer_kv(self, l):
@@ -136,8 +141,25 @@ class ModelRunner:
 
     def forward(self, v: Dict[str, torch.Tensor], T: int, Tp: int, Rp: int, Rd: int, Rs: int, max_q_len: int,
                 splits: int, stochastic: bool, host_meta=None, gather: bool = True):
+        if self.overlap and Rd:
+            self._forward_tokens(v, Tp, Rd)
         if self.sp:
-            return self.forward_sp(v, T, Tp, Rp, Rd, Rs, max_q_len, splits, stochastic, host_meta, gather)
+            out = self.forward_sp(v, T, Tp, Rp, Rd, Rs, max_q_len, splits, stochastic, host_meta, gather)
+        else:
+            out = self._forward_tp(v, T, Tp, Rp, Rd, Rs, max_q_len, splits, stochastic, host_meta, gather)
+        if self.overlap:
+            self.prev_tok[:Rs].copy_(out)
+        return out
+
+    def _forward_tokens(self, v, Tp: int, Rd: int):
+        """Decode rows whose input token was sampled by the previous step (not
+        yet on the host) take it from that step's output on the device."""
+        f = v["d_fwd"][:Rd]
+        tok = v["tokens"][Tp:Tp + Rd]
+        g = torch.index_select(self.prev_tok, 0, torch.clamp(f, 0, self.prev_tok.numel() - 1))
+        tok.copy_(torch.where(f >= 0, g, tok))
+
+    def _forward_tp(self, v, T, Tp, Rp, Rd, Rs, max_q_len, splits, stochastic, host_meta=None, gather=True):
         ops, s, w = self.ops, self.spec, self.w
         eps = s.rms_eps
         resid, h, delta = self.resid[:T], self.h[:T], self.delta[:T]
@@ -389,6 +411,12 @@ class ModelRunner:
             torch.cuda.nvtx.range_pop()
 
     def _execute(self, plan: StepPlan, table_matrix: np.ndarray) -> np.ndarray:
+        return self.wait(self.launch(plan, table_matrix))
+
+    def launch(self, plan: StepPlan, table_matrix: np.ndarray):
+        """Packs and uploads the step, launches it (graph replay or eager
+        forward) and queues the copy of its sampled ids to pinned host memory.
+        Returns a handle for ``wait``; nothing here waits for the device."""
         rows = plan.rows
         decode_only = all(r.decode for r in rows)
         stoch = any(r.sample and r.req.sampling.mode.value == 1 for r in rows)
@@ -403,8 +431,12 @@ class ModelRunner:
             self.in_evt[slot].synchronize()  # the previous upload from this pinned block has finished
         host_buf = self.in_host[slot]
         hs = build_host_step(plan, table_matrix, self.P, self.W, host_buf.numpy(), bucket=bucket)
+        if hs.any_forwarded and not self.overlap:
+            raise ValueError("a step forwards device tokens but the runner was built without overlap")
         L = hs.layout
         Rs_real = sum(1 for r in rows if r.sample)
+        oslot = self._oflip
+        self._oflip ^= 1
         if bucket is not None:
             key = (bucket, stoch)
             g = self.graphs.get(key)
@@ -414,35 +446,46 @@ class ModelRunner:
                 self.last_capture_s = time.perf_counter() - t0
             self._upload(hs, host_buf)
             self._record_upload(slot)
-            self._begin_step()
+            self._begin_step(oslot)
             g.replay()
             self.ops.launches += self.graph_launches[key]
         else:
             self._upload(hs, host_buf)
             self._record_upload(slot)
-            self._begin_step()
+            self._begin_step(oslot)
             v = device_views(self.in_dev, L)
             Tp = L.T - L.Rd
             splits = self.ops.decode_splits(L.Rd, self.Hkv, max(hs.max_seq, 1)) if L.Rd else 1
             self.forward(v, L.T, Tp, L.Rp, L.Rd, L.Rs, hs.max_q_len, splits, stoch, hs.host_meta)
         out = self.out_tok[:Rs_real]
+        dst = self.out_host[oslot][:Rs_real]
+        done = None
         if self.device.type == "cuda":
-            self._ev_end.record()
-            self.out_host[:Rs_real].copy_(out, non_blocking=True)
-            torch.cuda.current_stream(self.device).synchronize()
-            self.device_ms += self._ev_begin.elapsed_time(self._ev_end)
-            res = self.out_host[:Rs_real].numpy().copy()
+            self._ev_end[oslot].record()
+            dst.copy_(out, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record()
         else:
-            res = out.numpy().copy()
+            dst.copy_(out)
         self.d2h_bytes += Rs_real * 4
+        return (oslot, Rs_real, done)
+
+    def wait(self, handle) -> np.ndarray:
+        """Waits for a launched step and returns its sampled ids (sampling
+        rows, plan order)."""
+        oslot, Rs_real, done = handle
+        if done is not None:
+            done.synchronize()
+            self.device_ms += self._ev_begin[oslot].elapsed_time(self._ev_end[oslot])
+        res = self.out_host[oslot][:Rs_real].numpy().copy()
         self.steps += 1
         if self.check_every and self.steps % self.check_every == 0:
             self.check_device_errors()
         return res
 
-    def _begin_step(self):
+    def _begin_step(self, oslot: int):
         if self.device.type == "cuda":
-            self._ev_begin.record()
+            self._ev_begin[oslot].record()
 
     def _record_upload(self, slot):
         if self.device.type == "cuda":
@@ -461,6 +504,9 @@ class ModelRunner:
         the fixed offsets of ``make_layout(bucket, 0, bucket, bucket, W)``."""
         L = make_layout(bucket, 0, bucket, bucket, self.W)
         v = device_views(self.in_dev, L)
+        # a capture in the middle of overlapped steps must not lose the
+        # in-flight step's tokens (the warm-up passes overwrite them)
+        saved_prev = self.prev_tok.clone() if self.overlap else None
         splits = self.ops.decode_splits(bucket, self.Hkv, self.max_context)
         splits = min(splits, self.max_splits)
         # inputs for warm-up: every row a padded row (zero page, no KV write)
@@ -488,6 +534,8 @@ class ModelRunner:
         self.graph_launches[(bucket, stochastic)] = getattr(self.ops, "launches", 0) - before
         self.ops.launches = before
         self.graphs[(bucket, stochastic)] = g
+        if saved_prev is not None:
+            self.prev_tok.copy_(saved_prev)
         return g
 
     def capture_all(self, stochastic: bool = False):

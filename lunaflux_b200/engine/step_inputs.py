@@ -48,7 +48,7 @@ class Layout:
 
 def make_layout(T: int, Rp: int, Rd: int, Rs: int, W: int) -> Layout:
     fields = [("tokens", T), ("positions", T), ("slots", T), ("p_qstart", Rp + 1), ("p_seqlen", Rp),
-              ("p_bt", Rp * W), ("d_tok", Rd), ("d_seqlen", Rd), ("d_bt", Rd * W), ("s_idx", Rs),
+              ("p_bt", Rp * W), ("d_tok", Rd), ("d_seqlen", Rd), ("d_bt", Rd * W), ("d_fwd", Rd), ("s_idx", Rs),
               ("s_params", Rs * PARAM_INTS)]
     offs = []
     o = 0
@@ -67,6 +67,7 @@ class HostStep:
     any_stochastic: bool
     host_meta: Dict[str, np.ndarray]
     graph_bucket: Optional[int]
+    any_forwarded: bool = False     # some decode row reads its input token on the device
 
 
 def row_tokens(r: Row) -> np.ndarray:
@@ -139,7 +140,10 @@ def build_host_step(plan: StepPlan, table_matrix: np.ndarray, P: int, W: int, ou
         toks = view("tokens")[Tp:]
         pos = view("positions")[Tp:]
         slots = view("slots")[Tp:]
+        fwd = view("d_fwd")
+        fwd[:] = -1
         if nd:
+            fwd[:nd] = np.fromiter((r.fwd for r in dr), dtype=np.int32, count=nd)
             starts = np.fromiter((r.start for r in dr), dtype=np.int64, count=nd)
             tbl = np.fromiter((r.req.table.index for r in dr), dtype=np.int64, count=nd)
             toks[:nd] = np.fromiter((r.req.output[-1] if r.req.output else r.req.prompt[-1] for r in dr),
@@ -159,6 +163,7 @@ def build_host_step(plan: StepPlan, table_matrix: np.ndarray, P: int, W: int, ou
     sidx = view("s_idx")
     params = view("s_params").view(PARAM_DTYPE) if Rs else np.zeros(0, dtype=PARAM_DTYPE)
     any_stoch = False
+    any_fwd = bool(nd) and any(r.fwd >= 0 for r in dr)
     if Rs:
         params[:] = 0
         qs_arr = view("p_qstart") if Rp else None
@@ -176,7 +181,7 @@ def build_host_step(plan: StepPlan, table_matrix: np.ndarray, P: int, W: int, ou
             sp = r.req.sampling
             idx.append(row_last)
             seed.append(sp.seed)
-            count.append(len(r.req.output))
+            count.append(r.sample_index)
             if sp.mode.value == 1:
                 any_stoch = True
                 mode.append(1)
@@ -207,7 +212,7 @@ def build_host_step(plan: StepPlan, table_matrix: np.ndarray, P: int, W: int, ou
     if Rd:
         host_meta["d_seq_lens"] = view("d_seqlen").copy()
         host_meta["d_tok"] = view("d_tok").copy()
-    return HostStep(L, buf, max_q, max_seq, any_stoch, host_meta, bucket)
+    return HostStep(L, buf, max_q, max_seq, any_stoch, host_meta, bucket, any_fwd)
 
 
 def device_views(dev: torch.Tensor, L: Layout) -> Dict[str, torch.Tensor]:

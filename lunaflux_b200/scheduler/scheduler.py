@@ -72,6 +72,13 @@ class Request:
     table: Optional[TableId] = None
     pages: List[PageId] = dataclasses.field(default_factory=list)
     num_computed: int = 0
+    # Planning state, ahead of num_computed / output while steps are in
+    # flight: the KV length once every scheduled row has run, the sampled
+    # tokens not yet returned, and where the newest of them sits in its
+    # step's sampling order (its next decode row reads it on the device).
+    sched_len: int = 0
+    pending: int = 0
+    pending_slot: int = -1
     cached_tokens: int = 0
     output: List[int] = dataclasses.field(default_factory=list)
     prefix_nodes: list = dataclasses.field(default_factory=list)
@@ -106,6 +113,8 @@ class Row:
     sample: bool          # whether the row produces a token
     decode: bool
     generation: int
+    sample_index: int = 0     # index of the sampled token in the request's output
+    fwd: int = -1             # decode input taken on the device from the previous step's sample slot
 
 
 @dataclasses.dataclass
@@ -166,7 +175,11 @@ class Scheduler:
         self.step_seq = 0
         self.generation = 0
         self.terminals: List[Terminal] = []
-        self.in_flight: Optional[StepPlan] = None
+        # Plans handed to the device and not yet completed, oldest first.  With
+        # max_inflight = 2 the next step is planned while the current one runs:
+        # its decode rows read the pending tokens on the device.
+        self.inflight: List[StepPlan] = []
+        self.max_inflight = 1
         # metrics
         self.preemptions = 0
         self.prompt_tokens_computed = 0
@@ -194,7 +207,7 @@ class Scheduler:
         self.waiting.append(req)
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self.inflight)
 
     # ------------------------------------------------------------------ lifecycle
     def cancel(self, rid: int) -> bool:
@@ -220,7 +233,7 @@ class Scheduler:
             self.generation += 1
             req.generation = self.generation
             self._finish(req, RequestState.FAILED, None, code)
-        self.in_flight = None
+        self.inflight = []
 
     def take_terminals(self) -> List[Terminal]:
         t, self.terminals = self.terminals, []
@@ -286,6 +299,15 @@ class Scheduler:
     def _preempt(self, req: Request):
         self.running.remove(req)
         self._release_kv(req, publish=False)
+        # Rows of this request still in flight become stale and their tokens
+        # are recomputed after re-admission.  Its pages may go to a request of
+        # a later plan: that plan runs after the in-flight one on the same
+        # stream, so the stale writes land first and are overwritten.
+        self.generation += 1
+        req.generation = self.generation
+        req.pending = 0
+        req.pending_slot = -1
+        req.sched_len = 0
         req.num_computed = 0
         req.cached_tokens = 0
         req.state = RequestState.WAITING
@@ -301,6 +323,7 @@ class Scheduler:
         req.table = self.tables.allocate()
         req.pages = []
         req.num_computed = 0
+        req.sched_len = 0
         if self.prefix is not None and req.cache_enabled:
             seq_len = req.prefill_target
             toks = [req.token_at(i) for i in range(seq_len)]
@@ -315,6 +338,7 @@ class Scheduler:
                 self.tables.append_pages(req.table, pids)
                 req.pages = pids
                 req.num_computed = len(pids) * self.P
+                req.sched_len = req.num_computed
                 req.cached_tokens = req.num_computed
                 self.prefix_hit_tokens += req.num_computed
         self.waiting.remove(req)
@@ -324,7 +348,7 @@ class Scheduler:
 
     def schedule(self) -> Optional[StepPlan]:
         """Builds the next step plan (None when idle)."""
-        if self.in_flight is not None:
+        if len(self.inflight) >= self.max_inflight:
             raise SchedulerError("previous plan not completed")
         self.expire_deadlines()
         if not self.running and not self.waiting:
@@ -341,13 +365,17 @@ class Scheduler:
                 continue
             if len(decode_rows) >= max_rows or budget <= 0:
                 break
-            need = self._pages_needed(req, req.num_computed + 1)
+            produced = len(req.output) + req.pending
+            if produced >= req.max_new or len(req.prompt) + produced >= req.context_ceiling:
+                continue        # its last token is still in flight; it finishes on completion
+            need = self._pages_needed(req, req.sched_len + 1)
             if need and not self._make_room(need, req):
                 continue
             if req not in self.running:
                 continue
-            self._grow(req, req.num_computed + 1)
-            decode_rows.append(Row(req, req.num_computed, 1, True, True, req.generation))
+            self._grow(req, req.sched_len + 1)
+            decode_rows.append(Row(req, req.sched_len, 1, True, True, req.generation,
+                                   fwd=req.pending_slot if req.pending else -1))
             budget -= 1
         # drop rows whose request was preempted while making room for a later one
         decode_rows = [r for r in decode_rows if r.req in self.running]
@@ -370,36 +398,49 @@ class Scheduler:
                         break
                 if not self._admit(req):
                     break
-            chunk = min(req.prefill_target - req.num_computed, cfg.prefill_chunk_tokens, budget)
+            chunk = min(req.prefill_target - req.sched_len, cfg.prefill_chunk_tokens, budget)
             if chunk <= 0:
                 continue
-            need = self._pages_needed(req, req.num_computed + chunk)
+            need = self._pages_needed(req, req.sched_len + chunk)
             if need > self.allocator.free_page_count():
                 if self.prefix is not None:
                     self.prefix.evict(need - self.allocator.free_page_count())
                 if need > self.allocator.free_page_count():
-                    chunk = (len(req.pages) + self.allocator.free_page_count()) * self.P - req.num_computed
+                    chunk = (len(req.pages) + self.allocator.free_page_count()) * self.P - req.sched_len
                     if chunk <= 0:
                         if is_new:
                             self._preempt_new(req)
                         break
-            self._grow(req, req.num_computed + chunk)
-            final = req.num_computed + chunk == req.prefill_target
-            prefill_rows.append(Row(req, req.num_computed, chunk, final and not req.output, False, req.generation))
+            self._grow(req, req.sched_len + chunk)
+            final = req.sched_len + chunk == req.prefill_target
+            prefill_rows.append(Row(req, req.sched_len, chunk, final and not req.output, False, req.generation))
             budget -= chunk
             rows_used += 1
 
         rows = prefill_rows + decode_rows
         if not rows:
             return None
+        # advance the planning state (the committed state moves on completion)
+        slot = 0
+        for r in rows:
+            req = r.req
+            req.sched_len = r.start + r.n
+            if not r.decode and req.sched_len == req.prefill_target:
+                req.state = RequestState.DECODE
+            if r.sample:
+                r.sample_index = len(req.output) + req.pending
+                req.pending += 1
+                req.pending_slot = slot
+                slot += 1
         self.step_seq += 1
         plan = StepPlan(self.step_seq, rows)
-        self.in_flight = plan
+        self.inflight.append(plan)
         return plan
 
     def _preempt_new(self, req: Request):
         self.running.remove(req)
         self._release_kv(req, publish=False)
+        req.sched_len = 0
         req.state = RequestState.WAITING
         self.waiting.appendleft(req)
 
@@ -407,15 +448,14 @@ class Scheduler:
     def complete(self, plan: StepPlan, sampled: Sequence[int]) -> List[TokenOutput]:
         """Commits a finished step: ``sampled[i]`` is the token of the i-th
         sampling row, in plan order."""
-        if self.in_flight is not plan:
-            raise SchedulerError("completion for a plan that is not in flight")
-        self.in_flight = None
+        if not self.inflight or self.inflight[0] is not plan:
+            raise SchedulerError("completion for a plan that is not the oldest in flight")
+        self.inflight.pop(0)
         now = self.clock()
         outs: List[TokenOutput] = []
         append = outs.append
         toks = [int(t) for t in sampled]
         terminal = _TERMINAL_STATES
-        DECODE = RequestState.DECODE
         si = 0
         for row in plan.rows:
             tok = None
@@ -428,10 +468,9 @@ class Scheduler:
             req.num_computed = row.start + row.n
             if not row.decode:
                 self.prompt_tokens_computed += row.n
-                if req.num_computed == req.prefill_target:
-                    req.state = DECODE
             if tok is None:
                 continue
+            req.pending -= 1
             out = req.output
             out.append(tok)
             if req.first_token_time is None:
@@ -449,9 +488,10 @@ class Scheduler:
         return outs
 
     def abort_plan(self, plan: StepPlan):
-        """The step failed on the device: no state advances."""
-        if self.in_flight is plan:
-            self.in_flight = None
+        """The step failed on the device: the plan (and any planned after it)
+        is dropped; the caller fails the active requests."""
+        if plan in self.inflight:
+            self.inflight = self.inflight[:self.inflight.index(plan)]
 
     # ------------------------------------------------------------------ diagnostics
     def debug_check_invariants(self):

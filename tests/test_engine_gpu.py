@@ -19,7 +19,7 @@ def bf16_checkpoint(spec, seed=0):
     return {k: v.bfloat16().float() for k, v in ck.items()}
 
 
-def make_engine(spec, ck, graphs=True, budget=256, rows=8, prefix=False):
+def make_engine(spec, ck, graphs=True, budget=256, rows=8, prefix=False, overlap=False):
     from lunaflux_b200.config import CacheConfig, SchedulerConfig
     from lunaflux_b200.engine.engine import EngineOptions, LLMEngine
     from lunaflux_b200.models.weights import build_runtime
@@ -27,7 +27,8 @@ def make_engine(spec, ck, graphs=True, budget=256, rows=8, prefix=False):
     w = build_runtime(spec, lambda n: ck[n], device="cuda", dtype=torch.bfloat16)
     sched = SchedulerConfig(step_token_budget=budget, max_active_requests=rows, prefill_chunk_tokens=budget,
                             emergency_decode_page_reserve=4)
-    opts = EngineOptions(max_context=1024, num_pages=512, graph_sizes=(1, 2, 4, 8) if graphs else ())
+    opts = EngineOptions(max_context=1024, num_pages=512, graph_sizes=(1, 2, 4, 8) if graphs else (),
+                         overlap_steps=overlap)
     return LLMEngine(w, KernelOps(), "cuda", sched, CacheConfig(prefix_enabled=prefix), opts)
 
 
@@ -91,6 +92,22 @@ def test_decode_steps_allocate_nothing():
     assert torch.cuda.memory_stats()["allocation.all.allocated"] == before
     assert eng.runner.last_bucket is not None      # the steps replayed a captured graph
     assert eng.runner.ops.read_error(True)[0] == 0
+
+
+def test_overlapped_steps_equal_synchronous():
+    """Overlapped steps (decode inputs forwarded on the device, inside the
+    captured graphs) give the synchronous engine's tokens exactly."""
+    from lunaflux_b200.contracts import SamplingParameters
+    spec = small_spec()
+    ck = bf16_checkpoint(spec, seed=8)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, spec.vocab, (n,), generator=g).tolist() for n in (7, 50, 130, 260, 19)]
+    for sp in (None, SamplingParameters.sample(0.8, top_k=40, top_p=0.95, seed=5)):
+        a = make_engine(spec, ck).generate(prompts, 16, sp)
+        eng = make_engine(spec, ck, overlap=True)
+        b = eng.generate(prompts, 16, sp)
+        assert a == b
+        assert eng.runner.ops.read_error(True)[0] == 0
 
 
 def test_stochastic_is_reproducible():
