@@ -57,8 +57,9 @@ def parse():
                     help="row-parallel all-reduce: fused into the GEMM kernel, or NCCL after it")
     ap.add_argument("--sp", action="store_true",
                     help="sequence parallelism (residual stream sharded by tokens; library reduce-scatter / all-gather)")
-    ap.add_argument("--overlap", action="store_true",
-                    help="overlapped steps: plan and launch step n+1 before step n's tokens reach the host")
+    ap.add_argument("--no-overlap", dest="overlap", action="store_false",
+                    help="synchronous steps (default: overlapped, step n+1 planned and launched before step n's "
+                         "tokens reach the host)")
     ap.add_argument("--json-out", default="")
     ap.add_argument("--profile", default="", help="write a per-kernel time table of one extra pass here")
     return ap.parse_args()

@@ -21,7 +21,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, sp=False):
+def _worker(rank, world, port, q, sp=False, overlap=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -38,7 +38,8 @@ def _worker(rank, world, port, q, sp=False):
         w = build_runtime(spec, lambda n: ck[n], TPShard(rank, world, spec))
         eng = LLMEngine(w, TorchOps(), "cpu", SchedulerConfig(step_token_budget=64, max_active_requests=4,
                                                               prefill_chunk_tokens=64, emergency_decode_page_reserve=1),
-                        CacheConfig(), EngineOptions(max_context=256, num_pages=64, graph_sizes=(), sequence_parallel=sp),
+                        CacheConfig(), EngineOptions(max_context=256, num_pages=64, graph_sizes=(), sequence_parallel=sp,
+                                                    overlap_steps=overlap),
                         comm=TPComm())
         assert eng.runner.sp == sp
         g = torch.Generator().manual_seed(0)
@@ -49,11 +50,12 @@ def _worker(rank, world, port, q, sp=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,sp", [(2, False), (4, False), (2, True), (4, True)])
-def test_tp_matches_oracle(world, sp):
-    """TP alone, and TP with sequence parallelism (the residual stream sharded
+@pytest.mark.parametrize("world,sp,overlap", [(2, False, False), (4, False, False), (2, True, False),
+                                               (4, True, False), (2, False, True)])
+def test_tp_matches_oracle(world, sp, overlap):
+    """TP alone, TP with sequence parallelism (the residual stream sharded
     by tokens between a reduce-scatter and an all-gather, odd token counts
-    padded to a multiple of the world size)."""
+    padded to a multiple of the world size), and TP with overlapped steps."""
     from lunaflux_b200.models.spec import LlamaSpec
     from lunaflux_b200.models.weights import random_checkpoint
     from lunaflux_b200.oracle.reference import ReferenceModel
@@ -62,7 +64,7 @@ def test_tp_matches_oracle(world, sp):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, sp)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, sp, overlap)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=240) for _ in range(world))
