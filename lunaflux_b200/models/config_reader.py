@@ -6,8 +6,12 @@ admission rules: strict JSON (duplicate keys rejected); executable metadata
 fields rejected; untied embeddings; ``rope_scaling`` and ``sliding_window``
 null; ``hidden_act`` silu; no attention / MLP bias; ``pretraining_tp`` 1.
 Added: ``model_type == "mixtral"`` with ``num_local_experts`` and
-``num_experts_per_tok``, and a ``quantization_config`` for block-scaled fp8
-(``quant_method == "fp8"``, ``weight_block_size == [128, 128]``).
+``num_experts_per_tok``, a ``quantization_config`` for block-scaled fp8
+(``quant_method == "fp8"``, ``weight_block_size == [128, 128]``), and the
+field names newer ``transformers`` releases write: ``dtype`` (for
+``torch_dtype``) and ``rope_parameters`` (``{"rope_type": "default",
+"rope_theta": ...}``; any other rope type is rejected like a non-null
+``rope_scaling``).
 """
 from __future__ import annotations
 
@@ -31,9 +35,9 @@ _SEMANTIC = {"architectures", "model_type", "vocab_size", "hidden_size", "interm
              "num_local_experts", "num_experts_per_tok", "router_aux_loss_coef", "output_router_logits",
              "router_jitter_noise",
              # fp8
-             "quantization_config"}
+             "quantization_config", "rope_parameters"}
 _INERT = {"_name_or_path", "transformers_version", "bos_token_id", "eos_token_id", "pad_token_id",
-          "initializer_range", "use_cache"}
+          "initializer_range", "use_cache", "dtype"}
 
 
 def _int(d, k, required=True, default=None):
@@ -84,6 +88,16 @@ def parse_config(text: str | bytes, dtype: str = "bf16") -> LlamaSpec:
         raise ConfigReaderError("attention_dropout must be 0")
     if d.get("pretraining_tp", 1) != 1:
         raise ConfigReaderError("pretraining_tp must be 1")
+    rope_theta = _num(d, "rope_theta", 10000.0)
+    rp = d.get("rope_parameters")
+    if rp is not None:
+        if not isinstance(rp, dict) or rp.get("rope_type", "default") != "default" or \
+                set(rp) - {"rope_type", "rope_theta"}:
+            raise ConfigReaderError("rope_parameters: only the default rope type is supported")
+        if "rope_theta" in rp:
+            if "rope_theta" in d and _num(d, "rope_theta") != _num(rp, "rope_theta"):
+                raise ConfigReaderError("rope_theta and rope_parameters disagree")
+            rope_theta = _num(rp, "rope_theta")
     hidden = _int(d, "hidden_size")
     heads = _int(d, "num_attention_heads")
     kv = _int(d, "num_key_value_heads", default=heads)
@@ -103,7 +117,7 @@ def parse_config(text: str | bytes, dtype: str = "bf16") -> LlamaSpec:
     try:
         return LlamaSpec(hidden=hidden, layers=_int(d, "num_hidden_layers"), heads=heads, kv_heads=kv,
                          head_dim=head_dim, ffn=_int(d, "intermediate_size"), vocab=_int(d, "vocab_size"),
-                         rope_theta=_num(d, "rope_theta", 10000.0), rms_eps=_num(d, "rms_norm_eps", 1e-5),
+                         rope_theta=rope_theta, rms_eps=_num(d, "rms_norm_eps", 1e-5),
                          max_position=_int(d, "max_position_embeddings", default=4096), dtype=dtype,
                          experts=experts, experts_per_token=topk, fp8_block=fp8)
     except SpecError as e:

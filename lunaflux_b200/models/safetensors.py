@@ -133,8 +133,14 @@ class SafetensorsFile:
         return (st.st_size, st.st_mtime_ns) == self._stamp
 
     def close(self):
+        """Closes the file.  While tensors returned by ``tensor()`` are alive
+        the mapping stays (they are views of it) and is unmapped when the
+        last of them is freed."""
         if self._mm is not None:
-            self._mm.close()
+            try:
+                self._mm.close()
+            except BufferError:
+                pass
             self._mm = None
         self._f.close()
 

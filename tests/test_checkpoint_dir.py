@@ -61,3 +61,17 @@ def test_rejects_inconsistent_directories(tmp_path):
     os.makedirs(tmp_path / "c")
     with pytest.raises(CheckpointError):
         CheckpointDir(str(tmp_path / "c"))
+
+
+def test_config_reader_newer_transformers_fields():
+    from lunaflux_b200.models.config_reader import ConfigReaderError, parse_config
+    base = to_config(tiny_llama())
+    base.pop("torch_dtype")
+    base.pop("rope_theta")
+    d = dict(base, dtype="float32", rope_parameters={"rope_type": "default", "rope_theta": 5e5})
+    assert parse_config(json.dumps(d)).rope_theta == 5e5
+    for bad in ({"rope_type": "llama3", "rope_theta": 5e5, "factor": 8.0}, {"rope_type": "default", "x": 1}, [1]):
+        with pytest.raises(ConfigReaderError):
+            parse_config(json.dumps(dict(base, rope_parameters=bad)))
+    with pytest.raises(ConfigReaderError):
+        parse_config(json.dumps(dict(base, rope_theta=1e4, rope_parameters={"rope_theta": 5e5})))
