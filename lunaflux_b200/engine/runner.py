@@ -19,7 +19,7 @@ from typing import Dict, List, Optional, Sequence
 import numpy as np
 import torch
 
-from ..models.spec import LlamaSpec
+from ..models.spec import LlamaSpec, rope_inv_freq
 from ..models.weights import ModelWeights
 from ..scheduler.scheduler import StepPlan
 from .step_inputs import HostStep, build_host_step, device_views, make_layout
@@ -32,10 +32,12 @@ class StepFailed(RuntimeError):
         self.info = info
 
 
-def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
-    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+def rope_table(max_pos: int, head_dim: int, theta: float, device=None, scaling: tuple = ()) -> torch.Tensor:
+    """[max_pos, head_dim / 2, (cos, sin)] fp32, angles in float64."""
+    inv = rope_inv_freq(head_dim, theta, scaling)
     ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None]
-    return torch.stack([ang.cos(), ang.sin()], -1).float().contiguous().to(device)
+    t = torch.stack([ang.cos(), ang.sin()], -1).float().contiguous()
+    return t if device is None else t.to(device)
 
 
 class ModelRunner:
@@ -63,7 +65,7 @@ class ModelRunner:
         dev = self.device
         # KV arena: [layer][K/V][page][kv_head][16][D]
         self.kv = torch.zeros(s.layers, 2, self.num_pages, self.Hkv, page, self.D, dtype=dt, device=dev)
-        self.cos_sin = rope_table(s.max_position, s.head_dim, s.rope_theta, dev)
+        self.cos_sin = rope_table(s.max_position, s.head_dim, s.rope_theta, dev, s.rope_scaling)
         T, R = max_tokens, max_rows
         self.resid = torch.empty(T, H, dtype=dt, device=dev)
         self.h = torch.empty(T, H, dtype=dt, device=dev)

@@ -9,9 +9,11 @@ Added: ``model_type == "mixtral"`` with ``num_local_experts`` and
 ``num_experts_per_tok``, a ``quantization_config`` for block-scaled fp8
 (``quant_method == "fp8"``, ``weight_block_size == [128, 128]``), and the
 field names newer ``transformers`` releases write: ``dtype`` (for
-``torch_dtype``) and ``rope_parameters`` (``{"rope_type": "default",
-"rope_theta": ...}``; any other rope type is rejected like a non-null
-``rope_scaling``).
+``torch_dtype``) and ``rope_parameters``.  RoPE scaling: the reference
+requires ``rope_scaling`` null; here the Llama 3.1 rule (``rope_type``
+"llama3" with ``factor``, ``low_freq_factor``, ``high_freq_factor`` and
+``original_max_position_embeddings``) is also accepted, in ``rope_scaling``
+or in ``rope_parameters``; every other scaling type is rejected.
 """
 from __future__ import annotations
 
@@ -56,6 +58,32 @@ def _num(d, k, default=None):
     return float(v)
 
 
+_LLAMA3_KEYS = {"factor", "low_freq_factor", "high_freq_factor", "original_max_position_embeddings"}
+
+
+def _rope_scaling(v, where: str) -> tuple:
+    """() for no scaling (null, or rope type "default"), else the spec tuple."""
+    if v is None:
+        return ()
+    if not isinstance(v, dict):
+        raise ConfigReaderError(f"{where} must be an object or null")
+    kind = v.get("rope_type", v.get("type", "default"))
+    extra = set(v) - {"rope_type", "type"}
+    if kind == "default":
+        if extra:
+            raise ConfigReaderError(f"{where}: unexpected fields for the default rope type")
+        return ()
+    if kind != "llama3":
+        raise ConfigReaderError(f"{where}: rope type {kind!r} is not supported (default or llama3)")
+    if extra != _LLAMA3_KEYS:
+        raise ConfigReaderError(f"{where}: llama3 scaling needs exactly {sorted(_LLAMA3_KEYS)}")
+    factor, low, high = _num(v, "factor"), _num(v, "low_freq_factor"), _num(v, "high_freq_factor")
+    orig = _int(v, "original_max_position_embeddings")
+    if not (factor >= 1.0 and 0 < low < high):
+        raise ConfigReaderError(f"{where}: llama3 scaling needs factor >= 1 and 0 < low_freq_factor < high_freq_factor")
+    return ("llama3", factor, low, high, orig)
+
+
 def parse_config(text: str | bytes, dtype: str = "bf16") -> LlamaSpec:
     try:
         d: Dict[str, Any] = loads_strict(text)
@@ -76,9 +104,8 @@ def parse_config(text: str | bytes, dtype: str = "bf16") -> LlamaSpec:
         raise ConfigReaderError("exactly one architecture is required")
     if d.get("tie_word_embeddings", False) is not False:
         raise ConfigReaderError("tied embeddings are not supported")
-    for k in ("rope_scaling", "sliding_window"):
-        if d.get(k) is not None:
-            raise ConfigReaderError(f"{k} must be null")
+    if d.get("sliding_window") is not None:
+        raise ConfigReaderError("sliding_window must be null")
     if d.get("hidden_act", "silu") != "silu":
         raise ConfigReaderError("hidden_act must be silu")
     for k in ("attention_bias", "mlp_bias"):
@@ -89,15 +116,19 @@ def parse_config(text: str | bytes, dtype: str = "bf16") -> LlamaSpec:
     if d.get("pretraining_tp", 1) != 1:
         raise ConfigReaderError("pretraining_tp must be 1")
     rope_theta = _num(d, "rope_theta", 10000.0)
+    scaling = _rope_scaling(d.get("rope_scaling"), "rope_scaling")
     rp = d.get("rope_parameters")
     if rp is not None:
-        if not isinstance(rp, dict) or rp.get("rope_type", "default") != "default" or \
-                set(rp) - {"rope_type", "rope_theta"}:
-            raise ConfigReaderError("rope_parameters: only the default rope type is supported")
+        if not isinstance(rp, dict):
+            raise ConfigReaderError("rope_parameters must be an object")
         if "rope_theta" in rp:
             if "rope_theta" in d and _num(d, "rope_theta") != _num(rp, "rope_theta"):
                 raise ConfigReaderError("rope_theta and rope_parameters disagree")
             rope_theta = _num(rp, "rope_theta")
+        sc = _rope_scaling({k: v for k, v in rp.items() if k != "rope_theta"}, "rope_parameters")
+        if scaling and sc and sc != scaling:
+            raise ConfigReaderError("rope_scaling and rope_parameters disagree")
+        scaling = scaling or sc
     hidden = _int(d, "hidden_size")
     heads = _int(d, "num_attention_heads")
     kv = _int(d, "num_key_value_heads", default=heads)
@@ -119,7 +150,7 @@ def parse_config(text: str | bytes, dtype: str = "bf16") -> LlamaSpec:
                          head_dim=head_dim, ffn=_int(d, "intermediate_size"), vocab=_int(d, "vocab_size"),
                          rope_theta=rope_theta, rms_eps=_num(d, "rms_norm_eps", 1e-5),
                          max_position=_int(d, "max_position_embeddings", default=4096), dtype=dtype,
-                         experts=experts, experts_per_token=topk, fp8_block=fp8)
+                         experts=experts, experts_per_token=topk, fp8_block=fp8, rope_scaling=scaling)
     except SpecError as e:
         raise ConfigReaderError(str(e)) from None
 
@@ -131,7 +162,10 @@ def to_config(spec: LlamaSpec) -> Dict[str, Any]:
          "intermediate_size": spec.ffn, "num_hidden_layers": spec.layers, "num_attention_heads": spec.heads,
          "num_key_value_heads": spec.kv_heads, "head_dim": spec.head_dim,
          "max_position_embeddings": spec.max_position, "rope_theta": spec.rope_theta, "rms_norm_eps": spec.rms_eps,
-         "tie_word_embeddings": False, "hidden_act": "silu", "rope_scaling": None,
+         "tie_word_embeddings": False, "hidden_act": "silu",
+         "rope_scaling": None if not spec.rope_scaling else {
+             "rope_type": "llama3", "factor": spec.rope_scaling[1], "low_freq_factor": spec.rope_scaling[2],
+             "high_freq_factor": spec.rope_scaling[3], "original_max_position_embeddings": spec.rope_scaling[4]},
          "torch_dtype": "bfloat16" if spec.dtype == "bf16" else "float32"}
     if spec.is_moe:
         d["num_local_experts"] = spec.experts

@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import dataclasses
 import hashlib
+import math
 from typing import Optional
 
 DENSE_PLAN_SCHEMA = "lunaflux.dense-llama-plan.v2.full-context"
@@ -43,6 +44,9 @@ class LlamaSpec:
     # Block-scaled fp8 projections: e4m3 weights with one fp32 scale per
     # 128x128 block, e4m3 activations with one scale per token per 128 channels.
     fp8_block: int = 0
+    # RoPE frequency scaling: () for none, or ("llama3", factor, low_freq_factor,
+    # high_freq_factor, original_max_position) as in Llama 3.1 / 3.2 / 3.3.
+    rope_scaling: tuple = ()
 
     def __post_init__(self):
         pos = [self.hidden, self.layers, self.heads, self.kv_heads, self.head_dim, self.ffn, self.vocab,
@@ -61,6 +65,13 @@ class LlamaSpec:
             raise SpecError("experts_per_token must be in (0, experts]")
         if self.fp8_block not in (0, 128):
             raise SpecError("fp8 block size must be 128")
+        if self.rope_scaling:
+            rs = self.rope_scaling
+            if len(rs) != 5 or rs[0] != "llama3":
+                raise SpecError("rope_scaling must be () or ('llama3', factor, low, high, original_max_position)")
+            _, factor, low, high, orig = rs
+            if not (factor >= 1.0 and 0 < low < high and int(orig) > 0):
+                raise SpecError("llama3 rope scaling needs factor >= 1, 0 < low_freq_factor < high_freq_factor")
 
     # -- derived sizes ------------------------------------------------------
     @property
@@ -97,7 +108,9 @@ class LlamaSpec:
     # -- digests --------------------------------------------------------------
     def canonical_encoding(self, schema: Optional[str] = None) -> bytes:
         schema = schema or (MOE_PLAN_SCHEMA if self.is_moe else DENSE_PLAN_SCHEMA)
-        fields = [("schema", schema)] + [(f.name, getattr(self, f.name)) for f in dataclasses.fields(self)]
+        # rope_scaling is encoded only when set, so unscaled specs keep their digests
+        fields = [("schema", schema)] + [(f.name, getattr(self, f.name)) for f in dataclasses.fields(self)
+                                         if f.name != "rope_scaling" or self.rope_scaling]
         return "\n".join(f"{k}={_canon(v)}" for k, v in fields).encode("utf-8")
 
     def plan_digest(self) -> str:
@@ -113,6 +126,8 @@ class LlamaSpec:
 
 
 def _canon(v) -> str:
+    if isinstance(v, tuple):
+        return "(" + ",".join(_canon(x) for x in v) + ")"
     if isinstance(v, bool):
         return "true" if v else "false"
     if isinstance(v, float):
@@ -134,6 +149,12 @@ def llama3_8b(dtype: str = "bf16", layers: int = 32) -> LlamaSpec:
                      rope_theta=500000.0, rms_eps=1e-5, max_position=8192, dtype=dtype)
 
 
+def llama31_8b(dtype: str = "bf16", layers: int = 32) -> LlamaSpec:
+    """Llama 3.1 8B: the Llama 3 8B shape with 128K context through RoPE scaling."""
+    return dataclasses.replace(llama3_8b(dtype, layers), max_position=131072,
+                               rope_scaling=("llama3", 8.0, 1.0, 4.0, 8192))
+
+
 def llama3_70b(fp8: bool = True, layers: int = 80) -> LlamaSpec:
     return LlamaSpec(hidden=8192, layers=layers, heads=64, kv_heads=8, head_dim=128, ffn=28672, vocab=128256,
                      rope_theta=500000.0, rms_eps=1e-5, max_position=8192, dtype="bf16",
@@ -149,6 +170,25 @@ def mixtral_8x7b(layers: int = 32) -> LlamaSpec:
 PRESETS = {
     "tiny-llama": tiny_llama,
     "llama3-8b": llama3_8b,
+    "llama3.1-8b": llama31_8b,
     "llama3-70b-fp8": llama3_70b,
     "mixtral-8x7b": mixtral_8x7b,
 }
+
+
+def rope_inv_freq(head_dim: int, theta: float, scaling: tuple = ()):
+    """Per-pair RoPE frequencies (float64 tensor of head_dim / 2): theta^(-2i/D),
+    with Llama 3.1's frequency scaling when ``scaling`` is set (Meta's published
+    rule: wavelengths shorter than original_max_position / high_freq_factor
+    keep their frequency, those longer than original_max_position /
+    low_freq_factor are divided by ``factor``, and the band in between is
+    interpolated linearly in original_max_position / wavelength)."""
+    import torch
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    if not scaling:
+        return inv
+    _, factor, low, high, orig = scaling
+    wavelen = 2.0 * math.pi / inv
+    ratio = float(orig) / wavelen
+    smooth = ((ratio - low) / (high - low)).clamp(0.0, 1.0)
+    return (1.0 - smooth) * inv / factor + smooth * inv

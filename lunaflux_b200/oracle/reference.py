@@ -14,7 +14,7 @@ from typing import Dict, List, Sequence
 
 import torch
 
-from ..models.spec import LlamaSpec
+from ..models.spec import LlamaSpec, rope_inv_freq
 from ..models.weights import checkpoint_names, layer_prefix
 
 
@@ -22,8 +22,8 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
 
 
-def rope_angles(positions: torch.Tensor, head_dim: int, theta: float, dtype=torch.float64):
-    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+def rope_angles(positions: torch.Tensor, head_dim: int, theta: float, dtype=torch.float64, scaling: tuple = ()):
+    inv = rope_inv_freq(head_dim, theta, scaling)
     ang = positions.to(torch.float64)[:, None] * inv[None, :]
     return ang.cos().to(dtype), ang.sin().to(dtype)
 
@@ -87,7 +87,7 @@ class ReferenceModel:
         ids = torch.tensor(list(tokens), dtype=torch.long)
         x = t["model.embed_tokens.weight"][ids]
         T = x.shape[0]
-        cos, sin = rope_angles(torch.arange(T), s.head_dim, s.rope_theta, self.dtype)
+        cos, sin = rope_angles(torch.arange(T), s.head_dim, s.rope_theta, self.dtype, s.rope_scaling)
         scale = 1.0 / math.sqrt(s.head_dim)
         for i in range(s.layers):
             p = layer_prefix(i)

@@ -70,8 +70,23 @@ def test_config_reader_newer_transformers_fields():
     base.pop("rope_theta")
     d = dict(base, dtype="float32", rope_parameters={"rope_type": "default", "rope_theta": 5e5})
     assert parse_config(json.dumps(d)).rope_theta == 5e5
-    for bad in ({"rope_type": "llama3", "rope_theta": 5e5, "factor": 8.0}, {"rope_type": "default", "x": 1}, [1]):
+    for bad in ({"rope_type": "llama3", "rope_theta": 5e5, "factor": 8.0}, {"rope_type": "default", "x": 1}, [1],
+                {"rope_type": "yarn", "factor": 4.0}):
         with pytest.raises(ConfigReaderError):
             parse_config(json.dumps(dict(base, rope_parameters=bad)))
     with pytest.raises(ConfigReaderError):
         parse_config(json.dumps(dict(base, rope_theta=1e4, rope_parameters={"rope_theta": 5e5})))
+
+
+def test_config_reader_llama3_rope_scaling():
+    from lunaflux_b200.models.config_reader import parse_config
+    from lunaflux_b200.models.spec import llama3_8b
+    sc = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+          "original_max_position_embeddings": 8192}
+    base = to_config(llama3_8b())
+    a = parse_config(json.dumps(dict(base, rope_scaling=sc)))
+    assert a.rope_scaling == ("llama3", 8.0, 1.0, 4.0, 8192)
+    b = parse_config(json.dumps(dict(base, rope_scaling=None, rope_parameters=dict(sc, rope_theta=base["rope_theta"]))))
+    assert b == a
+    assert parse_config(json.dumps(to_config(a))) == a
+    assert a.plan_digest() != llama3_8b().plan_digest()
