@@ -13,6 +13,17 @@ longest-first, lowest id on ties, before BPE runs on the text between them.
 The byte <-> symbol alphabet is GPT-2's reversible byte-level map: printable
 Latin-1 bytes stand for themselves, the other 68 bytes are shifted to code
 points 256 and up.
+
+Beyond the reference's subset, the layout of the Llama 3 and GPT-2 style
+tokenizers is accepted too: a pre-tokenizer that splits the text with a
+regular expression before the byte-level map (``Split`` with a ``Regex``
+pattern and ``Isolated`` behaviour followed by ``ByteLevel`` without regex,
+or ``ByteLevel`` with ``use_regex`` and GPT-2's pattern); BPE with
+``ignore_merges`` (a pre-token that is itself in the vocabulary is emitted
+whole); a ``ByteLevel`` / ``TemplateProcessing`` post-processor whose single
+template is an optional leading special token and the sequence (the BOS that
+``encode(..., add_special_tokens=True)`` prepends).  Merge results per
+pre-token are cached.
 """
 from __future__ import annotations
 
@@ -20,6 +31,11 @@ import hashlib
 from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
 from ..utils.json_strict import loads_strict
+
+# GPT-2's pre-tokenisation pattern (ByteLevel with use_regex); it needs the
+# `regex` module's Unicode property classes.
+GPT2_SPLIT = r"""'s|'t|'re|'ve|'m|'ll|'d| ?\p{L}+| ?\p{N}+| ?[^\s\p{L}\p{N}]+|\s+(?!\S)|\s+"""
+_CACHE_MAX = 1 << 16
 
 
 class TokenizerError(ValueError):
@@ -45,8 +61,20 @@ _U2B = {u: b for b, u in _B2U.items()}
 
 class Tokenizer:
     def __init__(self, vocab: Dict[str, int], merges: Sequence[Tuple[str, str]], added: Sequence[Tuple[str, int]] = (),
-                 digest: str = ""):
+                 digest: str = "", split_pattern: Optional[str] = None, ignore_merges: bool = False,
+                 bos_id: Optional[int] = None):
         self.vocab = dict(vocab)
+        self.split_pattern = split_pattern
+        self._split = None
+        if split_pattern is not None:
+            import regex
+            try:
+                self._split = regex.compile(split_pattern)
+            except regex.error as e:
+                raise TokenizerError(f"pre-tokenizer pattern does not compile: {e}") from None
+        self.ignore_merges = bool(ignore_merges)
+        self.bos_id = bos_id
+        self._cache: Dict[bytes, List[int]] = {}
         self.id_to_token: Dict[int, str] = {}
         for t, i in self.vocab.items():
             if i in self.id_to_token:
@@ -78,26 +106,27 @@ class Tokenizer:
         except ImportError:
             pass
         self.vocab_size = max(self.id_to_token) + 1 if self.id_to_token else 0
+        if bos_id is not None and bos_id not in self.id_to_token:
+            raise TokenizerError("the post-processor's special token is not in the vocabulary")
 
     # ------------------------------------------------------------------ loading
     @classmethod
     def from_json(cls, text: str | bytes) -> "Tokenizer":
         raw = text.encode() if isinstance(text, str) else bytes(text)
         d = loads_strict(raw)
-        if d.get("normalizer") is not None or d.get("post_processor") is not None:
-            raise TokenizerError("normalizer and post_processor must be null")
-        for key in ("pre_tokenizer", "decoder"):
-            p = d.get(key)
-            if not isinstance(p, dict) or p.get("type") != "ByteLevel" or p.get("use_regex", True) or \
-                    p.get("add_prefix_space", False):
-                raise TokenizerError(f"{key} must be ByteLevel without regex or prefix space")
+        if d.get("normalizer") is not None:
+            raise TokenizerError("normalizer must be null")
+        split = _pre_tokenizer(d.get("pre_tokenizer"))
+        dec = d.get("decoder")
+        if not isinstance(dec, dict) or dec.get("type") != "ByteLevel":
+            raise TokenizerError("decoder must be ByteLevel")
         m = d.get("model")
         if not isinstance(m, dict) or m.get("type") != "BPE":
             raise TokenizerError("model must be BPE")
         for k in ("dropout", "unk_token", "continuing_subword_prefix", "end_of_word_suffix"):
             if m.get(k) is not None:
                 raise TokenizerError(f"BPE {k} is not supported")
-        for k in ("fuse_unk", "byte_fallback", "ignore_merges"):
+        for k in ("fuse_unk", "byte_fallback"):
             if m.get(k, False):
                 raise TokenizerError(f"BPE {k} is not supported")
         merges = []
@@ -116,7 +145,9 @@ class Tokenizer:
             if a.get("normalized") or a.get("lstrip") or a.get("rstrip") or a.get("single_word"):
                 raise TokenizerError("added-token flags are not supported")
             added.append((a["content"], int(a["id"])))
-        return cls(m["vocab"], merges, added, hashlib.sha256(raw).hexdigest())
+        bos = _post_processor(d.get("post_processor"))
+        return cls(m["vocab"], merges, added, hashlib.sha256(raw).hexdigest(), split_pattern=split,
+                   ignore_merges=bool(m.get("ignore_merges", False)), bos_id=bos)
 
     @classmethod
     def from_file(cls, path: str) -> "Tokenizer":
@@ -155,9 +186,38 @@ class Tokenizer:
                 syms = out
         return [self.vocab[s] for s in syms]
 
-    def encode_bytes(self, data: bytes, allow_special: bool = True) -> List[int]:
+    def _word(self, data: bytes) -> List[int]:
+        """One pre-token (cached)."""
+        ids = self._cache.get(data)
+        if ids is None:
+            whole = self.vocab.get("".join(_B2U[b] for b in data)) if self.ignore_merges else None
+            ids = [whole] if whole is not None else self._bpe(data)
+            if len(self._cache) >= _CACHE_MAX:
+                self._cache.clear()
+            self._cache[data] = ids
+        return ids
+
+    def _segment(self, data: bytes) -> List[int]:
+        """Text between special tokens: pre-tokenise, then BPE per piece."""
+        if self._split is None:
+            return self._word(data) if self.ignore_merges else self._bpe(data)
+        # bytes that are not UTF-8 travel through the split as lone surrogates
+        text = data.decode("utf-8", errors="surrogateescape")
+        ids: List[int] = []
+        for piece in self._split.findall(text):
+            if piece:
+                ids += self._word(piece.encode("utf-8", errors="surrogateescape"))
+        return ids
+
+    def encode_bytes(self, data: bytes, allow_special: bool = True, add_special_tokens: bool = False) -> List[int]:
+        ids = self._encode_bytes(data, allow_special)
+        if add_special_tokens and self.bos_id is not None:
+            ids.insert(0, self.bos_id)
+        return ids
+
+    def _encode_bytes(self, data: bytes, allow_special: bool) -> List[int]:
         if not self.added:
-            return self._bpe(data)
+            return self._segment(data)
         text = data
         ids: List[int] = []
         start = 0
@@ -175,16 +235,18 @@ class Tokenizer:
             if not allow_special:
                 raise TokenizerError("input contains a special token")
             if start < i:
-                ids += self._bpe(text[start:i])
+                ids += self._segment(text[start:i])
             ids.append(hit[1])
             i += len(hit[0])
             start = i
         if start < len(text):
-            ids += self._bpe(text[start:])
+            ids += self._segment(text[start:])
         return ids
 
-    def encode(self, text: str, allow_special: bool = True) -> List[int]:
-        return self.encode_bytes(text.encode("utf-8"), allow_special)
+    def encode(self, text: str, allow_special: bool = True, add_special_tokens: bool = False) -> List[int]:
+        """Token ids of ``text``; ``add_special_tokens`` applies the
+        post-processor's template (a leading BOS when it has one)."""
+        return self.encode_bytes(text.encode("utf-8"), allow_special, add_special_tokens)
 
     # ------------------------------------------------------------------ decode
     def token_bytes(self, tid: int) -> bytes:
@@ -203,6 +265,63 @@ class Tokenizer:
 
     def decode(self, ids: Iterable[int]) -> str:
         return self.decode_bytes(ids).decode("utf-8", errors="replace")
+
+
+def _pre_tokenizer(p) -> Optional[str]:
+    """The split pattern of an accepted pre-tokenizer (None: no split)."""
+    def byte_level(q, allow_regex):
+        if not isinstance(q, dict) or q.get("type") != "ByteLevel" or q.get("add_prefix_space", False):
+            return False
+        return allow_regex or not q.get("use_regex", True)
+
+    if isinstance(p, dict) and p.get("type") == "ByteLevel":
+        if not byte_level(p, True):
+            raise TokenizerError("pre_tokenizer: ByteLevel with a prefix space is not supported")
+        return GPT2_SPLIT if p.get("use_regex", True) else None
+    if isinstance(p, dict) and p.get("type") == "Sequence":
+        seq = p.get("pretokenizers")
+        if isinstance(seq, list) and len(seq) == 2 and byte_level(seq[1], False):
+            sp = seq[0]
+            pat = sp.get("pattern") if isinstance(sp, dict) else None
+            if isinstance(sp, dict) and sp.get("type") == "Split" and isinstance(pat, dict) and \
+                    isinstance(pat.get("Regex"), str) and sp.get("behavior") == "Isolated" and not sp.get("invert"):
+                return pat["Regex"]
+    raise TokenizerError("pre_tokenizer must be ByteLevel, or a regex Split (Isolated) then ByteLevel without regex")
+
+
+def _post_processor(p) -> Optional[int]:
+    """The BOS id of an accepted post-processor (None: nothing is added)."""
+    if p is None:
+        return None
+    if not isinstance(p, dict):
+        raise TokenizerError("post_processor must be an object or null")
+    kind = p.get("type")
+    if kind == "ByteLevel":
+        return None
+    if kind == "Sequence":
+        bos = None
+        for q in p.get("processors") or []:
+            b = _post_processor(q)
+            if b is not None:
+                if bos is not None:
+                    raise TokenizerError("post_processor: more than one template")
+                bos = b
+        return bos
+    if kind == "TemplateProcessing":
+        single = p.get("single")
+        if not isinstance(single, list) or not single or single[-1] != {"Sequence": {"id": "A", "type_id": 0}}:
+            raise TokenizerError("post_processor: the single template must end with the sequence")
+        if len(single) == 1:
+            return None
+        head = single[0].get("SpecialToken") if isinstance(single[0], dict) else None
+        if len(single) != 2 or not isinstance(head, dict):
+            raise TokenizerError("post_processor: only a leading special token is supported")
+        spec = (p.get("special_tokens") or {}).get(head.get("id"))
+        ids = spec.get("ids") if isinstance(spec, dict) else None
+        if not isinstance(ids, list) or len(ids) != 1 or type(ids[0]) is not int:
+            raise TokenizerError("post_processor: the special token needs exactly one id")
+        return ids[0]
+    raise TokenizerError(f"post_processor {kind!r} is not supported")
 
 
 def synthetic_byte_tokenizer(vocab_size: int = 256) -> Tokenizer:

@@ -73,7 +73,13 @@ def test_special_tokens_longest_match():
 
 @pytest.mark.parametrize("override", [
     {"normalizer": {"type": "NFC"}},
-    {"pre_tokenizer": {"type": "ByteLevel", "add_prefix_space": False, "use_regex": True}},
+    {"pre_tokenizer": {"type": "ByteLevel", "add_prefix_space": True, "use_regex": False}},
+    {"pre_tokenizer": {"type": "Sequence", "pretokenizers": [
+        {"type": "Split", "pattern": {"Regex": " "}, "behavior": "Removed", "invert": False},
+        {"type": "ByteLevel", "add_prefix_space": False, "use_regex": False}]}},
+    {"post_processor": {"type": "TemplateProcessing", "single": [{"Sequence": {"id": "A", "type_id": 0}},
+                                                                 {"SpecialToken": {"id": "</s>", "type_id": 0}}]}},
+    {"post_processor": {"type": "BertProcessing"}},
     {"pre_tokenizer": {"type": "Whitespace"}},
 ])
 def test_unsupported_subset_rejected(override):
