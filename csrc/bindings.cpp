@@ -261,12 +261,15 @@ int64_t gemm_plan_splitk(int64_t M, int64_t N, int64_t K) {
 
 int64_t gemm_choose_bn(int64_t M, int64_t N, int64_t epi) { return lf::gemm::choose_bn(M, N, epi); }
 
-// (cluster size, BN, k-blocks per CTA) of the cluster split-K plan; cluster size 0 = plain tiles.
+// (cluster size, BN, k-blocks per CTA, M-blocks per tile) of the cluster split-K plan;
+// cluster size 0 = plain tiles.
 std::vector<int64_t> gemm_plan_cluster(int64_t M, int64_t N, int64_t K, int64_t epi) {
-  int bn = 0, kb = 0;
-  const int c = lf::gemm::plan_cluster(M, N, K, epi, &bn, &kb);
-  return {c, bn, kb};
+  int bn = 0, kb = 0, mb = 1;
+  const int c = lf::gemm::plan_cluster(M, N, K, epi, &bn, &kb, &mb);
+  return {c, bn, kb, mb};
 }
+
+void gemm_set_cluster_mb2(bool on) { lf::gemm::set_cluster_mb2(on ? 1 : 0); }
 
 void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) {
   LF_CHECK(ids.scalar_type() == at::kInt && table.scalar_type() == at::kBFloat16, "embed dtypes");
@@ -438,6 +441,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan_splitk", &gemm_plan_splitk);
   m.def("device_report", &lf::rt::device_report, "devices, compute capability, peer access, NVLink multicast, typed status");
   m.def("gemm_plan_cluster", &gemm_plan_cluster);
+  m.def("gemm_set_cluster_mb2", &gemm_set_cluster_mb2);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("gemm_fp8", &gemm_fp8);

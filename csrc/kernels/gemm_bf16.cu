@@ -35,6 +35,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -173,12 +174,12 @@ int plan_splitk(int M, int N, int K, int* kb_per_out) {
 
 // Cluster split-K (skinny decode GEMMs): one cluster of c CTAs per output
 // tile, the partial tiles summed through distributed shared memory.
-template <int BN, int STAGES, int OUT>
+template <int BN, int STAGES, int OUT, int MB = 1>
 static bool cluster_fits(int c, int clusters) {
-  using S = Smem<BN, STAGES>;
+  using S = Smem<BN, STAGES, MB>;
   static int cached[9] = {0};
   if (cached[c] == 0) {
-    auto kfn = gemm_cluster_splitk_kernel<BN, STAGES, OUT>;
+    auto kfn = gemm_cluster_splitk_kernel<BN, STAGES, OUT, MB>;
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(c * clusters, 1, 1);
@@ -201,10 +202,10 @@ static bool cluster_fits(int c, int clusters) {
   return cached[c] >= clusters;
 }
 
-template <int BN, int STAGES, int OUT>
+template <int BN, int STAGES, int OUT, int MB = 1>
 static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int64_t ldd, cudaStream_t stream) {
-  using S = Smem<BN, STAGES>;
-  auto kfn = gemm_cluster_splitk_kernel<BN, STAGES, OUT>;
+  using S = Smem<BN, STAGES, MB>;
+  auto kfn = gemm_cluster_splitk_kernel<BN, STAGES, OUT, MB>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
@@ -212,7 +213,7 @@ static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int6
   }
   CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
   CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, BN);
-  const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
+  const int tiles = ((a.M + MB * BM - 1) / (MB * BM)) * (a.N / BN);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles * c, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -229,15 +230,64 @@ static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int6
   if (e != cudaSuccess) throw std::runtime_error(std::string("lunaflux cluster gemm launch: ") + cudaGetErrorString(e));
 }
 
+// 256-row cluster tiles (MB = 2) for 129..256-row GEMMs: off unless enabled
+// (LUNAFLUX_GEMM_CLUSTER_MB2=1 or set_cluster_mb2), until measured against
+// the 128-row tiles on every decode shape.
+static int g_cluster_mb2 = -1;
+
+void set_cluster_mb2(int on) { g_cluster_mb2 = on ? 1 : 0; }
+
+static bool cluster_mb2_enabled() {
+  if (g_cluster_mb2 < 0) {
+    const char* e = getenv("LUNAFLUX_GEMM_CLUSTER_MB2");
+    g_cluster_mb2 = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return g_cluster_mb2 == 1;
+}
+
+// 256-row variant: tiles of 256 x 256, so each weight slab is staged once for
+// both M-blocks.  Returns the cluster size (0: not applicable).
+static int plan_cluster_mb2(int M, int N, int K, int epi, int* kb_per_out) {
+  const int sms = num_sms();
+  const int num_kb = (K + BK - 1) / BK;
+  if (M <= BM || M > 2 * BM || N % 256 != 0 || K % 8 != 0) return 0;
+  const int tiles = N / 256;
+  if (tiles >= sms / 2) return 0;
+  int c = sms / tiles;
+  if (c > 8) c = 8;
+  if (c > num_kb / 2) c = num_kb / 2;
+  for (; c >= 2; --c) {
+    const bool fits = epi == kSwiGLU ? cluster_fits<256, 3, kSwiGLU, 2>(c, tiles)
+                      : epi == kStoreF32 ? cluster_fits<256, 3, kStoreF32, 2>(c, tiles)
+                                         : cluster_fits<256, 3, kStoreBf16, 2>(c, tiles);
+    if (fits) break;
+  }
+  if (c < 2) return 0;
+  const int kb_per = (num_kb + c - 1) / c;
+  c = (num_kb + kb_per - 1) / kb_per;  // no empty slice
+  if (c < 2) return 0;
+  *kb_per_out = kb_per;
+  return c;
+}
+
 // Plan: BN 256 when the 256-wide tiles times up to 8 splits reach half of
 // the SMs, else BN 128; as many splits (cluster size, <= 8) as one wave allows, with
 // at least two k-blocks per split; only when the plain tiles would leave more
 // than half of the SMs idle.  Returns the cluster size (0: no split).
-int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out) {
+int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out, int* mb_out) {
   const int sms = num_sms();
   const int num_m = (M + BM - 1) / BM;
   const int num_kb = (K + BK - 1) / BK;
+  if (mb_out != nullptr) *mb_out = 1;
   if (N % 128 != 0 || K % 8 != 0) return 0;
+  if (cluster_mb2_enabled()) {
+    const int c2 = plan_cluster_mb2(M, N, K, epi, kb_per_out);
+    if (c2 >= 2) {
+      *bn_out = 256;
+      if (mb_out != nullptr) *mb_out = 2;
+      return c2;
+    }
+  }
   const int t256 = N % 256 == 0 ? num_m * (N / 256) : 0;
   const int t128 = num_m * (N / 128);
   if ((t256 ? t256 : t128) >= sms / 2) return 0;
@@ -271,10 +321,14 @@ int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out) {
 }
 
 static bool run_cluster(const GemmArgs& a, int epi, void* out, int64_t ldd, cudaStream_t stream) {
-  int bn = 0, kb_per = 0;
-  const int c = plan_cluster(a.M, a.N, a.K, epi, &bn, &kb_per);
+  int bn = 0, kb_per = 0, mb = 1;
+  const int c = plan_cluster(a.M, a.N, a.K, epi, &bn, &kb_per, &mb);
   if (c < 2) return false;
-  if (bn == 256) {
+  if (mb == 2) {
+    if (epi == kSwiGLU) launch_cluster<256, 3, kSwiGLU, 2>(a, c, kb_per, out, ldd, stream);
+    else if (epi == kStoreF32) launch_cluster<256, 3, kStoreF32, 2>(a, c, kb_per, out, ldd, stream);
+    else launch_cluster<256, 3, kStoreBf16, 2>(a, c, kb_per, out, ldd, stream);
+  } else if (bn == 256) {
     if (epi == kSwiGLU) launch_cluster<256, 4, kSwiGLU>(a, c, kb_per, out, ldd, stream);
     else if (epi == kStoreF32) launch_cluster<256, 4, kStoreF32>(a, c, kb_per, out, ldd, stream);
     else launch_cluster<256, 4, kStoreBf16>(a, c, kb_per, out, ldd, stream);

@@ -25,8 +25,11 @@ struct GemmArgs {
 // accepted for interface stability and unused.
 void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws = nullptr, int64_t ws_elems = 0);
 int plan_splitk(int M, int N, int K, int* kb_per_out);
-// Cluster split-K plan: returns the cluster size (0 = plain tiles) and its BN / k-blocks per CTA.
-int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out);
+// Cluster split-K plan: returns the cluster size (0 = plain tiles) and its BN / k-blocks per CTA /
+// 128-row M-blocks per tile.
+int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out, int* mb_out = nullptr);
+// Enables the 256-row cluster tiles for 129..256-row GEMMs (off by default).
+void set_cluster_mb2(int on);
 
 // Peer view of one tensor-parallel group for the fused GEMM + all-reduce.
 // Two symmetric bf16 regions of [rows, N] (every rank holds both, same size):

@@ -463,13 +463,20 @@ struct ClusterRed {
 };
 
 // OUT: kStoreBf16, kStoreF32 or kSwiGLU (interleaved gate/up groups of 32).
-template <int BN, int STAGES, int OUT>
+// MB: 128-row M-blocks per tile.  With MB = 2 (decode batches of 129..256
+// rows) the two MMAs of a k-slab share the staged weight slab, so the weights
+// cross into shared memory once instead of once per M-block; the two partial
+// M-blocks are then reduced one after the other through the same staging
+// buffer (it holds one 128-row partial).
+template <int BN, int STAGES, int OUT, int MB = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_cluster_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M, int N,
                                int K, int ldd, int kb_per_split) {
-  using S = Smem<BN, STAGES>;
+  using S = Smem<BN, STAGES, MB>;
   static_assert(ClusterRed<BN>::kBytes <= STAGES * S::kStageBytes, "partial tile must fit the pipeline buffers");
+  static_assert(MB * BN <= 512, "accumulators must fit TMEM");
+  constexpr int TM = MB * BM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
@@ -482,14 +489,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int c = (int)cluster_nctarank();
   const int r = (int)cluster_ctarank();
-  const int num_m = (M + BM - 1) / BM;
+  const int num_m = (M + TM - 1) / TM;
   const int tile = blockIdx.x / c;
-  const int m0 = (tile % num_m) * BM;
+  const int m0 = (tile % num_m) * TM;
   const int n0 = (tile / num_m) * BN;
   const int num_kb = (K + BK - 1) / BK;
   const int kb0 = r * kb_per_split;
   const int kb1 = min(num_kb, kb0 + kb_per_split);
-  constexpr uint32_t kCols = BN < 32 ? 32 : BN;
+  constexpr uint32_t kCols = MB * BN < 32 ? 32 : MB * BN;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmap_a);
@@ -520,7 +527,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* sa = smem + stage * S::kStageBytes;
         uint8_t* sb = sa + S::kABytes;
         mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
-        tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, m0);
+#pragma unroll
+        for (int j = 0; j < MB; ++j) tma_load_2d(sa + j * BM * BK * 2, &tmap_a, &full_bar[stage], kb * BK, m0 + j * BM);
         tma_load_2d_hint(sb, &tmap_b, &full_bar[stage], kb * BK, n0, pol_b);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
@@ -537,9 +545,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
         const uint32_t sb = sa + S::kABytes;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          umma_f16_ss(tmem_base, sw128_kmajor_desc(sa + kk * 32), sw128_kmajor_desc(sb + kk * 32), idesc,
-                      (kb > kb0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BK / 16; ++kk) {
+#pragma unroll
+          for (int j = 0; j < MB; ++j)
+            umma_f16_ss(tmem_base + j * BN, sw128_kmajor_desc(sa + j * BM * BK * 2 + kk * 32),
+                        sw128_kmajor_desc(sb + kk * 32), idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+        }
         umma_commit(&empty_bar[stage]);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
@@ -548,14 +559,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) umma_commit(tfull_bar);
       else mbar_arrive(tfull_bar);
     }
-  } else {
-    // TMEM -> this CTA's fp32 partial tile in shared memory (row = TMEM lane)
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;
-    const bool have = kb1 > kb0;
-    if (mbar_wait(tfull_bar, 0, 13)) {
-      tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16);
+  }
+  const int quad = warp & 3;
+  const bool have = kb1 > kb0;
+  bool acc_ok = false;
+  if (warp >= 2) {
+    acc_ok = mbar_wait(tfull_bar, 0, 13);
+    if (acc_ok) tc_fence_after();
+  }
+  // Every CTA runs the same 2 * MB cluster barriers below (uniform control flow).
+#pragma unroll 1
+  for (int mb = 0; mb < MB; ++mb) {
+    if (warp >= 2 && acc_ok) {
+      // TMEM -> this CTA's fp32 partial of M-block mb in shared memory (row = TMEM lane)
+      const int row = quad * 32 + lane;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + mb * BN;
       float* dst = red + row * ClusterRed<BN>::kStride;
 #pragma unroll 1
       for (int col = 0; col < BN; col += 32) {
@@ -571,64 +589,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  }
-  // every CTA's partial tile is in its shared memory
-  cluster_sync_all();
-  if (warp >= 2) {
-    const int t = threadIdx.x - 64;
-    const int rows_per = (BM + c - 1) / c;
-    const int r0 = r * rows_per;
-    const int r1 = min(BM, r0 + rows_per);
-    const uint32_t red_base = smem_u32(red);
-    if constexpr (OUT == kSwiGLU) {
-      // thread -> (row, 4 consecutive output features): gate cols g*64 + j,
-      // up cols g*64 + 32 + j of the tile
-      constexpr int kQuads = BN / 2 / 4;
-      for (int i = t; i < (r1 - r0) * kQuads; i += 128) {
-        const int rl = r0 + i / kQuads;
-        const int j = (i % kQuads) * 4;            // output feature within the tile
-        const int gcol = (j / 32) * 64 + (j % 32);
-        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
-        const uint32_t off_g = red_base + (uint32_t)(rl * ClusterRed<BN>::kStride + gcol) * 4;
-        for (int q = 0; q < c; ++q) {
-          const float4 a = ld_shared_cluster_f4(mapa_shared(off_g, q));
-          const float4 b = ld_shared_cluster_f4(mapa_shared(off_g + 32 * 4, q));
-          g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
-          u.x += b.x; u.y += b.y; u.z += b.z; u.w += b.w;
+    // every CTA's partial of this M-block is in its shared memory
+    cluster_sync_all();
+    if (warp >= 2) {
+      const int t = threadIdx.x - 64;
+      const int rows_per = (BM + c - 1) / c;
+      const int r0 = r * rows_per;
+      const int r1 = min(BM, r0 + rows_per);
+      const int mrow0 = m0 + mb * BM;
+      const uint32_t red_base = smem_u32(red);
+      if constexpr (OUT == kSwiGLU) {
+        // thread -> (row, 4 consecutive output features): gate cols g*64 + j,
+        // up cols g*64 + 32 + j of the tile
+        constexpr int kQuads = BN / 2 / 4;
+        for (int i = t; i < (r1 - r0) * kQuads; i += 128) {
+          const int rl = r0 + i / kQuads;
+          const int j = (i % kQuads) * 4;            // output feature within the tile
+          const int gcol = (j / 32) * 64 + (j % 32);
+          float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+          const uint32_t off_g = red_base + (uint32_t)(rl * ClusterRed<BN>::kStride + gcol) * 4;
+          for (int q = 0; q < c; ++q) {
+            const float4 a = ld_shared_cluster_f4(mapa_shared(off_g, q));
+            const float4 b = ld_shared_cluster_f4(mapa_shared(off_g + 32 * 4, q));
+            g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
+            u.x += b.x; u.y += b.y; u.z += b.z; u.w += b.w;
+          }
+          const int grow = mrow0 + rl;
+          if (grow < M) {
+            __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)grow * ldd + n0 / 2 + j;
+            *reinterpret_cast<uint2*>(d) =
+                make_uint2(pack_bf16x2(silu(g.x) * u.x, silu(g.y) * u.y), pack_bf16x2(silu(g.z) * u.z, silu(g.w) * u.w));
+          }
         }
-        const int grow = m0 + rl;
-        if (grow < M) {
-          __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)grow * ldd + n0 / 2 + j;
-          *reinterpret_cast<uint2*>(d) =
-              make_uint2(pack_bf16x2(silu(g.x) * u.x, silu(g.y) * u.y), pack_bf16x2(silu(g.z) * u.z, silu(g.w) * u.w));
-        }
-      }
-    } else {
-      constexpr int kQuads = BN / 4;
-      for (int i = t; i < (r1 - r0) * kQuads; i += 128) {
-        const int rl = r0 + i / kQuads;
-        const int col = (i % kQuads) * 4;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        const uint32_t off = red_base + (uint32_t)(rl * ClusterRed<BN>::kStride + col) * 4;
-        for (int q = 0; q < c; ++q) {
-          const float4 a = ld_shared_cluster_f4(mapa_shared(off, q));
-          acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
-        }
-        const int grow = m0 + rl;
-        if (grow < M) {
-          if constexpr (OUT == kStoreF32) {
-            *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)grow * ldd + n0 + col) = acc;
-          } else {
-            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)grow * ldd + n0 + col) =
-                make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+      } else {
+        constexpr int kQuads = BN / 4;
+        for (int i = t; i < (r1 - r0) * kQuads; i += 128) {
+          const int rl = r0 + i / kQuads;
+          const int col = (i % kQuads) * 4;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          const uint32_t off = red_base + (uint32_t)(rl * ClusterRed<BN>::kStride + col) * 4;
+          for (int q = 0; q < c; ++q) {
+            const float4 a = ld_shared_cluster_f4(mapa_shared(off, q));
+            acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+          }
+          const int grow = mrow0 + rl;
+          if (grow < M) {
+            if constexpr (OUT == kStoreF32) {
+              *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)grow * ldd + n0 + col) = acc;
+            } else {
+              *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)grow * ldd + n0 + col) =
+                  make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+            }
           }
         }
       }
     }
+    // no CTA overwrites its staging buffer (next M-block) or leaves (and
+    // releases its shared memory) while a peer still reads it
+    if (mb + 1 == MB) tc_fence_before();
+    cluster_sync_all();
   }
-  // no CTA leaves (and releases its shared memory) while a peer still reads it
-  tc_fence_before();
-  cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kCols);

@@ -95,9 +95,9 @@ def bench_gemm(C, results, only_case=""):
         flops = 2.0 * M * N * K
         bytes_ = 2.0 * (M * K + N * K) + D.numel() * D.element_size()
         t_roof = max(flops / (tflops_peak * 1e12), bytes_ / (hbm * 1e9)) * 1e3
-        c, cbn, _ = C.gemm_plan_cluster(M, N, K, epi)
+        c, cbn, _, cmb = C.gemm_plan_cluster(M, N, K, epi)
         r = dict(kernel="gemm_bf16", case=name, M=M, N=N, K=K, bn=cbn if c else C.gemm_choose_bn(M, N, epi),
-                 cluster_splitk=c, ours_ms=ours,
+                 cluster_splitk=c, cluster_rows=128 * cmb if c else None, ours_ms=ours,
                  torch_ms=ref, speedup=ref / ours, tflops=flops / ours / 1e9, roofline_ms=t_roof,
                  frac_of_roofline=t_roof / ours, peaks=src)
         results.append(r)

@@ -1,6 +1,8 @@
 """Numerics of every sm_100a kernel against a plain PyTorch fp32 reference."""
 import math
 
+import os
+
 import pytest
 import torch
 
@@ -67,9 +69,13 @@ def test_gemm_splitk(C, M, N, K, epi):
 def test_gemm_cluster_splitk(C, M, N, K, epi):
     """Decode shapes that take the cluster split-K path: values against the fp32
     reference, bitwise reproducibility, and the plan itself."""
-    c, bn, kb = C.gemm_plan_cluster(M, N, K, epi)
-    assert c >= 2, (c, bn, kb)
+    c, bn, kb, mb = C.gemm_plan_cluster(M, N, K, epi)
+    assert c >= 2 and mb == 1, (c, bn, kb, mb)
     assert (c - 1) * kb < (K + 63) // 64 <= c * kb
+    _check_cluster_gemm(C, M, N, K, epi)
+
+
+def _check_cluster_gemm(C, M, N, K, epi):
     A = torch.randn(M, K, device="cuda").bfloat16()
     B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
     out_cols = N // 2 if epi == 2 else N
@@ -84,6 +90,23 @@ def test_gemm_cluster_splitk(C, M, N, K, epi):
     assert torch.equal(first, D)
     _close(D, ref, 3e-2, 3e-2, f"cluster split-K {M}x{N}x{K} epi={epi}")
     assert C.read_error(True)[0] == 0
+
+
+@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
+                    reason="256-row cluster tiles: first GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
+@pytest.mark.parametrize("M,N,K,epi", [(256, 6144, 4096, 0), (256, 4096, 14336, 0), (256, 4096, 4096, 1),
+                                       (129, 1024, 4096, 2), (250, 1536, 1024, 2), (200, 6144, 4096, 1)])
+def test_gemm_cluster_splitk_256_row_tiles(C, M, N, K, epi):
+    """Cluster split-K with 256-row tiles (two MMAs per staged weight slab,
+    the two partial M-blocks reduced in turn): values, reproducibility, plan."""
+    C.gemm_set_cluster_mb2(True)
+    try:
+        c, bn, kb, mb = C.gemm_plan_cluster(M, N, K, epi)
+        assert c >= 2 and mb == 2 and bn == 256, (c, bn, kb, mb)
+        assert (c - 1) * kb < (K + 63) // 64 <= c * kb
+        _check_cluster_gemm(C, M, N, K, epi)
+    finally:
+        C.gemm_set_cluster_mb2(False)
 
 
 @pytest.mark.parametrize("M,N,K,epi", [(200, 10240, 512, 0), (256, 28672, 4096, 2), (129, 32768, 256, 1),
