@@ -231,8 +231,9 @@ static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int6
 }
 
 // 256-row cluster tiles (MB = 2) for 129..256-row GEMMs: off unless enabled
-// (LUNAFLUX_GEMM_CLUSTER_MB2=1 or set_cluster_mb2), until measured against
-// the 128-row tiles on every decode shape.
+// (LUNAFLUX_GEMM_CLUSTER_MB2=1 or set_cluster_mb2).  Measured slower than
+// 128-row tiles on the Llama-3-8B decode shapes (fewer CTAs in flight, two
+// reductions in turn), so the default plan does not use them.
 static int g_cluster_mb2 = -1;
 
 void set_cluster_mb2(int on) { g_cluster_mb2 = on ? 1 : 0; }
