@@ -469,5 +469,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("max_q_len"), py::arg("progress") = 0);
   m.def("read_error", &read_error, py::arg("clear") = true);
   m.def("inject_error", &inject_error);
+  // programmatic dependent launch of the step kernels (off by default; LUNAFLUX_PDL=1)
+  m.def("set_pdl", [](bool on) { lf::rt::set_pdl(on); });
+  m.def("pdl_enabled", []() { return lf::rt::pdl_enabled(); });
   m.def("counter_unit", &counter_unit);
 }

@@ -96,6 +96,8 @@ __device__ __forceinline__ float2 unpack2(uint32_t u) {
 __global__ void __launch_bounds__(256, 2) finalize_ll_kernel(const float* __restrict__ ws, int splits, int M, int N,
                                                              __nv_bfloat16* __restrict__ out, int64_t ldd,
                                                              LLArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t half = N / 2;
   const int64_t P = (int64_t)M * half;
   const int64_t chunk = (P + a.world - 1) / a.world;
@@ -181,7 +183,8 @@ void finalize_ll(const float* ws, int splits, int M, int N, __nv_bfloat16* out, 
   const int64_t want = (pairs / a.world + 255) / 256;
   const int cap = per_sm * sms;
   const int grid = (int)(want < 1 ? 1 : (want < cap ? want : cap));
-  finalize_ll_kernel<<<grid, 256, 0, stream>>>(ws, splits, M, N, out, ldd, a);
+  launch_k(finalize_ll_kernel, dim3(grid), dim3(256), 0, stream, 1,
+         ws, splits, M, N, out, ldd, a);
 }
 
 }  // namespace ar

@@ -106,6 +106,8 @@ constexpr int kDecStages = 4;
 
 __global__ void __launch_bounds__(32) decode_kernel(const __grid_constant__ CUtensorMap tk,
                                                     const __grid_constant__ CUtensorMap tv, DecodeArgs a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * 2 * kPageBytes);
@@ -270,6 +272,8 @@ __global__ void __launch_bounds__(32) decode_kernel(const __grid_constant__ CUte
 
 // Merge split-KV partials: out = sum_s w_s * o_s with w_s = 2^(lse_s - lse_max) / sum.
 __global__ void decode_combine_kernel(DecodeArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x, h = blockIdx.y, d = threadIdx.x;  // blockDim = D
   const float* pl = a.part_lse + ((size_t)r * a.Hq + h) * a.splits;
   float mx = -INFINITY;
@@ -512,8 +516,10 @@ void decode(const DecodeArgs& a_in, const void* kcache, const void* vcache, cuda
   if (a.splits > 1 && (a.part_o == nullptr || a.part_lse == nullptr))
     throw std::runtime_error("lunaflux attention: split-KV decode needs a workspace");
   dim3 grid(a.rows, a.Hkv, a.splits);
-  decode_kernel<<<grid, 32, smem, stream>>>(tk, tv, a);
-  if (a.splits > 1) decode_combine_kernel<<<dim3(a.rows, a.Hq), D, 0, stream>>>(a);
+  launch_k(decode_kernel, dim3(grid), dim3(32), smem, stream, 1,
+         tk, tv, a);
+  if (a.splits > 1) launch_k(decode_combine_kernel, dim3(dim3(a.rows, a.Hq)), dim3(D), 0, stream, 1,
+         a);
 }
 
 void prefill(const PrefillArgs& a, const void* kcache, const void* vcache, cudaStream_t stream) {

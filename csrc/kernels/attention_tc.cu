@@ -128,6 +128,8 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
                                                             const __grid_constant__ CUtensorMap tk,
                                                             const __grid_constant__ CUtensorMap tv, PrefillArgs a,
                                                             int G) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -431,7 +433,7 @@ void prefill_tc(const PrefillArgs& a, const CUtensorMap& tk, const CUtensorMap& 
     attr = true;
   }
   dim3 grid((a.max_q_len + QT - 1) / QT, a.rows, a.Hkv);
-  tc::prefill_tc_kernel<<<grid, 192, tc::kSmem, stream>>>(tq, tk, tv, a, G);
+  launch_k(tc::prefill_tc_kernel, grid, dim3(192), tc::kSmem, stream, 1, tq, tk, tv, a, G);
 }
 
 }  // namespace attn

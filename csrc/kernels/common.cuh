@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace lf {
 
 // ---------------------------------------------------------------------------
@@ -42,7 +44,9 @@ namespace rt {
 using ErrReadFn = int (*)(bool clear, unsigned long long* info);
 using ErrInjectFn = void (*)(int code);
 void register_error_word(ErrReadFn read, ErrInjectFn inject);
+bool pdl_enabled();
 }  // namespace rt
+[[noreturn]] void launch_failed(cudaError_t e);  // throws std::runtime_error
 }  // namespace lf
 
 namespace {
@@ -87,6 +91,19 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // beyond any legitimate wait in these kernels (all of them finish in
 // milliseconds) and short enough that a broken pipeline returns promptly.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched by `launch_k()` with PDL on
+// may start while the previous kernel of the stream is still running: it
+// issues pdl_trigger() (its own dependents may then be scheduled once every
+// CTA of this grid has issued it), does its set-up that touches no global
+// memory (barriers, TMEM, descriptor prefetch), and calls pdl_wait() before
+// its first global read or write; pdl_wait() returns when the previous grid
+// has completed and its writes are visible.  Without the launch attribute
+// both instructions are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // Shared-memory address helpers.
@@ -344,6 +361,38 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// launch_k: host launch of a step kernel: cudaLaunchKernelEx with the programmatic
+// stream-serialization attribute when PDL is on (see pdl_wait), plus an
+// optional cluster shape.  Only kernels that call pdl_wait() before touching
+// global memory may be launched through here.  Throws on a launch error.
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (rt::pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) launch_failed(e);
 }
 
 }  // namespace lf

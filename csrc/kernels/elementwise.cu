@@ -28,6 +28,8 @@ namespace ew {
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const uint4* __restrict__ table,
                              uint4* __restrict__ out, int T, int vec_per_row, int vocab) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   int id = ids[t];
   if (id < 0 || id >= vocab) {
@@ -42,7 +44,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const uint4* __res
 void embed(const int32_t* ids, const void* table, void* out, int T, int H, int vocab, cudaStream_t s) {
   if (T <= 0) return;
   const int vpr = H / 8;
-  embed_kernel<<<T, 128, 0, s>>>(ids, reinterpret_cast<const uint4*>(table), reinterpret_cast<uint4*>(out), T, vpr, vocab);
+  launch_k(embed_kernel, dim3(T), dim3(128), 0, s, 1,
+         ids, reinterpret_cast<const uint4*>(table), reinterpret_cast<uint4*>(out), T, vpr, vocab);
 }
 
 // ---------------------------------------------------------------------------
@@ -55,6 +58,8 @@ template <int VPT>
 __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint4* __restrict__ x, uint4* __restrict__ residual,
                                                       const uint4* __restrict__ w, uint4* __restrict__ out,
                                                       int vec_per_row, float eps, int H) {
+  pdl_trigger();
+  pdl_wait();
   const size_t row = blockIdx.x;
   float v[VPT][8];
   float ss = 0.f;
@@ -113,11 +118,16 @@ void rmsnorm(const void* x, void* residual, const void* w, void* out, int T, int
   auto R = reinterpret_cast<uint4*>(residual);
   auto W = reinterpret_cast<const uint4*>(w);
   auto O = reinterpret_cast<uint4*>(out);
-  if (vpt <= 1) rmsnorm_kernel<1><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
-  else if (vpt <= 2) rmsnorm_kernel<2><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
-  else if (vpt <= 4) rmsnorm_kernel<4><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
-  else if (vpt <= 8) rmsnorm_kernel<8><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
-  else rmsnorm_kernel<16><<<T, 128, 0, s>>>(X, R, W, O, vpr, eps, H);
+  if (vpt <= 1) launch_k(rmsnorm_kernel<1>, dim3(T), dim3(128), 0, s, 1,
+         X, R, W, O, vpr, eps, H);
+  else if (vpt <= 2) launch_k(rmsnorm_kernel<2>, dim3(T), dim3(128), 0, s, 1,
+         X, R, W, O, vpr, eps, H);
+  else if (vpt <= 4) launch_k(rmsnorm_kernel<4>, dim3(T), dim3(128), 0, s, 1,
+         X, R, W, O, vpr, eps, H);
+  else if (vpt <= 8) launch_k(rmsnorm_kernel<8>, dim3(T), dim3(128), 0, s, 1,
+         X, R, W, O, vpr, eps, H);
+  else launch_k(rmsnorm_kernel<16>, dim3(T), dim3(128), 0, s, 1,
+         X, R, W, O, vpr, eps, H);
 }
 
 // ---------------------------------------------------------------------------
@@ -133,6 +143,8 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, cons
                                const int32_t* __restrict__ slots, const float2* __restrict__ cos_sin,
                                __nv_bfloat16* __restrict__ kcache, __nv_bfloat16* __restrict__ vcache, int Hq,
                                int Hkv, int D, int page, int max_pos, int64_t num_slots) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int half = D / 2;
   const int pos = positions[t];
@@ -178,7 +190,8 @@ void rope_kv_write(void* qkv, int64_t ld, const int32_t* positions, const int32_
                    void* kcache, void* vcache, int T, int Hq, int Hkv, int D, int page, int max_pos,
                    int64_t num_slots, cudaStream_t s) {
   if (T <= 0) return;
-  rope_kv_kernel<<<T, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(qkv), ld, positions, slots,
+  launch_k(rope_kv_kernel, dim3(T), dim3(256), 0, s, 1,
+         reinterpret_cast<__nv_bfloat16*>(qkv), ld, positions, slots,
                                     reinterpret_cast<const float2*>(cos_sin), reinterpret_cast<__nv_bfloat16*>(kcache),
                                     reinterpret_cast<__nv_bfloat16*>(vcache), Hq, Hkv, D, page, max_pos, num_slots);
 }
@@ -188,6 +201,8 @@ void rope_kv_write(void* qkv, int64_t ld, const int32_t* positions, const int32_
 // Used where the gate/up projection is not the fused tcgen05 epilogue.
 // ---------------------------------------------------------------------------
 __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int F) {
+  pdl_trigger();
+  pdl_wait();
   const size_t t = blockIdx.x;
   for (int i = threadIdx.x; i < F; i += blockDim.x) {
     const float g = __bfloat162float(gu[t * 2 * F + i]);
@@ -199,7 +214,8 @@ __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat1
 
 void swiglu(const void* gu, void* out, int T, int F, cudaStream_t s) {
   if (T <= 0) return;
-  swiglu_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), F);
+  launch_k(swiglu_kernel, dim3(T), dim3(256), 0, s, 1,
+         reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), F);
 }
 
 // ---------------------------------------------------------------------------
@@ -264,6 +280,8 @@ __device__ __forceinline__ int block_sum_i(int v, int* sh) {
 template <int NT>
 __global__ void __launch_bounds__(NT) argmax_kernel(const float* __restrict__ logits, int64_t ld, int V,
                                                     int32_t* __restrict__ out_tok, int32_t* __restrict__ status) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ uint64_t sh[NT / 32];
   __shared__ int shi[NT / 32];
   const float* row = logits + (size_t)blockIdx.x * ld;
@@ -285,7 +303,8 @@ __global__ void __launch_bounds__(NT) argmax_kernel(const float* __restrict__ lo
 
 void argmax(const float* logits, int64_t ld, int R, int V, int32_t* out, int32_t* status, cudaStream_t s) {
   if (R <= 0) return;
-  argmax_kernel<1024><<<R, 1024, 0, s>>>(logits, ld, V, out, status);
+  launch_k(argmax_kernel<1024>, dim3(R), dim3(1024), 0, s, 1,
+         logits, ld, V, out, status);
 }
 
 // Vocab-parallel greedy, step 1: per row, the composite key (logit, lowest id)
@@ -294,6 +313,8 @@ void argmax(const float* logits, int64_t ld, int R, int V, int32_t* out, int32_t
 template <int NT>
 __global__ void __launch_bounds__(NT) argmax_key_kernel(const float* __restrict__ logits, int64_t ld, int V,
                                                         int id_offset, unsigned long long* __restrict__ keys) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ uint64_t sh[NT / 32];
   const float* row = logits + (size_t)blockIdx.x * ld;
   uint64_t best = 0;
@@ -310,6 +331,8 @@ __global__ void __launch_bounds__(NT) argmax_key_kernel(const float* __restrict_
 // Step 2 (after an all-gather of keys [ranks, R]): the winning token per row.
 __global__ void keys_to_tokens_kernel(const unsigned long long* __restrict__ keys, int R, int ranks,
                                       int32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= R) return;
   uint64_t best = 0;
@@ -320,12 +343,14 @@ __global__ void keys_to_tokens_kernel(const unsigned long long* __restrict__ key
 void argmax_keys(const float* logits, int64_t ld, int R, int V, int id_offset, unsigned long long* keys,
                  cudaStream_t s) {
   if (R <= 0) return;
-  argmax_key_kernel<1024><<<R, 1024, 0, s>>>(logits, ld, V, id_offset, keys);
+  launch_k(argmax_key_kernel<1024>, dim3(R), dim3(1024), 0, s, 1,
+         logits, ld, V, id_offset, keys);
 }
 
 void keys_to_tokens(const unsigned long long* keys, int R, int ranks, int32_t* out, cudaStream_t s) {
   if (R <= 0) return;
-  keys_to_tokens_kernel<<<(R + 127) / 128, 128, 0, s>>>(keys, R, ranks, out);
+  launch_k(keys_to_tokens_kernel, dim3((R + 127) / 128), dim3(128), 0, s, 1,
+         keys, R, ranks, out);
 }
 
 // Counter-addressed uniform draw in [0, 1) with 53 random bits
@@ -350,6 +375,8 @@ template <int NT>
 __global__ void __launch_bounds__(NT) sample_kernel(const float* __restrict__ logits, int64_t ld, int V,
                                                     const SampleParams* __restrict__ params,
                                                     int32_t* __restrict__ out_tok, int32_t* __restrict__ status) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ uint64_t shk[NT / 32];
   __shared__ double shd[NT / 32];
   __shared__ int shi[NT / 32];
@@ -453,7 +480,8 @@ __global__ void __launch_bounds__(NT) sample_kernel(const float* __restrict__ lo
 void sample(const float* logits, int64_t ld, int R, int V, const SampleParams* params, int32_t* out, int32_t* status,
             cudaStream_t s) {
   if (R <= 0) return;
-  sample_kernel<512><<<R, 512, 0, s>>>(logits, ld, V, params, out, status);
+  launch_k(sample_kernel<512>, dim3(R), dim3(512), 0, s, 1,
+         logits, ld, V, params, out, status);
 }
 
 double host_counter_unit(uint64_t seed, int64_t idx) { return counter_unit(seed, idx); }

@@ -145,11 +145,13 @@ static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int k
   const int tiles = ((a.M + MB * BM - 1) / (MB * BM)) * (a.N / BN) * splits;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   if (kb_per <= 0) kb_per = (a.K + BK - 1) / BK;
+  const int* no_groups = nullptr;
   if (EPI == kSplitF32) {
-    kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, ws, a.M, a.N, a.K, a.N, splits, kb_per, ArArgs{}, nullptr, 0);
+    launch_k(kfn, dim3(grid), dim3(kThreads), S::kTotal, stream, 1, ta, tb, static_cast<void*>(ws), a.M, a.N, a.K, a.N,
+             splits, kb_per, ArArgs{}, no_groups, 0);
   } else {
-    kfn<<<grid, threads_for(EPI), S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, splits, kb_per, ar, nullptr,
-                                                       0);
+    launch_k(kfn, dim3(grid), dim3(threads_for(EPI)), S::kTotal, stream, 1, ta, tb, a.D, a.M, a.N, a.K, (int)a.ldd,
+             splits, kb_per, ar, no_groups, 0);
   }
 }
 
@@ -214,20 +216,8 @@ static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int6
   CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
   CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, BN);
   const int tiles = ((a.M + MB * BM - 1) / (MB * BM)) * (a.N / BN);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles * c, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = S::kTotal;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = c;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, out, a.M, a.N, a.K, (int)ldd, kb_per);
-  if (e != cudaSuccess) throw std::runtime_error(std::string("lunaflux cluster gemm launch: ") + cudaGetErrorString(e));
+  launch_k(kfn, dim3(tiles * c), dim3(kThreads), S::kTotal, stream, (unsigned)c, ta, tb, out, a.M, a.N, a.K, (int)ldd,
+           kb_per);
 }
 
 // 256-row cluster tiles (MB = 2) for 129..256-row GEMMs: off unless enabled

@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
   // read from device memory), and segment g multiplies B rows [g*N, (g+1)*N).
   // M is then an upper bound on groups[num_groups]; blocks past it are skipped.
   static_assert(MB == 1 || (EPI != kSplitF32 && EPI != kAllReduceBf16), "256-row tiles: plain epilogues only");
+  pdl_trigger();
   using S = Smem<BN, STAGES, MB>;
   constexpr int kAccs = tmem_accs<BN, MB>();
   constexpr int TM = MB * BM;                 // rows per tile
@@ -188,6 +189,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the set-up above touches no global memory
   __shared__ volatile int s_ar_ok;  // fused all-reduce: did the wait succeed
 
   if (warp == 0) {
@@ -476,6 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using S = Smem<BN, STAGES, MB>;
   static_assert(ClusterRed<BN>::kBytes <= STAGES * S::kStageBytes, "partial tile must fit the pipeline buffers");
   static_assert(MB * BN <= 512, "accumulators must fit TMEM");
+  pdl_trigger();
   constexpr int TM = MB * BM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -516,6 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the set-up above touches no global memory
 
   if (warp == 0) {
     if (lane == 0) {

@@ -4,6 +4,7 @@
 // with the step.  This file folds the per-translation-unit words together.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -50,6 +51,26 @@ ErrorState read_error(cudaStream_t s, bool clear) {
   }
   return st;
 }
+
+}  // namespace rt
+
+void launch_failed(cudaError_t e) {
+  throw std::runtime_error(std::string("lunaflux kernel launch: ") + cudaGetErrorString(e));
+}
+
+namespace rt {
+
+static int g_pdl = -1;
+
+bool pdl_enabled() {
+  if (g_pdl < 0) {
+    const char* e = getenv("LUNAFLUX_PDL");
+    g_pdl = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return g_pdl == 1;
+}
+
+void set_pdl(bool on) { g_pdl = on ? 1 : 0; }
 
 void inject_error(int code) {
   std::lock_guard<std::mutex> g(hooks_mu());

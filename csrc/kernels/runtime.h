@@ -9,5 +9,9 @@ struct ErrorState {
 };
 ErrorState read_error(cudaStream_t s, bool clear);
 void inject_error(int code);
+// Programmatic dependent launch for the kernels of the step (off unless
+// LUNAFLUX_PDL=1 or set_pdl(true)).
+bool pdl_enabled();
+void set_pdl(bool on);
 }  // namespace rt
 }  // namespace lf
