@@ -34,45 +34,10 @@
 
 #include "allreduce_ll.h"
 #include "common.cuh"
+#include "ll_words.cuh"
 
 namespace lf {
 namespace ar {
-
-__device__ __forceinline__ void st_word(uint2* p, uint32_t data, uint32_t ep) {
-  asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(ep) : "memory");
-}
-
-__device__ __forceinline__ void st_word_mc(uint2* p, uint32_t data, uint32_t ep) {
-  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(ep) : "memory");
-}
-
-__device__ __forceinline__ uint2 ld_word(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-  return v;
-}
-
-// Polls one inbox word until it carries epoch `ep`; false after recording a
-// timeout (or when another wait already failed).
-__device__ __forceinline__ bool poll_word(const uint2* p, uint32_t ep, uint32_t* data) {
-  uint2 v = ld_word(p);
-  if (v.y != ep) {
-    const uint64_t t0 = globaltimer_ns();
-    uint32_t spins = 0;
-    do {
-      if ((++spins & 255u) == 0) {
-        if (error_pending()) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          set_error(kErrPeerTimeout, 0x11ull);
-          return false;
-        }
-      }
-      v = ld_word(p);
-    } while (v.y != ep);
-  }
-  *data = v.x;
-  return true;
-}
 
 __device__ __forceinline__ float2 slab_pair(const float* __restrict__ ws, size_t slab, int splits, int64_t p) {
   float2 acc = make_float2(0.f, 0.f);
@@ -82,15 +47,6 @@ __device__ __forceinline__ float2 slab_pair(const float* __restrict__ ws, size_t
     acc.y += v.y;
   }
   return acc;
-}
-
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-__device__ __forceinline__ float2 unpack2(uint32_t u) {
-  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
 }
 
 __global__ void __launch_bounds__(256, 2) finalize_ll_kernel(const float* __restrict__ ws, int splits, int M, int N,

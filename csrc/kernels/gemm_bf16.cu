@@ -205,7 +205,8 @@ static bool cluster_fits(int c, int clusters) {
 }
 
 template <int BN, int STAGES, int OUT, int MB = 1>
-static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int64_t ldd, cudaStream_t stream) {
+static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int64_t ldd, cudaStream_t stream,
+                           const ar::LLArgs& ll = ar::LLArgs{}) {
   using S = Smem<BN, STAGES, MB>;
   auto kfn = gemm_cluster_splitk_kernel<BN, STAGES, OUT, MB>;
   static bool attr_set = false;
@@ -217,7 +218,7 @@ static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int6
   CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, BN);
   const int tiles = ((a.M + MB * BM - 1) / (MB * BM)) * (a.N / BN);
   launch_k(kfn, dim3(tiles * c), dim3(kThreads), S::kTotal, stream, (unsigned)c, ta, tb, out, a.M, a.N, a.K, (int)ldd,
-           kb_per);
+           kb_per, ll);
 }
 
 // 256-row cluster tiles (MB = 2) for 129..256-row GEMMs: off unless enabled
@@ -428,9 +429,37 @@ void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, flo
   }
 }
 
+// One kernel for the decode projection and its all-reduce (the cluster
+// split-K GEMM whose epilogue runs the low-latency protocol): off unless
+// LUNAFLUX_FUSED_LL_GEMM=1 or set_ll_gemm_fused(1).
+static int g_ll_gemm_fused = -1;
+
+void set_ll_gemm_fused(int on) { g_ll_gemm_fused = on ? 1 : 0; }
+
+static bool ll_gemm_fused_enabled() {
+  if (g_ll_gemm_fused < 0) {
+    const char* e = getenv("LUNAFLUX_FUSED_LL_GEMM");
+    g_ll_gemm_fused = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return g_ll_gemm_fused == 1;
+}
+
 void run_allreduce_ll(const GemmArgs& a, const ar::LLArgs& ll, cudaStream_t stream, float* ws, int64_t ws_elems) {
   if (a.M <= 0) return;
   if (a.N % 256 != 0 || a.K % 8 != 0) throw std::runtime_error("lunaflux gemm_allreduce_ll: N % 256 and K % 8 required");
+  if (ll.world < 1 || ll.world > ar::kMaxRanks || ll.rank < 0 || ll.rank >= ll.world)
+    throw std::runtime_error("lunaflux gemm_allreduce_ll: rank");
+  if (ll_gemm_fused_enabled() && (int64_t)a.M * a.N / 2 <= ll.max_pairs) {
+    int bn = 0, kb_per = 0, mb = 1;
+    const int c = plan_cluster(a.M, a.N, a.K, kStoreF32, &bn, &kb_per, &mb);
+    if (c >= 2 && mb == 1) {
+      // every CTA of the grid is resident at once (the plan keeps the grid
+      // within one wave), as the cross-rank waits of the epilogue require
+      if (bn == 256) launch_cluster<256, 4, kAllReduceLL>(a, c, kb_per, a.D, a.ldd, stream, ll);
+      else launch_cluster<128, 6, kAllReduceLL>(a, c, kb_per, a.D, a.ldd, stream, ll);
+      return;
+    }
+  }
   if ((int64_t)a.M * a.N > ws_elems) throw std::runtime_error("lunaflux gemm_allreduce_ll: workspace too small");
   // this rank's fp32 partial [M, N] in ws (cluster split-K when it pays), then the all-reduce
   run(GemmArgs{a.A, a.B, ws, a.M, a.N, a.K, a.lda, a.ldb, a.N}, kStoreF32, 0, stream);

@@ -8,6 +8,7 @@
 
 #include "common.cuh"
 #include "gemm_bf16.h"
+#include "ll_words.cuh"
 
 namespace lf {
 namespace gemm {
@@ -16,7 +17,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;                 // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;                 // TMA warp, MMA warp, 4 epilogue warps
 
-enum Epi : int { kStoreBf16 = 0, kStoreF32 = 1, kSwiGLU = 2, kSplitF32 = 3, kAllReduceBf16 = 4 };
+enum Epi : int { kStoreBf16 = 0, kStoreF32 = 1, kSwiGLU = 2, kSplitF32 = 3, kAllReduceBf16 = 4, kAllReduceLL = 5 };
 
 // The fused all-reduce adds 4 communication warps (6..9).
 constexpr int threads_for(int epi) { return epi == kAllReduceBf16 ? kThreads + 128 : kThreads; }
@@ -464,7 +465,124 @@ struct ClusterRed {
   static constexpr int kBytes = BM * kStride * 4;
 };
 
-// OUT: kStoreBf16, kStoreF32 or kSwiGLU (interleaved gate/up groups of 32).
+// Sum of the cluster's partials for 4 consecutive columns of one row.
+template <int BN>
+__device__ __forceinline__ float4 cluster_sum4(uint32_t red_base, int c, int rl, int col) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const uint32_t off = red_base + (uint32_t)(rl * ClusterRed<BN>::kStride + col) * 4;
+  for (int q = 0; q < c; ++q) {
+    const float4 a = ld_shared_cluster_f4(mapa_shared(off, q));
+    acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+  }
+  return acc;
+}
+
+// Epilogue of the fused decode all-reduce (kAllReduceLL), run by the 128
+// epilogue threads (t) of a CTA on its band of rows [r0, r1) of the tile.
+// Output pairs (two bf16 of one row) are numbered p = (row * N + col) / 2 and
+// dealt to the ranks in contiguous chunks, exactly as the standalone kernel
+// does, so the two share inboxes and epochs:
+//   1. every pair owned by another rank: this rank's bf16 partial -> the
+//      owner's reduce-scatter inbox (one 8-byte store with the epoch);
+//   2. every pair this rank owns: its own partial (rounded to bf16 like the
+//      others) plus the other ranks' inbox words, stored to `out` and to every
+//      rank's all-gather inbox (one multicast store, or one per peer);
+//   3. every pair owned by another rank: the owner's all-gather word -> `out`.
+// Step 2 waits only for step 1 of the other ranks and step 3 only for step 2,
+// and no rank waits before finishing its step 1, so the waits form no cycle
+// across ranks; every wait is bounded.
+template <int BN>
+__device__ __forceinline__ void ll_epilogue(const ar::LLArgs& ll, uint32_t ep, uint32_t red_base, int c, int r0,
+                                            int r1, int mrow0, int n0, int M, int N, int ldd,
+                                            __nv_bfloat16* __restrict__ out, int t) {
+  constexpr int kQuads = BN / 4;
+  const int64_t P = (int64_t)M * N / 2;
+  const int64_t chunk = (P + ll.world - 1) / ll.world;
+  const int64_t p_lo = ll.rank * chunk;
+  const int64_t p_hi = p_lo + chunk < P ? p_lo + chunk : P;
+  const int n_items = (r1 - r0) * kQuads;
+  // 1. partials of the pairs other ranks own
+  for (int i = t; i < n_items; i += 128) {
+    const int rl = r0 + i / kQuads;
+    const int col = (i % kQuads) * 4;
+    const int grow = mrow0 + rl;
+    if (grow >= M) continue;
+    const int64_t p = ((int64_t)grow * N + n0 + col) >> 1;
+    if (p >= p_lo && p + 1 < p_hi) continue;  // both pairs are this rank's
+    const float4 acc = cluster_sum4<BN>(red_base, c, rl, col);
+    const uint32_t w[2] = {ar::pack2(acc.x, acc.y), ar::pack2(acc.z, acc.w)};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int64_t pp = p + e;
+      const int owner = (int)(pp / chunk);
+      if (owner != ll.rank) ar::st_word(ll.rs[owner] + (int64_t)ll.rank * chunk + (pp - owner * chunk), w[e], ep);
+    }
+  }
+  // 2. the pairs this rank owns
+  bool ok = true;
+  for (int i = t; i < n_items && ok; i += 128) {
+    const int rl = r0 + i / kQuads;
+    const int col = (i % kQuads) * 4;
+    const int grow = mrow0 + rl;
+    if (grow >= M) continue;
+    const int64_t p = ((int64_t)grow * N + n0 + col) >> 1;
+    if (p + 1 < p_lo || p >= p_hi) continue;  // neither pair is this rank's
+    const float4 acc = cluster_sum4<BN>(red_base, c, rl, col);
+    const float2 own[2] = {make_float2(acc.x, acc.y), make_float2(acc.z, acc.w)};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int64_t pp = p + e;
+      if (pp < p_lo || pp >= p_hi || !ok) continue;
+      float2 sum = ar::unpack2(ar::pack2(own[e].x, own[e].y));  // the same bf16 rounding as every rank's partial
+      for (int src = 0; src < ll.world; ++src) {
+        if (src == ll.rank) continue;
+        uint32_t d;
+        if (!ar::poll_word(ll.rs[ll.rank] + (int64_t)src * chunk + (pp - p_lo), ep, &d)) {
+          ok = false;
+          break;
+        }
+        const float2 v = ar::unpack2(d);
+        sum.x += v.x;
+        sum.y += v.y;
+      }
+      if (!ok) break;
+      const uint32_t r = ar::pack2(sum.x, sum.y);
+      *reinterpret_cast<uint32_t*>(out + (size_t)grow * ldd + n0 + col + 2 * e) = r;
+      if (ll.ag_mc != nullptr) {
+        ar::st_word_mc(ll.ag_mc + pp, r, ep);
+      } else {
+        for (int k = 0; k < ll.world; ++k)
+          if (k != ll.rank) ar::st_word(ll.ag[k] + pp, r, ep);
+      }
+    }
+  }
+  // 3. the pairs other ranks own
+  for (int i = t; i < n_items && ok; i += 128) {
+    const int rl = r0 + i / kQuads;
+    const int col = (i % kQuads) * 4;
+    const int grow = mrow0 + rl;
+    if (grow >= M) continue;
+    const int64_t p = ((int64_t)grow * N + n0 + col) >> 1;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int64_t pp = p + e;
+      if (pp >= p_lo && pp < p_hi) continue;
+      uint32_t d;
+      if (!ar::poll_word(ll.ag[ll.rank] + pp, ep, &d)) {
+        ok = false;
+        break;
+      }
+      *reinterpret_cast<uint32_t*>(out + (size_t)grow * ldd + n0 + col + 2 * e) = d;
+    }
+  }
+}
+
+
+// OUT: kStoreBf16, kStoreF32, kSwiGLU (interleaved gate/up groups of 32), or
+// kAllReduceLL: bf16 out = sum over the tensor-parallel ranks, the epilogue
+// running the low-latency all-reduce protocol itself (`ll`, see
+// allreduce_ll.cu) on the cluster-reduced values, so the row-parallel decode
+// projection and its all-reduce are one kernel.
 // MB: 128-row M-blocks per tile.  With MB = 2 (decode batches of 129..256
 // rows) the two MMAs of a k-slab share the staged weight slab, so the weights
 // cross into shared memory once instead of once per M-block; the two partial
@@ -474,10 +592,11 @@ template <int BN, int STAGES, int OUT, int MB = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_cluster_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M, int N,
-                               int K, int ldd, int kb_per_split) {
+                               int K, int ldd, int kb_per_split, const ar::LLArgs ll) {
   using S = Smem<BN, STAGES, MB>;
   static_assert(ClusterRed<BN>::kBytes <= STAGES * S::kStageBytes, "partial tile must fit the pipeline buffers");
   static_assert(MB * BN <= 512, "accumulators must fit TMEM");
+  static_assert(OUT != kAllReduceLL || MB == 1, "fused all-reduce: 128-row tiles");
   pdl_trigger();
   constexpr int TM = MB * BM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -520,6 +639,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // the set-up above touches no global memory
+  // fused all-reduce: this operation's epoch (advanced by the grid's last CTA)
+  uint32_t ep = 0;
+  if constexpr (OUT == kAllReduceLL) ep = (uint32_t)(*reinterpret_cast<volatile int*>(ll.state)) + 1u;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -625,6 +747,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 make_uint2(pack_bf16x2(silu(g.x) * u.x, silu(g.y) * u.y), pack_bf16x2(silu(g.z) * u.z, silu(g.w) * u.w));
           }
         }
+      } else if constexpr (OUT == kAllReduceLL) {
+        ll_epilogue<BN>(ll, ep, red_base, c, r0, r1, mrow0, n0, M, N, ldd, reinterpret_cast<__nv_bfloat16*>(out), t);
       } else {
         constexpr int kQuads = BN / 4;
         for (int i = t; i < (r1 - r0) * kQuads; i += 128) {
@@ -656,6 +780,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kCols);
+  }
+  if constexpr (OUT == kAllReduceLL) {
+    // advance the epoch once every CTA has read it (all have passed the
+    // cluster barrier above, which follows their read)
+    if (threadIdx.x == 0 && atomicAdd(ll.state + 1, 1) == (int)gridDim.x - 1) {
+      ll.state[1] = 0;
+      *reinterpret_cast<volatile int*>(ll.state) = (int)ep;
+    }
   }
 }
 

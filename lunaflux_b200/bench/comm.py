@@ -73,12 +73,16 @@ def main(argv=None):
     ap.add_argument("--json", default="")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", default="")
+    ap.add_argument("--single-kernel-decode", action="store_true",
+                    help="decode rows: the cluster split-K GEMM runs the low-latency all-reduce in its epilogue")
     args = ap.parse_args(argv)
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     init_distributed("nccl", device_id=local)
     world, rank = dist.get_world_size(), dist.get_rank()
     C = _ext.load()
+    if args.single_kernel_decode:
+        C.gemm_set_ll_fused(True)
     hidden = 4096
     shapes = []
     for M in (256, 8192):

@@ -27,7 +27,7 @@ def _port():
 SHAPES = [(256, 4096, 512), (1, 4096, 1792), (8192, 4096, 512), (300, 4096, 1024), (37, 4096, 14336 // 8)]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, fused_ll=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     import torch.distributed as dist
@@ -41,6 +41,10 @@ def _worker(rank, world, port, q):
         # and the flag protocol everywhere (split-K finalize kernel, tile path)
         comms = [FusedTPComm(8192, 4096, dev), FusedTPComm(8192, 4096, dev, ll_rows=0, tile_min_k=0)]
         C = comms[0].C
+        if fused_ll:
+            # decode rows: the cluster split-K GEMM runs the low-latency protocol in its epilogue
+            C.gemm_set_ll_fused(True)
+            comms = comms[:1]
         ws = torch.zeros(512 * 32768, device=dev)
         errs = []
         for it in range(3):
@@ -82,12 +86,24 @@ def _worker(rank, world, port, q):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_fused_gemm_allreduce_matches_nccl():
+    _run(fused_ll=False)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
+                    reason="single-kernel decode GEMM + all-reduce: first multi-GPU run pending "
+                           "(set LUNAFLUX_TEST_NEW_KERNELS=1)")
+def test_single_kernel_decode_gemm_allreduce_matches_nccl():
+    _run(fused_ll=True)
+
+
+def _run(fused_ll):
     import torch.multiprocessing as mp
     world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, fused_ll)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
