@@ -312,6 +312,43 @@ void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tenso
                         cos_sin.size(0), num_slots, stream());
 }
 
+// QKV projection with RoPE and the paged K / V write fused into the GEMM
+// epilogue.  Returns false (nothing launched) when no tile plan has whole heads
+// per tile; the caller then runs the GEMM and rope_kv_write.
+bool gemm_qkv_rope(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const at::Tensor& positions,
+                   const at::Tensor& slots, const at::Tensor& cos_sin, at::Tensor& kcache, at::Tensor& vcache,
+                   int64_t Hq, int64_t Hkv, int64_t page) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(D, "D");
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  check_rowmajor(D, "D");
+  LF_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && D.scalar_type() == at::kBFloat16,
+           "gemm_qkv_rope is bf16");
+  LF_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.numel() % 128 == 0,
+           "cos_sin must be contiguous fp32 [max_pos, 64, 2]");
+  LF_CHECK(kcache.is_contiguous() && vcache.is_contiguous() && kcache.size(-1) == 128, "kv cache: head_dim 128");
+  LF_CHECK(positions.scalar_type() == at::kInt && slots.scalar_type() == at::kInt, "positions / slots int32");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  LF_CHECK(A.size(1) == B.size(1) && D.size(0) == M && D.size(1) == N, "gemm_qkv_rope shapes");
+  LF_CHECK(N == (Hq + 2 * Hkv) * 128, "gemm_qkv_rope: N must be (Hq + 2 Hkv) * 128");
+  LF_CHECK(positions.size(0) >= M && slots.size(0) >= M, "positions/slots length");
+  c10::cuda::CUDAGuard g(A.device());
+  lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), B.stride(0), D.stride(0)};
+  lf::gemm::RopeArgs r{positions.data_ptr<int32_t>(),
+                       slots.data_ptr<int32_t>(),
+                       reinterpret_cast<const float2*>(cos_sin.data_ptr()),
+                       reinterpret_cast<__nv_bfloat16*>(kcache.data_ptr()),
+                       reinterpret_cast<__nv_bfloat16*>(vcache.data_ptr()),
+                       (int)Hq,
+                       (int)Hkv,
+                       (int)page,
+                       (int)(cos_sin.numel() / 128),
+                       kcache.numel() / (Hkv * 128)};
+  return lf::gemm::run_qkv_rope(a, r, stream());
+}
+
 void swiglu(const at::Tensor& gu, at::Tensor& out) {
   LF_CHECK(gu.is_contiguous() && out.is_contiguous(), "swiglu needs contiguous tensors");
   c10::cuda::CUDAGuard g(gu.device());
@@ -442,6 +479,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("device_report", &lf::rt::device_report, "devices, compute capability, peer access, NVLink multicast, typed status");
   m.def("gemm_plan_cluster", &gemm_plan_cluster);
   m.def("gemm_set_cluster_mb2", &gemm_set_cluster_mb2);
+  m.def("gemm_qkv_rope", &gemm_qkv_rope);
   m.def("gemm_set_ll_fused", [](bool on) { lf::gemm::set_ll_gemm_fused(on ? 1 : 0); });
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_grouped", &gemm_grouped);

@@ -132,7 +132,7 @@ static int num_sms() {
 
 template <int BN, int STAGES, int EPI, int MB = 1>
 static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int kb_per = 0, float* ws = nullptr,
-                   const ArArgs& ar = ArArgs{}) {
+                   const ArArgs& ar = ArArgs{}, const RopeArgs& rope = RopeArgs{}) {
   using S = Smem<BN, STAGES, MB>;
   auto kfn = gemm_bf16_kernel<BN, STAGES, EPI, MB>;
   static bool attr_set = false;
@@ -148,10 +148,10 @@ static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int k
   const int* no_groups = nullptr;
   if (EPI == kSplitF32) {
     launch_k(kfn, dim3(grid), dim3(kThreads), S::kTotal, stream, 1, ta, tb, static_cast<void*>(ws), a.M, a.N, a.K, a.N,
-             splits, kb_per, ArArgs{}, no_groups, 0);
+             splits, kb_per, ArArgs{}, no_groups, 0, RopeArgs{});
   } else {
     launch_k(kfn, dim3(grid), dim3(threads_for(EPI)), S::kTotal, stream, 1, ta, tb, a.D, a.M, a.N, a.K, (int)a.ldd,
-             splits, kb_per, ar, no_groups, 0);
+             splits, kb_per, ar, no_groups, 0, rope);
   }
 }
 
@@ -206,7 +206,7 @@ static bool cluster_fits(int c, int clusters) {
 
 template <int BN, int STAGES, int OUT, int MB = 1>
 static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int64_t ldd, cudaStream_t stream,
-                           const ar::LLArgs& ll = ar::LLArgs{}) {
+                           const ar::LLArgs& ll = ar::LLArgs{}, const RopeArgs& rope = RopeArgs{}) {
   using S = Smem<BN, STAGES, MB>;
   auto kfn = gemm_cluster_splitk_kernel<BN, STAGES, OUT, MB>;
   static bool attr_set = false;
@@ -218,7 +218,7 @@ static void launch_cluster(const GemmArgs& a, int c, int kb_per, void* out, int6
   CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, BN);
   const int tiles = ((a.M + MB * BM - 1) / (MB * BM)) * (a.N / BN);
   launch_k(kfn, dim3(tiles * c), dim3(kThreads), S::kTotal, stream, (unsigned)c, ta, tb, out, a.M, a.N, a.K, (int)ldd,
-           kb_per, ll);
+           kb_per, ll, rope);
 }
 
 // 256-row cluster tiles (MB = 2) for 129..256-row GEMMs: off unless enabled
@@ -466,6 +466,28 @@ void run_allreduce_ll(const GemmArgs& a, const ar::LLArgs& ll, cudaStream_t stre
   ar::finalize_ll(ws, 1, a.M, a.N, reinterpret_cast<__nv_bfloat16*>(a.D), a.ldd, ll, stream);
 }
 
+bool run_qkv_rope(const GemmArgs& a, const RopeArgs& rope, cudaStream_t stream) {
+  if (a.M <= 0) return true;
+  if (a.N != (rope.Hq + 2 * rope.Hkv) * 128 || a.K % 8 != 0) return false;
+  int bn = 0, kb_per = 0, mb = 1;
+  const int c = plan_cluster(a.M, a.N, a.K, kStoreBf16, &bn, &kb_per, &mb);
+  if (c >= 2 && mb == 1) {
+    if (bn == 256) launch_cluster<256, 4, kQkvRope>(a, c, kb_per, a.D, a.ldd, stream, ar::LLArgs{}, rope);
+    else launch_cluster<128, 6, kQkvRope>(a, c, kb_per, a.D, a.ldd, stream, ar::LLArgs{}, rope);
+    return true;
+  }
+  if (c < 2 && a.M > BM && a.M <= 2 * BM && a.N % 256 == 0) {
+    launch<256, 3, kQkvRope, 2>(a, stream, 1, 0, nullptr, ArArgs{}, rope);
+    return true;
+  }
+  if (c >= 2) return false;  // a 256-row cluster plan: no fused variant
+  const int b = choose_bn(a.M, a.N, kStoreBf16);
+  if (b == 256) launch<256, 4, kQkvRope>(a, stream, 1, 0, nullptr, ArArgs{}, rope);
+  else if (b == 128) launch<128, 6, kQkvRope>(a, stream, 1, 0, nullptr, ArArgs{}, rope);
+  else return false;
+  return true;
+}
+
 // Grouped GEMM (mixture-of-experts): A [M_max, K] rows in expert segments
 // groups[0..num_groups] (device memory, multiples of BM), B [num_groups * N, K]
 // the experts' stacked weights, D [M_max, N] (or [M_max, N / 2] for SwiGLU).
@@ -483,7 +505,7 @@ static void launch_grouped(const GemmArgs& a, const int* groups, int num_groups,
   const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
   kfn<<<grid, kThreads, S::kTotal, stream>>>(ta, tb, a.D, a.M, a.N, a.K, a.ldd, 1, (a.K + BK - 1) / BK, ArArgs{},
-                                             groups, num_groups);
+                                             groups, num_groups, RopeArgs{});
 }
 
 void partials_allreduce(const float* ws, int M, int N, int splits, const ArArgs& ar, cudaStream_t stream) {

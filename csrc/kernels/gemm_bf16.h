@@ -47,6 +47,23 @@ void set_ll_gemm_fused(int on);
 // `cnt_*` address int32 counters: [0, cnt_capacity) arrivals, then
 // [cnt_capacity, 2 cnt_capacity) completions; every wait re-arms its counter.
 constexpr int kMaxRanks = 8;
+
+// QKV projection epilogue (kQkvRope): the output columns are Hq query heads,
+// then Hkv key heads, then Hkv value heads, 128 wide each.  Query heads are
+// rotated (split-half RoPE, angles from cos_sin [max_pos][64] (cos, sin)) and
+// written to D; key heads are rotated and value heads copied into the paged
+// cache ([page][kv_head][page_size][128] per K / V) at slots[row] (negative:
+// no write).  D's key / value columns are not written.
+struct RopeArgs {
+  const int32_t* positions;
+  const int32_t* slots;
+  const float2* cos_sin;
+  __nv_bfloat16* kcache;
+  __nv_bfloat16* vcache;
+  int Hq, Hkv, page, max_pos;
+  int64_t num_slots;
+};
+
 struct ArArgs {
   __nv_bfloat16* local;
   __nv_bfloat16* mc;
@@ -77,6 +94,10 @@ int choose_bn(int M, int N, int epi);
 // Decode shapes: GEMM into fp32 slabs of ws (split-K when it fills the SMs),
 // then the low-latency all-reduce (allreduce_ll.h) into a.D.
 void run_allreduce_ll(const GemmArgs& a, const ar::LLArgs& ll, cudaStream_t stream, float* ws, int64_t ws_elems);
+// QKV projection with RoPE and the paged K / V write in the epilogue (see
+// RopeArgs; D is [M, (Hq + 2 Hkv) * 128]).  Returns false, having launched
+// nothing, when the shape has no tile plan with whole heads per tile.
+bool run_qkv_rope(const GemmArgs& a, const RopeArgs& rope, cudaStream_t stream);
 
 CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
                          uint64_t cols, uint64_t ld_elems, uint32_t box_rows, uint32_t box_cols,

@@ -17,7 +17,15 @@ constexpr int BM = 128;
 constexpr int BK = 64;                 // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;                 // TMA warp, MMA warp, 4 epilogue warps
 
-enum Epi : int { kStoreBf16 = 0, kStoreF32 = 1, kSwiGLU = 2, kSplitF32 = 3, kAllReduceBf16 = 4, kAllReduceLL = 5 };
+enum Epi : int {
+  kStoreBf16 = 0,
+  kStoreF32 = 1,
+  kSwiGLU = 2,
+  kSplitF32 = 3,
+  kAllReduceBf16 = 4,
+  kAllReduceLL = 5,
+  kQkvRope = 6,  // QKV projection: RoPE on Q / K, K / V into the paged cache (RopeArgs)
+};
 
 // The fused all-reduce adds 4 communication warps (6..9).
 constexpr int threads_for(int epi) { return epi == kAllReduceBf16 ? kThreads + 128 : kThreads; }
@@ -137,12 +145,82 @@ __device__ __forceinline__ int group_of(const int* groups, int num_groups, int m
   return g;
 }
 
+// Rotation of one (x1, x2) split-half pair by the angle whose (cos, sin) is cs.
+__device__ __forceinline__ float2 rope_pair(float x1, float x2, float2 cs) {
+  return make_float2(x1 * cs.x - x2 * cs.y, x2 * cs.x + x1 * cs.y);
+}
+
+// kQkvRope epilogue of the persistent kernel: the thread owns one row (TMEM
+// lane) of a tile whose BN columns are BN / 128 whole heads.  tcgen05.ld is
+// warp-collective, so every lane loads and only live rows store.
+template <int BN>
+__device__ __forceinline__ void qkv_rope_row(const RopeArgs& rp, uint32_t taddr, int row, int M, int n0,
+                                             __nv_bfloat16* __restrict__ out, int ldd) {
+  static_assert(BN % 128 == 0, "whole heads per tile");
+  const bool live = row < M;
+  const int pos = live ? rp.positions[row] : 0;
+  const int slot = live ? rp.slots[row] : -1;
+  const bool pos_ok = pos >= 0 && pos < rp.max_pos;
+  if (live && !pos_ok) set_error(kErrBadIndex, (unsigned long long)row);
+  const bool slot_ok = slot >= 0 && (int64_t)slot < rp.num_slots;
+  const int pg = slot_ok ? slot / rp.page : 0, off = slot_ok ? slot % rp.page : 0;
+#pragma unroll 1
+  for (int j = 0; j < BN / 128; ++j) {
+    const int hd = n0 / 128 + j;
+    const bool is_q = hd < rp.Hq;
+    const bool is_v = hd >= rp.Hq + rp.Hkv;
+    __nv_bfloat16* dst;
+    if (is_q) {
+      dst = out + (size_t)row * ldd + (size_t)hd * 128;
+    } else {
+      const int kh = is_v ? hd - rp.Hq - rp.Hkv : hd - rp.Hq;
+      dst = (is_v ? rp.vcache : rp.kcache) + (((size_t)pg * rp.Hkv + kh) * rp.page + off) * 128;
+    }
+    const bool write = live && (is_q || slot_ok);
+#pragma unroll 1
+    for (int c = 0; c < 64; c += 32) {
+      uint32_t x1[32], x2[32];
+      tmem_ld_32x32b_x32(taddr + j * 128 + c, x1);
+      tmem_ld_32x32b_x32(taddr + j * 128 + 64 + c, x2);
+      tmem_wait_ld();
+      if (!write) continue;
+      uint32_t p1[16], p2[16];
+      if (!is_v) {
+        const float4* cs4 = reinterpret_cast<const float4*>(rp.cos_sin + (size_t)(pos_ok ? pos : 0) * 64 + c);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          // (cos, sin) of pairs c + 2e and c + 2e + 1
+          const float4 cs = pos_ok ? cs4[e] : make_float4(1.f, 0.f, 1.f, 0.f);
+          const float2 r0 = rope_pair(__uint_as_float(x1[2 * e]), __uint_as_float(x2[2 * e]), make_float2(cs.x, cs.y));
+          const float2 r1 =
+              rope_pair(__uint_as_float(x1[2 * e + 1]), __uint_as_float(x2[2 * e + 1]), make_float2(cs.z, cs.w));
+          p1[e] = pack_bf16x2(r0.x, r1.x);
+          p2[e] = pack_bf16x2(r0.y, r1.y);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          p1[e] = pack_bf16x2(__uint_as_float(x1[2 * e]), __uint_as_float(x1[2 * e + 1]));
+          p2[e] = pack_bf16x2(__uint_as_float(x2[2 * e]), __uint_as_float(x2[2 * e + 1]));
+        }
+      }
+      uint4* d1 = reinterpret_cast<uint4*>(dst + c);
+      uint4* d2 = reinterpret_cast<uint4*>(dst + 64 + c);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        d1[e] = make_uint4(p1[4 * e], p1[4 * e + 1], p1[4 * e + 2], p1[4 * e + 3]);
+        d2[e] = make_uint4(p2[4 * e], p2[4 * e + 1], p2[4 * e + 2], p2[4 * e + 3]);
+      }
+    }
+  }
+}
+
 template <int BN, int STAGES, int EPI, int MB = 1>
 __global__ void __launch_bounds__(threads_for(EPI), 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M,
                      int N, int K, int ldd, int splits, int kb_per_split, ArArgs ar,
-                     const int* __restrict__ groups, int num_groups) {
+                     const int* __restrict__ groups, int num_groups, const RopeArgs rope) {
   // Grouped mode (groups != nullptr, mixture-of-experts): A's rows are split
   // into num_groups segments, groups[g]..groups[g+1] (each a multiple of BM,
   // read from device memory), and segment g multiplies B rows [g*N, (g+1)*N).
@@ -280,7 +358,9 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
       const int m0 = (tile % num_m) * TM + mb * BM;
       const int row = m0 + quad * 32 + lane;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * MB * BN + mb * BN;
-      if constexpr (EPI == kSwiGLU) {
+      if constexpr (EPI == kQkvRope) {
+        qkv_rope_row<BN>(rope, taddr, row, M, n0, reinterpret_cast<__nv_bfloat16*>(out), ldd);
+      } else if constexpr (EPI == kSwiGLU) {
         // Weight rows are interleaved in groups of 64: 32 gate rows then the
         // 32 up rows of the same output features.
         const int o0 = n0 / 2;
@@ -477,6 +557,62 @@ __device__ __forceinline__ float4 cluster_sum4(uint32_t red_base, int c, int rl,
   return acc;
 }
 
+// kQkvRope epilogue of the cluster kernel: thread t of the 128 epilogue
+// threads takes (row, head of the tile, 4 consecutive split-half pairs) items
+// of its CTA's band of rows [r0, r1), sums the cluster's partials for the 4
+// first-half and the 4 matching second-half columns, rotates (Q, K) or copies
+// (V) them and stores Q to `out`, K / V into the paged cache.
+template <int BN>
+__device__ __forceinline__ void qkv_rope_cluster(const RopeArgs& rp, uint32_t red_base, int c, int r0, int r1,
+                                                 int mrow0, int n0, int M, __nv_bfloat16* __restrict__ out, int ldd,
+                                                 int t) {
+  static_assert(BN % 128 == 0, "whole heads per tile");
+  constexpr int kHeads = BN / 128;
+  constexpr int kPerRow = kHeads * 16;
+  for (int i = t; i < (r1 - r0) * kPerRow; i += 128) {
+    const int rl = r0 + i / kPerRow;
+    const int j = (i / 16) % kHeads;
+    const int q = (i % 16) * 4;  // first of the 4 pairs
+    const int grow = mrow0 + rl;
+    if (grow >= M) continue;
+    const int hd = n0 / 128 + j;
+    const bool is_q = hd < rp.Hq;
+    const bool is_v = hd >= rp.Hq + rp.Hkv;
+    const int pos = rp.positions[grow];
+    const int slot = rp.slots[grow];
+    const bool pos_ok = pos >= 0 && pos < rp.max_pos;
+    if (!pos_ok && q == 0 && j == 0) set_error(kErrBadIndex, (unsigned long long)grow);
+    const bool slot_ok = slot >= 0 && (int64_t)slot < rp.num_slots;
+    if (!is_q && !slot_ok) continue;
+    const float4 a = cluster_sum4<BN>(red_base, c, rl, j * 128 + q);
+    const float4 b = cluster_sum4<BN>(red_base, c, rl, j * 128 + 64 + q);
+    float o1[4] = {a.x, a.y, a.z, a.w}, o2[4] = {b.x, b.y, b.z, b.w};
+    if (!is_v) {
+      const float4* cs4 = reinterpret_cast<const float4*>(rp.cos_sin + (size_t)(pos_ok ? pos : 0) * 64 + q);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float4 cs = pos_ok ? cs4[e] : make_float4(1.f, 0.f, 1.f, 0.f);
+        const float2 r0v = rope_pair(o1[2 * e], o2[2 * e], make_float2(cs.x, cs.y));
+        const float2 r1v = rope_pair(o1[2 * e + 1], o2[2 * e + 1], make_float2(cs.z, cs.w));
+        o1[2 * e] = r0v.x;
+        o2[2 * e] = r0v.y;
+        o1[2 * e + 1] = r1v.x;
+        o2[2 * e + 1] = r1v.y;
+      }
+    }
+    __nv_bfloat16* dst;
+    if (is_q) {
+      dst = out + (size_t)grow * ldd + (size_t)hd * 128;
+    } else {
+      const int kh = is_v ? hd - rp.Hq - rp.Hkv : hd - rp.Hq;
+      const int pg = slot / rp.page, off = slot % rp.page;
+      dst = (is_v ? rp.vcache : rp.kcache) + (((size_t)pg * rp.Hkv + kh) * rp.page + off) * 128;
+    }
+    *reinterpret_cast<uint2*>(dst + q) = make_uint2(pack_bf16x2(o1[0], o1[1]), pack_bf16x2(o1[2], o1[3]));
+    *reinterpret_cast<uint2*>(dst + 64 + q) = make_uint2(pack_bf16x2(o2[0], o2[1]), pack_bf16x2(o2[2], o2[3]));
+  }
+}
+
 // Epilogue of the fused decode all-reduce (kAllReduceLL), run by the 128
 // epilogue threads (t) of a CTA on its band of rows [r0, r1) of the tile.
 // Output pairs (two bf16 of one row) are numbered p = (row * N + col) / 2 and
@@ -592,7 +728,7 @@ template <int BN, int STAGES, int OUT, int MB = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_cluster_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ out, int M, int N,
-                               int K, int ldd, int kb_per_split, const ar::LLArgs ll) {
+                               int K, int ldd, int kb_per_split, const ar::LLArgs ll, const RopeArgs rope) {
   using S = Smem<BN, STAGES, MB>;
   static_assert(ClusterRed<BN>::kBytes <= STAGES * S::kStageBytes, "partial tile must fit the pipeline buffers");
   static_assert(MB * BN <= 512, "accumulators must fit TMEM");
@@ -749,6 +885,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else if constexpr (OUT == kAllReduceLL) {
         ll_epilogue<BN>(ll, ep, red_base, c, r0, r1, mrow0, n0, M, N, ldd, reinterpret_cast<__nv_bfloat16*>(out), t);
+      } else if constexpr (OUT == kQkvRope) {
+        qkv_rope_cluster<BN>(rope, red_base, c, r0, r1, mrow0, n0, M, reinterpret_cast<__nv_bfloat16*>(out), ldd, t);
       } else {
         constexpr int kQuads = BN / 4;
         for (int i = t; i < (r1 - r0) * kQuads; i += 128) {

@@ -84,10 +84,10 @@ void launch_stack(const GemmArgs& a, cudaStream_t stream, int sms, int splits, i
   if (kb_per <= 0) kb_per = (a.K + BK - 1) / BK;
   if (EPI == kSplitF32) {
     gemm_bf16_kernel<BN, STAGES, EPI><<<grid, kThreads, Smem<BN, STAGES>::kTotal, stream>>>(
-        ta, tb, ws, a.M, a.N, a.K, a.N, splits, kb_per, ArArgs{}, nullptr, 0);
+        ta, tb, ws, a.M, a.N, a.K, a.N, splits, kb_per, ArArgs{}, nullptr, 0, RopeArgs{});
   } else {
     gemm_bf16_kernel<BN, STAGES, EPI><<<grid, kThreads, Smem<BN, STAGES>::kTotal, stream>>>(
-        ta, tb, a.D, a.M, a.N, a.K, (int)a.ldd, splits, kb_per, ArArgs{}, nullptr, 0);
+        ta, tb, a.D, a.M, a.N, a.K, (int)a.ldd, splits, kb_per, ArArgs{}, nullptr, 0, RopeArgs{});
   }
 }
 

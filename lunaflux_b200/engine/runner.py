@@ -227,8 +227,11 @@ class ModelRunner:
         ops, Hq, Hkv = self.ops, self.Hq, self.Hkv
         kc, vc = self._layer_kv(l)
         qkv, attn = self.qkv[:T], self.attn[:T]
-        self._proj(h, lw, "wqkv", qkv, 0)
-        ops.rope_kv_write(qkv, v["positions"], v["slots"], self.cos_sin, kc, vc, Hq, Hkv, self.P)
+        fused = (self._fp8(lw, "wqkv") is None and hasattr(ops, "qkv_rope")
+                 and ops.qkv_rope(h, lw.wqkv, qkv, v["positions"], v["slots"], self.cos_sin, kc, vc, Hq, Hkv, self.P))
+        if not fused:
+            self._proj(h, lw, "wqkv", qkv, 0)
+            ops.rope_kv_write(qkv, v["positions"], v["slots"], self.cos_sin, kc, vc, Hq, Hkv, self.P)
         if Rp:
             ops.attn_prefill(qkv[:Tp], attn[:Tp], v["p_qstart"], v["p_seqlen"], v["p_bt"], kc, vc, Hq, Hkv,
                              max_q_len, host={"q_start": hm.get("q_start"), "seq_lens": hm.get("seq_lens")})

@@ -7,6 +7,7 @@ count recorded while it was captured).
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -26,6 +27,9 @@ class KernelOps:
         self.launches = 0
         self.num_sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
         self._splitk = {}
+        # QKV GEMM with RoPE and the paged K / V write in its epilogue (one
+        # kernel instead of two); off unless LUNAFLUX_FUSE_QKV_ROPE=1
+        self.fuse_qkv_rope = os.environ.get("LUNAFLUX_FUSE_QKV_ROPE") == "1"
 
     def embed(self, ids, table, out):
         self.launches += 1
@@ -41,6 +45,16 @@ class KernelOps:
             return
         self.launches += 1   # plain tiles or cluster split-K: one kernel either way
         self.C.gemm(A, B, out, epi, 0, ws)
+
+    def qkv_rope(self, A, B, qkv, positions, slots, cos_sin, kc, vc, Hq, Hkv, page) -> bool:
+        """The fused QKV projection; False (nothing launched) when it is off
+        or the shape has no whole-head tile plan."""
+        if not self.fuse_qkv_rope or A.shape[0] == 0:
+            return False
+        if self.C.gemm_qkv_rope(A, B, qkv, positions, slots, cos_sin, kc, vc, Hq, Hkv, page):
+            self.launches += 1
+            return True
+        return False
 
     def rope_kv_write(self, qkv, positions, slots, cos_sin, kc, vc, Hq, Hkv, page):
         self.launches += 1

@@ -35,6 +35,9 @@ OPS: Tuple[OpEntry, ...] = (
             "csrc/kernels/gemm_fp8.cu"),
     OpEntry("rope_kv_write", "rope_kv_write", ("bf16",), "cap 7/8: RoPE and paged KV write",
             "csrc/kernels/elementwise.cu"),
+    OpEntry("linear_qkv_rope", "gemm_qkv_rope", ("bf16",),
+            "cap 3 + 7/8: QKV projection with RoPE and the paged KV write in the epilogue",
+            "csrc/kernels/gemm_bf16_kernel.cuh"),
     OpEntry("swiglu", "swiglu", ("bf16",), "cap 9: SwiGLU (also fused into the gate/up GEMM)",
             "csrc/kernels/elementwise.cu"),
     OpEntry("attn_prefill", "attn_prefill", ("bf16",), "cap 10: paged causal prefill attention",

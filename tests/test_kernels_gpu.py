@@ -419,3 +419,37 @@ def test_moe_kernels_match_torch(C):
         ref[rows_e] += (w * sel).sum(-1)[rows_e, None] * ye
     _close(out, ref, 3e-2, 5e-2, "moe forward")
     assert C.read_error(True)[0] == 0
+
+
+@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
+                    reason="QKV GEMM with RoPE + KV write epilogue: first GPU run pending "
+                           "(set LUNAFLUX_TEST_NEW_KERNELS=1)")
+@pytest.mark.parametrize("M,Hq,Hkv,K", [(1, 32, 8, 4096), (37, 32, 8, 4096), (256, 32, 8, 4096),
+                                        (200, 64, 8, 1024), (1000, 32, 8, 4096), (5000, 3, 1, 512),
+                                        (256, 4, 1, 4096)])
+def test_gemm_qkv_rope_matches_gemm_then_rope(C, M, Hq, Hkv, K):
+    """The fused QKV epilogue (cluster split-K, 256-row tiles and persistent
+    tiles, BN 256 and 128) against the GEMM followed by rope_kv_write: Q
+    columns and the K / V cache pages, within bf16 rounding."""
+    D, P, pages = 128, 16, 512
+    N = (Hq + 2 * Hkv) * D
+    g = torch.Generator(device="cuda").manual_seed(M + Hq)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    pos = torch.randint(0, 1000, (M,), device="cuda", generator=g, dtype=torch.int32)
+    slots = torch.randperm(pages * P, device="cuda", generator=g)[:M].int()
+    slots[::7] = -1                       # padding rows: no KV write
+    table = rope_table(1024, D, 500000.0).cuda()
+    kc = torch.zeros(pages, Hkv, P, D, device="cuda").bfloat16()
+    vc = torch.zeros_like(kc)
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+    ref = torch.empty(M, N, device="cuda").bfloat16()
+    C.gemm(A, B, ref, 0, 0, None)
+    C.rope_kv_write(ref, pos, slots, table, kc_ref, vc_ref, Hq, Hkv, P)
+    out = torch.zeros(M, N, device="cuda").bfloat16()
+    assert C.gemm_qkv_rope(A, B, out, pos, slots, table, kc, vc, Hq, Hkv, P)
+    torch.cuda.synchronize()
+    assert C.read_error(True)[0] == 0
+    _close(out[:, :Hq * D].float(), ref[:, :Hq * D].float(), 3e-2, 3e-2, "fused Q")
+    _close(kc.float(), kc_ref.float(), 3e-2, 3e-2, "fused K cache")
+    _close(vc.float(), vc_ref.float(), 3e-2, 3e-2, "fused V cache")
