@@ -332,6 +332,14 @@ static bool run_cluster(const GemmArgs& a, int epi, void* out, int64_t ldd, cuda
   return true;
 }
 
+}  // namespace gemm
+}  // namespace lf
+
+#include "gemm_bf16_2sm.cuh"
+
+namespace lf {
+namespace gemm {
+
 // Tile-width choice: the widest BN that still yields enough tiles to cover
 // the SMs (wide tiles reuse A best; narrow tiles spread a skinny decode GEMM
 // over more SMs so the weight stream uses all of HBM).
@@ -355,6 +363,7 @@ void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws, int
   if (a.M <= 0) return;
   (void)ws;
   (void)ws_elems;
+  if (bn == 0 && run_pair(a, epi, stream)) return;  // opt-in CTA-pair kernel for large GEMMs
   if (bn == 0 && run_cluster(a, epi, a.D, a.ldd, stream)) return;
   if (bn == 0 && a.M > BM && a.M <= 2 * BM && a.N % 256 == 0 && a.K % 8 == 0) {
     // 129..256 rows (decode batches): 256-row tiles, each weight slab staged

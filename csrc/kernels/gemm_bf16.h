@@ -32,6 +32,8 @@ int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out, int
 void set_cluster_mb2(int on);
 // Enables the single-kernel decode GEMM + low-latency all-reduce in run_allreduce_ll (off by default).
 void set_ll_gemm_fused(int on);
+// Enables the CTA-pair (tcgen05 cta_group::2) kernel for large GEMMs (off by default).
+void set_gemm_pair(int on);
 
 // Peer view of one tensor-parallel group for the fused GEMM + all-reduce.
 // Two symmetric bf16 regions of [rows, N] (every rank holds both, same size):

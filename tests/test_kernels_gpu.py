@@ -453,3 +453,29 @@ def test_gemm_qkv_rope_matches_gemm_then_rope(C, M, Hq, Hkv, K):
     _close(out[:, :Hq * D].float(), ref[:, :Hq * D].float(), 3e-2, 3e-2, "fused Q")
     _close(kc.float(), kc_ref.float(), 3e-2, 3e-2, "fused K cache")
     _close(vc.float(), vc_ref.float(), 3e-2, 3e-2, "fused V cache")
+
+
+@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
+                    reason="CTA-pair (cta_group::2) GEMM: first GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
+@pytest.mark.parametrize("M,N,K,epi", [(2048, 4096, 4096, 0), (8192, 6144, 4096, 0), (4096, 28672, 4096, 2),
+                                       (300, 32768, 512, 1), (2048, 4096, 1000, 0)])
+def test_gemm_cta_pair(C, M, N, K, epi):
+    """256 x 256 tiles on CTA pairs (tcgen05.mma cta_group::2, B split over
+    the pair): values against the fp32 reference, including a pair whose
+    second CTA's rows are all past M and a K tail."""
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    out_cols = N // 2 if epi == 2 else N
+    D = torch.empty(M, out_cols, device="cuda", dtype=torch.float32 if epi == 1 else torch.bfloat16)
+    C.gemm_set_pair(True)
+    try:
+        C.gemm(A, B, D, epi, 0, None)
+        torch.cuda.synchronize()
+    finally:
+        C.gemm_set_pair(False)
+    assert C.read_error(True)[0] == 0
+    ref = A.float() @ B.float().t()
+    if epi == 2:
+        v = ref.view(M, N // 64, 2, 32)
+        ref = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(M, N // 2)
+    _close(D, ref, 3e-2, 3e-2, f"cta-pair gemm {M}x{N}x{K} epi={epi}")
