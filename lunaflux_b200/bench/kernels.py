@@ -1,6 +1,6 @@
 """Kernel micro-benchmarks: each hot sm_100a kernel against its library baseline.
 
-    python -m lunaflux_b200.bench.kernels [--only gemm|attn|norm] [--json out.json]
+    python -m lunaflux_b200.bench.kernels [--only gemm|attn|norm] [--json out.json] [--variants]
 
 Timing: CUDA events on the launching stream, warm-up first, an L2 flush (a
 256 MB write) before every timed launch, median of the timed launches.  The
@@ -57,7 +57,7 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def bench_gemm(C, results, only_case=""):
+def bench_gemm(C, results, only_case="", variants=False):
     hbm, tflops_peak, src = peaks()
     shapes = [
         ("prefill qkv", 8192, 6144, 4096, 0), ("prefill o", 8192, 4096, 4096, 0),
@@ -92,6 +92,15 @@ def bench_gemm(C, results, only_case=""):
             def base():
                 A @ B.t()
         ref = time_fn(base)
+        extra = {}
+        if variants:
+            # opt-in kernel variants of the same call, timed the same way
+            for key, setter in (("pair_ms", C.gemm_set_pair), ("cluster_256_rows_ms", C.gemm_set_cluster_mb2)):
+                setter(True)
+                try:
+                    extra[key] = time_fn(lambda: C.gemm(A, B, D, epi, 0, ws))
+                finally:
+                    setter(False)
         flops = 2.0 * M * N * K
         bytes_ = 2.0 * (M * K + N * K) + D.numel() * D.element_size()
         t_roof = max(flops / (tflops_peak * 1e12), bytes_ / (hbm * 1e9)) * 1e3
@@ -99,10 +108,38 @@ def bench_gemm(C, results, only_case=""):
         r = dict(kernel="gemm_bf16", case=name, M=M, N=N, K=K, bn=cbn if c else C.gemm_choose_bn(M, N, epi),
                  cluster_splitk=c, cluster_rows=128 * cmb if c else None, ours_ms=ours,
                  torch_ms=ref, speedup=ref / ours, tflops=flops / ours / 1e9, roofline_ms=t_roof,
-                 frac_of_roofline=t_roof / ours, peaks=src)
+                 frac_of_roofline=t_roof / ours, peaks=src, **extra)
         results.append(r)
         print(json.dumps(r))
         del A, B, D
+
+
+def bench_qkv_rope(C, results):
+    """QKV projection followed by RoPE + paged KV write, against the single
+    kernel with both in its epilogue (Llama-3-8B heads at TP 1)."""
+    Hq, Hkv, D, P = 32, 8, 128, 16
+    K, N = 4096, (32 + 16) * 128
+    pages = 4096
+    table = torch.randn(8192, D // 2, 2, device="cuda")
+    kc = torch.zeros(pages, Hkv, P, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    B = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    for M in (256, 8192):
+        A = torch.randn(M, K, device="cuda").bfloat16()
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        pos = torch.randint(0, 8192, (M,), device="cuda", dtype=torch.int32)
+        slots = torch.randperm(pages * P, device="cuda")[:M].int()
+
+        def two():
+            C.gemm(A, B, out, 0, 0, None)
+            C.rope_kv_write(out, pos, slots, table, kc, vc, Hq, Hkv, P)
+
+        def one():
+            C.gemm_qkv_rope(A, B, out, pos, slots, table, kc, vc, Hq, Hkv, P)
+
+        r = dict(kernel="qkv_rope", M=M, N=N, K=K, gemm_then_rope_ms=time_fn(two), fused_ms=time_fn(one))
+        results.append(r)
+        print(json.dumps(r))
 
 
 def bench_attn(C, results):
@@ -176,11 +213,15 @@ def main():
     ap.add_argument("--only", default="")
     ap.add_argument("--json", default="")
     ap.add_argument("--case", default="", help="run only this GEMM case (for profiler captures)")
+    ap.add_argument("--variants", action="store_true",
+                    help="also time the opt-in GEMM variants (CTA pair, 256-row cluster tiles) and the fused QKV")
     args = ap.parse_args()
     C = _ext.load()
     results = []
     if args.only in ("", "gemm"):
-        bench_gemm(C, results, args.case)
+        bench_gemm(C, results, args.case, args.variants)
+    if args.variants and args.only in ("", "gemm"):
+        bench_qkv_rope(C, results)
     if args.only in ("", "attn"):
         bench_attn(C, results)
     if args.only in ("", "norm"):
