@@ -390,6 +390,32 @@ void sample(const at::Tensor& logits, const at::Tensor& params, at::Tensor& out,
                  status.has_value() ? status->data_ptr<int32_t>() : nullptr, stream());
 }
 
+// Vocabulary-parallel sampling, step 1: keys [rows, kc + 1] int64 (this
+// shard's kc largest keys, then a status word).
+void topk_keys(const at::Tensor& logits, int64_t id_offset, int64_t kc, at::Tensor& keys) {
+  check_rowmajor(logits, "logits");
+  LF_CHECK(logits.scalar_type() == at::kFloat, "logits must be fp32");
+  LF_CHECK(kc >= 1 && kc <= 1024, "kc in [1, 1024]");
+  LF_CHECK(keys.scalar_type() == at::kLong && keys.is_contiguous() && keys.numel() >= logits.size(0) * (kc + 1),
+           "keys must be int64 [rows, kc + 1]");
+  c10::cuda::CUDAGuard g(logits.device());
+  lf::ew::topk_keys(logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1), (int)id_offset,
+                    (int)kc, reinterpret_cast<unsigned long long*>(keys.data_ptr<int64_t>()), stream());
+}
+
+// Step 2: the draw over every shard's candidates (keys [ranks, rows, kc + 1]).
+void sample_keys(const at::Tensor& keys, int64_t rows, int64_t ranks, int64_t kc, const at::Tensor& params,
+                 at::Tensor& out, c10::optional<at::Tensor> status) {
+  LF_CHECK(keys.scalar_type() == at::kLong && keys.is_contiguous() && keys.numel() >= ranks * rows * (kc + 1),
+           "keys must be int64 [ranks, rows, kc + 1]");
+  LF_CHECK(params.is_contiguous() && params.nbytes() >= (size_t)rows * sizeof(lf::ew::SampleParams),
+           "sample params: one 32-byte record per row");
+  c10::cuda::CUDAGuard g(keys.device());
+  lf::ew::sample_keys(reinterpret_cast<const unsigned long long*>(keys.data_ptr<int64_t>()), rows, ranks, kc,
+                      reinterpret_cast<const lf::ew::SampleParams*>(params.data_ptr()), out.data_ptr<int32_t>(),
+                      status.has_value() ? status->data_ptr<int32_t>() : nullptr, stream());
+}
+
 void attn_decode(const at::Tensor& q, at::Tensor& out, const at::Tensor& tok_index, const at::Tensor& seq_lens,
                  const at::Tensor& block_table, const at::Tensor& kcache, const at::Tensor& vcache, int64_t Hq,
                  int64_t Hkv, int64_t splits, c10::optional<at::Tensor> part_o, c10::optional<at::Tensor> part_lse) {
@@ -502,6 +528,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_keys", &argmax_keys);
   m.def("keys_to_tokens", &keys_to_tokens);
   m.def("sample", &sample, py::arg("logits"), py::arg("params"), py::arg("out"), py::arg("status") = py::none());
+  m.def("topk_keys", &topk_keys);
+  m.def("sample_keys", &sample_keys, py::arg("keys"), py::arg("rows"), py::arg("ranks"), py::arg("kc"),
+        py::arg("params"), py::arg("out"), py::arg("status") = py::none());
   m.def("attn_decode", &attn_decode);
   m.def("attn_decode_splits", &attn_decode_splits);
   m.def("attn_prefill", &attn_prefill, py::arg("q"), py::arg("out"), py::arg("q_start"), py::arg("seq_lens"),

@@ -364,68 +364,103 @@ __host__ __device__ inline double counter_unit(uint64_t seed, int64_t sample_ind
   return (double)(v >> 11) * 1.1102230246251565e-16;
 }
 
-// Per-row sampling parameters (SampleParams in elementwise.h).
-// For each row: mode 0 = greedy, 1 = sample.
-//
-// Stochastic rows: every quantity over the sorted order is computed as a
-// function of a composite-key threshold K ("all tokens whose key >= K" is a
-// prefix of the reference's sorted order), and the thresholds are found by
-// bisection on the 64-bit key space (64 passes).  No sort and no scratch.
-template <int NT>
-__global__ void __launch_bounds__(NT) sample_kernel(const float* __restrict__ logits, int64_t ld, int V,
-                                                    const SampleParams* __restrict__ params,
-                                                    int32_t* __restrict__ out_tok, int32_t* __restrict__ status) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ uint64_t shk[NT / 32];
-  __shared__ double shd[NT / 32];
-  __shared__ int shi[NT / 32];
-  const int r = blockIdx.x;
-  const float* row = logits + (size_t)r * ld;
-  const SampleParams p = params[r];
+// Inverse of fkey.
+__device__ __forceinline__ float key_value(uint64_t k) {
+  const uint32_t u = (uint32_t)(k >> 32);
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+}
 
+// Entry sources of the sampler.  get(i, v, k) yields entry i's logit and
+// composite key (false: no entry there); bad(i) says whether entry i makes
+// the row invalid (a non-finite logit).
+struct RowSource {  // one full logits row: entry i is token i
+  const float* row;
+  int n;
+  __device__ __forceinline__ bool get(int i, float& v, uint64_t& k) const {
+    v = row[i];
+    if (!isfinite(v)) return false;
+    k = ckey(v, i);
+    return true;
+  }
+  __device__ __forceinline__ bool bad(int i) const { return !isfinite(row[i]); }
+};
+
+// The candidate keys of every vocabulary shard for one row (see
+// topk_keys_kernel): `ranks` blocks of `per` words, the last word of a block
+// being the shard's status (1 ok, 2 non-finite logits), unused slots 0.
+struct CandidateSource {
+  const unsigned long long* keys;  // [ranks][rows][per]
+  int row, rows, per, n;           // n = ranks * per
+  __device__ __forceinline__ const unsigned long long* at(int i) const {
+    return keys + ((size_t)(i / per) * rows + row) * per + i % per;
+  }
+  __device__ __forceinline__ bool get(int i, float& v, uint64_t& k) const {
+    if (i % per == per - 1) return false;
+    k = *at(i);
+    if (k == 0) return false;
+    v = key_value(k);
+    return true;
+  }
+  __device__ __forceinline__ bool bad(int i) const { return i % per == per - 1 && *at(i) == 2; }
+};
+
+// Counter-addressed sampling of one row (block of NT threads).  Every quantity
+// over the sorted order is a function of a composite-key threshold K ("all
+// entries whose key >= K" is a prefix of the reference's sorted order); the
+// thresholds are found by bisection on the 64-bit key space (64 passes).  No
+// sort and no scratch.  The result depends only on the entries' keys, so a
+// row given as per-shard candidates (every key of the top-k set present)
+// samples the same token as the full row.
+template <int NT, class Src>
+__device__ void sample_row(const Src& src, const SampleParams p, int32_t* out_tok, int32_t* status, uint64_t* shk,
+                           double* shd, int* shi) {
+  const int n = src.n;
   // Pass 1: validation and the top key (max logit, lowest id).
   uint64_t best = 0;
   int bad = 0;
-  for (int i = threadIdx.x; i < V; i += NT) {
-    const float v = row[i];
-    if (!isfinite(v)) { bad = 1; continue; }
-    const uint64_t k = ckey(v, i);
-    best = k > best ? k : best;
+  for (int i = threadIdx.x; i < n; i += NT) {
+    float v;
+    uint64_t k;
+    if (src.bad(i)) bad = 1;
+    if (src.get(i, v, k)) best = k > best ? k : best;
   }
   best = block_max_u64<NT>(best, shk);
   bad = block_sum_i<NT>(bad, shi);
   const int top_id = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
   if (bad) {
-    if (threadIdx.x == 0) { out_tok[r] = top_id; if (status) status[r] = -1; }
+    if (threadIdx.x == 0) { *out_tok = top_id; if (status) *status = -1; }
     return;
   }
   if (p.mode == 0 || !(p.temperature > 0.f)) {
-    if (threadIdx.x == 0) { out_tok[r] = top_id; if (status) status[r] = 0; }
+    if (threadIdx.x == 0) { *out_tok = top_id; if (status) *status = 0; }
     return;
   }
-  const float mx = row[top_id];
+  const float mx = key_value(best);
   const float inv_t = 1.0f / p.temperature;
 
   // Key-space bisection helpers.
   auto count_ge = [&](uint64_t K) -> int {
     int c = 0;
-    for (int i = threadIdx.x; i < V; i += NT) c += ckey(row[i], i) >= K;
+    for (int i = threadIdx.x; i < n; i += NT) {
+      float v;
+      uint64_t k;
+      c += src.get(i, v, k) && k >= K;
+    }
     return block_sum_i<NT>(c, shi);
   };
   auto mass_ge = [&](uint64_t K, uint64_t floor_key) -> double {
     double m = 0.0;
-    for (int i = threadIdx.x; i < V; i += NT) {
-      const float v = row[i];
-      const uint64_t k = ckey(v, i);
-      if (k >= K && k >= floor_key) m += (double)__expf((v - mx) * inv_t);
+    for (int i = threadIdx.x; i < n; i += NT) {
+      float v;
+      uint64_t k;
+      if (src.get(i, v, k) && k >= K && k >= floor_key) m += (double)__expf((v - mx) * inv_t);
     }
     return block_sum_f64<NT>(m, shd);
   };
 
   // Top-k: the k-th largest key (largest K with count_ge(K) >= k).
   uint64_t kfloor = 0;
-  if (p.top_k > 0 && p.top_k < V) {
+  if (p.top_k > 0 && count_ge(0) > p.top_k) {
     uint64_t lo = 0, hi = best;  // invariant: count_ge(lo) >= k, answer in [lo, hi]
     while (lo < hi) {
       const uint64_t mid = lo + (hi - lo + 1) / 2;
@@ -465,16 +500,119 @@ __global__ void __launch_bounds__(NT) sample_kernel(const float* __restrict__ lo
   }
   // `lo` is a key threshold; the selected token is the smallest existing key >= lo.
   uint64_t sel = ~0ull;
-  for (int i = threadIdx.x; i < V; i += NT) {
-    const uint64_t k = ckey(row[i], i);
-    if (k >= lo && k < sel) sel = k;
+  for (int i = threadIdx.x; i < n; i += NT) {
+    float v;
+    uint64_t k;
+    if (src.get(i, v, k) && k >= lo && k < sel) sel = k;
   }
   // block min via max of complements
   sel = ~block_max_u64<NT>(~sel, shk);
   if (threadIdx.x == 0) {
-    out_tok[r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(sel & 0xFFFFFFFFull));
-    if (status) status[r] = 0;
+    *out_tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(sel & 0xFFFFFFFFull));
+    if (status) *status = 0;
   }
+}
+
+// Per-row sampling parameters (SampleParams in elementwise.h); mode 0 =
+// greedy, 1 = sample.
+template <int NT>
+__global__ void __launch_bounds__(NT) sample_kernel(const float* __restrict__ logits, int64_t ld, int V,
+                                                    const SampleParams* __restrict__ params,
+                                                    int32_t* __restrict__ out_tok, int32_t* __restrict__ status) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ uint64_t shk[NT / 32];
+  __shared__ double shd[NT / 32];
+  __shared__ int shi[NT / 32];
+  const int r = blockIdx.x;
+  const RowSource src{logits + (size_t)r * ld, V};
+  sample_row<NT>(src, params[r], out_tok + r, status ? status + r : nullptr, shk, shd, shi);
+}
+
+// Vocabulary-parallel sampling, step 1: per row, the keys of this shard's kc
+// largest finite logits (token ids offset by id_offset) and a status word
+// (1 ok, 2 the shard has non-finite logits): out[row][0..kc] (unused slots 0).
+// The kc-th largest key is found by bisection on the key space.
+template <int NT>
+__global__ void __launch_bounds__(NT) topk_keys_kernel(const float* __restrict__ logits, int64_t ld, int V,
+                                                       int id_offset, int kc,
+                                                       unsigned long long* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ uint64_t shk[NT / 32];
+  __shared__ int shi[NT / 32];
+  __shared__ int s_count;
+  const float* row = logits + (size_t)blockIdx.x * ld;
+  unsigned long long* dst = out + (size_t)blockIdx.x * (kc + 1);
+  uint64_t best = 0;
+  int bad = 0, finite = 0;
+  for (int i = threadIdx.x; i < V; i += NT) {
+    const float v = row[i];
+    if (!isfinite(v)) { bad = 1; continue; }
+    ++finite;
+    const uint64_t k = ckey(v, i + id_offset);
+    best = k > best ? k : best;
+  }
+  best = block_max_u64<NT>(best, shk);
+  bad = block_sum_i<NT>(bad, shi);
+  finite = block_sum_i<NT>(finite, shi);
+  uint64_t thr = 0;
+  if (finite > kc) {
+    uint64_t lo = 0, hi = best;  // count of keys >= lo is >= kc
+    while (lo < hi) {
+      const uint64_t mid = lo + (hi - lo + 1) / 2;
+      int c = 0;
+      for (int i = threadIdx.x; i < V; i += NT) {
+        const float v = row[i];
+        c += isfinite(v) && ckey(v, i + id_offset) >= mid;
+      }
+      if (block_sum_i<NT>(c, shi) >= kc) lo = mid; else hi = mid - 1;
+    }
+    thr = lo;
+  }
+  if (threadIdx.x == 0) s_count = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < V; i += NT) {
+    const float v = row[i];
+    if (!isfinite(v)) continue;
+    const uint64_t k = ckey(v, i + id_offset);
+    if (k >= thr) {
+      const int slot = atomicAdd(&s_count, 1);
+      if (slot < kc) dst[slot] = k;
+    }
+  }
+  __syncthreads();
+  for (int j = s_count + threadIdx.x; j < kc; j += NT) dst[j] = 0;
+  if (threadIdx.x == 0) dst[kc] = bad ? 2ull : 1ull;
+}
+
+// Vocabulary-parallel sampling, step 2: the draw over the gathered candidates
+// of every shard (keys [ranks][rows][kc + 1]).  Exact when every stochastic
+// row has 0 < top_k <= kc (the top-k set is then among the candidates).
+template <int NT>
+__global__ void __launch_bounds__(NT) sample_keys_kernel(const unsigned long long* __restrict__ keys, int rows,
+                                                         int ranks, int kc, const SampleParams* __restrict__ params,
+                                                         int32_t* __restrict__ out_tok, int32_t* __restrict__ status) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ uint64_t shk[NT / 32];
+  __shared__ double shd[NT / 32];
+  __shared__ int shi[NT / 32];
+  const int r = blockIdx.x;
+  const CandidateSource src{keys, r, rows, kc + 1, ranks * (kc + 1)};
+  sample_row<NT>(src, params[r], out_tok + r, status ? status + r : nullptr, shk, shd, shi);
+}
+
+void topk_keys(const float* logits, int64_t ld, int R, int V, int id_offset, int kc, unsigned long long* out,
+               cudaStream_t s) {
+  if (R <= 0) return;
+  launch_k(topk_keys_kernel<512>, dim3(R), dim3(512), 0, s, 1, logits, ld, V, id_offset, kc, out);
+}
+
+void sample_keys(const unsigned long long* keys, int R, int ranks, int kc, const SampleParams* params, int32_t* out,
+                 int32_t* status, cudaStream_t s) {
+  if (R <= 0) return;
+  launch_k(sample_keys_kernel<256>, dim3(R), dim3(256), 0, s, 1, keys, R, ranks, kc, params, out, status);
 }
 
 void sample(const float* logits, int64_t ld, int R, int V, const SampleParams* params, int32_t* out, int32_t* status,

@@ -26,6 +26,13 @@ void argmax(const float* logits, int64_t ld, int R, int V, int32_t* out, int32_t
 void argmax_keys(const float* logits, int64_t ld, int R, int V, int id_offset, unsigned long long* keys,
                  cudaStream_t s);
 void keys_to_tokens(const unsigned long long* keys, int R, int ranks, int32_t* out, cudaStream_t s);
+// Vocabulary-parallel sampling: each shard's kc largest keys plus a status
+// word per row (out [R][kc + 1]); then the draw over all shards' candidates
+// (keys [ranks][R][kc + 1]), exact for rows with 0 < top_k <= kc.
+void topk_keys(const float* logits, int64_t ld, int R, int V, int id_offset, int kc, unsigned long long* out,
+               cudaStream_t s);
+void sample_keys(const unsigned long long* keys, int R, int ranks, int kc, const SampleParams* params, int32_t* out,
+                 int32_t* status, cudaStream_t s);
 void sample(const float* logits, int64_t ld, int R, int V, const SampleParams* params, int32_t* out, int32_t* status,
             cudaStream_t s);
 double host_counter_unit(uint64_t seed, int64_t idx);

@@ -40,10 +40,27 @@ def rope_table(max_pos: int, head_dim: int, theta: float, device=None, scaling: 
     return t if device is None else t.to(device)
 
 
+# Candidates per vocabulary shard for the vocabulary-parallel stochastic sampler.
+SAMPLE_KC = 64
+# forward()'s sampling mode: greedy, stochastic, stochastic with every
+# stochastic row's top_k in (0, SAMPLE_KC].
+SAMPLE_GREEDY, SAMPLE_FULL, SAMPLE_TOPK = 0, 1, 2
+
+
+def sample_mode(rows, candidates: bool) -> int:
+    stoch = [r for r in rows if r.sample and r.req.sampling.mode.value == 1]
+    if not stoch:
+        return SAMPLE_GREEDY
+    if candidates and all(0 < (r.req.sampling.top_k or 0) <= SAMPLE_KC for r in stoch):
+        return SAMPLE_TOPK
+    return SAMPLE_FULL
+
+
 class ModelRunner:
     def __init__(self, weights: ModelWeights, ops, device, num_pages: int, max_tokens: int, max_rows: int,
                  max_context: int, page: int = 16, graph_sizes: Sequence[int] = (), comm=None,
-                 check_errors_every: int = 16, sequence_parallel: bool = False, overlap: bool = False):
+                 check_errors_every: int = 16, sequence_parallel: bool = False, overlap: bool = False,
+                 sample_candidates: bool = False):
         self.w = weights
         self.spec: LlamaSpec = weights.spec
         self.shard = weights.shard
@@ -105,6 +122,13 @@ class ModelRunner:
             self.q8s = torch.zeros(T * (kmax // 128), dtype=torch.float32, device=dev)
         self.keys_local = torch.zeros(R, dtype=torch.int64, device=dev)
         self.keys_all = torch.zeros(R * sh.size, dtype=torch.int64, device=dev)
+        # Vocabulary-parallel stochastic sampling from per-shard candidates
+        # (each shard's SAMPLE_KC largest keys; exact when every stochastic row
+        # has 0 < top_k <= SAMPLE_KC) instead of gathering every shard's logits.
+        self.sample_candidates = bool(sample_candidates) and sh.size > 1
+        if self.sample_candidates:
+            self.cand_local = torch.zeros(R * (SAMPLE_KC + 1), dtype=torch.int64, device=dev)
+            self.cand_all = torch.zeros(sh.size * R * (SAMPLE_KC + 1), dtype=torch.int64, device=dev)
         # split-K GEMM workspace (kept all-zero between GEMMs) and split-KV decode partials
         ws_elems = 512 * max(32768, sh.qkv_size, 2 * sh.ffn_padded)
         if s.fp8_block and comm is not None and getattr(comm, "fused", False):
@@ -202,7 +226,16 @@ class ModelRunner:
         out = self.out_tok[:Rs]
         tp = self.shard.size
         if self.comm is not None and tp > 1:
-            if stochastic:
+            if stochastic == SAMPLE_TOPK and self.sample_candidates:
+                # every stochastic row keeps at most SAMPLE_KC tokens: exchange
+                # each shard's SAMPLE_KC largest keys, then draw on every rank
+                kc = SAMPLE_KC
+                cand = self.cand_local[: Rs * (kc + 1)]
+                ops.topk_keys(logits, self.shard.rank * self.shard.vocab, kc, cand)
+                allc = self.cand_all[: tp * Rs * (kc + 1)]
+                self.comm.all_gather_flat(cand, allc)
+                ops.sample_keys(allc, Rs, tp, kc, v["s_params"], out)
+            elif stochastic:
                 # top-k / top-p need the whole distribution: gather the vocab shards
                 full = self.full_logits[:Rs]
                 self.comm.all_gather_cols(logits, full)
@@ -424,7 +457,7 @@ class ModelRunner:
         Returns a handle for ``wait``; nothing here waits for the device."""
         rows = plan.rows
         decode_only = all(r.decode for r in rows)
-        stoch = any(r.sample and r.req.sampling.mode.value == 1 for r in rows)
+        stoch = sample_mode(rows, self.sample_candidates)
         bucket = None
         if decode_only and self.graph_sizes and self.device.type == "cuda":
             nd = len(rows)

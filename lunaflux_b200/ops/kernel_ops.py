@@ -90,6 +90,14 @@ class KernelOps:
         self.launches += 1
         self.C.keys_to_tokens(keys, rows, ranks, out)
 
+    def topk_keys(self, logits, id_offset, kc, keys):
+        self.launches += 1
+        self.C.topk_keys(logits, id_offset, kc, keys)
+
+    def sample_keys(self, keys, rows, ranks, kc, params, out):
+        self.launches += 1
+        self.C.sample_keys(keys, rows, ranks, kc, params, out)
+
     # ---------------------------------------------------------------- MoE
     def moe_route(self, h, router, bias, topk, ids, weights):
         self.launches += 1

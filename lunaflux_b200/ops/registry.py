@@ -51,6 +51,10 @@ OPS: Tuple[OpEntry, ...] = (
             "csrc/kernels/elementwise.cu"),
     OpEntry("sample", "sample", ("fp32",), "sampling: top-k / top-p / temperature, counter RNG",
             "csrc/kernels/elementwise.cu"),
+    OpEntry("topk_keys", "topk_keys", ("fp32",), "sampling: vocab-parallel per-shard candidate keys",
+            "csrc/kernels/elementwise.cu"),
+    OpEntry("sample_keys", "sample_keys", ("int64",), "sampling: vocab-parallel draw over gathered candidates",
+            "csrc/kernels/elementwise.cu"),
     OpEntry("moe_route", "moe_route", ("bf16",), "new: MoE router top-k", "csrc/kernels/moe.cu"),
     OpEntry("moe_align", "moe_align", ("int32",), "new: MoE expert-ordered permutation", "csrc/kernels/moe.cu"),
     OpEntry("moe_gather", "moe_gather", ("bf16",), "new: MoE gather", "csrc/kernels/moe.cu"),

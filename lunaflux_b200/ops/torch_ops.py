@@ -158,6 +158,55 @@ class TorchOps:
         fk = torch.where(u >= 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
         keys[:R] = (fk << 32) | (0xFFFFFFFF - (idx + id_offset))
 
+    @staticmethod
+    def _keys(logits, id_offset):
+        """Composite keys (logit, then lowest id) as unsigned-ordered int64:
+        the top bit is flipped so that signed comparison keeps the order."""
+        R, V = logits.shape
+        u = logits.float().contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+        fk = torch.where(u >= 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
+        ids = torch.arange(V, device=logits.device, dtype=torch.int64) + id_offset
+        return (fk << 32) | (0xFFFFFFFF - ids)[None, :]
+
+    def topk_keys(self, logits, id_offset, kc, keys):
+        R, V = logits.shape
+        k = self._keys(logits, id_offset)
+        finite = torch.isfinite(logits)
+        flip = torch.iinfo(torch.int64).min
+        ordered = torch.where(finite, k ^ flip, torch.full_like(k, flip))
+        n = min(kc, V)
+        top = ordered.topk(n, dim=1).values ^ flip
+        out = keys[: R * (kc + 1)].view(R, kc + 1)
+        out.zero_()
+        cnt = finite.sum(1)
+        for r in range(R):
+            m = int(min(n, int(cnt[r])))
+            out[r, :m] = top[r, :m]
+            out[r, kc] = 1 if bool(finite[r].all()) else 2
+
+    def sample_keys(self, keys, rows, ranks, kc, params, out):
+        k = keys[: ranks * rows * (kc + 1)].view(ranks, rows, kc + 1).cpu().numpy().astype(np.uint64)
+        p = params.detach().cpu().numpy().view(PARAM_DTYPE)[:rows]
+        res = np.zeros(rows, dtype=np.int32)
+        for r in range(rows):
+            c = k[:, r, :kc].reshape(-1)
+            c = c[c != 0]
+            hi = (c >> np.uint64(32)).astype(np.uint32)
+            bits = np.where(hi & 0x80000000, hi & 0x7FFFFFFF, ~hi).astype(np.uint32)
+            vals = bits.view(np.float32).astype(np.float64)
+            ids = (0xFFFFFFFF - (c & np.uint64(0xFFFFFFFF))).astype(np.int64)
+            top = int(ids[np.lexsort((ids, -vals))[0]])
+            bad = bool((k[:, r, kc] == 2).any())
+            if bad or p["mode"][r] == 0 or not p["temperature"][r] > 0:
+                res[r] = top
+                continue
+            tk = int(p["top_k"][r])
+            tp_ = float(p["top_p"][r])
+            u = counter_unit(int(p["seed"][r]), int(p["sample_index"][r]))
+            res[r] = stochastic_sample(vals, float(p["temperature"][r]), tk if tk > 0 else None,
+                                       tp_ if 0 < tp_ < 1 else None, u, ids=ids)
+        out[:rows] = torch.from_numpy(res).to(out.device)
+
     def keys_to_tokens(self, keys, rows, ranks, out):
         k = keys[: rows * ranks].view(ranks, rows)
         # int64 compare is signed; flip the top bit so unsigned order is kept

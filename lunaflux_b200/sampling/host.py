@@ -54,10 +54,13 @@ def greedy(logits: Sequence[float]) -> int:
     return int(np.argmax(a))  # numpy returns the first (lowest) index on ties
 
 
-def prepare_distribution(logits, temperature: float, top_k: Optional[int], top_p: Optional[float]
-                         ) -> Tuple[np.ndarray, np.ndarray, float]:
-    """Returns (token ids in sorted order, weights, retained mass) of the nucleus."""
+def prepare_distribution(logits, temperature: float, top_k: Optional[int], top_p: Optional[float],
+                         ids=None) -> Tuple[np.ndarray, np.ndarray, float]:
+    """Returns (token ids in sorted order, weights, retained mass) of the
+    nucleus.  ``ids`` gives the token id of each logit (default: its
+    position), for a distribution given as a subset of the vocabulary."""
     a = np.asarray(logits, dtype=np.float64)
+    tok = np.arange(a.size) if ids is None else np.asarray(ids, dtype=np.int64)
     if a.size == 0:
         raise SamplingError("empty input")
     if not (math.isfinite(temperature) and temperature > 0):
@@ -68,7 +71,7 @@ def prepare_distribution(logits, temperature: float, top_k: Optional[int], top_p
         raise SamplingError("invalid top_p")
     if not np.isfinite(a).all():
         raise SamplingError("non-finite logit")
-    order = np.lexsort((np.arange(a.size), -a))  # logit desc, then id asc
+    order = np.lexsort((tok, -a))  # logit desc, then id asc
     k = a.size if top_k is None else min(top_k, a.size)
     order = order[:k]
     mx = a[order[0]]
@@ -90,11 +93,12 @@ def prepare_distribution(logits, temperature: float, top_k: Optional[int], top_p
     ret = 0.0
     for x in w[:cnt]:
         ret += x
-    return order[:cnt], w[:cnt], ret
+    return tok[order[:cnt]], w[:cnt], ret
 
 
-def stochastic_sample(logits, temperature: float, top_k: Optional[int], top_p: Optional[float], u: float) -> int:
-    ids, w, mass = prepare_distribution(logits, temperature, top_k, top_p)
+def stochastic_sample(logits, temperature: float, top_k: Optional[int], top_p: Optional[float], u: float,
+                      ids=None) -> int:
+    ids, w, mass = prepare_distribution(logits, temperature, top_k, top_p, ids)
     target = u * mass
     cum = 0.0
     for i in range(len(ids)):

@@ -479,3 +479,29 @@ def test_gemm_cta_pair(C, M, N, K, epi):
         v = ref.view(M, N // 64, 2, 32)
         ref = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(M, N // 2)
     _close(D, ref, 3e-2, 3e-2, f"cta-pair gemm {M}x{N}x{K} epi={epi}")
+
+
+@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
+                    reason="vocab-parallel candidate sampler: first GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
+@pytest.mark.parametrize("ranks", [2, 8])
+def test_sample_from_shard_candidates_equals_full_row(C, ranks):
+    """Per-shard top-64 keys, gathered, then the draw: the same tokens as the
+    sampler over the whole row, for top_k <= 64 (greedy and stochastic rows)."""
+    from lunaflux_b200.sampling.host import pack_params
+    R, kc = 37, 64
+    V = 16032 * ranks                      # the Llama-3 vocabulary shard at TP 8, times the ranks
+    g = torch.Generator(device="cuda").manual_seed(ranks)
+    logits = torch.randn(R, V, device="cuda", generator=g) * 3
+    rows = [(0 if i % 5 == 0 else 1, 1 + (7 * i) % 64, 0.7 + 0.05 * (i % 9), 0.9 if i % 2 else 1.0, 1000 + i, i)
+            for i in range(R)]
+    params = torch.from_numpy(pack_params(rows).view("u1").copy()).cuda()
+    full = torch.empty(R, dtype=torch.int32, device="cuda")
+    C.sample(logits, params, full)
+    Vl = V // ranks
+    keys = torch.zeros(ranks, R, kc + 1, dtype=torch.int64, device="cuda")
+    for k in range(ranks):
+        C.topk_keys(logits[:, k * Vl:(k + 1) * Vl].contiguous(), k * Vl, kc, keys[k])
+    got = torch.empty(R, dtype=torch.int32, device="cuda")
+    C.sample_keys(keys, R, ranks, kc, params, got)
+    torch.cuda.synchronize()
+    assert torch.equal(got, full)
