@@ -154,7 +154,7 @@ def main():
         init_distributed("nccl", device_id=local)
     spec = specs.PRESETS[args.model]()
     if world > 1:
-        if args.impl == "ours" and args.comm == "fused" and not args.sp:
+        if args.impl == "ours" and args.comm == "fused":
             from lunaflux_b200.parallel.fused import FusedTPComm
             comm = FusedTPComm(args.step_token_budget + args.requests, spec.hidden, dev)
         else:

@@ -114,6 +114,30 @@ void gemm_allreduce(const at::Tensor& A, const at::Tensor& B, c10::optional<at::
   lf::gemm::run_allreduce(a, ar, stream(), wsp, ws_elems);
 }
 
+// Rows [rank * M / world, (rank + 1) * M / world) of the sum over ranks of
+// A . B^T into out_local [M / world, N] (the owner-computes tile path with the
+// owner keeping its rows; M / world a multiple of 128).
+void gemm_reduce_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& out_local, int64_t local, int64_t mc,
+                         std::vector<int64_t> peers, int64_t out_mc, std::vector<int64_t> out_peers,
+                         int64_t cnt_local, int64_t cnt_mc, std::vector<int64_t> cnt_peers, int64_t rank,
+                         int64_t cnt_capacity, int64_t trace) {
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  LF_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 &&
+               out_local.scalar_type() == at::kBFloat16 && out_local.is_contiguous(),
+           "gemm_reduce_scatter is bf16, contiguous output");
+  const int M = A.size(0), N = B.size(0), K = A.size(1);
+  lf::gemm::ArArgs ar =
+      make_ar(local, mc, peers, out_mc, out_peers, cnt_local, cnt_mc, cnt_peers, rank, cnt_capacity, trace);
+  LF_CHECK(M % ar.world == 0 && out_local.size(0) == M / ar.world && out_local.size(1) == N,
+           "gemm_reduce_scatter: out_local must be [M / world, N]");
+  ar.rs_rows = M / ar.world;
+  ar.rs_out = reinterpret_cast<__nv_bfloat16*>(out_local.data_ptr());
+  c10::cuda::CUDAGuard g(A.device());
+  lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), ar.out_peer[rank], M, N, K, A.stride(0), B.stride(0), N};
+  lf::gemm::run_reduce_scatter(a, ar, stream());
+}
+
 static lf::ar::LLArgs make_ll(const std::vector<int64_t>& rs, const std::vector<int64_t>& ag, int64_t ag_mc,
                               const at::Tensor& state, int64_t rank, int64_t max_pairs) {
   LF_CHECK(!rs.empty() && rs.size() <= (size_t)lf::ar::kMaxRanks && ag.size() == rs.size(), "low-latency all-reduce: peers");
@@ -513,6 +537,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8", &gemm_fp8);
   m.def("partials_allreduce", &partials_allreduce);
   m.def("gemm_allreduce_ll", &gemm_allreduce_ll);
+  m.def("gemm_reduce_scatter", &gemm_reduce_scatter);
   m.def("partials_allreduce_ll", &partials_allreduce_ll);
   m.def("act_quant", &act_quant);
   m.def("moe_route", &moe_route);

@@ -438,6 +438,25 @@ void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, flo
   }
 }
 
+void run_reduce_scatter(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream) {
+  if (a.M <= 0) return;
+  if (ar.world < 1 || ar.world > kMaxRanks || ar.rank < 0 || ar.rank >= ar.world)
+    throw std::runtime_error("lunaflux gemm_reduce_scatter: bad rank or world size");
+  if (ar.rs_rows <= 0 || ar.rs_rows % BM != 0 || (int64_t)ar.rs_rows * ar.world != a.M || ar.rs_out == nullptr)
+    throw std::runtime_error("lunaflux gemm_reduce_scatter: M must be world * rows, rows a multiple of 128");
+  if (a.N % 32 != 0 || a.K % 8 != 0) throw std::runtime_error("lunaflux gemm_reduce_scatter: N % 32 and K % 8 required");
+  const int bn = choose_bn(a.M, a.N, kStoreBf16);
+  const int tiles = (a.M / BM) * (a.N / bn);
+  if (tiles > ar.cnt_capacity - kFinReserved)
+    throw std::runtime_error("lunaflux gemm_reduce_scatter: too many tiles for the counters");
+  switch (bn) {
+    case 256: launch<256, 4, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
+    case 128: launch<128, 6, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
+    case 64: launch<64, 8, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
+    default: launch<32, 8, kAllReduceBf16>(a, stream, 1, 0, nullptr, ar); break;
+  }
+}
+
 // One kernel for the decode projection and its all-reduce (the cluster
 // split-K GEMM whose epilogue runs the low-latency protocol): off unless
 // LUNAFLUX_FUSED_LL_GEMM=1 or set_ll_gemm_fused(1).

@@ -82,6 +82,12 @@ struct ArArgs {
   // [4 t] partial published, [4 t + 1] owner saw every partial, [4 t + 2]
   // owner's sum written everywhere; [4 t + 3] = 1 + the owner CTA's index.
   unsigned long long* trace;
+  // Reduce-scatter mode (rs_rows > 0): rank r owns output rows
+  // [r rs_rows, (r + 1) rs_rows) (tiles are dealt by rows, rs_rows a multiple
+  // of 128), and the owner writes its sums only to rs_out ([rs_rows, N], row
+  // stride N) instead of every rank's result region.
+  int rs_rows;
+  __nv_bfloat16* rs_out;
 };
 
 // Sum of `splits` fp32 [M, N] slabs in ws, then the sum over the group, into
@@ -92,6 +98,10 @@ void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, 
 // computed and all-reduced over NVLink by one kernel (split-K shapes: the GEMM
 // and the finalize kernel that carries the all-reduce).  a.D is unused.
 void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, float* ws, int64_t ws_elems);
+// The row-parallel GEMM fused with a reduce-scatter by rows (ar.rs_rows,
+// ar.rs_out set; M == rs_rows * world): the owner-computes tile path with the
+// result kept by the owner.
+void run_reduce_scatter(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream);
 int choose_bn(int M, int N, int epi);
 // Decode shapes: GEMM into fp32 slabs of ws (split-K when it fills the SMs),
 // then the low-latency all-reduce (allreduce_ll.h) into a.D.

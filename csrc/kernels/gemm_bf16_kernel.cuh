@@ -76,6 +76,12 @@ __device__ __forceinline__ bool ar_wait(const ArArgs& ar, int idx, int target) {
   return true;
 }
 
+// Owner rank of an output tile: dealt round-robin (all-reduce), or by rows
+// (reduce-scatter mode).
+__device__ __forceinline__ int ar_owner(const ArArgs& ar, int tile, int num_m, int bm) {
+  return ar.rs_rows > 0 ? ((tile % num_m) * bm) / ar.rs_rows : tile % ar.world;
+}
+
 // Sum over ranks of the 8 bf16 partials at element offset `off` (fp32 accumulation).
 __device__ __forceinline__ uint4 ar_reduce8(const ArArgs& ar, size_t off) {
   uint4 r;
@@ -433,7 +439,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
         named_bar_sync(1, 128);
         if (threadIdx.x == 64) {
           fence_acq_rel_sys();
-          ar_signal_one(ar, tile % ar.world, tile);
+          ar_signal_one(ar, ar_owner(ar, tile, num_m, BM), tile);
           if (ar.trace != nullptr) ar.trace[4 * tile] = globaltimer_ns();
         }
       }
@@ -446,7 +452,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     const int t = threadIdx.x - 192;
     for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
       const int tile = unit % num_tiles;
-      if (tile % ar.world != ar.rank) continue;
+      if (ar_owner(ar, tile, num_m, BM) != ar.rank) continue;
       if (t == 0) {
         s_ar_ok = ar_wait(ar, tile, ar.world) ? 1 : 0;
         if (ar.trace != nullptr) ar.trace[4 * tile + 1] = globaltimer_ns();
@@ -473,8 +479,15 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
             if (r < M) v[j] = ar_reduce8(ar, off[j]);
           }
 #pragma unroll
-          for (int j = 0; j < kBatch; ++j)
-            if (off[j] != ~size_t(0)) ar_store8(ar, off[j], v[j]);
+          for (int j = 0; j < kBatch; ++j) {
+            if (off[j] == ~size_t(0)) continue;
+            if (ar.rs_rows > 0) {
+              // reduce-scatter: the owner keeps its rows
+              *reinterpret_cast<uint4*>(ar.rs_out + off[j] - (size_t)ar.rank * ar.rs_rows * N) = v[j];
+            } else {
+              ar_store8(ar, off[j], v[j]);
+            }
+          }
         }
       }
       named_bar_sync(2, 128);

@@ -297,6 +297,19 @@ class ModelRunner:
             comm.all_gather_rows(local, full)
             return full[:T]
 
+        def scatter_gemm(A, lw, name):
+            """delta = this rank's rows of the row-parallel projection: one
+            kernel with the reduce-scatter inside when the fused comm takes
+            the shape, else the partial GEMM and the library reduce-scatter."""
+            if (T == Tl * tp and self._fp8(lw, name) is None
+                    and hasattr(comm, "gemm_reduce_scatter")
+                    and comm.gemm_reduce_scatter(A, getattr(lw, name), delta)):
+                ops.launches += 1
+                return
+            part = self.delta[:T]
+            self._row_parallel_partial(A, lw, name, part, ws)
+            scatter_partial(part)
+
         def scatter_partial(partial_rows):
             # partial_rows: [T, H] this rank's partial sums; padding rows add zero
             if partial_rows.data_ptr() != full.data_ptr():
@@ -311,18 +324,16 @@ class ModelRunner:
                 ops.rmsnorm(delta, resid, lw.ln1, h, eps)
             hf = gather_rows(h)
             attn = self._attention(l, lw, v, hf, T, Tp, Rp, Rd, max_q_len, splits, hm)
-            o_part = self.delta[:T]
-            self._row_parallel_partial(attn, lw, "wo", o_part, ws)
-            scatter_partial(o_part)
+            scatter_gemm(attn, lw, "wo")
             ops.rmsnorm(delta, resid, lw.ln2, h, eps)
             hf = gather_rows(h)
-            d_part = self.delta[:T]
             if s.is_moe:
+                d_part = self.delta[:T]
                 self.moe(hf, d_part, lw, reduce=False)
+                scatter_partial(d_part)
             else:
                 self._proj(hf, lw, "wgu", act, 2)
-                self._row_parallel_partial(act, lw, "wd", d_part, ws)
-            scatter_partial(d_part)
+                scatter_gemm(act, lw, "wd")
         ops.rmsnorm(delta, resid, w.norm, h, eps)
         hf = gather_rows(h)
         return self._sample(hf, v, Rs, stochastic, gather)

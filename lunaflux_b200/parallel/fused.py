@@ -157,6 +157,19 @@ class FusedTPComm(TPComm):
         self.C.gemm_allreduce(A, B, ws, *self._args(s))
         return s["result"][: M * self.hidden].view(M, self.hidden)
 
+    def gemm_reduce_scatter(self, A: torch.Tensor, B: torch.Tensor, out_local: torch.Tensor) -> bool:
+        """out_local [M / world, hidden] = this rank's rows of the sum over
+        ranks of A . B^T, by the row-parallel GEMM with the reduce-scatter in
+        the kernel (owner-computes tiles dealt by rows).  Returns False, having
+        done nothing, when M / world is not a multiple of 128 or the shape
+        exceeds the symmetric buffer (the caller then reduces another way)."""
+        M = A.shape[0]
+        if M % self.world or (M // self.world) % 128 or M > self.max_rows or B.shape[0] != self.hidden:
+            return False
+        s = self._slot()
+        self.C.gemm_reduce_scatter(A, B, out_local, *self._args(s))
+        return True
+
     def reduce_partials(self, part: torch.Tensor) -> torch.Tensor:
         """Returns the bf16 sum over ranks of this rank's fp32 partial ``part``."""
         M, N = part.shape

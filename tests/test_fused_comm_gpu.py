@@ -117,3 +117,62 @@ def _run(fused_ll):
         for (ci, M, N, K, code, bad, mx) in errs:
             assert code == 0, f"rank {r} comm {ci} {M}x{N}x{K}: device error {code}"
             assert bad == 0, f"rank {r} comm {ci} {M}x{N}x{K}: {bad} elements off (max {mx}); multicast={mc}"
+
+
+def _rs_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    try:
+        from lunaflux_b200.parallel.comm import init_distributed
+        from lunaflux_b200.parallel.fused import FusedTPComm
+        init_distributed("nccl", timeout_s=120, device_id=rank)
+        comm = FusedTPComm(8192, 4096, dev)
+        errs = []
+        for it in range(3):
+            for rows, K in ((128, 512), (1024, 1792), (256, 4096 // world)):
+                M, N = rows * world, 4096
+                g = torch.Generator(device=dev).manual_seed(100 * rank + it + rows)
+                A = torch.randn(M, K, device=dev, generator=g).bfloat16()
+                B = (torch.randn(N, K, device=dev, generator=g) * 0.05).bfloat16()
+                part = A.float() @ B.float().t()
+                ref = torch.empty(rows, N, device=dev)
+                dist.reduce_scatter_tensor(ref, part)
+                out = torch.empty(rows, N, device=dev, dtype=torch.bfloat16)
+                ok = comm.gemm_reduce_scatter(A, B, out)
+                torch.cuda.synchronize(dev)
+                code = comm.C.read_error(True)[0]
+                err = (out.float() - ref).abs()
+                tol = (3e-2 + 3e-2 * ref.abs()) * max(1.0, world / 2)
+                errs.append((rows, K, ok, code, int((err > tol).sum().item()), float(err.max().item())))
+        q.put((rank, errs))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
+                    reason="GEMM + reduce-scatter: first multi-GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
+def test_gemm_reduce_scatter_matches_nccl():
+    """The row-parallel GEMM with the reduce-scatter in the kernel (tiles
+    dealt to their rows' owner) against the fp32 partials reduce-scattered by
+    NCCL, over repeated calls (both ping-pong slots)."""
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_rs_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r, errs in res.items():
+        assert not isinstance(errs, str), errs
+        for (rows, K, ok, code, bad, mx) in errs:
+            assert ok and code == 0 and bad == 0, (r, rows, K, ok, code, bad, mx)

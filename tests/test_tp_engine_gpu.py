@@ -59,7 +59,7 @@ def _worker(rank, world, port, q):
                                 emergency_decode_page_reserve=4)
         outs = {}
         for name, comm, sp in (("fused", FusedTPComm(512, spec.hidden, dev), False), ("nccl", TPComm(), False),
-                               ("sp", TPComm(), True)):
+                               ("sp", TPComm(), True), ("sp_fused", FusedTPComm(512, spec.hidden, dev), True)):
             opts = EngineOptions(max_context=1024, num_pages=256, graph_sizes=(1, 2, 4), overlap_steps=True,
                                  sequence_parallel=sp)
             eng = LLMEngine(w, KernelOps(), dev, sched, CacheConfig(prefix_enabled=False), opts, comm=comm)
@@ -94,7 +94,7 @@ def test_tp_engine_tracks_oracle():
     spec = _spec()
     ref = ReferenceModel(spec, _checkpoint(spec))
     prompts = _prompts(spec)
-    for name in ("fused", "nccl", "sp"):
+    for name in ("fused", "nccl", "sp", "sp_fused"):
         for r in range(world):
             assert res[r][name + "_err"] == 0, (name, r)
             assert res[r][name] == res[0][name], f"{name}: rank {r} differs from rank 0"
