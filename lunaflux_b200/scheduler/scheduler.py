@@ -353,6 +353,44 @@ class Scheduler:
         self.expire_deadlines()
         if not self.running and not self.waiting:
             return None
+        rows = self._plan_rows(admit=True)
+        while not rows and self.running and not self.inflight:
+            # Every running request is blocked on KV pages (none can take a
+            # row) and nothing in flight will free any: recompute the youngest
+            # (its pages go to the older ones), or fail a request that cannot
+            # fit the cache on its own.  No admission during the retry, so the
+            # freed pages reach the requests already running.
+            if len(self.running) > 1:
+                self._preempt(self.running[-1])
+            else:
+                req = self.running[0]
+                self.generation += 1
+                req.generation = self.generation
+                self._finish(req, RequestState.FAILED, None, PublicErrorCode.CONTEXT_OVERFLOW)
+            rows = self._plan_rows(admit=False)
+        if not rows:
+            return None
+        # advance the planning state (the committed state moves on completion)
+        slot = 0
+        for r in rows:
+            req = r.req
+            req.sched_len = r.start + r.n
+            if not r.decode and req.sched_len == req.prefill_target:
+                req.state = RequestState.DECODE
+            if r.sample:
+                r.sample_index = len(req.output) + req.pending
+                req.pending += 1
+                req.pending_slot = slot
+                slot += 1
+        self.step_seq += 1
+        plan = StepPlan(self.step_seq, rows)
+        self.inflight.append(plan)
+        return plan
+
+    def _plan_rows(self, admit: bool) -> List[Row]:
+        """Decode rows, then prefill chunks, within the step budget (KV pages
+        allocated as rows are chosen); waiting requests are admitted only when
+        ``admit``."""
         cfg = self.cfg
         budget = cfg.step_token_budget
         max_rows = cfg.max_rows_per_step
@@ -386,6 +424,8 @@ class Scheduler:
         aged = [r for r in self.waiting if self.step_seq - r.enqueued_step >= cfg.waiting_age_threshold_steps]
         partial = [r for r in self.running if r.state is RequestState.PREFILL]
         fresh = [r for r in self.waiting if r not in aged]
+        if not admit:
+            aged, fresh = [], []
         for req in aged + partial + fresh:
             if budget <= 0 or rows_used >= max_rows:
                 break
@@ -417,25 +457,7 @@ class Scheduler:
             budget -= chunk
             rows_used += 1
 
-        rows = prefill_rows + decode_rows
-        if not rows:
-            return None
-        # advance the planning state (the committed state moves on completion)
-        slot = 0
-        for r in rows:
-            req = r.req
-            req.sched_len = r.start + r.n
-            if not r.decode and req.sched_len == req.prefill_target:
-                req.state = RequestState.DECODE
-            if r.sample:
-                r.sample_index = len(req.output) + req.pending
-                req.pending += 1
-                req.pending_slot = slot
-                slot += 1
-        self.step_seq += 1
-        plan = StepPlan(self.step_seq, rows)
-        self.inflight.append(plan)
-        return plan
+        return prefill_rows + decode_rows
 
     def _preempt_new(self, req: Request):
         self.running.remove(req)

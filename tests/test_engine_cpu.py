@@ -166,3 +166,28 @@ def test_worker_failure_fails_active_keeps_waiting(tiny):
     assert eng.results[r1].error is PublicErrorCode.WORKER_UNAVAILABLE
     eng.run_until_done()
     assert len(eng.results[r2].tokens) == 5
+
+
+def test_page_starvation_never_stalls(tiny):
+    """Every running request blocked on KV pages mid-prefill: the scheduler
+    recomputes the youngest instead of stalling, and a request that cannot fit
+    the cache on its own fails with context_overflow."""
+    spec, ck = tiny
+    ref = ReferenceModel(spec, ck)
+    eng = engine(spec, ck, rows=4, budget=16, pages=6, prefix=False)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, 256, (n,), generator=g).tolist() for n in (30, 31, 29, 33)]
+    rids = [eng.add_request(p, 6) for p in prompts]
+    steps = eng.run_until_done(max_steps=2000)
+    assert not eng.has_work() and steps < 2000
+    for p, r in zip(prompts, rids):
+        assert eng.results[r].tokens == ref.generate_greedy(p, 6)
+    assert eng.scheduler.preemptions > 0
+    from lunaflux_b200.scheduler.scheduler import AdmissionRejected
+    with pytest.raises(AdmissionRejected):
+        eng.add_request(torch.randint(0, 256, (100,), generator=g).tolist(), 4)      # 7 pages > 6
+    big = eng.add_request(torch.randint(0, 256, (60,), generator=g).tolist(), 40)    # grows past the arena
+    eng.run_until_done(max_steps=200)
+    assert eng.results[big].error is PublicErrorCode.CONTEXT_OVERFLOW
+    assert 0 < len(eng.results[big].tokens) < 40
+    assert eng.scheduler.allocator.allocated_page_count() == 0

@@ -125,3 +125,58 @@ def test_overlap_cancel_in_flight(tiny):
         assert eng.results[rids[i]].tokens == ref.generate_greedy(ps[i], 20)
     assert eng.scheduler.allocator.allocated_page_count() == 0
     eng.scheduler.debug_check_invariants()
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_overlap_randomized_workload_equals_sync(tiny, seed):
+    """Random arrivals, prompt and output lengths, stop tokens, cancellations
+    and page pressure (preemption): the overlapped engine finishes every
+    request with the synchronous engine's tokens and reasons."""
+    import random
+    spec, ck = tiny
+    rnd = random.Random(seed)
+    events = []          # (step, kind, payload)
+    for i in range(14):
+        n = rnd.randint(1, 40)
+        prompt = [rnd.randrange(256) for _ in range(n)]
+        events.append((rnd.randint(0, 20), "add", (i, prompt, rnd.randint(8, 48), [rnd.randrange(256)])))
+    for i in rnd.sample(range(14), 3):
+        events.append((rnd.randint(2, 30), "cancel", i))
+
+    def run(overlap):
+        eng = engine(spec, ck, overlap=overlap, rows=4, budget=32, pages=9, prefix=False)
+        rid_of = {}
+        step = 0
+        while step < 400:
+            for (at, kind, payload) in events:
+                if at != step:
+                    continue
+                if kind == "add":
+                    i, prompt, max_new, stops = payload
+                    rid_of[i] = eng.add_request(prompt, max_new, stop_ids=stops)
+                elif payload in rid_of:
+                    eng.cancel(rid_of[payload])
+            eng.step()
+            step += 1
+            if step > 31 and not eng.has_work():
+                break
+        assert not eng.has_work()
+        eng.scheduler.debug_check_invariants()
+        assert eng.scheduler.allocator.allocated_page_count() == 0
+        stats["preemptions"] += eng.scheduler.preemptions
+        return {i: (eng.results[r].tokens, eng.results[r].reason, eng.results[r].error) for i, r in rid_of.items()}
+
+    stats = {"preemptions": 0}
+
+    a, b = run(False), run(True)
+    assert stats["preemptions"] > 0          # the page budget forces preemption
+    # a cancellation lands on a different step boundary relative to the
+    # in-flight token, so cancelled requests may differ in length; every
+    # other request must be identical
+    for i in a:
+        if a[i][1] is FinishReason.CANCELLED or b[i][1] is FinishReason.CANCELLED:
+            assert a[i][1] is b[i][1]
+            n = min(len(a[i][0]), len(b[i][0]))
+            assert a[i][0][:n] == b[i][0][:n]
+        else:
+            assert a[i] == b[i], i
