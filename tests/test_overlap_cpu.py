@@ -180,3 +180,38 @@ def test_overlap_randomized_workload_equals_sync(tiny, seed):
             assert a[i][0][:n] == b[i][0][:n]
         else:
             assert a[i] == b[i], i
+
+
+@pytest.mark.parametrize("seed,overlap", [(3, False), (3, True), (4, True)])
+def test_randomized_prefix_sharing_matches_oracle(tiny, seed, overlap):
+    """Shared prompt prefixes (radix cache hits, publication on finish),
+    staggered arrivals, stop tokens and page pressure: every request's greedy
+    tokens equal the unpaged oracle's, truncated at its stop token."""
+    import random
+    spec, ck = tiny
+    ref = ReferenceModel(spec, ck)
+    rnd = random.Random(seed)
+    prefixes = [[rnd.randrange(256) for _ in range(rnd.choice((16, 32)))] for _ in range(2)]
+    reqs = []
+    for i in range(10):
+        p = rnd.choice(prefixes) + [rnd.randrange(256) for _ in range(rnd.randint(1, 12))]
+        reqs.append((rnd.randint(0, 12), p, rnd.randint(2, 10), rnd.randrange(256)))
+    eng = engine(spec, ck, overlap=overlap, rows=3, budget=24, pages=14, prefix=True)
+    rid_of = {}
+    step = 0
+    while step < 500 and (step <= 12 or eng.has_work()):
+        for i, (at, p, n, stop) in enumerate(reqs):
+            if at == step:
+                rid_of[i] = eng.add_request(p, n, stop_ids=[stop])
+        eng.step()
+        step += 1
+    assert not eng.has_work()
+    for i, (at, p, n, stop) in enumerate(reqs):
+        want = ref.generate_greedy(p, n)
+        if stop in want:
+            want = want[:want.index(stop) + 1]
+        assert eng.results[rid_of[i]].tokens == want, i
+    s = eng.scheduler
+    assert s.prefix_hit_tokens > 0
+    s.debug_check_invariants()
+    assert s.allocator.allocated_page_count() == s.prefix.page_count()
