@@ -237,6 +237,8 @@ def serve(args: List[str]):
     ap.add_argument("--tokenizer", default="")
     ap.add_argument("--max-context", type=int, default=4096)
     ap.add_argument("--metrics-port", type=int, default=-1, help="HTTP /metrics and /health (-1: off, 0: any)")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="synchronous steps (default: the next step is planned and launched while one runs)")
     ap.add_argument("--model-dir", default="",
                     help="Hugging Face style directory: config.json, safetensors weights (index or single), tokenizer.json")
     a = ap.parse_args(args)
@@ -276,7 +278,8 @@ def serve(args: List[str]):
             tok_from_dir = ckpt.tokenizer()
         ckpt.close()
     eng = LLMEngine(w, KernelOps() if cuda else TorchOps(), dev, sched, cache,
-                    EngineOptions(max_context=a.max_context, graph_sizes=EngineOptions().graph_sizes if cuda else ()))
+                    EngineOptions(max_context=a.max_context, graph_sizes=EngineOptions().graph_sizes if cuda else (),
+                                  overlap_steps=not a.no_overlap))
     tok = Tokenizer.from_file(a.tokenizer) if a.tokenizer else (tok_from_dir or synthetic_byte_tokenizer())
     svc = EngineService(eng, tok, default_limits(spec.vocab, a.max_context))
     svc.start()
