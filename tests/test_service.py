@@ -193,3 +193,80 @@ def test_tcp_end_to_end():
     assert isinstance(a[-1], CompletedEvent) and a[-1].reason is FinishReason.TOKEN_LIMIT
     assert isinstance(b[-1], CompletedEvent) and sum(isinstance(e, TokenEvent) for e in b) == 4
     assert isinstance(c[-1], FailedEvent) and c[-1].code is PublicErrorCode.INVALID_REQUEST
+
+
+def test_tcp_many_clients_overlapped_with_disconnects():
+    """Twelve concurrent TCP clients on an engine with overlapped steps; three
+    disconnect after their first token.  Every other client receives the
+    oracle's tokens, a usage record and one terminal event; the engine drains
+    and every KV page returns."""
+    import random
+    from lunaflux_b200.config import CacheConfig, SchedulerConfig
+    from lunaflux_b200.engine.engine import EngineOptions, LLMEngine
+    from lunaflux_b200.models.spec import tiny_llama
+    from lunaflux_b200.models.weights import build_runtime, random_checkpoint
+    from lunaflux_b200.ops.torch_ops import TorchOps
+    from lunaflux_b200.oracle.reference import ReferenceModel
+    from lunaflux_b200.service.framed_wire import EVENT_HEADER
+    from lunaflux_b200.service.server import EngineService, TCPServer
+    from lunaflux_b200.tokenizer.bpe import synthetic_byte_tokenizer
+
+    spec = tiny_llama()
+    ck = random_checkpoint(spec, 0)
+    ref = ReferenceModel(spec, ck)
+    eng = LLMEngine(build_runtime(spec, lambda n: ck[n]), TorchOps(), "cpu",
+                    SchedulerConfig(step_token_budget=48, max_active_requests=4, prefill_chunk_tokens=48,
+                                    emergency_decode_page_reserve=1),
+                    CacheConfig(prefix_enabled=False),
+                    EngineOptions(max_context=256, num_pages=24, graph_sizes=(), overlap_steps=True))
+    svc = EngineService(eng, synthetic_byte_tokenizer(), LIM)
+    svc.start()
+    rnd = random.Random(7)
+    jobs = [(100 + i, tuple(rnd.randrange(256) for _ in range(rnd.randint(2, 30))), rnd.randint(3, 9), i in (2, 5, 9))
+            for i in range(12)]
+
+    async def client(port, rid, prompt, n, drop):
+        r, w = await asyncio.open_connection("127.0.0.1", port)
+        w.write(encode_request(GenerateRequest(rid, input_tokens=prompt, max_new_tokens=n)))
+        await w.drain()
+        fr = FrameReader(EVENT_MAGIC, header=EVENT_HEADER)
+        events = []
+        while True:
+            data = await r.read(65536)
+            if not data:
+                break
+            for f in fr.feed(data):
+                events.append(decode_event(f, rid))
+            if drop and any(isinstance(e, TokenEvent) for e in events):
+                break
+            if events and isinstance(events[-1], (CompletedEvent, FailedEvent)):
+                break
+        w.close()
+        return events
+
+    async def main():
+        server = TCPServer(svc)
+        port = await server.start()
+        outs = await asyncio.gather(*(client(port, *j) for j in jobs))
+        for _ in range(200):                       # the dropped requests are cancelled and drained
+            if not eng.has_work() and not eng.live:
+                break
+            await asyncio.sleep(0.05)
+        server.close()
+        return outs
+
+    try:
+        outs = asyncio.run(main())
+    finally:
+        svc.stop()
+    for (rid, prompt, n, drop), ev in zip(jobs, outs):
+        toks = [e.token_id for e in ev if isinstance(e, TokenEvent)]
+        if drop:
+            assert toks and toks == ref.generate_greedy(list(prompt), n)[:len(toks)]
+            continue
+        assert toks == ref.generate_greedy(list(prompt), n), rid
+        assert isinstance(ev[-2], Usage) and ev[-2].output_tokens == n
+        assert isinstance(ev[-1], CompletedEvent)
+        assert sum(isinstance(e, (CompletedEvent, FailedEvent)) for e in ev) == 1
+    assert not eng.has_work()
+    assert eng.scheduler.allocator.allocated_page_count() == 0
