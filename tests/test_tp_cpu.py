@@ -51,7 +51,7 @@ def _worker(rank, world, port, q, sp=False, overlap=False):
 
 
 @pytest.mark.parametrize("world,sp,overlap", [(2, False, False), (4, False, False), (2, True, False),
-                                               (4, True, False), (2, False, True)])
+                                               (4, True, False), (2, False, True), (4, True, True)])
 def test_tp_matches_oracle(world, sp, overlap):
     """TP alone, TP with sequence parallelism (the residual stream sharded
     by tokens between a reduce-scatter and an all-gather, odd token counts
