@@ -38,6 +38,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--no-realtime", action="store_true", help="ignore arrival times (all at t = 0)")
     ap.add_argument("--step-token-budget", type=int, default=8192)
+    ap.add_argument("--no-overlap", action="store_true", help="synchronous steps")
     ap.add_argument("--json-out", default="")
     a = ap.parse_args()
     rank, world, local = env_rank_world()
@@ -73,7 +74,7 @@ def main():
     if wl.prefix_cache:
         pages += 8 * 2048 // 16
     eng = LLMEngine(weights, KernelOps(), dev, sched, CacheConfig(prefix_enabled=wl.prefix_cache),
-                    EngineOptions(max_context=max_ctx, num_pages=pages), comm=comm)
+                    EngineOptions(max_context=max_ctx, num_pages=pages, overlap_steps=not a.no_overlap), comm=comm)
     if spec.is_moe and wl.router_zipf:
         eng.runner.router_bias = W.zipf_router_bias(spec.experts, wl.router_zipf, dev)
     for _ in range(a.warmup):
