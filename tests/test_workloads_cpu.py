@@ -1,5 +1,6 @@
 """Benchmark workload generators and the workload driver (CPU, tiny model)."""
 import numpy as np
+import pytest
 
 from lunaflux_b200.bench import workloads as W
 from lunaflux_b200.config import CacheConfig, SchedulerConfig
@@ -28,13 +29,14 @@ def test_generators_match_the_named_configs():
     assert b[0] > b[7]
 
 
-def test_driver_with_arrivals_cancels_and_prefix_hits():
+@pytest.mark.parametrize("overlap", [False, True])
+def test_driver_with_arrivals_cancels_and_prefix_hits(overlap):
     spec = tiny_llama()
     ck = random_checkpoint(spec, 0)
     eng = LLMEngine(build_runtime(spec, lambda n: ck[n]), TorchOps(), "cpu",
                     SchedulerConfig(step_token_budget=64, max_active_requests=4, prefill_chunk_tokens=64,
                                     emergency_decode_page_reserve=1),
-                    CacheConfig(), EngineOptions(max_context=256, num_pages=96, graph_sizes=()))
+                    CacheConfig(), EngineOptions(max_context=256, num_pages=96, graph_sizes=(), overlap_steps=overlap))
     rng = np.random.default_rng(0)
     shared = rng.integers(0, 256, 48, dtype=np.int32)
     items = [W.WorkItem(np.concatenate([shared, rng.integers(0, 256, 5, dtype=np.int32)]), 6, SamplingParameters(),
