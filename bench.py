@@ -56,7 +56,8 @@ def parse():
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="row-parallel all-reduce: fused into the GEMM kernel, or NCCL after it")
     ap.add_argument("--sp", action="store_true",
-                    help="sequence parallelism (residual stream sharded by tokens; library reduce-scatter / all-gather)")
+                    help="sequence parallelism (residual stream sharded by tokens; reduce-scatter inside the "
+                         "GEMM with the fused comm where the shape allows, library all-gather)")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="synchronous steps (default: overlapped, step n+1 planned and launched before step n's "
                          "tokens reach the host)")
