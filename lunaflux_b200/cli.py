@@ -237,6 +237,8 @@ def serve(args: List[str]):
     ap.add_argument("--tokenizer", default="")
     ap.add_argument("--max-context", type=int, default=4096)
     ap.add_argument("--metrics-port", type=int, default=-1, help="HTTP /metrics and /health (-1: off, 0: any)")
+    ap.add_argument("--http-port", type=int, default=-1,
+                    help="also serve OpenAI-style /v1/completions on this port (0: any free port)")
     ap.add_argument("--no-overlap", action="store_true",
                     help="synchronous steps (default: the next step is planned and launched while one runs)")
     ap.add_argument("--model-dir", default="",
@@ -291,6 +293,10 @@ def serve(args: List[str]):
         if a.metrics_port >= 0:
             ms = MetricsServer(svc, a.host, a.metrics_port)
             print(f"lunaflux metrics on http://{a.host}:{await ms.start()}/metrics", flush=True)
+        if a.http_port >= 0:
+            from .service.http_api import CompletionsServer
+            hs = CompletionsServer(svc, a.host, a.http_port, model=preset)
+            print(f"lunaflux completions on http://{a.host}:{await hs.start()}/v1/completions", flush=True)
         await srv.serve_forever()
 
     try:

@@ -1,0 +1,138 @@
+"""OpenAI-style /v1/completions over HTTP on the CPU engine: JSON and SSE
+responses carry the oracle's greedy continuation, stop strings end a
+completion, bad bodies get 400s, and a disconnect cancels the request."""
+import asyncio
+import json
+
+import pytest
+
+from lunaflux_b200.contracts.inference import default_limits
+
+
+@pytest.fixture(scope="module")
+def stack():
+    from lunaflux_b200.config import CacheConfig, SchedulerConfig
+    from lunaflux_b200.engine.engine import EngineOptions, LLMEngine
+    from lunaflux_b200.models.spec import tiny_llama
+    from lunaflux_b200.models.weights import build_runtime, random_checkpoint
+    from lunaflux_b200.ops.torch_ops import TorchOps
+    from lunaflux_b200.oracle.reference import ReferenceModel
+    from lunaflux_b200.service.server import EngineService
+    from lunaflux_b200.tokenizer.bpe import synthetic_byte_tokenizer
+    spec = tiny_llama()
+    ck = random_checkpoint(spec, 0)
+    eng = LLMEngine(build_runtime(spec, lambda n: ck[n]), TorchOps(), "cpu",
+                    SchedulerConfig(step_token_budget=64, max_active_requests=4, prefill_chunk_tokens=64,
+                                    emergency_decode_page_reserve=1),
+                    CacheConfig(), EngineOptions(max_context=256, num_pages=64, graph_sizes=(), overlap_steps=True))
+    svc = EngineService(eng, synthetic_byte_tokenizer(), default_limits(256, 512))
+    svc.start()
+    yield svc, ReferenceModel(spec, ck), eng
+    svc.stop()
+
+
+async def _http(port, method, path, body=None):
+    r, w = await asyncio.open_connection("127.0.0.1", port)
+    data = b"" if body is None else json.dumps(body).encode()
+    w.write(f"{method} {path} HTTP/1.1\r\nHost: x\r\nContent-Length: {len(data)}\r\n\r\n".encode() + data)
+    await w.drain()
+    raw = await r.read()
+    w.close()
+    head, _, payload = raw.partition(b"\r\n\r\n")
+    return int(head.split()[1]), payload
+
+
+def _run(svc, coro_fn):
+    from lunaflux_b200.service.http_api import CompletionsServer
+
+    async def main():
+        srv = CompletionsServer(svc, model="tiny")
+        port = await srv.start()
+        try:
+            return await coro_fn(port)
+        finally:
+            srv.close()
+    return asyncio.run(main())
+
+
+def test_completion_json_and_stream(stack):
+    svc, ref, eng = stack
+    prompt = [72, 101, 108, 108, 111]
+    want = bytes(ref.generate_greedy(prompt, 8)).decode("utf-8", errors="replace")
+
+    async def go(port):
+        a = await _http(port, "POST", "/v1/completions", {"prompt": prompt, "max_tokens": 8})
+        b = await _http(port, "POST", "/v1/completions", {"prompt": prompt, "max_tokens": 8, "stream": True})
+        m = await _http(port, "GET", "/v1/models")
+        return a, b, m
+
+    (sa, pa), (sb, pb), (sm, pm) = _run(svc, go)
+    assert sa == 200 and sb == 200 and sm == 200
+    body = json.loads(pa)
+    assert body["object"] == "text_completion" and body["choices"][0]["text"] == want
+    assert body["choices"][0]["finish_reason"] == "length"
+    assert body["usage"] == {"prompt_tokens": 5, "completion_tokens": 8, "total_tokens": 13}
+    events = [ln[len(b"data: "):] for ln in pb.split(b"\n\n") if ln.startswith(b"data: ")]
+    assert events[-1] == b"[DONE]"
+    chunks = [json.loads(e) for e in events[:-1]]
+    assert "".join(c["choices"][0]["text"] for c in chunks) == want
+    assert chunks[-1]["choices"][0]["finish_reason"] == "length" and chunks[-1]["usage"]["completion_tokens"] == 8
+    assert json.loads(pm)["data"][0]["id"] == "tiny"
+
+
+def test_completion_text_prompt_stop_string_and_sampling(stack):
+    svc, ref, eng = stack
+    prompt = [72, 105, 33]
+    full = bytes(ref.generate_greedy(prompt, 12))
+    stop = full[4:6].decode("latin-1")
+
+    async def go(port):
+        a = await _http(port, "POST", "/v1/completions", {"prompt": prompt, "max_tokens": 12, "stop": stop})
+        b = await _http(port, "POST", "/v1/completions", {"prompt": "Hi!", "max_tokens": 5, "temperature": 0.8,
+                                                          "top_k": 20, "top_p": 0.9, "seed": 3})
+        return a, b
+
+    (sa, pa), (sb, pb) = _run(svc, go)
+    if all(c < 128 for c in full[:6]):      # a stop string that is valid UTF-8
+        body = json.loads(pa)
+        assert body["choices"][0]["finish_reason"] == "stop"
+        assert body["choices"][0]["text"].endswith(stop)
+    assert sb == 200 and json.loads(pb)["usage"]["completion_tokens"] == 5
+
+
+def test_completion_errors(stack):
+    svc, ref, eng = stack
+
+    async def go(port):
+        out = []
+        for body in ({"prompt": [], "max_tokens": 4}, {"prompt": [1, 2], "max_tokens": 0},
+                     {"prompt": [1, 2], "temperature": -1}, {"prompt": [999], "max_tokens": 2}, [1, 2]):
+            out.append(await _http(port, "POST", "/v1/completions", body))
+        out.append(await _http(port, "GET", "/v1/completions"))
+        out.append(await _http(port, "GET", "/nope"))
+        return out
+
+    res = _run(svc, go)
+    assert [s for s, _ in res] == [400, 400, 400, 400, 400, 405, 404]
+    assert all("error" in json.loads(p) for _, p in res)
+
+
+def test_disconnect_cancels(stack):
+    svc, ref, eng = stack
+
+    async def go(port):
+        r, w = await asyncio.open_connection("127.0.0.1", port)
+        data = json.dumps({"prompt": [1, 2, 3], "max_tokens": 200, "stream": True}).encode()
+        w.write(f"POST /v1/completions HTTP/1.1\r\nContent-Length: {len(data)}\r\n\r\n".encode() + data)
+        await w.drain()
+        await r.read(200)            # the stream has started
+        w.close()
+        for _ in range(200):
+            await asyncio.sleep(0.02)
+            if not eng.has_work():
+                return True
+        return False
+
+    assert _run(svc, go)
+    assert not eng.live
+    assert 'reason="cancelled"' in eng.metrics.registry.render_prometheus()
