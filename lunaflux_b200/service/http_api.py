@@ -185,6 +185,7 @@ class CompletionsServer:
         usage = None
         # a client that goes away cancels its request
         gone = asyncio.ensure_future(reader.read(1))
+        finished = False
         try:
             if stream:
                 writer.write(self._head(200, "text/event-stream"))
@@ -193,7 +194,6 @@ class CompletionsServer:
                 done, _ = await asyncio.wait({get, gone}, return_when=asyncio.FIRST_COMPLETED)
                 if get not in done:
                     get.cancel()
-                    self.service.cancel(rid)
                     return
                 ev = get.result()
                 if isinstance(ev, TokenEvent):
@@ -209,6 +209,7 @@ class CompletionsServer:
                     u = usage or ev.usage
                     usage_obj = {"prompt_tokens": u.input_tokens, "completion_tokens": u.output_tokens,
                                  "total_tokens": u.input_tokens + u.output_tokens}
+                    finished = True
                     if stream:
                         self._sse(writer, cid, created, ev.final_delta.decode("utf-8", errors="replace"), reason,
                                   usage_obj)
@@ -221,6 +222,7 @@ class CompletionsServer:
                             "usage": usage_obj})
                     return
                 elif isinstance(ev, FailedEvent):
+                    finished = True
                     err = {"error": {"message": ev.code.value, "type": "engine_error", "retryable": ev.retryable}}
                     if stream:
                         writer.write(b"data: " + json.dumps(err).encode() + b"\n\n")
@@ -229,6 +231,9 @@ class CompletionsServer:
                     return
         finally:
             gone.cancel()
+            if not finished:
+                # the client went away, or writing to it failed
+                self.service.cancel(rid)
 
     def _sse(self, writer, cid, created, text, reason, usage=None):
         chunk = {"id": cid, "object": "text_completion", "created": created, "model": self.model,
