@@ -270,3 +270,30 @@ def test_tcp_many_clients_overlapped_with_disconnects():
         assert sum(isinstance(e, (CompletedEvent, FailedEvent)) for e in ev) == 1
     assert not eng.has_work()
     assert eng.scheduler.allocator.allocated_page_count() == 0
+
+
+def test_request_decoder_fuzz():
+    """Random mutations of a valid frame and random bytes: the decoder either
+    returns a request that passes validation or raises FramedWireError;
+    nothing else escapes."""
+    import random
+    base = encode_request(full_request())
+    rnd = random.Random(5)
+    outcomes = {"ok": 0, "rejected": 0}
+    for i in range(3000):
+        if i % 3 == 0:
+            data = bytes(rnd.randrange(256) for _ in range(rnd.randint(0, 200)))
+        else:
+            b = bytearray(base)
+            for _ in range(rnd.randint(1, 6)):
+                b[rnd.randrange(len(b))] = rnd.randrange(256)
+            if rnd.random() < 0.2:
+                b = b[: rnd.randrange(len(b))]
+            data = bytes(b)
+        try:
+            req = decode_request(data, LIM)
+            req.validate(LIM)
+            outcomes["ok"] += 1
+        except FramedWireError:
+            outcomes["rejected"] += 1
+    assert outcomes["rejected"] > 2000 and outcomes["ok"] >= 0

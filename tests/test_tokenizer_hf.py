@@ -76,3 +76,18 @@ def test_encode_matches_tokenizers(layout, ignore_merges):
             assert ours.decode(got) == ref.decode(want, skip_special_tokens=False)
     if layout == "llama3":
         assert ours.bos_id == ref.token_to_id(SPECIALS[0])
+
+
+def test_random_text_matches_tokenizers():
+    """Random Unicode text (letters, digits, marks, whitespace runs, emoji,
+    apostrophes) through both implementations, Llama 3 layout."""
+    js = trained("llama3", True)
+    ref = tk.Tokenizer.from_str(js)
+    ours = Tokenizer.from_json(js)
+    rnd = random.Random(11)
+    alphabet = (list("abcxyzABCXYZ0123456789 \t\n\r'’.,;:!?-_()[]{}<>/\\\"") +
+                ["é", "ß", "ñ", "東", "京", "д", "ы", "🙂", "👍🏽", "́", "​", "  ", "\n\n", "'s", "'LL"])
+    for _ in range(300):
+        text = "".join(rnd.choice(alphabet) for _ in range(rnd.randint(0, 60)))
+        assert ours.encode(text) == ref.encode(text, add_special_tokens=False).ids, repr(text)
+        assert ours.decode(ours.encode(text)) == text
