@@ -41,6 +41,7 @@ class EngineOptions:
     sequence_parallel: bool = False        # TP only: residual stream sharded by tokens (reduce-scatter / all-gather)
     overlap_steps: bool = False            # plan and launch step n+1 before step n's tokens reach the host
     tp_sample_candidates: bool = False     # TP stochastic sampling from per-shard top-k candidates (top_k <= 64)
+    moe_all_to_all: bool = False           # with sequence parallelism: experts by dispatch / combine all-to-all
 
 
 @dataclasses.dataclass
@@ -83,7 +84,7 @@ class LLMEngine:
                                   sched.max_rows_per_step, opts.max_context, P, opts.graph_sizes, comm=comm,
                                   check_errors_every=opts.check_errors_every,
                                   sequence_parallel=opts.sequence_parallel, overlap=opts.overlap_steps,
-                                  sample_candidates=opts.tp_sample_candidates)
+                                  sample_candidates=opts.tp_sample_candidates, moe_all_to_all=opts.moe_all_to_all)
         if opts.overlap_steps:
             self.scheduler.max_inflight = 2
         self._launched: List[tuple] = []       # (plan, runner handle, t0), oldest first

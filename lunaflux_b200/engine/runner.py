@@ -60,7 +60,7 @@ class ModelRunner:
     def __init__(self, weights: ModelWeights, ops, device, num_pages: int, max_tokens: int, max_rows: int,
                  max_context: int, page: int = 16, graph_sizes: Sequence[int] = (), comm=None,
                  check_errors_every: int = 16, sequence_parallel: bool = False, overlap: bool = False,
-                 sample_candidates: bool = False):
+                 sample_candidates: bool = False, moe_all_to_all: bool = False):
         self.w = weights
         self.spec: LlamaSpec = weights.spec
         self.shard = weights.shard
@@ -93,9 +93,18 @@ class ModelRunner:
         # row-parallel partial sums are reduce-scattered instead of all-reduced
         # and the normed rows all-gathered before the next projection.
         self.sp = bool(sequence_parallel) and comm is not None and sh.size > 1
+        # expert parallelism over the token-sharded rows (dispatch / combine
+        # all-to-all) instead of experts on the gathered rows
+        self.moe_a2a = None
+        if self.sp and s.is_moe and moe_all_to_all:
+            from ..parallel.moe_a2a import LibraryExpertAllToAll
+            if weights.ep_size != sh.size:
+                raise ValueError("the expert all-to-all needs experts sharded over every rank (ep_size == tp)")
+            self.moe_a2a = LibraryExpertAllToAll(s.experts, s.experts_per_token, sh.size, sh.rank,
+                                                 getattr(comm, "group", None))
+            if dev.type == "cuda":
+                graph_sizes = ()     # the library exchange sizes itself on the host: not capturable
         if self.sp:
-            if getattr(comm, "fused", False):
-                raise ValueError("sequence parallelism uses the library reduce-scatter / all-gather")
             tp = sh.size
             Tl = -(-T // tp)
             self.sp_full = torch.zeros(Tl * tp, H, dtype=dt, device=dev)    # gathered rows / partial sums
@@ -326,12 +335,16 @@ class ModelRunner:
             attn = self._attention(l, lw, v, hf, T, Tp, Rp, Rd, max_q_len, splits, hm)
             scatter_gemm(attn, lw, "wo")
             ops.rmsnorm(delta, resid, lw.ln2, h, eps)
-            hf = gather_rows(h)
-            if s.is_moe:
+            if s.is_moe and self.moe_a2a is not None:
+                # tokens stay sharded: dispatch to the experts' ranks and back
+                delta.copy_(self.moe_a2a.forward(h, lw, ops, self.router_bias))
+            elif s.is_moe:
+                hf = gather_rows(h)
                 d_part = self.delta[:T]
                 self.moe(hf, d_part, lw, reduce=False)
                 scatter_partial(d_part)
             else:
+                hf = gather_rows(h)
                 self._proj(hf, lw, "wgu", act, 2)
                 scatter_gemm(act, lw, "wd")
         ops.rmsnorm(delta, resid, w.norm, h, eps)
