@@ -12,6 +12,7 @@
 #include "kernels/gemm_bf16.h"
 #include "kernels/gemm_fp8.h"
 #include "kernels/moe.h"
+#include "kernels/moe_a2a.h"
 #include "kernels/runtime.h"
 
 namespace lf {
@@ -136,6 +137,85 @@ void gemm_reduce_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& o
   c10::cuda::CUDAGuard g(A.device());
   lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), ar.out_peer[rank], M, N, K, A.stride(0), B.stride(0), N};
   lf::gemm::run_reduce_scatter(a, ar, stream());
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel dispatch / combine (moe_a2a.cu).  Pointer lists: one entry
+// per rank, the symmetric buffer as mapped on that rank.
+static lf::a2a::Args make_a2a(const std::vector<int64_t>& recv_x, const std::vector<int64_t>& recv_meta,
+                              const std::vector<int64_t>& recv_flag, const std::vector<int64_t>& comb_y,
+                              const std::vector<int64_t>& comb_flag, const at::Tensor& state,
+                              const at::Tensor& counts, int64_t rank, int64_t experts_local, int64_t topk,
+                              int64_t cap, int64_t hidden) {
+  const size_t W = recv_x.size();
+  LF_CHECK(W >= 1 && W <= (size_t)lf::a2a::kMaxRanks && recv_meta.size() == W && recv_flag.size() == W &&
+               comb_y.size() == W && comb_flag.size() == W,
+           "moe all-to-all: peer lists");
+  LF_CHECK(state.is_cuda() && state.scalar_type() == at::kInt && state.numel() >= 4, "moe all-to-all: state");
+  LF_CHECK(counts.is_cuda() && counts.scalar_type() == at::kInt && counts.numel() >= (int64_t)(2 * W),
+           "moe all-to-all: counts");
+  lf::a2a::Args a{};
+  for (size_t i = 0; i < W; ++i) {
+    a.recv_x[i] = reinterpret_cast<__nv_bfloat16*>(recv_x[i]);
+    a.recv_meta[i] = reinterpret_cast<int2*>(recv_meta[i]);
+    a.recv_flag[i] = reinterpret_cast<unsigned long long*>(recv_flag[i]);
+    a.comb_y[i] = reinterpret_cast<__nv_bfloat16*>(comb_y[i]);
+    a.comb_flag[i] = reinterpret_cast<unsigned long long*>(comb_flag[i]);
+  }
+  a.state = state.data_ptr<int>();
+  a.counts = counts.data_ptr<int>();
+  a.rank = (int)rank;
+  a.world = (int)W;
+  a.experts_local = (int)experts_local;
+  a.topk = (int)topk;
+  a.cap = (int)cap;
+  a.hidden = (int)hidden;
+  return a;
+}
+
+#define LF_A2A_ARGS                                                                                          \
+  std::vector<int64_t> recv_x, std::vector<int64_t> recv_meta, std::vector<int64_t> recv_flag,             \
+      std::vector<int64_t> comb_y, std::vector<int64_t> comb_flag, const at::Tensor &state,                 \
+      const at::Tensor &counts, int64_t rank, int64_t experts_local, int64_t topk, int64_t cap, int64_t hidden
+#define LF_A2A_MAKE \
+  make_a2a(recv_x, recv_meta, recv_flag, comb_y, comb_flag, state, counts, rank, experts_local, topk, cap, hidden)
+
+void moe_a2a_dispatch(const at::Tensor& h, const at::Tensor& ids, at::Tensor& slot, LF_A2A_ARGS) {
+  LF_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && h.size(1) == hidden, "dispatch: h [T, H] bf16");
+  LF_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && ids.numel() == h.size(0) * topk, "dispatch: ids");
+  LF_CHECK(slot.scalar_type() == at::kInt && slot.numel() >= ids.numel(), "dispatch: slot scratch");
+  c10::cuda::CUDAGuard g(h.device());
+  lf::a2a::dispatch(reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), ids.data_ptr<int32_t>(), h.size(0),
+                    slot.data_ptr<int32_t>(), LF_A2A_MAKE, stream());
+}
+
+void moe_a2a_receive(at::Tensor& groups, at::Tensor& perm, at::Tensor& back, at::Tensor& x, LF_A2A_ARGS) {
+  LF_CHECK(groups.scalar_type() == at::kInt && groups.numel() >= experts_local + 1, "receive: groups");
+  LF_CHECK(perm.scalar_type() == at::kInt && back.scalar_type() == at::kLong && back.numel() >= perm.numel(),
+           "receive: perm / back");
+  LF_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.size(0) >= perm.numel() && x.size(1) == hidden,
+           "receive: x [rows_max, H]");
+  c10::cuda::CUDAGuard g(x.device());
+  const lf::a2a::Args a = LF_A2A_MAKE;
+  lf::a2a::receive_plan(groups.data_ptr<int32_t>(), perm.data_ptr<int32_t>(),
+                        reinterpret_cast<long long*>(back.data_ptr<int64_t>()), (int)perm.numel(), a, stream());
+  lf::a2a::gather(groups.data_ptr<int32_t>(), perm.data_ptr<int32_t>(),
+                  reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), (int)perm.numel(), a, stream());
+}
+
+void moe_a2a_combine(const at::Tensor& y, const at::Tensor& groups, const at::Tensor& perm, const at::Tensor& back,
+                     const at::Tensor& w, at::Tensor& out, LF_A2A_ARGS) {
+  LF_CHECK(y.scalar_type() == at::kBFloat16 && y.is_contiguous() && y.size(1) == hidden, "combine: y");
+  LF_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && out.scalar_type() == at::kBFloat16 &&
+               out.is_contiguous() && w.numel() == out.size(0) * topk,
+           "combine: w [T, k] fp32, out [T, H] bf16");
+  c10::cuda::CUDAGuard g(y.device());
+  const lf::a2a::Args a = LF_A2A_MAKE;
+  lf::a2a::combine_send(reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), groups.data_ptr<int32_t>(),
+                        perm.data_ptr<int32_t>(), reinterpret_cast<const long long*>(back.data_ptr<int64_t>()), a,
+                        stream());
+  lf::a2a::combine_receive(w.data_ptr<float>(), out.size(0), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), a,
+                           stream());
 }
 
 static lf::ar::LLArgs make_ll(const std::vector<int64_t>& rs, const std::vector<int64_t>& ag, int64_t ag_mc,
@@ -538,6 +618,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("partials_allreduce", &partials_allreduce);
   m.def("gemm_allreduce_ll", &gemm_allreduce_ll);
   m.def("gemm_reduce_scatter", &gemm_reduce_scatter);
+  m.def("moe_a2a_dispatch", &moe_a2a_dispatch);
+  m.def("moe_a2a_receive", &moe_a2a_receive);
+  m.def("moe_a2a_combine", &moe_a2a_combine);
   m.def("partials_allreduce_ll", &partials_allreduce_ll);
   m.def("act_quant", &act_quant);
   m.def("moe_route", &moe_route);

@@ -13,6 +13,7 @@ the device and only the sampled int32 ids come back to the host.
 from __future__ import annotations
 
 import math
+import os
 import time
 from typing import Dict, List, Optional, Sequence
 
@@ -97,13 +98,18 @@ class ModelRunner:
         # all-to-all) instead of experts on the gathered rows
         self.moe_a2a = None
         if self.sp and s.is_moe and moe_all_to_all:
-            from ..parallel.moe_a2a import LibraryExpertAllToAll
+            from ..parallel.moe_a2a import ExpertAllToAll, LibraryExpertAllToAll
             if weights.ep_size != sh.size:
                 raise ValueError("the expert all-to-all needs experts sharded over every rank (ep_size == tp)")
-            self.moe_a2a = LibraryExpertAllToAll(s.experts, s.experts_per_token, sh.size, sh.rank,
-                                                 getattr(comm, "group", None))
-            if dev.type == "cuda":
-                graph_sizes = ()     # the library exchange sizes itself on the host: not capturable
+            if dev.type == "cuda" and os.environ.get("LUNAFLUX_MOE_A2A_LIBRARY") != "1":
+                ffn = weights.layers[0].experts_d.shape[-1]
+                self.moe_a2a = ExpertAllToAll(s.experts, s.experts_per_token, sh.size, sh.rank, s.hidden, ffn,
+                                              -(-T // sh.size), dev, getattr(comm, "group", None))
+            else:
+                self.moe_a2a = LibraryExpertAllToAll(s.experts, s.experts_per_token, sh.size, sh.rank,
+                                                     getattr(comm, "group", None))
+                if dev.type == "cuda":
+                    graph_sizes = ()     # the library exchange sizes itself on the host: not capturable
         if self.sp:
             tp = sh.size
             Tl = -(-T // tp)

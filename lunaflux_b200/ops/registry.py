@@ -60,6 +60,12 @@ OPS: Tuple[OpEntry, ...] = (
     OpEntry("moe_gather", "moe_gather", ("bf16",), "new: MoE gather", "csrc/kernels/moe.cu"),
     OpEntry("moe_grouped_linear", "gemm_grouped", ("bf16",), "new: MoE grouped GEMM", "csrc/kernels/gemm_bf16.cu"),
     OpEntry("moe_combine", "moe_combine", ("bf16",), "new: MoE weighted combine", "csrc/kernels/moe.cu"),
+    OpEntry("moe_a2a_dispatch", "moe_a2a_dispatch", ("bf16",),
+            "new: expert-parallel dispatch into the expert ranks' memory", "csrc/kernels/moe_a2a.cu"),
+    OpEntry("moe_a2a_receive", "moe_a2a_receive", ("bf16",),
+            "new: expert-ordered layout of the received rows", "csrc/kernels/moe_a2a.cu"),
+    OpEntry("moe_a2a_combine", "moe_a2a_combine", ("bf16",),
+            "new: expert outputs back to their tokens, top-k weighted sum", "csrc/kernels/moe_a2a.cu"),
     OpEntry("linear_allreduce", "gemm_allreduce", ("bf16",), "new: GEMM + all-reduce over NVLink (tile path)",
             "csrc/kernels/gemm_bf16.cu"),
     OpEntry("linear_allreduce_ll", "gemm_allreduce_ll", ("bf16",),

@@ -10,9 +10,12 @@ sum.  Per layer and rank this moves each local token to its k experts and
 back, about 4 H bytes x k x (W - 1) / W per token, instead of an all-gather
 before the experts and a reduce-scatter after them.
 
-``LibraryExpertAllToAll`` is this path on ``torch.distributed.all_to_all_single``
-(the pair counts cross to the host to size the exchange); it runs on gloo
-ranks on the CPU and serves as the baseline on NCCL.  The experts themselves
+``ExpertAllToAll`` runs the exchange with device kernels that store rows
+straight into the peers' symmetric buffers (no host round trip, capturable);
+``LibraryExpertAllToAll`` is the same path on
+``torch.distributed.all_to_all_single`` (the pair counts cross to the host to
+size the exchange), which runs on gloo ranks on the CPU and is the baseline
+on NCCL.  The experts themselves
 go through the same operator set as the tensor-parallel MoE (routing, the
 expert-ordered segment alignment padded to 128 rows, the grouped GEMMs).
 """
@@ -84,3 +87,71 @@ class LibraryExpertAllToAll:
         pairs[order] = y_back
         out = (pairs.view(T, k, H).float() * w.view(T, k, 1)).sum(1)
         return out.to(h.dtype)
+
+
+class ExpertAllToAll:
+    """The same exchange on the GPU with no host round trip: the dispatch and
+    combine kernels store rows straight into the peers' symmetric buffers
+    (csrc/kernels/moe_a2a.cu), so a layer is capturable in a CUDA graph.
+    Buffers are sized for ``max_tokens`` local rows per layer."""
+
+    def __init__(self, experts: int, topk: int, world: int, rank: int, hidden: int, ffn: int, max_tokens: int,
+                 device, group=None):
+        import torch.distributed._symmetric_memory as symm
+
+        from ..ops import _ext
+        if experts % world:
+            raise ValueError("experts must divide over the expert-parallel ranks")
+        self.C = _ext.load()
+        self.E, self.k, self.W, self.rank = experts, topk, world, rank
+        self.El = experts // world
+        self.H = hidden
+        self.cap = max_tokens * topk
+        g = group or dist.group.WORLD
+        name = g.group_name
+        self.recv_x = symm.empty(world * self.cap * hidden, dtype=torch.bfloat16, device=device)
+        self.recv_meta = symm.empty(world * self.cap * 2, dtype=torch.int32, device=device)
+        self.comb_y = symm.empty(self.cap * hidden, dtype=torch.bfloat16, device=device)
+        self.flags = symm.empty(2 * world, dtype=torch.int64, device=device)
+        for t in (self.recv_meta, self.flags):
+            t.zero_()
+        handles = [symm.rendezvous(t, name) for t in (self.recv_x, self.recv_meta, self.comb_y, self.flags)]
+        torch.cuda.synchronize(device)
+        dist.barrier(group=g)
+        hx, hm, hy, hf = handles
+        self._handles = handles
+        self.ptrs = (list(hx.buffer_ptrs), list(hm.buffer_ptrs), list(hf.buffer_ptrs), list(hy.buffer_ptrs),
+                     [p + world * 8 for p in hf.buffer_ptrs])
+        self.state = torch.zeros(4, dtype=torch.int32, device=device)
+        self.counts = torch.zeros(2 * world, dtype=torch.int32, device=device)
+        self.rows_max = -(-world * self.cap // 128) * 128 + self.El * 128
+        self.x = torch.zeros(self.rows_max, hidden, dtype=torch.bfloat16, device=device)
+        self.act = torch.zeros(self.rows_max, ffn, dtype=torch.bfloat16, device=device)
+        self.y = torch.zeros(self.rows_max, hidden, dtype=torch.bfloat16, device=device)
+        self.groups = torch.zeros(self.El + 1, dtype=torch.int32, device=device)
+        self.perm = torch.full((self.rows_max,), -1, dtype=torch.int32, device=device)
+        self.back = torch.zeros(self.rows_max, dtype=torch.int64, device=device)
+        self.slot = torch.zeros(self.cap, dtype=torch.int32, device=device)
+        self.ids = torch.zeros(max_tokens, topk, dtype=torch.int32, device=device)
+        self.w = torch.zeros(max_tokens, topk, dtype=torch.float32, device=device)
+        self.out = torch.zeros(max_tokens, hidden, dtype=torch.bfloat16, device=device)
+        self.calls = 0
+
+    def _args(self):
+        rx, rm, rf, cy, cf = self.ptrs
+        return (rx, rm, rf, cy, cf, self.state, self.counts, self.rank, self.El, self.k, self.cap, self.H)
+
+    def forward(self, h: torch.Tensor, lw, ops, router_bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+        T = h.shape[0]
+        ids, w, out = self.ids[:T], self.w[:T], self.out[:T]
+        ops.moe_route(h, lw.router, router_bias, self.k, ids, w)
+        a = self._args()
+        self.C.moe_a2a_dispatch(h, ids, self.slot, *a)
+        self.C.moe_a2a_receive(self.groups, self.perm, self.back, self.x, *a)
+        ops.gemm_grouped(self.x, lw.experts_gu, self.act, self.groups, self.El, 2)
+        ops.gemm_grouped(self.act, lw.experts_d, self.y, self.groups, self.El, 0)
+        self.C.moe_a2a_combine(self.y, self.groups, self.perm, self.back, w, out, *a)
+        if hasattr(ops, "launches"):
+            ops.launches += 6          # plan, dispatch, receive plan, gather, combine send, combine receive
+        self.calls += 1
+        return out

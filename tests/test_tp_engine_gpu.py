@@ -105,3 +105,79 @@ def test_tp_engine_tracks_oracle():
                 row = logits[len(p) - 1 + i]
                 gap = (row.max() - row[tok]).item()
                 assert gap <= 0.05 * row.std().item() + 1e-4, f"{name}: token {i} gap {gap:.4g}"
+
+
+def _moe_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    try:
+        from lunaflux_b200.config import CacheConfig, SchedulerConfig
+        from lunaflux_b200.engine.engine import EngineOptions, LLMEngine
+        from lunaflux_b200.models.weights import build_runtime
+        from lunaflux_b200.ops import KernelOps
+        from lunaflux_b200.parallel.comm import TPComm, init_distributed
+        from lunaflux_b200.parallel.tp import TPShard
+        init_distributed("nccl", timeout_s=120, device_id=rank)
+        spec = _moe_spec()
+        ck = _checkpoint(spec)
+        w = build_runtime(spec, lambda n: ck[n], TPShard(rank, world, spec), device=dev, dtype=torch.bfloat16,
+                          ep_rank=rank, ep_size=world)
+        sched = SchedulerConfig(step_token_budget=256, max_active_requests=8, prefill_chunk_tokens=256,
+                                emergency_decode_page_reserve=4)
+        outs = {}
+        for name, a2a in (("replicated", False), ("all_to_all", True)):
+            opts = EngineOptions(max_context=1024, num_pages=256, graph_sizes=(1, 2, 4), overlap_steps=True,
+                                 sequence_parallel=a2a, moe_all_to_all=a2a)
+            eng = LLMEngine(w, KernelOps(), dev, sched, CacheConfig(prefix_enabled=False), opts, comm=TPComm())
+            outs[name] = eng.generate(_prompts(spec), 8)
+            torch.cuda.synchronize(dev)
+            outs[name + "_err"] = eng.runner.ops.read_error(True)[0]
+        q.put((rank, outs))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+def _moe_spec():
+    from lunaflux_b200.models.spec import LlamaSpec
+    return LlamaSpec(hidden=1024, layers=2, heads=8, kv_heads=2, head_dim=128, ffn=1024, vocab=4096,
+                     rope_theta=500000.0, max_position=2048, dtype="bf16", experts=8, experts_per_token=2)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
+                    reason="expert all-to-all over NVLink: first multi-GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
+def test_moe_expert_all_to_all_tracks_oracle():
+    """Experts sharded over the GPUs: on replicated rows (all-reduce), and on
+    token-sharded rows with the device dispatch / combine; both track the
+    fp32 oracle within bf16 near-ties."""
+    import torch.multiprocessing as mp
+    from lunaflux_b200.oracle.reference import ReferenceModel
+    world = 2 if torch.cuda.device_count() < 4 else (4 if torch.cuda.device_count() < 8 else 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_moe_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r, outs in res.items():
+        assert not isinstance(outs, str), f"rank {r}: {outs}"
+    spec = _moe_spec()
+    ref = ReferenceModel(spec, _checkpoint(spec))
+    for name in ("replicated", "all_to_all"):
+        for r in range(world):
+            assert res[r][name + "_err"] == 0, (name, r)
+            assert res[r][name] == res[0][name], f"{name}: rank {r} differs from rank 0"
+        for p, o in zip(_prompts(spec), res[0][name]):
+            logits = ref.forward(p + o)
+            for i, tok in enumerate(o):
+                row = logits[len(p) - 1 + i]
+                gap = (row.max() - row[tok]).item()
+                assert gap <= 0.05 * row.std().item() + 1e-4, f"{name}: token {i} gap {gap:.4g}"
