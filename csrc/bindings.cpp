@@ -13,6 +13,7 @@
 #include "kernels/gemm_fp8.h"
 #include "kernels/moe.h"
 #include "kernels/moe_a2a.h"
+#include "kernels/sp_gather.h"
 #include "kernels/runtime.h"
 
 namespace lf {
@@ -216,6 +217,36 @@ void moe_a2a_combine(const at::Tensor& y, const at::Tensor& groups, const at::Te
                         stream());
   lf::a2a::combine_receive(w.data_ptr<float>(), out.size(0), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), a,
                            stream());
+}
+
+// Sequence-parallel RMSNorm with the all-gather in its epilogue (sp_gather.cu).
+static lf::sp::GatherArgs make_gather(const std::vector<int64_t>& dst, const std::vector<int64_t>& flag,
+                                      const at::Tensor& state, int64_t rank, int64_t rows_local) {
+  LF_CHECK(!dst.empty() && dst.size() <= (size_t)lf::sp::kMaxRanks && flag.size() == dst.size(),
+           "norm_gather: peer lists");
+  LF_CHECK(state.is_cuda() && state.scalar_type() == at::kInt && state.numel() >= 2, "norm_gather: state");
+  lf::sp::GatherArgs g{};
+  for (size_t i = 0; i < dst.size(); ++i) {
+    g.dst[i] = reinterpret_cast<__nv_bfloat16*>(dst[i]);
+    g.flag[i] = reinterpret_cast<unsigned long long*>(flag[i]);
+  }
+  g.state = state.data_ptr<int>();
+  g.rank = (int)rank;
+  g.world = (int)dst.size();
+  g.rows_local = (int)rows_local;
+  return g;
+}
+
+void norm_gather(const at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w, double eps,
+                 std::vector<int64_t> dst, std::vector<int64_t> flag, const at::Tensor& state, int64_t rank) {
+  LF_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && w.is_contiguous(), "norm_gather: bf16 rows");
+  if (residual.has_value())
+    LF_CHECK(residual->is_contiguous() && residual->sizes() == x.sizes(), "norm_gather: residual shape");
+  const lf::sp::GatherArgs g = make_gather(dst, flag, state, rank, x.size(0));
+  c10::cuda::CUDAGuard gd(x.device());
+  lf::sp::norm_gather(x.data_ptr(), residual.has_value() ? residual->data_ptr() : nullptr, w.data_ptr(), (float)eps,
+                      x.size(1), g, stream());
+  lf::sp::gather_wait(g, stream());
 }
 
 static lf::ar::LLArgs make_ll(const std::vector<int64_t>& rs, const std::vector<int64_t>& ag, int64_t ag_mc,
@@ -618,6 +649,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("partials_allreduce", &partials_allreduce);
   m.def("gemm_allreduce_ll", &gemm_allreduce_ll);
   m.def("gemm_reduce_scatter", &gemm_reduce_scatter);
+  m.def("norm_gather", &norm_gather);
   m.def("moe_a2a_dispatch", &moe_a2a_dispatch);
   m.def("moe_a2a_receive", &moe_a2a_receive);
   m.def("moe_a2a_combine", &moe_a2a_combine);

@@ -113,6 +113,8 @@ class ModelRunner:
         if self.sp:
             tp = sh.size
             Tl = -(-T // tp)
+            if getattr(comm, "fused", False) and hasattr(comm, "enable_norm_gather"):
+                comm.enable_norm_gather(Tl, dev)   # RMSNorm with the all-gather in its epilogue
             self.sp_full = torch.zeros(Tl * tp, H, dtype=dt, device=dev)    # gathered rows / partial sums
             self.sp_resid = torch.zeros(Tl, H, dtype=dt, device=dev)
             self.sp_h = torch.zeros(Tl, H, dtype=dt, device=dev)
@@ -312,6 +314,20 @@ class ModelRunner:
             comm.all_gather_rows(local, full)
             return full[:T]
 
+        fused_gather = getattr(comm, "ng_rows", 0) >= Tl
+        if getattr(comm, "fused", False):
+            comm.begin_forward()
+
+        def norm_gather(x, residual, weight, final=False):
+            """RMSNorm of the local rows (residual added in place), gathered:
+            in one kernel with the all-gather in its epilogue when the fused
+            comm is set up for it, else the norm and the library all-gather."""
+            if fused_gather:
+                ops.launches += 2
+                return comm.norm_gather(x, residual, weight, eps, final)[:T]
+            ops.rmsnorm(x, residual, weight, h, eps)
+            return gather_rows(h)
+
         def scatter_gemm(A, lw, name):
             """delta = this rank's rows of the row-parallel projection: one
             kernel with the reduce-scatter inside when the fused comm takes
@@ -334,27 +350,25 @@ class ModelRunner:
 
         for l, lw in enumerate(w.layers):
             if l == 0:
-                ops.rmsnorm(resid, None, lw.ln1, h, eps)
+                hf = norm_gather(resid, None, lw.ln1)
             else:
-                ops.rmsnorm(delta, resid, lw.ln1, h, eps)
-            hf = gather_rows(h)
+                hf = norm_gather(delta, resid, lw.ln1)
             attn = self._attention(l, lw, v, hf, T, Tp, Rp, Rd, max_q_len, splits, hm)
             scatter_gemm(attn, lw, "wo")
-            ops.rmsnorm(delta, resid, lw.ln2, h, eps)
             if s.is_moe and self.moe_a2a is not None:
                 # tokens stay sharded: dispatch to the experts' ranks and back
+                ops.rmsnorm(delta, resid, lw.ln2, h, eps)
                 delta.copy_(self.moe_a2a.forward(h, lw, ops, self.router_bias))
             elif s.is_moe:
-                hf = gather_rows(h)
+                hf = norm_gather(delta, resid, lw.ln2)
                 d_part = self.delta[:T]
                 self.moe(hf, d_part, lw, reduce=False)
                 scatter_partial(d_part)
             else:
-                hf = gather_rows(h)
+                hf = norm_gather(delta, resid, lw.ln2)
                 self._proj(hf, lw, "wgu", act, 2)
                 scatter_gemm(act, lw, "wd")
-        ops.rmsnorm(delta, resid, w.norm, h, eps)
-        hf = gather_rows(h)
+        hf = norm_gather(delta, resid, w.norm, final=True)
         return self._sample(hf, v, Rs, stochastic, gather)
 
     def _row_parallel_partial(self, A, lw, name, out, ws):

@@ -60,6 +60,10 @@ OPS: Tuple[OpEntry, ...] = (
     OpEntry("moe_gather", "moe_gather", ("bf16",), "new: MoE gather", "csrc/kernels/moe.cu"),
     OpEntry("moe_grouped_linear", "gemm_grouped", ("bf16",), "new: MoE grouped GEMM", "csrc/kernels/gemm_bf16.cu"),
     OpEntry("moe_combine", "moe_combine", ("bf16",), "new: MoE weighted combine", "csrc/kernels/moe.cu"),
+    OpEntry("norm_gather", "norm_gather", ("bf16",),
+            "cap 2 + all-gather: sequence-parallel RMSNorm storing its rows on every rank", "csrc/kernels/sp_gather.cu"),
+    OpEntry("linear_reduce_scatter", "gemm_reduce_scatter", ("bf16",),
+            "new: row-parallel GEMM with the reduce-scatter in the kernel", "csrc/kernels/gemm_bf16_kernel.cuh"),
     OpEntry("moe_a2a_dispatch", "moe_a2a_dispatch", ("bf16",),
             "new: expert-parallel dispatch into the expert ranks' memory", "csrc/kernels/moe_a2a.cu"),
     OpEntry("moe_a2a_receive", "moe_a2a_receive", ("bf16",),

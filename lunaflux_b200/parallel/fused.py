@@ -121,8 +121,10 @@ class FusedTPComm(TPComm):
 
     def begin_forward(self):
         """Every forward has an even number of fused operations, so starting
-        each forward on slot 0 keeps the strict slot alternation."""
+        each forward on slot 0 keeps the strict slot alternation (and the
+        layer norms' gathered buffers alternate the same way)."""
         self.op_index = 0
+        self.ng_index = 0
 
     def _slot(self):
         s = self.slots[self.op_index & 1]
@@ -156,6 +158,46 @@ class FusedTPComm(TPComm):
         s = self._slot()
         self.C.gemm_allreduce(A, B, ws, *self._args(s))
         return s["result"][: M * self.hidden].view(M, self.hidden)
+
+    def enable_norm_gather(self, rows_local: int, device):
+        """Symmetric buffers of the sequence-parallel RMSNorm with the
+        all-gather in its epilogue: three gathered [world * rows_local,
+        hidden] buffers (two alternating over the layers, one for the final
+        norm) and the per-rank arrival words."""
+        import torch.distributed._symmetric_memory as symm
+        if getattr(self, "ng_rows", 0) >= rows_local:
+            return
+        g = self.group or dist.group.WORLD
+        full = self.world * rows_local
+        self.ng_buf = symm.empty(3 * full * self.hidden, dtype=torch.bfloat16, device=device)
+        self.ng_flag = symm.empty(self.world, dtype=torch.int64, device=device)
+        self.ng_flag.zero_()
+        hb = symm.rendezvous(self.ng_buf, g.group_name)
+        hf = symm.rendezvous(self.ng_flag, g.group_name)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=g)
+        nbytes = full * self.hidden * 2
+        self.ng_dst = [[p + b * nbytes for p in hb.buffer_ptrs] for b in range(3)]
+        self.ng_flags = list(hf.buffer_ptrs)
+        self.ng_state = torch.zeros(2, dtype=torch.int32, device=device)
+        self.ng_rows = rows_local
+        self.ng_index = 0
+        self._ng_handles = (hb, hf)
+
+    def norm_gather(self, x: torch.Tensor, residual, w: torch.Tensor, eps: float, final: bool = False) -> torch.Tensor:
+        """RMSNorm of this rank's rows x [rows_local, H] (residual added in
+        place when given), gathered on every rank: returns the local
+        [world * rows_local, H] view, ready for the next projection."""
+        rows = x.shape[0]
+        if rows > self.ng_rows:
+            raise ValueError("norm_gather: more rows than the enabled size")
+        b = 2 if final else (self.ng_index & 1)
+        if not final:
+            self.ng_index += 1
+        self.calls += 1
+        self.C.norm_gather(x, residual, w, eps, self.ng_dst[b], self.ng_flags, self.ng_state, self.rank)
+        full = self.world * rows * self.hidden
+        return self.ng_buf[b * full:(b + 1) * full].view(self.world * rows, self.hidden)
 
     def gemm_reduce_scatter(self, A: torch.Tensor, B: torch.Tensor, out_local: torch.Tensor) -> bool:
         """out_local [M / world, hidden] = this rank's rows of the sum over
