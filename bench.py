@@ -180,7 +180,7 @@ def main():
     pages = args.requests * (-(-max_ctx // 16)) + 2 * args.requests + 64
     opts = EngineOptions(max_context=max_ctx, num_pages=pages,
                          graph_sizes=() if (args.no_graphs or args.impl != "ours") else EngineOptions().graph_sizes,
-                         sequence_parallel=args.sp, overlap_steps=args.overlap and args.impl == "ours")
+                         sequence_parallel=args.sp, overlap_steps=args.overlap)
     engine = LLMEngine(weights, ops, dev, sched, CacheConfig(prefix_enabled=False), opts, comm=comm)
     if args.impl == "ours":
         engine.runner.capture_all(False)
