@@ -19,6 +19,7 @@ import hashlib
 import os
 import sys
 import tempfile
+import time
 from typing import List, Optional
 
 from .contracts import PROTOCOL_VERSION
@@ -253,7 +254,15 @@ def serve(args: List[str]):
         preset = cfg.model.preset or preset
         a.host, a.port = cfg.service.listen_host, cfg.service.listen_port
     cuda = torch.cuda.is_available()
-    dev = torch.device("cuda", 0) if cuda else torch.device("cpu")
+    from .parallel.comm import env_rank_world, init_distributed
+    rank, world, local = env_rank_world()
+    dev = torch.device("cuda", local) if cuda else torch.device("cpu")
+    ctrl = None
+    if world > 1:
+        # tensor parallel: one process per GPU (under torchrun); rank 0 serves
+        if cuda:
+            torch.cuda.set_device(local)
+        ctrl = init_distributed("nccl" if cuda else "gloo", device_id=local if cuda else None)
     ckpt = None
     if a.model_dir:
         from .models.checkpoint import CheckpointDir
@@ -273,15 +282,34 @@ def serve(args: List[str]):
     if not adm.ok:
         raise CliError("model not admitted: " + "; ".join(adm.details))
     source = ckpt.source() if ckpt is not None else random_source(spec, 0, dev, torch.bfloat16 if cuda else torch.float32)
-    w = build_runtime(spec, source, device=dev)
+    from .parallel.tp import TPShard
+    shard = TPShard(rank, world, spec)
+    ep = world if (spec.is_moe and world > 1) else 1
+    w = build_runtime(spec, source, shard, device=dev, ep_rank=rank if ep > 1 else 0, ep_size=ep)
+    comm = None
+    if world > 1:
+        from .parallel.comm import TPComm
+        if cuda and not spec.is_moe:
+            from .parallel.fused import FusedTPComm
+            comm = FusedTPComm(sched.step_token_budget + sched.max_active_requests, spec.hidden, dev)
+        else:
+            comm = TPComm()
     tok_from_dir = None
     if ckpt is not None:
         if not a.tokenizer:
             tok_from_dir = ckpt.tokenizer()
         ckpt.close()
+    from .service.spmd import SharedClock, SpmdLeader, follower_loop
+    # every rank's scheduler sees the leader's clock (deadlines expire in lock step)
+    clock = SharedClock() if world > 1 else time.monotonic
     eng = LLMEngine(w, KernelOps() if cuda else TorchOps(), dev, sched, cache,
                     EngineOptions(max_context=a.max_context, graph_sizes=EngineOptions().graph_sizes if cuda else (),
-                                  overlap_steps=not a.no_overlap))
+                                  overlap_steps=not a.no_overlap), comm=comm, clock=clock)
+    if world > 1 and rank != 0:
+        follower_loop(eng, clock, ctrl)
+        return
+    if world > 1:
+        eng = SpmdLeader(eng, clock, ctrl)
     tok = Tokenizer.from_file(a.tokenizer) if a.tokenizer else (tok_from_dir or synthetic_byte_tokenizer())
     svc = EngineService(eng, tok, default_limits(spec.vocab, a.max_context))
     svc.start()
@@ -303,6 +331,8 @@ def serve(args: List[str]):
         asyncio.run(main())
     finally:
         svc.stop()
+        if world > 1:
+            eng.shutdown()
 
 
 def main(argv: Optional[List[str]] = None) -> int:

@@ -201,6 +201,9 @@ class EngineService:
                     self.failed = True
                     self.engine.scheduler.fail_active(PublicErrorCode.WORKER_UNAVAILABLE)
                     self.engine._drain_terminals()
+            elif hasattr(self.engine, "idle"):
+                # a tensor-parallel leader keeps its followers in lock step while idle
+                self.engine.idle()
             self._drain_terminals()
 
 
