@@ -295,9 +295,11 @@ def serve(args: List[str]):
         else:
             comm = TPComm()
     tok_from_dir = None
+    chat_template, eos_ids = None, []
     if ckpt is not None:
         if not a.tokenizer:
             tok_from_dir = ckpt.tokenizer()
+        chat_template, eos_ids = ckpt.chat()
         ckpt.close()
     from .service.spmd import SharedClock, SpmdLeader, follower_loop
     # every rank's scheduler sees the leader's clock (deadlines expire in lock step)
@@ -323,7 +325,8 @@ def serve(args: List[str]):
             print(f"lunaflux metrics on http://{a.host}:{await ms.start()}/metrics", flush=True)
         if a.http_port >= 0:
             from .service.http_api import CompletionsServer
-            hs = CompletionsServer(svc, a.host, a.http_port, model=preset)
+            hs = CompletionsServer(svc, a.host, a.http_port, model=preset, chat_template=chat_template,
+                                   eos_ids=eos_ids)
             print(f"lunaflux completions on http://{a.host}:{await hs.start()}/v1/completions", flush=True)
         await srv.serve_forever()
 

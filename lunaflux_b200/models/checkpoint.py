@@ -101,6 +101,20 @@ class CheckpointDir:
         from ..tokenizer.bpe import Tokenizer
         return Tokenizer.from_json(self._read("tokenizer.json", 1 << 28))
 
+    def chat(self):
+        """(ChatTemplate or None, end-of-turn token ids) from tokenizer_config.json
+        and generation_config.json, when the directory has them."""
+        from ..tokenizer.chat import ChatTemplate
+        template, eos = None, []
+        if self.has("tokenizer_config.json"):
+            cfg = json.loads(self._read("tokenizer_config.json", 1 << 24))
+            template = ChatTemplate.from_tokenizer_config(cfg)
+        if self.has("generation_config.json"):
+            g = json.loads(self._read("generation_config.json", 1 << 20))
+            e = g.get("eos_token_id")
+            eos = [e] if type(e) is int else [x for x in (e or []) if type(x) is int]
+        return template, eos
+
     def tensor(self, name: str) -> torch.Tensor:
         f = self.where.get(name)
         if f is None:

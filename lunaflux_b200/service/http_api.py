@@ -1,9 +1,14 @@
 """OpenAI-style completions over HTTP/1.1, next to the framed TCP protocol.
 
-    POST /v1/completions   {"prompt": str | [token ids], "max_tokens": int,
-                            "temperature": float, "top_p": float, "top_k": int,
-                            "seed": int, "stop": str | [str], "stream": bool}
+    POST /v1/completions        {"prompt": str | [token ids], "max_tokens": int,
+                                 "temperature": float, "top_p": float, "top_k": int,
+                                 "seed": int, "stop": str | [str], "stream": bool}
+    POST /v1/chat/completions   {"messages": [{"role", "content"}], ...same options}
     GET  /v1/models
+
+Chat requests are rendered with the model's chat template (Jinja, from
+tokenizer_config.json), tokenized with its special tokens, and end at the
+model's end-of-turn ids, whose text is not part of the reply.
 
 The reference serves only its framed request/event protocol
 (service/online_tcp); this endpoint is an addition for clients that speak the
@@ -17,6 +22,7 @@ client that disconnects cancels its request.
 from __future__ import annotations
 
 import asyncio
+import dataclasses
 import itertools
 import json
 import time
@@ -84,8 +90,10 @@ def build_request(body: dict, request_id: int) -> GenerateRequest:
 
 class CompletionsServer:
     def __init__(self, service: EngineService, host: str = "127.0.0.1", port: int = 0, model: str = "lunaflux",
-                 max_body: int = 4 << 20):
+                 max_body: int = 4 << 20, chat_template=None, eos_ids=()):
         self.service = service
+        self.chat_template = chat_template
+        self.eos_ids = tuple(int(e) for e in eos_ids)
         self.host = host
         self.port = port
         self.model = model
@@ -149,14 +157,16 @@ class CompletionsServer:
                         raise HTTPError(405, "use GET")
                     self._json(writer, 200, {"object": "list", "data": [{"id": self.model, "object": "model",
                                                                           "owned_by": "lunaflux"}]})
-                elif path == "/v1/completions":
+                elif path in ("/v1/completions", "/v1/chat/completions"):
                     if method != "POST":
                         raise HTTPError(405, "use POST")
                     try:
                         parsed = json.loads(body or b"null")
                     except ValueError:
                         raise HTTPError(400, "the body is not JSON") from None
-                    await self._complete(parsed, reader, writer)
+                    if path == "/v1/chat/completions":
+                        parsed = await self._chat_body(parsed)
+                    await self._complete(parsed, reader, writer, chat=path == "/v1/chat/completions")
                 else:
                     raise HTTPError(404, "no such endpoint")
             except HTTPError as e:
@@ -168,9 +178,32 @@ class CompletionsServer:
             writer.close()
 
     # ------------------------------------------------------------------ completions
-    async def _complete(self, body, reader, writer):
+    async def _chat_body(self, body):
+        """The completions body of a chat request: the rendered, tokenized prompt."""
+        from ..tokenizer.chat import ChatTemplateError
+        if self.chat_template is None or self.service.tokenizer is None:
+            raise HTTPError(404, "this model has no chat template")
+        if not isinstance(body, dict):
+            raise HTTPError(400, "the body must be a JSON object")
+        try:
+            text = self.chat_template.render(body.get("messages"))
+        except ChatTemplateError as e:
+            raise HTTPError(400, str(e)) from None
+        loop = asyncio.get_running_loop()
+        try:
+            ids = await loop.run_in_executor(None, lambda: self.service.tokenizer.encode(text, allow_special=True))
+        except ValueError as e:
+            raise HTTPError(400, f"prompt does not tokenize: {e}") from None
+        out = dict(body)
+        out.pop("messages", None)
+        out["prompt"] = ids
+        return out
+
+    async def _complete(self, body, reader, writer, chat: bool = False):
         rid = next(self._ids)
         req = build_request(body, rid)
+        if chat and self.eos_ids:
+            req = dataclasses.replace(req, stop=StopConditions(self.eos_ids, req.stop.strings))
         try:
             req.validate(self.service.limits)
         except ContractError as e:
@@ -179,7 +212,8 @@ class CompletionsServer:
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
         self.service.submit(req, lambda ev: loop.call_soon_threadsafe(q.put_nowait, ev))
-        cid = f"cmpl-{rid - _ID_BASE}"
+        cid = f"{'chatcmpl' if chat else 'cmpl'}-{rid - _ID_BASE}"
+        kind = "chat.completion" if chat else "text_completion"
         created = int(time.time())
         text = bytearray()
         usage = None
@@ -197,9 +231,11 @@ class CompletionsServer:
                     return
                 ev = get.result()
                 if isinstance(ev, TokenEvent):
+                    if chat and ev.token_id in self.eos_ids:
+                        continue          # the end-of-turn token is not part of the reply
                     text += ev.delta
                     if stream and ev.delta:
-                        self._sse(writer, cid, created, ev.delta.decode("utf-8", errors="replace"), None)
+                        self._sse(writer, cid, created, ev.delta.decode("utf-8", errors="replace"), None, kind=kind)
                         await writer.drain()
                 elif isinstance(ev, Usage):
                     usage = ev
@@ -212,14 +248,15 @@ class CompletionsServer:
                     finished = True
                     if stream:
                         self._sse(writer, cid, created, ev.final_delta.decode("utf-8", errors="replace"), reason,
-                                  usage_obj)
+                                  usage_obj, kind=kind)
                         writer.write(b"data: [DONE]\n\n")
                     else:
-                        self._json(writer, 200, {
-                            "id": cid, "object": "text_completion", "created": created, "model": self.model,
-                            "choices": [{"index": 0, "text": text.decode("utf-8", errors="replace"),
-                                         "finish_reason": reason, "logprobs": None}],
-                            "usage": usage_obj})
+                        content = text.decode("utf-8", errors="replace")
+                        choice = ({"index": 0, "message": {"role": "assistant", "content": content},
+                                   "finish_reason": reason} if chat else
+                                  {"index": 0, "text": content, "finish_reason": reason, "logprobs": None})
+                        self._json(writer, 200, {"id": cid, "object": kind, "created": created, "model": self.model,
+                                                 "choices": [choice], "usage": usage_obj})
                     return
                 elif isinstance(ev, FailedEvent):
                     finished = True
@@ -235,9 +272,13 @@ class CompletionsServer:
                 # the client went away, or writing to it failed
                 self.service.cancel(rid)
 
-    def _sse(self, writer, cid, created, text, reason, usage=None):
-        chunk = {"id": cid, "object": "text_completion", "created": created, "model": self.model,
-                 "choices": [{"index": 0, "text": text, "finish_reason": reason, "logprobs": None}]}
+    def _sse(self, writer, cid, created, text, reason, usage=None, kind="text_completion"):
+        if kind == "chat.completion":
+            choice = {"index": 0, "delta": {"content": text} if text else {}, "finish_reason": reason}
+            kind = "chat.completion.chunk"
+        else:
+            choice = {"index": 0, "text": text, "finish_reason": reason, "logprobs": None}
+        chunk = {"id": cid, "object": kind, "created": created, "model": self.model, "choices": [choice]}
         if usage is not None:
             chunk["usage"] = usage
         writer.write(b"data: " + json.dumps(chunk).encode() + b"\n\n")

@@ -136,3 +136,71 @@ def test_disconnect_cancels(stack):
     assert _run(svc, go)
     assert not eng.live
     assert 'reason="cancelled"' in eng.metrics.registry.render_prometheus()
+
+
+def test_chat_template_rendering_and_checkpoint(tmp_path):
+    """A chat template from tokenizer_config.json (named templates, special
+    tokens as {content}) and the end-of-turn ids from generation_config.json."""
+    from lunaflux_b200.tokenizer.chat import ChatTemplate, ChatTemplateError
+    cfg = {"bos_token": {"content": "<s>"}, "eos_token": "</s>",
+           "chat_template": [{"name": "default", "template":
+                              "{{ bos_token }}{% for m in messages %}<|{{ m['role'] }}|>{{ m['content'] }}</s>"
+                              "{% endfor %}{% if tools is defined and tools %}X{% endif %}"
+                              "{% if add_generation_prompt %}<|assistant|>{% endif %}"}]}
+    t = ChatTemplate.from_tokenizer_config(cfg)
+    out = t.render([{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}])
+    assert out == "<s><|system|>be brief</s><|user|>hi</s><|assistant|>"
+    with pytest.raises(ChatTemplateError):
+        t.render([{"role": "user"}])
+    with pytest.raises(ChatTemplateError):
+        ChatTemplate("{% if %}")
+    bad = ChatTemplate("{{ raise_exception('no system role') }}")
+    with pytest.raises(ChatTemplateError):
+        bad.render([{"role": "system", "content": "x"}])
+    # from a model directory
+    from lunaflux_b200.models.checkpoint import CheckpointDir, save_sharded
+    from lunaflux_b200.models.config_reader import to_config
+    from lunaflux_b200.models.spec import tiny_llama
+    from lunaflux_b200.models.weights import random_checkpoint
+    spec = tiny_llama()
+    save_sharded(random_checkpoint(spec, 0), str(tmp_path), config=to_config(spec))
+    (tmp_path / "tokenizer_config.json").write_text(json.dumps(cfg))
+    (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": [7, 9]}))
+    with CheckpointDir(str(tmp_path)) as ck:
+        tmpl, eos = ck.chat()
+    assert eos == [7, 9] and tmpl.render([{"role": "user", "content": "x"}]).endswith("<|assistant|>")
+
+
+def test_chat_completions_endpoint(stack):
+    svc, ref, eng = stack
+    from lunaflux_b200.service.http_api import CompletionsServer
+    from lunaflux_b200.tokenizer.chat import ChatTemplate
+    tmpl = ChatTemplate("{% for m in messages %}[{{ m.role }}]{{ m.content }}{% endfor %}"
+                        "{% if add_generation_prompt %}[assistant]{% endif %}")
+    messages = [{"role": "user", "content": "Hello"}]
+    prompt = list(tmpl.render(messages).encode())
+    full = ref.generate_greedy(prompt, 10)
+    eos = full[3]
+    want = bytes(full[:full.index(eos)]).decode("utf-8", errors="replace")
+
+    async def main():
+        srv = CompletionsServer(svc, model="tiny", chat_template=tmpl, eos_ids=(eos,))
+        port = await srv.start()
+        try:
+            a = await _http(port, "POST", "/v1/chat/completions", {"messages": messages, "max_tokens": 10})
+            b = await _http(port, "POST", "/v1/chat/completions", {"messages": messages, "max_tokens": 10,
+                                                                   "stream": True})
+            c = await _http(port, "POST", "/v1/chat/completions", {"messages": "nope"})
+            return a, b, c
+        finally:
+            srv.close()
+
+    (sa, pa), (sb, pb), (sc, pc) = asyncio.run(main())
+    body = json.loads(pa)
+    assert sa == 200 and body["object"] == "chat.completion"
+    assert body["choices"][0]["message"] == {"role": "assistant", "content": want}
+    assert body["choices"][0]["finish_reason"] == "stop"
+    chunks = [json.loads(e[len(b"data: "):]) for e in pb.split(b"\n\n") if e.startswith(b"data: {")]
+    assert all(c["object"] == "chat.completion.chunk" for c in chunks)
+    assert "".join(c["choices"][0]["delta"].get("content", "") for c in chunks) == want
+    assert sc == 400
