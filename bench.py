@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="synchronous steps (default: overlapped, step n+1 planned and launched before step n's "
                          "tokens reach the host)")
+    ap.add_argument("--opt", default="",
+                    help="comma-separated opt-in paths to enable: " + ",".join(sorted(OPT_IN)))
     ap.add_argument("--json-out", default="")
     ap.add_argument("--profile", default="", help="write a per-kernel time table of one extra pass here")
     return ap.parse_args()
@@ -128,11 +130,27 @@ class ClockSampler:
                 "power_w_max": max((num(r[3]) or 0) for r in rows)}
 
 
+# Opt-in kernel paths (off by default until measured), as environment switches
+# read by the extension and the operator set at first use.
+OPT_IN = {
+    "pdl": "LUNAFLUX_PDL",
+    "qkv_rope": "LUNAFLUX_FUSE_QKV_ROPE",
+    "ll_gemm": "LUNAFLUX_FUSED_LL_GEMM",
+    "gemm_2sm": "LUNAFLUX_GEMM_2SM",
+    "cluster_mb2": "LUNAFLUX_GEMM_CLUSTER_MB2",
+}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_unavailable(args)
         return 0
+    opts_on = [o for o in args.opt.split(",") if o]
+    for o in opts_on:
+        if o not in OPT_IN:
+            raise SystemExit(f"unknown --opt {o!r} (known: {', '.join(sorted(OPT_IN))})")
+        os.environ[OPT_IN[o]] = "1"
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -252,7 +270,7 @@ def main():
         "impl": args.impl,
         "config": {"model": f"{args.model} ({spec.layers} layers)", "global_batch": args.requests,
                    "seq_len": args.prompt_len, "output_len": args.output_len, "parallelism": f"tp{world}", "comm": (args.comm if world > 1 else "none"),
-                   "overlap_steps": bool(args.overlap),
+                   "overlap_steps": bool(args.overlap), "opt_in": opts_on,
                    "l2": "weights (16 GB) and KV (>10 GB) exceed L2 every step; no flush needed",
                    "engine_iterations_per_step": steps_run / args.steps},
         "ttft_p50_ms": round(statistics.median(ttfts), 2) if ttfts else None,
