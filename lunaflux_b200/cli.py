@@ -9,7 +9,8 @@ same argument order) and cmd/lunaflux_plan/plan.mbt:1-80; ``serve``,
     lunaflux plan ROOT CONFIG_REL CONFIG_SHA256 DECLARED_MODEL_SHA256 KV_BUDGET_BYTES TOKENS_PER_PAGE
     lunaflux reference ROOT CONFIG_REL TOKENIZER_REL WEIGHTS_REL CONFIG_SHA TOKENIZER_SHA WEIGHTS_SHA MAX_NEW TOKEN_IDS
     lunaflux version
-    lunaflux serve [--config FILE | --preset NAME] [--host H] [--port P] [--layers N]
+    lunaflux serve [--config FILE | --preset NAME | --model-dir DIR] [--host H] [--port P] [--http-port P]
+                   [--metrics-port P] [--layers N]   (under torchrun: tensor parallel, rank 0 serves)
     lunaflux bench [bench.py arguments]
     lunaflux inspect-kernels
 """
@@ -36,7 +37,8 @@ def usage() -> str:
         "  lunaflux reference ROOT CONFIG_REL TOKENIZER_REL WEIGHTS_REL CONFIG_SHA TOKENIZER_SHA WEIGHTS_SHA "
         "MAX_NEW TOKEN_IDS",
         "  lunaflux version",
-        "  lunaflux serve [--config FILE | --preset NAME] [--host H] [--port P] [--layers N]",
+        "  lunaflux serve [--config FILE | --preset NAME | --model-dir DIR] [--host H] [--port P] [--http-port P]",
+        "                 [--metrics-port P] [--layers N]   (under torchrun: tensor parallel, rank 0 serves)",
         "  lunaflux bench [bench.py arguments]",
         "  lunaflux inspect-kernels",
     ])
