@@ -309,6 +309,9 @@ def serve(args: List[str]):
     eng = LLMEngine(w, KernelOps() if cuda else TorchOps(), dev, sched, cache,
                     EngineOptions(max_context=a.max_context, graph_sizes=EngineOptions().graph_sizes if cuda else (),
                                   overlap_steps=not a.no_overlap), comm=comm, clock=clock)
+    if cuda:
+        # capture the decode graphs now (every rank, same order), not on the first requests
+        eng.runner.capture_all(False)
     if world > 1 and rank != 0:
         follower_loop(eng, clock, ctrl)
         return
