@@ -1,6 +1,10 @@
 """Headline benchmark: Llama-3-8B-shaped serving on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|torch|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|library|reference]
+
+``--impl library`` is the measured baseline: the same engine, scheduler and
+workload on cuBLAS GEMMs, vLLM's paged flash-attention, torch elementwise ops
+and NCCL collectives, with the same CUDA-graph decode buckets.
 
 Workload: 256 concurrent requests, 1024-token prompts
 drawn uniformly from the vocabulary (seeded), 256 greedy output tokens each,
@@ -44,7 +48,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "torch", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "library", "torch", "reference"],
+                    help="torch is an alias of library")
     ap.add_argument("--model", default="llama3-8b")
     ap.add_argument("--layers", type=int, default=0, help="0 = the full model")
     ap.add_argument("--requests", type=int, default=256)
@@ -66,6 +71,15 @@ def parse():
     ap.add_argument("--json-out", default="")
     ap.add_argument("--profile", default="", help="write a per-kernel time table of one extra pass here")
     return ap.parse_args()
+
+
+def pct(xs, q, nd):
+    """The q-th percentile (nearest rank) of xs, rounded; None when empty."""
+    if not xs:
+        return None
+    ys = sorted(xs)
+    k = min(len(ys) - 1, max(0, int(round(q / 100.0 * len(ys) + 0.5)) - 1))
+    return round(ys[k], nd)
 
 
 def reference_unavailable(args):
@@ -146,6 +160,8 @@ def main():
     if args.impl == "reference":
         reference_unavailable(args)
         return 0
+    if args.impl == "torch":
+        args.impl = "library"
     opts_on = [o for o in args.opt.split(",") if o]
     for o in opts_on:
         if o not in OPT_IN:
@@ -189,18 +205,18 @@ def main():
         from lunaflux_b200.ops import KernelOps
         ops = KernelOps()
     else:
-        from lunaflux_b200.ops import TorchOps
-        ops = TorchOps(dev)
+        from lunaflux_b200.ops import LibraryOps
+        ops = LibraryOps(dev)
     max_ctx = args.prompt_len + args.output_len + 16
     sched = SchedulerConfig(step_token_budget=args.step_token_budget, max_active_requests=args.requests,
                             prefill_chunk_tokens=args.step_token_budget, emergency_decode_page_reserve=args.requests,
                             max_waiting_requests=max(4096, args.requests))
     pages = args.requests * (-(-max_ctx // 16)) + 2 * args.requests + 64
     opts = EngineOptions(max_context=max_ctx, num_pages=pages,
-                         graph_sizes=() if (args.no_graphs or args.impl != "ours") else EngineOptions().graph_sizes,
+                         graph_sizes=() if args.no_graphs else EngineOptions().graph_sizes,
                          sequence_parallel=args.sp, overlap_steps=args.overlap)
     engine = LLMEngine(weights, ops, dev, sched, CacheConfig(prefix_enabled=False), opts, comm=comm)
-    if args.impl == "ours":
+    if not args.no_graphs:
         engine.runner.capture_all(False)
     torch.cuda.synchronize()
 
@@ -228,6 +244,13 @@ def main():
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ttfts, tpots = [], []
+    emits = []     # wall time of every engine iteration that emitted tokens (inter-token latency)
+
+    def on_outputs(outs):
+        if outs:
+            emits.append(time.perf_counter())
+
+    engine.listeners.append(on_outputs)
     tokens = 0
     wall0 = time.perf_counter()
     ev0.record()
@@ -247,6 +270,8 @@ def main():
     ev1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - wall0
+    engine.listeners.remove(on_outputs)
+    itls = [(b - a) * 1e3 for a, b in zip(emits, emits[1:])]
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
@@ -273,8 +298,10 @@ def main():
                    "overlap_steps": bool(args.overlap), "opt_in": opts_on,
                    "l2": "weights (16 GB) and KV (>10 GB) exceed L2 every step; no flush needed",
                    "engine_iterations_per_step": steps_run / args.steps},
-        "ttft_p50_ms": round(statistics.median(ttfts), 2) if ttfts else None,
-        "tpot_p50_ms": round(statistics.median(tpots), 3) if tpots else None,
+        "ttft_p50_ms": pct(ttfts, 50, 2), "ttft_p95_ms": pct(ttfts, 95, 2), "ttft_p99_ms": pct(ttfts, 99, 2),
+        "tpot_p50_ms": pct(tpots, 50, 3), "tpot_p95_ms": pct(tpots, 95, 3), "tpot_p99_ms": pct(tpots, 99, 3),
+        "itl_p50_ms": pct(itls, 50, 3), "itl_p95_ms": pct(itls, 95, 3), "itl_p99_ms": pct(itls, 99, 3),
+        "goodput_req_s": round(args.requests * args.steps / wall, 2),
         "e2e": {"value": round(e2e, 1), "unit": "output tokens/s through LLMEngine.generate (wall clock)",
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": launches,

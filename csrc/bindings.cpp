@@ -642,6 +642,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_set_cluster_mb2", &gemm_set_cluster_mb2);
   m.def("gemm_qkv_rope", &gemm_qkv_rope);
   m.def("gemm_set_pair", [](bool on) { lf::gemm::set_gemm_pair(on ? 1 : 0); });
+  m.def("gemm_get_pair", []() { return lf::gemm::get_gemm_pair() != 0; });
   m.def("gemm_set_ll_fused", [](bool on) { lf::gemm::set_ll_gemm_fused(on ? 1 : 0); });
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_grouped", &gemm_grouped);

@@ -107,12 +107,18 @@ __device__ __forceinline__ float ex2_approx(float x) {
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// Diagnostics: the CTA's progress code, written through to host-visible memory.
+// Diagnostics, compiled in only with -DLF_ATTN_PROGRESS_TRACE: the CTA's
+// progress code, written through to host-visible memory (PrefillArgs.progress).
 __device__ __forceinline__ void mark(const PrefillArgs& a, int code) {
+#ifdef LF_ATTN_PROGRESS_TRACE
   if (a.progress != nullptr) {
     const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
     asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(a.progress + cta), "r"(code) : "memory");
   }
+#else
+  (void)a;
+  (void)code;
+#endif
 }
 
 __device__ __forceinline__ int bt_page(const PrefillArgs& a, int r, int idx) {

@@ -158,8 +158,9 @@ static void launch(const GemmArgs& a, cudaStream_t stream, int splits = 1, int k
 // Split-K plan for skinny GEMMs: 256-wide tiles (so the activations are
 // re-read from L2 as few times as possible) and enough K-splits to cover the
 // SMs, each split at least 4 k-blocks.  Returns splits (1 = no split).
-int plan_splitk(int M, int N, int K, int* kb_per_out) {
-  const int sms = num_sms();
+int plan_splitk(int M, int N, int K, int* kb_per_out) { return plan_splitk_sms(M, N, K, num_sms(), kb_per_out); }
+
+int plan_splitk_sms(int M, int N, int K, int sms, int* kb_per_out) {
   const int num_m = (M + BM - 1) / BM;
   const int num_kb = (K + BK - 1) / BK;
   if (N % 256 != 0) return 1;
@@ -343,8 +344,9 @@ namespace gemm {
 // Tile-width choice: the widest BN that still yields enough tiles to cover
 // the SMs (wide tiles reuse A best; narrow tiles spread a skinny decode GEMM
 // over more SMs so the weight stream uses all of HBM).
-int choose_bn(int M, int N, int epi) {
-  const int sms = num_sms();
+int choose_bn(int M, int N, int epi) { return choose_bn_sms(M, N, epi, num_sms()); }
+
+int choose_bn_sms(int M, int N, int epi, int sms) {
   const int num_m = (M + BM - 1) / BM;
   const int cands[4] = {256, 128, 64, 32};
   for (int i = 0; i < 4; ++i) {

@@ -25,6 +25,8 @@ struct GemmArgs {
 // accepted for interface stability and unused.
 void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws = nullptr, int64_t ws_elems = 0);
 int plan_splitk(int M, int N, int K, int* kb_per_out);
+// The same plan for a device with `sms` multiprocessors.
+int plan_splitk_sms(int M, int N, int K, int sms, int* kb_per_out);
 // Cluster split-K plan: returns the cluster size (0 = plain tiles) and its BN / k-blocks per CTA /
 // 128-row M-blocks per tile.
 int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out, int* mb_out = nullptr);
@@ -32,8 +34,9 @@ int plan_cluster(int M, int N, int K, int epi, int* bn_out, int* kb_per_out, int
 void set_cluster_mb2(int on);
 // Enables the single-kernel decode GEMM + low-latency all-reduce in run_allreduce_ll (off by default).
 void set_ll_gemm_fused(int on);
-// Enables the CTA-pair (tcgen05 cta_group::2) kernel for large GEMMs (off by default).
+// Enables the CTA-pair (tcgen05 cta_group::2) kernel for large GEMMs (on by default).
 void set_gemm_pair(int on);
+int get_gemm_pair();
 
 // Peer view of one tensor-parallel group for the fused GEMM + all-reduce.
 // Two symmetric bf16 regions of [rows, N] (every rank holds both, same size):
@@ -103,6 +106,7 @@ void run_allreduce(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream, flo
 // result kept by the owner.
 void run_reduce_scatter(const GemmArgs& a, const ArArgs& ar, cudaStream_t stream);
 int choose_bn(int M, int N, int epi);
+int choose_bn_sms(int M, int N, int epi, int sms);
 // Decode shapes: GEMM into fp32 slabs of ws (split-K when it fills the SMs),
 // then the low-latency all-reduce (allreduce_ll.h) into a.D.
 void run_allreduce_ll(const GemmArgs& a, const ar::LLArgs& ll, cudaStream_t stream, float* ws, int64_t ws_elems);

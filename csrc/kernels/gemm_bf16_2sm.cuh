@@ -288,13 +288,17 @@ static int g_pair = -1;
 
 void set_gemm_pair(int on) { g_pair = on ? 1 : 0; }  // declared in gemm_bf16.h
 
+// On by default (it beats the single-CTA kernel on every large shape
+// measured); LUNAFLUX_GEMM_2SM=0 turns it off.
 static bool pair_enabled() {
   if (g_pair < 0) {
     const char* e = getenv("LUNAFLUX_GEMM_2SM");
-    g_pair = (e != nullptr && e[0] == '1') ? 1 : 0;
+    g_pair = (e != nullptr && e[0] == '0') ? 0 : 1;
   }
   return g_pair == 1;
 }
+
+int get_gemm_pair() { return pair_enabled() ? 1 : 0; }  // declared in gemm_bf16.h
 
 // Launches the CTA-pair kernel for large GEMMs (enough 256 x 256 tiles to fill
 // the SMs) when it is enabled; returns false otherwise.

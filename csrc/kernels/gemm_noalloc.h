@@ -21,12 +21,16 @@
 // Set-up: the first call on each device, made with that device current,
 // resolves the scratch array's device address (cudaGetSymbolAddress) and sets
 // the kernels' shared-memory limits.  Make that first call before any stream
-// capture on that device.
+// capture on that device.  A set-up that fails returns
+// LF_NOALLOC_SETUP_FAILED and is retried by the next call.
 //
 // Semantics: D[M, N] = A[M, K] . B[N, K]^T with bf16 A/B (row strides lda,
 // ldb in elements) and, by `epi`: 0 bf16 D, 1 fp32 D, 2 SwiGLU (B's rows are
-// gate/up interleaved in groups of 32 rows; D is bf16 [M, N/2]).  Results are
-// identical to the allocating entry point given a large enough workspace.
+// gate/up interleaved in groups of 32 rows; D is bf16 [M, N/2]).  Skinny
+// shapes are split over K into fp32 slabs in the scratch array and summed by
+// a second kernel, a different plan from the allocating entry point's (which
+// reduces split partials in distributed shared memory): the two agree within
+// bf16 rounding, not bitwise.
 #pragma once
 #include <stdint.h>
 
@@ -44,8 +48,10 @@ extern "C" {
 #endif
 
 // `stream` is a cudaStream_t (0 = the legacy default stream).  Returns one of
-// the LF_NOALLOC_* codes; nothing is launched unless it returns LF_NOALLOC_OK
-// or LF_NOALLOC_LAUNCH_FAILED.
+// the LF_NOALLOC_* codes; nothing is launched (and D is untouched) unless it
+// returns LF_NOALLOC_OK or LF_NOALLOC_LAUNCH_FAILED.  Each launch's own return
+// code decides LF_NOALLOC_LAUNCH_FAILED: errors left by the caller's earlier
+// CUDA calls are neither reported nor cleared.
 int lf_gemm_bf16_noalloc(const void* A, const void* B, void* D, int M, int N, int K, int64_t lda, int64_t ldb,
                          int64_t ldd, int epi, void* stream);
 

@@ -95,12 +95,15 @@ def bench_gemm(C, results, only_case="", variants=False):
         extra = {}
         if variants:
             # opt-in kernel variants of the same call, timed the same way
-            for key, setter in (("pair_ms", C.gemm_set_pair), ("cluster_256_rows_ms", C.gemm_set_cluster_mb2)):
-                setter(True)
+            # (the CTA-pair kernel is on by default: time the single-CTA kernel)
+            pair_was = C.gemm_get_pair()
+            for key, setter, on in (("single_cta_ms", C.gemm_set_pair, False),
+                                    ("cluster_256_rows_ms", C.gemm_set_cluster_mb2, True)):
+                setter(on)
                 try:
                     extra[key] = time_fn(lambda: C.gemm(A, B, D, epi, 0, ws))
                 finally:
-                    setter(False)
+                    setter(pair_was if setter is C.gemm_set_pair else False)
         flops = 2.0 * M * N * K
         bytes_ = 2.0 * (M * K + N * K) + D.numel() * D.element_size()
         t_roof = max(flops / (tflops_peak * 1e12), bytes_ / (hbm * 1e9)) * 1e3

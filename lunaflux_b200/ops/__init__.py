@@ -9,3 +9,9 @@
 """
 from .kernel_ops import KernelOps  # noqa: F401
 from .torch_ops import TorchOps  # noqa: F401
+
+
+def LibraryOps(device):
+    """The library baseline operator set (cuBLAS, vLLM flash-attention, torch)."""
+    from .library_ops import LibraryOps as _L
+    return _L(device)

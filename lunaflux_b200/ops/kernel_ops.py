@@ -28,8 +28,8 @@ class KernelOps:
         self.num_sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
         self._splitk = {}
         # QKV GEMM with RoPE and the paged K / V write in its epilogue (one
-        # kernel instead of two); off unless LUNAFLUX_FUSE_QKV_ROPE=1
-        self.fuse_qkv_rope = os.environ.get("LUNAFLUX_FUSE_QKV_ROPE") == "1"
+        # kernel instead of two); on unless LUNAFLUX_FUSE_QKV_ROPE=0
+        self.fuse_qkv_rope = os.environ.get("LUNAFLUX_FUSE_QKV_ROPE") != "0"
 
     def embed(self, ids, table, out):
         self.launches += 1

@@ -90,9 +90,6 @@ def test_fused_gemm_allreduce_matches_nccl():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
-                    reason="single-kernel decode GEMM + all-reduce: first multi-GPU run pending "
-                           "(set LUNAFLUX_TEST_NEW_KERNELS=1)")
 def test_single_kernel_decode_gemm_allreduce_matches_nccl():
     _run(fused_ll=True)
 
@@ -155,8 +152,6 @@ def _rs_worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
-                    reason="GEMM + reduce-scatter: first multi-GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
 def test_gemm_reduce_scatter_matches_nccl():
     """The row-parallel GEMM with the reduce-scatter in the kernel (tiles
     dealt to their rows' owner) against the fp32 partials reduce-scattered by

@@ -92,9 +92,6 @@ def _check_cluster_gemm(C, M, N, K, epi):
     assert C.read_error(True)[0] == 0
 
 
-@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
-                    reason="256-row cluster tiles: an opt-in variant, slower on the decode shapes (set "
-                           "LUNAFLUX_TEST_NEW_KERNELS=1)")
 @pytest.mark.parametrize("M,N,K,epi", [(256, 6144, 4096, 0), (256, 4096, 14336, 0), (256, 4096, 4096, 1),
                                        (129, 1024, 4096, 2), (250, 1536, 1024, 2), (200, 6144, 4096, 1)])
 def test_gemm_cluster_splitk_256_row_tiles(C, M, N, K, epi):
@@ -421,9 +418,6 @@ def test_moe_kernels_match_torch(C):
     assert C.read_error(True)[0] == 0
 
 
-@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
-                    reason="QKV GEMM with RoPE + KV write epilogue: first GPU run pending "
-                           "(set LUNAFLUX_TEST_NEW_KERNELS=1)")
 @pytest.mark.parametrize("M,Hq,Hkv,K", [(1, 32, 8, 4096), (37, 32, 8, 4096), (256, 32, 8, 4096),
                                         (200, 64, 8, 1024), (1000, 32, 8, 4096), (5000, 3, 1, 512),
                                         (256, 4, 1, 4096)])
@@ -455,8 +449,6 @@ def test_gemm_qkv_rope_matches_gemm_then_rope(C, M, Hq, Hkv, K):
     _close(vc.float(), vc_ref.float(), 3e-2, 3e-2, "fused V cache")
 
 
-@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
-                    reason="CTA-pair (cta_group::2) GEMM: first GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
 @pytest.mark.parametrize("M,N,K,epi", [(2048, 4096, 4096, 0), (8192, 6144, 4096, 0), (4096, 28672, 4096, 2),
                                        (300, 32768, 512, 1), (2048, 4096, 1000, 0)])
 def test_gemm_cta_pair(C, M, N, K, epi):
@@ -467,12 +459,13 @@ def test_gemm_cta_pair(C, M, N, K, epi):
     B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
     out_cols = N // 2 if epi == 2 else N
     D = torch.empty(M, out_cols, device="cuda", dtype=torch.float32 if epi == 1 else torch.bfloat16)
+    was = C.gemm_get_pair()
     C.gemm_set_pair(True)
     try:
         C.gemm(A, B, D, epi, 0, None)
         torch.cuda.synchronize()
     finally:
-        C.gemm_set_pair(False)
+        C.gemm_set_pair(was)
     assert C.read_error(True)[0] == 0
     ref = A.float() @ B.float().t()
     if epi == 2:
@@ -481,8 +474,6 @@ def test_gemm_cta_pair(C, M, N, K, epi):
     _close(D, ref, 3e-2, 3e-2, f"cta-pair gemm {M}x{N}x{K} epi={epi}")
 
 
-@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
-                    reason="vocab-parallel candidate sampler: first GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
 @pytest.mark.parametrize("ranks", [2, 8])
 def test_sample_from_shard_candidates_equals_full_row(C, ranks):
     """Per-shard top-64 keys, gathered, then the draw: the same tokens as the

@@ -96,3 +96,27 @@ def test_no_todo_markers(tree):
                     if any(m in line for m in ("TODO", "FIXME", "XXX")):
                         hits.append(f"{path}:{i}")
     assert not hits, hits
+
+
+def _native_sources():
+    for tree in ("csrc", "lunaflux_b200"):
+        for dirpath, _, files in os.walk(os.path.join(ROOT, tree)):
+            for f in files:
+                if f.endswith((".py", ".cu", ".cuh", ".cpp", ".hpp", ".h")):
+                    yield os.path.join(dirpath, f)
+
+
+def test_no_tma_or_bulk_load_with_cluster_multicast():
+    """No bulk or tensor (TMA) copy anywhere in the sources carries the
+    cluster-multicast qualifier: a multicast load whose source can be another
+    GPU's memory is not allowed, and the multi-GPU paths share these files.
+    `tcgen05.commit ... .multicast::cluster` is an mbarrier arrive, not a
+    load, and stays allowed."""
+    import re
+    pat = re.compile(r"cp\.async\.bulk[^\"\n]*multicast")
+    hits = []
+    for path in _native_sources():
+        for i, line in enumerate(open(path, encoding="utf-8", errors="replace"), 1):
+            if pat.search(line):
+                hits.append(f"{path}:{i}")
+    assert not hits, hits

@@ -58,13 +58,20 @@ def _worker(rank, world, port, q):
         sched = SchedulerConfig(step_token_budget=256, max_active_requests=8, prefill_chunk_tokens=256,
                                 emergency_decode_page_reserve=4)
         outs = {}
-        for name, comm, sp in (("fused", FusedTPComm(512, spec.hidden, dev), False), ("nccl", TPComm(), False),
-                               ("sp", TPComm(), True), ("sp_fused", FusedTPComm(512, spec.hidden, dev), True)):
+        ops = KernelOps()
+        for name, comm, sp, ll in (("fused", FusedTPComm(512, spec.hidden, dev), False, False),
+                                   ("fused_ll", FusedTPComm(512, spec.hidden, dev), False, True),
+                                   ("nccl", TPComm(), False, False), ("sp", TPComm(), True, False),
+                                   ("sp_fused", FusedTPComm(512, spec.hidden, dev), True, False)):
             opts = EngineOptions(max_context=1024, num_pages=256, graph_sizes=(1, 2, 4), overlap_steps=True,
                                  sequence_parallel=sp)
-            eng = LLMEngine(w, KernelOps(), dev, sched, CacheConfig(prefix_enabled=False), opts, comm=comm)
-            outs[name] = eng.generate(_prompts(spec), 10)
-            torch.cuda.synchronize(dev)
+            ops.C.gemm_set_ll_fused(ll)    # decode GEMM + low-latency all-reduce in one kernel
+            try:
+                eng = LLMEngine(w, ops, dev, sched, CacheConfig(prefix_enabled=False), opts, comm=comm)
+                outs[name] = eng.generate(_prompts(spec), 10)
+                torch.cuda.synchronize(dev)
+            finally:
+                ops.C.gemm_set_ll_fused(False)
             outs[name + "_err"] = eng.runner.ops.read_error(True)[0]
         q.put((rank, outs))
         dist.barrier()
@@ -74,8 +81,6 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
-                    reason="first multi-GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
 def test_tp_engine_tracks_oracle():
     import torch.multiprocessing as mp
     from lunaflux_b200.oracle.reference import ReferenceModel
@@ -94,7 +99,7 @@ def test_tp_engine_tracks_oracle():
     spec = _spec()
     ref = ReferenceModel(spec, _checkpoint(spec))
     prompts = _prompts(spec)
-    for name in ("fused", "nccl", "sp", "sp_fused"):
+    for name in ("fused", "fused_ll", "nccl", "sp", "sp_fused"):
         for r in range(world):
             assert res[r][name + "_err"] == 0, (name, r)
             assert res[r][name] == res[0][name], f"{name}: rank {r} differs from rank 0"
@@ -149,8 +154,6 @@ def _moe_spec():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.skipif(os.environ.get("LUNAFLUX_TEST_NEW_KERNELS") != "1",
-                    reason="expert all-to-all over NVLink: first multi-GPU run pending (set LUNAFLUX_TEST_NEW_KERNELS=1)")
 def test_moe_expert_all_to_all_tracks_oracle():
     """Experts sharded over the GPUs: on replicated rows (all-reduce), and on
     token-sharded rows with the device dispatch / combine; both track the
