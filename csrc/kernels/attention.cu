@@ -128,6 +128,38 @@ __global__ void __launch_bounds__(32) decode_kernel(const __grid_constant__ CUte
   }
   __syncwarp();
 
+  const int count = p_end > p_begin ? p_end - p_begin : 0;
+  // Block-table window in registers: lane j holds the page of split-relative
+  // index win_base + j; the next window is loaded 32 pages ahead of its use,
+  // so no refill waits on a block-table read.
+  int win_base = 0;
+  int win = lane < count ? checked_page(bt, p_begin + lane, a.num_pages) : 0;
+  int win_next = 32 + lane < count ? checked_page(bt, p_begin + 32 + lane, a.num_pages) : 0;
+  auto page_at = [&](int idx) {  // idx increases monotonically; called by the whole (converged) warp
+    while (idx >= win_base + 32) {
+      win = win_next;
+      win_base += 32;
+      const int j = win_base + 32 + lane;
+      win_next = j < count ? checked_page(bt, p_begin + j, a.num_pages) : 0;
+    }
+    return __shfl_sync(0xffffffffu, win, idx - win_base);
+  };
+  {
+    // first pages in flight before Q is read
+    int first[kDecStages];
+#pragma unroll
+    for (int i = 0; i < kDecStages; ++i) first[i] = i < count ? page_at(i) : 0;
+    if (lane == 0) {
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      for (int i = 0; i < kDecStages && i < count; ++i) {
+        uint8_t* sk = smem + i * 2 * kPageBytes;
+        mbar_arrive_expect_tx(&full[i], 2 * kPageBytes);
+        load_page(&tk, &tv, sk, sk + kPageBytes, &full[i], first[i], kvh, a.Hkv);
+      }
+    }
+  }
+
   const int g = lane >> 2;
   const __nv_bfloat16* qbase = a.q + (size_t)tok * a.q_ld + (size_t)kvh * G * D;
   uint32_t qa[8][4];
@@ -138,16 +170,6 @@ __global__ void __launch_bounds__(32) decode_kernel(const __grid_constant__ CUte
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
-  const int count = p_end > p_begin ? p_end - p_begin : 0;
-  if (lane == 0) {
-    tma_prefetch_desc(&tk);
-    tma_prefetch_desc(&tv);
-    for (int i = 0; i < kDecStages && i < count; ++i) {
-      uint8_t* sk = smem + i * 2 * kPageBytes;
-      mbar_arrive_expect_tx(&full[i], 2 * kPageBytes);
-      load_page(&tk, &tv, sk, sk + kPageBytes, &full[i], checked_page(bt, p_begin + i, a.num_pages), kvh, a.Hkv);
-    }
-  }
   bool ok = true;
   for (int i = 0; i < count; ++i) {
     const int s = i % kDecStages;
@@ -221,12 +243,14 @@ __global__ void __launch_bounds__(32) decode_kernel(const __grid_constant__ CUte
       mma_bf16(o[2 * nn + 1], pa0, pa1, pa2, pa3, v2, v3);
     }
     __syncwarp();
-    if (lane == 0 && i + kDecStages < count) {
-      fence_proxy_async_smem();
-      uint8_t* skp = smem + s * 2 * kPageBytes;
-      mbar_arrive_expect_tx(&full[s], 2 * kPageBytes);
-      load_page(&tk, &tv, skp, skp + kPageBytes, &full[s], checked_page(bt, p_begin + i + kDecStages, a.num_pages),
-                kvh, a.Hkv);
+    if (i + kDecStages < count) {
+      const int pg = page_at(i + kDecStages);
+      if (lane == 0) {
+        fence_proxy_async_smem();
+        uint8_t* skp = smem + s * 2 * kPageBytes;
+        mbar_arrive_expect_tx(&full[s], 2 * kPageBytes);
+        load_page(&tk, &tv, skp, skp + kPageBytes, &full[s], pg, kvh, a.Hkv);
+      }
     }
   }
   if (!ok) return;
@@ -491,13 +515,44 @@ static CUtensorMap cache_map(const void* base, int64_t rows) {
   return m;
 }
 
+// Decode CTAs (one warp each) resident per SM, from the kernel's resources.
+static int decode_ctas_per_sm() {
+  static int n = 0;
+  if (n == 0) {
+    const int smem = kDecStages * 2 * kPageBytes + 1024 + 64;
+    cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel, 32, smem) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = 6;
+    }
+  }
+  return n;
+}
+
+// Split-KV count.  Each (row, head, split) is one CTA and all of them take
+// about the same time, so the grid runs in waves of num_sms x ctas_per_sm:
+// the cost model is waves x (pages per split + a fixed per-CTA start-up of
+// about 3 page times) + the combine pass (about one page time per split),
+// minimised over 1..32 splits with at least 8 pages per split.  For 256 rows
+// x 8 heads x 72 pages on 148 SMs this picks 3 splits (7 full waves) over 1
+// split (2.3 waves, the last one a third full).
 int decode_splits(int rows, int Hkv, int max_seq, int num_sms) {
   const int units = rows * Hkv;
   const int pages = (max_seq + PAGE - 1) / PAGE;
-  int s = 1;
-  // Aim for ~4 warps per SM of work; keep >= 8 pages per split.
-  while (units * s < 4 * num_sms && pages / (s * 2) >= 8 && s < 32) s *= 2;
-  return s;
+  if (units <= 0 || pages <= 0) return 1;
+  const int64_t slots = (int64_t)num_sms * decode_ctas_per_sm();
+  int best = 1;
+  double best_cost = 1e30;
+  for (int s = 1; s <= 32; ++s) {
+    if (s > 1 && pages / s < 8) break;
+    const int64_t waves = ((int64_t)units * s + slots - 1) / slots;
+    const double cost = (double)waves * ((pages + s - 1) / s + 3) + (s > 1 ? s : 0);
+    if (cost < best_cost * 0.98) {  // prefer fewer splits unless clearly better
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
 }
 
 void decode(const DecodeArgs& a_in, const void* kcache, const void* vcache, cudaStream_t stream) {

@@ -9,17 +9,19 @@ deadlines; process/README.mbt.md:1-20).  One frame per message:
 length poisons the channel: every later call raises ``ChannelClosed``.  The
 C++ core (``lunaflux_b200._host.Channel``) is used when it is built; the
 class below is its reference implementation (same wire format, tested side
-by side).  ``MessageChannel`` carries pickled tuples over either.
+by side).  ``MessageChannel`` carries the rank-control frames of
+``worker_wire`` over either.
 """
 from __future__ import annotations
 
-import pickle
 import select
 import socket
 import struct
 import threading
 import time
 from typing import Optional
+
+from . import worker_wire
 
 MAGIC = 0x3143464C
 _HDR = struct.Struct("<IIQ")
@@ -167,21 +169,23 @@ TIMEOUT_ERRORS = _timeout_errors()
 
 
 class MessageChannel:
-    """Pickled-tuple messages over a framed channel.  ``recv`` returns None
-    on timeout and raises ``EOFError`` once the peer is gone or the framing
-    broke (the supervisor treats both as a lost rank)."""
+    """Rank-control messages (``engine/worker_wire.py`` binary frames) over a
+    framed channel.  ``recv`` returns None on timeout and raises ``EOFError``
+    once the peer is gone, the framing broke or a frame fails validation
+    (the supervisor treats all of them as a lost rank)."""
 
     def __init__(self, sock: socket.socket, send_timeout_s: float = 30.0, native: Optional[bool] = None):
         self._sock = sock  # keeps the descriptor's origin alive until close()
         self._ch = open_channel(sock.fileno(), native=native)
         self.send_timeout_s = send_timeout_s
+        self.generation = 0
 
     def fileno(self) -> int:
         return self._ch.fileno()
 
     def send(self, msg) -> None:
         try:
-            self._ch.send(pickle.dumps(msg, protocol=pickle.HIGHEST_PROTOCOL), self.send_timeout_s)
+            self._ch.send(worker_wire.encode(msg, self.generation), self.send_timeout_s)
         except CLOSED_ERRORS + TIMEOUT_ERRORS as e:
             raise BrokenPipeError(str(e)) from None
 
@@ -190,7 +194,15 @@ class MessageChannel:
             data = self._ch.recv(timeout_s)
         except CLOSED_ERRORS + TIMEOUT_ERRORS as e:
             raise EOFError(str(e)) from None
-        return None if data is None else pickle.loads(data)
+        if data is None:
+            return None
+        try:
+            msg, generation = worker_wire.decode_with_generation(data)
+        except worker_wire.WireError as e:
+            raise EOFError(str(e)) from None
+        if generation != self.generation:
+            raise EOFError(f"frame of generation {generation} on a generation {self.generation} channel")
+        return msg
 
     def close(self):
         self._ch.close()

@@ -49,6 +49,7 @@ def _rank_main(rank: int, world: int, port: int, factory: Callable, sock, heartb
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), LUNAFLUX_GENERATION=str(generation))
     conn = MessageChannel(sock)
+    conn.generation = generation
     stop = threading.Event()
 
     def send(msg):
@@ -141,7 +142,9 @@ class Supervisor:
             p.start()
             child.close()
             self.procs.append(p)
-            self.conns.append(MessageChannel(parent))
+            conn = MessageChannel(parent)
+            conn.generation = self.generation    # frames of another generation are rejected
+            self.conns.append(conn)
         now = time.monotonic()
         self.last_beat = {r: now for r in range(self.world)}
         self.ready = set()  # heartbeats are checked once a rank has finished starting
