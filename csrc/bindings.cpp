@@ -679,6 +679,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("max_q_len"), py::arg("progress") = 0);
   m.def("read_error", &read_error, py::arg("clear") = true);
   m.def("inject_error", &inject_error);
+  m.def("set_wait_limit_ns", [](int64_t ns) {
+    LF_CHECK(ns > 0, "set_wait_limit_ns: the limit must be positive");
+    lf::rt::set_wait_limit_ns((unsigned long long)ns);
+  });
   // programmatic dependent launch of the step kernels (off by default; LUNAFLUX_PDL=1)
   m.def("set_pdl", [](bool on) { lf::rt::set_pdl(on); });
   m.def("pdl_enabled", []() { return lf::rt::pdl_enabled(); });

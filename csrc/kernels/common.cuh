@@ -38,12 +38,18 @@ enum ErrorCode : int {
 // `lf::rt::read_error` folds all of them.
 static __device__ int lf_device_error = 0;
 static __device__ unsigned long long lf_device_error_info = 0;
+// Wall-clock limit of every bounded wait in this translation unit's kernels
+// (nanoseconds; default one second).  The host sets every unit's copy on the
+// current device with lf::rt::set_wait_limit_ns (tests shorten it to make a
+// wait run out quickly).
+static __device__ unsigned long long lf_wait_limit_ns = 1000000000ull;
 
 namespace lf {
 namespace rt {
 using ErrReadFn = int (*)(bool clear, unsigned long long* info);
 using ErrInjectFn = void (*)(int code);
-void register_error_word(ErrReadFn read, ErrInjectFn inject);
+using WaitLimitFn = void (*)(unsigned long long ns);
+void register_error_word(ErrReadFn read, ErrInjectFn inject, WaitLimitFn wait_limit);
 bool pdl_enabled();
 }  // namespace rt
 [[noreturn]] void launch_failed(cudaError_t e);  // throws std::runtime_error
@@ -63,8 +69,11 @@ int lf_tu_read_error(bool clear, unsigned long long* info) {
   return code;
 }
 void lf_tu_inject_error(int code) { cudaMemcpyToSymbol(lf_device_error, &code, sizeof(int)); }
+void lf_tu_set_wait_limit(unsigned long long ns) { cudaMemcpyToSymbol(lf_wait_limit_ns, &ns, sizeof(ns)); }
 struct LfErrorWordRegistration {
-  LfErrorWordRegistration() { lf::rt::register_error_word(&lf_tu_read_error, &lf_tu_inject_error); }
+  LfErrorWordRegistration() {
+    lf::rt::register_error_word(&lf_tu_read_error, &lf_tu_inject_error, &lf_tu_set_wait_limit);
+  }
 };
 static LfErrorWordRegistration lf_error_word_registration;
 }  // namespace
@@ -87,10 +96,13 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Wall-clock limit for any single wait inside a kernel.  One second is far
-// beyond any legitimate wait in these kernels (all of them finish in
-// milliseconds) and short enough that a broken pipeline returns promptly.
-constexpr uint64_t kWaitLimitNs = 1000000000ull;
+// Wall-clock limit for any single wait inside a kernel.  The default of one
+// second is far beyond any legitimate wait in these kernels (all of them
+// finish in milliseconds) and short enough that a broken pipeline returns
+// promptly; read from device memory so the host can change it.
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+  return *reinterpret_cast<volatile unsigned long long*>(&lf_wait_limit_ns);
+}
 
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch.  A kernel launched by `launch_k()` with PDL on
@@ -155,7 +167,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for `parity` to complete on `bar`.  Returns false (and records
-// kErrMbarTimeout) if the wait exceeds kWaitLimitNs, or if another thread
+// kErrMbarTimeout) if the wait exceeds the wait limit, or if another thread
 // already recorded an error, so callers can unwind.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t where = 0) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -165,7 +177,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 255u) == 0) {
       if (error_pending()) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > wait_limit_ns()) {
         set_error(kErrMbarTimeout, (unsigned long long)where);
         return false;
       }

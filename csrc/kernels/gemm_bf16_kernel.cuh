@@ -63,7 +63,7 @@ __device__ __forceinline__ bool ar_wait(const ArArgs& ar, int idx, int target) {
     while (ld_acquire_sys(c) < target) {
       if ((++spins & 63u) == 0) {
         if (error_pending()) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > wait_limit_ns()) {
           set_error(kErrPeerTimeout, (unsigned long long)idx);
           return false;
         }
@@ -984,7 +984,7 @@ __device__ __forceinline__ bool grid_rank_barrier(const ArArgs& ar, int xidx) {
       const uint64_t t0 = globaltimer_ns();
       uint32_t spins = 0;
       while (ld_acquire_gpu(gen) == g) {
-        if ((++spins & 63u) == 0 && (error_pending() || globaltimer_ns() - t0 > kWaitLimitNs)) {
+        if ((++spins & 63u) == 0 && (error_pending() || globaltimer_ns() - t0 > wait_limit_ns())) {
           if (!error_pending()) set_error(kErrPeerTimeout, (unsigned long long)xidx);
           ok = false;
           break;

@@ -36,7 +36,7 @@ __device__ __forceinline__ bool poll_word(const uint2* p, uint32_t ep, uint32_t*
     do {
       if ((++spins & 255u) == 0) {
         if (error_pending()) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > wait_limit_ns()) {
           set_error(kErrPeerTimeout, 0x11ull);
           return false;
         }

@@ -64,7 +64,7 @@ __device__ int wait_word(const unsigned long long* p, uint32_t ep, unsigned long
     do {
       if ((++spins & 255u) == 0) {
         if (error_pending()) return -1;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > wait_limit_ns()) {
           set_error(kErrPeerTimeout, where);
           return -1;
         }

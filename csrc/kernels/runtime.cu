@@ -20,6 +20,7 @@ namespace {
 struct Hooks {
   ErrReadFn read;
   ErrInjectFn inject;
+  WaitLimitFn wait_limit;
 };
 std::vector<Hooks>& hooks() {
   static std::vector<Hooks> h;
@@ -31,9 +32,14 @@ std::mutex& hooks_mu() {
 }
 }  // namespace
 
-void register_error_word(ErrReadFn read, ErrInjectFn inject) {
+void register_error_word(ErrReadFn read, ErrInjectFn inject, WaitLimitFn wait_limit) {
   std::lock_guard<std::mutex> g(hooks_mu());
-  hooks().push_back({read, inject});
+  hooks().push_back({read, inject, wait_limit});
+}
+
+void set_wait_limit_ns(unsigned long long ns) {
+  std::lock_guard<std::mutex> g(hooks_mu());
+  for (auto& h : hooks()) h.wait_limit(ns);
 }
 
 ErrorState read_error(cudaStream_t s, bool clear) {

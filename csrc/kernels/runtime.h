@@ -9,6 +9,9 @@ struct ErrorState {
 };
 ErrorState read_error(cudaStream_t s, bool clear);
 void inject_error(int code);
+// Limit of every bounded wait in every kernel, on the current device
+// (nanoseconds; default 1e9).
+void set_wait_limit_ns(unsigned long long ns);
 // Programmatic dependent launch for the kernels of the step (off unless
 // LUNAFLUX_PDL=1 or set_pdl(true)).
 bool pdl_enabled();

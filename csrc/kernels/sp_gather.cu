@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(32) gather_wait_kernel(GatherArgs g) {
       while (ld_acquire_u64(p) < ep) {
         if ((++spins & 255u) == 0) {
           if (error_pending()) break;
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          if (globaltimer_ns() - t0 > wait_limit_ns()) {
             set_error(kErrPeerTimeout, 0x5A900ull + threadIdx.x);
             break;
           }

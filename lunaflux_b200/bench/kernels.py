@@ -163,8 +163,24 @@ def bench_attn(C, results):
         pl = torch.empty(rows * Hq * splits, device="cuda")
         ms = time_fn(lambda: C.attn_decode(q, out, tok, sl, bt, kc, vc, Hq, Hkv, splits, po, pl))
         kv_bytes = rows * L * Hkv * D * 2 * 2
+        # every split count the model could pick, timed the same way (checks the cost model)
+        sweep = {}
+        for s_ in (1, 2, 3, 4, 6, 8):
+            if s_ > 1 and math.ceil(L / P) // s_ < 8:
+                break
+            po_ = torch.empty(rows * Hq * s_ * D, device="cuda")
+            pl_ = torch.empty(rows * Hq * s_, device="cuda")
+            sweep[s_] = time_fn(lambda: C.attn_decode(q, out, tok, sl, bt, kc, vc, Hq, Hkv, s_, po_, pl_))
+        lib_ms = None
+        try:   # vLLM's paged flash-attention on the same cache (the library baseline's kernel)
+            from lunaflux_b200.ops.library_ops import LibraryOps
+            lib = LibraryOps("cuda")
+            lib_ms = time_fn(lambda: lib.attn_decode(q, out, tok, sl, bt, kc, vc, Hq, Hkv, 1, po, pl))
+        except Exception:
+            pass
         r = dict(kernel="attn_decode", rows=rows, seq=L, Hq=Hq, Hkv=Hkv, splits=splits, ours_ms=ms,
-                 gbs=kv_bytes / ms / 1e6, frac_of_hbm=kv_bytes / ms / 1e6 / hbm, peaks=src)
+                 gbs=kv_bytes / ms / 1e6, frac_of_hbm=kv_bytes / ms / 1e6 / hbm, peaks=src,
+                 split_sweep_ms=sweep, library_ms=lib_ms)
         results.append(r)
         print(json.dumps(r))
     # prefill: 8 prompts x 1024 tokens, causal

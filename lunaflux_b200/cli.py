@@ -10,7 +10,8 @@ same argument order) and cmd/lunaflux_plan/plan.mbt:1-80; ``serve``,
     lunaflux reference ROOT CONFIG_REL TOKENIZER_REL WEIGHTS_REL CONFIG_SHA TOKENIZER_SHA WEIGHTS_SHA MAX_NEW TOKEN_IDS
     lunaflux version
     lunaflux serve [--config FILE | --preset NAME | --model-dir DIR] [--host H] [--port P] [--http-port P]
-                   [--metrics-port P] [--layers N]   (under torchrun: tensor parallel, rank 0 serves)
+                   [--metrics-port P] [--layers N] [--tp N]
+                   (--tp N: supervised rank processes; under torchrun: tensor parallel, rank 0 serves)
     lunaflux bench [bench.py arguments]
     lunaflux inspect-kernels
 """
@@ -38,7 +39,8 @@ def usage() -> str:
         "MAX_NEW TOKEN_IDS",
         "  lunaflux version",
         "  lunaflux serve [--config FILE | --preset NAME | --model-dir DIR] [--host H] [--port P] [--http-port P]",
-        "                 [--metrics-port P] [--layers N]   (under torchrun: tensor parallel, rank 0 serves)",
+        "                 [--metrics-port P] [--layers N] [--tp N]",
+        "                 (--tp N: supervised rank processes; under torchrun: tensor parallel, rank 0 serves)",
         "  lunaflux bench [bench.py arguments]",
         "  lunaflux inspect-kernels",
     ])
@@ -217,20 +219,8 @@ def inspect_kernels(out=print):
     return names
 
 
-def serve(args: List[str]):
+def _serve_parser():
     import argparse
-    import asyncio
-
-    import torch
-
-    from .config import CacheConfig, SchedulerConfig, parse_document
-    from .contracts import default_limits
-    from .engine.engine import EngineOptions, LLMEngine
-    from .models import spec as specs
-    from .models.weights import build_runtime, random_source
-    from .ops import KernelOps, TorchOps
-    from .service.server import EngineService, MetricsServer, TCPServer
-    from .tokenizer.bpe import Tokenizer, synthetic_byte_tokenizer
     ap = argparse.ArgumentParser(prog="lunaflux serve")
     ap.add_argument("--config", default="")
     ap.add_argument("--preset", default="tiny-llama")
@@ -246,7 +236,19 @@ def serve(args: List[str]):
                     help="synchronous steps (default: the next step is planned and launched while one runs)")
     ap.add_argument("--model-dir", default="",
                     help="Hugging Face style directory: config.json, safetensors weights (index or single), tokenizer.json")
-    a = ap.parse_args(args)
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor parallel over this many GPUs as supervised rank processes: the serving process "
+                         "holds no GPU state and survives a lost rank (its active requests fail retryably, "
+                         "waiting ones run in the next generation)")
+    return ap
+
+
+def _serve_model(a):
+    """(spec, preset, scheduler config, cache config, checkpoint dir or None) of the serve arguments."""
+    import torch
+
+    from .config import CacheConfig, SchedulerConfig, parse_document
+    from .models import spec as specs
     sched, cache = SchedulerConfig(), CacheConfig()
     preset = a.preset
     if a.config:
@@ -256,15 +258,6 @@ def serve(args: List[str]):
         preset = cfg.model.preset or preset
         a.host, a.port = cfg.service.listen_host, cfg.service.listen_port
     cuda = torch.cuda.is_available()
-    from .parallel.comm import env_rank_world, init_distributed
-    rank, world, local = env_rank_world()
-    dev = torch.device("cuda", local) if cuda else torch.device("cpu")
-    ctrl = None
-    if world > 1:
-        # tensor parallel: one process per GPU (under torchrun); rank 0 serves
-        if cuda:
-            torch.cuda.set_device(local)
-        ctrl = init_distributed("nccl" if cuda else "gloo", device_id=local if cuda else None)
     ckpt = None
     if a.model_dir:
         from .models.checkpoint import CheckpointDir
@@ -277,6 +270,21 @@ def serve(args: List[str]):
             spec = spec.with_layers(a.layers)
         if not cuda:
             spec = specs.LlamaSpec(**{**spec.__dict__, "dtype": "fp32"})
+    return spec, preset, sched, cache, ckpt
+
+
+def _build_engine(a, rank: int, world: int, local: int, clock):
+    """This rank's engine for the serve arguments (weights sharded over
+    `world` ranks), its decode graphs captured.  Returns (engine, checkpoint
+    dir or None, spec, preset)."""
+    import torch
+
+    from .engine.engine import EngineOptions, LLMEngine
+    from .models.weights import build_runtime, random_source
+    from .ops import KernelOps, TorchOps
+    spec, preset, sched, cache, ckpt = _serve_model(a)
+    cuda = torch.cuda.is_available()
+    dev = torch.device("cuda", local) if cuda else torch.device("cpu")
     from .models.admission import admit
     adm = admit(spec, max_context=a.max_context, max_batch=sched.max_active_requests,
                 step_tokens=sched.step_token_budget,
@@ -296,27 +304,89 @@ def serve(args: List[str]):
             comm = FusedTPComm(sched.step_token_budget + sched.max_active_requests, spec.hidden, dev)
         else:
             comm = TPComm()
-    tok_from_dir = None
-    chat_template, eos_ids = None, []
-    if ckpt is not None:
-        if not a.tokenizer:
-            tok_from_dir = ckpt.tokenizer()
-        chat_template, eos_ids = ckpt.chat()
-        ckpt.close()
-    from .service.spmd import SharedClock, SpmdLeader, follower_loop
-    # every rank's scheduler sees the leader's clock (deadlines expire in lock step)
-    clock = SharedClock() if world > 1 else time.monotonic
     eng = LLMEngine(w, KernelOps() if cuda else TorchOps(), dev, sched, cache,
                     EngineOptions(max_context=a.max_context, graph_sizes=EngineOptions().graph_sizes if cuda else (),
                                   overlap_steps=not a.no_overlap), comm=comm, clock=clock)
     if cuda:
         # capture the decode graphs now (every rank, same order), not on the first requests
         eng.runner.capture_all(False)
-    if world > 1 and rank != 0:
-        follower_loop(eng, clock, ctrl)
-        return
-    if world > 1:
-        eng = SpmdLeader(eng, clock, ctrl)
+    return eng, ckpt, spec, preset
+
+
+def serve_rank_factory(args: List[str], rank: int, world: int):
+    """A supervised rank of ``lunaflux serve --tp N``: joins the rank group
+    (the supervisor set MASTER_ADDR / MASTER_PORT / RANK / WORLD_SIZE) and
+    builds its engine shard.  The engine's clock is the supervisor's, carried
+    by every step command, so all ranks' schedulers see the same time."""
+    import torch
+
+    from .parallel.comm import init_distributed
+    from .service.spmd import SharedClock
+    a = _serve_parser().parse_args(args)
+    cuda = torch.cuda.is_available()
+    if cuda:
+        torch.cuda.set_device(rank)
+    init_distributed("nccl" if cuda else "gloo", device_id=rank if cuda else None)
+    clock = SharedClock()
+    eng, ckpt, _, _ = _build_engine(a, rank, world, rank, clock)
+    if ckpt is not None:
+        ckpt.close()
+    eng.shared_clock = clock
+    return eng
+
+
+def serve(args: List[str]):
+    import asyncio
+    import functools
+
+    import torch
+
+    from .contracts import default_limits
+    from .service.server import EngineService, MetricsServer, TCPServer
+    from .tokenizer.bpe import Tokenizer, synthetic_byte_tokenizer
+    a = _serve_parser().parse_args(args)
+    cuda = torch.cuda.is_available()
+    from .parallel.comm import env_rank_world, init_distributed
+    rank, world, local = env_rank_world()
+    if a.tp > 1 and world > 1:
+        raise CliError("--tp starts its own rank processes: do not combine it with torchrun")
+    ctrl = None
+    tok_from_dir = None
+    chat_template, eos_ids = None, []
+    if a.tp > 1:
+        # supervised ranks: this process serves and supervises, the ranks hold the GPUs
+        from .engine.engine import EngineOptions
+        from .engine.supervised import SupervisedEngine
+        from .engine.supervisor import Supervisor
+        spec, preset, _, _, ckpt = _serve_model(a)
+        if ckpt is not None:
+            if not a.tokenizer:
+                tok_from_dir = ckpt.tokenizer()
+            chat_template, eos_ids = ckpt.chat()
+            ckpt.close()
+        sup = Supervisor(a.tp, functools.partial(serve_rank_factory, list(args)), step_timeout_s=600.0)
+        sup.start()
+        eng = SupervisedEngine(sup, spec, EngineOptions(max_context=a.max_context), time.monotonic)
+    else:
+        if world > 1:
+            # tensor parallel: one process per GPU (under torchrun); rank 0 serves
+            if cuda:
+                torch.cuda.set_device(local)
+            ctrl = init_distributed("nccl" if cuda else "gloo", device_id=local if cuda else None)
+        from .service.spmd import SharedClock, SpmdLeader, follower_loop
+        # every rank's scheduler sees the leader's clock (deadlines expire in lock step)
+        clock = SharedClock() if world > 1 else time.monotonic
+        eng, ckpt, spec, preset = _build_engine(a, rank, world, local, clock)
+        if ckpt is not None:
+            if not a.tokenizer:
+                tok_from_dir = ckpt.tokenizer()
+            chat_template, eos_ids = ckpt.chat()
+            ckpt.close()
+        if world > 1 and rank != 0:
+            follower_loop(eng, clock, ctrl)
+            return
+        if world > 1:
+            eng = SpmdLeader(eng, clock, ctrl)
     tok = Tokenizer.from_file(a.tokenizer) if a.tokenizer else (tok_from_dir or synthetic_byte_tokenizer())
     svc = EngineService(eng, tok, default_limits(spec.vocab, a.max_context))
     svc.start()
@@ -339,7 +409,9 @@ def serve(args: List[str]):
         asyncio.run(main())
     finally:
         svc.stop()
-        if world > 1:
+        if a.tp > 1:
+            eng.close()
+        elif world > 1:
             eng.shutdown()
 
 

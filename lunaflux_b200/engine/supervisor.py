@@ -78,6 +78,9 @@ def _rank_main(rank: int, world: int, port: int, factory: Callable, sock, heartb
             elif kind == "cancel":
                 engine.cancel(msg[1])
             elif kind == "step":
+                shared = getattr(engine, "shared_clock", None)
+                if shared is not None:
+                    shared.now = msg[1]    # every rank's scheduler sees the supervisor's clock
                 outs = engine.step()
                 done = [(rid, r.reason.name if r.reason else None, r.error.name if r.error else None)
                         for rid, r in list(engine.results.items())]
@@ -129,6 +132,9 @@ class Supervisor:
         self.reqs: Dict[int, _Req] = {}
         self.failures = 0
         self.ready = set()
+        self.last_outs: List = []      # rank 0's (rid, token, finished) of the last step
+        self.last_done: List = []      # rank 0's (rid, reason, error) terminals of the last step
+        self.last_failed: List[int] = []   # requests failed by the last recovery
 
     # ------------------------------------------------------------------ lifecycle
     def start(self):
@@ -235,7 +241,7 @@ class Supervisor:
         A lost rank triggers recovery and returns True (the new generation
         continues with the surviving requests)."""
         try:
-            self._send_all(("step",))
+            self._send_all(("step", time.monotonic()))
             replies = {}
             deadline = time.monotonic() + self.step_timeout_s
             while len(replies) < self.world:
@@ -243,9 +249,11 @@ class Supervisor:
                     if msg[0] == "outs":
                         replies[r] = msg
         except WorkerLost:
+            self.last_outs, self.last_done = [], []
             self._recover()
             return True
         _, _, outs, done, more = replies[0]
+        self.last_outs, self.last_done = outs, done
         for rid, tok, _fin in outs:
             if rid in self.reqs:
                 self.reqs[rid].tokens.append(tok)
@@ -261,9 +269,11 @@ class Supervisor:
         tokens, keep the rest, start the next generation."""
         self.failures += 1
         self._reap()
+        self.last_failed = []
         for q in self.reqs.values():
             if not q.done and q.tokens:
                 q.done, q.error = True, PublicErrorCode.WORKER_UNAVAILABLE
+                self.last_failed.append(q.rid)
         self.start()
 
     def run_until_done(self, max_steps: int = 100000):

@@ -55,7 +55,7 @@ class Kind(enum.IntEnum):
     HEARTBEAT = 2    # rank -> supervisor: liveness
     ADD = 3          # supervisor -> rank: admit a request
     CANCEL = 4       # supervisor -> rank: cancel a request
-    STEP = 5         # supervisor -> rank: run one engine iteration
+    STEP = 5         # supervisor -> rank: run one engine iteration at the supervisor's clock
     CLOSE = 6        # supervisor -> rank: leave
     OUTPUTS = 7      # rank -> supervisor: one iteration's tokens and terminals
     ERROR = 8        # rank -> supervisor: the rank failed (traceback text)
@@ -212,7 +212,9 @@ def encode(msg: Tuple, generation: int = 0) -> bytes:
         w.i32s(stop_ids or (), MAX_STOP_IDS)
     elif kind is Kind.CANCEL:
         w.u64(_nonneg(msg[1], "rid"))
-    elif kind in (Kind.STEP, Kind.CLOSE):
+    elif kind is Kind.STEP:
+        w.f64(float(msg[1]))
+    elif kind is Kind.CLOSE:
         pass
     elif kind is Kind.OUTPUTS:
         _, rank, outs, done, has_work = msg
@@ -273,7 +275,9 @@ def decode_with_generation(frame) -> Tuple[Tuple, int]:
         msg = (name, rid, prompt, max_new, sampling, stop_ids)
     elif kind is Kind.CANCEL:
         msg = (name, r.u64())
-    elif kind in (Kind.STEP, Kind.CLOSE):
+    elif kind is Kind.STEP:
+        msg = (name, r.f64())
+    elif kind is Kind.CLOSE:
         msg = (name,)
     elif kind is Kind.OUTPUTS:
         rank = r.u32()

@@ -496,3 +496,42 @@ def test_sample_from_shard_candidates_equals_full_row(C, ranks):
     C.sample_keys(keys, R, ranks, kc, params, got)
     torch.cuda.synchronize()
     assert torch.equal(got, full)
+
+
+def test_peer_wait_runs_out_and_the_step_fails(C):
+    """A bounded wait on another rank's words that never arrive: the
+    low-latency all-reduce is launched as rank 0 of a group of 2 on one GPU,
+    with rank 1's inboxes in local memory that nothing writes.  With the wait
+    limit shortened to 50 ms the kernel returns on its own, records
+    kErrPeerTimeout, the context stays usable and the runner's error check
+    raises StepFailed."""
+    import time
+    import types
+    from lunaflux_b200.engine.runner import ModelRunner, StepFailed
+    from lunaflux_b200.ops import KernelOps
+    M, N = 4, 256
+    pairs = M * N // 2
+    words = lambda n: torch.zeros(n, 2, dtype=torch.int32, device="cuda")  # noqa: E731 (uint2 words)
+    rs = [words(2 * pairs), words(2 * pairs)]
+    ag = [words(pairs), words(pairs)]
+    state = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ws = torch.randn(M * N, device="cuda")
+    D = torch.zeros(M, N, dtype=torch.bfloat16, device="cuda")
+    C.read_error(True)
+    C.set_wait_limit_ns(50_000_000)
+    try:
+        t0 = time.perf_counter()
+        C.partials_allreduce_ll(ws, 1, D, [t.data_ptr() for t in rs], [t.data_ptr() for t in ag], 0, state, 0, pairs)
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - t0
+    finally:
+        C.set_wait_limit_ns(1_000_000_000)
+    assert elapsed < 5.0, elapsed
+    runner = types.SimpleNamespace(ops=KernelOps())
+    with pytest.raises(StepFailed) as e:
+        ModelRunner.check_device_errors(runner)
+    assert e.value.code == 2          # kErrPeerTimeout
+    # the context is still usable
+    x = torch.ones(1024, device="cuda")
+    assert float(x.sum()) == 1024.0
+    assert C.read_error(True)[0] == 0

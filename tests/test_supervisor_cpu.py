@@ -104,3 +104,78 @@ def test_supervised_tp_ranks(fault, monkeypatch):
         assert sup.reqs[rid].error is PublicErrorCode.WORKER_UNAVAILABLE
     for rid in (3, 4):
         assert sup.reqs[rid].error is None and sup.reqs[rid].tokens == expect[rid - 1]
+
+
+def test_service_over_supervised_ranks_survives_a_lost_rank(monkeypatch):
+    """The serving path on supervised rank processes: rank 1 exits in its
+    third step.  The service keeps running; the requests that were producing
+    tokens fail with the retryable worker_unavailable code, the ones still
+    waiting complete in the next generation with the oracle's tokens, and a
+    request submitted after the recovery completes too."""
+    import threading
+    import time
+
+    from lunaflux_b200.contracts import GenerateRequest
+    from lunaflux_b200.engine.engine import EngineOptions
+    from lunaflux_b200.engine.supervised import SupervisedEngine
+    from lunaflux_b200.contracts import CompletedEvent, FailedEvent, TokenEvent
+    from lunaflux_b200.service.server import EngineService
+    from lunaflux_b200.contracts import default_limits
+
+    monkeypatch.setenv("LF_TEST_FAULT", "exit")
+    sup = Supervisor(2, tiny_factory, heartbeat_s=0.1, dead_after_s=2.0, step_timeout_s=60.0)
+    sup.start()
+    eng = SupervisedEngine(sup, _spec(), EngineOptions(max_context=256), time.monotonic)
+    svc = EngineService(eng, None, default_limits(256, 256))
+    events = {}
+    done = {}
+    lock = threading.Lock()
+
+    def sink_for(rid):
+        def sink(ev):
+            with lock:
+                events.setdefault(rid, []).append(ev)
+                if isinstance(ev, (CompletedEvent, FailedEvent)):
+                    done[rid] = ev
+        return sink
+
+    def wait_for(rids, timeout=120.0):
+        t0 = time.monotonic()
+        while time.monotonic() - t0 < timeout:
+            with lock:
+                if all(r in done for r in rids):
+                    return
+            time.sleep(0.02)
+        raise AssertionError(f"requests {rids} did not finish: {sorted(done)}")
+
+    svc.start()
+    try:
+        for rid in (1, 2):
+            svc.submit(GenerateRequest(request_id=rid, input_tokens=tuple(PROMPTS[rid - 1]), max_new_tokens=6),
+                       sink_for(rid))
+        # the first two produce tokens before the fault; the next two wait until then
+        t0 = time.monotonic()
+        while time.monotonic() - t0 < 60:
+            with lock:
+                if all(any(isinstance(e, TokenEvent) for e in events.get(r, [])) for r in (1, 2)):
+                    break
+            time.sleep(0.01)
+        for rid in (3, 4):
+            svc.submit(GenerateRequest(request_id=rid, input_tokens=tuple(PROMPTS[rid - 1]), max_new_tokens=6),
+                       sink_for(rid))
+        wait_for([1, 2, 3, 4])
+        svc.submit(GenerateRequest(request_id=5, input_tokens=tuple(PROMPTS[0]), max_new_tokens=6), sink_for(5))
+        wait_for([5])
+        assert svc.alive()
+    finally:
+        svc.stop()
+        eng.close()
+    expect = _expect(PROMPTS, 6)
+    assert sup.failures == 1 and sup.generation == 2
+    for rid in (1, 2):
+        ev = done[rid]
+        assert isinstance(ev, FailedEvent) and ev.code is PublicErrorCode.WORKER_UNAVAILABLE and ev.retryable, ev
+    for rid, want in ((3, expect[2]), (4, expect[3]), (5, expect[0])):
+        assert isinstance(done[rid], CompletedEvent), done[rid]
+        toks = [e.token_id for e in events[rid] if isinstance(e, TokenEvent)]
+        assert toks == want, (rid, toks, want)

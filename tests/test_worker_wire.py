@@ -16,7 +16,7 @@ MESSAGES = [
     ("add", 2**40, list(range(1000)), 1, SamplingParameters(SamplingMode.SAMPLE, 0.7, 40, 0.9, 99), (5, 6)),
     ("add", 0, [], 0, SamplingParameters(SamplingMode.SAMPLE, 1.0, None, None, 1), ()),
     ("cancel", 11),
-    ("step",),
+    ("step", 1234.5),
     ("close",),
     ("outs", 0, [(1, 42, False), (2, 7, True)], [(2, "TOKEN_LIMIT", None), (9, None, "WORKER_UNAVAILABLE")], True),
     ("outs", 5, [], [], False),
@@ -53,7 +53,7 @@ def test_trailing_bytes_are_rejected(msg):
 
 
 def test_header_corruptions():
-    frame = bytearray(ww.encode(("step",)))
+    frame = bytearray(ww.encode(("close",)))
     bad = bytearray(frame)
     bad[0] ^= 1
     assert _issue(bytes(bad)) is ww.WireIssue.BAD_MAGIC
@@ -111,10 +111,10 @@ def test_channel_rejects_a_stale_generation():
     a, b = socket.socketpair()
     ca, cb = MessageChannel(a), MessageChannel(b)
     ca.generation, cb.generation = 2, 2
-    ca.send(("step",))
-    assert cb.recv(5.0) == ("step",)
+    ca.send(("step", 1.0))
+    assert cb.recv(5.0) == ("step", 1.0)
     ca.generation = 1
-    ca.send(("step",))
+    ca.send(("step", 2.0))
     with pytest.raises(EOFError):
         cb.recv(5.0)
     ca.close()
