@@ -529,30 +529,22 @@ static int decode_ctas_per_sm() {
   return n;
 }
 
-// Split-KV count.  Each (row, head, split) is one CTA and all of them take
-// about the same time, so the grid runs in waves of num_sms x ctas_per_sm:
-// the cost model is waves x (pages per split + a fixed per-CTA start-up of
-// about 3 page times) + the combine pass (about one page time per split),
-// minimised over 1..32 splits with at least 8 pages per split.  For 256 rows
-// x 8 heads x 72 pages on 148 SMs this picks 3 splits (7 full waves) over 1
-// split (2.3 waves, the last one a third full).
+// Split-KV count: the fewest splits that give about half of the resident CTA
+// slots (num_sms x ctas_per_sm) work, with at least 8 pages per split and at
+// most 32 splits.  Measured on B200 (one warp per CTA, 6 per SM): 256 rows x
+// 8 heads x 72 pages and 64 x 8 x 128 run fastest unsplit (2048 and 512
+// CTAs), 128 rows x 1 head x 144 pages with 4 splits, 1 row x 8 heads x 256
+// pages with 16 or more; splitting a grid that already fills the slots only
+// adds the combine pass.
 int decode_splits(int rows, int Hkv, int max_seq, int num_sms) {
   const int units = rows * Hkv;
   const int pages = (max_seq + PAGE - 1) / PAGE;
   if (units <= 0 || pages <= 0) return 1;
-  const int64_t slots = (int64_t)num_sms * decode_ctas_per_sm();
-  int best = 1;
-  double best_cost = 1e30;
-  for (int s = 1; s <= 32; ++s) {
-    if (s > 1 && pages / s < 8) break;
-    const int64_t waves = ((int64_t)units * s + slots - 1) / slots;
-    const double cost = (double)waves * ((pages + s - 1) / s + 3) + (s > 1 ? s : 0);
-    if (cost < best_cost * 0.98) {  // prefer fewer splits unless clearly better
-      best_cost = cost;
-      best = s;
-    }
-  }
-  return best;
+  const int64_t half_slots = (int64_t)num_sms * decode_ctas_per_sm() / 2;
+  int s = (int)((half_slots + units - 1) / units);
+  if (s > 32) s = 32;
+  while (s > 1 && pages / s < 8) --s;
+  return s < 1 ? 1 : s;
 }
 
 void decode(const DecodeArgs& a_in, const void* kcache, const void* vcache, cudaStream_t stream) {

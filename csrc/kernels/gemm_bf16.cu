@@ -365,7 +365,7 @@ void run(const GemmArgs& a, int epi, int bn, cudaStream_t stream, float* ws, int
   if (a.M <= 0) return;
   (void)ws;
   (void)ws_elems;
-  if (bn == 0 && run_pair(a, epi, stream)) return;  // opt-in CTA-pair kernel for large GEMMs
+  if (bn == 0 && run_pair(a, epi, stream)) return;  // CTA-pair kernel for large GEMMs (LUNAFLUX_GEMM_2SM=0: off)
   if (bn == 0 && run_cluster(a, epi, a.D, a.ldd, stream)) return;
   if (bn == 0 && a.M > BM && a.M <= 2 * BM && a.N % 256 == 0 && a.K % 8 == 0) {
     // 129..256 rows (decode batches): 256-row tiles, each weight slab staged
@@ -499,6 +499,7 @@ void run_allreduce_ll(const GemmArgs& a, const ar::LLArgs& ll, cudaStream_t stre
 bool run_qkv_rope(const GemmArgs& a, const RopeArgs& rope, cudaStream_t stream) {
   if (a.M <= 0) return true;
   if (a.N != (rope.Hq + 2 * rope.Hkv) * 128 || a.K % 8 != 0) return false;
+  if (run_pair(a, kQkvRope, stream, rope)) return true;   // large (prefill) shapes on CTA pairs
   int bn = 0, kb_per = 0, mb = 1;
   const int c = plan_cluster(a.M, a.N, a.K, kStoreBf16, &bn, &kb_per, &mb);
   if (c >= 2 && mb == 1) {

@@ -109,8 +109,8 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                     void* __restrict__ out, int M, int N, int K, int ldd) {
-  static_assert(EPI == kStoreBf16 || EPI == kStoreF32 || EPI == kSwiGLU, "plain epilogues");
+                     void* __restrict__ out, int M, int N, int K, int ldd, const RopeArgs rope) {
+  static_assert(EPI == kStoreBf16 || EPI == kStoreF32 || EPI == kSwiGLU || EPI == kQkvRope, "plain or QKV epilogues");
   pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -216,7 +216,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = (tile / num_m) * kTileN;
       const int row = m0 + quad * 32 + lane;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * kTileN;
-      if constexpr (EPI == kSwiGLU) {
+      if constexpr (EPI == kQkvRope) {
+        // two whole heads per tile: RoPE on Q / K, K / V into the paged cache
+        qkv_rope_row<kTileN>(rope, taddr, row, M, n0, reinterpret_cast<__nv_bfloat16*>(out), ldd);
+      } else if constexpr (EPI == kSwiGLU) {
         const int o0 = n0 / 2;
 #pragma unroll 1
         for (int c = 0; c < kTileN / 2; c += 16) {
@@ -302,19 +305,21 @@ int get_gemm_pair() { return pair_enabled() ? 1 : 0; }  // declared in gemm_bf16
 
 // Launches the CTA-pair kernel for large GEMMs (enough 256 x 256 tiles to fill
 // the SMs) when it is enabled; returns false otherwise.
-static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream) {
+static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream, const RopeArgs& rope = RopeArgs{}) {
   if (!pair_enabled()) return false;
   if (a.M <= 0 || a.N % pair::kTileN != 0 || a.K % 8 != 0) return false;
-  if (epi != kStoreBf16 && epi != kStoreF32 && epi != kSwiGLU) return false;
+  if (epi != kStoreBf16 && epi != kStoreF32 && epi != kSwiGLU && epi != kQkvRope) return false;
   const int sms = num_sms();
   const int tiles = ((a.M + pair::kTileM - 1) / pair::kTileM) * (a.N / pair::kTileN);
   if (tiles < sms / 2) return false;  // skinny shapes keep the split-K kernels
-  auto kfn = epi == kSwiGLU ? pair::gemm_pair_kernel<kSwiGLU>
-                            : (epi == kStoreF32 ? pair::gemm_pair_kernel<kStoreF32> : pair::gemm_pair_kernel<kStoreBf16>);
-  static bool attr_set[3] = {false, false, false};
-  if (!attr_set[epi]) {
+  const int slot = epi == kQkvRope ? 3 : epi;
+  auto kfn = epi == kQkvRope ? pair::gemm_pair_kernel<kQkvRope>
+             : epi == kSwiGLU ? pair::gemm_pair_kernel<kSwiGLU>
+             : (epi == kStoreF32 ? pair::gemm_pair_kernel<kStoreF32> : pair::gemm_pair_kernel<kStoreBf16>);
+  static bool attr_set[4] = {false, false, false, false};
+  if (!attr_set[slot]) {
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::kSmem);
-    attr_set[epi] = true;
+    attr_set[slot] = true;
   }
   static int max_pairs = 0;
   if (max_pairs == 0) {
@@ -340,7 +345,8 @@ static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream) {
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
   CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
   CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, pair::kTileN / 2);
-  launch_k(kfn, dim3(2 * pairs), dim3(kThreads), pair::kSmem, stream, 2u, ta, tb, a.D, a.M, a.N, a.K, (int)a.ldd);
+  launch_k(kfn, dim3(2 * pairs), dim3(kThreads), pair::kSmem, stream, 2u, ta, tb, a.D, a.M, a.N, a.K, (int)a.ldd,
+           rope);
   return true;
 }
 

@@ -87,6 +87,12 @@ def main():
     st = W.run(eng, wl, comm, realtime=not a.no_realtime)
     torch.cuda.synchronize()
     dev_ms = eng.runner.device_ms - dev_ms0
+    # every request has ended (finished or cancelled): once the prefix cache
+    # gives its pages back, no page may still be allocated
+    sched_ = eng.scheduler
+    if getattr(sched_, "prefix", None) is not None:
+        sched_.prefix.evict(1 << 30)
+    leaked = sched_.allocator.allocated_page_count()
     if world > 1:
         t = torch.tensor([dev_ms, st.wall_s], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -95,7 +101,7 @@ def main():
             "parallelism": f"tp{world}" + (f"+ep{ep}" if ep > 1 else ""), "comm": a.comm if world > 1 else "none",
             "requests": len(wl.items), "scaled": a.scale < 1.0 or bool(a.layers),
             "output_tok_per_s_device": round(st.tokens / (dev_ms / 1e3), 1) if dev_ms else None,
-            "output_tok_per_s_wall": round(st.tokens / st.wall_s, 1), **st.summary(), "load_s": round(load_s, 1),
+            "output_tok_per_s_wall": round(st.tokens / st.wall_s, 1), **st.summary(), "load_s": round(load_s, 1), "leaked_pages": leaked,
             "data": "synthetic (seeded), random-init weights"}
     if rank == 0:
         print(json.dumps(line), flush=True)
