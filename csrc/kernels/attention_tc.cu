@@ -14,7 +14,10 @@
 //   S_j  = Q . K_j^T          tcgen05.mma, Q and K_j K-major in shared memory,
 //                             S in TMEM (double-buffered, so S_{j+1} is
 //                             computed while the softmax works on S_j)
-//   P_j  = exp2(S_j - m)      4 softmax warps, one TMEM lane (row) per thread;
+//   P_j  = exp2(S_j - m)      8 softmax warps, two per TMEM lane quadrant: a
+//                             row (TMEM lane) is shared by two threads, each
+//                             taking 64 of its 128 scores; the halves swap
+//                             their partial maxima through shared memory.
 //                             P written to shared memory (bf16, 128-byte
 //                             swizzle, double-buffered, so the softmax of
 //                             block j+1 overlaps the P.V MMA of block j)
@@ -27,9 +30,11 @@
 // Between such events P may exceed 1 by at most 2^8, well inside fp32 and
 // bf16 range; the final O / l is unchanged.
 //
-// Warp roles (192 threads): warp 0 lane 0 issues the TMA loads (Q once, then
+// Warp roles (320 threads): warp 0 lane 0 issues the TMA loads (Q once, then
 // K and V pages of each block into a 2-stage ring), warp 1 owns TMEM and its
-// lane 0 issues the MMAs, warps 2..5 run the softmax and the epilogue.  All
+// lane 0 issues the MMAs, warps 2..9 run the softmax and the epilogue (warps
+// w and w + 4 share the TMEM lanes of quadrant w % 4: columns 0..63 and
+// 64..127 of S, P and O).  All
 // waits are bounded (common.cuh); every TMA load fills only its own CTA.
 // Block-table entries are bounds-checked (kErrBadIndex, zero page instead).
 #include <cuda.h>
@@ -61,7 +66,10 @@ constexpr int kOffK = kTile;
 constexpr int kOffV = 3 * kTile;
 constexpr int kOffP = 5 * kTile;
 constexpr int kOffBar = 7 * kTile;
-constexpr int kSmem = 7 * kTile + 256 + 1024;
+constexpr int kOffRed = kOffBar + 256;     // [2 halves][128 rows] fp32: partial row maxima / sums
+constexpr int kOffFlag = kOffRed + 1024;   // [2 halves][4 quadrants] int: the warp's pipeline is sound
+constexpr int kSmem = 7 * kTile + 256 + 1024 + 1024 + 64;
+constexpr int kThreadsTc = 320;
 constexpr uint32_t kColsS0 = 0, kColsS1 = 128, kColsO = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -105,6 +113,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void bar_sync_n(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Diagnostics, compiled in only with -DLF_ATTN_PROGRESS_TRACE: the CTA's
@@ -130,7 +139,7 @@ __device__ __forceinline__ int bt_page(const PrefillArgs& a, int r, int idx) {
   return p;
 }
 
-__global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tq,
                                                             const __grid_constant__ CUtensorMap tk,
                                                             const __grid_constant__ CUtensorMap tv, PrefillArgs a,
                                                             int G) {
@@ -178,10 +187,10 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 128);
+      mbar_init(&s_empty[s], 256);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&p_full[b], 128);
+      mbar_init(&p_full[b], 256);
       mbar_init(&pv_done[b], 1);
     }
     fence_barrier_init();
@@ -270,8 +279,11 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
       }
     }
   } else {
-    // softmax + epilogue: one row per thread; warp w reads TMEM lanes of quadrant w % 4
+    // softmax + epilogue: warp w reads TMEM lanes of quadrant w % 4; warps
+    // 2..5 take columns 0..63 of their rows, warps 6..9 columns 64..127
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int c0 = half * 64;
     const int row = quad * 32 + lane;
     const int g = row / QT, t = row % QT;
     const int tok = t0 + t;
@@ -279,83 +291,106 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
     const int pos = pos0 + tok;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = a.scale_log2;
+    float* red = reinterpret_cast<float*>(smem + kOffRed);   // [2][128]
+    volatile int* flag = reinterpret_cast<volatile int*>(smem + kOffFlag);   // [2][4]
+    const int bar_id = 1 + quad;                             // the two warps of this quadrant
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    uint8_t* prow0 = smem + kOffP + row * 128;
-    for (int j = 0; j < nkb && ok; ++j) {
+    uint8_t* prow0 = smem + kOffP + half * kHalf + row * 128;
+    // The two warps of a quadrant meet at named barriers twice per block.  A
+    // failed (timed-out) wait never makes one of them leave alone: it only
+    // marks the warp unsound, both warps publish their state at the next
+    // exchange and leave the loop there together, so neither is left at a
+    // barrier the other will not reach.
+    for (int j = 0; j < nkb; ++j) {
       const int s = j & 1;
       // every wait before a warp-collective TMEM access is made warp-uniform:
       // tcgen05.ld / st are .sync.aligned and must not run in a diverged warp
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[s], (j >> 1) & 1, 28))) { ok = false; break; }
-      tc_fence_after();
-      // the whole S row: four TMEM loads in flight, one wait
-      uint32_t v0[32], v1[32], v2[32], v3[32];
-      const uint32_t srow = tmem + lane_off + (s ? kColsS1 : kColsS0);
-      tmem_ld_32x32b_x32(srow, v0);
-      tmem_ld_32x32b_x32(srow + 32, v1);
-      tmem_ld_32x32b_x32(srow + 64, v2);
-      tmem_ld_32x32b_x32(srow + 96, v3);
-      tmem_wait_ld();
-      float x[128];
+      if (ok && !__all_sync(0xffffffffu, mbar_wait(&s_full[s], (j >> 1) & 1, 28))) ok = false;
+      float x[64];
+      float pm = -INFINITY;
+      if (ok) {
+        tc_fence_after();
+        // this thread's 64 scores of its row: two TMEM loads in flight, one wait
+        uint32_t v0[32], v1[32];
+        const uint32_t srow = tmem + lane_off + (s ? kColsS1 : kColsS0) + c0;
+        tmem_ld_32x32b_x32(srow, v0);
+        tmem_ld_32x32b_x32(srow + 32, v1);
+        tmem_wait_ld();
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        x[e] = __uint_as_float(v0[e]);
-        x[32 + e] = __uint_as_float(v1[e]);
-        x[64 + e] = __uint_as_float(v2[e]);
-        x[96 + e] = __uint_as_float(v3[e]);
-      }
-      tc_fence_before();
-      mbar_arrive(&s_empty[s]);     // the MMA warp may compute S_{j+2} into this buffer
-      // row maximum of the raw scores (scale > 0 commutes with max); the mask
-      // is applied only on blocks that cross this row's causal limit
-      const int key0 = j * KB;
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (valid && key0 + KB - 1 <= pos) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          if (!valid || key0 + c > pos) x[c] = -INFINITY;
-          m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+        for (int e = 0; e < 32; ++e) {
+          x[e] = __uint_as_float(v0[e]);
+          x[32 + e] = __uint_as_float(v1[e]);
         }
+        tc_fence_before();
+        mbar_arrive(&s_empty[s]);     // the MMA warp may compute S_{j+2} into this buffer
+        // row maximum of the raw scores (scale > 0 commutes with max); the
+        // mask is applied only on blocks that cross this row's causal limit
+        const int key0 = j * KB + c0;
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (valid && key0 + 63 <= pos) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            if (!valid || key0 + c > pos) x[c] = -INFINITY;
+            m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+          }
+        }
+        pm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
-      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;   // log2 units
+      // the row maximum over both halves, and both warps' state, through shared memory
+      red[half * 128 + row] = pm;
+      if (lane == 0) flag[half * 4 + quad] = ok ? 1 : 0;
+      bar_sync_n(bar_id, 64);
+      const bool both_ok = flag[quad] != 0 && flag[4 + quad] != 0;
+      const float mx = fmaxf(red[row], red[128 + row]) * sl2;   // log2 units
+      bar_sync_n(bar_id, 64);                                   // both read before the next write
+      if (!both_ok) {
+        ok = false;
+        break;
+      }
       // P buffer j % 2 is free once P . V of block j - 2 is done; a rescale of O
       // also needs P . V of block j - 1 done
-      if (j > 1 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[s], ((j >> 1) & 1) ^ 1, 29))) { ok = false; break; }
+      if (j > 1 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[s], ((j >> 1) & 1) ^ 1, 29))) {
+        ok = false;
+        continue;   // leave together with the partner warp at the next exchange
+      }
       uint8_t* prow = prow0 + s * kTile;
       // The rescale touches O through TMEM with warp-collective instructions,
-      // so the whole warp rescales when any of its rows needs to; rows whose
-      // maximum moved less rescale by their own (exact) factor.
+      // so the whole warp rescales when any of its rows needs to; both warps
+      // of a quadrant hold the same rows and the same maxima, so they decide
+      // alike, and rows whose maximum moved less rescale by their own factor.
       if (__any_sync(0xffffffffu, mx > m_used + kRescaleThreshold)) {
         if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[s ^ 1], ((j - 1) >> 1) & 1, 31))) {
           ok = false;
-          break;
+          continue;
         }
         const float m_new = fmaxf(m_used, mx);
         const float alpha = m_used == -INFINITY ? (m_new == -INFINITY ? 1.f : 0.f) : ex2_approx(m_used - m_new);
         if (j > 0) {
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 128; c += 32) {
+          for (int c = 0; c < 64; c += 32) {
             uint32_t v[32];
-            tmem_ld_32x32b_x32(tmem + lane_off + kColsO + c, v);
+            tmem_ld_32x32b_x32(tmem + lane_off + kColsO + c0 + c, v);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            tmem_st_32x32b_x32(tmem + lane_off + kColsO + c, v);
+            tmem_st_32x32b_x32(tmem + lane_off + kColsO + c0 + c, v);
           }
           tmem_wait_st();
         }
         l *= alpha;
         m_used = m_new;
       }
-      // P = exp2(s * scale_log2 - m) as bf16 into the swizzled [key-half][row][128 B] tile
+      // P = exp2(s * scale_log2 - m) as bf16 into this half of the swizzled
+      // [key-half][row][128 B] tile
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;   // all-masked row: every p is 0
       float l2[2] = {0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 128; c += 8) {
+      for (int c = 0; c < 64; c += 8) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -365,8 +400,8 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
           l2[1] += p1;
           w[e] = pack_bf16x2(p0, p1);
         }
-        const int half = c >> 6, chunk = (c & 63) >> 3;
-        *reinterpret_cast<uint4*>(prow + half * kHalf + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        const int chunk = c >> 3;
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l += l2[0] + l2[1];
       fence_async_smem();
@@ -374,14 +409,19 @@ __global__ void __launch_bounds__(192, 1) prefill_tc_kernel(const __grid_constan
       mbar_arrive(&p_full[s]);
       if (threadIdx.x == 64) mark(a, 10 + j);
     }
+    // the row sum over both halves (both warps of the quadrant arrive here
+    // exactly once: they leave the loop at the same exchange or finish it)
+    red[half * 128 + row] = l;
+    bar_sync_n(bar_id, 64);
+    const float l_row = red[row] + red[128 + row];
     if (__all_sync(0xffffffffu, ok && mbar_wait(&pv_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, 30))) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = a.out + (int64_t)(qs + tok) * a.out_ld + (h * G + g) * D;
+      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+      __nv_bfloat16* dst = a.out + (int64_t)(qs + tok) * a.out_ld + (h * G + g) * D + c0;
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
+      for (int c = 0; c < 64; c += 32) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + kColsO + c, v);
+        tmem_ld_32x32b_x32(tmem + lane_off + kColsO + c0 + c, v);
         tmem_wait_ld();
         if (valid) {
           uint32_t pk[16];
@@ -439,7 +479,7 @@ void prefill_tc(const PrefillArgs& a, const CUtensorMap& tk, const CUtensorMap& 
     attr = true;
   }
   dim3 grid((a.max_q_len + QT - 1) / QT, a.rows, a.Hkv);
-  launch_k(tc::prefill_tc_kernel, grid, dim3(192), tc::kSmem, stream, 1, tq, tk, tv, a, G);
+  launch_k(tc::prefill_tc_kernel, grid, dim3(tc::kThreadsTc), tc::kSmem, stream, 1, tq, tk, tv, a, G);
 }
 
 }  // namespace attn

@@ -59,6 +59,15 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint4* __restrict__ 
                                                       const uint4* __restrict__ w, uint4* __restrict__ out,
                                                       int vec_per_row, float eps, int H) {
   pdl_trigger();
+  // The weight does not depend on the previous kernel: load it before the
+  // dependency wait (under PDL this overlaps the producer's tail) instead of
+  // after the reduction, where it would be a second dependent round trip.
+  uint4 wreg[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * 128;
+    wreg[j] = i < vec_per_row ? w[i] : make_uint4(0u, 0u, 0u, 0u);
+  }
   pdl_wait();
   const size_t row = blockIdx.x;
   float v[VPT][8];
@@ -99,7 +108,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint4* __restrict__ 
   for (int j = 0; j < VPT; ++j) {
     const int i = threadIdx.x + j * 128;
     if (i < vec_per_row) {
-      uint4 wv = w[i];
+      const uint4 wv = wreg[j];
       const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv);
       uint4 o;
       __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);

@@ -1,6 +1,6 @@
 """Kernel micro-benchmarks: each hot sm_100a kernel against its library baseline.
 
-    python -m lunaflux_b200.bench.kernels [--only gemm|attn|norm] [--json out.json] [--variants]
+    python -m lunaflux_b200.bench.kernels [--only gemm|attn|norm|sample|fp8|moe] [--json out.json] [--variants]
 
 Timing: CUDA events on the launching stream, warm-up first, an L2 flush (a
 256 MB write) before every timed launch, median of the timed launches.  The
@@ -205,9 +205,25 @@ def bench_attn(C, results):
         qf = q[:, : Hq * D].view(nreq, L, Hq, D).transpose(1, 2)
         kf = torch.randn(nreq, Hkv, L, D, device="cuda").bfloat16().repeat_interleave(Hq // Hkv, 1)
         vf = torch.randn_like(kf)
-        base = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(qf, kf, vf, is_causal=True))
-        r = dict(kernel="attn_prefill", nreq=nreq, seq=L, ours_ms=ms, mma_sync_ms=ms_sync, sdpa_dense_ms=base,
-                 tflops=flops / ms / 1e9, peaks=src)
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        dense = {}
+        for name_, be in (("flash", SDPBackend.FLASH_ATTENTION), ("cudnn", SDPBackend.CUDNN_ATTENTION)):
+            try:
+                with sdpa_kernel([be]):
+                    dense[name_] = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(
+                        qf, kf, vf, is_causal=True))
+            except Exception:
+                dense[name_] = None
+        lib_ms = None
+        try:   # vLLM's paged flash-attention on the same paged cache (the library baseline's kernel)
+            from lunaflux_b200.ops.library_ops import LibraryOps
+            lib = LibraryOps("cuda")
+            host = {"seq_lens": sl.cpu().numpy()}
+            lib_ms = time_fn(lambda: lib.attn_prefill(q, out, qs, sl, bt, kc, vc, Hq, Hkv, L, host=host))
+        except Exception:
+            pass
+        r = dict(kernel="attn_prefill", nreq=nreq, seq=L, ours_ms=ms, mma_sync_ms=ms_sync,
+                 sdpa_dense_ms=dense, library_paged_ms=lib_ms, tflops=flops / ms / 1e9, peaks=src)
         results.append(r)
         print(json.dumps(r))
 
@@ -223,6 +239,133 @@ def bench_norm(C, results):
         byts = 4 * T * H * 2
         r = dict(kernel="rmsnorm_residual", T=T, H=H, ours_ms=ms, gbs=byts / ms / 1e6, frac_of_hbm=byts / ms / 1e6 / hbm,
                  peaks=src)
+        results.append(r)
+        print(json.dumps(r))
+
+
+def bench_sample(C, results):
+    """Greedy argmax and the top-k / top-p sampler over a Llama-3 logits row
+    block, against torch.argmax and torch.topk + softmax + multinomial."""
+    from lunaflux_b200.sampling.host import pack_params
+    hbm, _, src = peaks()
+    for R, V in [(256, 128256), (1, 128256), (256, 16032)]:
+        logits = torch.randn(R, V, device="cuda") * 3
+        out = torch.empty(R, dtype=torch.int32, device="cuda")
+        ms_arg = time_fn(lambda: C.argmax(logits, out, None))
+        base_arg = time_fn(lambda: torch.argmax(logits, -1))
+        rows = [(1, 40, 0.7, 0.9, 1000 + i, i) for i in range(R)]
+        params = torch.from_numpy(pack_params(rows).view("u1").copy()).cuda()
+        ms_s = time_fn(lambda: C.sample(logits, params, out, None))
+
+        def torch_sample():
+            v, i = torch.topk(logits / 0.7, 40, dim=-1)
+            p = torch.softmax(v, -1)
+            c = torch.cumsum(p, -1)
+            p = torch.where(c - p > 0.9, torch.zeros_like(p), p)
+            return i.gather(1, torch.multinomial(p, 1))
+
+        base_s = time_fn(torch_sample)
+        byts = R * V * 4
+        r = dict(kernel="sample", rows=R, vocab=V, argmax_ms=ms_arg, torch_argmax_ms=base_arg, topk_topp_ms=ms_s,
+                 torch_topk_topp_ms=base_s, argmax_frac_of_hbm=byts / ms_arg / 1e6 / hbm, peaks=src)
+        results.append(r)
+        print(json.dumps(r))
+
+
+def bench_fp8(C, results):
+    """Block-scaled e4m3 GEMM (128 x 128 weight blocks, 1 x 128 activation
+    groups) on the Llama-3-70B TP 8 shard shapes, against cuBLAS bf16 and
+    torch._scaled_mm (row-wise fp8 scales, the library's fp8 path)."""
+    from lunaflux_b200.models.fp8 import quantize_act, quantize_weight
+    _, tflops_peak, src = peaks()
+    shapes = [("tp8 qkv", 1280, 8192), ("tp8 o", 8192, 1024), ("tp8 gate_up", 7168, 8192), ("tp8 down", 8192, 3584)]
+    for M in (128, 8192):
+        for name, N, K in shapes:
+            x = torch.randn(M, K, device="cuda").bfloat16()
+            w = (torch.randn(N, K, device="cuda") * 0.02)
+            w8, sw = quantize_weight(w)
+            q, s_ = quantize_act(x)
+            q, s_ = q.cuda().contiguous(), s_.cuda().contiguous()
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            ms = time_fn(lambda: C.gemm_fp8(q, s_, w8.cuda(), sw.cuda(), out, 0))
+            wb = w.bfloat16()
+            base_bf16 = time_fn(lambda: x @ wb.t())
+            scaled = None
+            try:
+                a8 = x.to(torch.float8_e4m3fn)
+                b8 = w.to(torch.float8_e4m3fn)
+                sa = torch.ones(M, 1, device="cuda")
+                sb = torch.ones(1, N, device="cuda")
+                scaled = time_fn(lambda: torch._scaled_mm(a8, b8.t(), sa, sb, out_dtype=torch.bfloat16))
+            except Exception:
+                pass
+            flops = 2.0 * M * N * K
+            r = dict(kernel="gemm_fp8_block", case=f"M{M} {name}", M=M, N=N, K=K, ours_ms=ms, cublas_bf16_ms=base_bf16,
+                     scaled_mm_rowwise_ms=scaled, tflops=flops / ms / 1e9, peaks=src)
+            results.append(r)
+            print(json.dumps(r))
+
+
+def bench_moe(C, results):
+    """Mixtral-8x7B MoE layer pieces at one GPU (8 experts, top 2): routing,
+    alignment, gather, grouped gate/up + SwiGLU, grouped down, combine; the
+    library baseline loops over experts with index_select + cuBLAS."""
+    _, _, src = peaks()
+    E, topk, H, F = 8, 2, 4096, 14336
+    for T in (512, 8192):
+        h = torch.randn(T, H, device="cuda").bfloat16()
+        router = torch.randn(E, H, device="cuda") * 0.02
+        wgu = (torch.randn(E, 2 * F, H, device="cuda") * 0.02).bfloat16()
+        wd = (torch.randn(E, H, F, device="cuda") * 0.02).bfloat16()
+        ids = torch.empty(T, topk, dtype=torch.int32, device="cuda")
+        wts = torch.empty(T, topk, dtype=torch.float32, device="cuda")
+        cap = -(-(T * topk + E * 127) // 128) * 128
+        groups = torch.empty(E + 1, dtype=torch.int32, device="cuda")
+        perm = torch.empty(cap, dtype=torch.int32, device="cuda")
+        slot = torch.empty(T * topk, dtype=torch.int32, device="cuda")
+        xg = torch.empty(cap, H, device="cuda", dtype=torch.bfloat16)
+        act = torch.empty(cap, F, device="cuda", dtype=torch.bfloat16)
+        y = torch.empty(cap, H, device="cuda", dtype=torch.bfloat16)
+        out = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+
+        def ours():
+            C.moe_route(h, router, None, topk, ids, wts)
+            C.moe_align(ids, T, topk, 0, E, groups, perm, slot)
+            C.moe_gather(h, perm, groups, E, topk, xg)
+            C.gemm_grouped(xg, wgu, act, groups, E, 2)
+            C.gemm_grouped(act, wd, y, groups, E, 0)
+            C.moe_combine(y, slot, wts, T, topk, out)
+
+        pieces = {}
+        ours()
+        for key, fn in (("route", lambda: C.moe_route(h, router, None, topk, ids, wts)),
+                        ("align", lambda: C.moe_align(ids, T, topk, 0, E, groups, perm, slot)),
+                        ("gather", lambda: C.moe_gather(h, perm, groups, E, topk, xg)),
+                        ("grouped_gate_up", lambda: C.gemm_grouped(xg, wgu, act, groups, E, 2)),
+                        ("grouped_down", lambda: C.gemm_grouped(act, wd, y, groups, E, 0)),
+                        ("combine", lambda: C.moe_combine(y, slot, wts, T, topk, out))):
+            pieces[key] = time_fn(fn)
+        total = time_fn(ours)
+
+        def library():
+            logits = h.float() @ router.t()
+            w_, i_ = torch.softmax(logits, -1).topk(topk, -1)
+            w_ = w_ / w_.sum(-1, keepdim=True)
+            acc = torch.zeros(T, H, device="cuda", dtype=torch.float32)
+            for e in range(E):
+                rows, k = (i_ == e).nonzero(as_tuple=True)
+                if rows.numel() == 0:
+                    continue
+                xe = h.index_select(0, rows)
+                gu = xe @ wgu[e].t()
+                v = gu.view(-1, 2 * F // 64, 2, 32)
+                a = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(-1, F)
+                acc.index_add_(0, rows, (a @ wd[e].t()).float() * w_[rows, k, None])
+            return acc
+
+        base = time_fn(library)
+        r = dict(kernel="moe_layer", tokens=T, experts=E, topk=topk, ours_ms=total, pieces_ms=pieces,
+                 library_ms=base, speedup=base / total, peaks=src)
         results.append(r)
         print(json.dumps(r))
 
@@ -245,6 +388,12 @@ def main():
         bench_attn(C, results)
     if args.only in ("", "norm"):
         bench_norm(C, results)
+    if args.only in ("", "sample"):
+        bench_sample(C, results)
+    if args.only in ("", "fp8"):
+        bench_fp8(C, results)
+    if args.only in ("", "moe"):
+        bench_moe(C, results)
     if args.json:
         with open(args.json, "w") as f:
             json.dump(results, f, indent=1)

@@ -243,6 +243,14 @@ def _serve_parser():
     return ap
 
 
+def _drain_ms(a) -> int:
+    from .config import ServiceConfig, parse_document
+    if a.config:
+        with open(a.config, "rb") as f:
+            return parse_document(f.read()).service.graceful_drain_ms
+    return ServiceConfig().graceful_drain_ms
+
+
 def _serve_model(a):
     """(spec, preset, scheduler config, cache config, checkpoint dir or None) of the serve arguments."""
     import torch
@@ -345,6 +353,7 @@ def serve(args: List[str]):
     from .service.server import EngineService, MetricsServer, TCPServer
     from .tokenizer.bpe import Tokenizer, synthetic_byte_tokenizer
     a = _serve_parser().parse_args(args)
+    drain_ms = _drain_ms(a)
     cuda = torch.cuda.is_available()
     from .parallel.comm import env_rank_world, init_distributed
     rank, world, local = env_rank_world()
@@ -403,7 +412,21 @@ def serve(args: List[str]):
             hs = CompletionsServer(svc, a.host, a.http_port, model=preset, chat_template=chat_template,
                                    eos_ids=eos_ids)
             print(f"lunaflux completions on http://{a.host}:{await hs.start()}/v1/completions", flush=True)
-        await srv.serve_forever()
+        # SIGTERM / SIGINT: graceful drain (refuse new requests, let the live
+        # ones finish for up to graceful_drain_ms, fail the rest retryably)
+        import signal
+        loop = asyncio.get_running_loop()
+        stop = asyncio.Event()
+        for sig in (signal.SIGTERM, signal.SIGINT):
+            try:
+                loop.add_signal_handler(sig, stop.set)
+            except (NotImplementedError, RuntimeError):
+                pass
+        serving = asyncio.ensure_future(srv.serve_forever())
+        await stop.wait()
+        drained = await loop.run_in_executor(None, svc.drain, drain_ms / 1000.0)
+        print(f"lunaflux drained ({'all requests finished' if drained else 'deadline reached'})", flush=True)
+        serving.cancel()
 
     try:
         asyncio.run(main())

@@ -81,7 +81,12 @@ class EngineService:
     # -------------------------------------------------------------- producer side
     def submit(self, req: GenerateRequest, sink: Callable[[object], None]):
         """Queues a request for the engine thread.  Text prompts are tokenized
-        first on the tokenizer pool, so a long prompt never stalls a step."""
+        first on the tokenizer pool, so a long prompt never stalls a step.
+        While draining, new requests are refused here (retryable
+        ``overloaded``); those queued before the drain began are admitted."""
+        if self.draining:
+            sink(FailedEvent(req.request_id, PublicErrorCode.OVERLOADED, True))
+            return
         if req.input_text is not None and self.tokenizer is not None:
             self._tok_pool.submit(self._tokenize_then_queue, req, sink)
             return
@@ -108,11 +113,37 @@ class EngineService:
             self._inbox.append(("cancel", rid, None))
             self._cv.notify()
 
+    def drain(self, timeout_s: float, poll_s: float = 0.01) -> bool:
+        """Graceful drain (the service configuration's graceful_drain_ms):
+        new requests are refused from now on (retryable ``overloaded``), the
+        live ones may finish for up to ``timeout_s``; whatever is still live
+        then is cancelled in the engine and fails with the retryable
+        ``worker_unavailable`` code.  Returns True when every live request
+        finished in time.  Reference: config/service/service.mbt:39-107
+        (graceful_drain_milliseconds) and the drain path of
+        service/online_session."""
+        self.draining = True
+        deadline = time.monotonic() + max(0.0, timeout_s)
+        while time.monotonic() < deadline:
+            with self._cv:
+                if not self._live and not self._inbox:
+                    return True
+            time.sleep(poll_s)
+        with self._cv:
+            if not self._live and not self._inbox:
+                return True
+            done = threading.Event()
+            self._inbox.append(("drain_deadline", done, None))
+            self._cv.notify()
+        # the engine thread fails the remaining requests
+        while not done.wait(poll_s) and self._thread.is_alive():
+            pass
+        return False
+
     # -------------------------------------------------------------- engine thread
     def _admit(self, req: GenerateRequest, sink):
-        if self.draining or self.failed:
-            sink(FailedEvent(req.request_id, PublicErrorCode.WORKER_UNAVAILABLE if self.failed
-                             else PublicErrorCode.OVERLOADED, True))
+        if self.failed:
+            sink(FailedEvent(req.request_id, PublicErrorCode.WORKER_UNAVAILABLE, True))
             return
         if (req.model_content_digest and self.content_digest and req.model_content_digest != self.content_digest) or \
                 (req.model_plan_digest and req.model_plan_digest != self.plan_digest):
@@ -194,6 +225,12 @@ class EngineService:
                     self._admit(a, b)
                 elif kind == "cancel":
                     self.engine.cancel(a)
+                elif kind == "drain_deadline":
+                    for rid in list(self._live):
+                        self._finish(rid, None, PublicErrorCode.WORKER_UNAVAILABLE)
+                        self.engine.cancel(rid)
+                    self.engine.results.clear()
+                    a.set()
             if self.engine.has_work():
                 try:
                     self.engine.step()
@@ -310,8 +347,8 @@ class TCPServer:
 
 class MetricsServer:
     """Minimal HTTP endpoint for the engine's metrics: ``GET /metrics``
-    (Prometheus text) and ``GET /health`` (200 while the engine loop runs,
-    503 otherwise).  Read-only, no request payloads, one response per
+    (Prometheus text) and ``GET /health`` (200 while the engine loop runs
+    and the service is not draining, 503 otherwise).  Read-only, no request payloads, one response per
     connection."""
 
     def __init__(self, service: EngineService, host: str = "127.0.0.1", port: int = 0):
@@ -334,8 +371,8 @@ class MetricsServer:
                 body = self.service.engine.metrics.registry.render_prometheus().encode()
                 status = "200 OK"
             elif path == "/health":
-                alive = self.service.alive()
-                body = b"ok\n" if alive else b"unavailable\n"
+                alive = self.service.alive() and not self.service.draining
+                body = b"ok\n" if alive else (b"draining\n" if self.service.draining else b"unavailable\n")
                 status = "200 OK" if alive else "503 Service Unavailable"
             else:
                 body, status = b"not found\n", "404 Not Found"

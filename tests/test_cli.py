@@ -145,6 +145,13 @@ def test_serve_model_dir_end_to_end(tmp_path):
         toks = [e.token_id for e in evs if hasattr(e, "token_id")]
         assert isinstance(evs[-1], CompletedEvent)
         assert toks == ReferenceModel(spec, ck).generate_greedy(list(prompt), 6)
+        # SIGTERM: graceful drain, then a clean exit
+        import signal
+        p.send_signal(signal.SIGTERM)
+        rest, _ = p.communicate(timeout=60)
+        assert "lunaflux drained (all requests finished)" in rest, rest
+        assert p.returncode == 0, rest
     finally:
-        p.kill()
-        p.wait(timeout=30)
+        if p.poll() is None:
+            p.kill()
+            p.wait(timeout=30)

@@ -297,3 +297,69 @@ def test_request_decoder_fuzz():
         except FramedWireError:
             outcomes["rejected"] += 1
     assert outcomes["rejected"] > 2000 and outcomes["ok"] >= 0
+
+
+def test_graceful_drain():
+    """drain(): new requests are refused (retryable overloaded), live ones may
+    finish until the deadline, the rest fail with the retryable
+    worker_unavailable code and are cancelled in the engine."""
+    import threading
+    import time
+
+    from lunaflux_b200.config import CacheConfig, SchedulerConfig
+    from lunaflux_b200.contracts import CompletedEvent, FailedEvent, GenerateRequest, PublicErrorCode
+    from lunaflux_b200.engine.engine import EngineOptions, LLMEngine
+    from lunaflux_b200.models.spec import tiny_llama
+    from lunaflux_b200.models.weights import build_runtime, random_checkpoint
+    from lunaflux_b200.ops.torch_ops import TorchOps
+    from lunaflux_b200.service.server import EngineService
+
+    spec = tiny_llama()
+    ck = random_checkpoint(spec, 0)
+
+    def service():
+        eng = LLMEngine(build_runtime(spec, lambda n: ck[n]), TorchOps(), "cpu",
+                        SchedulerConfig(step_token_budget=64, max_active_requests=4, prefill_chunk_tokens=64,
+                                        emergency_decode_page_reserve=1),
+                        CacheConfig(), EngineOptions(max_context=512, num_pages=128, graph_sizes=()))
+        svc = EngineService(eng, None, LIM)
+        svc.start()
+        return svc, eng
+
+    ends = {}
+    lock = threading.Lock()
+
+    def sink(rid):
+        def f(ev):
+            if isinstance(ev, (CompletedEvent, FailedEvent)):
+                with lock:
+                    ends[rid] = ev
+        return f
+
+    # short requests finish inside the drain window
+    svc, eng = service()
+    for rid in (1, 2):
+        svc.submit(GenerateRequest(request_id=rid, input_tokens=(3, 4, 5), max_new_tokens=3), sink(rid))
+    assert svc.drain(30.0)
+    assert isinstance(ends[1], CompletedEvent) and isinstance(ends[2], CompletedEvent)
+    svc.submit(GenerateRequest(request_id=3, input_tokens=(3, 4), max_new_tokens=2), sink(3))
+    t0 = time.monotonic()
+    while 3 not in ends and time.monotonic() - t0 < 10:
+        time.sleep(0.01)
+    assert isinstance(ends[3], FailedEvent) and ends[3].code is PublicErrorCode.OVERLOADED and ends[3].retryable
+    svc.stop()
+
+    # a long request outlives the deadline: it fails retryably and leaves the engine
+    svc, eng = service()
+    svc.submit(GenerateRequest(request_id=10, input_tokens=(7, 8, 9), max_new_tokens=400), sink(10))
+    t0 = time.monotonic()
+    while not eng.has_work() and time.monotonic() - t0 < 10:
+        time.sleep(0.005)
+    assert not svc.drain(0.05)
+    ev = ends[10]
+    assert isinstance(ev, FailedEvent) and ev.code is PublicErrorCode.WORKER_UNAVAILABLE and ev.retryable
+    t0 = time.monotonic()
+    while eng.has_work() and time.monotonic() - t0 < 10:
+        time.sleep(0.01)
+    assert not eng.has_work()
+    svc.stop()
