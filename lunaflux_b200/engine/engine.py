@@ -114,7 +114,8 @@ class LLMEngine:
             self._next_rid += 1
         sampling = sampling or SamplingParameters()
         now = self.clock()
-        req = Request(rid=rid, prompt=list(int(t) for t in prompt), max_new=max_new_tokens, sampling=sampling,
+        toks = prompt.tolist() if hasattr(prompt, "tolist") else [int(t) for t in prompt]   # plain ints
+        req = Request(rid=rid, prompt=toks, max_new=max_new_tokens, sampling=sampling,
                       stop_ids=frozenset(int(t) for t in stop_ids),
                       deadline=None if deadline_s is None else now + deadline_s, cache_scope=cache_scope,
                       cache_enabled=use_prefix_cache, arrival=arrival if arrival is not None else now)

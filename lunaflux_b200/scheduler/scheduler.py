@@ -98,6 +98,13 @@ class Request:
         n = len(self.prompt)
         return self.prompt[i] if i < n else self.output[i - n]
 
+    def tokens_upto(self, n: int) -> List[int]:
+        """The first n tokens of prompt + output, as one list (slices, no per-token calls)."""
+        p = self.prompt
+        if n <= len(p):
+            return list(p[:n])
+        return list(p) + list(self.output[: n - len(p)])
+
     @property
     def prefill_target(self) -> int:
         """KV length at which prefill ends (the whole prompt, or after a
@@ -245,7 +252,7 @@ class Scheduler:
         if publish and self.prefix is not None and req.cache_enabled:
             n_full = req.num_computed // self.P
             if n_full:
-                toks = [req.token_at(i) for i in range(n_full * self.P)]
+                toks = req.tokens_upto(n_full * self.P)
                 self.prefix.insert(self._ident(req), toks, req.pages[:n_full])
         if req.prefix_nodes:
             self.prefix.release(req.prefix_nodes)
@@ -326,7 +333,7 @@ class Scheduler:
         req.sched_len = 0
         if self.prefix is not None and req.cache_enabled:
             seq_len = req.prefill_target
-            toks = [req.token_at(i) for i in range(seq_len)]
+            toks = req.tokens_upto(seq_len)
             # keep at least one token to compute so the row produces logits
             nodes = self.prefix.lookup(self._ident(req), toks, max_pages=(seq_len - 1) // self.P)
             if nodes:
