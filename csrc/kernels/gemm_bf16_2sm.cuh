@@ -47,7 +47,29 @@ namespace gemm {
 namespace pair {
 
 constexpr int kTileM = 256;            // rows per pair tile (128 per CTA)
-constexpr int kTileN = 256;            // columns per pair tile (B: 128 rows per CTA)
+constexpr int kTileN = 256;            // widest pair tile (B: 128 rows per CTA); TMEM columns per accumulator
+constexpr int kBoxRows = 32;           // B rows per TMA box (a CTA loads bn / 2 rows as bn / 64 boxes)
+
+// Column tiling of N: `wide` tiles of base + 64 columns, then base-wide
+// tiles.  Uniform 256-wide tiles for most shapes; a GEMM with one M-tile
+// whose 256-wide tiles would leave pairs idle in the last round is cut into
+// k tiles per pair of near-equal width (multiples of 64), so every pair gets
+// the same number of tiles.
+struct ColPlan {
+  int tiles_n;
+  int wide;
+  int base;
+};
+
+__host__ __device__ __forceinline__ void tile_cols(const ColPlan& cp, int tn, int& n0, int& bn) {
+  if (tn < cp.wide) {
+    bn = cp.base + 64;
+    n0 = tn * bn;
+  } else {
+    bn = cp.base;
+    n0 = cp.wide * (cp.base + 64) + (tn - cp.wide) * cp.base;
+  }
+}
 constexpr int kStageBytes = BM * BK * 2 + (kTileN / 2) * BK * 2;  // 32 KB per CTA
 constexpr int kStages = 6;
 constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
@@ -109,7 +131,7 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                     void* __restrict__ out, int M, int N, int K, int ldd, const RopeArgs rope) {
+                     void* __restrict__ out, int M, int N, int K, int ldd, const ColPlan cp, const RopeArgs rope) {
   static_assert(EPI == kStoreBf16 || EPI == kStoreF32 || EPI == kSwiGLU || EPI == kQkvRope, "plain or QKV epilogues");
   pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -125,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = cluster_ctarank();     // 0: leader of the pair
   const bool leader = rank == 0;
   const int num_m = (M + kTileM - 1) / kTileM;
-  const int num_tiles = num_m * (N / kTileN);
+  const int num_tiles = num_m * cp.tiles_n;
   const int num_kb = (K + BK - 1) / BK;
   const int pair_id = blockIdx.x / 2;
   const int num_pairs = gridDim.x / 2;
@@ -164,28 +186,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
         const int m0 = (tile % num_m) * kTileM + (int)rank * BM;
-        const int n0 = (tile / num_m) * kTileN + (int)rank * (kTileN / 2);
+        int n0, bn;
+        tile_cols(cp, tile / num_m, n0, bn);
+        const int half = bn / 2;                       // B rows this CTA stages
+        n0 += (int)rank * half;
+        const uint32_t stage_tx = 2u * (uint32_t)(BM * BK * 2 + half * BK * 2);   // both CTAs' bytes
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, 21)) { ok = false; break; }
           const uint32_t sa = smem_u32(smem + stage * kStageBytes);
           const uint32_t sb = sa + BM * BK * 2;
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kStageBytes);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], stage_tx);
           const uint32_t fb = full_leader + stage * 8;
           tma_load_pair(sa, &tmap_a, fb, kb * BK, m0, 0ull);
-          tma_load_pair(sb, &tmap_b, fb, kb * BK, n0, pol_b);
+          for (int b = 0; b < half; b += kBoxRows)
+            tma_load_pair(sb + b * BK * 2, &tmap_b, fb, kb * BK, n0 + b, pol_b);
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
       }
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kTileM, kTileN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
       for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs, ++local) {
         const int acc = local & 1;
+        int n0_unused, bn;
+        tile_cols(cp, tile / num_m, n0_unused, bn);
+        const uint32_t idesc = idesc_bf16_f32(kTileM, bn);
         if (!mbar_wait(&tempty_bar[acc], ((local >> 1) & 1) ^ 1, 22)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kTileN;
@@ -213,7 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, 24)) break;
       tc_fence_after();
       const int m0 = (tile % num_m) * kTileM + (int)rank * BM;
-      const int n0 = (tile / num_m) * kTileN;
+      int n0, bn;
+      tile_cols(cp, tile / num_m, n0, bn);
       const int row = m0 + quad * 32 + lane;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * kTileN;
       if constexpr (EPI == kQkvRope) {
@@ -222,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if constexpr (EPI == kSwiGLU) {
         const int o0 = n0 / 2;
 #pragma unroll 1
-        for (int c = 0; c < kTileN / 2; c += 16) {
+        for (int c = 0; c < bn / 2; c += 16) {
           const int grp = c / 32, off = c % 32;
           uint32_t g[16], u[16];
           tmem_ld_32x32b_x16(taddr + grp * 64 + off, g);
@@ -243,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < kTileN; c += 32) {
+        for (int c = 0; c < bn; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(taddr + c, r);
           tmem_wait_ld();
@@ -342,11 +372,24 @@ static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream, const Rope
     max_pairs = n;
   }
   if (max_pairs < 1) return false;
-  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  pair::ColPlan cp{a.N / pair::kTileN, 0, pair::kTileN};
+  const int num_m = (a.M + pair::kTileM - 1) / pair::kTileM;
+  if (num_m == 1 && epi != kQkvRope && a.N % 64 == 0) {
+    // one M-tile: k tiles per pair of near-equal width instead of a partial last round
+    const int t_min = a.N / pair::kTileN;
+    const int k = (t_min + max_pairs - 1) / max_pairs;
+    const int t = k * max_pairs;
+    const int base = (a.N / (64 * t)) * 64;
+    const int wide = base >= 64 ? (a.N - base * t) / 64 : 0;
+    if (base >= 64 && base + (wide > 0 ? 64 : 0) <= pair::kTileN && t % max_pairs == 0 && t_min % max_pairs != 0)
+      cp = pair::ColPlan{t, wide, base};
+  }
+  const int all_tiles = num_m * cp.tiles_n;
+  const int pairs = all_tiles < max_pairs ? all_tiles : max_pairs;
   CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
-  CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, pair::kTileN / 2);
+  CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, pair::kBoxRows);
   launch_k(kfn, dim3(2 * pairs), dim3(kThreads), pair::kSmem, stream, 2u, ta, tb, a.D, a.M, a.N, a.K, (int)a.ldd,
-           rope);
+           cp, rope);
   return true;
 }
 

@@ -450,7 +450,9 @@ def test_gemm_qkv_rope_matches_gemm_then_rope(C, M, Hq, Hkv, K):
 
 
 @pytest.mark.parametrize("M,N,K,epi", [(2048, 4096, 4096, 0), (8192, 6144, 4096, 0), (4096, 28672, 4096, 2),
-                                       (300, 32768, 512, 1), (2048, 4096, 1000, 0)])
+                                       (300, 32768, 512, 1), (2048, 4096, 1000, 0),
+                                       # one M-tile: 192- and 256-wide tiles, two or more per pair
+                                       (256, 28672, 4096, 2), (129, 32768, 256, 1), (200, 28672, 1024, 0)])
 def test_gemm_cta_pair(C, M, N, K, epi):
     """256 x 256 tiles on CTA pairs (tcgen05.mma cta_group::2, B split over
     the pair): values against the fp32 reference, including a pair whose
