@@ -107,7 +107,10 @@ constexpr int kDecStages = 4;
 __global__ void __launch_bounds__(32) decode_kernel(const __grid_constant__ CUtensorMap tk,
                                                     const __grid_constant__ CUtensorMap tv, DecodeArgs a) {
   pdl_trigger();
-  pdl_wait();
+  // The step's inputs (lengths, token rows, block table) were uploaded before
+  // the step's first kernel, and every K / V page except a row's last one was
+  // written by earlier steps: the first pages are fetched before the
+  // dependency wait (pdl_wait below), the row's last page and Q after it.
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * 2 * kPageBytes);
@@ -145,18 +148,27 @@ __global__ void __launch_bounds__(32) decode_kernel(const __grid_constant__ CUte
     return __shfl_sync(0xffffffffu, win, idx - win_base);
   };
   {
-    // first pages in flight before Q is read
+    // first pages in flight before Q is read; the row's last page (this
+    // step's token) only after the previous kernel has written it
     int first[kDecStages];
 #pragma unroll
     for (int i = 0; i < kDecStages; ++i) first[i] = i < count ? page_at(i) : 0;
+    const int last = n_pages - 1 - p_begin;   // split-relative index of the row's last page
     if (lane == 0) {
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
       for (int i = 0; i < kDecStages && i < count; ++i) {
+        if (i == last) continue;
         uint8_t* sk = smem + i * 2 * kPageBytes;
         mbar_arrive_expect_tx(&full[i], 2 * kPageBytes);
         load_page(&tk, &tv, sk, sk + kPageBytes, &full[i], first[i], kvh, a.Hkv);
       }
+    }
+    pdl_wait();
+    if (lane == 0 && last >= 0 && last < kDecStages && last < count) {
+      uint8_t* sk = smem + last * 2 * kPageBytes;
+      mbar_arrive_expect_tx(&full[last], 2 * kPageBytes);
+      load_page(&tk, &tv, sk, sk + kPageBytes, &full[last], first[last], kvh, a.Hkv);
     }
   }
 

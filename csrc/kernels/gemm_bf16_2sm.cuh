@@ -175,15 +175,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_wait();  // the set-up above touches no global memory
+  // The weight slabs do not depend on the previous kernel: the first tile's
+  // first stages of B go out before the dependency wait (overlapping the
+  // previous kernel's tail under programmatic dependent launch); the A loads
+  // of those stages follow it.
+  const uint64_t pol_b = l2_policy_evict_first();
+  const uint32_t full_leader = peer_addr(smem_u32(full_bar), 0);
+  int pre = 0;
+  if (warp == 0 && lane == 0 && pair_id < num_tiles) {
+    int n0, bn;
+    tile_cols(cp, pair_id / num_m, n0, bn);
+    const int half = bn / 2;
+    n0 += (int)rank * half;
+    const uint32_t stage_tx = 2u * (uint32_t)(BM * BK * 2 + half * BK * 2);
+    pre = min(kStages, num_kb);
+    for (int i = 0; i < pre; ++i) {
+      const uint32_t sb = smem_u32(smem + i * kStageBytes) + BM * BK * 2;
+      if (leader) mbar_arrive_expect_tx(&full_bar[i], stage_tx);
+      for (int b = 0; b < half; b += kBoxRows)
+        tma_load_pair(sb + b * BK * 2, &tmap_b, full_leader + i * 8, i * BK, n0 + b, pol_b);
+    }
+  }
+  pdl_wait();  // everything above touches no memory the previous kernel writes
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint64_t pol_b = l2_policy_evict_first();
-      const uint32_t full_leader = peer_addr(smem_u32(full_bar), 0);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      bool first = true;
       for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
         const int m0 = (tile % num_m) * kTileM + (int)rank * BM;
         int n0, bn;
@@ -192,16 +212,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         n0 += (int)rank * half;
         const uint32_t stage_tx = 2u * (uint32_t)(BM * BK * 2 + half * BK * 2);   // both CTAs' bytes
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, 21)) { ok = false; break; }
           const uint32_t sa = smem_u32(smem + stage * kStageBytes);
           const uint32_t sb = sa + BM * BK * 2;
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], stage_tx);
           const uint32_t fb = full_leader + stage * 8;
+          if (!(first && kb < pre)) {
+            if (!mbar_wait(&empty_bar[stage], phase ^ 1, 21)) { ok = false; break; }
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], stage_tx);
+            for (int b = 0; b < half; b += kBoxRows)
+              tma_load_pair(sb + b * BK * 2, &tmap_b, fb, kb * BK, n0 + b, pol_b);
+          }
           tma_load_pair(sa, &tmap_a, fb, kb * BK, m0, 0ull);
-          for (int b = 0; b < half; b += kBoxRows)
-            tma_load_pair(sb + b * BK * 2, &tmap_b, fb, kb * BK, n0 + b, pol_b);
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
+        first = false;
       }
     }
   } else if (warp == 1) {

@@ -787,24 +787,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_wait();  // the set-up above touches no global memory
+  // The weight slabs do not depend on the previous kernel: the first stages'
+  // B loads go out before the dependency wait (under programmatic dependent
+  // launch they overlap the previous kernel's tail); their A loads follow it.
+  const int pre = (warp == 0 && lane == 0) ? min(STAGES, kb1 - kb0) : 0;
+  const uint64_t pol_b = l2_policy_evict_first();
+  for (int i = 0; i < pre; ++i) {
+    mbar_arrive_expect_tx(&full_bar[i], S::kStageBytes);
+    tma_load_2d_hint(smem + i * S::kStageBytes + S::kABytes, &tmap_b, &full_bar[i], (kb0 + i) * BK, n0, pol_b);
+  }
+  pdl_wait();  // everything above touches no memory the previous kernel writes
   // fused all-reduce: this operation's epoch (advanced by the grid's last CTA)
   uint32_t ep = 0;
   if constexpr (OUT == kAllReduceLL) ep = (uint32_t)(*reinterpret_cast<volatile int*>(ll.state)) + 1u;
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint64_t pol_b = l2_policy_evict_first();
       int stage = 0;
       uint32_t phase = 0;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1, 11)) break;
         uint8_t* sa = smem + stage * S::kStageBytes;
         uint8_t* sb = sa + S::kABytes;
-        mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
+        if (kb - kb0 >= pre) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, 11)) break;
+          mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
+          tma_load_2d_hint(sb, &tmap_b, &full_bar[stage], kb * BK, n0, pol_b);
+        }
 #pragma unroll
         for (int j = 0; j < MB; ++j) tma_load_2d(sa + j * BM * BK * 2, &tmap_a, &full_bar[stage], kb * BK, m0 + j * BM);
-        tma_load_2d_hint(sb, &tmap_b, &full_bar[stage], kb * BK, n0, pol_b);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
