@@ -48,7 +48,7 @@ namespace pair {
 
 constexpr int kTileM = 256;            // rows per pair tile (128 per CTA)
 constexpr int kTileN = 256;            // widest pair tile (B: 128 rows per CTA); TMEM columns per accumulator
-constexpr int kBoxRows = 32;           // B rows per TMA box (a CTA loads bn / 2 rows as bn / 64 boxes)
+constexpr int kBoxRowsNarrow = 32;     // B rows per TMA box with 192 / 256-wide tiles (bn / 64 boxes per stage)
 
 // Column tiling of N: `wide` tiles of base + 64 columns, then base-wide
 // tiles.  Uniform 256-wide tiles for most shapes; a GEMM with one M-tile
@@ -59,6 +59,7 @@ struct ColPlan {
   int tiles_n;
   int wide;
   int base;
+  int box_rows;   // B rows per TMA box: 128 (one box per stage) for uniform tiles, 32 otherwise
 };
 
 __host__ __device__ __forceinline__ void tile_cols(const ColPlan& cp, int tn, int& n0, int& bn) {
@@ -192,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < pre; ++i) {
       const uint32_t sb = smem_u32(smem + i * kStageBytes) + BM * BK * 2;
       if (leader) mbar_arrive_expect_tx(&full_bar[i], stage_tx);
-      for (int b = 0; b < half; b += kBoxRows)
+      for (int b = 0; b < half; b += cp.box_rows)
         tma_load_pair(sb + b * BK * 2, &tmap_b, full_leader + i * 8, i * BK, n0 + b, pol_b);
     }
   }
@@ -218,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(first && kb < pre)) {
             if (!mbar_wait(&empty_bar[stage], phase ^ 1, 21)) { ok = false; break; }
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], stage_tx);
-            for (int b = 0; b < half; b += kBoxRows)
+            for (int b = 0; b < half; b += cp.box_rows)
               tma_load_pair(sb + b * BK * 2, &tmap_b, fb, kb * BK, n0 + b, pol_b);
           }
           tma_load_pair(sa, &tmap_a, fb, kb * BK, m0, 0ull);
@@ -395,7 +396,7 @@ static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream, const Rope
     max_pairs = n;
   }
   if (max_pairs < 1) return false;
-  pair::ColPlan cp{a.N / pair::kTileN, 0, pair::kTileN};
+  pair::ColPlan cp{a.N / pair::kTileN, 0, pair::kTileN, pair::kTileN / 2};
   const int num_m = (a.M + pair::kTileM - 1) / pair::kTileM;
   if (num_m == 1 && epi != kQkvRope && a.N % 64 == 0) {
     // one M-tile: k tiles per pair of near-equal width instead of a partial last round
@@ -405,12 +406,12 @@ static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream, const Rope
     const int base = (a.N / (64 * t)) * 64;
     const int wide = base >= 64 ? (a.N - base * t) / 64 : 0;
     if (base >= 64 && base + (wide > 0 ? 64 : 0) <= pair::kTileN && t % max_pairs == 0 && t_min % max_pairs != 0)
-      cp = pair::ColPlan{t, wide, base};
+      cp = pair::ColPlan{t, wide, base, pair::kBoxRowsNarrow};
   }
   const int all_tiles = num_m * cp.tiles_n;
   const int pairs = all_tiles < max_pairs ? all_tiles : max_pairs;
   CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
-  CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, pair::kBoxRows);
+  CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, (uint32_t)cp.box_rows);
   launch_k(kfn, dim3(2 * pairs), dim3(kThreads), pair::kSmem, stream, 2u, ta, tb, a.D, a.M, a.N, a.K, (int)a.ldd,
            cp, rope);
   return true;
