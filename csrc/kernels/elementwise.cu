@@ -413,28 +413,102 @@ struct CandidateSource {
   __device__ __forceinline__ bool bad(int i) const { return i % per == per - 1 && *at(i) == 2; }
 };
 
+template <int NT>
+__device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v, unsigned long long* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  unsigned long long r = 0;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) r += sh[i];
+  return r;
+}
+
+// Fixed-point weight of a token: exp((v - max) / T) in units of 2^-44.  Each
+// weight is at most 2^44 and a row has fewer than 2^19 entries, so every sum
+// fits in 64 bits; integer sums are exact and order-independent, so every
+// tensor-parallel rank draws the same token from the same logits.
+constexpr float kMassScale = 17592186044416.0f;   // 2^44
+
+// Radix selection over the composite keys, largest first: the key of the
+// first entry (in descending key order, restricted to keys >= floor_key) at
+// which the cumulative weight satisfies  cum >= thr  (strict = false) or
+// cum > thr  (strict = true).  One byte of the 64-bit key per pass (8 passes);
+// each pass builds a 256-bin histogram of the entries that match the bytes
+// chosen so far.  The caller guarantees that the total weight satisfies the
+// predicate, so the selected key is an existing entry's.
+template <int NT, class Src, class WFn>
+__device__ uint64_t select_desc(const Src& src, uint64_t floor_key, WFn wfn, unsigned long long thr, bool strict,
+                                unsigned long long* hist, unsigned long long* state) {
+  const int n = src.n;
+  uint64_t P = 0;
+  unsigned long long above = 0;
+  for (int d = 7; d >= 0; --d) {
+    for (int i = threadIdx.x; i < 256; i += NT) hist[i] = 0;
+    __syncthreads();
+    const int sh = 8 * d;
+    const uint64_t hi_mask = d == 7 ? 0ull : (~0ull << (sh + 8));
+    for (int i = threadIdx.x; i < n; i += NT) {
+      float v;
+      uint64_t k;
+      if (src.get(i, v, k) && k >= floor_key && (k & hi_mask) == P)
+        atomicAdd(&hist[(k >> sh) & 255u], wfn(v));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long a = above;
+      int b = 255;
+      for (; b > 0; --b) {
+        const unsigned long long c = a + hist[b];
+        if (strict ? c > thr : c >= thr) break;
+        a = c;
+      }
+      state[0] = P | ((uint64_t)b << sh);
+      state[1] = a;
+    }
+    __syncthreads();
+    P = state[0];
+    above = state[1];
+    __syncthreads();
+  }
+  return P;
+}
+
 // Counter-addressed sampling of one row (block of NT threads).  Every quantity
-// over the sorted order is a function of a composite-key threshold K ("all
-// entries whose key >= K" is a prefix of the reference's sorted order); the
-// thresholds are found by bisection on the 64-bit key space (64 passes).  No
-// sort and no scratch.  The result depends only on the entries' keys, so a
-// row given as per-shard candidates (every key of the top-k set present)
-// samples the same token as the full row.
+// over the reference's sorted order (logit descending, id ascending == the
+// composite key descending) is the crossing point of a cumulative count or
+// mass, found by radix selection on the 64-bit key (8 passes each): the
+// k-th largest key (top-k), the first key at which the cumulative mass reaches
+// top_p of the total (top-p), the first key at which it exceeds u times the
+// retained mass (the draw).  About 28 passes over the row, no sort, no global
+// scratch.  The result depends only on the entries' keys, so a row given as
+// per-shard candidates (every key of the top-k set present) samples the same
+// token as the full row.
 template <int NT, class Src>
 __device__ void sample_row(const Src& src, const SampleParams p, int32_t* out_tok, int32_t* status, uint64_t* shk,
                            double* shd, int* shi) {
+  (void)shd;
+  __shared__ unsigned long long hist[256];
+  __shared__ unsigned long long state[2];
+  __shared__ unsigned long long shu[NT / 32];
   const int n = src.n;
-  // Pass 1: validation and the top key (max logit, lowest id).
+  // Pass 1: validation, the top key (max logit, lowest id), the finite count.
   uint64_t best = 0;
-  int bad = 0;
+  int bad = 0, finite = 0;
   for (int i = threadIdx.x; i < n; i += NT) {
     float v;
     uint64_t k;
     if (src.bad(i)) bad = 1;
-    if (src.get(i, v, k)) best = k > best ? k : best;
+    if (src.get(i, v, k)) {
+      best = k > best ? k : best;
+      ++finite;
+    }
   }
   best = block_max_u64<NT>(best, shk);
   bad = block_sum_i<NT>(bad, shi);
+  finite = block_sum_i<NT>(finite, shi);
   const int top_id = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
   if (bad) {
     if (threadIdx.x == 0) { *out_tok = top_id; if (status) *status = -1; }
@@ -446,76 +520,37 @@ __device__ void sample_row(const Src& src, const SampleParams p, int32_t* out_to
   }
   const float mx = key_value(best);
   const float inv_t = 1.0f / p.temperature;
-
-  // Key-space bisection helpers.
-  auto count_ge = [&](uint64_t K) -> int {
-    int c = 0;
+  auto one = [](float) -> unsigned long long { return 1ull; };
+  auto mass = [&](float v) -> unsigned long long { return __float2ull_rn(__expf((v - mx) * inv_t) * kMassScale); };
+  auto mass_ge = [&](uint64_t K) -> unsigned long long {
+    unsigned long long m = 0;
     for (int i = threadIdx.x; i < n; i += NT) {
       float v;
       uint64_t k;
-      c += src.get(i, v, k) && k >= K;
+      if (src.get(i, v, k) && k >= K) m += mass(v);
     }
-    return block_sum_i<NT>(c, shi);
-  };
-  auto mass_ge = [&](uint64_t K, uint64_t floor_key) -> double {
-    double m = 0.0;
-    for (int i = threadIdx.x; i < n; i += NT) {
-      float v;
-      uint64_t k;
-      if (src.get(i, v, k) && k >= K && k >= floor_key) m += (double)__expf((v - mx) * inv_t);
-    }
-    return block_sum_f64<NT>(m, shd);
+    return block_sum_u64<NT>(m, shu);
   };
 
-  // Top-k: the k-th largest key (largest K with count_ge(K) >= k).
+  // Top-k: the k-th largest key.
   uint64_t kfloor = 0;
-  if (p.top_k > 0 && count_ge(0) > p.top_k) {
-    uint64_t lo = 0, hi = best;  // invariant: count_ge(lo) >= k, answer in [lo, hi]
-    while (lo < hi) {
-      const uint64_t mid = lo + (hi - lo + 1) / 2;
-      if (count_ge(mid) >= p.top_k) lo = mid; else hi = mid - 1;
-    }
-    kfloor = lo;
-  }
-  const double total = mass_ge(0, kfloor);
+  if (p.top_k > 0 && finite > p.top_k) kfloor = select_desc<NT>(src, 0, one, (unsigned long long)p.top_k, false, hist, state);
+  const unsigned long long total = mass_ge(kfloor);
 
-  // Top-p: smallest prefix with cumulative >= top_p * total
-  //   == the largest K with mass_ge(K) >= threshold.
+  // Top-p: the smallest prefix whose cumulative mass reaches top_p * total.
   uint64_t pfloor = kfloor;
+  unsigned long long retained = total;
   if (p.top_p > 0.f && p.top_p < 1.f) {
-    const double thr = (double)p.top_p * total;
-    uint64_t lo = kfloor, hi = best;
-    while (lo < hi) {
-      const uint64_t mid = lo + (hi - lo + 1) / 2;
-      if (mass_ge(mid, kfloor) >= thr) lo = mid; else hi = mid - 1;
-    }
-    pfloor = lo;
+    unsigned long long thr = (unsigned long long)ceil((double)p.top_p * (double)total);
+    if (thr < 1ull) thr = 1ull;
+    pfloor = select_desc<NT>(src, kfloor, mass, thr, false, hist, state);
+    retained = mass_ge(pfloor);
   }
-  const double retained = mass_ge(pfloor, pfloor);
 
-  // Draw: the first sorted token whose inclusive cumulative mass exceeds
-  // u * retained  == the largest K with mass_ge(K) > target; if rounding leaves
-  // none, the final nucleus member closes the gap.
+  // Draw: the first sorted token whose inclusive cumulative mass exceeds u * retained.
   const double u = counter_unit(p.seed, p.sample_index);
-  const double target = u * retained;
-  uint64_t lo = pfloor, hi = best;
-  if (!(mass_ge(lo, pfloor) > target)) {
-    hi = lo;
-  } else {
-    while (lo < hi) {
-      const uint64_t mid = lo + (hi - lo + 1) / 2;
-      if (mass_ge(mid, pfloor) > target) lo = mid; else hi = mid - 1;
-    }
-  }
-  // `lo` is a key threshold; the selected token is the smallest existing key >= lo.
-  uint64_t sel = ~0ull;
-  for (int i = threadIdx.x; i < n; i += NT) {
-    float v;
-    uint64_t k;
-    if (src.get(i, v, k) && k >= lo && k < sel) sel = k;
-  }
-  // block min via max of complements
-  sel = ~block_max_u64<NT>(~sel, shk);
+  const unsigned long long target = (unsigned long long)floor(u * (double)retained);
+  const uint64_t sel = select_desc<NT>(src, pfloor, mass, target, true, hist, state);
   if (threadIdx.x == 0) {
     *out_tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(sel & 0xFFFFFFFFull));
     if (status) *status = 0;
