@@ -137,19 +137,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       float acc[BN];
 #pragma unroll
       for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+      const float* sa_row = sa + (size_t)rr * lds_a;
+      const float* sb_blk = sb + (size_t)(n0 / 128) * ksb;
+      float scale_next = sa_row[0] * sb_blk[0];
       for (int kb = 0; kb < num_kb; ++kb, ++tb) {
         const int b = tb & 1;
+        // this block's scale was loaded during the previous block; the next
+        // one is requested before waiting for the accumulator
+        const float scale = scale_next;
+        if (kb + 1 < num_kb) scale_next = sa_row[kb + 1] * sb_blk[kb + 1];
         if (!mbar_wait(&tfull[b], (tb >> 1) & 1, 34)) { ok = false; break; }
         tc_fence_after();
-        const float scale = sa[(size_t)rr * lds_a + kb] * sb[(size_t)(n0 / 128) * ksb + kb];
         const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + b * BN;
+        // two halves of 64 columns: four loads in flight per wait
 #pragma unroll
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(taddr + c, r);
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t r[64];
+          tmem_ld_32x32b_x16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_ld_32x32b_x16(taddr + c + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+          tmem_ld_32x32b_x16(taddr + c + 32, *reinterpret_cast<uint32_t(*)[16]>(r + 32));
+          tmem_ld_32x32b_x16(taddr + c + 48, *reinterpret_cast<uint32_t(*)[16]>(r + 48));
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[c + j] = fmaf(__uint_as_float(r[j]), scale, acc[c + j]);
+          for (int j = 0; j < 64; ++j) acc[c + j] = fmaf(__uint_as_float(r[j]), scale, acc[c + j]);
         }
         tc_fence_before();
         mbar_arrive(&tempty[b]);
