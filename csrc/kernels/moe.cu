@@ -29,18 +29,26 @@ namespace moe {
 constexpr int kMaxExperts = 64;
 constexpr int kMaxTopK = 8;
 
+// One CTA of kRouteThreads per token: each thread takes every 128th group of
+// 8 hidden features, the per-expert partial logits are reduced through shared
+// memory, and thread 0 does the softmax and the top-k (ties: lowest expert id).
+constexpr int kRouteThreads = 128;
+
 template <int E>
-__global__ void route_kernel(const __nv_bfloat16* __restrict__ h, const float* __restrict__ wr,
-                             const float* __restrict__ bias, int T, int H, int topk, int32_t* __restrict__ ids,
-                             float* __restrict__ weights) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  const __nv_bfloat16* x = h + (size_t)warp * H;
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const __nv_bfloat16* __restrict__ h,
+                                                              const float* __restrict__ wr,
+                                                              const float* __restrict__ bias, int T, int H, int topk,
+                                                              int32_t* __restrict__ ids, float* __restrict__ weights) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float part[kRouteThreads / 32][E];
+  const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const __nv_bfloat16* x = h + (size_t)t * H;
   float acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  for (int i = lane * 8; i < H; i += 256) {
+  for (int i = threadIdx.x * 8; i < H; i += kRouteThreads * 8) {
     const uint4 v = *reinterpret_cast<const uint4*>(x + i);
     const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
     float xf[8];
@@ -55,21 +63,26 @@ __global__ void route_kernel(const __nv_bfloat16* __restrict__ h, const float* _
     }
   }
 #pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = warp_sum(acc[e]);
-  if (lane != 0) return;
+  for (int e = 0; e < E; ++e) {
+    acc[e] = warp_sum(acc[e]);
+    if (lane == 0) part[warp][e] = acc[e];
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  float logit[E];
   float mx = -INFINITY;
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    if (bias != nullptr) acc[e] += bias[e];
-    mx = fmaxf(mx, acc[e]);
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kRouteThreads / 32; ++w) a += part[w][e];
+    if (bias != nullptr) a += bias[e];
+    logit[e] = a;
+    mx = fmaxf(mx, a);
   }
   float p[E];
-  float sum = 0.f;
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    p[e] = __expf(acc[e] - mx);
-    sum += p[e];
-  }
+  for (int e = 0; e < E; ++e) p[e] = __expf(logit[e] - mx);
   // top-k by probability (ties: lowest expert id), renormalised over the k kept
   int sel[kMaxTopK];
   float ws = 0.f;
@@ -85,23 +98,21 @@ __global__ void route_kernel(const __nv_bfloat16* __restrict__ h, const float* _
     ws += p[best];
   }
   for (int k = 0; k < topk; ++k) {
-    ids[(size_t)warp * topk + k] = sel[k];
-    weights[(size_t)warp * topk + k] = p[sel[k]] / ws;
+    ids[(size_t)t * topk + k] = sel[k];
+    weights[(size_t)t * topk + k] = p[sel[k]] / ws;
   }
-  (void)sum;
 }
 
 void route(const void* h, const float* wr, const float* bias, int T, int H, int E, int topk, int32_t* ids,
            float* weights, cudaStream_t s) {
   if (T <= 0) return;
-  const int threads = 256;
-  const int blocks = (T * 32 + threads - 1) / threads;
   auto hp = reinterpret_cast<const __nv_bfloat16*>(h);
+  const dim3 grid(T), block(kRouteThreads);
   switch (E) {
-    case 2: route_kernel<2><<<blocks, threads, 0, s>>>(hp, wr, bias, T, H, topk, ids, weights); break;
-    case 4: route_kernel<4><<<blocks, threads, 0, s>>>(hp, wr, bias, T, H, topk, ids, weights); break;
-    case 8: route_kernel<8><<<blocks, threads, 0, s>>>(hp, wr, bias, T, H, topk, ids, weights); break;
-    case 16: route_kernel<16><<<blocks, threads, 0, s>>>(hp, wr, bias, T, H, topk, ids, weights); break;
+    case 2: launch_k(route_kernel<2>, grid, block, 0, s, 1, hp, wr, bias, T, H, topk, ids, weights); break;
+    case 4: launch_k(route_kernel<4>, grid, block, 0, s, 1, hp, wr, bias, T, H, topk, ids, weights); break;
+    case 8: launch_k(route_kernel<8>, grid, block, 0, s, 1, hp, wr, bias, T, H, topk, ids, weights); break;
+    case 16: launch_k(route_kernel<16>, grid, block, 0, s, 1, hp, wr, bias, T, H, topk, ids, weights); break;
     default: break;
   }
 }
