@@ -139,10 +139,42 @@ __device__ __forceinline__ int bt_page(const PrefillArgs& a, int r, int idx) {
   return p;
 }
 
+// One work item: (query tile qb, row r, KV head h).  Items are numbered
+// longest tile first; an item whose tile starts past the row's queries is empty.
+struct Item {
+  bool live;
+  int r, h, qs, n, t0, pos0, kmax, nkb;
+};
+
+__device__ __forceinline__ Item item_of(const PrefillArgs& a, int w, int nq, int QT) {
+  Item it;
+  const int per = a.rows * a.Hkv;
+  const int qb = nq - 1 - w / per;
+  const int rem = w % per;
+  it.r = rem / a.Hkv;
+  it.h = rem % a.Hkv;
+  it.qs = a.q_start[it.r];
+  it.n = a.q_start[it.r + 1] - it.qs;
+  it.t0 = qb * QT;
+  it.live = it.t0 < it.n;
+  const int L = a.seq_lens[it.r];
+  it.pos0 = L - it.n;                                   // position of the row's first query
+  it.kmax = it.pos0 + min(it.n, it.t0 + QT) - 1;        // last key any query of the tile sees
+  it.nkb = it.live ? it.kmax / KB + 1 : 0;
+  return it;
+}
+
+// Persistent: CTA c takes items c, c + gridDim.x, ...  The K / V ring, the S
+// buffers and the P buffers are indexed by a block counter that runs across
+// the CTA's items, so the next item's Q, K and V loads and its first S MMA
+// overlap the previous item's last softmax and epilogue.  Q is reloaded once
+// the previous item's last S MMA is done (q_empty); the first P . V of an item
+// overwrites O only after the softmax warps have read the previous item's O
+// (o_empty).
 __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tq,
                                                             const __grid_constant__ CUtensorMap tk,
                                                             const __grid_constant__ CUtensorMap tv, PrefillArgs a,
-                                                            int G) {
+                                                            int G, int nq) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -157,30 +189,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   uint64_t* s_empty = bars + 11;   // [2]
   uint64_t* p_full = bars + 13;    // [2] per P buffer
   uint64_t* pv_done = bars + 15;   // [2] per P buffer: P . V of that buffer's block done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* q_empty = bars + 17;   // the item's last S MMA is done: Q may be reloaded
+  uint64_t* o_empty = bars + 18;   // the softmax warps have read the item's O
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int QT = 128 / G;                         // query tokens per tile
-  const int r = blockIdx.y, h = blockIdx.z;
-  const int qb = gridDim.x - 1 - blockIdx.x;      // longest tiles first
-  const int qs = a.q_start[r];
-  const int n = a.q_start[r + 1] - qs;
-  const int t0 = qb * QT;
-  if (t0 >= n) {                                  // uniform for the CTA: before any barrier
-    if (threadIdx.x == 0) mark(a, 1001);
-    return;
-  }
-  const int L = a.seq_lens[r];
-  const int pos0 = L - n;                         // position of the row's first query
-  const int kmax = pos0 + min(n, t0 + QT) - 1;    // last key any query of the tile sees
-  const int nkb = kmax / KB + 1;
+  const int W = nq * a.rows * a.Hkv;
 
-  if (threadIdx.x == 0) mark(a, 1);
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(o_empty, 256);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
@@ -204,41 +227,49 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
-  if (threadIdx.x == 0) mark(a, 2);
 
   if (warp == 0) {
     if (lane == 0) {
-      // Q: G heads x QT tokens, each a [QT][64] box per 64-column half
-      mbar_arrive_expect_tx(q_full, kTile);
-      for (int g = 0; g < G; ++g)
-        for (int half = 0; half < 2; ++half)
-          tma_load_2d(smem + kOffQ + half * kHalf + g * QT * 128, &tq, q_full, (h * G + g) * D + half * 64, qs + t0);
-      for (int j = 0; j < nkb; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        int pages[8];
+      bool ok = true;
+      int gb = 0, ni = 0;   // blocks and items this CTA has loaded
+      for (int w = blockIdx.x; w < W && ok; w += gridDim.x) {
+        const Item it = item_of(a, w, nq, QT);
+        if (!it.live) continue;
+        // Q: G heads x QT tokens, each a [QT][64] box per 64-column half
+        if (!mbar_wait(q_empty, (ni & 1) ^ 1, 20)) break;
+        mbar_arrive_expect_tx(q_full, kTile);
+        for (int g = 0; g < G; ++g)
+          for (int half = 0; half < 2; ++half)
+            tma_load_2d(smem + kOffQ + half * kHalf + g * QT * 128, &tq, q_full, (it.h * G + g) * D + half * 64,
+                        it.qs + it.t0);
+        ++ni;
+        for (int j = 0; j < it.nkb; ++j, ++gb) {
+          const int s = gb & 1;
+          const uint32_t ph = ((gb >> 1) & 1) ^ 1;
+          int pages[8];
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          const int idx = j * 8 + p;
-          pages[p] = idx * PAGE <= kmax ? bt_page(a, r, idx) : 0;   // past the last key: the zero page
-        }
-        if (!mbar_wait(&k_empty[s], ph, 21)) break;
-        mbar_arrive_expect_tx(&k_full[s], kTile);
+          for (int p = 0; p < 8; ++p) {
+            const int idx = j * 8 + p;
+            pages[p] = idx * PAGE <= it.kmax ? bt_page(a, it.r, idx) : 0;   // past the last key: the zero page
+          }
+          if (!mbar_wait(&k_empty[s], ph, 21)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[s], kTile);
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          const int row = (pages[p] * a.Hkv + h) * PAGE;
-          uint8_t* dst = smem + kOffK + s * kTile + p * 2048;
-          tma_load_2d(dst, &tk, &k_full[s], 0, row);
-          tma_load_2d(dst + kHalf, &tk, &k_full[s], 64, row);
-        }
-        if (!mbar_wait(&v_empty[s], ph, 22)) break;
-        mbar_arrive_expect_tx(&v_full[s], kTile);
+          for (int p = 0; p < 8; ++p) {
+            const int row = (pages[p] * a.Hkv + it.h) * PAGE;
+            uint8_t* dst = smem + kOffK + s * kTile + p * 2048;
+            tma_load_2d(dst, &tk, &k_full[s], 0, row);
+            tma_load_2d(dst + kHalf, &tk, &k_full[s], 64, row);
+          }
+          if (!mbar_wait(&v_empty[s], ph, 22)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[s], kTile);
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          const int row = (pages[p] * a.Hkv + h) * PAGE;
-          uint8_t* dst = smem + kOffV + s * kTile + p * 2048;
-          tma_load_2d(dst, &tv, &v_full[s], 0, row);
-          tma_load_2d(dst + kHalf, &tv, &v_full[s], 64, row);
+          for (int p = 0; p < 8; ++p) {
+            const int row = (pages[p] * a.Hkv + it.h) * PAGE;
+            uint8_t* dst = smem + kOffV + s * kTile + p * 2048;
+            tma_load_2d(dst, &tv, &v_full[s], 0, row);
+            tma_load_2d(dst + kHalf, &tv, &v_full[s], 64, row);
+          }
         }
       }
     }
@@ -246,11 +277,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128);              // Q . K^T, both K-major
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128) | (1u << 16); // P . V, V MN-major
-      bool ok = mbar_wait(q_full, 0, 23);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j >> 1) & 1, 24)) return false;
-        if (!mbar_wait(&s_empty[s], ((j >> 1) & 1) ^ 1, 25)) return false;
+      bool ok = true;
+      int gb = 0, ni = 0;
+      auto issue_s = [&](int g) -> bool {
+        const int s = g & 1;
+        if (!mbar_wait(&k_full[s], (g >> 1) & 1, 24)) return false;
+        if (!mbar_wait(&s_empty[s], ((g >> 1) & 1) ^ 1, 25)) return false;
         tc_fence_after();
         const uint32_t dS = tmem + (s ? kColsS1 : kColsS0);
         const uint32_t qa = sbase + kOffQ, kb = sbase + kOffK + s * kTile;
@@ -264,18 +296,36 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
         umma_commit(&s_full[s]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < nkb && ok; ++j) {
-        if (j + 1 < nkb && !issue_s(j + 1)) break;
-        const int s = j & 1;
-        if (!mbar_wait(&p_full[s], (j >> 1) & 1, 26) || !mbar_wait(&v_full[s], (j >> 1) & 1, 27)) break;
+      for (int w = blockIdx.x; w < W && ok; w += gridDim.x) {
+        const Item it = item_of(a, w, nq, QT);
+        if (!it.live) continue;
+        if (!mbar_wait(q_full, ni & 1, 23)) break;
         tc_fence_after();
-        const uint32_t pa = sbase + kOffP + s * kTile, vb = sbase + kOffV + s * kTile;
+        if (!issue_s(gb)) break;
+        if (it.nkb == 1) umma_commit(q_empty);
+        for (int j = 0; j < it.nkb; ++j) {
+          const int g = gb + j;
+          if (j + 1 < it.nkb) {
+            if (!issue_s(g + 1)) { ok = false; break; }
+            if (j + 2 == it.nkb) umma_commit(q_empty);    // the item's last S MMA has been issued
+          }
+          const int s = g & 1;
+          if (!mbar_wait(&p_full[s], (g >> 1) & 1, 26) || !mbar_wait(&v_full[s], (g >> 1) & 1, 27)) {
+            ok = false;
+            break;
+          }
+          // the first P . V of an item overwrites O: the previous item's O has been read
+          if (j == 0 && !mbar_wait(o_empty, (ni & 1) ^ 1, 28)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t pa = sbase + kOffP + s * kTile, vb = sbase + kOffV + s * kTile;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16_ss(tmem + kColsO, kmajor_desc(pa, kk), mnmajor_desc(vb, kk), idesc_o, (j > 0 || kk > 0));
-        umma_commit(&v_empty[s]);
-        umma_commit(&pv_done[s]);
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16_ss(tmem + kColsO, kmajor_desc(pa, kk), mnmajor_desc(vb, kk), idesc_o, (j > 0 || kk > 0));
+          umma_commit(&v_empty[s]);
+          umma_commit(&pv_done[s]);
+        }
+        gb += it.nkb;
+        ++ni;
       }
     }
   } else {
@@ -286,163 +336,179 @@ __global__ void __launch_bounds__(kThreadsTc, 1) prefill_tc_kernel(const __grid_
     const int c0 = half * 64;
     const int row = quad * 32 + lane;
     const int g = row / QT, t = row % QT;
-    const int tok = t0 + t;
-    const bool valid = tok < n;
-    const int pos = pos0 + tok;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const float sl2 = a.scale_log2;
     float* red = reinterpret_cast<float*>(smem + kOffRed);   // [2][128]
     volatile int* flag = reinterpret_cast<volatile int*>(smem + kOffFlag);   // [2][4]
     const int bar_id = 1 + quad;                             // the two warps of this quadrant
-    float m_used = -INFINITY, l = 0.f;
-    bool ok = true;
     uint8_t* prow0 = smem + kOffP + half * kHalf + row * 128;
-    // The two warps of a quadrant meet at named barriers twice per block.  A
-    // failed (timed-out) wait never makes one of them leave alone: it only
-    // marks the warp unsound, both warps publish their state at the next
-    // exchange and leave the loop there together, so neither is left at a
-    // barrier the other will not reach.
-    for (int j = 0; j < nkb; ++j) {
-      const int s = j & 1;
-      // every wait before a warp-collective TMEM access is made warp-uniform:
-      // tcgen05.ld / st are .sync.aligned and must not run in a diverged warp
-      if (ok && !__all_sync(0xffffffffu, mbar_wait(&s_full[s], (j >> 1) & 1, 28))) ok = false;
-      float x[64];
-      float pm = -INFINITY;
-      if (ok) {
-        tc_fence_after();
-        // this thread's 64 scores of its row: two TMEM loads in flight, one wait
-        uint32_t v0[32], v1[32];
-        const uint32_t srow = tmem + lane_off + (s ? kColsS1 : kColsS0) + c0;
-        tmem_ld_32x32b_x32(srow, v0);
-        tmem_ld_32x32b_x32(srow + 32, v1);
-        tmem_wait_ld();
+    bool ok = true;
+    int gb = 0;
+    for (int w = blockIdx.x; w < W && ok; w += gridDim.x) {
+      const Item it = item_of(a, w, nq, QT);
+      if (!it.live) continue;
+      const int tok = it.t0 + t;
+      const bool valid = tok < it.n;
+      const int pos = it.pos0 + tok;
+      const int nkb = it.nkb;
+      float m_used = -INFINITY, l = 0.f;
+      // The two warps of a quadrant meet at named barriers twice per block.  A
+      // failed (timed-out) wait never makes one of them leave alone: it only
+      // marks the warp unsound, both warps publish their state at the next
+      // exchange and leave the loop there together, so neither is left at a
+      // barrier the other will not reach.
+      for (int j = 0; j < nkb; ++j) {
+        const int gj = gb + j;
+        const int s = gj & 1;
+        // every wait before a warp-collective TMEM access is made warp-uniform:
+        // tcgen05.ld / st are .sync.aligned and must not run in a diverged warp
+        if (ok && !__all_sync(0xffffffffu, mbar_wait(&s_full[s], (gj >> 1) & 1, 28))) ok = false;
+        float x[64];
+        float pm = -INFINITY;
+        if (ok) {
+          tc_fence_after();
+          // this thread's 64 scores of its row: two TMEM loads in flight, one wait
+          uint32_t v0[32], v1[32];
+          const uint32_t srow = tmem + lane_off + (s ? kColsS1 : kColsS0) + c0;
+          tmem_ld_32x32b_x32(srow, v0);
+          tmem_ld_32x32b_x32(srow + 32, v1);
+          tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          x[e] = __uint_as_float(v0[e]);
-          x[32 + e] = __uint_as_float(v1[e]);
-        }
-        tc_fence_before();
-        mbar_arrive(&s_empty[s]);     // the MMA warp may compute S_{j+2} into this buffer
-        // row maximum of the raw scores (scale > 0 commutes with max); the
-        // mask is applied only on blocks that cross this row's causal limit
-        const int key0 = j * KB + c0;
-        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (valid && key0 + 63 <= pos) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            if (!valid || key0 + c > pos) x[c] = -INFINITY;
-            m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+          for (int e = 0; e < 32; ++e) {
+            x[e] = __uint_as_float(v0[e]);
+            x[32 + e] = __uint_as_float(v1[e]);
           }
+          tc_fence_before();
+          mbar_arrive(&s_empty[s]);     // the MMA warp may compute S_{j+2} into this buffer
+          // row maximum of the raw scores (scale > 0 commutes with max); the
+          // mask is applied only on blocks that cross this row's causal limit
+          const int key0 = j * KB + c0;
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+          if (valid && key0 + 63 <= pos) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+              if (!valid || key0 + c > pos) x[c] = -INFINITY;
+              m4[c & 3] = fmaxf(m4[c & 3], x[c]);
+            }
+          }
+          pm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         }
-        pm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        // the row maximum over both halves, and both warps' state, through shared memory
+        red[half * 128 + row] = pm;
+        if (lane == 0) flag[half * 4 + quad] = ok ? 1 : 0;
+        bar_sync_n(bar_id, 64);
+        const bool both_ok = flag[quad] != 0 && flag[4 + quad] != 0;
+        const float mx = fmaxf(red[row], red[128 + row]) * sl2;   // log2 units
+        bar_sync_n(bar_id, 64);                                   // both read before the next write
+        if (!both_ok) {
+          ok = false;
+          break;
+        }
+        // P buffer gj % 2 is free once P . V of block gj - 2 is done (that block
+        // may belong to the previous item); a rescale of O also needs P . V of
+        // this item's previous block done
+        if (gj > 1 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[s], ((gj >> 1) & 1) ^ 1, 29))) {
+          ok = false;
+          continue;   // leave together with the partner warp at the next exchange
+        }
+        uint8_t* prow = prow0 + s * kTile;
+        // The rescale touches O through TMEM with warp-collective instructions,
+        // so the whole warp rescales when any of its rows needs to; both warps
+        // of a quadrant hold the same rows and the same maxima, so they decide
+        // alike, and rows whose maximum moved less rescale by their own factor.
+        if (__any_sync(0xffffffffu, mx > m_used + kRescaleThreshold)) {
+          if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[s ^ 1], ((gj - 1) >> 1) & 1, 31))) {
+            ok = false;
+            continue;
+          }
+          const float m_new = fmaxf(m_used, mx);
+          const float alpha = m_used == -INFINITY ? (m_new == -INFINITY ? 1.f : 0.f) : ex2_approx(m_used - m_new);
+          if (j > 0) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 64; c += 32) {
+              uint32_t v[32];
+              tmem_ld_32x32b_x32(tmem + lane_off + kColsO + c0 + c, v);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+              tmem_st_32x32b_x32(tmem + lane_off + kColsO + c0 + c, v);
+            }
+            tmem_wait_st();
+          }
+          l *= alpha;
+          m_used = m_new;
+        }
+        // P = exp2(s * scale_log2 - m) as bf16 into this half of the swizzled
+        // [key-half][row][128 B] tile
+        const float neg_m = m_used == -INFINITY ? 0.f : -m_used;   // all-masked row: every p is 0
+        float l2[2] = {0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          uint32_t wv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = ex2_approx(fmaf(x[c + 2 * e], sl2, neg_m));
+            const float p1 = ex2_approx(fmaf(x[c + 2 * e + 1], sl2, neg_m));
+            l2[0] += p0;
+            l2[1] += p1;
+            wv[e] = pack_bf16x2(p0, p1);
+          }
+          const int chunk = c >> 3;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+        l += l2[0] + l2[1];
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(&p_full[s]);
       }
-      // the row maximum over both halves, and both warps' state, through shared memory
-      red[half * 128 + row] = pm;
+      // O is complete once P . V of the item's last block is done.  That wait,
+      // too, can only fail: its outcome and the row sum are exchanged with the
+      // partner warp, and both act on the joint state (both write the item's
+      // output and go on, or both leave), so neither is ever left alone at a
+      // named barrier of the next item.
+      const int gl = gb + nkb - 1;
+      if (ok && !__all_sync(0xffffffffu, mbar_wait(&pv_done[gl & 1], (gl >> 1) & 1, 30))) ok = false;
+      red[half * 128 + row] = l;
       if (lane == 0) flag[half * 4 + quad] = ok ? 1 : 0;
       bar_sync_n(bar_id, 64);
-      const bool both_ok = flag[quad] != 0 && flag[4 + quad] != 0;
-      const float mx = fmaxf(red[row], red[128 + row]) * sl2;   // log2 units
-      bar_sync_n(bar_id, 64);                                   // both read before the next write
-      if (!both_ok) {
-        ok = false;
-        break;
-      }
-      // P buffer j % 2 is free once P . V of block j - 2 is done; a rescale of O
-      // also needs P . V of block j - 1 done
-      if (j > 1 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[s], ((j >> 1) & 1) ^ 1, 29))) {
-        ok = false;
-        continue;   // leave together with the partner warp at the next exchange
-      }
-      uint8_t* prow = prow0 + s * kTile;
-      // The rescale touches O through TMEM with warp-collective instructions,
-      // so the whole warp rescales when any of its rows needs to; both warps
-      // of a quadrant hold the same rows and the same maxima, so they decide
-      // alike, and rows whose maximum moved less rescale by their own factor.
-      if (__any_sync(0xffffffffu, mx > m_used + kRescaleThreshold)) {
-        if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&pv_done[s ^ 1], ((j - 1) >> 1) & 1, 31))) {
-          ok = false;
-          continue;
-        }
-        const float m_new = fmaxf(m_used, mx);
-        const float alpha = m_used == -INFINITY ? (m_new == -INFINITY ? 1.f : 0.f) : ex2_approx(m_used - m_new);
-        if (j > 0) {
-          tc_fence_after();
+      const float l_row = red[row] + red[128 + row];
+      ok = flag[quad] != 0 && flag[4 + quad] != 0;
+      bar_sync_n(bar_id, 64);                                     // both read before the next item's writes
+      if (ok) {
+        tc_fence_after();
+        const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+        __nv_bfloat16* dst = a.out + (int64_t)(it.qs + tok) * a.out_ld + (it.h * G + g) * D + c0;
 #pragma unroll 1
-          for (int c = 0; c < 64; c += 32) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tmem + lane_off + kColsO + c0 + c, v);
-            tmem_wait_ld();
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem + lane_off + kColsO + c0 + c, v);
+          tmem_wait_ld();
+          if (valid) {
+            uint32_t pk[16];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            tmem_st_32x32b_x32(tmem + lane_off + kColsO + c0 + c, v);
+            for (int e = 0; e < 16; ++e)
+              pk[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * inv, __uint_as_float(v[2 * e + 1]) * inv);
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) d4[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
           }
-          tmem_wait_st();
         }
-        l *= alpha;
-        m_used = m_new;
+        tc_fence_before();
+        mbar_arrive(o_empty);          // the next item's first P . V may overwrite O
       }
-      // P = exp2(s * scale_log2 - m) as bf16 into this half of the swizzled
-      // [key-half][row][128 B] tile
-      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;   // all-masked row: every p is 0
-      float l2[2] = {0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 64; c += 8) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(fmaf(x[c + 2 * e], sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(x[c + 2 * e + 1], sl2, neg_m));
-          l2[0] += p0;
-          l2[1] += p1;
-          w[e] = pack_bf16x2(p0, p1);
-        }
-        const int chunk = c >> 3;
-        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      l += l2[0] + l2[1];
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(&p_full[s]);
-      if (threadIdx.x == 64) mark(a, 10 + j);
-    }
-    // the row sum over both halves (both warps of the quadrant arrive here
-    // exactly once: they leave the loop at the same exchange or finish it)
-    red[half * 128 + row] = l;
-    bar_sync_n(bar_id, 64);
-    const float l_row = red[row] + red[128 + row];
-    if (__all_sync(0xffffffffu, ok && mbar_wait(&pv_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, 30))) {
-      tc_fence_after();
-      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
-      __nv_bfloat16* dst = a.out + (int64_t)(qs + tok) * a.out_ld + (h * G + g) * D + c0;
-#pragma unroll 1
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + kColsO + c0 + c, v);
-        tmem_wait_ld();
-        if (valid) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            pk[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * inv, __uint_as_float(v[2 * e + 1]) * inv);
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) d4[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
-        }
-      }
+      gb += nkb;
     }
   }
   tc_fence_before();
-  if (threadIdx.x == 64) mark(a, 1000);
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-  if (threadIdx.x == 32) mark(a, 1001);
 }
 
 static std::mutex g_mu;
@@ -478,8 +544,16 @@ void prefill_tc(const PrefillArgs& a, const CUtensorMap& tk, const CUtensorMap& 
     cudaFuncSetAttribute(tc::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmem);
     attr = true;
   }
-  dim3 grid((a.max_q_len + QT - 1) / QT, a.rows, a.Hkv);
-  launch_k(tc::prefill_tc_kernel, grid, dim3(tc::kThreadsTc), tc::kSmem, stream, 1, tq, tk, tv, a, G);
+  const int nq = (a.max_q_len + QT - 1) / QT;
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int items = nq * a.rows * a.Hkv;
+  const int grid = items < sms ? items : sms;   // persistent: one CTA per SM (224 KB of shared memory)
+  launch_k(tc::prefill_tc_kernel, dim3(grid), dim3(tc::kThreadsTc), tc::kSmem, stream, 1, tq, tk, tv, a, G, nq);
 }
 
 }  // namespace attn
