@@ -196,8 +196,10 @@ class FusedTPComm(TPComm):
             self.ng_index += 1
         self.calls += 1
         self.C.norm_gather(x, residual, w, eps, self.ng_dst[b], self.ng_flags, self.ng_state, self.rank)
-        full = self.world * rows * self.hidden
-        return self.ng_buf[b * full:(b + 1) * full].view(self.world * rows, self.hidden)
+        # buffer b starts at b * world * ng_rows rows (sized for the largest
+        # step); this step's gathered rows are its first world * rows rows
+        base = b * self.world * self.ng_rows * self.hidden
+        return self.ng_buf[base: base + self.world * rows * self.hidden].view(self.world * rows, self.hidden)
 
     def gemm_reduce_scatter(self, A: torch.Tensor, B: torch.Tensor, out_local: torch.Tensor) -> bool:
         """out_local [M / world, hidden] = this rank's rows of the sum over

@@ -28,8 +28,16 @@ def _spec():
 
 
 def _checkpoint(spec):
+    """bf16-representable random weights.  MoE routers are scaled up so the
+    top-2 choice has clear margins: with random routers, bf16 activations flip
+    near-tied expert choices against the fp32 oracle, and one flipped token
+    moves the logits far beyond the near-tie tolerance whatever the kernels."""
     from lunaflux_b200.models.weights import random_checkpoint
-    return {k: v.bfloat16().float() for k, v in random_checkpoint(spec, 11).items()}
+    ck = random_checkpoint(spec, 11)
+    for k in ck:
+        if k.endswith("block_sparse_moe.gate.weight"):
+            ck[k] = ck[k] * 16.0
+    return {k: v.bfloat16().float() for k, v in ck.items()}
 
 
 def _prompts(spec):
