@@ -887,6 +887,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // thread -> (row, 4 consecutive output features): gate cols g*64 + j,
         // up cols g*64 + 32 + j of the tile
         constexpr int kQuads = BN / 2 / 4;
+        // unrolled: several iterations' remote loads in flight per thread
+#pragma unroll 4
         for (int i = t; i < (r1 - r0) * kQuads; i += 128) {
           const int rl = r0 + i / kQuads;
           const int j = (i % kQuads) * 4;            // output feature within the tile
@@ -912,6 +914,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         qkv_rope_cluster<BN>(rope, red_base, c, r0, r1, mrow0, n0, M, reinterpret_cast<__nv_bfloat16*>(out), ldd, t);
       } else {
         constexpr int kQuads = BN / 4;
+        // unrolled: several iterations' remote loads in flight per thread
+#pragma unroll 4
         for (int i = t; i < (r1 - r0) * kQuads; i += 128) {
           const int rl = r0 + i / kQuads;
           const int col = (i % kQuads) * 4;
