@@ -450,11 +450,38 @@ __device__ uint64_t select_desc(const Src& src, uint64_t floor_key, WFn wfn, uns
     __syncthreads();
     const int sh = 8 * d;
     const uint64_t hi_mask = d == 7 ? 0ull : (~0ull << (sh + 8));
-    for (int i = threadIdx.x; i < n; i += NT) {
-      float v;
-      uint64_t k;
-      if (src.get(i, v, k) && k >= floor_key && (k & hi_mask) == P)
-        atomicAdd(&hist[(k >> sh) & 255u], wfn(v));
+    if (d >= 6) {
+      // The top two key bytes (sign, exponent, leading mantissa bits) put most
+      // entries into a few bins: lanes of a warp with the same bin are summed
+      // by shuffles first and one of them adds the group's weight.
+      const int lane = threadIdx.x & 31;
+      for (int base = 0; base < n; base += NT) {
+        const int i = base + threadIdx.x;
+        float v;
+        uint64_t k;
+        int bin = 256;
+        unsigned long long wv = 0;
+        if (i < n && src.get(i, v, k) && k >= floor_key && (k & hi_mask) == P) {
+          bin = (int)((k >> sh) & 255u);
+          wv = wfn(v);
+        }
+        const unsigned m = __match_any_sync(0xffffffffu, bin);
+        unsigned long long sum = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const unsigned long long x = __shfl_sync(0xffffffffu, wv, j);
+          if ((m >> j) & 1u) sum += x;
+        }
+        if (bin < 256 && __ffs(m) - 1 == lane) atomicAdd(&hist[bin], sum);
+      }
+    } else {
+      // deeper bytes: only the few entries matching the chosen prefix remain
+      for (int i = threadIdx.x; i < n; i += NT) {
+        float v;
+        uint64_t k;
+        if (src.get(i, v, k) && k >= floor_key && (k & hi_mask) == P)
+          atomicAdd(&hist[(k >> sh) & 255u], wfn(v));
+      }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
