@@ -301,7 +301,7 @@ void partials_allreduce_ll(const at::Tensor& ws, int64_t splits, at::Tensor& D, 
 }
 
 void gemm_grouped(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const at::Tensor& groups,
-                  int64_t num_groups, int64_t epi) {
+                  int64_t num_groups, int64_t epi, int64_t align) {
   check_rowmajor(A, "A");
   check_rowmajor(D, "D");
   LF_CHECK(B.is_contiguous() && B.dim() == 3 && B.size(0) >= num_groups, "grouped B must be [groups, N, K]");
@@ -311,7 +311,8 @@ void gemm_grouped(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const
   LF_CHECK(D.size(0) == M && D.size(1) == (epi == 2 ? N / 2 : N), "grouped output shape");
   c10::cuda::CUDAGuard g(A.device());
   lf::gemm::GemmArgs a{A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, A.stride(0), K, D.stride(0)};
-  lf::gemm::run_grouped(a, groups.data_ptr<int32_t>(), (int)num_groups, (int)epi, stream());
+  LF_CHECK(align == 128 || align == 256, "grouped gemm: segments aligned to 128 or 256 rows");
+  lf::gemm::run_grouped(a, groups.data_ptr<int32_t>(), (int)num_groups, (int)epi, stream(), (int)align);
 }
 
 void moe_route(const at::Tensor& h, const at::Tensor& wr, c10::optional<at::Tensor> bias, int64_t topk,
@@ -326,11 +327,12 @@ void moe_route(const at::Tensor& h, const at::Tensor& wr, c10::optional<at::Tens
 }
 
 void moe_align(const at::Tensor& ids, int64_t T, int64_t topk, int64_t e0, int64_t El, at::Tensor& groups,
-               at::Tensor& perm, at::Tensor& slot) {
+               at::Tensor& perm, at::Tensor& slot, int64_t align) {
   LF_CHECK(El >= 1 && El <= 64, "1..64 local experts");
+  LF_CHECK(align == 128 || align == 256, "moe_align: segments aligned to 128 or 256 rows");
   c10::cuda::CUDAGuard g(ids.device());
   lf::moe::align(ids.data_ptr<int32_t>(), T, topk, e0, El, perm.numel(), groups.data_ptr<int32_t>(),
-                 perm.data_ptr<int32_t>(), slot.data_ptr<int32_t>(), stream());
+                 perm.data_ptr<int32_t>(), slot.data_ptr<int32_t>(), stream(), (int)align);
 }
 
 void moe_gather(const at::Tensor& h, const at::Tensor& perm, const at::Tensor& groups, int64_t El, int64_t topk,
@@ -645,7 +647,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_get_pair", []() { return lf::gemm::get_gemm_pair() != 0; });
   m.def("gemm_set_ll_fused", [](bool on) { lf::gemm::set_ll_gemm_fused(on ? 1 : 0); });
   m.def("gemm_allreduce", &gemm_allreduce);
-  m.def("gemm_grouped", &gemm_grouped);
+  m.def("gemm_grouped", &gemm_grouped, py::arg("A"), py::arg("B"), py::arg("D"), py::arg("groups"),
+        py::arg("num_groups"), py::arg("epi"), py::arg("align") = 128);
   m.def("gemm_fp8", &gemm_fp8);
   m.def("partials_allreduce", &partials_allreduce);
   m.def("gemm_allreduce_ll", &gemm_allreduce_ll);
@@ -657,7 +660,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("partials_allreduce_ll", &partials_allreduce_ll);
   m.def("act_quant", &act_quant);
   m.def("moe_route", &moe_route);
-  m.def("moe_align", &moe_align);
+  m.def("moe_align", &moe_align, py::arg("ids"), py::arg("T"), py::arg("topk"), py::arg("e0"), py::arg("El"),
+        py::arg("groups"), py::arg("perm"), py::arg("slot"), py::arg("align") = 128);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
   m.def("gemm_choose_bn", &gemm_choose_bn);

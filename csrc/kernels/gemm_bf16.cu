@@ -547,8 +547,12 @@ void partials_allreduce(const float* ws, int M, int N, int splits, const ArArgs&
   splitk_finalize_ar_kernel<<<grid, 256, 0, stream>>>(ws, M, N, splits, ar);
 }
 
-void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, cudaStream_t stream) {
+void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, cudaStream_t stream, int align) {
   if (a.M <= 0) return;
+  // segments of whole 256-row tiles: the CTA-pair kernel, one expert per tile
+  if (align == 256 && a.M % 256 == 0 && (epi == kStoreBf16 || epi == kSwiGLU) &&
+      run_pair(a, epi, stream, RopeArgs{}, groups, num_groups))
+    return;
   if (a.M % BM != 0) throw std::runtime_error("lunaflux grouped gemm: M_max must be a multiple of 128");
   if (a.K % 8 != 0 || a.N % 64 != 0) throw std::runtime_error("lunaflux grouped gemm: K % 8 and N % 64 required");
   const int bn = a.N % 256 == 0 && ((a.M / BM) * (a.N / 256) >= num_sms()) ? 256 : (a.N % 128 == 0 ? 128 : 64);

@@ -96,7 +96,9 @@ struct ArArgs {
 // Sum of `splits` fp32 [M, N] slabs in ws, then the sum over the group, into
 // the result region (the split-K finalize kernel with its fused all-reduce).
 void partials_allreduce(const float* ws, int M, int N, int splits, const ArArgs& ar, cudaStream_t stream);
-void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, cudaStream_t stream);
+// align: the segments' row multiple (128, or 256: CTA-pair tiles, one expert per 256-row tile).
+void run_grouped(const GemmArgs& a, const int* groups, int num_groups, int epi, cudaStream_t stream,
+                 int align = 128);
 // Result region = sum over the tensor-parallel group of this rank's A . B^T,
 // computed and all-reduced over NVLink by one kernel (split-K shapes: the GEMM
 // and the finalize kernel that carries the all-reduce).  a.D is unused.

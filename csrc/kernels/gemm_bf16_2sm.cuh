@@ -132,7 +132,8 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                     void* __restrict__ out, int M, int N, int K, int ldd, const ColPlan cp, const RopeArgs rope) {
+                     void* __restrict__ out, int M, int N, int K, int ldd, const ColPlan cp, const RopeArgs rope,
+                     const int* __restrict__ groups, int num_groups) {
   static_assert(EPI == kStoreBf16 || EPI == kStoreF32 || EPI == kSwiGLU || EPI == kQkvRope, "plain or QKV epilogues");
   pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -183,7 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint64_t pol_b = l2_policy_evict_first();
   const uint32_t full_leader = peer_addr(smem_u32(full_bar), 0);
   int pre = 0;
-  if (warp == 0 && lane == 0 && pair_id < num_tiles) {
+  // (grouped mode: the group table is the previous kernel's output, so no early loads)
+  if (warp == 0 && lane == 0 && pair_id < num_tiles && groups == nullptr) {
     int n0, bn;
     tile_cols(cp, pair_id / num_m, n0, bn);
     const int half = bn / 2;
@@ -211,6 +213,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_cols(cp, tile / num_m, n0, bn);
         const int half = bn / 2;                       // B rows this CTA stages
         n0 += (int)rank * half;
+        if (groups != nullptr) {                       // the expert of this 256-row tile
+          const int g = group_of(groups, num_groups, (tile % num_m) * kTileM);
+          if (g < 0) continue;
+          n0 += g * N;
+        }
         const uint32_t stage_tx = 2u * (uint32_t)(BM * BK * 2 + half * BK * 2);   // both CTAs' bytes
         for (int kb = 0; kb < num_kb; ++kb) {
           const uint32_t sa = smem_u32(smem + stage * kStageBytes);
@@ -234,7 +241,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs, ++local) {
+      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+        // a skipped tile (grouped mode, past the last segment) uses no accumulator
+        if (groups != nullptr && group_of(groups, num_groups, (tile % num_m) * kTileM) < 0) continue;
         const int acc = local & 1;
         int n0_unused, bn;
         tile_cols(cp, tile / num_m, n0_unused, bn);
@@ -255,15 +264,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
         if (ok) umma_commit_pair(&tfull_bar[acc]);
+        ++local;
       }
     }
   } else {
     const int quad = warp & 3;
     const uint32_t tempty_leader = peer_addr(smem_u32(tempty_bar), 0);
     int local = 0;
-    for (int tile = pair_id; tile < num_tiles; tile += num_pairs, ++local) {
+    for (int tile = pair_id; tile < num_tiles; tile += num_pairs) {
+      if (groups != nullptr && group_of(groups, num_groups, (tile % num_m) * kTileM) < 0) continue;
       const int acc = local & 1;
-      if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, 24)) break;
+      ++local;
+      if (!mbar_wait(&tfull_bar[acc], ((local - 1) >> 1) & 1, 24)) break;
       tc_fence_after();
       const int m0 = (tile % num_m) * kTileM + (int)rank * BM;
       int n0, bn;
@@ -359,7 +371,8 @@ int get_gemm_pair() { return pair_enabled() ? 1 : 0; }  // declared in gemm_bf16
 
 // Launches the CTA-pair kernel for large GEMMs (enough 256 x 256 tiles to fill
 // the SMs) when it is enabled; returns false otherwise.
-static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream, const RopeArgs& rope = RopeArgs{}) {
+static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream, const RopeArgs& rope = RopeArgs{},
+                     const int* groups = nullptr, int num_groups = 0) {
   if (!pair_enabled()) return false;
   if (a.M <= 0 || a.N % pair::kTileN != 0 || a.K % 8 != 0) return false;
   if (epi != kStoreBf16 && epi != kStoreF32 && epi != kSwiGLU && epi != kQkvRope) return false;
@@ -398,7 +411,7 @@ static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream, const Rope
   if (max_pairs < 1) return false;
   pair::ColPlan cp{a.N / pair::kTileN, 0, pair::kTileN, pair::kTileN / 2};
   const int num_m = (a.M + pair::kTileM - 1) / pair::kTileM;
-  if (num_m == 1 && epi != kQkvRope && a.N % 64 == 0) {
+  if (num_m == 1 && epi != kQkvRope && groups == nullptr && a.N % 64 == 0) {
     // one M-tile: k tiles per pair of near-equal width instead of a partial last round
     const int t_min = a.N / pair::kTileN;
     const int k = (t_min + max_pairs - 1) / max_pairs;
@@ -411,9 +424,10 @@ static bool run_pair(const GemmArgs& a, int epi, cudaStream_t stream, const Rope
   const int all_tiles = num_m * cp.tiles_n;
   const int pairs = all_tiles < max_pairs ? all_tiles : max_pairs;
   CUtensorMap ta = cached_tmap_bf16(a.A, a.M, a.K, a.lda, BM);
-  CUtensorMap tb = cached_tmap_bf16(a.B, a.N, a.K, a.ldb, (uint32_t)cp.box_rows);
+  CUtensorMap tb = cached_tmap_bf16(a.B, (uint64_t)a.N * (groups != nullptr ? num_groups : 1), a.K, a.ldb,
+                                    (uint32_t)cp.box_rows);
   launch_k(kfn, dim3(2 * pairs), dim3(kThreads), pair::kSmem, stream, 2u, ta, tb, a.D, a.M, a.N, a.K, (int)a.ldd,
-           cp, rope);
+           cp, rope, groups, num_groups);
   return true;
 }
 

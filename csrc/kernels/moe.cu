@@ -117,12 +117,13 @@ void route(const void* h, const float* wr, const float* bias, int T, int H, int 
   }
 }
 
-// One CTA.  Local experts are [e0, e0 + El).  groups[El + 1] gets the padded
-// segment offsets, perm[row] the (token * topk + k) assignment of each row
+// One CTA.  Local experts are [e0, e0 + El).  groups[El + 1] gets the segment
+// offsets, each segment padded to a multiple of `align` rows (128, or 256 for
+// the CTA-pair grouped GEMM), perm[row] the (token * topk + k) assignment of each row
 // (-1 for padding), slot[t * topk + k] the row of an assignment (-1 when the
 // expert is not on this rank).
 __global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__ ids, int T, int topk, int e0,
-                                                     int El, int max_rows, int32_t* __restrict__ groups,
+                                                     int El, int max_rows, int align, int32_t* __restrict__ groups,
                                                      int32_t* __restrict__ perm, int32_t* __restrict__ slot) {
   __shared__ int cnt[kMaxExperts];
   __shared__ int off[kMaxExperts + 1];
@@ -140,7 +141,7 @@ __global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__
     for (int e = 0; e < El; ++e) {
       off[e] = o;
       cursor[e] = o;
-      o += (cnt[e] + 127) / 128 * 128;
+      o += (cnt[e] + align - 1) / align * align;
     }
     off[El] = o;
     if (o > max_rows) set_error(kErrBadIndex, (unsigned long long)o);
@@ -162,8 +163,8 @@ __global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__
 }
 
 void align(const int32_t* ids, int T, int topk, int e0, int El, int max_rows, int32_t* groups, int32_t* perm,
-           int32_t* slot, cudaStream_t s) {
-  align_kernel<<<1, 1024, 0, s>>>(ids, T, topk, e0, El, max_rows, groups, perm, slot);
+           int32_t* slot, cudaStream_t s, int align_rows) {
+  align_kernel<<<1, 1024, 0, s>>>(ids, T, topk, e0, El, max_rows, align_rows, groups, perm, slot);
 }
 
 __global__ void gather_kernel(const uint4* __restrict__ h, const int32_t* __restrict__ perm,

@@ -431,17 +431,26 @@ class ModelRunner:
             self.comm.all_reduce(out)
         return out
 
-    def _moe_rows(self, T: int) -> int:
+    # Steps of at least this many tokens pad expert segments to 256 rows, so
+    # the grouped GEMMs run on CTA pairs (one expert per 256-row tile); smaller
+    # steps (decode, captured in graphs) keep 128-row segments.
+    MOE_PAIR_TOKENS = 2048
+
+    def _moe_align(self, T: int) -> int:
+        return 256 if T >= self.MOE_PAIR_TOKENS and self.device.type == "cuda" else 128
+
+    def _moe_rows(self, T: int, align: Optional[int] = None) -> int:
         """Rows of the expert-ordered activations for T tokens: every
-        assignment plus up to 127 padding rows per local expert."""
-        return -(-(T * self.spec.experts_per_token + self.moe_El * 127) // 128) * 128
+        assignment plus up to align - 1 padding rows per local expert."""
+        a = self._moe_align(T) if align is None else align
+        return -(-(T * self.spec.experts_per_token + self.moe_El * (a - 1)) // a) * a
 
     def _init_moe(self, T: int, dev):
         s = self.spec
         k = s.experts_per_token
         self.moe_El = s.experts // self.w.ep_size
         self.moe_e0 = self.w.ep_rank * self.moe_El
-        rows = self._moe_rows(T)
+        rows = max(self._moe_rows(T, 128), self._moe_rows(T, 256))
         Fp = self.w.layers[0].experts_d.shape[-1]
         self.moe_ids = torch.zeros(T, k, dtype=torch.int32, device=dev)
         self.moe_w = torch.zeros(T, k, dtype=torch.float32, device=dev)
@@ -459,13 +468,14 @@ class ModelRunner:
         the sum over ranks (experts or expert shards live on different ranks)."""
         ops, k, El = self.ops, self.spec.experts_per_token, self.moe_El
         T = h.shape[0]
-        rows = self._moe_rows(T)
+        al = self._moe_align(T)
+        rows = self._moe_rows(T, al)
         ids, w = self.moe_ids[:T], self.moe_w[:T]
         ops.moe_route(h, lw.router, self.router_bias, k, ids, w)
-        ops.moe_align(ids, T, k, self.moe_e0, El, self.moe_groups, self.moe_perm[:rows], self.moe_slot[:T * k])
+        ops.moe_align(ids, T, k, self.moe_e0, El, self.moe_groups, self.moe_perm[:rows], self.moe_slot[:T * k], al)
         ops.moe_gather(h, self.moe_perm[:rows], self.moe_groups, El, k, self.moe_x[:rows])
-        ops.gemm_grouped(self.moe_x[:rows], lw.experts_gu, self.moe_act[:rows], self.moe_groups, El, 2)
-        ops.gemm_grouped(self.moe_act[:rows], lw.experts_d, self.moe_y[:rows], self.moe_groups, El, 0)
+        ops.gemm_grouped(self.moe_x[:rows], lw.experts_gu, self.moe_act[:rows], self.moe_groups, El, 2, al)
+        ops.gemm_grouped(self.moe_act[:rows], lw.experts_d, self.moe_y[:rows], self.moe_groups, El, 0, al)
         ops.moe_combine(self.moe_y[:rows], self.moe_slot[:T * k], w, T, k, delta)
         if self.comm is not None and reduce:
             self.comm.all_reduce(delta)

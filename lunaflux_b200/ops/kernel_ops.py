@@ -103,17 +103,17 @@ class KernelOps:
         self.launches += 1
         self.C.moe_route(h, router, bias, topk, ids, weights)
 
-    def moe_align(self, ids, T, topk, e0, El, groups, perm, slot):
+    def moe_align(self, ids, T, topk, e0, El, groups, perm, slot, align: int = 128):
         self.launches += 1
-        self.C.moe_align(ids, T, topk, e0, El, groups, perm, slot)
+        self.C.moe_align(ids, T, topk, e0, El, groups, perm, slot, align)
 
     def moe_gather(self, h, perm, groups, El, topk, out):
         self.launches += 1
         self.C.moe_gather(h, perm, groups, El, topk, out)
 
-    def gemm_grouped(self, A, B, out, groups, num_groups, epi):
+    def gemm_grouped(self, A, B, out, groups, num_groups, epi, align: int = 128):
         self.launches += 1
-        self.C.gemm_grouped(A, B, out, groups, num_groups, epi)
+        self.C.gemm_grouped(A, B, out, groups, num_groups, epi, align)
 
     def moe_combine(self, y, slot, w, T, topk, out):
         self.launches += 1

@@ -225,7 +225,7 @@ class TorchOps:
         ids[:T] = i.to(torch.int32)
         weights[:T] = w / w.sum(-1, keepdim=True)
 
-    def moe_align(self, ids, T, topk, e0, El, groups, perm, slot):
+    def moe_align(self, ids, T, topk, e0, El, groups, perm, slot, align: int = 128):
         flat = ids[:T].reshape(-1).long().cpu()
         perm.fill_(-1)
         slot_h = torch.full((T * topk,), -1, dtype=torch.int32)
@@ -237,7 +237,7 @@ class TorchOps:
             for j, a in enumerate(sel.tolist()):
                 perm[off + j] = a
                 slot_h[a] = off + j
-            off += -(-len(sel) // 128) * 128
+            off += -(-len(sel) // align) * align
         offs.append(off)
         groups[:El + 1] = torch.tensor(offs, dtype=torch.int32)
         slot.view(-1)[:T * topk] = slot_h.to(slot.device)
@@ -249,7 +249,7 @@ class TorchOps:
         out[:used] = 0
         out[:used][ok] = h[(p[ok] // topk)]
 
-    def gemm_grouped(self, A, B, out, groups, num_groups, epi):
+    def gemm_grouped(self, A, B, out, groups, num_groups, epi, align: int = 128):
         g = groups[:num_groups + 1].tolist()
         for e in range(num_groups):
             if g[e + 1] > g[e]:

@@ -537,3 +537,38 @@ def test_peer_wait_runs_out_and_the_step_fails(C):
     x = torch.ones(1024, device="cuda")
     assert float(x.sum()) == 1024.0
     assert C.read_error(True)[0] == 0
+
+
+@pytest.mark.parametrize("epi", [0, 2])
+def test_grouped_gemm_256_row_segments_on_cta_pairs(C, epi):
+    """Expert segments padded to 256 rows run on the CTA-pair kernel (one
+    expert per 256-row tile, tiles past the last segment skipped): every
+    segment's rows against the fp32 product with its expert's weights."""
+    E, T, k, H, N = 8, 4096, 2, 1024, 2048
+    g = torch.Generator(device="cuda").manual_seed(7 + epi)
+    ids = torch.randint(0, E, (T, k), device="cuda", generator=g, dtype=torch.int32)
+    ids[:, 1] = (ids[:, 0] + 1 + torch.randint(0, E - 1, (T,), device="cuda", generator=g, dtype=torch.int32)) % E
+    rows = -(-(T * k + E * 255) // 256) * 256
+    groups = torch.zeros(E + 1, dtype=torch.int32, device="cuda")
+    perm = torch.empty(rows, dtype=torch.int32, device="cuda")
+    slot = torch.empty(T * k, dtype=torch.int32, device="cuda")
+    C.moe_align(ids, T, k, 0, E, groups, perm, slot, 256)
+    gh = groups.tolist()
+    assert all(x % 256 == 0 for x in gh)
+    A = (torch.randn(rows, H, device="cuda", generator=g)).bfloat16()
+    B = (torch.randn(E, N, H, device="cuda", generator=g) * 0.05).bfloat16()
+    cols = N // 2 if epi == 2 else N
+    D = torch.full((rows, cols), 7.0, device="cuda", dtype=torch.bfloat16)
+    C.gemm_grouped(A, B, D, groups, E, epi, 256)
+    torch.cuda.synchronize()
+    assert C.read_error(True)[0] == 0
+    for e in range(E):
+        a, b = gh[e], gh[e + 1]
+        if a == b:
+            continue
+        ref = A[a:b].float() @ B[e].float().t()
+        if epi == 2:
+            v = ref.view(b - a, N // 64, 2, 32)
+            ref = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(b - a, N // 2)
+        _close(D[a:b], ref, 3e-2, 3e-2, f"expert {e} rows {a}..{b} epi={epi}")
+    assert bool((D[gh[E]:] == 7.0).all()), "rows past the last segment were written"
