@@ -12,8 +12,8 @@ void inject_error(int code);
 // Limit of every bounded wait in every kernel, on the current device
 // (nanoseconds; default 1e9).
 void set_wait_limit_ns(unsigned long long ns);
-// Programmatic dependent launch for the kernels of the step (off unless
-// LUNAFLUX_PDL=1 or set_pdl(true)).
+// Programmatic dependent launch for the kernels of the step (on unless
+// LUNAFLUX_PDL=0 or set_pdl(false)).
 bool pdl_enabled();
 void set_pdl(bool on);
 }  // namespace rt
