@@ -466,12 +466,11 @@ __device__ uint64_t select_desc(const Src& src, uint64_t floor_key, WFn wfn, uns
           wv = wfn(v);
         }
         const unsigned m = __match_any_sync(0xffffffffu, bin);
-        unsigned long long sum = 0;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const unsigned long long x = __shfl_sync(0xffffffffu, wv, j);
-          if ((m >> j) & 1u) sum += x;
-        }
+        // the group's sum by the warp reduction unit: a weight is below 2^44,
+        // so it is added as two 22-bit limbs (32 limbs fit in 32 bits)
+        const unsigned lo = __reduce_add_sync(m, (unsigned)(wv & 0x3FFFFFull));
+        const unsigned hi = __reduce_add_sync(m, (unsigned)(wv >> 22));
+        const unsigned long long sum = ((unsigned long long)hi << 22) + lo;
         if (bin < 256 && __ffs(m) - 1 == lane) atomicAdd(&hist[bin], sum);
       }
     } else {
