@@ -23,6 +23,7 @@ import torch
 from ..models.spec import LlamaSpec, rope_inv_freq
 from ..models.weights import ModelWeights
 from ..scheduler.scheduler import StepPlan
+from ..ops.launch_contract import check_paged_step
 from .step_inputs import HostStep, build_host_step, device_views, make_layout
 
 
@@ -75,6 +76,8 @@ class ModelRunner:
         self.W = -(-max_context // page)
         self.num_pages = num_pages + 1          # physical page 0 is the reserved zero page
         self.check_every = check_errors_every
+        # admit each packed step against the KV arena before its upload
+        self.check_steps = os.environ.get("LUNAFLUX_CHECK_LAUNCHES") == "1"
         s, sh = self.spec, self.shard
         dt = weights.embed.dtype
         self.dtype = dt
@@ -523,6 +526,8 @@ class ModelRunner:
             self.in_evt[slot].synchronize()  # the previous upload from this pinned block has finished
         host_buf = self.in_host[slot]
         hs = build_host_step(plan, table_matrix, self.P, self.W, host_buf.numpy(), bucket=bucket)
+        if self.check_steps:
+            check_paged_step(hs.layout, hs.buf, self.num_pages, self.P, self.spec.vocab)
         if hs.any_forwarded and not self.overlap:
             raise ValueError("a step forwards device tokens but the runner was built without overlap")
         L = hs.layout

@@ -30,6 +30,9 @@ class KernelOps:
         # QKV GEMM with RoPE and the paged K / V write in its epilogue (one
         # kernel instead of two); on unless LUNAFLUX_FUSE_QKV_ROPE=0
         self.fuse_qkv_rope = os.environ.get("LUNAFLUX_FUSE_QKV_ROPE") != "0"
+        if os.environ.get("LUNAFLUX_CHECK_LAUNCHES") == "1":
+            from .launch_contract import install
+            install(self)   # every launch admitted against its operand contract first
 
     def embed(self, ids, table, out):
         self.launches += 1

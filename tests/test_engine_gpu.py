@@ -200,3 +200,21 @@ def test_moe_engine_matches_oracle():
     assert eng.runner.ops.read_error(True)[0] == 0
     for p, o in zip(prompts, outs):
         check_near_argmax(ref, p, o, slack=0.1)
+
+
+def test_every_launch_admitted_by_its_contract(monkeypatch):
+    """With LUNAFLUX_CHECK_LAUNCHES=1 every KernelOps call of a mixed prefill /
+    decode / prefix-hit workload (graphs on) passes its operand contract, and
+    every packed step passes paged admission against the KV arena."""
+    monkeypatch.setenv("LUNAFLUX_CHECK_LAUNCHES", "1")
+    spec = small_spec()
+    ck = bf16_checkpoint(spec, seed=4)
+    eng = make_engine(spec, ck, graphs=True, prefix=True)
+    ops = eng.runner.ops
+    assert eng.runner.check_steps and ops.admitted == 0
+    g = torch.Generator().manual_seed(5)
+    shared = torch.randint(0, spec.vocab, (48,), generator=g).tolist()
+    prompts = [shared + torch.randint(0, spec.vocab, (n,), generator=g).tolist() for n in (3, 90, 200)]
+    outs = eng.generate(prompts, 10)
+    assert all(len(o) == 10 for o in outs)
+    assert ops.admitted > 0 and ops.read_error(True)[0] == 0
