@@ -405,8 +405,10 @@ class Scheduler:
         prefill_rows: List[Row] = []
 
         # 1. decode-first
+        # (a request preempted below to make room leaves DECODE for WAITING)
+        decoding = RequestState.DECODE
         for req in list(self.running):
-            if req.state is not RequestState.DECODE or req not in self.running:
+            if req.state is not decoding:
                 continue
             if len(decode_rows) >= max_rows or budget <= 0:
                 break
@@ -416,23 +418,23 @@ class Scheduler:
             need = self._pages_needed(req, req.sched_len + 1)
             if need and not self._make_room(need, req):
                 continue
-            if req not in self.running:
-                continue
             self._grow(req, req.sched_len + 1)
             decode_rows.append(Row(req, req.sched_len, 1, True, True, req.generation,
                                    fwd=req.pending_slot if req.pending else -1))
             budget -= 1
         # drop rows whose request was preempted while making room for a later one
-        decode_rows = [r for r in decode_rows if r.req in self.running]
+        decode_rows = [r for r in decode_rows if r.req.state is decoding]
 
         # 2. prefill: aged waiting requests, then partial prefills, then FIFO waiting
         rows_used = len(decode_rows)
         reserve = cfg.emergency_decode_page_reserve
-        aged = [r for r in self.waiting if self.step_seq - r.enqueued_step >= cfg.waiting_age_threshold_steps]
+        aged: List[Request] = []
+        fresh: List[Request] = []
+        if admit:     # one pass over the queue (it can hold thousands of requests)
+            cut = self.step_seq - cfg.waiting_age_threshold_steps
+            for r in self.waiting:
+                (aged if r.enqueued_step <= cut else fresh).append(r)
         partial = [r for r in self.running if r.state is RequestState.PREFILL]
-        fresh = [r for r in self.waiting if r not in aged]
-        if not admit:
-            aged, fresh = [], []
         for req in aged + partial + fresh:
             if budget <= 0 or rows_used >= max_rows:
                 break
