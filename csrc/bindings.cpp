@@ -408,29 +408,53 @@ std::vector<int64_t> gemm_plan_cluster(int64_t M, int64_t N, int64_t K, int64_t 
 
 void gemm_set_cluster_mb2(bool on) { lf::gemm::set_cluster_mb2(on ? 1 : 0); }
 
-void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) {
+void embed(at::Tensor& ids, const at::Tensor& table, at::Tensor& out, c10::optional<at::Tensor> fwd,
+           int64_t fwd_first, c10::optional<at::Tensor> prev) {
   LF_CHECK(ids.scalar_type() == at::kInt && table.scalar_type() == at::kBFloat16, "embed dtypes");
   LF_CHECK(table.is_contiguous() && out.is_contiguous() && ids.is_contiguous(), "embed needs contiguous tensors");
   LF_CHECK(table.size(1) % 8 == 0, "hidden must be a multiple of 8");
   LF_CHECK(out.size(0) >= ids.size(0), "embed output too small");
+  const int32_t* f = nullptr;
+  const int32_t* p = nullptr;
+  int nf = 0, np = 0;
+  if (fwd.has_value()) {
+    LF_CHECK(prev.has_value(), "embed: forwarded rows need the previous step's tokens");
+    LF_CHECK(fwd->scalar_type() == at::kInt && prev->scalar_type() == at::kInt && fwd->is_contiguous() &&
+                 prev->is_contiguous(), "embed: fwd / prev int32 contiguous");
+    LF_CHECK(fwd_first >= 0 && fwd_first + fwd->numel() <= ids.size(0), "embed: forwarded rows outside the step");
+    f = fwd->data_ptr<int32_t>();
+    p = prev->data_ptr<int32_t>();
+    nf = fwd->numel();
+    np = prev->numel();
+  }
   c10::cuda::CUDAGuard g(table.device());
   lf::ew::embed(ids.data_ptr<int32_t>(), table.data_ptr(), out.data_ptr(), ids.size(0), table.size(1), table.size(0),
-                stream());
+                stream(), f, (int)fwd_first, nf, p, np);
 }
 
 void rmsnorm(const at::Tensor& x, c10::optional<at::Tensor> residual, const at::Tensor& w, at::Tensor& out,
-             double eps) {
+             double eps, c10::optional<at::Tensor> rows) {
   LF_CHECK(x.is_contiguous() && out.is_contiguous() && w.is_contiguous(), "rmsnorm needs contiguous tensors");
-  LF_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "rmsnorm is bf16");
+  LF_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+               out.scalar_type() == at::kBFloat16, "rmsnorm is bf16");
   const int H = x.size(-1);
-  LF_CHECK(H % 8 == 0 && w.numel() == H, "rmsnorm hidden size");
+  LF_CHECK(H % 8 == 0 && w.numel() == H && out.size(-1) == H, "rmsnorm hidden size");
   void* r = nullptr;
   if (residual.has_value()) {
     LF_CHECK(residual->is_contiguous() && residual->numel() == x.numel(), "residual shape");
     r = residual->data_ptr();
   }
+  const int in_rows = x.numel() / H;
+  int out_rows = in_rows;
+  const int32_t* idx = nullptr;
+  if (rows.has_value()) {
+    LF_CHECK(rows->scalar_type() == at::kInt && rows->is_contiguous(), "rmsnorm rows: int32 contiguous");
+    out_rows = rows->numel();
+    idx = rows->data_ptr<int32_t>();
+  }
+  LF_CHECK(out.numel() >= (int64_t)out_rows * H, "rmsnorm output too small");
   c10::cuda::CUDAGuard g(x.device());
-  lf::ew::rmsnorm(x.data_ptr(), r, w.data_ptr(), out.data_ptr(), x.numel() / H, H, (float)eps, stream());
+  lf::ew::rmsnorm(x.data_ptr(), r, w.data_ptr(), out.data_ptr(), out_rows, H, (float)eps, stream(), idx, in_rows);
 }
 
 void rope_kv_write(at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slots, const at::Tensor& cos_sin,
@@ -665,8 +689,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
   m.def("gemm_choose_bn", &gemm_choose_bn);
-  m.def("embed", &embed);
-  m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"));
+  m.def("embed", &embed, py::arg("ids"), py::arg("table"), py::arg("out"), py::arg("fwd") = py::none(),
+        py::arg("fwd_first") = 0, py::arg("prev") = py::none());
+  m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"),
+        py::arg("rows") = py::none());
   m.def("rope_kv_write", &rope_kv_write);
   m.def("swiglu", &swiglu);
   m.def("argmax", &argmax, py::arg("logits"), py::arg("out"), py::arg("status") = py::none());

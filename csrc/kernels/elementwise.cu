@@ -25,13 +25,28 @@ namespace ew {
 
 // ---------------------------------------------------------------------------
 // Embedding gather: out[t, :] = E[ids[t], :]   (bf16, 16-byte vectors)
+//
+// Forwarded decode tokens: with `fwd` set, row t in [fwd_first, fwd_first +
+// nfwd) whose fwd[t - fwd_first] = j >= 0 takes its id from prev[j] (the
+// previous step's sample, still on the device while the host plans ahead)
+// and stores it back into ids[t]; j outside [0, nprev) is a bad index.
 // ---------------------------------------------------------------------------
-__global__ void embed_kernel(const int32_t* __restrict__ ids, const uint4* __restrict__ table,
-                             uint4* __restrict__ out, int T, int vec_per_row, int vocab) {
+__global__ void embed_kernel(int32_t* __restrict__ ids, const uint4* __restrict__ table,
+                             uint4* __restrict__ out, int T, int vec_per_row, int vocab,
+                             const int32_t* __restrict__ fwd, int fwd_first, int nfwd,
+                             const int32_t* __restrict__ prev, int nprev) {
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.x;
   int id = ids[t];
+  if (fwd != nullptr && t >= fwd_first && t < fwd_first + nfwd) {
+    const int j = fwd[t - fwd_first];
+    if (j >= 0) {
+      id = (j < nprev) ? prev[j] : -1;
+      __syncthreads();                       // every thread has read ids[t] before it is replaced
+      if (threadIdx.x == 0) ids[t] = id;
+    }
+  }
   if (id < 0 || id >= vocab) {
     if (threadIdx.x == 0) set_error(kErrBadIndex, (unsigned long long)t);
     for (int i = threadIdx.x; i < vec_per_row; i += blockDim.x) out[(size_t)t * vec_per_row + i] = make_uint4(0, 0, 0, 0);
@@ -41,11 +56,13 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const uint4* __res
     out[(size_t)t * vec_per_row + i] = table[(size_t)id * vec_per_row + i];
 }
 
-void embed(const int32_t* ids, const void* table, void* out, int T, int H, int vocab, cudaStream_t s) {
+void embed(int32_t* ids, const void* table, void* out, int T, int H, int vocab, cudaStream_t s,
+           const int32_t* fwd, int fwd_first, int nfwd, const int32_t* prev, int nprev) {
   if (T <= 0) return;
   const int vpr = H / 8;
   launch_k(embed_kernel, dim3(T), dim3(128), 0, s, 1,
-         ids, reinterpret_cast<const uint4*>(table), reinterpret_cast<uint4*>(out), T, vpr, vocab);
+         ids, reinterpret_cast<const uint4*>(table), reinterpret_cast<uint4*>(out), T, vpr, vocab,
+         fwd, fwd_first, nfwd, prev, nprev);
 }
 
 // ---------------------------------------------------------------------------
@@ -53,11 +70,15 @@ void embed(const int32_t* ids, const void* table, void* out, int T, int H, int v
 //   r = x + residual;  residual = r;  out = r * rsqrt(mean(r^2) + eps) * w
 // else out = x * rsqrt(mean(x^2) + eps) * w.   fp32 math, bf16 storage.
 // One CTA per row, each thread owns VPT 16-byte vectors held in registers.
+// Gathered form (`rows` non-null): output row i normalises input row rows[i]
+// and the residual is not written back (the final norm before the LM head
+// only needs the sampled rows); an index outside [0, in_rows) is a bad index.
 // ---------------------------------------------------------------------------
 template <int VPT>
 __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint4* __restrict__ x, uint4* __restrict__ residual,
                                                       const uint4* __restrict__ w, uint4* __restrict__ out,
-                                                      int vec_per_row, float eps, int H) {
+                                                      int vec_per_row, float eps, int H,
+                                                      const int32_t* __restrict__ rows, int in_rows) {
   pdl_trigger();
   // The weight does not depend on the previous kernel: load it before the
   // dependency wait (under PDL this overlaps the producer's tail) instead of
@@ -69,7 +90,22 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint4* __restrict__ 
     wreg[j] = i < vec_per_row ? w[i] : make_uint4(0u, 0u, 0u, 0u);
   }
   pdl_wait();
-  const size_t row = blockIdx.x;
+  const size_t orow = blockIdx.x;
+  size_t row = orow;
+  if (rows != nullptr) {
+    const int r = rows[orow];
+    if (r < 0 || r >= in_rows) {
+      if (threadIdx.x == 0) set_error(kErrBadIndex, (unsigned long long)orow);
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int i = threadIdx.x + j * 128;
+        if (i < vec_per_row) out[orow * vec_per_row + i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      return;
+    }
+    row = (size_t)r;
+  }
+  const bool write_residual = rows == nullptr;
   float v[VPT][8];
   float ss = 0.f;
 #pragma unroll
@@ -89,7 +125,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint4* __restrict__ 
           sb[e] = __float2bfloat16(__bfloat162float(ab[e]) + __bfloat162float(rb[e]));
           v[j][e] = __bfloat162float(sb[e]);
         }
-        residual[row * vec_per_row + i] = sum;
+        if (write_residual) residual[row * vec_per_row + i] = sum;
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[j][e] = __bfloat162float(ab[e]);
@@ -114,12 +150,13 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint4* __restrict__ 
       __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
 #pragma unroll
       for (int e = 0; e < 8; ++e) ob[e] = __float2bfloat16(v[j][e] * inv * __bfloat162float(wb[e]));
-      out[row * vec_per_row + i] = o;
+      out[orow * vec_per_row + i] = o;
     }
   }
 }
 
-void rmsnorm(const void* x, void* residual, const void* w, void* out, int T, int H, float eps, cudaStream_t s) {
+void rmsnorm(const void* x, void* residual, const void* w, void* out, int T, int H, float eps, cudaStream_t s,
+             const int32_t* rows, int in_rows) {
   if (T <= 0) return;
   const int vpr = H / 8;
   const int vpt = (vpr + 127) / 128;
@@ -128,15 +165,15 @@ void rmsnorm(const void* x, void* residual, const void* w, void* out, int T, int
   auto W = reinterpret_cast<const uint4*>(w);
   auto O = reinterpret_cast<uint4*>(out);
   if (vpt <= 1) launch_k(rmsnorm_kernel<1>, dim3(T), dim3(128), 0, s, 1,
-         X, R, W, O, vpr, eps, H);
+         X, R, W, O, vpr, eps, H, rows, in_rows);
   else if (vpt <= 2) launch_k(rmsnorm_kernel<2>, dim3(T), dim3(128), 0, s, 1,
-         X, R, W, O, vpr, eps, H);
+         X, R, W, O, vpr, eps, H, rows, in_rows);
   else if (vpt <= 4) launch_k(rmsnorm_kernel<4>, dim3(T), dim3(128), 0, s, 1,
-         X, R, W, O, vpr, eps, H);
+         X, R, W, O, vpr, eps, H, rows, in_rows);
   else if (vpt <= 8) launch_k(rmsnorm_kernel<8>, dim3(T), dim3(128), 0, s, 1,
-         X, R, W, O, vpr, eps, H);
+         X, R, W, O, vpr, eps, H, rows, in_rows);
   else launch_k(rmsnorm_kernel<16>, dim3(T), dim3(128), 0, s, 1,
-         X, R, W, O, vpr, eps, H);
+         X, R, W, O, vpr, eps, H, rows, in_rows);
 }
 
 // ---------------------------------------------------------------------------

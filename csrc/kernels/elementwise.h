@@ -16,8 +16,13 @@ struct SampleParams {
 };
 static_assert(sizeof(SampleParams) == 32, "SampleParams is a 32-byte wire record");
 
-void embed(const int32_t* ids, const void* table, void* out, int T, int H, int vocab, cudaStream_t s);
-void rmsnorm(const void* x, void* residual, const void* w, void* out, int T, int H, float eps, cudaStream_t s);
+// fwd / prev: forwarded decode tokens (see elementwise.cu); null for none.
+void embed(int32_t* ids, const void* table, void* out, int T, int H, int vocab, cudaStream_t s,
+           const int32_t* fwd = nullptr, int fwd_first = 0, int nfwd = 0, const int32_t* prev = nullptr,
+           int nprev = 0);
+// rows: gathered form (output row i from input row rows[i] of in_rows; no residual write-back).
+void rmsnorm(const void* x, void* residual, const void* w, void* out, int T, int H, float eps, cudaStream_t s,
+             const int32_t* rows = nullptr, int in_rows = 0);
 void rope_kv_write(void* qkv, int64_t ld, const int32_t* positions, const int32_t* slots, const void* cos_sin,
                    void* kcache, void* vcache, int T, int Hq, int Hkv, int D, int page, int max_pos,
                    int64_t num_slots, cudaStream_t s);

@@ -166,6 +166,7 @@ class ModelRunner:
         self.out_host = [torch.zeros(R, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         self._oflip = 0
         self._flip = 0
+        self._embed_fwd = None
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         self.graph_launches: Dict[tuple, int] = {}
         self.graph_sizes = sorted(b for b in graph_sizes if b <= R)
@@ -187,8 +188,9 @@ class ModelRunner:
 
     def forward(self, v: Dict[str, torch.Tensor], T: int, Tp: int, Rp: int, Rd: int, Rs: int, max_q_len: int,
                 splits: int, stochastic: bool, host_meta=None, gather: bool = True):
-        if self.overlap and Rd:
-            self._forward_tokens(v, Tp, Rd)
+        # decode rows whose input token was sampled by the previous step (not
+        # yet on the host) take it from that step's output inside the embedding
+        self._embed_fwd = (v["d_fwd"][:Rd], Tp, self.prev_tok) if self.overlap and Rd else None
         if self.sp:
             out = self.forward_sp(v, T, Tp, Rp, Rd, Rs, max_q_len, splits, stochastic, host_meta, gather)
         else:
@@ -196,14 +198,6 @@ class ModelRunner:
         if self.overlap:
             self.prev_tok[:Rs].copy_(out)
         return out
-
-    def _forward_tokens(self, v, Tp: int, Rd: int):
-        """Decode rows whose input token was sampled by the previous step (not
-        yet on the host) take it from that step's output on the device."""
-        f = v["d_fwd"][:Rd]
-        tok = v["tokens"][Tp:Tp + Rd]
-        g = torch.index_select(self.prev_tok, 0, torch.clamp(f, 0, self.prev_tok.numel() - 1))
-        tok.copy_(torch.where(f >= 0, g, tok))
 
     def _forward_tp(self, v, T, Tp, Rp, Rd, Rs, max_q_len, splits, stochastic, host_meta=None, gather=True):
         ops, s, w = self.ops, self.spec, self.w
@@ -214,7 +208,7 @@ class ModelRunner:
         hm = host_meta or {}
         if self.comm is not None and getattr(self.comm, "fused", False):
             self.comm.begin_forward()
-        ops.embed(v["tokens"], w.embed, resid)
+        ops.embed(v["tokens"], w.embed, resid, self._embed_fwd)
         for l, lw in enumerate(w.layers):
             if l == 0:
                 ops.rmsnorm(resid, None, lw.ln1, h, eps)
@@ -229,6 +223,11 @@ class ModelRunner:
             else:
                 self._proj(h, lw, "wgu", act, 2)
                 delta = self._row_parallel(act, lw, "wd", self.delta[:T], ws)
+        if gather:
+            # the final norm only for the sampled rows, gathered as it reads them
+            hs = self.hs[:Rs]
+            ops.rmsnorm(delta, resid, w.norm, hs, eps, v["s_idx"])
+            return self._sample(hs, v, Rs, stochastic, False)
         ops.rmsnorm(delta, resid, w.norm, h, eps)
         return self._sample(h, v, Rs, stochastic, gather)
 
@@ -308,7 +307,7 @@ class ModelRunner:
         ws = self.gemm_ws
         # embeddings of every token, then this rank's rows (padding rows are zero)
         emb = self.h[:T]
-        ops.embed(v["tokens"], w.embed, emb)
+        ops.embed(v["tokens"], w.embed, emb, self._embed_fwd)
         full[T:].zero_()
         full[:T].copy_(emb)
         resid.copy_(full[rank * Tl:(rank + 1) * Tl])

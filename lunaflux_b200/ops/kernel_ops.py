@@ -34,13 +34,18 @@ class KernelOps:
             from .launch_contract import install
             install(self)   # every launch admitted against its operand contract first
 
-    def embed(self, ids, table, out):
+    def embed(self, ids, table, out, fwd=None):
+        """fwd = (slots, first, prev): rows first.. take prev[slot] where slot >= 0."""
         self.launches += 1
-        self.C.embed(ids, table, out)
+        if fwd is None:
+            self.C.embed(ids, table, out)
+        else:
+            self.C.embed(ids, table, out, fwd[0], fwd[1], fwd[2])
 
-    def rmsnorm(self, x, residual, w, out, eps):
+    def rmsnorm(self, x, residual, w, out, eps, rows=None):
+        """rows: output row i normalises input row rows[i] (no residual write-back)."""
         self.launches += 1
-        self.C.rmsnorm(x, residual, w, out, eps)
+        self.C.rmsnorm(x, residual, w, out, eps, rows)
 
     def gemm(self, A, B, out, epi: int = EPI_BF16, ws: Optional[torch.Tensor] = None):
         M, N, K = A.shape[0], B.shape[0], A.shape[1]

@@ -182,12 +182,16 @@ CONTRACTS: Dict[str, Contract] = {c.op: c for c in (
              params=("Hq",)),
     Contract("rmsnorm", "rmsnorm",
              (Role("x", BF16, ("T", "H")), Role("residual", BF16, ("T", "H"), optional=True),
-              Role("w", BF16, ("H",), rowmajor=False), Role("out", BF16, ("T", "H"))),
-             (_r("H % 8 == 0 (16-byte vectors)", lambda d: d["H"] % 8 == 0),)),
+              Role("w", BF16, ("H",), rowmajor=False), Role("out", BF16, ("To", "H")),
+              Role("rows", I32, ("R",), rowmajor=False, optional=True)),
+             (_r("H % 8 == 0 (16-byte vectors)", lambda d: d["H"] % 8 == 0),
+              _r("out holds every output row", lambda d: d["To"] >= d.get("R", d["T"])))),
     Contract("embed", "embed",
              (Role("ids", I32, ("T",), rowmajor=False), Role("table", BF16, ("V", "H")),
-              Role("out", BF16, ("To", "H"))),
-             (_r("out holds every token", lambda d: d["To"] >= d["T"]), _r("H % 8 == 0", lambda d: d["H"] % 8 == 0))),
+              Role("out", BF16, ("To", "H")), Role("fwd", I32, ("F",), rowmajor=False, optional=True),
+              Role("prev", I32, ("Pv",), rowmajor=False, optional=True)),
+             (_r("out holds every token", lambda d: d["To"] >= d["T"]), _r("H % 8 == 0", lambda d: d["H"] % 8 == 0),
+              _r("forwarded rows inside the step", lambda d: d.get("first", 0) + d.get("F", 0) <= d["T"]))),
     Contract("rope_kv_write", "rope_kv_write",
              (Role("qkv", BF16, ("T", "Nq")), Role("positions", I32, ("Tp",), rowmajor=False),
               Role("slots", I32, ("Ts",), rowmajor=False), Role("cos_sin", F32, ("*",), rowmajor=False),
@@ -355,8 +359,10 @@ def launch_checks():
         "gemm": lambda A, B, out, epi=0, ws=None: (C["linear"], (A, B, out), {"epi": epi}),
         "qkv_rope": lambda A, B, qkv, positions, slots, cos_sin, kc, vc, Hq, Hkv, page:
             (C["linear_qkv_rope"], (A, B, qkv, positions, slots, cos_sin, kc, vc), {"Hq": Hq, "Hkv": Hkv, "page": page}),
-        "rmsnorm": lambda x, residual, w, out, eps: (C["rmsnorm"], (x, residual, w, out), {}),
-        "embed": lambda ids, table, out: (C["embed"], (ids, table, out), {}),
+        "rmsnorm": lambda x, residual, w, out, eps, rows=None: (C["rmsnorm"], (x, residual, w, out, rows), {}),
+        "embed": lambda ids, table, out, fwd=None:
+            (C["embed"], (ids, table, out) + ((None, None) if fwd is None else (fwd[0], fwd[2])),
+             {} if fwd is None else {"first": fwd[1]}),
         "rope_kv_write": lambda qkv, positions, slots, cos_sin, kc, vc, Hq, Hkv, page:
             (C["rope_kv_write"], (qkv, positions, slots, cos_sin, kc, vc), {"Hq": Hq, "Hkv": Hkv, "page": page}),
         "attn_prefill": lambda q, out, q_start, seq_lens, bt, kc, vc, Hq, Hkv, max_q_len, host=None:

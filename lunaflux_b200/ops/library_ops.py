@@ -52,10 +52,14 @@ class LibraryOps(TorchOps):
         self._arange = torch.arange(0, 4097, dtype=torch.int32, device=self.device)
 
     # ------------------------------------------------------------ dense ops
-    def embed(self, ids, table, out):
+    def embed(self, ids, table, out, fwd=None):
+        if fwd is not None:
+            self.forward_tokens(ids, fwd)
         torch.index_select(table, 0, ids.long(), out=out[: ids.shape[0]])
 
-    def rmsnorm(self, x, residual, w, out, eps):
+    def rmsnorm(self, x, residual, w, out, eps, rows=None):
+        if rows is not None:
+            return super().rmsnorm(x, residual, w, out, eps, rows)
         if residual is not None:
             residual.add_(x)
             src = residual

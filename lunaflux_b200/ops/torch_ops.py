@@ -24,11 +24,27 @@ class TorchOps:
         self.device = torch.device(device)
         self.launches = 0
 
-    def embed(self, ids, table, out):
+    @staticmethod
+    def forward_tokens(ids, fwd):
+        """Rows fwd[1].. whose slot fwd[0][i] >= 0 take fwd[2][slot] (in place)."""
+        f, first, prev = fwd
+        tok = ids[first:first + f.shape[0]]
+        g = torch.index_select(prev, 0, torch.clamp(f, 0, prev.numel() - 1))
+        tok.copy_(torch.where(f >= 0, g, tok))
+
+    def embed(self, ids, table, out, fwd=None):
+        if fwd is not None:
+            self.forward_tokens(ids, fwd)
         out[: ids.shape[0]] = table[ids.long()]
 
-    def rmsnorm(self, x, residual, w, out, eps):
-        if residual is not None:
+    def rmsnorm(self, x, residual, w, out, eps, rows=None):
+        if rows is not None:
+            idx = rows.long()
+            src = x.index_select(0, idx)
+            if residual is not None:
+                src = (src + residual.index_select(0, idx)).to(x.dtype)
+            out = out[: idx.shape[0]]
+        elif residual is not None:
             residual.copy_(x + residual)
             src = residual
         else:

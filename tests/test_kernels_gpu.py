@@ -180,6 +180,54 @@ def test_embed(C):
     assert torch.equal(out, E[ids.long()])
 
 
+@pytest.mark.parametrize("H", [64, 4096])
+def test_rmsnorm_gathered_rows(C, H):
+    """Output row i normalises input row rows[i] (residual added, not written
+    back): bitwise what the full norm gives on that row."""
+    T = 29
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    r = torch.randn(T, H, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16()
+    rows = torch.tensor([28, 0, 5, 5, 17], device="cuda", dtype=torch.int32)
+    out = torch.zeros(rows.numel(), H, device="cuda", dtype=torch.bfloat16)
+    r_keep = r.clone()
+    C.rmsnorm(x, r, w, out, 1e-5, rows)
+    torch.cuda.synchronize()
+    assert torch.equal(r, r_keep)
+    s = (x.float() + r.float()).bfloat16().float()[rows.long()]
+    ref = s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+    _close(out, ref, 2e-2, 2e-2, "gathered rmsnorm")
+    full = torch.empty_like(x)
+    C.rmsnorm(x, r.clone(), w, full, 1e-5)
+    assert torch.equal(out, full[rows.long()])
+    # an index outside the input is a bad index: the row is zeroed and the error word set
+    C.read_error(True)
+    bad = torch.tensor([3, T], device="cuda", dtype=torch.int32)
+    out2 = torch.ones(2, H, device="cuda", dtype=torch.bfloat16)
+    C.rmsnorm(x, r, w, out2, 1e-5, bad)
+    torch.cuda.synchronize()
+    assert C.read_error(True)[0] != 0 and out2[1].abs().sum().item() == 0
+    assert torch.equal(out2[0], full[3])
+
+
+def test_embed_forwarded_tokens(C):
+    """Rows from `first` with a slot >= 0 take prev[slot] (and store it in ids)."""
+    E = torch.randn(1000, 256, device="cuda").bfloat16()
+    ids = torch.randint(0, 1000, (12,), device="cuda", dtype=torch.int32)
+    prev = torch.tensor([7, 999, 42, 3], device="cuda", dtype=torch.int32)
+    fwd = torch.tensor([2, -1, 0, 1, -1], device="cuda", dtype=torch.int32)
+    first = 6
+    want = ids.clone()
+    for i, f in enumerate(fwd.tolist()):
+        if f >= 0:
+            want[first + i] = prev[f]
+    out = torch.empty(12, 256, device="cuda", dtype=torch.bfloat16)
+    C.embed(ids, E, out, fwd, first, prev)
+    torch.cuda.synchronize()
+    assert torch.equal(ids, want)
+    assert torch.equal(out, E[want.long()])
+
+
 def rope_table(max_pos, D, theta):
     inv = 1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.float64) / D))
     ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None]
