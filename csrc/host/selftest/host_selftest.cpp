@@ -10,6 +10,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
@@ -18,9 +19,11 @@
 #include <vector>
 
 #include "approved_fs.hpp"
+#include "block_table.hpp"
 #include "bpe.hpp"
 #include "channel.hpp"
 #include "page_allocator.hpp"
+#include "prefix_tree.hpp"
 
 using namespace lf_host;
 
@@ -153,12 +156,82 @@ static void test_approved_fs(const std::string& dir) {
   CHECK(throws<ApprovedFsError>([&] { r.stat("sub/data.bin"); }));
 }
 
+static void test_block_tables() {
+  PageAllocator a(32, 1, 1 << 20, 1 << 10, 1 << 10);
+  BlockTableArena t(3, 4, 16);
+  auto tid = t.allocate();
+  t.append_pages(tid.first, tid.second, a.allocate_run(3));
+  CHECK(t.page_count(tid.first, tid.second) == 3);
+  CHECK(t.matrix_data()[tid.first * 4 + 2] == t.page_at(tid.first, tid.second, 2).first);
+  CHECK(t.resolve_token_position(tid.first, tid.second, 33).second == 1);
+  CHECK(throws<BlockTableError>([&] { t.resolve_token_position(tid.first, tid.second, 48); }));
+  CHECK(throws<BlockTableError>([&] { t.append_pages(tid.first, tid.second, a.allocate_run(2)); }));
+  t.checkpoint();
+  t.note(tid.first);
+  auto extra = a.allocate_run(1);
+  t.append_pages(tid.first, tid.second, extra);
+  t.rollback();
+  CHECK(t.page_count(tid.first, tid.second) == 3 && t.matrix_data()[tid.first * 4 + 3] == 0);
+  a.release_active(extra[0].first, extra[0].second);
+  CHECK(t.truncate(tid.first, tid.second, 1, &a).size() == 2);
+  CHECK(throws<BlockTableError>([&] { t.release(tid.first, tid.second); }));
+  t.reset_and_release(tid.first, tid.second, &a);
+  CHECK(throws<BlockTableError>([&] { t.page_count(tid.first, tid.second); }));
+  t.debug_check_invariants();
+  a.debug_check_invariants();
+  for (int i = 0; i < 3; ++i) t.allocate();
+  CHECK(throws<BlockTableError>([&] { t.allocate(); }));
+}
+
+static void test_prefix_tree() {
+  const int P = 2;
+  PageAllocator a(64, 1, 1 << 20, 1 << 10, 1 << 10);
+  PrefixTree tree(a, P, 40);
+  const int r0 = tree.new_root(), r1 = tree.new_root();
+  std::mt19937 rng(7);
+  std::vector<std::vector<int>> held;
+  for (int step = 0; step < 3000; ++step) {
+    const int op = rng() % 5;
+    const int root = (rng() & 1) ? r0 : r1;
+    std::vector<int32_t> toks(rng() % 10);
+    for (auto& x : toks) x = (int32_t)(rng() % 3);
+    if (op <= 1) {
+      const int n = std::min<int>((int)(toks.size() / P), a.free_page_count());
+      auto pages = a.allocate_run(n);
+      tree.insert(root, toks.data(), (int64_t)toks.size(), pages);
+      for (auto& p : pages) a.release_active(p.first, p.second);
+    } else if (op == 2) {
+      auto nodes = tree.lookup(root, toks.data(), (int64_t)toks.size(), -1);
+      CHECK(tree.pages_of(nodes).size() == nodes.size());
+      if (!nodes.empty() && (rng() & 1)) {
+        tree.retain(nodes);
+        held.push_back(nodes);
+      }
+    } else if (op == 3 && !held.empty()) {
+      tree.release(held.back());
+      held.pop_back();
+    } else {
+      tree.evict(rng() % 5);
+    }
+    if (step % 500 == 0) tree.debug_check_invariants();
+  }
+  for (auto& h : held) tree.release(h);
+  tree.evict(1 << 30);
+  CHECK(tree.page_count() == 0 && a.free_page_count() == 64);
+  CHECK(throws<PrefixError>([&] { tree.retain({12345}); }));
+  CHECK(throws<PrefixError>([&] { tree.lookup(999, nullptr, 0, -1); }));
+  tree.debug_check_invariants();
+  a.debug_check_invariants();
+}
+
 int main(int argc, char** argv) {
   if (argc < 2) {
     std::fprintf(stderr, "usage: host_selftest SCRATCH_DIR\n");
     return 2;
   }
   test_allocator();
+  test_block_tables();
+  test_prefix_tree();
   test_bpe();
   test_channel();
   test_approved_fs(argv[1]);

@@ -7,6 +7,11 @@ Tables live in an arena of generational slots; each table holds at most
 stripped, as the reference does before upload:
 engine/device_step/README.mbt.md:23-29) that the engine slices directly into
 the per-step descriptor without per-row Python loops.
+
+``BlockTableArena`` is the C++ core (``lunaflux_b200._host.BlockTables``,
+which owns the matrix; Python sees a numpy view) whenever the host extension
+is built; ``PyBlockTableArena`` is the reference implementation it is tested
+against.
 """
 from __future__ import annotations
 
@@ -26,7 +31,7 @@ class TableId(NamedTuple):
     generation: int
 
 
-class BlockTableArena:
+class PyBlockTableArena:
     def __init__(self, capacity: int, max_pages: int, tokens_per_page: int = 16):
         self.capacity = capacity
         self.max_pages = max_pages
@@ -128,3 +133,99 @@ class BlockTableArena:
                 del self._pages[s][n:]
                 self.matrix[s, n:n + extra] = 0
         self._ckpt = None
+
+
+class NativeBlockTableArena:
+    """The same arena backed by the C++ core."""
+
+    def __init__(self, capacity: int, max_pages: int, tokens_per_page: int = 16):
+        from .. import _host
+        self._h = _host
+        self._c = _host.BlockTables(capacity, max_pages, tokens_per_page)
+        self.capacity = capacity
+        self.max_pages = max_pages
+        self.tokens_per_page = tokens_per_page
+        self.matrix = self._c.matrix()      # view of the core's own matrix
+
+    def _call(self, fn, *a):
+        try:
+            return fn(*a)
+        except self._h.BlockTableError as e:
+            raise BlockTableError(str(e)) from None
+        except self._h.PageError as e:
+            from .page_allocator import PageAllocatorError
+            raise PageAllocatorError(str(e)) from None
+
+    def free_table_count(self) -> int:
+        return self._c.free_table_count()
+
+    def allocated_table_count(self) -> int:
+        return self._c.allocated_table_count()
+
+    def allocate(self) -> TableId:
+        return TableId(*self._call(self._c.allocate))
+
+    def release(self, tid: TableId):
+        self._call(self._c.release, tid.index, tid.generation)
+
+    def page_count(self, tid: TableId) -> int:
+        return self._call(self._c.page_count, tid.index, tid.generation)
+
+    def pages(self, tid: TableId) -> List[PageId]:
+        return [PageId(i, g) for i, g in self._call(self._c.pages, tid.index, tid.generation)]
+
+    def append_pages(self, tid: TableId, pids: List[PageId]):
+        self._call(self._c.append_pages, tid.index, tid.generation, pids)
+
+    def page_at(self, tid: TableId, logical: int) -> PageId:
+        return PageId(*self._call(self._c.page_at, tid.index, tid.generation, logical))
+
+    def resolve_token_position(self, tid: TableId, position: int):
+        return self._call(self._c.resolve_token_position, tid.index, tid.generation, position)
+
+    @staticmethod
+    def _native_alloc(allocator):
+        return getattr(allocator, "_c", None) if allocator is not None and hasattr(allocator, "_h") else None
+
+    def truncate(self, tid: TableId, keep: int, allocator: Optional[PageAllocator] = None) -> List[PageId]:
+        na = self._native_alloc(allocator)
+        dropped = [PageId(i, g) for i, g in self._call(self._c.truncate, tid.index, tid.generation, keep, na)]
+        if allocator is not None and na is None:
+            for p in dropped:
+                allocator.release_active(p)
+        return dropped
+
+    def reset_and_release(self, tid: TableId, allocator: PageAllocator):
+        na = self._native_alloc(allocator)
+        if na is not None:
+            self._call(self._c.reset_and_release, tid.index, tid.generation, na)
+        else:
+            self.truncate(tid, 0, allocator)
+            self.release(tid)
+
+    def checkpoint(self):
+        self._call(self._c.checkpoint)
+        return True
+
+    def note(self, tid: TableId):
+        self._c.note(tid.index)
+
+    def commit_checkpoint(self):
+        self._c.commit_checkpoint()
+
+    def rollback(self):
+        self._c.rollback()
+
+    def debug_check_invariants(self):
+        self._call(self._c.debug_check_invariants)
+
+
+def _select():
+    import os
+    from .page_allocator import native_available
+    if os.environ.get("LUNAFLUX_HOST_CORE", "native") == "native" and native_available():
+        return NativeBlockTableArena
+    return PyBlockTableArena
+
+
+BlockTableArena = _select()

@@ -12,6 +12,12 @@ linearly (O(tokens x nodes)); here each edge is one page of tokens, children
 are found by a dict keyed on that page's token tuple, so a lookup is O(pages)
 and eviction pops leaves from a recency heap.  Unlike the reference, this
 index is wired into the scheduler's admission path.
+
+``PrefixIndex(allocator, ...)`` builds the C++ core (``_host.PrefixTree``,
+which takes and drops its cached page references in the native allocator
+directly) when the allocator is the native one, else ``PyPrefixIndex``, the
+reference implementation the core is tested against.  Both return opaque
+node handles from ``lookup``; ``pages_of`` maps them to their PageIds.
 """
 from __future__ import annotations
 
@@ -43,7 +49,7 @@ class _Node:
     depth: int = 0
 
 
-class PrefixIndex:
+class PyPrefixIndex:
     def __init__(self, allocator: PageAllocator, tokens_per_page: int, max_pages: int = 1 << 30):
         self.allocator = allocator
         self.P = tokens_per_page
@@ -94,6 +100,9 @@ class PrefixIndex:
             self.hit_tokens += len(out) * self.P
             self._push_leaf(out[-1])
         return out
+
+    def pages_of(self, nodes: Sequence[_Node]) -> List[PageId]:
+        return [n.page for n in nodes]
 
     def retain(self, nodes: Sequence[_Node]):
         for n in nodes:
@@ -177,3 +186,85 @@ class PrefixIndex:
                 assert c.parent is n
                 stack.append((c, d + 1))
         assert total == self._pages
+
+
+class NativePrefixIndex:
+    """The same index backed by the C++ core; node handles are ints."""
+
+    def __init__(self, allocator, tokens_per_page: int, max_pages: int = 1 << 30):
+        from .. import _host
+        self._h = _host
+        self.allocator = allocator
+        self.P = tokens_per_page
+        self.max_pages = max_pages
+        self._c = _host.PrefixTree(allocator._c, tokens_per_page, max_pages)
+        self._roots: Dict[PrefixIdentity, int] = {}
+
+    def _call(self, fn, *a):
+        try:
+            return fn(*a)
+        except self._h.PrefixError as e:
+            raise RuntimeError(str(e)) from None
+        except self._h.PageError as e:
+            from ..kv.page_allocator import PageAllocatorError
+            raise PageAllocatorError(str(e)) from None
+
+    def _root(self, ident: PrefixIdentity) -> int:
+        if ident.tokens_per_page != self.P:
+            raise ValueError("identity layout does not match this index")
+        r = self._roots.get(ident)
+        if r is None:
+            r = self._roots[ident] = self._c.new_root()
+        return r
+
+    @property
+    def hits(self) -> int:
+        return self._c.stats()[0]
+
+    @property
+    def lookups(self) -> int:
+        return self._c.stats()[1]
+
+    @property
+    def hit_tokens(self) -> int:
+        return self._c.stats()[2]
+
+    @property
+    def evicted_pages(self) -> int:
+        return self._c.stats()[3]
+
+    def page_count(self) -> int:
+        return self._c.page_count()
+
+    def lookup(self, ident: PrefixIdentity, tokens: Sequence[int], max_pages: Optional[int] = None) -> List[int]:
+        return self._call(self._c.lookup, self._root(ident), tokens, -1 if max_pages is None else max(0, max_pages))
+
+    def pages_of(self, nodes: Sequence[int]) -> List[PageId]:
+        return [PageId(i, g) for i, g in self._call(self._c.pages_of, list(nodes))]
+
+    def retain(self, nodes: Sequence[int]):
+        self._call(self._c.retain, list(nodes))
+
+    def release(self, nodes: Sequence[int]):
+        self._call(self._c.release, list(nodes))
+
+    def insert(self, ident: PrefixIdentity, tokens: Sequence[int], pages: Sequence[PageId]) -> int:
+        return self._call(self._c.insert, self._root(ident), tokens, list(pages))
+
+    def evict(self, pages_needed: int) -> int:
+        return self._call(self._c.evict, pages_needed)
+
+    def evictable_pages(self) -> int:
+        return self._c.evictable_pages()
+
+    def debug_check_invariants(self):
+        self._call(self._c.debug_check_invariants)
+
+
+def PrefixIndex(allocator, tokens_per_page: int, max_pages: int = 1 << 30):
+    """The prefix index for `allocator`: the C++ core over the native page
+    allocator (unless LUNAFLUX_HOST_CORE=python), else the Python class."""
+    import os
+    if hasattr(allocator, "_c") and hasattr(allocator, "_h") and os.environ.get("LUNAFLUX_HOST_CORE", "native") == "native":
+        return NativePrefixIndex(allocator, tokens_per_page, max_pages)
+    return PyPrefixIndex(allocator, tokens_per_page, max_pages)

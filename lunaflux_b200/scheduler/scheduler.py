@@ -339,7 +339,7 @@ class Scheduler:
             if nodes:
                 self.prefix.retain(nodes)
                 req.prefix_nodes = nodes
-                pids = [n.page for n in nodes]
+                pids = self.prefix.pages_of(nodes)
                 for p in pids:
                     self.allocator.retain_active(p)
                 self.tables.append_pages(req.table, pids)

@@ -3,8 +3,8 @@
     python setup.py build_ext --inplace
 
 * ``lunaflux_b200._C``    hand-written sm_100a CUDA kernels (tcgen05/TMA/mma).
-* ``lunaflux_b200._host`` C++ host runtime: page allocator, BPE encoder,
-  process channel, approved filesystem.
+* ``lunaflux_b200._host`` C++ host runtime: page allocator, block tables,
+  radix prefix tree, BPE encoder, process channel, approved filesystem.
 
 Only sm_100a (B200) code is generated.
 """

@@ -142,7 +142,7 @@ def test_radix_lookup_insert_full_pages_only():
     assert idx.insert(ident(), toks, pids) == 2  # only 2 full pages of 4
     assert idx.page_count() == 2
     hit = idx.lookup(ident(), list(range(8)) + [99])
-    assert [n.page for n in hit] == pids[:2]
+    assert idx.pages_of(hit) == pids[:2]
     assert idx.lookup(ident(b"other"), toks) == []  # identity salting
     assert idx.lookup(ident(), [1] + toks) == []
     idx.debug_check_invariants()
