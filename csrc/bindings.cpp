@@ -365,7 +365,7 @@ void partials_allreduce(const at::Tensor& ws, int64_t M, int64_t N, int64_t spli
 }
 
 void gemm_fp8(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, const at::Tensor& sb, at::Tensor& D,
-              int64_t epi) {
+              int64_t epi, c10::optional<at::Tensor> ws) {
   check_rowmajor(A, "A");
   check_rowmajor(B, "B");
   check_rowmajor(D, "D");
@@ -379,7 +379,15 @@ void gemm_fp8(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, co
   c10::cuda::CUDAGuard g(A.device());
   lf::fp8::Fp8Args a{A.data_ptr(), B.data_ptr(), sa.data_ptr<float>(), sa.stride(0), sb.data_ptr<float>(), D.data_ptr(),
                      M, N, K, A.stride(0), B.stride(0), D.stride(0)};
-  lf::fp8::run(a, (int)epi, stream());
+  float* w = nullptr;
+  int64_t w_elems = 0;
+  if (ws.has_value()) {   // all-zero fp32 split-K workspace (left all-zero)
+    LF_CHECK(ws->scalar_type() == at::kFloat && ws->is_contiguous() && ws->device() == A.device(),
+             "fp8 gemm workspace: contiguous fp32 on the operands' device");
+    w = ws->data_ptr<float>();
+    w_elems = ws->numel();
+  }
+  lf::fp8::run(a, (int)epi, stream(), w, w_elems);
 }
 
 void act_quant(const at::Tensor& x, at::Tensor& q, at::Tensor& s) {
@@ -673,7 +681,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_grouped", &gemm_grouped, py::arg("A"), py::arg("B"), py::arg("D"), py::arg("groups"),
         py::arg("num_groups"), py::arg("epi"), py::arg("align") = 128);
-  m.def("gemm_fp8", &gemm_fp8);
+  m.def("gemm_fp8", &gemm_fp8, py::arg("A"), py::arg("sa"), py::arg("B"), py::arg("sb"), py::arg("D"), py::arg("epi"),
+        py::arg("ws") = py::none());
+  m.def("fp8_plan_splits", [](int tiles, int num_kb, int sms) {
+    int per = 0;
+    const int s = lf::fp8::plan_splits(tiles, num_kb, sms, &per);
+    return py::make_tuple(s, per);
+  });
   m.def("partials_allreduce", &partials_allreduce);
   m.def("gemm_allreduce_ll", &gemm_allreduce_ll);
   m.def("gemm_reduce_scatter", &gemm_reduce_scatter);

@@ -17,6 +17,13 @@
 //   warps 2..5  scale-and-accumulate, then the epilogue (bf16 store, fp32
 //               store, or SwiGLU over 32-row interleaved gate/up weights)
 // All waits are bounded (common.cuh); every TMA load fills only its own CTA.
+//
+// Split-K (decode shapes with fewer tiles than SMs): a work item is a (tile,
+// K range) pair; each item adds its fp32 partial tile into a zeroed fp32
+// workspace [M, N] with vector atomics (red.global.add on L2), and a finalize
+// kernel applies the epilogue and zeroes the workspace again.  The order of
+// the partial sums is not fixed, so split results may differ in the last
+// fp32 bits from run to run.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
@@ -48,7 +55,7 @@ template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const float* __restrict__ sa, int64_t lds_a, const float* __restrict__ sb, void* __restrict__ out,
-                    int M, int N, int K, int64_t ldd) {
+                    int M, int N, int K, int64_t ldd, int splits, int kb_per, float* __restrict__ ws) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
@@ -59,6 +66,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM, num_n = N / BN, tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
+  const int items = tiles * splits;
   constexpr uint32_t kCols = 2 * BN;
 
   if (threadIdx.x == 0) {
@@ -89,9 +97,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const int tile = item % tiles, kb0 = (item / tiles) * kb_per;
+        const int kb1 = min(num_kb, kb0 + kb_per);
         const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, 31)) { ok = false; break; }
           uint8_t* sa_s = smem + stage * kStageBytes;
           mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
@@ -107,8 +117,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, tb = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-        for (int kb = 0; kb < num_kb; ++kb, ++tb) {
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const int kb0 = (item / tiles) * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+        for (int kb = kb0; kb < kb1; ++kb, ++tb) {
           const int b = tb & 1;
           if (!mbar_wait(&tempty[b], ((tb >> 1) & 1) ^ 1, 32)) { ok = false; break; }
           if (!mbar_wait(&full_bar[stage], phase, 33)) { ok = false; break; }
@@ -130,7 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ksb = (K + BK - 1) / BK;  // scale blocks per row
     uint32_t tb = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+    for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+      const int tile = item % tiles, kb0 = (item / tiles) * kb_per;
+      const int kb1 = min(num_kb, kb0 + kb_per);
       const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
       const int row = m0 + quad * 32 + lane;
       const int rr = row < M ? row : M - 1;
@@ -139,13 +152,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < BN; ++j) acc[j] = 0.f;
       const float* sa_row = sa + (size_t)rr * lds_a;
       const float* sb_blk = sb + (size_t)(n0 / 128) * ksb;
-      float scale_next = sa_row[0] * sb_blk[0];
-      for (int kb = 0; kb < num_kb; ++kb, ++tb) {
+      float scale_next = sa_row[kb0] * sb_blk[kb0];
+      for (int kb = kb0; kb < kb1; ++kb, ++tb) {
         const int b = tb & 1;
         // this block's scale was loaded during the previous block; the next
         // one is requested before waiting for the accumulator
         const float scale = scale_next;
-        if (kb + 1 < num_kb) scale_next = sa_row[kb + 1] * sb_blk[kb + 1];
+        if (kb + 1 < kb1) scale_next = sa_row[kb + 1] * sb_blk[kb + 1];
         if (!mbar_wait(&tfull[b], (tb >> 1) & 1, 34)) { ok = false; break; }
         tc_fence_after();
         const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + b * BN;
@@ -165,6 +178,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&tempty[b]);
       }
       if (!ok || row >= M) continue;
+      if (splits > 1) {
+        float* dst = ws + (size_t)row * N + n0;
+#pragma unroll
+        for (int j = 0; j < BN; j += 4)
+          atomicAdd(reinterpret_cast<float4*>(dst + j), make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]));
+        continue;
+      }
       if constexpr (EPI == kSwiGLU) {
         __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + n0 / 2;
 #pragma unroll
@@ -200,6 +220,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kCols);
+  }
+}
+
+// Split-K finalize: out = epilogue(ws), then ws = 0.  One thread per 8
+// output columns (bf16 / fp32), or per 8 SwiGLU outputs (16 workspace
+// columns: 8 gate, and the 8 up columns 32 further on).
+template <int EPI>
+__global__ void splitk_finalize_kernel(float* __restrict__ ws, void* __restrict__ out, int M, int N, int64_t ldd) {
+  pdl_trigger();
+  pdl_wait();
+  const int per_row = EPI == kSwiGLU ? N / 16 : N / 8;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)M * per_row) return;
+  const int row = (int)(i / per_row), c = (int)(i % per_row);
+  float* src = ws + (size_t)row * N;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  if constexpr (EPI == kSwiGLU) {
+    const int g = c / 4, j = (c % 4) * 8;             // group of 64 columns, 8 of its 32 outputs
+    float4* gp = reinterpret_cast<float4*>(src + g * 64 + j);
+    float4* up = reinterpret_cast<float4*>(src + g * 64 + 32 + j);
+    const float4 g0 = gp[0], g1 = gp[1], u0 = up[0], u1 = up[1];
+    gp[0] = z; gp[1] = z; up[0] = z; up[1] = z;
+    uint4 v = make_uint4(pack_bf16x2(silu(g0.x) * u0.x, silu(g0.y) * u0.y), pack_bf16x2(silu(g0.z) * u0.z, silu(g0.w) * u0.w),
+                         pack_bf16x2(silu(g1.x) * u1.x, silu(g1.y) * u1.y), pack_bf16x2(silu(g1.z) * u1.z, silu(g1.w) * u1.w));
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + g * 32 + j) = v;
+  } else {
+    float4* p = reinterpret_cast<float4*>(src + c * 8);
+    const float4 a = p[0], b = p[1];
+    p[0] = z;
+    p[1] = z;
+    if constexpr (EPI == kF32) {
+      float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)row * ldd + c * 8);
+      d[0] = a;
+      d[1] = b;
+    } else {
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)row * ldd + c * 8) =
+          make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+    }
   }
 }
 
@@ -256,7 +314,7 @@ CUtensorMap map_u8(const void* p, uint64_t rows, uint64_t cols, uint64_t ld, uin
   return m;
 }
 template <int EPI>
-void launch(const Fp8Args& a, cudaStream_t s) {
+void launch(const Fp8Args& a, cudaStream_t s, float* ws, int64_t ws_elems) {
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(gemm_fp8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
@@ -265,17 +323,39 @@ void launch(const Fp8Args& a, cudaStream_t s) {
   const CUtensorMap ta = map_u8(a.A, a.M, a.K, a.lda, BM);
   const CUtensorMap tb = map_u8(a.B, a.N, a.K, a.ldb, BN);
   const int tiles = ((a.M + BM - 1) / BM) * (a.N / BN);
-  const int grid = tiles < sms() ? tiles : sms();
-  gemm_fp8_kernel<EPI><<<grid, kThreads, kSmem, s>>>(ta, tb, a.sa, a.lds_a, a.sb, a.D, a.M, a.N, a.K, a.ldd);
+  int kb_per = 0;
+  const int splits = (ws != nullptr && (int64_t)a.M * a.N <= ws_elems) ? plan_splits(tiles, a.K / BK, sms(), &kb_per) : 1;
+  if (splits == 1) kb_per = a.K / BK;
+  const int items = tiles * splits;
+  const int grid = items < sms() ? items : sms();
+  gemm_fp8_kernel<EPI><<<grid, kThreads, kSmem, s>>>(ta, tb, a.sa, a.lds_a, a.sb, a.D, a.M, a.N, a.K, a.ldd, splits,
+                                                     kb_per, ws);
+  if (splits > 1) {
+    const int64_t threads = (int64_t)a.M * (EPI == kSwiGLU ? a.N / 16 : a.N / 8);
+    launch_k(splitk_finalize_kernel<EPI>, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, s, 1, ws, a.D, a.M, a.N,
+             a.ldd);
+  }
 }
 }  // namespace
 
-void run(const Fp8Args& a, int epi, cudaStream_t s) {
+int plan_splits(int tiles, int num_kb, int sms, int* kb_per) {
+  // Fill about one wave: as many K splits as the tiles leave SMs free, each
+  // split at least 4 K blocks (512 channels) so the pipeline fill amortises.
+  int splits = tiles >= sms ? 1 : sms / tiles;
+  const int max_splits = num_kb / 4;
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  const int per = (num_kb + splits - 1) / splits;
+  *kb_per = per;
+  return (num_kb + per - 1) / per;
+}
+
+void run(const Fp8Args& a, int epi, cudaStream_t s, float* ws, int64_t ws_elems) {
   if (a.M <= 0) return;
   if (a.N % BN != 0 || a.K % BK != 0) throw std::runtime_error("lunaflux fp8 gemm: N and K must be multiples of 128");
-  if (epi == kSwiGLU) launch<kSwiGLU>(a, s);
-  else if (epi == kF32) launch<kF32>(a, s);
-  else launch<kBf16>(a, s);
+  if (epi == kSwiGLU) launch<kSwiGLU>(a, s, ws, ws_elems);
+  else if (epi == kF32) launch<kF32>(a, s, ws, ws_elems);
+  else launch<kBf16>(a, s, ws, ws_elems);
 }
 
 void act_quant(const void* x, int64_t ldx, int M, int K, void* q, float* s, int64_t lds, cudaStream_t st) {

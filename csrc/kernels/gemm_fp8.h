@@ -17,7 +17,12 @@ struct Fp8Args {
 };
 
 // epi: 0 bf16, 1 fp32, 2 SwiGLU (gate/up rows interleaved in groups of 32).
-void run(const Fp8Args& a, int epi, cudaStream_t s);
+// ws: an all-zero fp32 workspace of ws_elems (>= M * N for split-K; null or
+// too small: no split); it is all-zero again when the GEMM has run.
+void run(const Fp8Args& a, int epi, cudaStream_t s, float* ws = nullptr, int64_t ws_elems = 0);
+// K splits for `tiles` output tiles over num_kb 128-wide K blocks on `sms`
+// SMs (1: no split); *kb_per receives the K blocks per split.
+int plan_splits(int tiles, int num_kb, int sms, int* kb_per);
 // Per-token, per-128-channel e4m3 quantisation of a bf16 activation.
 void act_quant(const void* x, int64_t ldx, int M, int K, void* q, float* s, int64_t lds, cudaStream_t st);
 

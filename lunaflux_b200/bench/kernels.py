@@ -287,7 +287,10 @@ def bench_fp8(C, results):
             q, s_ = quantize_act(x)
             q, s_ = q.cuda().contiguous(), s_.cuda().contiguous()
             out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-            ms = time_fn(lambda: C.gemm_fp8(q, s_, w8.cuda(), sw.cuda(), out, 0))
+            w8c, swc = w8.cuda(), sw.cuda()
+            ms_nosplit = time_fn(lambda: C.gemm_fp8(q, s_, w8c, swc, out, 0))
+            ws = torch.zeros(M * N, device="cuda") if M <= 256 else None
+            ms = time_fn(lambda: C.gemm_fp8(q, s_, w8c, swc, out, 0, ws)) if ws is not None else ms_nosplit
             wb = w.bfloat16()
             base_bf16 = time_fn(lambda: x @ wb.t())
             scaled = None
@@ -300,7 +303,8 @@ def bench_fp8(C, results):
             except Exception:
                 pass
             flops = 2.0 * M * N * K
-            r = dict(kernel="gemm_fp8_block", case=f"M{M} {name}", M=M, N=N, K=K, ours_ms=ms, cublas_bf16_ms=base_bf16,
+            r = dict(kernel="gemm_fp8_block", case=f"M{M} {name}", M=M, N=N, K=K, ours_ms=ms, ours_no_split_ms=ms_nosplit,
+                     cublas_bf16_ms=base_bf16,
                      scaled_mm_rowwise_ms=scaled, tflops=flops / ms / 1e9, peaks=src)
             results.append(r)
             print(json.dumps(r))

@@ -140,6 +140,10 @@ class ModelRunner:
             kmax = max(H, self.Hq * self.D, sh.ffn_padded)
             self.q8 = torch.zeros(T * kmax, dtype=torch.float8_e4m3fn, device=dev)
             self.q8s = torch.zeros(T * (kmax // 128), dtype=torch.float32, device=dev)
+            # split-K workspace of the decode-sized fp8 GEMMs (all-zero between GEMMs)
+            nmax = max(H, sh.qkv_size, 2 * sh.ffn_padded)
+            self.fp8_ws = (torch.zeros(min(T, 256) * nmax, dtype=torch.float32, device=dev)
+                           if dev.type == "cuda" else None)
         self.keys_local = torch.zeros(R, dtype=torch.int64, device=dev)
         self.keys_all = torch.zeros(R * sh.size, dtype=torch.int64, device=dev)
         # Vocabulary-parallel stochastic sampling from per-shard candidates
@@ -378,7 +382,7 @@ class ModelRunner:
         f = self._fp8(lw, name)
         if f is not None:
             q, s = self._quant(A)
-            self.ops.gemm_fp8(q, s, f[0], f[1], out, 0)
+            self.ops.gemm_fp8(q, s, f[0], f[1], out, 0, self.fp8_ws)
         else:
             self.ops.gemm(A, getattr(lw, name), out, 0, ws)
 
@@ -399,7 +403,7 @@ class ModelRunner:
         f = self._fp8(lw, name)
         if f is not None:
             q, s = self._quant(x)
-            self.ops.gemm_fp8(q, s, f[0], f[1], out, epi)
+            self.ops.gemm_fp8(q, s, f[0], f[1], out, epi, self.fp8_ws)
         else:
             self.ops.gemm(x, getattr(lw, name), out, epi, self.gemm_ws)
 
@@ -415,10 +419,10 @@ class ModelRunner:
             q, s = self._quant(A)
             if fused:
                 part = ws[: out.numel()].view(out.shape)
-                self.ops.gemm_fp8(q, s, f[0], f[1], part, 1)
+                self.ops.gemm_fp8(q, s, f[0], f[1], part, 1, self.fp8_ws)
                 self.ops.launches += 1
                 return self.comm.reduce_partials(part)
-            self.ops.gemm_fp8(q, s, f[0], f[1], out, 0)
+            self.ops.gemm_fp8(q, s, f[0], f[1], out, 0, self.fp8_ws)
             if self.comm is not None:
                 self.comm.all_reduce(out)
             return out

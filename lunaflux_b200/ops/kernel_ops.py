@@ -132,6 +132,14 @@ class KernelOps:
         self.launches += 1
         self.C.act_quant(x, q, s)
 
-    def gemm_fp8(self, q, s, w8, sw, out, epi):
-        self.launches += 1
-        self.C.gemm_fp8(q, s, w8, sw, out, epi)
+    def gemm_fp8(self, q, s, w8, sw, out, epi, ws=None):
+        """ws: all-zero fp32 split-K workspace (decode shapes split K over the
+        idle SMs and add a finalize kernel)."""
+        M, N, K = q.shape[0], w8.shape[0], q.shape[1]
+        if M == 0:
+            return
+        splits = 1
+        if ws is not None and M * N <= ws.numel():
+            splits = self.C.fp8_plan_splits(-(-M // 128) * (N // 128), K // 128, self.num_sms)[0]
+        self.launches += 2 if splits > 1 else 1
+        self.C.gemm_fp8(q, s, w8, sw, out, epi, ws)

@@ -373,7 +373,7 @@ def launch_checks():
         "sample": lambda logits, params, out: (C["sample"], (logits, params, out), {}),
         "gemm_grouped": lambda A, B, out, groups, num_groups, epi, align=128:
             (C["moe_grouped_linear"], (A, B, out, groups), {"epi": epi, "align": align, "num_groups": num_groups}),
-        "gemm_fp8": lambda q, s, w8, sw, out, epi: (C["linear_fp8"], (q, s, w8, sw, out), {"epi": epi}),
+        "gemm_fp8": lambda q, s, w8, sw, out, epi, ws=None: (C["linear_fp8"], (q, s, w8, sw, out), {"epi": epi}),
         "act_quant": lambda x, q, s: (C["act_quant"], (x, q, s), {}),
         "moe_route": lambda h, router, bias, topk, ids, weights:
             (C["moe_route"], (h, router, bias, ids, weights), {"topk": topk}),

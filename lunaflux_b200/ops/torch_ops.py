@@ -286,7 +286,7 @@ class TorchOps:
         q.copy_(rq)
         s.copy_(rs)
 
-    def gemm_fp8(self, q, s, w8, sw, out, epi):
+    def gemm_fp8(self, q, s, w8, sw, out, epi, ws=None):
         from ..models.fp8 import dequantize_weight
         a = (q.float() * s.repeat_interleave(128, 1)).to(torch.bfloat16)
         w = dequantize_weight(w8, sw).to(torch.bfloat16)

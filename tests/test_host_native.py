@@ -146,7 +146,8 @@ def test_channel_partial_frame_times_out_and_eof_is_closed(native):
         c2.recv(1.0)
 
 
-def test_message_channel_pickles_tuples():
+def test_message_channel_carries_wire_frames():
+    """Control messages cross the channel as binary worker-wire frames (no pickle)."""
     a, b = socket.socketpair()
     ma, mb = chan.MessageChannel(a), chan.MessageChannel(b)
     ma.send(("outs", 1, [(3, 7, False)], [], True))
