@@ -112,6 +112,8 @@ def build_host_step(plan: StepPlan, table_matrix: np.ndarray, P: int, W: int, ou
     # --- prefill rows
     max_q = 0
     max_seq = 0
+    if not Rp:
+        put("p_qstart", (0,))      # the field exists (Rp + 1 = 1 word): no stale word from a reused buffer
     if Rp:
         ns = np.fromiter((r.n for r in pr), dtype=np.int64, count=Rp)
         starts = np.fromiter((r.start for r in pr), dtype=np.int64, count=Rp)

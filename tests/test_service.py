@@ -102,6 +102,27 @@ def test_frame_reader_splits_and_poisons():
         r.feed(b"\x00" * 16)
 
 
+def test_frame_reader_is_chunk_size_invariant():
+    """Three request frames fed in chunks of every size from 1 byte to the
+    whole stream come out as the same frames and decode to the same requests
+    (reference: service/request_admission, 'direct framed preparation is
+    equivalent across every chunk size')."""
+    from lunaflux_b200.service.framed_wire import REQUEST_MAGIC
+    reqs = [full_request(), GenerateRequest(request_id=5, input_tokens=(3,), max_new_tokens=1),
+            GenerateRequest(request_id=6, input_tokens=tuple(range(40)), max_new_tokens=4,
+                            stop=StopConditions((), (b"x",)))]
+    frames = [encode_request(r) for r in reqs]
+    stream = b"".join(frames)
+    for chunk in range(1, len(stream) + 1):
+        rd = FrameReader(REQUEST_MAGIC)
+        got = []
+        for o in range(0, len(stream), chunk):
+            got += rd.feed(stream[o:o + chunk])
+        assert got == frames, chunk
+        assert [decode_request(f, LIM) for f in got] == reqs
+        assert not rd.buf
+
+
 def test_incremental_output_stop_across_tokens_and_utf8():
     o = IncrementalOutput([b"STOP"])
     assert o.push(b"hello S") == (b"hello ", False)  # "S" withheld: may start STOP
