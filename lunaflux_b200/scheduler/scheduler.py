@@ -481,6 +481,10 @@ class Scheduler:
         sampling row, in plan order."""
         if not self.inflight or self.inflight[0] is not plan:
             raise SchedulerError("completion for a plan that is not the oldest in flight")
+        n_sample = sum(1 for r in plan.rows if r.sample)
+        if len(sampled) != n_sample:
+            # checked before anything moves: the plan stays in flight for a correct retry
+            raise SchedulerError(f"completion carries {len(sampled)} tokens for {n_sample} sampling rows")
         self.inflight.pop(0)
         now = self.clock()
         outs: List[TokenOutput] = []

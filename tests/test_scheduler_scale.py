@@ -36,3 +36,33 @@ def test_planning_cost_is_flat_in_the_queue_length():
     small = min(_plan_ms(64) for _ in range(2))
     large = min(_plan_ms(4096) for _ in range(2))
     assert large < 3.0 * small + 0.5, f"{large:.2f} ms with 4096 queued vs {small:.2f} ms with 64"
+
+
+def test_completion_validates_before_mutation():
+    """A completion must carry exactly one token per sampling row and be for
+    the oldest plan in flight; a rejected one changes nothing and the correct
+    completion still applies (reference: engine/worker_protocol completion
+    validation rejects wrong counts and stale plans without mutation)."""
+    import pytest
+    from lunaflux_b200.scheduler.scheduler import SchedulerError
+    cfg = SchedulerConfig(step_token_budget=64, max_active_requests=4, prefill_chunk_tokens=8,
+                          emergency_decode_page_reserve=1)
+    s = Scheduler(cfg, CacheConfig(prefix_enabled=False), 32, None, max_context=128)
+    s.max_inflight = 2
+    for i in range(3):
+        s.add_request(Request(rid=i + 1, prompt=[1 + i] * 12, max_new=3, sampling=SamplingParameters()))
+    first = s.schedule()           # chunks of 8: no row finishes its prompt, nothing sampled
+    second = s.schedule()          # the remaining 4 tokens: every row samples
+    assert not first.sample_rows and len(second.sample_rows) == 3
+    before = [(r.num_computed, list(r.output), r.pending) for r in s.running]
+    with pytest.raises(SchedulerError):
+        s.complete(second, [5, 5, 5])          # not the oldest in flight
+    with pytest.raises(SchedulerError):
+        s.complete(first, [5])                 # a token for a row that samples nothing
+    assert [(r.num_computed, list(r.output), r.pending) for r in s.running] == before
+    assert s.inflight == [first, second]
+    s.complete(first, [])
+    with pytest.raises(SchedulerError):
+        s.complete(second, [5, 5])             # one token short
+    outs = s.complete(second, [5, 6, 7])
+    assert [o.token for o in outs] == [5, 6, 7] and not s.inflight
