@@ -283,8 +283,16 @@ class GenerateRequest:
                 _bad(ContractField.INPUT_TEXT, ContractIssue.INVALID_FORMAT)
         if not (0 < self.max_new_tokens <= limits.max_new_tokens):
             _bad(ContractField.MAXIMUM_NEW_TOKENS, ContractIssue.OUT_OF_RANGE)
-        if self.context_ceiling is not None and not (0 < self.context_ceiling <= limits.max_context_tokens):
-            _bad(ContractField.CONTEXT_CEILING, ContractIssue.OUT_OF_RANGE)
+        if self.context_ceiling is not None:
+            # reference: contracts/inference/request.mbt:272-281 (the prompt and
+            # every requested token must fit under the ceiling)
+            if not (0 < self.context_ceiling <= limits.max_context_tokens):
+                _bad(ContractField.CONTEXT_CEILING, ContractIssue.OUT_OF_RANGE)
+            if self.max_new_tokens > self.context_ceiling:
+                _bad(ContractField.CONTEXT_CEILING, ContractIssue.INCONSISTENT)
+            if (self.input_tokens is not None
+                    and len(self.input_tokens) > self.context_ceiling - self.max_new_tokens):
+                _bad(ContractField.CONTEXT_CEILING, ContractIssue.INCONSISTENT)
         self.sampling.validate(limits)
         self.stop.validate(limits)
         if self.deadline_millis is not None and not (0 < self.deadline_millis <= limits.max_deadline_millis):

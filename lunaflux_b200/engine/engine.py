@@ -108,7 +108,8 @@ class LLMEngine:
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt: Sequence[int], max_new_tokens: int, sampling: SamplingParameters = None,
                     stop_ids: Iterable[int] = (), rid: Optional[int] = None, deadline_s: Optional[float] = None,
-                    cache_scope: bytes = b"", use_prefix_cache: bool = True, arrival: Optional[float] = None) -> int:
+                    cache_scope: bytes = b"", use_prefix_cache: bool = True, arrival: Optional[float] = None,
+                    context_ceiling: Optional[int] = None) -> int:
         if rid is None:
             rid = self._next_rid
             self._next_rid += 1
@@ -118,7 +119,8 @@ class LLMEngine:
         req = Request(rid=rid, prompt=toks, max_new=max_new_tokens, sampling=sampling,
                       stop_ids=frozenset(int(t) for t in stop_ids),
                       deadline=None if deadline_s is None else now + deadline_s, cache_scope=cache_scope,
-                      cache_enabled=use_prefix_cache, arrival=arrival if arrival is not None else now)
+                      cache_enabled=use_prefix_cache, arrival=arrival if arrival is not None else now,
+                      **({} if context_ceiling is None else {"context_ceiling": context_ceiling}))
         self.scheduler.add_request(req)
         self.live[rid] = req
         self.metrics.requests.inc()
@@ -129,7 +131,8 @@ class LLMEngine:
             raise ValueError("text requests must be tokenized by the service layer first")
         return self.add_request(g.input_tokens, g.max_new_tokens, g.sampling, g.stop.token_ids, rid=g.request_id,
                                 deadline_s=None if g.deadline_millis is None else g.deadline_millis / 1000.0,
-                                cache_scope=g.cache.scope, use_prefix_cache=g.cache.permission.value != 0)
+                                cache_scope=g.cache.scope, use_prefix_cache=g.cache.permission.value != 0,
+                                context_ceiling=g.context_ceiling)
 
     def cancel(self, rid: int) -> bool:
         ok = self.scheduler.cancel(rid)

@@ -163,6 +163,10 @@ class EngineService:
         if not prompt or max(prompt) > self.limits.max_token_id:
             sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
             return
+        if req.context_ceiling is not None and len(prompt) > req.context_ceiling - req.max_new_tokens:
+            # a text prompt is measured against the ceiling once it is tokenized
+            sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
+            return
         try:
             self.engine.submit(GenerateRequest(**{**req.__dict__, "input_tokens": tuple(prompt), "input_text": None}))
         except AdmissionRejected as e:

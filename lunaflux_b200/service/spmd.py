@@ -56,12 +56,12 @@ class SpmdLeader:
         return getattr(self._engine, name)
 
     def add_request(self, prompt, max_new_tokens, sampling=None, stop_ids=(), rid=None, deadline_s=None,
-                    cache_scope=b"", use_prefix_cache=True, arrival=None):
+                    cache_scope=b"", use_prefix_cache=True, arrival=None, context_ceiling=None):
         self._clock.now = time.monotonic()
         rid = self._engine.add_request(prompt, max_new_tokens, sampling, stop_ids, rid, deadline_s, cache_scope,
-                                       use_prefix_cache, arrival)
+                                       use_prefix_cache, arrival, context_ceiling)
         self._log.append(("add", (list(prompt), max_new_tokens, sampling, tuple(stop_ids), rid, deadline_s,
-                                  cache_scope, use_prefix_cache, self._clock.now)))
+                                  cache_scope, use_prefix_cache, self._clock.now, context_ceiling)))
         return rid
 
     def submit(self, g):
@@ -98,9 +98,10 @@ def follower_loop(engine, clock: SharedClock, group=None, on_step: Optional[Call
         now, log, step = msg
         for kind, payload in log:
             if kind == "add":
-                prompt, max_new, sampling, stop_ids, rid, deadline_s, scope, use_prefix, t_add = payload
+                prompt, max_new, sampling, stop_ids, rid, deadline_s, scope, use_prefix, t_add, ceiling = payload
                 clock.now = t_add
-                engine.add_request(prompt, max_new, sampling, stop_ids, rid, deadline_s, scope, use_prefix)
+                engine.add_request(prompt, max_new, sampling, stop_ids, rid, deadline_s, scope, use_prefix,
+                                   context_ceiling=ceiling)
             else:
                 engine.cancel(payload)
         clock.now = now

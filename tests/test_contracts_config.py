@@ -117,3 +117,17 @@ def test_specs_and_digests():
     with pytest.raises(SpecError):
         LlamaSpec(hidden=64, layers=1, heads=3, kv_heads=2, head_dim=16, ffn=64, vocab=10)
     assert tiny_llama().group == 2
+
+
+def test_context_ceiling_consistency():
+    """The prompt and every requested token must fit under the ceiling
+    (reference: contracts/inference/request.mbt:272-281)."""
+    lim = default_limits(1000, 4096)
+    GenerateRequest(1, input_tokens=(1,) * 6, max_new_tokens=4, context_ceiling=10).validate(lim)
+    for toks, new, ceil in (((1,) * 7, 4, 10), ((1,), 11, 10)):
+        with pytest.raises(ContractError) as e:
+            GenerateRequest(1, input_tokens=toks, max_new_tokens=new, context_ceiling=ceil).validate(lim)
+        assert (e.value.field, e.value.issue) == (ContractField.CONTEXT_CEILING, ContractIssue.INCONSISTENT)
+    with pytest.raises(ContractError) as e:
+        GenerateRequest(1, input_tokens=(1,), max_new_tokens=4, context_ceiling=5000).validate(lim)
+    assert e.value.issue is ContractIssue.OUT_OF_RANGE
