@@ -314,16 +314,18 @@ def bench_moe(C, results):
     """Mixtral-8x7B MoE layer pieces at one GPU (8 experts, top 2): routing,
     alignment, gather, grouped gate/up + SwiGLU, grouped down, combine; the
     library baseline loops over experts with index_select + cuBLAS."""
+    from ..engine.runner import ModelRunner
     _, _, src = peaks()
     E, topk, H, F = 8, 2, 4096, 14336
     for T in (512, 8192):
+        al = 256 if T >= ModelRunner.MOE_PAIR_TOKENS else 128      # the runner's segment alignment
         h = torch.randn(T, H, device="cuda").bfloat16()
         router = torch.randn(E, H, device="cuda") * 0.02
         wgu = (torch.randn(E, 2 * F, H, device="cuda") * 0.02).bfloat16()
         wd = (torch.randn(E, H, F, device="cuda") * 0.02).bfloat16()
         ids = torch.empty(T, topk, dtype=torch.int32, device="cuda")
         wts = torch.empty(T, topk, dtype=torch.float32, device="cuda")
-        cap = -(-(T * topk + E * 127) // 128) * 128
+        cap = -(-(T * topk + E * (al - 1)) // al) * al
         groups = torch.empty(E + 1, dtype=torch.int32, device="cuda")
         perm = torch.empty(cap, dtype=torch.int32, device="cuda")
         slot = torch.empty(T * topk, dtype=torch.int32, device="cuda")
@@ -334,19 +336,19 @@ def bench_moe(C, results):
 
         def ours():
             C.moe_route(h, router, None, topk, ids, wts)
-            C.moe_align(ids, T, topk, 0, E, groups, perm, slot)
+            C.moe_align(ids, T, topk, 0, E, groups, perm, slot, al)
             C.moe_gather(h, perm, groups, E, topk, xg)
-            C.gemm_grouped(xg, wgu, act, groups, E, 2)
-            C.gemm_grouped(act, wd, y, groups, E, 0)
+            C.gemm_grouped(xg, wgu, act, groups, E, 2, al)
+            C.gemm_grouped(act, wd, y, groups, E, 0, al)
             C.moe_combine(y, slot, wts, T, topk, out)
 
         pieces = {}
         ours()
         for key, fn in (("route", lambda: C.moe_route(h, router, None, topk, ids, wts)),
-                        ("align", lambda: C.moe_align(ids, T, topk, 0, E, groups, perm, slot)),
+                        ("align", lambda: C.moe_align(ids, T, topk, 0, E, groups, perm, slot, al)),
                         ("gather", lambda: C.moe_gather(h, perm, groups, E, topk, xg)),
-                        ("grouped_gate_up", lambda: C.gemm_grouped(xg, wgu, act, groups, E, 2)),
-                        ("grouped_down", lambda: C.gemm_grouped(act, wd, y, groups, E, 0)),
+                        ("grouped_gate_up", lambda: C.gemm_grouped(xg, wgu, act, groups, E, 2, al)),
+                        ("grouped_down", lambda: C.gemm_grouped(act, wd, y, groups, E, 0, al)),
                         ("combine", lambda: C.moe_combine(y, slot, wts, T, topk, out))):
             pieces[key] = time_fn(fn)
         total = time_fn(ours)
@@ -368,7 +370,9 @@ def bench_moe(C, results):
             return acc
 
         base = time_fn(library)
-        r = dict(kernel="moe_layer", tokens=T, experts=E, topk=topk, ours_ms=total, pieces_ms=pieces,
+        flops = 2.0 * T * topk * (2 * F * H + F * H)
+        r = dict(kernel="moe_layer", tokens=T, experts=E, topk=topk, align=al, ours_ms=total, pieces_ms=pieces,
+                 expert_tflops=flops / (pieces["grouped_gate_up"] + pieces["grouped_down"]) / 1e9,
                  library_ms=base, speedup=base / total, peaks=src)
         results.append(r)
         print(json.dumps(r))
