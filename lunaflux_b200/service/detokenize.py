@@ -6,7 +6,9 @@ string is matched across token and code-point boundaries, any suffix that may
 still grow into a stop string is withheld, and the withheld tail is flushed
 with the terminal event.  Matching here uses the Knuth-Morris-Pratt failure
 function of each stop string, advanced byte by byte, so the scan is linear in
-the output and never re-reads released bytes.
+the output and never re-reads released bytes.  Every released delta is
+valid UTF-8: bytes that cannot start or continue a scalar (an unknown
+token's raw bytes, a stray continuation byte) are published as U+FFFD.
 """
 from __future__ import annotations
 
@@ -39,6 +41,15 @@ def _utf8_complete_prefix(b: bytes) -> int:
     need = 1 if lead < 0x80 else 2 if (lead & 0xE0) == 0xC0 else 3 if (lead & 0xF0) == 0xE0 else \
         4 if (lead & 0xF8) == 0xF0 else 1
     return n if n - i >= need else i
+
+
+def _safe(b: bytes) -> bytes:
+    """Valid UTF-8 for a released range (it never ends inside a sequence)."""
+    try:
+        b.decode("utf-8")
+        return b
+    except UnicodeDecodeError:
+        return b.decode("utf-8", errors="replace").encode("utf-8")
 
 
 class IncrementalOutput:
@@ -75,13 +86,13 @@ class IncrementalOutput:
                 break
         if cut is not None:
             self.stopped = True
-            delta = bytes(self.buf[self.released:cut])
+            delta = _safe(bytes(self.buf[self.released:cut]))
             self.released = cut
             return delta, True
         hold = max(self.state) if self.state else 0
         safe = len(self.buf) - hold
         safe = self.released + _utf8_complete_prefix(bytes(self.buf[self.released:safe]))
-        delta = bytes(self.buf[self.released:safe])
+        delta = _safe(bytes(self.buf[self.released:safe]))
         self.released = safe
         return delta, False
 

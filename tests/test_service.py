@@ -384,3 +384,29 @@ def test_graceful_drain():
         time.sleep(0.01)
     assert not eng.has_work()
     svc.stop()
+
+
+def test_incremental_output_is_payload_safe_and_split_invariant():
+    """Random byte pieces (valid text, stray continuation bytes, 0xFF,
+    truncated sequences), no stop strings: every delta is valid UTF-8 and the
+    deltas plus the terminal tail equal the replacement-decoded whole output,
+    however the bytes were split into tokens (reference: incremental_output
+    'UTF-8 split across byte tokens publishes only a complete scalar',
+    'invalid UTF-8 unknown tokens ... are payload safe')."""
+    import random
+    rng = random.Random(3)
+    alphabet = [b"a", b"\xc3\xa9", b"\xe2\x82\xac", b"\xf0\x9f\x98\x80", b"\xff", b"\x80", b"\xe2\x82", b" "]
+    for trial in range(300):
+        raw = b"".join(rng.choice(alphabet) for _ in range(rng.randint(0, 12)))
+        cuts = sorted(rng.sample(range(1, len(raw)), min(len(raw) - 1, rng.randint(0, 6)))) if len(raw) > 1 else []
+        pieces = [raw[a:b] for a, b in zip([0] + cuts, cuts + [len(raw)])] if raw else []
+        io = IncrementalOutput(())
+        out = b""
+        for pc in pieces:
+            d, hit = io.push(pc)
+            d.decode("utf-8")                      # valid on its own
+            assert not hit
+            out += d
+        tail = io.finish()
+        tail.decode("utf-8")
+        assert (out + tail).decode("utf-8") == raw.decode("utf-8", errors="replace"), (raw, pieces)
