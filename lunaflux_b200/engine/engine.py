@@ -26,7 +26,7 @@ from ..metrics import EngineMetrics
 from ..models.spec import LlamaSpec
 from ..models.weights import ModelWeights
 from ..prefix.radix import PrefixIdentity
-from ..scheduler.scheduler import Request, Scheduler, StepPlan, TokenOutput
+from ..scheduler.scheduler import AdmissionRejected, Request, Scheduler, StepPlan, TokenOutput
 from .runner import ModelRunner, StepFailed  # noqa: F401  (re-exported)
 
 
@@ -65,6 +65,13 @@ class RequestResult:
         if self.first_token_time is None or self.finish_time is None or len(self.tokens) < 2:
             return None
         return (self.finish_time - self.first_token_time) / (len(self.tokens) - 1)
+
+
+def check_token_ids(toks, vocab: int):
+    """Admission rejects prompt ids outside the loaded vocabulary (they would
+    otherwise reach the embedding kernel and fail the whole step)."""
+    if toks and (min(toks) < 0 or max(toks) >= vocab):
+        raise AdmissionRejected(PublicErrorCode.INVALID_REQUEST, "prompt token id outside the model's vocabulary")
 
 
 class LLMEngine:
@@ -116,6 +123,7 @@ class LLMEngine:
         sampling = sampling or SamplingParameters()
         now = self.clock()
         toks = prompt.tolist() if hasattr(prompt, "tolist") else [int(t) for t in prompt]   # plain ints
+        check_token_ids(toks, self.spec.vocab)
         req = Request(rid=rid, prompt=toks, max_new=max_new_tokens, sampling=sampling,
                       stop_ids=frozenset(int(t) for t in stop_ids),
                       deadline=None if deadline_s is None else now + deadline_s, cache_scope=cache_scope,

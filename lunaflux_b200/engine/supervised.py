@@ -59,10 +59,13 @@ class SupervisedEngine:
     # ------------------------------------------------------------ requests
     def add_request(self, prompt, max_new_tokens: int, sampling=None, stop_ids=(), rid: Optional[int] = None,
                     deadline_s=None, cache_scope=b"", use_prefix_cache=True, arrival=None) -> int:
+        from .engine import check_token_ids
+        prompt = list(prompt)
+        check_token_ids(prompt, self.spec.vocab)     # rejected here, before any rank sees it
         if rid is None:
             rid = self._next_rid
         self._next_rid = max(self._next_rid, rid + 1)
-        self.sup.submit(rid, list(prompt), max_new_tokens, sampling, tuple(stop_ids))
+        self.sup.submit(rid, prompt, max_new_tokens, sampling, tuple(stop_ids))
         self._live[rid] = {"prompt_len": len(prompt), "tokens": [], "arrival": self.clock() if arrival is None
                            else arrival, "first": None}
         return rid

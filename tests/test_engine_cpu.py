@@ -191,3 +191,17 @@ def test_page_starvation_never_stalls(tiny):
     assert eng.results[big].error is PublicErrorCode.CONTEXT_OVERFLOW
     assert 0 < len(eng.results[big].tokens) < 40
     assert eng.scheduler.allocator.allocated_page_count() == 0
+
+
+def test_admission_rejects_token_ids_outside_the_vocabulary(tiny):
+    """Reference: scheduler/core 'admission rejects token IDs outside the
+    loaded worker vocabulary'; nothing is queued and the engine keeps serving."""
+    from lunaflux_b200.scheduler.scheduler import AdmissionRejected
+    spec, ck = tiny
+    eng = engine(spec, ck)
+    for bad in ([1, 2, spec.vocab], [-1, 3]):
+        with pytest.raises(AdmissionRejected) as e:
+            eng.add_request(bad, 4)
+        assert e.value.code is PublicErrorCode.INVALID_REQUEST
+    assert not eng.has_work()
+    assert len(eng.generate([[1, 2, 3]], 3)[0]) == 3
