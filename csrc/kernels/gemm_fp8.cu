@@ -341,7 +341,17 @@ void launch(const Fp8Args& a, cudaStream_t s, float* ws, int64_t ws_elems) {
 int plan_splits(int tiles, int num_kb, int sms, int* kb_per) {
   // Fill about one wave: as many K splits as the tiles leave SMs free, each
   // split at least 4 K blocks (512 channels) so the pipeline fill amortises.
-  int splits = tiles >= sms ? 1 : sms / tiles;
+  // Only where the tiles leave more than half the SMs idle and K is long
+  // (>= 32 blocks): measured on the 70B TP 8 shapes at 128 rows, splitting
+  // qkv (10 tiles, K 8192) took 33.8 -> 15.4 us and gate/up (56 tiles)
+  // 35.9 -> 29.7 us, while o (64 tiles, K 1024) went 13.3 -> 19.4 us and
+  // down (K 3584) 20.5 -> 23.6 us: there the fp32 partial traffic and the
+  // finalize pass cost more than the idle SMs return.
+  if (tiles * 2 > sms || num_kb < 32) {
+    *kb_per = num_kb;
+    return 1;
+  }
+  int splits = sms / tiles;
   const int max_splits = num_kb / 4;
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;

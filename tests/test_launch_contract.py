@@ -230,3 +230,23 @@ def test_engine_steps_pass_paged_admission(monkeypatch):
     prompts = [torch.randint(0, spec.vocab, (n,), generator=g).tolist() for n in (5, 19, 33, 40)]
     outs = eng.generate(prompts, 8)
     assert all(len(o) == 8 for o in outs) and len(calls) >= 8
+
+
+def test_fp8_split_plan_covers_k_exactly():
+    """The fp8 split-K plan (host code of the extension): every split gets at
+    least 4 K blocks, the splits cover K exactly, and shapes with many tiles
+    or short K are not split."""
+    from lunaflux_b200.ops import _ext
+    try:
+        C = _ext.load()
+    except Exception as e:   # pragma: no cover - the extension is built by build()
+        pytest.skip(f"extension not loadable here: {e}")
+    for tiles in (1, 8, 10, 20, 56, 64, 74, 75, 148, 300):
+        for num_kb in (1, 8, 28, 31, 32, 64, 112):
+            splits, per = C.fp8_plan_splits(tiles, num_kb, 148)
+            assert splits >= 1 and per >= 1
+            assert (splits - 1) * per < num_kb <= splits * per
+            if splits > 1:
+                assert per >= 4 and tiles * 2 <= 148 and num_kb >= 32 and tiles * splits <= 148
+            if tiles * 2 > 148 or num_kb < 32:
+                assert splits == 1
