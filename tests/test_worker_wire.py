@@ -119,3 +119,37 @@ def test_channel_rejects_a_stale_generation():
         cb.recv(5.0)
     ca.close()
     cb.close()
+
+
+GOLDEN = [
+    (("cancel", 11), "4c4c46570100040008000000030000000b00000000000000"),
+    (("step", 1234.5), "4c4c465701000500080000000300000000000000004a9340"),
+    (("close",), "4c4c4657010006000000000003000000"),
+    (("add", 7, [1, 2, 3], 16, SamplingParameters(SamplingMode.SAMPLE, 0.5, 40, 0.75, 99), (5,)),
+     "4c4c465701000300410000000300000007000000000000001000000001000000000000e03f28000000000000000000e83f63"
+     "00000000000000030000000100000002000000030000000100000005000000"),
+    (("outs", 2, [(1, 42, False)], [(9, None, "WORKER_UNAVAILABLE")], True),
+     "4c4c465701000700240000000300000002000000010100000001000000000000002a000000000100000009000000000000"
+     "000004"),
+]
+
+
+@pytest.mark.parametrize("msg,hexbytes", GOLDEN, ids=[g[0][0] for g in GOLDEN])
+def test_golden_bytes(msg, hexbytes):
+    """The encoding is byte-for-byte deterministic and pinned: a change of
+    layout, of a kind tag or of a reason / error tag shows up here
+    (reference: 'canonical encoding is byte-for-byte deterministic', 'wire
+    tags are pinned independently in both directions')."""
+    assert ww.encode(msg, generation=3).hex() == hexbytes
+    assert ww.decode_with_generation(bytes.fromhex(hexbytes)) == (msg, 3)
+
+
+def test_tags_are_pinned_in_both_directions():
+    from lunaflux_b200.contracts import FinishReason, PublicErrorCode
+    kinds = {"READY": 1, "HEARTBEAT": 2, "ADD": 3, "CANCEL": 4, "STEP": 5, "CLOSE": 6, "OUTPUTS": 7, "ERROR": 8}
+    assert {k.name: int(k) for k in ww.Kind} == kinds
+    assert [None if r is None else r.name for r in ww._REASONS] == [None, "STOP_SEQUENCE", "TOKEN_LIMIT", "CANCELLED"]
+    assert [None if e is None else e.name for e in ww._ERRORS] == [
+        None, "INVALID_REQUEST", "OVERLOADED", "DEADLINE_EXCEEDED", "WORKER_UNAVAILABLE", "INTERNAL",
+        "CONTEXT_OVERFLOW", "CANCELLED"]
+    assert set(ww._REASONS[1:]) == set(FinishReason) and set(ww._ERRORS[1:]) == set(PublicErrorCode)
