@@ -203,7 +203,8 @@ class LLMEngine:
     def _fail(self, plan):
         self._launched = []
         self.scheduler.abort_plan(plan)
-        self.scheduler.fail_active(PublicErrorCode.INTERNAL)
+        # the worker's step failed, not the request: retryable, as a lost rank is
+        self.scheduler.fail_active(PublicErrorCode.WORKER_UNAVAILABLE)
         self._drain_terminals()
 
     def _observe_queue(self, plan, t0):

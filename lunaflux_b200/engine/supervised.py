@@ -66,14 +66,17 @@ class SupervisedEngine:
             rid = self._next_rid
         self._next_rid = max(self._next_rid, rid + 1)
         self.sup.submit(rid, prompt, max_new_tokens, sampling, tuple(stop_ids))
-        self._live[rid] = {"prompt_len": len(prompt), "tokens": [], "arrival": self.clock() if arrival is None
-                           else arrival, "first": None}
+        now = self.clock()
+        self._live[rid] = {"prompt_len": len(prompt), "tokens": [], "arrival": now if arrival is None
+                           else arrival, "first": None,
+                           "deadline": None if deadline_s is None else now + deadline_s}
         return rid
 
     def submit(self, g) -> int:
         if g.input_tokens is None:
             raise ValueError("text requests must be tokenized by the service layer first")
-        return self.add_request(g.input_tokens, g.max_new_tokens, g.sampling, g.stop.token_ids, rid=g.request_id)
+        return self.add_request(g.input_tokens, g.max_new_tokens, g.sampling, g.stop.token_ids, rid=g.request_id,
+                                deadline_s=None if g.deadline_millis is None else g.deadline_millis / 1000.0)
 
     def cancel(self, rid: int) -> bool:
         if rid not in self._live:
@@ -97,7 +100,17 @@ class SupervisedEngine:
         else:
             self.metrics.finished.inc(reason=reason.name.lower() if reason else "none")
 
+    def _expire_deadlines(self):
+        # the ranks' schedulers are not told deadlines: they expire here, in
+        # the front process, and the ranks get a cancel
+        now = self.clock()
+        for rid, st in list(self._live.items()):
+            if st["deadline"] is not None and now >= st["deadline"]:
+                self.sup.cancel(rid)
+                self._terminal(rid, None, PublicErrorCode.DEADLINE_EXCEEDED)
+
     def step(self) -> List[TokenOutput]:
+        self._expire_deadlines()
         failures = self.sup.failures
         self.sup.step()
         outs: List[TokenOutput] = []
@@ -119,7 +132,8 @@ class SupervisedEngine:
             if finished:
                 r = done.get(rid, (None, None))[0]
                 reason = FinishReason[r] if r else FinishReason.TOKEN_LIMIT
-            outs.append(TokenOutput(rid, token, len(st["tokens"]) - 1, finished, reason))
+            # position in the sequence, as the in-process engine reports it
+            outs.append(TokenOutput(rid, token, st["prompt_len"] + len(st["tokens"]) - 1, finished, reason))
         if outs:
             self.metrics.output_tokens.inc(len(outs))
             for cb in self.listeners:

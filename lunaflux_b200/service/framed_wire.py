@@ -383,6 +383,7 @@ class FrameReader:
         self.header = header
         self.buf = bytearray()
         self.poisoned = False
+        self._first = 0.0        # receipt time of the first buffered byte
 
     def feed(self, data: bytes) -> List[bytes]:
         if self.poisoned:
@@ -398,4 +399,19 @@ class FrameReader:
                 break
             out.append(bytes(self.buf[:total]))
             del self.buf[:total]
+        return out
+
+    def feed_timed(self, data: bytes, now: float) -> List[Tuple[bytes, float]]:
+        """As ``feed``, with each frame's receipt time: the time passed with
+        the chunk that carried the frame's first byte.  The first frame a
+        chunk completes may have started in an earlier chunk; every later one
+        started in this chunk (the frame before it ended here)."""
+        if not self.buf and data:
+            self._first = now
+        frames = self.feed(data)
+        out = []
+        for i, f in enumerate(frames):
+            out.append((f, self._first if i == 0 else now))
+        if frames:
+            self._first = now     # the bytes left over (if any) arrived in this chunk
         return out

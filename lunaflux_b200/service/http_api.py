@@ -149,6 +149,7 @@ class CompletionsServer:
         writer.write(self._head(status, "application/json", len(data)) + data)
 
     async def _client(self, reader: asyncio.StreamReader, writer: asyncio.StreamWriter):
+        receipt = self.service.clock()     # the connection is accepted: the request's receipt time
         try:
             try:
                 method, path, body = await self._read_request(reader)
@@ -166,7 +167,8 @@ class CompletionsServer:
                         raise HTTPError(400, "the body is not JSON") from None
                     if path == "/v1/chat/completions":
                         parsed = await self._chat_body(parsed)
-                    await self._complete(parsed, reader, writer, chat=path == "/v1/chat/completions")
+                    await self._complete(parsed, reader, writer, chat=path == "/v1/chat/completions",
+                                         receipt=receipt)
                 else:
                     raise HTTPError(404, "no such endpoint")
             except HTTPError as e:
@@ -199,7 +201,7 @@ class CompletionsServer:
         out["prompt"] = ids
         return out
 
-    async def _complete(self, body, reader, writer, chat: bool = False):
+    async def _complete(self, body, reader, writer, chat: bool = False, receipt: Optional[float] = None):
         rid = next(self._ids)
         req = build_request(body, rid)
         if chat and self.eos_ids:
@@ -211,7 +213,7 @@ class CompletionsServer:
         stream = bool(body.get("stream", False))
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
-        self.service.submit(req, lambda ev: loop.call_soon_threadsafe(q.put_nowait, ev))
+        self.service.submit(req, lambda ev: loop.call_soon_threadsafe(q.put_nowait, ev), receipt)
         cid = f"{'chatcmpl' if chat else 'cmpl'}-{rid - _ID_BASE}"
         kind = "chat.completion" if chat else "text_completion"
         created = int(time.time())

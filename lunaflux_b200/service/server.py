@@ -3,8 +3,10 @@
 Reference: service/online_session (LunaOnlineInstance begin / progress /
 take_event, admission.mbt:90, progression.mbt:225), service/online_tcp
 (endpoint_prepare.mbt:53, endpoint_reactor.mbt:203), service/request_admission
-(prepare_luna_request, admit.mbt:329).  Kept: request receipt time is taken
-before the first byte is parsed and the deadline is derived from it once;
+(prepare_luna_request, admit.mbt:329).  Kept: the receipt time is the
+monotonic time at which the request's first byte arrived (framed TCP) or the
+connection was accepted (HTTP); the deadline is derived from it once, checked
+before and after tokenization, and what is left of it goes to the scheduler;
 the event order Accepted -> Token* -> Usage -> Completed | Failed; a worker
 failure fails active requests with ``worker_unavailable`` (retryable);
 draining rejects new admissions.  Changed: many concurrent connections and
@@ -47,8 +49,11 @@ class EngineService:
     """Owns the engine thread; thread-safe submit / cancel; events via sinks."""
 
     def __init__(self, engine: LLMEngine, tokenizer: Optional[Tokenizer], limits: InferenceLimits,
-                 content_digest: str = "", plan_digest: str = "", tokenizer_threads: int = 2):
+                 content_digest: str = "", plan_digest: str = "", tokenizer_threads: int = 2,
+                 clock: Callable[[], float] = time.monotonic):
         self.engine = engine
+        # receipt times and deadlines; the engine's scheduler gets the time left
+        self.clock = clock
         self.tokenizer = tokenizer
         self.limits = limits
         self.content_digest = content_digest
@@ -79,25 +84,37 @@ class EngineService:
         self._tok_pool.shutdown(wait=False, cancel_futures=True)
 
     # -------------------------------------------------------------- producer side
-    def submit(self, req: GenerateRequest, sink: Callable[[object], None]):
-        """Queues a request for the engine thread.  Text prompts are tokenized
-        first on the tokenizer pool, so a long prompt never stalls a step.
-        While draining, new requests are refused here (retryable
+    def submit(self, req: GenerateRequest, sink: Callable[[object], None], receipt: Optional[float] = None):
+        """Queues a request for the engine thread.  ``receipt`` is when the
+        request arrived on this service's clock (now if not given); a
+        request's ``deadline_millis`` counts from it.  Text prompts are
+        tokenized first on the tokenizer pool, so a long prompt never stalls a
+        step.  While draining, new requests are refused here (retryable
         ``overloaded``); those queued before the drain began are admitted."""
+        if receipt is None:
+            receipt = self.clock()
         if self.draining:
             sink(FailedEvent(req.request_id, PublicErrorCode.OVERLOADED, True))
             return
-        if req.input_text is not None and self.tokenizer is not None:
-            self._tok_pool.submit(self._tokenize_then_queue, req, sink)
+        if self._expired(req, receipt, sink):
             return
-        self._queue(req, sink)
+        if req.input_text is not None and self.tokenizer is not None:
+            self._tok_pool.submit(self._tokenize_then_queue, req, sink, receipt)
+            return
+        self._queue(req, sink, receipt)
 
-    def _queue(self, req, sink):
+    def _expired(self, req: GenerateRequest, receipt: float, sink) -> bool:
+        if req.deadline_millis is not None and self.clock() >= receipt + req.deadline_millis / 1000.0:
+            sink(FailedEvent(req.request_id, PublicErrorCode.DEADLINE_EXCEEDED, False))
+            return True
+        return False
+
+    def _queue(self, req, sink, receipt):
         with self._cv:
-            self._inbox.append(("add", req, sink))
+            self._inbox.append(("add", (req, receipt), sink))
             self._cv.notify()
 
-    def _tokenize_then_queue(self, req: GenerateRequest, sink):
+    def _tokenize_then_queue(self, req: GenerateRequest, sink, receipt: float):
         try:
             ids = tuple(self.tokenizer.encode_bytes(req.input_text, allow_special=False))
         except ValueError:
@@ -106,7 +123,9 @@ class EngineService:
         if not ids:
             sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
             return
-        self._queue(GenerateRequest(**{**req.__dict__, "input_tokens": ids, "input_text": None}), sink)
+        if self._expired(req, receipt, sink):
+            return
+        self._queue(GenerateRequest(**{**req.__dict__, "input_tokens": ids, "input_text": None}), sink, receipt)
 
     def cancel(self, rid: int):
         with self._cv:
@@ -141,7 +160,7 @@ class EngineService:
         return False
 
     # -------------------------------------------------------------- engine thread
-    def _admit(self, req: GenerateRequest, sink):
+    def _admit(self, req: GenerateRequest, receipt: float, sink):
         if self.failed:
             sink(FailedEvent(req.request_id, PublicErrorCode.WORKER_UNAVAILABLE, True))
             return
@@ -167,8 +186,15 @@ class EngineService:
             # a text prompt is measured against the ceiling once it is tokenized
             sink(FailedEvent(req.request_id, PublicErrorCode.INVALID_REQUEST, False))
             return
+        fields = {**req.__dict__, "input_tokens": tuple(prompt), "input_text": None}
+        if req.deadline_millis is not None:
+            left = receipt + req.deadline_millis / 1000.0 - self.clock()
+            if left <= 0.0:
+                sink(FailedEvent(req.request_id, PublicErrorCode.DEADLINE_EXCEEDED, False))
+                return
+            fields["deadline_millis"] = left * 1000.0      # what is left of it, for the scheduler
         try:
-            self.engine.submit(GenerateRequest(**{**req.__dict__, "input_tokens": tuple(prompt), "input_text": None}))
+            self.engine.submit(GenerateRequest(**fields))
         except AdmissionRejected as e:
             sink(FailedEvent(req.request_id, e.code, e.code is PublicErrorCode.OVERLOADED))
             return
@@ -226,7 +252,7 @@ class EngineService:
                 self._inbox.clear()
             for kind, a, b in items:
                 if kind == "add":
-                    self._admit(a, b)
+                    self._admit(a[0], a[1], b)
                 elif kind == "cancel":
                     self.engine.cancel(a)
                 elif kind == "drain_deadline":
@@ -321,12 +347,12 @@ class TCPServer:
                 if not data:
                     break
                 try:
-                    for fr in frames.feed(data):
+                    for fr, receipt in frames.feed_timed(data, self.service.clock()):
                         req = decode_request(fr, self.service.limits)
                         if req.request_id in open_rids:
                             raise FramedWireError("request", "duplicate_id")
                         open_rids.add(req.request_id)
-                        self.service.submit(req, sink_for(req.request_id))
+                        self.service.submit(req, sink_for(req.request_id), receipt)
                 except FramedWireError:
                     # malformed input: drop the connection and its requests
                     for rid in list(open_rids):

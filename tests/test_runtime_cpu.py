@@ -98,9 +98,8 @@ def test_engine_fails_active_requests_on_device_fault(kind):
     a = eng.add_request(list(range(3, 30)), 8)
     with pytest.raises((StepFailed, InjectedLaunchError)):
         eng.run_until_done()
-    if kind == "error_word":
-        # the step that saw the error word failed every active request, retryably
-        assert eng.results[a].error is PublicErrorCode.INTERNAL
+    # the step that failed failed every active request, retryably
+    assert eng.results[a].error is PublicErrorCode.WORKER_UNAVAILABLE
     # the engine keeps serving new work afterwards (no GPU state was harmed)
     b = eng.add_request(list(range(5, 20)), 4)
     eng.run_until_done()

@@ -179,3 +179,6 @@ def test_service_over_supervised_ranks_survives_a_lost_rank(monkeypatch):
         assert isinstance(done[rid], CompletedEvent), done[rid]
         toks = [e.token_id for e in events[rid] if isinstance(e, TokenEvent)]
         assert toks == want, (rid, toks, want)
+        # positions count from the prompt, as the in-process engine reports them
+        n = len(PROMPTS[(rid - 1) % 4])
+        assert [e.position for e in events[rid] if isinstance(e, TokenEvent)] == list(range(n, n + 6))
