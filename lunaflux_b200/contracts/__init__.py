@@ -11,4 +11,5 @@ from .inference import (  # noqa: F401
     ContractError, ContractField, ContractIssue, InferenceLimits, SamplingMode, SamplingParameters,
     StopConditions, GenerateRequest, CacheScope, FinishReason, PublicErrorCode, Usage,
     AcceptedEvent, TokenEvent, CompletedEvent, FailedEvent, StreamEvent, default_limits, derive_seed,
+    RETRYABLE_CODES, validate_event,
 )

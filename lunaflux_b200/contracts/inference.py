@@ -145,7 +145,17 @@ class SamplingParameters:
     seed: int = 1
 
     def validate(self, limits: InferenceLimits) -> "SamplingParameters":
-        if self.mode is SamplingMode.SAMPLE:
+        if self.mode is SamplingMode.GREEDY:
+            # greedy carries the neutral values only: a filter or temperature
+            # that would be ignored is a client error, not a silent no-op
+            # (reference: request_authority_wbtest.mbt:310-324)
+            if self.temperature != 1.0:
+                _bad(ContractField.TEMPERATURE, ContractIssue.INCONSISTENT)
+            if self.top_k is not None:
+                _bad(ContractField.TOP_K, ContractIssue.INCONSISTENT)
+            if self.top_p is not None:
+                _bad(ContractField.TOP_P, ContractIssue.INCONSISTENT)
+        elif self.mode is SamplingMode.SAMPLE:
             if not math.isfinite(self.temperature):
                 _bad(ContractField.TEMPERATURE, ContractIssue.NON_FINITE)
             if not (0.0 < self.temperature <= limits.max_temperature):
@@ -363,6 +373,59 @@ class FailedEvent:
 
 
 StreamEvent = Union[AcceptedEvent, TokenEvent, CompletedEvent, FailedEvent, Usage]
+
+# Failures a client may retry unchanged: the service was busy or lost a worker.
+RETRYABLE_CODES = frozenset({PublicErrorCode.OVERLOADED, PublicErrorCode.WORKER_UNAVAILABLE})
+
+
+def _utf8(data: bytes, field: ContractField, max_bytes: int):
+    if len(data) > max_bytes:
+        _bad(field, ContractIssue.TOO_LONG)
+    try:
+        data.decode("utf-8")
+    except UnicodeDecodeError:
+        _bad(field, ContractIssue.INVALID_FORMAT)
+
+
+def validate_event(ev, max_token_id: int = HARD_MAX_TOKEN_ID,
+                   max_delta_bytes: int = HARD_MAX_DECODED_DELTA_BYTES):
+    """Checks an outgoing stream event: ids and positions in range, decoded
+    text valid UTF-8 and bounded, usage counts consistent (cached input within
+    the input), and a failure's retryability matching its code.  Reference:
+    contracts/inference/events.mbt:3-324 and events_test.mbt ("token event
+    validates UTF-8 token identity and position bounds", "usage construction
+    and advancement enforce monotonic accounting", "terminal events expose
+    bounded reasons usage and retryability")."""
+    if isinstance(ev, Usage):        # the usage event belongs to the stream it is written on
+        _validate_usage(ev)
+        return ev
+    if not (0 <= ev.request_id < (1 << 64)):
+        _bad(ContractField.REQUEST_ID, ContractIssue.OUT_OF_RANGE)
+    if isinstance(ev, TokenEvent):
+        if not (0 <= ev.token_id <= max_token_id):
+            _bad(ContractField.INPUT_TOKEN, ContractIssue.OUT_OF_RANGE)
+        if not (0 <= ev.position < HARD_MAX_CONTEXT_TOKENS):
+            _bad(ContractField.TOKEN_POSITION, ContractIssue.OUT_OF_RANGE)
+        _utf8(ev.delta, ContractField.DECODED_DELTA, max_delta_bytes)
+    elif isinstance(ev, CompletedEvent):
+        if not isinstance(ev.reason, FinishReason):
+            _bad(ContractField.PUBLIC_ERROR_CODE, ContractIssue.UNSUPPORTED)
+        _validate_usage(ev.usage)
+        _utf8(ev.final_delta, ContractField.DECODED_DELTA, max_delta_bytes)
+    elif isinstance(ev, FailedEvent):
+        if not isinstance(ev.code, PublicErrorCode):
+            _bad(ContractField.PUBLIC_ERROR_CODE, ContractIssue.UNSUPPORTED)
+        if bool(ev.retryable) != (ev.code in RETRYABLE_CODES):
+            _bad(ContractField.PUBLIC_ERROR_CODE, ContractIssue.INCONSISTENT)
+    return ev
+
+
+def _validate_usage(u: Usage):
+    for v in (u.input_tokens, u.cached_input_tokens, u.output_tokens):
+        if not (0 <= v <= HARD_MAX_CONTEXT_TOKENS):
+            _bad(ContractField.USAGE, ContractIssue.OUT_OF_RANGE)
+    if u.cached_input_tokens > u.input_tokens:
+        _bad(ContractField.USAGE, ContractIssue.INCONSISTENT)
 
 
 def token_tuple(tokens: Sequence[int]) -> Tuple[int, ...]:

@@ -36,7 +36,7 @@ from typing import List, Optional, Tuple, Union
 
 from ..contracts.inference import (CachePermission, CacheScope, CompletedEvent, ContractError, FailedEvent,
                                    FinishReason, GenerateRequest, InferenceLimits, PublicErrorCode, SamplingMode,
-                                   SamplingParameters, StopConditions, TokenEvent, Usage)
+                                   SamplingParameters, StopConditions, TokenEvent, Usage, validate_event)
 
 REQUEST_MAGIC = 0x5152464C
 EVENT_MAGIC = 0x5645464C
@@ -250,6 +250,11 @@ def _usage_into(h, u: Usage):
 
 
 def encode_event(ev: Event) -> bytes:
+    if not isinstance(ev, AcceptedWire):
+        try:
+            validate_event(ev)
+        except ContractError as e:
+            raise FramedWireError("event", f"contract:{e.field.name}") from None
     h = bytearray(EVENT_HEADER)
     payload = b""
     if isinstance(ev, AcceptedWire):

@@ -325,10 +325,20 @@ class TCPServer:
         async def pump():
             # Writes events in order; a broken transport cancels the client's requests.
             try:
+                broken = set()
                 while True:
                     rid, ev = await q.get()
-                    if ev is not None:
-                        writer.write(encode_event(ev))
+                    if ev is not None and rid not in broken:
+                        try:
+                            frame = encode_event(ev)
+                        except FramedWireError:
+                            # an event that breaks the stream contract is a server
+                            # fault: the request ends with a typed failure
+                            broken.add(rid)
+                            self.service.cancel(rid)
+                            ev = FailedEvent(rid, PublicErrorCode.INTERNAL, False)
+                            frame = encode_event(ev)
+                        writer.write(frame)
                         await writer.drain()
                         if isinstance(ev, (CompletedEvent, FailedEvent)):
                             open_rids.discard(rid)
