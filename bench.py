@@ -302,6 +302,7 @@ def main():
         "tpot_p50_ms": pct(tpots, 50, 3), "tpot_p95_ms": pct(tpots, 95, 3), "tpot_p99_ms": pct(tpots, 99, 3),
         "itl_p50_ms": pct(itls, 50, 3), "itl_p95_ms": pct(itls, 95, 3), "itl_p99_ms": pct(itls, 99, 3),
         "goodput_req_s": round(args.requests * args.steps / wall, 2),
+        "serving": serving_summary(engine.metrics),
         "e2e": {"value": round(e2e, 1), "unit": "output tokens/s through LLMEngine.generate (wall clock)",
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": launches,
@@ -335,6 +336,30 @@ def main():
         sys.stderr.flush()
         os._exit(0)
     return 0
+
+
+def serving_summary(m):
+    """The engine's serving metrics over the warm-up and timed passes (the
+    reference's benchmark set: queue time, tokens per step, prefix hit rate,
+    graph-capture time, failure and cancellation counts).  Queue quantiles are
+    histogram bucket upper bounds."""
+    def hist(h):
+        return h.snapshot().get("", {"count": 0, "sum": 0.0, "p50": None, "p99": None})
+
+    q, tok, rows, cap = hist(m.queue), hist(m.step_tokens), hist(m.step_rows), hist(m.graph_capture)
+    steps = sum(m.graph.values.values())
+    hit = m.prefix_hit_rate()
+    return {
+        "queue_p50_ms_le": None if q["p50"] is None else round(q["p50"] * 1e3, 3),
+        "queue_p99_ms_le": None if q["p99"] is None else round(q["p99"] * 1e3, 3),
+        "tokens_per_step_mean": round(tok["sum"] / tok["count"], 2) if tok["count"] else None,
+        "rows_per_step_mean": round(rows["sum"] / rows["count"], 2) if rows["count"] else None,
+        "graph_captures": cap["count"], "graph_capture_s": round(cap["sum"], 3),
+        "graph_step_share": round(m.graph.get(mode="captured") / steps, 4) if steps else None,
+        "prefix_hit_rate": None if hit is None else round(hit, 4),
+        "finished": {k or "none": int(v) for k, v in m.finished.snapshot().items()},
+        "failed": {k: int(v) for k, v in m.failed.snapshot().items()},
+    }
 
 
 if __name__ == "__main__":

@@ -62,3 +62,38 @@ def test_engine_updates_metrics():
     assert m.graph.get(mode="eager") >= 1
     assert m.kv_pages.get(state="free") + m.kv_pages.get(state="allocated") > 0
     assert "lunaflux_ttft_seconds_count 3" in m.registry.render_prometheus()
+
+
+def test_bench_serving_summary_reads_the_engine_metrics():
+    """bench.py's serving block (queue time, tokens per step, graph capture,
+    prefix hit rate, finish / failure counts) from a populated metric set and
+    from an empty one."""
+    import importlib.util
+    import os
+    from lunaflux_b200.metrics import EngineMetrics
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("lf_bench", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    m = EngineMetrics()
+    for v in (0.001, 0.002, 0.2):
+        m.queue.observe(v)
+    for t in (256, 8192):
+        m.step_tokens.observe(t)
+        m.step_rows.observe(8)
+    m.graph.inc(mode="captured")
+    m.graph.inc(mode="captured")
+    m.graph.inc(mode="eager")
+    m.graph_capture.observe(0.25)
+    m.prompt_tokens.inc(100)
+    m.cached_tokens.inc(25)
+    m.finished.inc(reason="token_limit")
+    m.failed.inc(code="deadline_exceeded")
+    s = bench.serving_summary(m)
+    assert s["tokens_per_step_mean"] == 4224.0 and s["rows_per_step_mean"] == 8.0
+    assert s["graph_captures"] == 1 and s["graph_capture_s"] == 0.25 and s["graph_step_share"] == round(2 / 3, 4)
+    assert s["prefix_hit_rate"] == 0.25
+    assert s["queue_p50_ms_le"] >= 2.0 and s["queue_p99_ms_le"] >= 200.0
+    assert s["finished"] == {"token_limit": 1} and s["failed"] == {"deadline_exceeded": 1}
+    empty = bench.serving_summary(EngineMetrics())
+    assert empty["tokens_per_step_mean"] is None and empty["finished"] == {}
