@@ -165,7 +165,6 @@ class LLMEngine:
             self._drain_terminals()
             return []
         self._observe_queue(plan, t0)
-        graphs_before = len(self.runner.graphs)
         try:
             sampled = self.runner.execute(plan, self.scheduler.tables.matrix)
         except Exception:
@@ -173,11 +172,10 @@ class LLMEngine:
             # void; active requests fail (retryably), waiting ones stay queued
             self._fail(plan)
             raise
-        return self._commit(plan, sampled, t0, graphs_before)
+        return self._commit(plan, sampled, t0)
 
     def _step_overlap(self) -> List[TokenOutput]:
         t0 = self.clock()
-        graphs_before = len(self.runner.graphs)
         plan = self.scheduler.schedule()
         if plan is not None:
             self._observe_queue(plan, t0)
@@ -198,7 +196,7 @@ class LLMEngine:
         except Exception:
             self._fail(old)
             raise
-        return self._commit(old, sampled, ts, graphs_before)
+        return self._commit(old, sampled, ts)
 
     def _fail(self, plan):
         self._launched = []
@@ -212,7 +210,7 @@ class LLMEngine:
             if not r.decode and r.start == r.req.cached_tokens:
                 self.metrics.queue.observe(t0 - r.req.arrival)        # first step of this request
 
-    def _commit(self, plan, sampled, t0, graphs_before) -> List[TokenOutput]:
+    def _commit(self, plan, sampled, t0) -> List[TokenOutput]:
         m = self.metrics
         outs = self.scheduler.complete(plan, sampled)
         for cb in self.listeners:
@@ -224,8 +222,8 @@ class LLMEngine:
         m.step_tokens.observe(plan.num_tokens)
         m.step_rows.observe(len(plan.rows))
         m.graph.inc(mode="captured" if self.runner.last_bucket is not None else "eager")
-        if len(self.runner.graphs) > graphs_before:
-            m.graph_capture.observe(self.runner.last_capture_s)
+        for seconds in self.runner.take_capture_times():      # in steps or ahead of them
+            m.graph_capture.observe(seconds)
         if outs:
             m.output_tokens.inc(len(outs))
             if m._last_emit is not None:

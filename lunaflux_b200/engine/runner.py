@@ -177,7 +177,7 @@ class ModelRunner:
         self.stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
         self.steps = 0
         self.last_bucket: Optional[int] = None      # graph bucket of the last step (None: eager)
-        self.last_capture_s = 0.0
+        self.capture_times: List[float] = []      # seconds per capture, until taken
         # accounting for the bench
         self.h2d_bytes = 0
         self.d2h_bytes = 0
@@ -541,9 +541,7 @@ class ModelRunner:
             key = (bucket, stoch)
             g = self.graphs.get(key)
             if g is None:
-                t0 = time.perf_counter()
                 g = self.capture(bucket, stoch)
-                self.last_capture_s = time.perf_counter() - t0
             self._upload(hs, host_buf)
             self._record_upload(slot)
             self._begin_step(oslot)
@@ -602,6 +600,7 @@ class ModelRunner:
     def capture(self, bucket: int, stochastic: bool) -> "torch.cuda.CUDAGraph":
         """Captures the decode step for ``bucket`` rows reading its inputs at
         the fixed offsets of ``make_layout(bucket, 0, bucket, bucket, W)``."""
+        t_start = time.perf_counter()
         L = make_layout(bucket, 0, bucket, bucket, self.W)
         v = device_views(self.in_dev, L)
         # a capture in the middle of overlapped steps must not lose the
@@ -636,7 +635,12 @@ class ModelRunner:
         self.graphs[(bucket, stochastic)] = g
         if saved_prev is not None:
             self.prev_tok.copy_(saved_prev)
+        self.capture_times.append(time.perf_counter() - t_start)
         return g
+
+    def take_capture_times(self) -> List[float]:
+        t, self.capture_times = self.capture_times, []
+        return t
 
     def capture_all(self, stochastic: bool = False):
         for b in self.graph_sizes:
