@@ -155,11 +155,17 @@ class Supervisor:
         self.last_beat = {r: now for r in range(self.world)}
         self.ready = set()  # heartbeats are checked once a rank has finished starting
         deadline = now + self.step_timeout_s
-        while len(self.ready) < self.world:
-            for r, msg in self._poll(deadline):
-                if msg[0] == "ready":
-                    self.ready.add(r)
-                    self.last_beat[r] = time.monotonic()
+        try:
+            while len(self.ready) < self.world:
+                for r, msg in self._poll(deadline):
+                    if msg[0] == "ready":
+                        self.ready.add(r)
+                        self.last_beat[r] = time.monotonic()
+        except WorkerLost:
+            # a rank that cannot start fails the whole start: no rank of this
+            # generation is left running
+            self._reap()
+            raise
         # re-submit requests that were waiting when the previous generation died
         for q in self.reqs.values():
             if not q.done:

@@ -182,3 +182,45 @@ def test_service_over_supervised_ranks_survives_a_lost_rank(monkeypatch):
         # positions count from the prompt, as the in-process engine reports them
         n = len(PROMPTS[(rid - 1) % 4])
         assert [e.position for e in events[rid] if isinstance(e, TokenEvent)] == list(range(n, n + 6))
+
+
+def failing_factory(rank, world):
+    if rank == 1:
+        raise RuntimeError("model directory unreadable")
+    import time
+    time.sleep(0.5)
+    return tiny_factory(rank, world)
+
+
+def test_a_rank_that_cannot_start_fails_the_start_and_leaves_nothing_running():
+    """Startup handshake (reference: worker_process 'startup handshake rejects
+    an incompatible child before readiness'): a rank whose engine cannot be
+    built reports the error; start() raises and every rank of that
+    generation is reaped."""
+    from lunaflux_b200.engine.supervisor import WorkerLost
+    sup = Supervisor(2, failing_factory, heartbeat_s=0.1, dead_after_s=2.0, step_timeout_s=60.0)
+    with pytest.raises(WorkerLost, match="rank 1"):
+        sup.start()
+    assert sup.procs == [] and sup.conns == []
+
+
+def test_cancel_and_close_through_the_supervisor(monkeypatch):
+    """A request cancelled between steps ends CANCELLED on every rank while
+    the other completes with the oracle's tokens; close() reaps every rank."""
+    monkeypatch.setenv("LF_TEST_FAULT", "")
+    sup = Supervisor(2, tiny_factory, heartbeat_s=0.1, dead_after_s=2.0, step_timeout_s=60.0)
+    sup.start()
+    procs = list(sup.procs)
+    try:
+        sup.submit(1, PROMPTS[0], 40)
+        sup.submit(2, PROMPTS[1], 6)
+        sup.step()
+        sup.step()
+        sup.cancel(1)
+        sup.run_until_done()
+    finally:
+        sup.close()
+    assert all(not p.is_alive() for p in procs)
+    assert sup.reqs[1].done and sup.reqs[1].reason == "CANCELLED" and len(sup.reqs[1].tokens) < 40
+    assert sup.reqs[2].tokens == _expect([PROMPTS[1]], 6)[0] and sup.reqs[2].reason == "TOKEN_LIMIT"
+    assert sup.failures == 0
