@@ -183,3 +183,17 @@ def test_bytelevel_bpe_matches_hf_tokenizers():
         # the native merge loop and the Python restatement agree
         data = c["text"].encode("utf-8")
         assert tok._bpe_reference(data) == tok._bpe(data), c["name"]
+
+
+def test_cli_reference_on_the_pinned_model(corpus):
+    """`lunaflux reference ROOT CONFIG TOKENIZER WEIGHTS SHA... N IDS`, with the
+    digests pinned above, reaches each model case's transformers continuation."""
+    from lunaflux_b200 import cli
+    names = ("config.json", "compatible_bytelevel_tokenizer.json", "model.safetensors")
+    shas = [SHA256[os.path.join(LLAMA, n)] for n in names]
+    for case in corpus["model_cases"]:
+        lines = []
+        ids = ",".join(map(str, case["input_ids"]))
+        gen = cli.reference(LLAMA, *names, *shas, "4", ids, out=lines.append)
+        assert gen == case["greedy_continuation"]
+        assert lines[-1] == "generated tokens: " + ",".join(map(str, gen))
