@@ -23,7 +23,7 @@ from ..contracts import FinishReason, PublicErrorCode
 from ..metrics import EngineMetrics
 from ..scheduler.scheduler import TokenOutput
 from .engine import RequestResult
-from .supervisor import Supervisor
+from .supervisor import Supervisor, WorkerLost
 
 
 class _SchedulerView:
@@ -81,8 +81,15 @@ class SupervisedEngine:
     def cancel(self, rid: int) -> bool:
         if rid not in self._live:
             return False
-        self.sup.cancel(rid)
+        self._cancel_on_ranks(rid)
         return True
+
+    def _cancel_on_ranks(self, rid: int):
+        # a rank lost here is found again, and recovered from, by the next step
+        try:
+            self.sup.cancel(rid)
+        except WorkerLost:
+            pass
 
     def has_work(self) -> bool:
         return bool(self._live)
@@ -106,8 +113,8 @@ class SupervisedEngine:
         now = self.clock()
         for rid, st in list(self._live.items()):
             if st["deadline"] is not None and now >= st["deadline"]:
-                self.sup.cancel(rid)
                 self._terminal(rid, None, PublicErrorCode.DEADLINE_EXCEEDED)
+                self._cancel_on_ranks(rid)
 
     def step(self) -> List[TokenOutput]:
         self._expire_deadlines()

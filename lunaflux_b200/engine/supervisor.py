@@ -237,10 +237,19 @@ class Supervisor:
         from ..contracts import SamplingParameters
         q = _Req(rid, list(prompt), max_new, sampling or SamplingParameters(), tuple(stop_ids))
         self.reqs[rid] = q
-        self._send_all(("add", rid, q.prompt, max_new, q.sampling, q.stop_ids))
+        try:
+            self._send_all(("add", rid, q.prompt, max_new, q.sampling, q.stop_ids))
+        except WorkerLost:
+            pass    # the next step finds the lost rank; recovery re-submits this request
 
     def cancel(self, rid: int):
-        self._send_all(("cancel", rid))
+        try:
+            self._send_all(("cancel", rid))
+        except WorkerLost:
+            # the next step recovers; the request must not come back with it
+            q = self.reqs.get(rid)
+            if q is not None and not q.done:
+                q.done, q.reason = True, "CANCELLED"
 
     def step(self) -> bool:
         """One engine iteration on every rank.  Returns whether work remains.

@@ -252,7 +252,13 @@ class EngineService:
                 self._inbox.clear()
             for kind, a, b in items:
                 if kind == "add":
-                    self._admit(a[0], a[1], b)
+                    try:
+                        self._admit(a[0], a[1], b)
+                    except Exception:
+                        # an admission that fails unexpectedly fails its request,
+                        # not the engine loop
+                        self._live.pop(a[0].request_id, None)
+                        b(FailedEvent(a[0].request_id, PublicErrorCode.INTERNAL, False))
                 elif kind == "cancel":
                     self.engine.cancel(a)
                 elif kind == "drain_deadline":

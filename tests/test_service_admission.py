@@ -280,3 +280,26 @@ def test_a_failed_step_fails_active_requests_retryably_and_later_ones_too(tiny):
     assert [e.position for e in first if isinstance(e, TokenEvent)] == [2, 3]
     assert later == [FailedEvent(2, PublicErrorCode.WORKER_UNAVAILABLE, True)]
     assert not svc.alive()
+
+
+def test_an_unexpected_admission_error_fails_only_its_request(tiny):
+    svc, eng = service(tiny)
+    orig = eng.submit
+
+    def flaky(g):
+        if g.request_id == 1:
+            raise RuntimeError("backend refused the request")
+        return orig(g)
+
+    eng.submit = flaky
+    c = Client()
+    svc.start()
+    try:
+        svc.submit(GenerateRequest(1, input_tokens=(5, 6), max_new_tokens=2), c.sink(1))
+        first = c.wait(1)
+        svc.submit(GenerateRequest(2, input_tokens=(5, 6), max_new_tokens=2), c.sink(2))
+        second = c.wait(2)
+    finally:
+        svc.stop()
+    assert first == [FailedEvent(1, PublicErrorCode.INTERNAL, False)]
+    assert isinstance(second[-1], CompletedEvent)
