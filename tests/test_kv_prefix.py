@@ -175,3 +175,100 @@ def test_kv_layout_offsets():
     assert L.element_offset(10, 0, 0, 1, 0, 0, 0) == 8 * 16 * 128
     with pytest.raises(IndexError):
         L.element_offset(10, 0, 2, 0, 0, 0, 0)
+
+
+def _prefix_classes():
+    from lunaflux_b200.prefix import radix
+    out = [radix.PyPrefixIndex]
+    try:
+        from lunaflux_b200 import _host  # noqa: F401
+        out.append(radix.NativePrefixIndex)
+    except ImportError:
+        pass
+    return out
+
+
+@pytest.mark.parametrize("cls", _prefix_classes(), ids=lambda c: c.__name__)
+@pytest.mark.parametrize("seed", range(4))
+def test_radix_matches_a_path_model_with_lru_eviction(cls, seed):
+    """Model check of the prefix index (reference: prefix/radix/index.mbt and
+    eviction.mbt): the cached set is a prefix-closed set of page paths;
+    lookup returns the longest cached path (its pages are the ones first
+    inserted for it); evicting one page removes the least recently used
+    unreferenced leaf; every cached page holds exactly one cached reference
+    and is freed when evicted."""
+    rng = random.Random(seed)
+    P = 2
+    a = PageAllocator(4096)
+    idx = cls(a, P)
+    idn = ident(P=P)
+    model = {}       # path (tuple of page keys) -> page
+    recency = {}     # path -> last touch
+    refs = {}        # path -> retain count
+    held = []        # (nodes, paths) retained by "requests"
+    clock = 0
+
+    def paths_of(tokens, n):
+        return [tuple(tuple(tokens[j * P:(j + 1) * P]) for j in range(i + 1)) for i in range(n)]
+
+    for _ in range(400):
+        op = rng.random()
+        toks = [rng.randrange(3) for _ in range(rng.randrange(1, 11))]
+        full = len(toks) // P
+        if op < 0.4:
+            pages = a.allocate_run(full) if full else []
+            clock += 1
+            added = idx.insert(idn, toks, pages)
+            new = 0
+            for p, pid in zip(paths_of(toks, full), pages):
+                if p not in model:
+                    model[p] = pid
+                    new += 1
+                recency[p] = clock
+            assert added == new
+            for pid in pages:
+                a.release_active(pid)        # the cache (if it took the page) is the only owner now
+        elif op < 0.7:
+            clock += 1
+            nodes = idx.lookup(idn, toks)
+            want = 0
+            for p in paths_of(toks, full):
+                if p not in model:
+                    break
+                want += 1
+                recency[p] = clock
+            assert len(nodes) == want
+            ps = paths_of(toks, want)
+            assert idx.pages_of(nodes) == [model[p] for p in ps]
+            if nodes and rng.random() < 0.5:
+                idx.retain(nodes)
+                for p in ps:
+                    refs[p] = refs.get(p, 0) + 1
+                held.append((nodes, ps))
+        elif op < 0.85 and held:
+            nodes, ps = held.pop(rng.randrange(len(held)))
+            idx.release(nodes)
+            for p in ps:
+                refs[p] -= 1
+        else:
+            leaves = [p for p in model if refs.get(p, 0) == 0
+                      and not any(q[:len(p)] == p and len(q) > len(p) for q in model)]
+            freed = idx.evict(1)
+            if not leaves:
+                assert freed == 0
+                continue
+            assert freed == 1
+            oldest = min(leaves, key=lambda p: recency[p])
+            del model[oldest]
+            recency.pop(oldest)
+            # every other leaf is still there (each probe is a lookup: it touches the path)
+            for p in leaves:
+                clock += 1
+                got = len(idx.lookup(idn, [t for k in p for t in k]))
+                assert got == (len(p) - 1 if p == oldest else len(p)), (p, oldest)
+                for i in range(1, got + 1):
+                    recency[p[:i]] = clock
+        idx.debug_check_invariants()
+        a.debug_check_invariants()
+        assert idx.page_count() == len(model)
+        assert a.free_page_count() == a.capacity - len(model)
