@@ -28,6 +28,7 @@ enum ErrorCode : int {
   kErrBadIndex = 3,        // a page / token / row index failed its bounds check
   kErrTmemAlloc = 4,       // TMEM allocation returned an unusable address
   kErrHostInjected = 5,    // set by the host to exercise the recovery path
+  kErrNonFinite = 6,       // a sampler met a non-finite logit (info: the row)
 };
 
 }  // namespace lf

@@ -321,8 +321,9 @@ __device__ __forceinline__ int block_sum_i(int v, int* sh) {
   return r;
 }
 
-// Greedy: per row, the max finite logit, lowest id on ties.  Non-finite logits
-// record kErrBadIndex-free status -1 in out_status[row].
+// Greedy: per row, the max finite logit, lowest id on ties.  A row with a
+// non-finite logit gets status -1 in out_status[row] or, without a status
+// array, records kErrNonFinite (info: the row) so the step fails closed.
 template <int NT>
 __global__ void __launch_bounds__(NT) argmax_kernel(const float* __restrict__ logits, int64_t ld, int V,
                                                     int32_t* __restrict__ out_tok, int32_t* __restrict__ status) {
@@ -344,6 +345,7 @@ __global__ void __launch_bounds__(NT) argmax_kernel(const float* __restrict__ lo
   if (threadIdx.x == 0) {
     out_tok[blockIdx.x] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
     if (status) status[blockIdx.x] = bad ? -1 : 0;
+    else if (bad) set_error(kErrNonFinite, blockIdx.x);
   }
 }
 
@@ -364,13 +366,15 @@ __global__ void __launch_bounds__(NT) argmax_key_kernel(const float* __restrict_
   __shared__ uint64_t sh[NT / 32];
   const float* row = logits + (size_t)blockIdx.x * ld;
   uint64_t best = 0;
+  bool bad = false;
   for (int i = threadIdx.x; i < V; i += NT) {
     const float v = row[i];
-    if (!isfinite(v)) continue;
+    if (!isfinite(v)) { bad = true; continue; }
     const uint64_t k = ckey(v, i + id_offset);
     best = k > best ? k : best;
   }
   best = block_max_u64<NT>(best, sh);
+  if (bad) set_error(kErrNonFinite, blockIdx.x);   // any thread: the word keeps the first code
   if (threadIdx.x == 0) keys[blockIdx.x] = best;
 }
 
@@ -574,7 +578,11 @@ __device__ void sample_row(const Src& src, const SampleParams p, int32_t* out_to
   finite = block_sum_i<NT>(finite, shi);
   const int top_id = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
   if (bad) {
-    if (threadIdx.x == 0) { *out_tok = top_id; if (status) *status = -1; }
+    if (threadIdx.x == 0) {
+      *out_tok = top_id;
+      if (status) *status = -1;
+      else set_error(kErrNonFinite, blockIdx.x);
+    }
     return;
   }
   if (p.mode == 0 || !(p.temperature > 0.f)) {

@@ -17,12 +17,16 @@ import torch.nn.functional as F
 from ..sampling.host import PARAM_DTYPE, counter_unit, stochastic_sample
 
 
+ERR_NON_FINITE = 6      # the device error code of csrc/kernels/common.cuh
+
+
 class TorchOps:
     name = "torch"
 
     def __init__(self, device="cpu"):
         self.device = torch.device(device)
         self.launches = 0
+        self._error = (0, 0)      # (code, info) as the device error word keeps them
 
     @staticmethod
     def forward_tokens(ids, fwd):
@@ -143,10 +147,22 @@ class TorchOps:
         o = torch.matmul(p, V.float()).reshape(R, Hq * D)
         out[tok_t, : Hq * D] = o.to(out.dtype)
 
+    def _finite(self, logits):
+        """Non-finite logits fail the step (error code 6, info = the first
+        bad row), as the device samplers record them; the row is still
+        sampled over its finite entries."""
+        ok = torch.isfinite(logits)
+        if bool(ok.all()):
+            return logits
+        if not self._error[0]:
+            self._error = (ERR_NON_FINITE, int((~ok).any(-1).nonzero()[0]))
+        return torch.where(ok, logits, torch.full_like(logits, float("-inf")))
+
     def argmax(self, logits, out):
-        out[: logits.shape[0]] = torch.argmax(logits, -1).to(torch.int32)
+        out[: logits.shape[0]] = torch.argmax(self._finite(logits), -1).to(torch.int32)
 
     def sample(self, logits, params, out):
+        logits = self._finite(logits)
         R = logits.shape[0]
         p = params.detach().cpu().numpy().view(PARAM_DTYPE)[:R]
         lg = logits.detach().double().cpu().numpy()
@@ -163,7 +179,10 @@ class TorchOps:
         out[:R] = torch.from_numpy(res).to(out.device)
 
     def read_error(self, clear=True):
-        return (0, 0)
+        e = self._error
+        if clear:
+            self._error = (0, 0)
+        return e
 
     # vocab-parallel greedy: composite key (logit, lowest global id) per row
     def argmax_keys(self, logits, id_offset, keys):

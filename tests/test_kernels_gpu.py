@@ -356,6 +356,17 @@ def test_argmax(C):
     exp[3] = 77
     assert torch.equal(out.long(), exp)
     assert int(st.abs().sum()) == 0
+    # a non-finite logit: status -1 for its row, or (no status array, as the
+    # engine calls it) error code 6 with the row, so the step fails closed
+    logits[5, 10] = float("nan")
+    logits[5, 11] = 60.0
+    C.read_error(True)
+    C.argmax(logits, out, st)
+    torch.cuda.synchronize()
+    assert int(out[5]) == 11 and int(st[5]) == -1 and C.read_error(True)[0] == 0
+    C.argmax(logits, out, None)
+    torch.cuda.synchronize()
+    assert C.read_error(True) == (6, 5)
 
 
 def _params(rows):

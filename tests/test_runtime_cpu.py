@@ -104,3 +104,38 @@ def test_engine_fails_active_requests_on_device_fault(kind):
     b = eng.add_request(list(range(5, 20)), 4)
     eng.run_until_done()
     assert len(eng.results[b].tokens) == 4 and eng.results[b].error is None
+
+
+def test_non_finite_logits_fail_the_step_closed():
+    """A sampler that meets a non-finite logit records error code 6 with the
+    row; the engine fails the step (active requests fail retryably) instead of
+    emitting a token picked around it (reference: engine/device_step
+    'non-finite BF16 terminal output fails closed')."""
+    from lunaflux_b200.contracts import PublicErrorCode
+    from lunaflux_b200.engine.runner import StepFailed
+    from lunaflux_b200.ops.torch_ops import ERR_NON_FINITE, TorchOps
+
+    ops = TorchOps()
+    out = torch.empty(3, dtype=torch.int32)
+    lg = torch.randn(3, 50)
+    lg[1, 7] = float("nan")
+    lg[1, 9] = 100.0
+    ops.argmax(lg, out)
+    assert int(out[1]) == 9 and ops.read_error(True) == (ERR_NON_FINITE, 1) and ops.read_error() == (0, 0)
+
+    class PoisonedOps(TorchOps):
+        calls = 0
+
+        def argmax(self, logits, out):
+            PoisonedOps.calls += 1
+            if PoisonedOps.calls == 3:
+                logits = logits.clone()
+                logits[0, 0] = float("inf")
+            super().argmax(logits, out)
+
+    eng = _engine(PoisonedOps())
+    a = eng.add_request(list(range(3, 30)), 8)
+    with pytest.raises(StepFailed) as e:
+        eng.run_until_done()
+    assert e.value.code == ERR_NON_FINITE
+    assert eng.results[a].error is PublicErrorCode.WORKER_UNAVAILABLE
