@@ -139,3 +139,23 @@ def test_non_finite_logits_fail_the_step_closed():
         eng.run_until_done()
     assert e.value.code == ERR_NON_FINITE
     assert eng.results[a].error is PublicErrorCode.WORKER_UNAVAILABLE
+
+
+def test_registry_matches_the_built_extension_and_the_sources():
+    """Every registered op names an existing source file and, when the
+    extension is built here, an entry point it exports (reference:
+    kernels/catalog, a closed capability table checked at load time)."""
+    import os
+    from lunaflux_b200.ops import registry
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ops = [e.op for e in registry.OPS]
+    assert len(ops) == len(set(ops)), "an op is registered twice"
+    for e in registry.OPS:
+        assert os.path.isfile(os.path.join(root, e.source)), e
+        assert e.capability
+    try:
+        from lunaflux_b200 import _C
+    except ImportError:
+        pytest.skip("extension not built")
+    registry.validate(_C)
+    assert not any("MISSING" in line for line in registry.manifest(_C))
