@@ -139,6 +139,11 @@ def test_non_finite_logits_fail_the_step_closed():
         eng.run_until_done()
     assert e.value.code == ERR_NON_FINITE
     assert eng.results[a].error is PublicErrorCode.WORKER_UNAVAILABLE
+    # the failed step left the KV arena balanced (reference: worker_service
+    # 'worker failure ... balanced KV')
+    sch = eng.scheduler
+    sch.debug_check_invariants()
+    assert not sch.running and not sch.inflight and sch.allocator.free_page_count() == sch.allocator.capacity
 
 
 def test_registry_matches_the_built_extension_and_the_sources():
