@@ -110,7 +110,8 @@ class ApprovedRoot {
       opened.push_back(nfd);
       dfd = nfd;
     }
-    const int fd = ::openat(dfd, parts.back().c_str(), O_RDONLY | O_NOFOLLOW | O_CLOEXEC);
+    // O_NONBLOCK: opening a FIFO must not wait for a writer (it is rejected below)
+    const int fd = ::openat(dfd, parts.back().c_str(), O_RDONLY | O_NOFOLLOW | O_CLOEXEC | O_NONBLOCK);
     const int err = errno;
     cleanup();
     if (fd < 0) throw ApprovedFsError(std::string("cannot open locator: ") + std::strerror(err));
@@ -119,6 +120,7 @@ class ApprovedRoot {
       ::close(fd);
       throw ApprovedFsError("locator is not a regular file");
     }
+    ::fcntl(fd, F_SETFL, ::fcntl(fd, F_GETFL) & ~O_NONBLOCK);
     return fd;
   }
 

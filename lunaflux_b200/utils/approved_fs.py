@@ -74,7 +74,8 @@ class PyApprovedRoot:
                 nfd = os.open(p, os.O_RDONLY | os.O_DIRECTORY | os.O_NOFOLLOW | os.O_CLOEXEC, dir_fd=dfd)
                 opened.append(nfd)
                 dfd = nfd
-            fd = os.open(parts[-1], os.O_RDONLY | os.O_NOFOLLOW | os.O_CLOEXEC, dir_fd=dfd)
+            # O_NONBLOCK: opening a FIFO must not wait for a writer (it is rejected below)
+            fd = os.open(parts[-1], os.O_RDONLY | os.O_NOFOLLOW | os.O_CLOEXEC | os.O_NONBLOCK, dir_fd=dfd)
         except OSError as e:
             raise ApprovedFsError(f"cannot open locator: {e.strerror}") from None
         finally:
@@ -83,6 +84,7 @@ class PyApprovedRoot:
         if not stat.S_ISREG(os.fstat(fd).st_mode):
             os.close(fd)
             raise ApprovedFsError("locator is not a regular file")
+        os.set_blocking(fd, True)
         return fd
 
     def read_snapshot(self, locator: str, max_bytes: int = 1 << 34) -> Tuple[bytes, Stamp]:

@@ -90,3 +90,74 @@ def test_config_reader_llama3_rope_scaling():
     assert b == a
     assert parse_config(json.dumps(to_config(a))) == a
     assert a.plan_digest() != llama3_8b().plan_digest()
+
+
+def _one_file_dir(path):
+    spec = tiny_llama()
+    ck = random_checkpoint(spec, 1)
+    save_sharded(ck, str(path), max_shard_bytes=1 << 30, config=to_config(spec))
+    return [f for f in os.listdir(path) if f.endswith(".safetensors")][0]
+
+
+def test_weight_locators_that_are_links_or_not_files_are_rejected(tmp_path):
+    """Reference: model/device_materialize 'inspection rejects symlink
+    locators', 'inspection rejects a non-regular locator'."""
+    real = tmp_path / "real"
+    name = _one_file_dir(real)
+    linked = tmp_path / "linked"
+    os.makedirs(linked)
+    os.symlink(real / "config.json", linked / "config.json")
+    os.symlink(real / name, linked / name)
+    with pytest.raises(CheckpointError):
+        CheckpointDir(str(linked)).spec()
+    fifo_dir = tmp_path / "fifo"
+    os.makedirs(fifo_dir)
+    os.mkfifo(fifo_dir / "model.safetensors")
+    with pytest.raises((CheckpointError, ValueError, OSError)):
+        CheckpointDir(str(fifo_dir))
+
+
+def test_content_digest_follows_the_bytes_not_the_stamps(tmp_path):
+    """Same size, same file, one byte changed: the content digest changes
+    (reference: 'readmission hashes exact bytes instead of trusting old file
+    stamps')."""
+    name = _one_file_dir(tmp_path)
+    p = tmp_path / name
+    with CheckpointDir(str(tmp_path)) as d:
+        before = d.content_digest()
+    st = os.stat(p)
+    data = bytearray(p.read_bytes())
+    data[-1] ^= 0x01                    # inside the last tensor's payload
+    p.write_bytes(bytes(data))
+    os.utime(p, ns=(st.st_atime_ns, st.st_mtime_ns))
+    with CheckpointDir(str(tmp_path)) as d:
+        after = d.content_digest()
+    assert before != after and len(after) == 64
+
+
+def test_truncated_weights_are_rejected(tmp_path):
+    name = _one_file_dir(tmp_path)
+    p = tmp_path / name
+    data = p.read_bytes()
+    p.write_bytes(data[:-7])
+    with pytest.raises((CheckpointError, ValueError)):
+        with CheckpointDir(str(tmp_path)) as d:
+            for n in d.names():
+                d.tensor(n)
+
+
+@pytest.mark.parametrize("impl", ["PyApprovedRoot", "NativeApprovedRoot"])
+def test_approved_root_refuses_a_fifo_without_blocking(tmp_path, impl):
+    """Opening a named pipe would wait for a writer: the approved root opens
+    without blocking and refuses anything that is not a regular file."""
+    from lunaflux_b200.utils import approved_fs
+    cls = getattr(approved_fs, impl)
+    if impl == "NativeApprovedRoot":
+        pytest.importorskip("lunaflux_b200._host")
+    os.mkfifo(tmp_path / "pipe")
+    (tmp_path / "ok.bin").write_bytes(b"abc")
+    root = cls(str(tmp_path))
+    with pytest.raises(approved_fs.ApprovedFsError, match="regular file"):
+        root.read_snapshot("pipe", 10)
+    data, st = root.read_snapshot("ok.bin", 10)
+    assert data == b"abc" and st.size == 3
