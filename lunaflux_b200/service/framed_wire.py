@@ -390,6 +390,11 @@ class FrameReader:
         self.poisoned = False
         self._first = 0.0        # receipt time of the first buffered byte
 
+    @property
+    def first_byte_time(self) -> float:
+        """Receipt time (as passed to ``feed_timed``) of the buffered partial frame."""
+        return self._first
+
     def feed(self, data: bytes) -> List[bytes]:
         if self.poisoned:
             raise FramedWireError("stream", "poisoned")

@@ -284,7 +284,7 @@ class TCPServer:
     """Framed request-v1 / event-v2 endpoint on asyncio; many concurrent clients."""
 
     def __init__(self, service: EngineService, host: str = "127.0.0.1", port: int = 0, max_frame: int = 16 << 20,
-                 max_pending_events: int = 1 << 16):
+                 max_pending_events: int = 1 << 16, receipt_timeout_s: float = 30.0):
         self.service = service
         self.host = host
         self.port = port
@@ -293,6 +293,11 @@ class TCPServer:
         # this many undelivered events its requests are cancelled and the
         # connection is closed.
         self.max_pending_events = max_pending_events
+        # A frame whose first byte arrived must be complete within this time;
+        # a client that stalls mid-frame is disconnected (its partial frame
+        # would otherwise hold up to max_frame bytes for as long as it likes).
+        self.receipt_timeout_s = receipt_timeout_s
+        self.receipt_timeouts = 0
         self.overflows = 0
         self.server: Optional[asyncio.AbstractServer] = None
 
@@ -359,7 +364,18 @@ class TCPServer:
         pump_task = asyncio.create_task(pump())
         try:
             while True:
-                data = await reader.read(65536)
+                if frames.buf:
+                    left = frames.first_byte_time + self.receipt_timeout_s - self.service.clock()
+                    try:
+                        data = await asyncio.wait_for(reader.read(65536), max(left, 0.0))
+                    except asyncio.TimeoutError:
+                        self.receipt_timeouts += 1
+                        for rid in list(open_rids):
+                            self.service.cancel(rid)
+                        open_rids.clear()
+                        break
+                else:
+                    data = await reader.read(65536)
                 if not data:
                     break
                 try:

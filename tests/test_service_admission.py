@@ -303,3 +303,38 @@ def test_an_unexpected_admission_error_fails_only_its_request(tiny):
         svc.stop()
     assert first == [FailedEvent(1, PublicErrorCode.INTERNAL, False)]
     assert isinstance(second[-1], CompletedEvent)
+
+
+def test_a_client_stalled_mid_frame_is_disconnected(tiny):
+    """A frame must be complete within the receipt timeout of its first byte
+    (reference: request_admission 'pre-View hard receipt deadline expires and
+    frees scanner authority'); a connection that only sent whole frames is not
+    affected by the timeout."""
+    import asyncio
+    from lunaflux_b200.service.server import TCPServer
+    svc, _ = service(tiny)
+    svc.start()
+    frame = encode_request(GenerateRequest(1, input_tokens=(5, 6), max_new_tokens=2))
+
+    async def main():
+        server = TCPServer(svc, receipt_timeout_s=0.3)
+        port = await server.start()
+        # an idle connection with no partial frame stays open
+        r0, w0 = await asyncio.open_connection("127.0.0.1", port)
+        r, w = await asyncio.open_connection("127.0.0.1", port)
+        w.write(frame[:40])
+        await w.drain()
+        t0 = time.monotonic()
+        rest = await asyncio.wait_for(r.read(), 10)          # EOF once the server drops us
+        waited = time.monotonic() - t0
+        idle_open = not r0.at_eof()
+        w.close()
+        w0.close()
+        server.close()
+        return rest, waited, server.receipt_timeouts, idle_open
+
+    try:
+        rest, waited, n, idle_open = asyncio.run(main())
+    finally:
+        svc.stop()
+    assert rest == b"" and 0.2 <= waited < 5.0 and n == 1 and idle_open
