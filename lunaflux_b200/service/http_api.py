@@ -98,6 +98,7 @@ class CompletionsServer:
         self.port = port
         self.model = model
         self.max_body = max_body
+        self.request_timeout_s = 30.0
         self._ids = itertools.count(_ID_BASE)
         self.server: Optional[asyncio.AbstractServer] = None
 
@@ -152,7 +153,8 @@ class CompletionsServer:
         receipt = self.service.clock()     # the connection is accepted: the request's receipt time
         try:
             try:
-                method, path, body = await self._read_request(reader)
+                # the whole request (line, headers, body) within one deadline
+                method, path, body = await asyncio.wait_for(self._read_request(reader), self.request_timeout_s)
                 if path == "/v1/models":
                     if method != "GET":
                         raise HTTPError(405, "use GET")
