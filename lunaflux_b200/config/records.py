@@ -2,6 +2,7 @@
 from __future__ import annotations
 
 import dataclasses
+import typing
 from typing import Any, Dict, List, Optional, Tuple
 
 from ..utils.json_strict import loads_strict
@@ -50,6 +51,8 @@ class ModelConfig:
     def __post_init__(self):
         if not self.artifact_path and not self.preset:
             raise ConfigError("model needs artifact_path or preset")
+        if not 0 <= self.seed < (1 << 64):
+            raise ConfigError("seed must be in [0, 2^64)")
         if self.expected_digest and (len(self.expected_digest) != 64
                                      or any(c not in "0123456789abcdef" for c in self.expected_digest)):
             raise ConfigError("expected_digest must be 64 lowercase hex characters")
@@ -63,6 +66,8 @@ class DeviceConfig:
     def __post_init__(self):
         if not self.visible_devices or len(set(self.visible_devices)) != len(self.visible_devices):
             raise ConfigError("visible_devices must be a non-empty set")
+        if any(d < 0 for d in self.visible_devices):
+            raise ConfigError("visible_devices must be device ordinals")
         _pos("memory_ceiling_bytes", self.memory_ceiling_bytes)
 
 
@@ -128,6 +133,8 @@ class KernelConfig:
     def __post_init__(self):
         if list(self.graph_batch_sizes) != sorted(set(self.graph_batch_sizes)) or not self.graph_batch_sizes:
             raise ConfigError("graph_batch_sizes must be strictly increasing")
+        if self.graph_batch_sizes[0] < 1:
+            raise ConfigError("graph_batch_sizes must be positive")
 
 
 @dataclasses.dataclass(frozen=True)
@@ -147,6 +154,19 @@ _SECTIONS = {
 }
 
 
+def _type_ok(v, t) -> bool:
+    """Whether a JSON value has the field's declared type exactly (no bool for
+    an int, no 1.0 for an int, no number for a string)."""
+    if t is bool or t is int or t is str:
+        return type(v) is t
+    if t is float:
+        return type(v) in (int, float)
+    if typing.get_origin(t) is tuple:
+        (elem, _ellipsis) = typing.get_args(t)
+        return isinstance(v, tuple) and all(_type_ok(x, elem) for x in v)
+    return True
+
+
 def _build(cls, obj: Dict[str, Any], where: str):
     if not isinstance(obj, dict):
         raise ConfigError(f"{where} must be an object")
@@ -154,10 +174,13 @@ def _build(cls, obj: Dict[str, Any], where: str):
     unknown = set(obj) - set(fields)
     if unknown:
         raise ConfigError(f"{where}: unknown field(s) {sorted(unknown)}")
+    hints = typing.get_type_hints(cls)
     kw = {}
     for k, v in obj.items():
         if isinstance(v, list):
             v = tuple(v)
+        if not _type_ok(v, hints[k]):
+            raise ConfigError(f"{where}.{k} has the wrong type")
         kw[k] = v
     try:
         return cls(**kw)
@@ -165,8 +188,13 @@ def _build(cls, obj: Dict[str, Any], where: str):
         raise ConfigError(f"{where}: {e}") from None
 
 
+MAX_DOCUMENT_BYTES = 1 << 20       # checked before any parsing
+
+
 def parse_document(text: str | bytes) -> EngineConfig:
     """Parses one strict JSON config document (duplicate / unknown keys rejected)."""
+    if len(text) > MAX_DOCUMENT_BYTES:
+        raise ConfigError(f"config document exceeds {MAX_DOCUMENT_BYTES} bytes")
     try:
         obj = loads_strict(text)
     except ValueError as e:
