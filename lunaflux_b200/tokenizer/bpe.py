@@ -94,6 +94,10 @@ class Tokenizer:
         self.added_ids = {i for _, i in added}
         for s, i in added:
             self.id_to_token.setdefault(i, s)
+        # ids are dense from 0 (every id below the largest decodes to a token)
+        ids = self.id_to_token.keys()
+        if any(type(i) is not int or i < 0 for i in ids) or (ids and max(ids) + 1 != len(ids)):
+            raise TokenizerError("token ids must be dense from 0")
         self.digest = digest
         # The merge loop runs in the C++ host core when it is built (same
         # semantics, on ids); the Python loop below is its reference.

@@ -62,13 +62,25 @@ def test_unicode_and_zero_byte_roundtrip():
 
 
 def test_special_tokens_longest_match():
-    text, vocab = make_json(MERGES, added=[("<s>", 300), ("<s>x", 301)])
+    _, vocab = make_json(MERGES)
+    s, sx = len(vocab), len(vocab) + 1          # added ids continue the dense range
+    text, vocab = make_json(MERGES, added=[("<s>", s), ("<s>x", sx)])
     tok = Tokenizer.from_json(text)
-    assert tok.encode("<s>xunrelated") == [301, vocab["unrelated"]]
-    assert tok.encode("a<s>b") == [vocab["a"], 300, vocab["b"]]
+    assert tok.encode("<s>xunrelated") == [sx, vocab["unrelated"]]
+    assert tok.encode("a<s>b") == [vocab["a"], s, vocab["b"]]
     with pytest.raises(TokenizerError):
         tok.encode("a<s>b", allow_special=False)
-    assert tok.decode([300]) == "<s>"
+    assert tok.decode([s]) == "<s>"
+
+
+def test_token_ids_must_be_dense_from_zero():
+    """Reference: tokenizer 'token IDs must be dense within the vocabulary
+    range'; an id gap or a negative id is refused at load."""
+    _, vocab = make_json(MERGES)
+    for added in ([("<s>", len(vocab) + 5)], [("<s>", -1)]):
+        text, _ = make_json(MERGES, added=added)
+        with pytest.raises(TokenizerError, match="dense"):
+            Tokenizer.from_json(text)
 
 
 @pytest.mark.parametrize("override", [
