@@ -75,7 +75,8 @@ def prepare_distribution(logits, temperature: float, top_k: Optional[int], top_p
     k = a.size if top_k is None else min(top_k, a.size)
     order = order[:k]
     mx = a[order[0]]
-    w = np.exp((a[order] - mx) / temperature)
+    with np.errstate(over="ignore"):       # the spread of extreme finite logits may overflow to -inf: weight 0
+        w = np.exp((a[order] - mx) / temperature)
     total = float(np.sum(w)) if k < 64 else math.fsum(w)
     if not (total > 0 and math.isfinite(total)):
         raise SamplingError("invalid distribution")
