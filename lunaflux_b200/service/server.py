@@ -45,6 +45,17 @@ class _Live:
     n_out: int = 0
 
 
+def _guarded(sink: Callable[[object], None]) -> Callable[[object], None]:
+    """A sink whose failure (a client's event loop already closed, a broken
+    callback) drops that event instead of ending the engine thread."""
+    def emit(ev):
+        try:
+            sink(ev)
+        except Exception:
+            pass
+    return emit
+
+
 class EngineService:
     """Owns the engine thread; thread-safe submit / cancel; events via sinks."""
 
@@ -93,6 +104,7 @@ class EngineService:
         ``overloaded``); those queued before the drain began are admitted."""
         if receipt is None:
             receipt = self.clock()
+        sink = _guarded(sink)
         if self.draining:
             sink(FailedEvent(req.request_id, PublicErrorCode.OVERLOADED, True))
             return
@@ -284,8 +296,13 @@ class TCPServer:
     """Framed request-v1 / event-v2 endpoint on asyncio; many concurrent clients."""
 
     def __init__(self, service: EngineService, host: str = "127.0.0.1", port: int = 0, max_frame: int = 16 << 20,
-                 max_pending_events: int = 1 << 16, receipt_timeout_s: float = 30.0):
+                 max_pending_events: int = 1 << 16, receipt_timeout_s: float = 30.0, max_connections: int = 4096):
         self.service = service
+        # connections beyond this are closed at accept (each holds a frame
+        # buffer and an event queue)
+        self.max_connections = max_connections
+        self.connections = 0
+        self.refused_connections = 0
         self.host = host
         self.port = port
         self.max_frame = max_frame
@@ -307,6 +324,17 @@ class TCPServer:
         return self.port
 
     async def _client(self, reader: asyncio.StreamReader, writer: asyncio.StreamWriter):
+        if self.connections >= self.max_connections:
+            self.refused_connections += 1
+            writer.close()
+            return
+        self.connections += 1
+        try:
+            await self._serve_client(reader, writer)
+        finally:
+            self.connections -= 1
+
+    async def _serve_client(self, reader: asyncio.StreamReader, writer: asyncio.StreamWriter):
         loop = asyncio.get_running_loop()
         frames = FrameReader(REQUEST_MAGIC, self.max_frame)
         open_rids = set()

@@ -338,3 +338,54 @@ def test_a_client_stalled_mid_frame_is_disconnected(tiny):
     finally:
         svc.stop()
     assert rest == b"" and 0.2 <= waited < 5.0 and n == 1 and idle_open
+
+
+def test_connections_beyond_the_limit_are_closed_at_accept(tiny):
+    import asyncio
+    from lunaflux_b200.service.server import TCPServer
+    svc, _ = service(tiny)
+    svc.start()
+
+    async def main():
+        server = TCPServer(svc, max_connections=2)
+        port = await server.start()
+        conns = [await asyncio.open_connection("127.0.0.1", port) for _ in range(2)]
+        await asyncio.sleep(0.2)
+        r3, w3 = await asyncio.open_connection("127.0.0.1", port)
+        third = await asyncio.wait_for(r3.read(), 5)         # closed by the server
+        for _, w in conns:
+            w.close()
+        w3.close()
+        await asyncio.sleep(0.2)
+        # a slot freed by a closed connection is usable again
+        r4, w4 = await asyncio.open_connection("127.0.0.1", port)
+        w4.write(encode_request(GenerateRequest(4, input_tokens=(5, 6), max_new_tokens=1)))
+        await w4.drain()
+        got = await asyncio.wait_for(r4.read(208), 10)
+        w4.close()
+        server.close()
+        return third, got, server.refused_connections
+
+    try:
+        third, got, refused = asyncio.run(main())
+    finally:
+        svc.stop()
+    assert third == b"" and refused == 1 and len(got) > 0
+
+
+def test_a_failing_sink_does_not_end_the_engine_thread(tiny):
+    svc, _ = service(tiny)
+    c = Client()
+
+    def broken(ev):
+        raise RuntimeError("Event loop is closed")
+
+    svc.start()
+    try:
+        svc.submit(GenerateRequest(1, input_tokens=(5, 6), max_new_tokens=3), broken)
+        svc.submit(GenerateRequest(2, input_tokens=(5, 6), max_new_tokens=3), c.sink(2))
+        evs = c.wait(2)
+        assert svc.alive()
+    finally:
+        svc.stop()
+    assert isinstance(evs[-1], CompletedEvent)
