@@ -49,13 +49,20 @@ def _reason_phrase(status: int) -> str:
             503: "Service Unavailable"}.get(status, "Error")
 
 
+def _utf8(s: str, what: str) -> bytes:
+    try:
+        return s.encode("utf-8")
+    except UnicodeEncodeError:          # a lone surrogate escape in the JSON text
+        raise HTTPError(400, f"{what} is not valid Unicode") from None
+
+
 def build_request(body: dict, request_id: int) -> GenerateRequest:
     """The engine request of a completions body (validated by the caller)."""
     if not isinstance(body, dict):
         raise HTTPError(400, "the body must be a JSON object")
     prompt = body.get("prompt")
     if isinstance(prompt, str):
-        tokens, text = None, prompt.encode("utf-8")
+        tokens, text = None, _utf8(prompt, "prompt")
     elif isinstance(prompt, list) and prompt and all(type(t) is int for t in prompt):
         tokens, text = tuple(prompt), None
     else:
@@ -85,7 +92,7 @@ def build_request(body: dict, request_id: int) -> GenerateRequest:
     if not isinstance(stop, list) or not all(isinstance(s, str) for s in stop):
         raise HTTPError(400, "stop must be a string or a list of strings")
     return GenerateRequest(request_id, input_tokens=tokens, input_text=text, max_new_tokens=max_tokens,
-                           sampling=sampling, stop=StopConditions((), tuple(s.encode("utf-8") for s in stop)))
+                           sampling=sampling, stop=StopConditions((), tuple(_utf8(s, "stop") for s in stop)))
 
 
 class CompletionsServer:
@@ -175,6 +182,9 @@ class CompletionsServer:
                     raise HTTPError(404, "no such endpoint")
             except HTTPError as e:
                 self._json(writer, e.status, {"error": {"message": e.message, "type": "invalid_request_error"}})
+            except (ValueError, asyncio.LimitOverrunError):
+                # an over-long line, undecodable bytes: the request is malformed
+                self._json(writer, 400, {"error": {"message": "malformed request", "type": "invalid_request_error"}})
             await writer.drain()
         except (asyncio.TimeoutError, asyncio.IncompleteReadError, ConnectionError, OSError):
             pass

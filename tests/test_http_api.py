@@ -204,3 +204,31 @@ def test_chat_completions_endpoint(stack):
     assert all(c["object"] == "chat.completion.chunk" for c in chunks)
     assert "".join(c["choices"][0]["delta"].get("content", "") for c in chunks) == want
     assert sc == 400
+
+
+def test_hostile_http_requests_get_a_400(stack):
+    """A lone surrogate in the prompt or a stop string, an over-long header
+    line, a body that is not JSON or is over the size limit: each gets an
+    error response, and the server keeps serving."""
+    svc, ref, eng = stack
+
+    async def raw(port, payload):
+        r, w = await asyncio.open_connection("127.0.0.1", port)
+        w.write(payload)
+        await w.drain()
+        out = await r.read()
+        w.close()
+        return int(out.split()[1]) if out else None
+
+    async def go(port):
+        res = []
+        for body in (b'{"prompt": "\\ud800", "max_tokens": 2}', b'{"prompt": [1], "stop": "\\udfff"}',
+                     b"{not json"):
+            res.append(await raw(port, b"POST /v1/completions HTTP/1.1\r\nContent-Length: %d\r\n\r\n" % len(body)
+                                 + body))
+        res.append(await raw(port, b"POST /v1/completions HTTP/1.1\r\nX: " + b"a" * 70000 + b"\r\n\r\n"))
+        res.append(await raw(port, b"POST /v1/completions HTTP/1.1\r\nContent-Length: 99999999\r\n\r\n"))
+        res.append((await _http(port, "POST", "/v1/completions", {"prompt": [1, 2], "max_tokens": 2}))[0])
+        return res
+
+    assert _run(svc, go) == [400, 400, 400, 400, 413, 200]
