@@ -28,6 +28,7 @@ admitted at t = 0 and run to completion).  Metrics:
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -219,6 +220,10 @@ def main():
     if not args.no_graphs:
         engine.runner.capture_all(False)
     torch.cuda.synchronize()
+    # as a server does once it is up: the start-up objects leave the cyclic
+    # collector's generations, so a full collection does not stall a step
+    gc.collect()
+    gc.freeze()
 
     # synthetic seeded prompts, uniform over the vocabulary, held in pinned host memory
     g = torch.Generator().manual_seed(args.seed)

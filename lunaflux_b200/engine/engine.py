@@ -122,7 +122,9 @@ class LLMEngine:
             self._next_rid += 1
         sampling = sampling or SamplingParameters()
         now = self.clock()
-        toks = prompt.tolist() if hasattr(prompt, "tolist") else [int(t) for t in prompt]   # plain ints
+        # plain ints in a tuple: a tuple of ints is not tracked by the cyclic
+        # garbage collector, so a long queue of prompts adds nothing to a pass
+        toks = tuple(prompt.tolist() if hasattr(prompt, "tolist") else [int(t) for t in prompt])
         check_token_ids(toks, self.spec.vocab)
         req = Request(rid=rid, prompt=toks, max_new=max_new_tokens, sampling=sampling,
                       stop_ids=frozenset(int(t) for t in stop_ids),

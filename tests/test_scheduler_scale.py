@@ -66,3 +66,10 @@ def test_completion_validates_before_mutation():
         s.complete(second, [5, 5])             # one token short
     outs = s.complete(second, [5, 6, 7])
     assert [o.token for o in outs] == [5, 6, 7] and not s.inflight
+
+
+def test_host_step_benchmark_runs_small():
+    from lunaflux_b200.bench.host import run
+    res = run(requests=64, rows=16, prompt=96, output=8, budget=256, steps=80)
+    assert res["prefill"]["steps"] > 0 and res["decode"]["steps"] > 0
+    assert all(v >= 0 for kind in res.values() for v in kind.values())
