@@ -28,6 +28,7 @@ pre-token are cached.
 from __future__ import annotations
 
 import hashlib
+from dataclasses import dataclass
 from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
 from ..utils.json_strict import loads_strict
@@ -39,7 +40,53 @@ _CACHE_MAX = 1 << 16
 
 
 class TokenizerError(ValueError):
-    pass
+    """A tokenizer failure.  ``kind`` names the failure class (the reference's
+    typed errors, tokenizer/types.mbt: ``input_too_long``, ``output_too_long``,
+    ``special_token_rejected``, ``unknown_token_id``, ``decoded_too_long``,
+    ``invalid_utf8``, ``limit`` ...; ``invalid`` for a malformed document) and
+    ``fields`` its integers (``actual`` / ``maximum`` / ``token_id``); neither
+    carries text from the input."""
+
+    def __init__(self, message: str, kind: str = "invalid", **fields: int):
+        super().__init__(message)
+        self.kind = kind
+        self.fields = fields
+
+
+@dataclass(frozen=True)
+class TokenizerLimits:
+    """Resource bounds checked at load and on every bounded call (reference:
+    ``TokenizerLimits``, tokenizer/types.mbt).  The defaults admit the Llama 3
+    tokenizer (128256 ids, 280147 merges, 256 special tokens)."""
+    max_input_bytes: int = 1 << 26
+    max_output_tokens: int = 1 << 24
+    max_decoded_bytes: int = 1 << 26
+    max_vocab_entries: int = 1 << 21
+    max_merge_rules: int = 1 << 21
+    max_token_bytes: int = 1 << 12
+    max_special_tokens: int = 1 << 16
+
+    def __post_init__(self):
+        for k, v in self.__dict__.items():
+            if type(v) is not int or v <= 0:
+                raise TokenizerError(f"tokenizer limit {k} must be a positive int", "limit")
+
+
+@dataclass(frozen=True)
+class EncodeResult:
+    """One bounded encode: the ids, the input's byte length and whether the
+    ids were cut at the output limit."""
+    token_ids: List[int]
+    input_bytes: int
+    truncated: bool
+
+
+#: encode-side special-token policies: emit them, refuse the input, or treat
+#: their text as ordinary bytes (no special matching at all)
+SPECIAL_POLICIES = ("allow", "reject", "ordinary")
+#: decode-side policies: keep the special tokens' text, or drop it
+DECODE_SPECIAL_POLICIES = ("preserve", "skip")
+TRUNCATION_POLICIES = ("reject", "truncate")
 
 
 def byte_alphabet() -> Dict[int, str]:
@@ -59,10 +106,26 @@ _B2U = byte_alphabet()
 _U2B = {u: b for b, u in _B2U.items()}
 
 
+def _piece_bytes(sym: str) -> Optional[bytes]:
+    """The bytes a byte-level vocabulary string stands for (None: not one)."""
+    try:
+        return bytes(_U2B[c] for c in sym)
+    except KeyError:
+        return None
+
+
 class Tokenizer:
     def __init__(self, vocab: Dict[str, int], merges: Sequence[Tuple[str, str]], added: Sequence[Tuple[str, int]] = (),
                  digest: str = "", split_pattern: Optional[str] = None, ignore_merges: bool = False,
-                 bos_id: Optional[int] = None):
+                 bos_id: Optional[int] = None, limits: Optional[TokenizerLimits] = None):
+        self.limits = lim = limits if limits is not None else TokenizerLimits()
+        if len(vocab) > lim.max_vocab_entries:
+            raise TokenizerError("vocabulary too large", "limit", actual=len(vocab), maximum=lim.max_vocab_entries)
+        if len(merges) > lim.max_merge_rules:
+            raise TokenizerError("merge table too large", "limit", actual=len(merges), maximum=lim.max_merge_rules)
+        if len(added) > lim.max_special_tokens:
+            raise TokenizerError("too many special tokens", "limit", actual=len(added),
+                                 maximum=lim.max_special_tokens)
         self.vocab = dict(vocab)
         self.split_pattern = split_pattern
         self._split = None
@@ -82,7 +145,13 @@ class Tokenizer:
             self.id_to_token[i] = t
         for b, u in _B2U.items():
             if u not in self.vocab:
-                raise TokenizerError("vocabulary lacks the byte-level alphabet")
+                raise TokenizerError("vocabulary lacks the byte-level alphabet", "missing_byte", byte_value=b)
+        for t, i in self.vocab.items():
+            if not t:
+                raise TokenizerError("empty token piece", "empty_piece", token_id=i)
+            if len(t) > lim.max_token_bytes:   # symbols: one per byte of the piece
+                raise TokenizerError("token piece too long", "limit", token_id=i, actual=len(t),
+                                     maximum=lim.max_token_bytes)
         self.ranks: Dict[Tuple[str, str], int] = {}
         for r, (a, b) in enumerate(merges):
             if a not in self.vocab or b not in self.vocab or (a + b) not in self.vocab:
@@ -92,7 +161,21 @@ class Tokenizer:
             self.ranks[(a, b)] = r
         self.added = sorted(((s, i) for s, i in added), key=lambda x: (-len(x[0].encode()), x[1]))
         self.added_ids = {i for _, i in added}
+        seen_special: Dict[str, int] = {}
         for s, i in added:
+            if not s:
+                raise TokenizerError("empty special token", "empty_piece", token_id=i)
+            if len(s.encode()) > lim.max_token_bytes:
+                raise TokenizerError("special token too long", "limit", token_id=i, actual=len(s.encode()),
+                                     maximum=lim.max_token_bytes)
+            if seen_special.setdefault(s, i) != i:
+                raise TokenizerError("two special tokens with the same text", "duplicate_piece",
+                                     first=seen_special[s], duplicate=i)
+            prev = self.id_to_token.get(i)
+            if prev is not None and prev != s and _piece_bytes(prev) != s.encode():
+                # an id already taken by another piece (a vocabulary entry with
+                # different bytes, or an earlier special token)
+                raise TokenizerError("duplicate token id", "duplicate_id", token_id=i)
             self.id_to_token.setdefault(i, s)
         # ids are dense from 0 (every id below the largest decodes to a token)
         ids = self.id_to_token.keys()
@@ -237,7 +320,7 @@ class Tokenizer:
                 i += 1
                 continue
             if not allow_special:
-                raise TokenizerError("input contains a special token")
+                raise TokenizerError("input contains a special token", "special_token_rejected", token_id=hit[1])
             if start < i:
                 ids += self._segment(text[start:i])
             ids.append(hit[1])
@@ -252,11 +335,49 @@ class Tokenizer:
         post-processor's template (a leading BOS when it has one)."""
         return self.encode_bytes(text.encode("utf-8"), allow_special, add_special_tokens)
 
+    def encode_bounded(self, data: bytes | str, special_policy: str = "allow", output_limit: Optional[int] = None,
+                       truncation: str = "reject", add_special_tokens: bool = False) -> EncodeResult:
+        """Bounded encode (reference: ``TokenizerSpec::encode_bytes`` /
+        ``encode_text``, tokenizer/encode.mbt).  ``special_policy``: "allow"
+        emits special tokens (longest match), "reject" fails at the first one
+        with its id, "ordinary" encodes their text as plain bytes.  The input
+        must fit ``max_input_bytes``; ``output_limit`` (default and ceiling:
+        ``max_output_tokens``) bounds the ids: "reject" fails with the full
+        count, "truncate" keeps the first ``output_limit`` and sets
+        ``truncated``."""
+        if isinstance(data, str):
+            data = data.encode("utf-8")
+        data = bytes(data)
+        lim = self.limits
+        if special_policy not in SPECIAL_POLICIES:
+            raise TokenizerError(f"special_policy must be one of {SPECIAL_POLICIES}", "invalid_argument")
+        if truncation not in TRUNCATION_POLICIES:
+            raise TokenizerError(f"truncation must be one of {TRUNCATION_POLICIES}", "invalid_argument")
+        if output_limit is None:
+            output_limit = lim.max_output_tokens
+        if type(output_limit) is not int or output_limit <= 0 or output_limit > lim.max_output_tokens:
+            raise TokenizerError("output limit outside 1..max_output_tokens", "invalid_output_limit",
+                                 requested=output_limit if type(output_limit) is int else -1,
+                                 maximum=lim.max_output_tokens)
+        if len(data) > lim.max_input_bytes:
+            raise TokenizerError("input too long", "input_too_long", actual=len(data), maximum=lim.max_input_bytes)
+        if special_policy == "ordinary":
+            ids = self._segment(data) if data else []
+        else:
+            ids = self._encode_bytes(data, special_policy == "allow")
+        if add_special_tokens and self.bos_id is not None:
+            ids.insert(0, self.bos_id)
+        if len(ids) > output_limit:
+            if truncation == "reject":
+                raise TokenizerError("output too long", "output_too_long", actual=len(ids), maximum=output_limit)
+            return EncodeResult(ids[:output_limit], len(data), True)
+        return EncodeResult(ids, len(data), False)
+
     # ------------------------------------------------------------------ decode
     def token_bytes(self, tid: int) -> bytes:
-        t = self.id_to_token.get(tid)
+        t = self.id_to_token.get(tid) if type(tid) is int else None
         if t is None:
-            raise TokenizerError("unknown token id")
+            raise TokenizerError("unknown token id", "unknown_token_id", token_id=tid if type(tid) is int else -1)
         if tid in self.added_ids:
             return t.encode("utf-8")
         try:
@@ -264,10 +385,41 @@ class Tokenizer:
         except KeyError:
             raise TokenizerError("token outside the byte-level alphabet") from None
 
-    def decode_bytes(self, ids: Iterable[int]) -> bytes:
-        return b"".join(self.token_bytes(i) for i in ids)
+    def decode_bytes(self, ids: Iterable[int], special_policy: str = "preserve") -> bytes:
+        """The bytes of ``ids`` (reference: tokenizer/decode.mbt): every id is
+        checked first, "skip" drops special tokens, and the output is bounded
+        by ``max_decoded_bytes`` (nothing is returned past the bound)."""
+        if special_policy not in DECODE_SPECIAL_POLICIES:
+            raise TokenizerError(f"special_policy must be one of {DECODE_SPECIAL_POLICIES}", "invalid_argument")
+        skip = special_policy == "skip"
+        cap = self.limits.max_decoded_bytes
+        out = []
+        n = 0
+        for i in ids:
+            piece = self.token_bytes(i)
+            if skip and i in self.added_ids:
+                continue
+            n += len(piece)
+            if n > cap:
+                raise TokenizerError("decoded output too long", "decoded_too_long", maximum=cap)
+            out.append(piece)
+        return b"".join(out)
+
+    def decode_text(self, ids: Iterable[int], special_policy: str = "preserve") -> str:
+        """Strict text decode: the bytes must be valid UTF-8 (a token sequence
+        that ends inside a character, or carries arbitrary bytes, fails)."""
+        data = self.decode_bytes(ids, special_policy)
+        try:
+            return data.decode("utf-8")
+        except UnicodeDecodeError:
+            raise TokenizerError("decoded bytes are not valid UTF-8", "invalid_utf8") from None
+
+    def decoded_piece_bytes(self, tid: int, special_policy: str = "preserve") -> int:
+        """Byte length of one token's decoded piece (0 for a skipped special)."""
+        return len(self.decode_bytes([tid], special_policy))
 
     def decode(self, ids: Iterable[int]) -> str:
+        """Lenient text decode: invalid UTF-8 becomes U+FFFD."""
         return self.decode_bytes(ids).decode("utf-8", errors="replace")
 
 

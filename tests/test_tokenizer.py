@@ -110,3 +110,153 @@ def test_bpe_model_flags_rejected():
     d["model"]["merges"].append("zz qq")
     with pytest.raises(TokenizerError):
         Tokenizer.from_json(json.dumps(d))
+
+
+# --------------------------------------------------------------------------
+# Bounded encode / decode (reference: tokenizer/tokenizer_test.mbt "special
+# token policy is explicit and longest-match", "output and input bounds reject
+# or truncate deterministically", "decode rejects unknown IDs and decoded byte
+# overflow", "Unicode uses exact UTF-8 bytes and arbitrary bytes round trip").
+
+from lunaflux_b200.tokenizer.bpe import EncodeResult, TokenizerLimits  # noqa: E402
+
+
+def _special_tok(limits=None):
+    _, vocab = make_json(MERGES)
+    eos, e = len(vocab), len(vocab) + 1
+    text, vocab = make_json(MERGES, added=[("<eos>", eos), ("<e", e)])
+    tok = Tokenizer.from_json(text)
+    if limits is not None:
+        tok = Tokenizer(tok.vocab, [tuple(k) for k in sorted(tok.ranks, key=tok.ranks.get)],
+                        [("<eos>", eos), ("<e", e)], limits=limits)
+    return tok, vocab, eos, e
+
+
+def test_special_policies_encode():
+    tok, vocab, eos, e = _special_tok()
+    r = tok.encode_bounded("unrelated<eos><e", special_policy="allow")
+    assert r == EncodeResult([vocab["unrelated"], eos, e], 16, False)
+    # ordinary: the special text is plain bytes, nothing is matched
+    r = tok.encode_bounded("<e>", special_policy="ordinary")
+    assert r.token_ids == [vocab["<"], vocab["e"], vocab[">"]]
+    # reject: fails at the first special token, naming its id
+    with pytest.raises(TokenizerError) as ei:
+        tok.encode_bounded("prefix<eos>", special_policy="reject")
+    assert ei.value.kind == "special_token_rejected" and ei.value.fields == {"token_id": eos}
+    # longest match: "<eos>" wins over its prefix "<e"
+    assert tok.encode_bounded("<eos>").token_ids == [eos]
+    with pytest.raises(TokenizerError, match="special_policy"):
+        tok.encode_bounded("x", special_policy="maybe")
+
+
+def test_output_bound_truncates_or_rejects():
+    tok, vocab, _, _ = _special_tok()
+    r = tok.encode_bounded("unrelated!", special_policy="ordinary", output_limit=1, truncation="truncate")
+    assert r == EncodeResult([vocab["unrelated"]], 10, True)
+    with pytest.raises(TokenizerError) as ei:
+        tok.encode_bounded("unrelated!", output_limit=1)
+    assert ei.value.kind == "output_too_long" and ei.value.fields == {"actual": 2, "maximum": 1}
+    # exactly at the limit is not truncated
+    assert tok.encode_bounded("unrelated!", output_limit=2, truncation="truncate").truncated is False
+    for bad in (0, -1, tok.limits.max_output_tokens + 1, 1.5):
+        with pytest.raises(TokenizerError) as ei:
+            tok.encode_bounded("a", output_limit=bad)
+        assert ei.value.kind == "invalid_output_limit"
+
+
+def test_input_bound():
+    tok, _, _, _ = _special_tok(TokenizerLimits(max_input_bytes=2))
+    assert tok.encode_bounded(b"ab").input_bytes == 2
+    with pytest.raises(TokenizerError) as ei:
+        tok.encode_bounded(b"abc")
+    assert ei.value.kind == "input_too_long" and ei.value.fields == {"actual": 3, "maximum": 2}
+
+
+def test_decode_special_skip_and_unknown_ids():
+    tok, vocab, eos, e = _special_tok()
+    ids = tok.encode("unrelated<eos>")
+    assert tok.decode_text(ids, special_policy="skip") == "unrelated"
+    assert tok.decode_text(ids) == "unrelated<eos>"
+    assert tok.decoded_piece_bytes(eos, "skip") == 0
+    assert tok.decoded_piece_bytes(vocab["unrelated"]) == 9
+    for bad in (9999, -1, tok.vocab_size):
+        with pytest.raises(TokenizerError) as ei:
+            tok.decode_bytes([vocab["a"], bad])
+        assert ei.value.kind == "unknown_token_id" and ei.value.fields == {"token_id": bad}
+    # an unknown id fails even where it would be skipped
+    with pytest.raises(TokenizerError):
+        tok.decode_bytes([9999], special_policy="skip")
+
+
+def test_decoded_byte_bound():
+    tok, vocab, _, _ = _special_tok(TokenizerLimits(max_decoded_bytes=2))
+    assert tok.decode_bytes([vocab["a"], vocab["b"]]) == b"ab"
+    with pytest.raises(TokenizerError) as ei:
+        tok.decode_bytes([vocab["a"], vocab["b"], vocab["c"]])
+    assert ei.value.kind == "decoded_too_long" and ei.value.fields == {"maximum": 2}
+
+
+def test_arbitrary_bytes_round_trip_but_strict_text_fails():
+    tok, _, _, _ = _special_tok()
+    arbitrary = bytes([0xFF, 0x00, 0xC3, 0x28, 0x80])
+    r = tok.encode_bounded(arbitrary, special_policy="ordinary")
+    assert len(r.token_ids) == 5 and tok.decode_bytes(r.token_ids) == arbitrary
+    with pytest.raises(TokenizerError) as ei:
+        tok.decode_text(r.token_ids)
+    assert ei.value.kind == "invalid_utf8"
+    assert tok.decode(r.token_ids) == arbitrary.decode("utf-8", errors="replace")
+    # a character split across tokens decodes strictly only when complete
+    ids = tok.encode("é")
+    assert len(ids) == 2 and tok.decode_text(ids) == "é"
+    with pytest.raises(TokenizerError):
+        tok.decode_text(ids[:1])
+
+
+def test_load_limits_and_duplicates_fail_closed():
+    text, vocab = make_json(MERGES)
+    base = Tokenizer.from_json(text)
+    merges = [tuple(k) for k in sorted(base.ranks, key=base.ranks.get)]
+    with pytest.raises(TokenizerError) as ei:
+        Tokenizer(vocab, merges, limits=TokenizerLimits(max_vocab_entries=256))
+    assert ei.value.kind == "limit" and ei.value.fields["actual"] == len(vocab)
+    with pytest.raises(TokenizerError) as ei:
+        Tokenizer(vocab, merges, limits=TokenizerLimits(max_merge_rules=len(merges) - 1))
+    assert ei.value.kind == "limit"
+    with pytest.raises(TokenizerError) as ei:
+        Tokenizer(vocab, merges, limits=TokenizerLimits(max_token_bytes=8))   # "unrelated" is 9
+    assert ei.value.kind == "limit" and ei.value.fields["actual"] == 9
+    with pytest.raises(TokenizerError) as ei:
+        Tokenizer(vocab, merges, [("<a>", len(vocab)), ("<b>", len(vocab) + 1)],
+                  limits=TokenizerLimits(max_special_tokens=1))
+    assert ei.value.kind == "limit"
+    # two special tokens with one text, or one id for two pieces
+    with pytest.raises(TokenizerError) as ei:
+        Tokenizer(vocab, merges, [("<a>", len(vocab)), ("<a>", len(vocab) + 1)])
+    assert ei.value.kind == "duplicate_piece"
+    with pytest.raises(TokenizerError) as ei:
+        Tokenizer(vocab, merges, [("<a>", vocab["a"])])
+    assert ei.value.kind == "duplicate_id"
+    with pytest.raises(TokenizerError) as ei:
+        Tokenizer(vocab, merges, [("", len(vocab))])
+    assert ei.value.kind == "empty_piece"
+    # a missing byte symbol names the byte
+    partial = dict(vocab)
+    del partial[byte_alphabet()[255]]
+    with pytest.raises(TokenizerError) as ei:
+        Tokenizer(partial, [])
+    assert ei.value.kind == "missing_byte" and ei.value.fields == {"byte_value": 255}
+    for bad in (0, -3, 1.0):
+        with pytest.raises(TokenizerError):
+            TokenizerLimits(max_input_bytes=bad)
+
+
+def test_special_token_also_in_vocab_is_admitted():
+    """GPT-2 style: the special token is a vocabulary entry with the same id
+    and bytes; that is one piece, not a duplicate."""
+    text, vocab = make_json(MERGES)
+    vocab = dict(vocab)
+    eot = len(vocab)
+    vocab["<|endoftext|>"] = eot
+    tok = Tokenizer(vocab, [], [("<|endoftext|>", eot)])
+    assert tok.encode("a<|endoftext|>") == [vocab["a"], eot]
+    assert tok.decode_text([eot], special_policy="skip") == ""
