@@ -37,7 +37,41 @@ _TORCH_TO_ST = {v[0]: k for k, v in _DTYPES.items()}
 
 
 class SafetensorsError(ValueError):
-    pass
+    """A rejected file.  ``kind`` names the check that failed (the reader's
+    typed errors, model/safetensors_reader/reader.mbt): ``missing_length``,
+    ``header_too_large``, ``truncated_header``, ``envelope``, ``encoding``,
+    ``json``, ``metadata``, ``tensor_field``, ``integer``, ``dtype``,
+    ``rank``, ``name``, ``too_many_tensors``, ``byte_range``, ``outside_payload``,
+    ``size_mismatch``, ``size_overflow``, ``overlap``, ``payload_mismatch``;
+    ``entry`` is the tensor's index in the header (-1 for file-level checks)."""
+
+    def __init__(self, message: str, kind: str = "invalid", entry: int = -1):
+        super().__init__(message)
+        self.kind = kind
+        self.entry = entry
+
+
+@dataclass(frozen=True)
+class ReaderLimits:
+    """Bounds checked before the header is decoded or a tensor is admitted."""
+    max_header_bytes: int = MAX_HEADER_BYTES
+    max_tensor_count: int = 1 << 16
+    max_rank: int = 8
+    max_name_length: int = 1024
+    max_payload_bytes: int = 1 << 40
+
+
+_I64_MAX = (1 << 63) - 1
+
+
+def _exact_int(v, entry: int) -> int:
+    """A JSON number that is an exact int64 (``2``, ``2.0`` and ``2e0`` are
+    the same value; ``2.5``, ``true`` and values past int64 are not)."""
+    if type(v) is float and v.is_integer() and abs(v) <= 2.0 ** 63:
+        v = int(v)
+    if type(v) is not int or not -_I64_MAX - 1 <= v <= _I64_MAX:
+        raise SafetensorsError("not an exact int64", "integer", entry)
+    return v
 
 
 @dataclass(frozen=True)
@@ -53,51 +87,113 @@ class TensorMeta:
         return self.end - self.begin
 
 
-def parse_header(buf: bytes, file_size: int) -> Tuple[int, Dict[str, TensorMeta], Dict[str, str]]:
-    if len(buf) < 8:
-        raise SafetensorsError("file shorter than the header length field")
-    (hlen,) = struct.unpack("<Q", buf[:8])
-    if hlen == 0 or hlen > MAX_HEADER_BYTES or 8 + hlen > file_size:
-        raise SafetensorsError("declared header length out of range")
-    raw = bytes(buf[8:8 + hlen])
-    try:
-        obj = loads_strict(raw.decode("utf-8"))
-    except (UnicodeDecodeError, ValueError) as e:
-        raise SafetensorsError(f"header is not strict JSON: {e}") from None
-    if not isinstance(obj, dict):
-        raise SafetensorsError("header must be a JSON object")
+def declared_header_bytes(prefix: bytes, limits: ReaderLimits = ReaderLimits()) -> int:
+    """The header length that an 8-byte little-endian prefix declares, bounded
+    by ``max_header_bytes`` (the prefix must be exactly 8 bytes)."""
+    if len(prefix) != 8:
+        raise SafetensorsError("the length prefix is 8 bytes", "envelope")
+    (hlen,) = struct.unpack("<Q", prefix)
+    if hlen > _I64_MAX:
+        raise SafetensorsError("declared header length overflows", "header_too_large")
+    if hlen > limits.max_header_bytes:
+        raise SafetensorsError("declared header length above the limit", "header_too_large")
+    return hlen
+
+
+def parse_header(buf: bytes, file_size: int,
+                 limits: ReaderLimits = ReaderLimits()) -> Tuple[int, Dict[str, TensorMeta], Dict[str, str]]:
+    """Validates the length prefix, the header envelope and JSON, every
+    tensor entry, and that the tensors tile the payload exactly (no overlap,
+    no hole, no trailing bytes).  ``buf`` holds at least the prefix and the
+    header; ``file_size`` is the whole file's size.  Returns (payload start,
+    tensors, metadata)."""
+    if len(buf) < 8 or file_size < 8:
+        raise SafetensorsError("file shorter than the header length field", "missing_length")
+    hlen = declared_header_bytes(bytes(buf[:8]), limits)
+    if hlen == 0:
+        raise SafetensorsError("empty header", "envelope")
+    if 8 + hlen > file_size or 8 + hlen > len(buf):
+        raise SafetensorsError("header truncated", "truncated_header")
     payload = file_size - 8 - hlen
+    if payload > limits.max_payload_bytes:
+        raise SafetensorsError("payload above the limit", "outside_payload")
+    raw = bytes(buf[8:8 + hlen])
+    # envelope: an object that starts the header; only space padding follows it
+    body = raw.rstrip(b" ")
+    if not body.startswith(b"{") or not body.endswith(b"}"):
+        raise SafetensorsError("header is not one JSON object padded with spaces", "envelope")
+    try:
+        text = raw.decode("utf-8")
+    except UnicodeDecodeError:
+        raise SafetensorsError("header is not UTF-8", "encoding") from None
+    try:
+        obj = loads_strict(text)
+    except ValueError as e:
+        raise SafetensorsError(f"header is not strict JSON: {e}", "json") from None
+    if not isinstance(obj, dict):
+        raise SafetensorsError("header must be a JSON object", "envelope")
+    n_tensors = len(obj) - ("__metadata__" in obj)
+    if n_tensors > limits.max_tensor_count:
+        raise SafetensorsError("too many tensors", "too_many_tensors")
     metadata = {}
     tensors: Dict[str, TensorMeta] = {}
+    idx = -1
     for name, spec in obj.items():
         if name == "__metadata__":
             if not isinstance(spec, dict) or not all(isinstance(v, str) for v in spec.values()):
-                raise SafetensorsError("__metadata__ must map strings to strings")
+                raise SafetensorsError("__metadata__ must map strings to strings", "metadata")
             metadata = dict(spec)
             continue
-        if not isinstance(spec, dict) or set(spec) != {"dtype", "shape", "data_offsets"}:
-            raise SafetensorsError(f"tensor entry {name!r} has unexpected fields")
+        idx += 1
+        if not name or len(name.encode()) > limits.max_name_length:
+            raise SafetensorsError("tensor name empty or too long", "name", idx)
+        if not isinstance(spec, dict):
+            raise SafetensorsError("tensor entry must be an object", "tensor_field", idx)
+        if set(spec) - {"dtype", "shape", "data_offsets"}:
+            raise SafetensorsError(f"tensor entry {idx} has unexpected fields", "tensor_field", idx)
+        if set(spec) != {"dtype", "shape", "data_offsets"}:
+            raise SafetensorsError(f"tensor entry {idx} lacks a field", "tensor_field", idx)
         dt = spec["dtype"]
+        if not isinstance(dt, str):
+            raise SafetensorsError("dtype must be a string", "tensor_field", idx)
         if dt not in _DTYPES:
-            raise SafetensorsError(f"unsupported dtype {dt!r}")
+            raise SafetensorsError(f"unsupported dtype {dt!r}", "dtype", idx)
         shape = spec["shape"]
         offs = spec["data_offsets"]
-        if (not isinstance(shape, list) or not all(type(d) is int and d >= 0 for d in shape)):
-            raise SafetensorsError("shape must be non-negative integers")
-        if (not isinstance(offs, list) or len(offs) != 2 or not all(type(o) is int and o >= 0 for o in offs)
-                or offs[0] > offs[1] or offs[1] > payload):
-            raise SafetensorsError("data_offsets out of range")
-        n = 1
+        if not isinstance(shape, list):
+            raise SafetensorsError("shape must be a list", "tensor_field", idx)
+        if not isinstance(offs, list) or len(offs) != 2:
+            raise SafetensorsError("data_offsets must be a pair", "tensor_field", idx)
+        shape = [_exact_int(d, idx) for d in shape]
+        offs = [_exact_int(o, idx) for o in offs]
+        if len(shape) > limits.max_rank:
+            raise SafetensorsError("tensor rank above the limit", "rank", idx)
+        if any(d < 0 for d in shape):
+            raise SafetensorsError("shape must be non-negative", "integer", idx)
+        if offs[0] < 0 or offs[0] > offs[1]:
+            raise SafetensorsError("data_offsets is not a byte range", "byte_range", idx)
+        if offs[1] > payload:
+            raise SafetensorsError("data_offsets outside the payload", "outside_payload", idx)
+        n = _DTYPES[dt][1]
         for d in shape:
             n *= d
-        if n * _DTYPES[dt][1] != offs[1] - offs[0]:
-            raise SafetensorsError(f"tensor {name!r} size does not match its shape")
+            if n > _I64_MAX:
+                raise SafetensorsError("tensor byte size overflows", "size_overflow", idx)
+        if n != offs[1] - offs[0]:
+            raise SafetensorsError(f"tensor {idx} size does not match its shape", "size_mismatch", idx)
         tensors[name] = TensorMeta(name, dt, tuple(shape), offs[0], offs[1])
-    # Overlap check: sorted by begin, each must start at or after the previous end.
+    # The tensors tile the payload: sorted by begin, each starts where the
+    # previous ended, and the last ends at the payload's end.
     spans = sorted((m.begin, m.end, m.name) for m in tensors.values() if m.end > m.begin)
-    for (b0, e0, n0), (b1, e1, n1) in zip(spans, spans[1:]):
-        if b1 < e0:
-            raise SafetensorsError(f"tensors {n0!r} and {n1!r} overlap")
+    at = 0
+    for b, e, nm in spans:
+        if b < at:
+            raise SafetensorsError(f"tensor {nm!r} overlaps its predecessor", "overlap")
+        if b > at:
+            raise SafetensorsError("payload has a hole between tensors", "payload_mismatch")
+        at = e
+    if at != payload:
+        raise SafetensorsError("payload has bytes no tensor covers", "payload_mismatch")
     return 8 + hlen, tensors, metadata
 
 
