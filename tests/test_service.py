@@ -410,3 +410,49 @@ def test_incremental_output_is_payload_safe_and_split_invariant():
         tail = io.finish()
         tail.decode("utf-8")
         assert (out + tail).decode("utf-8") == raw.decode("utf-8", errors="replace"), (raw, pieces)
+
+
+def _first_stop(full: bytes, stops):
+    """Oracle: the start of the stop string that completes first in ``full``
+    (the earliest end; on equal ends the longer match), or None."""
+    best = None
+    for s in stops:
+        i = full.find(s)
+        while i >= 0:
+            end = i + len(s)
+            if best is None or end < best[0] or (end == best[0] and i < best[1]):
+                best = (end, i)
+            i = full.find(s, i + 1)
+    return None if best is None else best[1]
+
+
+def test_incremental_output_stop_strings_split_invariant():
+    """Stop strings (overlapping, sharing prefixes, multi-byte) are found at
+    the same place however the bytes are cut into token pieces, nothing after
+    the stop is released, and without a hit the deltas plus the terminal tail
+    are the whole text (reference: service/incremental_output/output_wbtest.mbt,
+    'stop text spanning token pieces is withheld before terminal',
+    'stop matcher spans UTF-8 bytes')."""
+    import random
+    rng = random.Random(11)
+    alphabet = [b"a", b"b", b"c", b"\xc3\xa9", b"\xe2\x82\xac", b" "]
+    stop_sets = [[b"abca"], [b"abcd", b"bc"], [b"aa", b"aab"], ["é€".encode()], [b"ab", "b€".encode(), b"ca c"]]
+    for trial in range(400):
+        stops = rng.choice(stop_sets)
+        full = b"".join(rng.choice(alphabet) for _ in range(rng.randint(0, 16)))
+        cuts = sorted(rng.sample(range(1, len(full)), min(len(full) - 1, rng.randint(0, 8)))) if len(full) > 1 else []
+        pieces = [full[a:b] for a, b in zip([0] + cuts, cuts + [len(full)])] if full else []
+        io = IncrementalOutput(stops)
+        out, hit = b"", False
+        for pc in pieces:
+            d, hit = io.push(pc)
+            out += d
+            if hit:
+                break
+        cut = _first_stop(full, stops)
+        if cut is None:
+            assert not hit
+            assert out + io.finish() == full, (stops, pieces)
+        else:
+            assert hit and out == full[:cut], (stops, pieces, out)
+            assert io.finish() == b"" and io.push(b"more") == (b"", True)
