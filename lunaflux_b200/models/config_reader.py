@@ -18,6 +18,7 @@ or in ``rope_parameters``; every other scaling type is rejected.
 from __future__ import annotations
 
 import hashlib
+import math
 from typing import Any, Dict
 
 from ..utils.json_strict import loads_strict
@@ -42,20 +43,32 @@ _INERT = {"_name_or_path", "transformers_version", "bos_token_id", "eos_token_id
           "initializer_range", "use_cache", "dtype"}
 
 
+_MAX_INT = (1 << 31) - 1
+
+
 def _int(d, k, required=True, default=None):
+    """A positive integer field (missing, mistyped, fractional and values past
+    2^31 - 1 are refused; ``bool`` is not an integer here)."""
     v = d.get(k, default)
     if v is None and not required:
         return None
-    if type(v) is not int or v <= 0:
-        raise ConfigReaderError(f"{k} must be a positive integer")
+    if type(v) is not int or not 0 < v <= _MAX_INT:
+        raise ConfigReaderError(f"{k} must be a positive integer below 2^31")
     return v
 
 
 def _num(d, k, default=None):
+    """A finite number field (JSON overflow such as 1e999 reads as inf)."""
     v = d.get(k, default)
-    if isinstance(v, bool) or not isinstance(v, (int, float)):
-        raise ConfigReaderError(f"{k} must be a number")
+    if isinstance(v, bool) or not isinstance(v, (int, float)) or not math.isfinite(v):
+        raise ConfigReaderError(f"{k} must be a finite number")
     return float(v)
+
+
+_DTYPE_NAMES = {"bfloat16", "float16", "float32"}
+_ARCHITECTURES = {"llama": "LlamaForCausalLM", "mixtral": "MixtralForCausalLM"}
+_MOE_ONLY = {"num_local_experts", "num_experts_per_tok", "router_aux_loss_coef", "output_router_logits",
+             "router_jitter_noise"}
 
 
 _LLAMA3_KEYS = {"factor", "low_freq_factor", "high_freq_factor", "original_max_position_embeddings"}
@@ -102,6 +115,15 @@ def parse_config(text: str | bytes, dtype: str = "bf16") -> LlamaSpec:
     arch = d.get("architectures")
     if arch is not None and (not isinstance(arch, list) or len(arch) != 1):
         raise ConfigReaderError("exactly one architecture is required")
+    if arch is not None and arch[0] != _ARCHITECTURES[mt]:
+        raise ConfigReaderError(f"architecture must be {_ARCHITECTURES[mt]} for model_type {mt}")
+    if mt == "llama" and _MOE_ONLY & set(d):
+        raise ConfigReaderError("expert fields on a dense llama config")
+    for k in ("torch_dtype", "dtype"):
+        if k in d and d[k] is not None and d[k] not in _DTYPE_NAMES:
+            raise ConfigReaderError(f"{k} must be one of {sorted(_DTYPE_NAMES)}")
+    if "torch_dtype" in d and "dtype" in d and d["torch_dtype"] != d["dtype"]:
+        raise ConfigReaderError("torch_dtype and dtype disagree")
     if d.get("tie_word_embeddings", False) is not False:
         raise ConfigReaderError("tied embeddings are not supported")
     if d.get("sliding_window") is not None:
@@ -132,7 +154,11 @@ def parse_config(text: str | bytes, dtype: str = "bf16") -> LlamaSpec:
     hidden = _int(d, "hidden_size")
     heads = _int(d, "num_attention_heads")
     kv = _int(d, "num_key_value_heads", default=heads)
-    head_dim = d.get("head_dim") or hidden // heads
+    head_dim = _int(d, "head_dim", required=False)
+    if head_dim is None:
+        if hidden % heads:
+            raise ConfigReaderError("hidden_size must be a multiple of num_attention_heads")
+        head_dim = hidden // heads
     if hidden != heads * head_dim:
         raise ConfigReaderError("hidden_size must equal heads * head_dim")
     experts = topk = 0

@@ -19,6 +19,11 @@ PAGED_PLAN_SCHEMA = "lunaflux.dense-llama-plan.v2.paged"
 MOE_PLAN_SCHEMA = "lunaflux.mixtral-plan.v1.paged"
 
 
+#: bound on every dimension (and on heads * head_dim): sizes stay well inside
+#: 32-bit kernel index arithmetic
+MAX_DIMENSION = (1 << 31) - 1
+
+
 class SpecError(ValueError):
     pass
 
@@ -51,18 +56,27 @@ class LlamaSpec:
     def __post_init__(self):
         pos = [self.hidden, self.layers, self.heads, self.kv_heads, self.head_dim, self.ffn, self.vocab,
                self.max_position]
-        if any(int(v) <= 0 for v in pos):
-            raise SpecError("all dimensions must be positive")
+        if any(type(v) is not int for v in pos + [self.experts, self.experts_per_token, self.fp8_block]):
+            raise SpecError("dimensions must be integers")
+        if any(v <= 0 or v > MAX_DIMENSION for v in pos):
+            raise SpecError(f"all dimensions must be in 1..{MAX_DIMENSION}")
+        if self.heads * self.head_dim > MAX_DIMENSION or self.experts < 0 or self.experts > 1024:
+            raise SpecError("geometry out of range")
         if self.heads % self.kv_heads != 0:
             raise SpecError("heads must be a multiple of kv_heads (GQA)")
         if self.head_dim % 2 != 0:
             raise SpecError("head_dim must be even for split-half RoPE")
-        if not (self.rope_theta > 0 and self.rms_eps > 0):
-            raise SpecError("rope_theta and rms_eps must be positive")
+        for v in (self.rope_theta, self.rms_eps):
+            if isinstance(v, bool) or not isinstance(v, (int, float)) or not math.isfinite(v):
+                raise SpecError("rope_theta and rms_eps must be finite numbers")
+        if not (self.rope_theta > 0 and 0 < self.rms_eps < 1):
+            raise SpecError("rope_theta must be positive and rms_eps in (0, 1)")
         if self.dtype not in ("bf16", "fp32"):
             raise SpecError("dtype must be bf16 or fp32")
         if self.experts and not (0 < self.experts_per_token <= self.experts):
             raise SpecError("experts_per_token must be in (0, experts]")
+        if not self.experts and self.experts_per_token:
+            raise SpecError("experts_per_token without experts")
         if self.fp8_block not in (0, 128):
             raise SpecError("fp8 block size must be 128")
         if self.rope_scaling:
@@ -70,6 +84,8 @@ class LlamaSpec:
             if len(rs) != 5 or rs[0] != "llama3":
                 raise SpecError("rope_scaling must be () or ('llama3', factor, low, high, original_max_position)")
             _, factor, low, high, orig = rs
+            if not all(math.isfinite(x) for x in (factor, low, high)) or type(orig) is not int:
+                raise SpecError("llama3 rope scaling needs finite factors and an integer original length")
             if not (factor >= 1.0 and 0 < low < high and int(orig) > 0):
                 raise SpecError("llama3 rope scaling needs factor >= 1, 0 < low_freq_factor < high_freq_factor")
 

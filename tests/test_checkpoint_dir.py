@@ -161,3 +161,76 @@ def test_approved_root_refuses_a_fifo_without_blocking(tmp_path, impl):
         root.read_snapshot("pipe", 10)
     data, st = root.read_snapshot("ok.bin", 10)
     assert data == b"abc" and st.size == 3
+
+
+def _base_config():
+    from lunaflux_b200.models.config_reader import to_config
+    from lunaflux_b200.models.spec import tiny_llama
+    return to_config(tiny_llama())
+
+
+@pytest.mark.parametrize("patch", [
+    {"hidden_size": 64.0}, {"hidden_size": True}, {"hidden_size": "64"}, {"hidden_size": -64},
+    {"hidden_size": 1 << 40}, {"num_hidden_layers": 0}, {"vocab_size": 2.5}, {"head_dim": 16.0},
+    {"head_dim": 0}, {"head_dim": True},
+    {"num_key_value_heads": 3},                         # 4 heads are not a multiple of 3
+    {"head_dim": 17, "hidden_size": 68},                # odd head_dim: split-half RoPE
+    {"head_dim": None, "hidden_size": 66},              # hidden not a multiple of heads
+    {"rms_norm_eps": 0.0}, {"rms_norm_eps": 1.5}, {"rms_norm_eps": "1e-5"},
+    {"rope_theta": -1.0}, {"rope_theta": 0},
+    {"torch_dtype": "int8"}, {"torch_dtype": 16}, {"dtype": "float64"},
+    {"dtype": "float16", "torch_dtype": "bfloat16"},
+    {"architectures": ["MixtralForCausalLM"]}, {"architectures": ["LlamaForCausalLM", "X"]},
+    {"num_local_experts": 8},                           # expert fields on a dense model
+])
+def test_config_dimensions_types_and_semantics_fail_closed(patch):
+    """Reference: model/config_reader/reader_test.mbt ('missing mistyped
+    fractional and overflowing dimensions are bounded', 'invalid head
+    relationships reach the model specification validator', 'dtype RoPE
+    architecture and unsupported semantic variants fail closed', 'RMS
+    normalization epsilon is explicit and bounded')."""
+    from lunaflux_b200.models.config_reader import ConfigReaderError, parse_config
+    d = {**_base_config(), **patch}
+    d = {k: v for k, v in d.items() if v is not None}
+    with pytest.raises(ConfigReaderError):
+        parse_config(json.dumps(d))
+
+
+def test_config_overflowing_float_is_not_infinity():
+    """JSON 1e999 parses to inf; a non-finite epsilon or theta is refused."""
+    from lunaflux_b200.models.config_reader import ConfigReaderError, parse_config
+    text = json.dumps(_base_config())
+    for k in ("rms_norm_eps", "rope_theta"):
+        d = json.loads(text)
+        d[k] = 1.0
+        bad = json.dumps(d).replace(f'"{k}": 1.0', f'"{k}": 1e999')
+        assert "1e999" in bad
+        with pytest.raises(ConfigReaderError):
+            parse_config(bad)
+
+
+def test_config_accepted_variants():
+    """Missing KV head count means multi-head attention; the dtype spellings
+    transformers writes are accepted; the epsilon is kept exactly."""
+    from lunaflux_b200.models.config_reader import parse_config
+    d = _base_config()
+    d.pop("num_key_value_heads")
+    d.pop("head_dim")
+    d["rms_norm_eps"] = 1e-6
+    s = parse_config(json.dumps(dict(d, torch_dtype="bfloat16", dtype="bfloat16")))
+    assert s.kv_heads == s.heads and s.head_dim == s.hidden // s.heads and s.rms_eps == 1e-6
+    assert parse_config(json.dumps(d).encode()) == parse_config(json.dumps(d))   # bytes and str alike
+
+
+def test_spec_rejects_forged_geometry():
+    import dataclasses
+
+    from lunaflux_b200.models.spec import SpecError, tiny_llama
+    t = tiny_llama()
+    for kw in ({"head_dim": 16.0}, {"hidden": True}, {"layers": 0}, {"vocab": 1 << 31}, {"rms_eps": float("inf")},
+               {"rope_theta": float("nan")}, {"experts_per_token": 2}, {"experts": 4, "experts_per_token": 5},
+               {"fp8_block": 64}, {"dtype": "fp16"},
+               {"rope_scaling": ("llama3", float("inf"), 1.0, 4.0, 8192)},
+               {"rope_scaling": ("llama3", 8.0, 1.0, 4.0, 8192.0)}):
+        with pytest.raises(SpecError):
+            dataclasses.replace(t, **kw)

@@ -86,8 +86,8 @@ def test_config_reader_rejections():
                   {"attention_bias": True}]:
         with pytest.raises(ConfigReaderError):
             parse_config(json.dumps({**base, **patch}))
-    m = parse_config(json.dumps({**base, "model_type": "mixtral", "num_local_experts": 8,
-                                 "num_experts_per_tok": 2}))
+    m = parse_config(json.dumps({**base, "model_type": "mixtral", "architectures": ["MixtralForCausalLM"],
+                                 "num_local_experts": 8, "num_experts_per_tok": 2}))
     assert m.is_moe and m.experts == 8
 
 
