@@ -53,7 +53,8 @@ class NativePageAllocator:
                  max_active_refs: int = 1 << 20, max_cached_refs: int = 1 << 20):
         from .. import _host
         self._h = _host
-        self._c = _host.PageAllocator(capacity, first_index, max_generation, max_active_refs, max_cached_refs)
+        self._c = self._call(_host.PageAllocator, capacity, first_index, max_generation, max_active_refs,
+                             max_cached_refs)
         self.capacity = capacity
         self.first_index = first_index
 
