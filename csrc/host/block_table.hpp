@@ -103,6 +103,9 @@ class BlockTableArena {
     if (keep < 0) throw BlockTableError("negative length");
     if (keep >= (int)v.size()) return {};
     std::vector<Page> dropped(v.begin() + keep, v.end());
+    // preflight: a release that would fail throws here, with the table and
+    // the allocator untouched
+    if (alloc != nullptr) alloc->check_release_active(dropped);
     v.resize(keep);
     int32_t* row = matrix_.data() + (size_t)s * maxp_;
     for (size_t i = 0; i < dropped.size(); ++i) row[keep + i] = 0;

@@ -91,6 +91,7 @@ PYBIND11_MODULE(_host, m) {
       .def("allocate_run", &PageAllocator::allocate_run)
       .def("retain_active", &PageAllocator::retain_active)
       .def("release_active", &PageAllocator::release_active)
+      .def("check_release_active", &PageAllocator::check_release_active)
       .def("retain_cached", &PageAllocator::retain_cached)
       .def("release_cached", &PageAllocator::release_cached)
       .def("active_reference_count", &PageAllocator::active_reference_count)

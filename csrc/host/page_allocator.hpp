@@ -5,6 +5,7 @@
 // checkpoint with exact rollback.  O(1) per page.  Exact restatement of the
 // Python reference class PyPageAllocator (lunaflux_b200/kv/page_allocator.py).
 #pragma once
+#include <algorithm>
 #include <cstdint>
 #include <deque>
 #include <stdexcept>
@@ -87,6 +88,21 @@ class PageAllocator {
     if (cached_[s] <= 0) throw PageError("no cached reference to release");
     --cached_[s];
     maybe_free(s);
+  }
+  // Throws, changing nothing, unless release_active could run once for every
+  // entry of `pages` (a page listed n times needs n active references).
+  void check_release_active(const std::vector<std::pair<int, int64_t>>& pages) const {
+    no_ckpt();
+    std::vector<std::pair<int, int>> need;  // (slot, count), sorted below
+    need.reserve(pages.size());
+    for (const auto& p : pages) need.emplace_back(slot(p.first, p.second), 1);
+    std::sort(need.begin(), need.end());
+    for (size_t i = 0; i < need.size();) {
+      size_t j = i;
+      while (j < need.size() && need[j].first == need[i].first) ++j;
+      if (active_[need[i].first] < (int)(j - i)) throw PageError("no active reference to release");
+      i = j;
+    }
   }
   int active_reference_count(int idx, int64_t g) const { return active_[slot(idx, g)]; }
   int cached_reference_count(int idx, int64_t g) const { return cached_[slot(idx, g)]; }

@@ -85,19 +85,33 @@ class PyBlockTableArena:
         self.matrix[s, n:n + len(pids)] = [p.index for p in pids]
 
     def page_at(self, tid: TableId, logical: int) -> PageId:
-        return self._pages[self._slot(tid)][logical]
+        v = self._pages[self._slot(tid)]
+        if not 0 <= logical < len(v):
+            raise BlockTableError("logical page out of range")
+        return v[logical]
 
     def resolve_token_position(self, tid: TableId, position: int):
         """(physical page index, offset in page) of a token position."""
         s = self._slot(tid)
+        if position < 0:
+            raise BlockTableError("negative position")
         lp, off = divmod(position, self.tokens_per_page)
         if lp >= len(self._pages[s]):
             raise BlockTableError("position beyond the table")
         return self._pages[s][lp].index, off
 
     def truncate(self, tid: TableId, keep: int, allocator: Optional[PageAllocator] = None) -> List[PageId]:
+        """Drops the pages from ``keep`` on (releasing their active reference
+        when an allocator is given) and returns them.  A release that would
+        fail raises before anything changes, in the table or the allocator."""
         s = self._slot(tid)
+        if keep < 0:
+            raise BlockTableError("negative length")
         dropped = self._pages[s][keep:]
+        if not dropped:
+            return []
+        if allocator is not None:
+            allocator.check_release_active(dropped)
         del self._pages[s][keep:]
         self.matrix[s, keep:keep + len(dropped)] = 0
         if allocator is not None:
@@ -189,6 +203,8 @@ class NativeBlockTableArena:
 
     def truncate(self, tid: TableId, keep: int, allocator: Optional[PageAllocator] = None) -> List[PageId]:
         na = self._native_alloc(allocator)
+        if allocator is not None and na is None and keep >= 0:
+            allocator.check_release_active(self.pages(tid)[keep:])   # preflight, as the core does
         dropped = [PageId(i, g) for i, g in self._call(self._c.truncate, tid.index, tid.generation, keep, na)]
         if allocator is not None and na is None:
             for p in dropped:

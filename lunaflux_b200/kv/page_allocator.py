@@ -91,6 +91,9 @@ class NativePageAllocator:
         for p in pids:
             self.release_active(p)
 
+    def check_release_active(self, pids: Iterable[PageId]):
+        self._call(self._c.check_release_active, [(p.index, p.generation) for p in pids])
+
     def retain_cached(self, pid: PageId):
         self._call(self._c.retain_cached, pid.index, pid.generation)
 
@@ -225,6 +228,16 @@ class PyPageAllocator:
     def release_active_many(self, pids: Iterable[PageId]):
         for p in pids:
             self.release_active(p)
+
+    def check_release_active(self, pids: Iterable[PageId]):
+        """Raises, changing nothing, unless ``release_active`` could run once
+        for every entry of ``pids`` (a page listed n times needs n active
+        references)."""
+        self._no_ckpt()
+        need = collections.Counter(self._slot(p) for p in pids)
+        for s, n in need.items():
+            if self._active[s] < n:
+                raise PageAllocatorError("no active reference to release")
 
     def retain_cached(self, pid: PageId):
         self._no_ckpt()

@@ -123,3 +123,74 @@ def test_rollback_restores_several_runs_atomically(impl):
 def test_construction_limits(impl, cap):
     with pytest.raises((PageAllocatorError, ValueError)):
         impl(cap)
+
+
+# ----------------------------------------------------------------- block tables
+# Reference: kv/block_table/arena_test.mbt ('append failures are
+# transactional', 'truncate preflight preserves table and reusable output',
+# 'dense mapping resolves exact logical pages and token offsets').
+
+from lunaflux_b200.kv.block_table import BlockTableError, NativeBlockTableArena, PyBlockTableArena  # noqa: E402
+
+TABLES = [PyBlockTableArena] + ([NativeBlockTableArena] if native_available() else [])
+
+
+@pytest.fixture(params=[(t, a) for t in TABLES for a in IMPLS], ids=lambda p: f"{p[0].__name__}-{p[1].__name__}")
+def arena_alloc(request):
+    t, a = request.param
+    return t(4, 4, tokens_per_page=16), a(16)
+
+
+def table_state(bt, tid):
+    return bt.pages(tid), bt.matrix[tid.index].tolist()
+
+
+def test_table_bounds_checks(arena_alloc):
+    bt, a = arena_alloc
+    tid = bt.allocate()
+    pages = a.allocate_run(3)
+    bt.append_pages(tid, pages)
+    assert bt.page_at(tid, 2) == pages[2]
+    assert bt.resolve_token_position(tid, 47) == (pages[2].index, 15)
+    for bad in (-1, 3):
+        with pytest.raises(BlockTableError):
+            bt.page_at(tid, bad)
+    for bad in (-1, -16, 48):
+        with pytest.raises(BlockTableError):
+            bt.resolve_token_position(tid, bad)
+    before = table_state(bt, tid)
+    with pytest.raises(BlockTableError):
+        bt.append_pages(tid, a.allocate_run(2))          # 3 + 2 > 4
+    with pytest.raises(BlockTableError):
+        bt.truncate(tid, -1, a)
+    assert table_state(bt, tid) == before
+    assert bt.truncate(tid, 5, a) == [] and table_state(bt, tid) == before
+
+
+def test_truncate_preflight_keeps_table_and_allocator(arena_alloc):
+    bt, a = arena_alloc
+    tid = bt.allocate()
+    pages = a.allocate_run(3)
+    bt.append_pages(tid, pages)
+    ids = list(pages)
+    # the last page lost its active reference elsewhere: releasing it would fail
+    a.retain_cached(pages[2])
+    a.release_active(pages[2])
+    before = (table_state(bt, tid), snapshot(a, ids[:2]), a.cached_reference_count(pages[2]))
+    with pytest.raises(PageAllocatorError):
+        bt.truncate(tid, 1, a)
+    assert (table_state(bt, tid), snapshot(a, ids[:2]), a.cached_reference_count(pages[2])) == before
+    # counts frozen by an open allocator checkpoint: also refused up front
+    a.retain_active(pages[2])
+    t = a.checkpoint()
+    with pytest.raises(PageAllocatorError):
+        bt.truncate(tid, 0, a)
+    a.rollback_to(t)
+    assert bt.pages(tid) == pages
+    # a valid truncate releases exactly the dropped pages
+    assert bt.truncate(tid, 1, a) == pages[1:]
+    assert a.validate_active(pages[0]) and not a.validate_active(pages[1])
+    assert bt.matrix[tid.index].tolist() == [pages[0].index, 0, 0, 0]
+    bt.reset_and_release(tid, a)
+    a.release_cached(pages[2])
+    assert a.free_page_count() == 16 and bt.free_table_count() == 4
