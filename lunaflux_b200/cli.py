@@ -294,9 +294,12 @@ def _build_engine(a, rank: int, world: int, local: int, clock):
     cuda = torch.cuda.is_available()
     dev = torch.device("cuda", local) if cuda else torch.device("cpu")
     from .models.admission import admit
-    adm = admit(spec, max_context=a.max_context, max_batch=sched.max_active_requests,
+    # the plan of THIS rank: attention and dense MLP split over the world,
+    # Mixtral experts spread one group per rank
+    adm = admit(spec, tp=world, ep=world if (spec.is_moe and world > 1) else 1,
+                max_context=a.max_context, max_batch=sched.max_active_requests,
                 step_tokens=sched.step_token_budget,
-                device_bytes=torch.cuda.get_device_properties(0).total_memory if cuda else 0, kernels=cuda)
+                device_bytes=torch.cuda.get_device_properties(dev).total_memory if cuda else 0, kernels=cuda)
     if not adm.ok:
         raise CliError("model not admitted: " + "; ".join(adm.details))
     source = ckpt.source() if ckpt is not None else random_source(spec, 0, dev, torch.bfloat16 if cuda else torch.float32)

@@ -27,7 +27,8 @@ class Rejection(enum.Enum):
     EP_EXPERTS = "ep_experts"              # experts not divisible by the EP degree
     FP8_BLOCK = "fp8_block"                # block-scaled fp8 needs 128-aligned projection dims
     GEMM_ALIGN = "gemm_align"              # hidden size not a multiple of 256 (GEMM tiles)
-    CONTEXT = "context"                    # requested context beyond max_position
+    CONTEXT = "context"                    # requested context not in 1..max_position
+    BATCH = "batch"                        # batch rows or step tokens not positive
     MEMORY = "memory"                      # weights + KV + workspace exceed the device memory
 
 
@@ -57,21 +58,40 @@ def _elem(spec: LlamaSpec) -> int:
 
 def memory_plan(spec: LlamaSpec, tp: int, ep: int, max_context: int, max_batch: int, step_tokens: int,
                 page: int = 16, device_bytes: int = 0) -> MemoryPlan:
+    """Bytes one rank holds.  The weight term follows the runtime layout
+    exactly (``models/weights.py`` ``build_runtime``): the embedding table is
+    replicated, the LM head holds this rank's vocabulary rows, each FFN shard
+    is padded to the 32-row gate/up interleave group, the MoE router is
+    fp32, and fp8 projections carry one fp32 scale per 128 x 128 block."""
     e = _elem(spec)
     H, D = spec.hidden, spec.head_dim
     q = spec.heads * D
     kv = spec.kv_heads * D
-    per_layer_attn = H * (q + 2 * kv) + q * H
+    tp = max(tp, 1)
+    ep = max(ep, 1)
+
+    def pad32(n: int) -> int:
+        return -(-n // 32) * 32
+
+    def blocks(o: int, i: int) -> int:
+        return -(-o // 128) * -(-i // 128)
+
+    q_l, kv_l = q // tp, max(kv // tp, D)
+    attn = [((q_l + 2 * kv_l), H), (H, q_l)]                 # wqkv, wo: (out, in)
     if spec.is_moe:
-        per_layer_mlp = (spec.experts // max(ep, 1)) * 3 * H * spec.ffn + H * spec.experts
-        attn_share = per_layer_attn // tp
-        mlp_share = per_layer_mlp if ep > 1 else per_layer_mlp // tp
+        f_l = pad32(spec.ffn if ep > 1 else spec.ffn // tp)
+        e_l = spec.experts // ep
+        mlp_elems = e_l * 3 * H * f_l
+        per_layer = (sum(o * i for o, i in attn) + mlp_elems) * e + spec.experts * H * 4
     else:
-        attn_share = per_layer_attn // tp
-        mlp_share = 3 * H * spec.ffn // tp
-    wbytes_per = 1 if spec.fp8_block else e
-    weights = spec.layers * (attn_share + mlp_share) * wbytes_per
-    weights += 2 * spec.vocab * H * e // tp + (2 * spec.layers + 1) * H * e
+        f_l = pad32(spec.ffn // tp)
+        mats = attn + [(2 * f_l, H), (H, f_l)]
+        if spec.fp8_block:
+            per_layer = sum(o * i + 4 * blocks(o, i) for o, i in mats)
+        else:
+            per_layer = sum(o * i for o, i in mats) * e
+    per_layer += 2 * H * e                                  # the two RMSNorm weights
+    weights = spec.layers * per_layer + spec.vocab * H * e + (spec.vocab // tp) * H * e + H * e
     kv_heads_local = max(1, spec.kv_heads // tp)
     pages = max_batch * -(-max_context // page)
     kv_bytes = spec.layers * 2 * pages * kv_heads_local * page * D * e
@@ -110,14 +130,20 @@ def admit(spec: LlamaSpec, tp: int = 1, ep: int = 1, max_context: int = 4096, ma
             no(Rejection.TP_FFN, f"ffn {spec.ffn} over {tp} ranks")
         if spec.vocab % tp:
             no(Rejection.TP_VOCAB, f"vocab {spec.vocab} over {tp} ranks")
-    if ep > 1 and (not spec.is_moe or spec.experts % ep):
+    if not 1 <= ep <= 8:
+        no(Rejection.EP_EXPERTS, f"expert-parallel degree {ep} (1..8 in one NVSwitch domain)")
+    elif ep > 1 and (not spec.is_moe or spec.experts % ep):
         no(Rejection.EP_EXPERTS, f"{spec.experts} experts over {ep} expert-parallel ranks")
     if kernels and spec.fp8_block and (spec.hidden % 128 or (spec.ffn // max(tp, 1)) % 128 or (spec.heads * spec.head_dim) % 128):
         no(Rejection.FP8_BLOCK, "fp8 projections need hidden, per-rank ffn and heads*head_dim multiples of 128")
     if kernels and spec.hidden % 256:
         no(Rejection.GEMM_ALIGN, f"hidden {spec.hidden} is not a multiple of 256")
-    if max_context > spec.max_position:
-        no(Rejection.CONTEXT, f"context {max_context} beyond max_position {spec.max_position}")
+    if not 0 < max_context <= spec.max_position:
+        no(Rejection.CONTEXT, f"context {max_context} outside 1..max_position {spec.max_position}")
+    if max_batch <= 0 or step_tokens <= 0:
+        no(Rejection.BATCH, f"max_batch {max_batch} and step_tokens {step_tokens} must be positive")
+    if not 0.0 <= reserve_fraction < 1.0:
+        raise ValueError("reserve_fraction must be in [0, 1)")
     mem = memory_plan(spec, max(tp, 1), ep, max_context, max_batch, step_tokens, device_bytes=device_bytes)
     if device_bytes > 0 and mem.total > device_bytes * (1.0 - reserve_fraction):
         no(Rejection.MEMORY, f"needs {mem.total / 2**30:.1f} GiB per rank, device has {device_bytes / 2**30:.1f} GiB")

@@ -130,6 +130,8 @@ class ModelWeights:
                 v = getattr(l, f.name)
                 if isinstance(v, torch.Tensor):
                     n += v.nbytes
+                elif isinstance(v, dict):          # fp8: (e4m3 weight, fp32 block scales)
+                    n += sum(t.nbytes for pair in v.values() for t in pair)
         return n
 
 
