@@ -229,8 +229,11 @@ class EngineService:
             lv.n_out += 1
             delta = b""
             stop_hit = False
-            if self.tokenizer is not None and o.token in self.tokenizer.id_to_token:
-                delta, stop_hit = lv.out.push(self.tokenizer.token_bytes(o.token))
+            # special tokens (EOS, chat markers) carry no text in the stream,
+            # and a string stop never matches inside one
+            tok = self.tokenizer
+            if tok is not None and o.token in tok.id_to_token and o.token not in tok.added_ids:
+                delta, stop_hit = lv.out.push(tok.token_bytes(o.token))
             lv.sink(TokenEvent(o.rid, o.position, o.token, delta))
             if stop_hit and not o.finished:
                 self.engine.scheduler.cancel(o.rid)

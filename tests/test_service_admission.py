@@ -389,3 +389,34 @@ def test_a_failing_sink_does_not_end_the_engine_thread(tiny):
     finally:
         svc.stop()
     assert isinstance(evs[-1], CompletedEvent)
+
+
+def test_special_tokens_carry_no_text_in_the_stream():
+    """Generated special tokens (EOS, chat markers) are streamed as token ids
+    with an empty delta, so no "<|eot_id|>" text reaches the client
+    (reference: service/incremental_output/output_wbtest.mbt, skipped
+    specials are payload safe)."""
+    from lunaflux_b200.models.spec import LlamaSpec
+    from lunaflux_b200.tokenizer.bpe import Tokenizer, byte_alphabet
+    spec = LlamaSpec(hidden=64, layers=2, heads=4, kv_heads=2, head_dim=16, ffn=172, vocab=512, rope_theta=10000.0,
+                     max_position=512, dtype="fp32")
+    ck = random_checkpoint(spec, 0)
+    alpha = byte_alphabet()
+    tok = Tokenizer({alpha[b]: b for b in range(256)}, [], [(f"<|s{i}|>", i) for i in range(256, 512)])
+    prompt = tok.encode("hello")
+    want = ReferenceModel(spec, ck).generate_greedy(prompt, 24)
+    assert any(t >= 256 for t in want) and any(t < 256 for t in want)   # both kinds are generated
+    svc, eng = service((spec, ck), tokenizer=tok)
+    c = Client()
+    svc.start()
+    try:
+        svc.submit(GenerateRequest(1, input_text=b"hello", max_new_tokens=24), c.sink(1))
+        evs = c.wait(1)
+    finally:
+        svc.stop()
+    toks = [e for e in evs if isinstance(e, TokenEvent)]
+    assert [e.token_id for e in toks] == want
+    assert all(e.delta == b"" for e in toks if e.token_id >= 256)
+    delivered = b"".join(e.delta for e in toks) + evs[-1].final_delta
+    text = b"".join(bytes([t]) for t in want if t < 256)
+    assert delivered == text.decode("utf-8", "replace").encode("utf-8")
