@@ -28,6 +28,7 @@ pre-token are cached.
 from __future__ import annotations
 
 import hashlib
+import re
 from dataclasses import dataclass
 from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
@@ -161,6 +162,8 @@ class Tokenizer:
             self.ranks[(a, b)] = r
         self.added = sorted(((s, i) for s, i in added), key=lambda x: (-len(x[0].encode()), x[1]))
         self.added_ids = {i for _, i in added}
+        self._special_ids = {t.encode(): i for t, i in self.added}
+        self._special_re = re.compile(b"|".join(re.escape(t.encode()) for t, _ in self.added)) if self.added else None
         seen_special: Dict[str, int] = {}
         for s, i in added:
             if not s:
@@ -305,29 +308,20 @@ class Tokenizer:
     def _encode_bytes(self, data: bytes, allow_special: bool) -> List[int]:
         if not self.added:
             return self._segment(data)
-        text = data
         ids: List[int] = []
         start = 0
-        i = 0
-        specials = [(s.encode(), t) for s, t in self.added]
-        while i < len(text):
-            hit = None
-            for s, t in specials:
-                if text.startswith(s, i):
-                    hit = (s, t)
-                    break
-            if hit is None:
-                i += 1
-                continue
+        # one scan for the leftmost special token; the alternation lists the
+        # longest first, so the first alternative that matches is the longest
+        for m in self._special_re.finditer(data):
+            tid = self._special_ids[m.group()]
             if not allow_special:
-                raise TokenizerError("input contains a special token", "special_token_rejected", token_id=hit[1])
-            if start < i:
-                ids += self._segment(text[start:i])
-            ids.append(hit[1])
-            i += len(hit[0])
-            start = i
-        if start < len(text):
-            ids += self._segment(text[start:])
+                raise TokenizerError("input contains a special token", "special_token_rejected", token_id=tid)
+            if start < m.start():
+                ids += self._segment(data[start:m.start()])
+            ids.append(tid)
+            start = m.end()
+        if start < len(data):
+            ids += self._segment(data[start:])
         return ids
 
     def encode(self, text: str, allow_special: bool = True, add_special_tokens: bool = False) -> List[int]:

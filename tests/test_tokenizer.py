@@ -260,3 +260,36 @@ def test_special_token_also_in_vocab_is_admitted():
     tok = Tokenizer(vocab, [], [("<|endoftext|>", eot)])
     assert tok.encode("a<|endoftext|>") == [vocab["a"], eot]
     assert tok.decode_text([eot], special_policy="skip") == ""
+
+
+def test_special_matching_equals_a_position_scan():
+    """The compiled special-token scan picks, at the leftmost position where
+    any special token starts, the longest one: the same ids as trying every
+    special token at every byte."""
+    import random
+    _, vocab = make_json(MERGES)
+    n = len(vocab)
+    specials = [("<a>", n), ("<a>b", n + 1), ("<", n + 2), ("a<a", n + 3), ("é|", n + 4), ("|é|", n + 5)]
+    text, vocab = make_json(MERGES, added=specials)
+    tok = Tokenizer.from_json(text)
+    order = sorted(((s.encode(), i) for s, i in specials), key=lambda x: -len(x[0]))
+
+    def scan(data):
+        ids, start, i = [], 0, 0
+        while i < len(data):
+            hit = next(((s, t) for s, t in order if data.startswith(s, i)), None)
+            if hit is None:
+                i += 1
+                continue
+            if start < i:
+                ids += tok._segment(data[start:i])
+            ids.append(hit[1])
+            i += len(hit[0])
+            start = i
+        return ids + (tok._segment(data[start:]) if start < len(data) else [])
+
+    rng = random.Random(5)
+    pieces = ["<", "a", ">", "b", "é", "|", "un", "related", " "]
+    for _ in range(500):
+        s = "".join(rng.choice(pieces) for _ in range(rng.randint(0, 14))).encode()
+        assert tok.encode_bytes(s) == scan(s), s
