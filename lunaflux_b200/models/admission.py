@@ -93,7 +93,7 @@ def memory_plan(spec: LlamaSpec, tp: int, ep: int, max_context: int, max_batch: 
     per_layer += 2 * H * e                                  # the two RMSNorm weights
     weights = spec.layers * per_layer + spec.vocab * H * e + (spec.vocab // tp) * H * e + H * e
     kv_heads_local = max(1, spec.kv_heads // tp)
-    pages = max_batch * -(-max_context // page)
+    pages = max_batch * -(-max_context // page) + 1        # + the reserved all-zero page
     kv_bytes = spec.layers * 2 * pages * kv_heads_local * page * D * e
     T = step_tokens + max_batch
     ws = T * (4 * H + (q + 2 * kv) // tp + 2 * spec.ffn // tp) * e + max_batch * spec.vocab * 4 // tp

@@ -85,3 +85,18 @@ def test_plan_arguments_out_of_range_are_rejections():
     assert admit(s, max_context=1296, max_batch=256, device_bytes=need, reserve_fraction=0.0).ok
     a = admit(s, max_context=1296, max_batch=256, device_bytes=need, reserve_fraction=0.05)
     assert a.reasons == [Rejection.MEMORY] and len(a.details) == 1
+
+
+def test_memory_plan_kv_equals_the_runner_arena():
+    """The KV term is the runner's arena: every sequence's pages plus the
+    reserved all-zero page that padded rows read."""
+    from lunaflux_b200.config import CacheConfig, SchedulerConfig
+    from lunaflux_b200.engine.engine import EngineOptions, LLMEngine
+    from lunaflux_b200.models.weights import build_runtime, random_checkpoint
+    from lunaflux_b200.ops import TorchOps
+    spec = specs.tiny_llama()
+    ck = random_checkpoint(spec, 0)
+    eng = LLMEngine(build_runtime(spec, ck.__getitem__), TorchOps(), "cpu",
+                    SchedulerConfig(step_token_budget=64, max_active_requests=4, prefill_chunk_tokens=64),
+                    CacheConfig(), EngineOptions(max_context=256, num_pages=4 * 256 // 16, graph_sizes=()))
+    assert memory_plan(spec, 1, 1, 256, 4, 64).kv_bytes == eng.runner.kv.nbytes
